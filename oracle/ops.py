@@ -1,0 +1,139 @@
+"""numpy front-end of the C oracle (TEST INFRASTRUCTURE ONLY -- see oracle/__init__.py).
+
+bf16 tensors are numpy uint16 bit patterns throughout.  Each wrapper names the C function (and
+through it the reference file:line) it forwards to.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import numpy as np
+
+from . import build as _build
+
+_lib = None
+_lock = threading.Lock()
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                L = ctypes.CDLL(str(_build.build()))
+                L.qo_exp.argtypes = [ctypes.c_float]
+                L.qo_exp.restype = ctypes.c_float
+                L.qo_log.argtypes = [ctypes.c_float]
+                L.qo_log.restype = ctypes.c_float
+                _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return a.ctypes.data_as(_P)
+
+
+# ---------------------------------------------------------------- bf16 helpers
+def f32_to_bf16(a) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16 bits; NaN -> 0x7FC0 (the library's rule)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = 0x7FC0
+    return r
+
+
+def bf16_to_f32(h) -> np.ndarray:
+    return (np.ascontiguousarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def bf16_round(a) -> np.ndarray:
+    return bf16_to_f32(f32_to_bf16(a))
+
+
+# ---------------------------------------------------------------- elementwise math
+def exp(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().qo_exp_arr(_p(x), _p(y), ctypes.c_long(x.size))
+    return y
+
+
+def log(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().qo_log_arr(_p(x), _p(y), ctypes.c_long(x.size))
+    return y
+
+
+def bf16_formulas(x_bits) -> dict:
+    """sigmoid_bf, silu_bf, softplus_bf (gdn_fused.py:22-41) and silu_f32 over bf16 bit patterns."""
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    out = {k: np.empty(x.size, np.float32) for k in ("sigmoid", "silu", "softplus", "silu_f32")}
+    lib().qo_bf16_formulas(_p(x), _I(x.size), _p(out["sigmoid"]), _p(out["silu"]), _p(out["softplus"]),
+                           _p(out["silu_f32"]))
+    return out
+
+
+def decode_tables():
+    """(e2m1[16], e4m3[256], e8m0[256]) as float32."""
+    a, b, c = np.empty(16, np.float32), np.empty(256, np.float32), np.empty(256, np.float32)
+    lib().qo_decode_tables(_p(a), _p(b), _p(c))
+    return a, b, c
+
+
+# ---------------------------------------------------------------- quantized GEMV
+def quantize_affine(w_bf16: np.ndarray, group_size: int = 64):
+    """C qo_quantize_affine: bf16 [N, K] -> (wq uint32 [N, K/8], scales bf16, biases bf16)."""
+    w = np.ascontiguousarray(w_bf16, dtype=np.uint16)
+    N, K = w.shape
+    wq = np.empty((N, K // 8), np.uint32)
+    s = np.empty((N, K // group_size), np.uint16)
+    b = np.empty((N, K // group_size), np.uint16)
+    lib().qo_quantize_affine(_p(w), _p(wq), _p(s), _p(b), _I(N), _I(K), _I(group_size))
+    return wq, s, b
+
+
+def qmv_affine(x_bf16, wq, s, b) -> np.ndarray:
+    """C qo_qmv_affine (canonical qmv, qmv_kernel.py:31-75 order of roles): y bf16 [M, N]."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16).reshape(-1, np.shape(x_bf16)[-1])
+    wq = np.ascontiguousarray(wq).view(np.uint32)
+    s = np.ascontiguousarray(s, dtype=np.uint16)
+    b = np.ascontiguousarray(b, dtype=np.uint16)
+    M, K = x.shape
+    N = wq.shape[0]
+    y = np.empty((M, N), np.uint16)
+    rc = lib().qo_qmv_affine(_p(x), _p(wq), _p(s), _p(b), _p(y), _I(M), _I(N), _I(K))
+    if rc != 0:
+        raise ValueError("qo_qmv_affine: unsupported shape")
+    return y
+
+
+def qmv_nvfp4(x_bf16, wq, s_u8) -> np.ndarray:
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16).reshape(-1, np.shape(x_bf16)[-1])
+    wq = np.ascontiguousarray(wq).view(np.uint32)
+    s = np.ascontiguousarray(s_u8, dtype=np.uint8)
+    M, K = x.shape
+    N = wq.shape[0]
+    y = np.empty((M, N), np.uint16)
+    rc = lib().qo_qmv_nvfp4(_p(x), _p(wq), _p(s), _p(y), _I(M), _I(N), _I(K))
+    if rc != 0:
+        raise ValueError("qo_qmv_nvfp4: unsupported shape")
+    return y
+
+
+def dequant_affine(wq, s, b, group_size: int = 64) -> np.ndarray:
+    """float64 dequantized weights (for tolerance checks against plain math)."""
+    wq = np.ascontiguousarray(wq).view(np.uint32)
+    N = wq.shape[0]
+    K = wq.shape[1] * 8
+    q = np.empty((N, K), np.float64)
+    for i in range(8):
+        q[:, i::8] = (wq >> (4 * i)) & 15
+    sf = np.repeat(bf16_to_f32(s).astype(np.float64), group_size, axis=1)
+    bf = np.repeat(bf16_to_f32(b).astype(np.float64), group_size, axis=1)
+    return sf * q + bf

@@ -1,0 +1,222 @@
+// Shared device helpers for libqmtp (sm_100a only).
+//
+// Arithmetic rule for every kernel in this library: the fp32 operation sequence is fixed and
+// written with explicit round-to-nearest intrinsics (__fmaf_rn, __fadd_rn, __fmul_rn, __fdiv_rn,
+// __fsqrt_rn); the library is also built with -fmad=false so nothing is contracted behind our
+// back.  The CPU oracle (oracle/qmtp_oracle.c) states the same sequences, so kernel results are
+// bit-identical to it.  exp/log below are this library's own (Cody-Waite reduction, Taylor /
+// atanh series), not CUDA's math library, for the same reason.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/qmtp.h"
+
+namespace qmtp {
+
+// ----------------------------------------------------------------------------- errors
+enum : unsigned { DEVERR_TIMEOUT = 1u, DEVERR_BADARG = 2u };
+unsigned* device_error_ptr();  // per-device address of the library's device error word
+int sm_count();                 // SMs of the current device (cached)
+
+#define QMTP_CUDA_TRY(expr)                          \
+  do {                                               \
+    cudaError_t e__ = (expr);                        \
+    if (e__ != cudaSuccess) return QMTP_ERR_CUDA;    \
+  } while (0)
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ----------------------------------------------------------------------------- bf16 bits
+__device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float(uint32_t(h) << 16); }
+__device__ __forceinline__ float bflo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bfhi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
+// fp32 -> bf16 round-to-nearest-even; NaN -> 0x7FC0 (same rule as the oracle).
+__device__ __forceinline__ uint16_t f2bf(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0;
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return uint16_t(u >> 16);
+}
+__device__ __forceinline__ float R(float x) { return bf2f(f2bf(x)); }
+
+// ----------------------------------------------------------------------------- exp / log
+__device__ __forceinline__ float q_expf(float x) {
+  if (x != x) return x;
+  if (x > 88.72283935546875f) return __int_as_float(0x7F800000);
+  if (x < -103.972084045410156f) return 0.0f;
+  const float kf = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+  float r = __fmaf_rn(-kf, 0.693145751953125f, x);
+  r = __fmaf_rn(-kf, 1.428606765330187045e-06f, r);
+  float p = 1.98412701138295233249664e-04f;
+  p = __fmaf_rn(p, r, 1.38888892251998186111450e-03f);
+  p = __fmaf_rn(p, r, 8.33333376795053482055664e-03f);
+  p = __fmaf_rn(p, r, 4.16666679084300994873047e-02f);
+  p = __fmaf_rn(p, r, 1.66666671633720397949219e-01f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int k = int(kf);
+  const int k1 = k / 2, k2 = k - k1;
+  const float s1 = __uint_as_float(uint32_t(k1 + 127) << 23);
+  const float s2 = __uint_as_float(uint32_t(k2 + 127) << 23);
+  return __fmul_rn(__fmul_rn(p, s1), s2);
+}
+
+__device__ __forceinline__ float q_logf(float x) {
+  if (x != x) return x;
+  if (x < 0.0f) return __int_as_float(0x7FC00000);
+  if (x == 0.0f) return __int_as_float(0xFF800000);
+  if (x == __int_as_float(0x7F800000)) return x;
+  int e = 0;
+  uint32_t ix = __float_as_uint(x);
+  if (ix < 0x00800000u) { x = __fmul_rn(x, 8388608.0f); ix = __float_as_uint(x); e = -23; }
+  e += int(ix >> 23) - 127;
+  float m = __uint_as_float((ix & 0x007FFFFFu) | 0x3F800000u);
+  if (m > 1.41421353816986083984375f) { m = __fmul_rn(m, 0.5f); e += 1; }
+  const float f = __fsub_rn(m, 1.0f);
+  const float s = __fdiv_rn(f, __fadd_rn(2.0f, f));
+  const float z = __fmul_rn(s, s);
+  float p = 2.22222223877906799316406e-01f;
+  p = __fmaf_rn(p, z, 2.85714298486709594726562e-01f);
+  p = __fmaf_rn(p, z, 4.00000005960464477539062e-01f);
+  p = __fmaf_rn(p, z, 6.66666686534881591796875e-01f);
+  const float lm = __fmaf_rn(__fmul_rn(s, z), p, __fmul_rn(2.0f, s));
+  const float ef = float(e);
+  return __fmaf_rn(ef, 0.693145751953125f, __fmaf_rn(ef, 1.428606765330187045e-06f, lm));
+}
+
+// bf16 activation formulas of gdn_fused.py:22-41 (round after every op).
+__device__ __forceinline__ float sigmoid_bf(float x) {
+  const float y = R(__fdiv_rn(1.0f, R(__fadd_rn(1.0f, R(q_expf(fabsf(x)))))));
+  return x < 0.0f ? y : R(__fsub_rn(1.0f, y));
+}
+__device__ __forceinline__ float silu_bf(float x) { return R(__fmul_rn(x, sigmoid_bf(x))); }
+__device__ __forceinline__ float log1p_bf(float x) {
+  const float xp1 = __fadd_rn(1.0f, x);
+  if (xp1 == 1.0f) return x;
+  const float t = __fdiv_rn(q_logf(xp1), __fsub_rn(xp1, 1.0f));
+  return R(__fmul_rn(x, t));
+}
+__device__ __forceinline__ float softplus_bf(float x) {
+  const float hi = x > 0.0f ? x : 0.0f, lo = x < 0.0f ? x : 0.0f;
+  return R(__fadd_rn(hi, log1p_bf(R(q_expf(R(__fsub_rn(lo, hi)))))));
+}
+__device__ __forceinline__ float silu_f32(float x) {
+  const float y = __fdiv_rn(1.0f, __fadd_rn(1.0f, q_expf(fabsf(x))));
+  return __fmul_rn(x, x < 0.0f ? y : __fsub_rn(1.0f, y));
+}
+__device__ __forceinline__ float sigmoid_f32(float x) {
+  const float y = __fdiv_rn(1.0f, __fadd_rn(1.0f, q_expf(fabsf(x))));
+  return x < 0.0f ? y : __fsub_rn(1.0f, y);
+}
+// 1/sqrt(v) from two correctly rounded ops (identical to the oracle's 1.0f / sqrtf(v)).
+__device__ __forceinline__ float rsqrt_rn(float v) { return __fdiv_rn(1.0f, __fsqrt_rn(v)); }
+
+// ----------------------------------------------------------------------------- warp sums
+// 32-lane xor butterfly (strides 16..1): every lane ends with the same bits.
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, d));
+  return v;
+}
+
+// Recursive-halving reduce-scatter of VP values (VP a power of two <= 32) across the warp.  For
+// every value the additions form exactly the xor butterfly tree of warp_sum (fp add commutes), so
+// the result is bit-identical to warp_sum applied value by value.  On return, v[0] holds value
+// `idx`; `owner` is true for one lane per value.
+template <int VP>
+__device__ __forceinline__ void warp_reduce_scatter(float (&v)[VP], int lane, int& idx, bool& owner) {
+  int n = VP;
+  idx = 0;
+  int rem_mask = 0;
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) {
+    if (n > 1) {
+      const int half = n >> 1;
+      const bool up = (lane & d) != 0;
+#pragma unroll
+      for (int i = 0; i < VP / 2; ++i) {
+        if (i < half) {
+          const float send = up ? v[i] : v[i + half];
+          const float keep = up ? v[i + half] : v[i];
+          v[i] = __fadd_rn(keep, __shfl_xor_sync(0xFFFFFFFFu, send, d));
+        }
+      }
+      if (up) idx += half;
+      n = half;
+    } else {
+      v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xFFFFFFFFu, v[0], d));
+      rem_mask |= d;
+    }
+  }
+  owner = (lane & rem_mask) == 0;
+}
+
+// ----------------------------------------------------------------------------- TMA / mbarrier
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// 1-D bulk copy global -> shared, completion counted on `bar`.  dst/src 16-B aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after `limit` polls, records DEVERR_TIMEOUT and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err,
+                                                  uint32_t limit = (1u << 24)) {
+  for (uint32_t it = 0; it < limit; ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  if (err) atomicOr(err, DEVERR_TIMEOUT);
+  return false;
+}
+
+// ----------------------------------------------------------------------------- loads
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+}  // namespace qmtp

@@ -1,0 +1,354 @@
+// Multi-row 4-bit GEMV (qmv) for B200: affine group-64 and NVFP4 group-16.
+//
+// Replaces qmv_kernel.py:14-101 (qmv_nvfp4_multi) and the MLX quantized_matmul route for 1-4
+// activation rows.  Design (HBM-bound streaming of the weights, each byte read once per call):
+//   * one CTA per SM-slot, persistent over a contiguous range of output rows;
+//   * the CTA's weight / scale / bias rows arrive by 1-D TMA bulk copies (cp.async.bulk) into an
+//     NS-stage shared-memory ring, completion tracked by mbarriers (bounded waits);
+//   * "x-stationary": warp w, lane l owns K-chunk c = 32w + l (32 elements) for the whole kernel
+//     and keeps those x values (all M rows) in registers, so x is read from HBM/L2 once per CTA;
+//   * nibbles become exact floats with one AND/OR on a shifted word (2048+q / 128+q), the offsets
+//     are removed through precomputed per-chunk x sums (see the oracle for the exact sequence);
+//   * the per-chunk partials of TR rows x M columns are reduced across the warp with a
+//     reduce-scatter (one shuffle + add per value) and across warps in shared memory.
+// The fp32 operation order is the one of oracle/qmtp_oracle.c:qo_qmv_affine / qo_qmv_nvfp4.
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace qmtp {
+
+enum QFmt { FMT_AFFINE = 0, FMT_NVFP4 = 1 };
+
+template <int FMT, int M, int W, int TR, int NS>
+struct QmvCfg {
+  static constexpr int K = W * 1024;
+  static constexpr int WB = K / 2;                               // weight bytes per row
+  static constexpr int SB = (FMT == FMT_AFFINE) ? K / 32 : K / 16;  // scale bytes per row
+  static constexpr int BB = (FMT == FMT_AFFINE) ? K / 32 : 0;       // bias bytes per row
+  static constexpr int NV = TR * M;
+  static constexpr int VP = NV <= 1 ? 1 : NV <= 2 ? 2 : NV <= 4 ? 4 : NV <= 8 ? 8 : NV <= 16 ? 16 : 32;
+  static_assert(NV <= 32, "TR*M must be <= 32");
+  static constexpr int OFF_S = NS * TR * WB;
+  static constexpr int OFF_B = OFF_S + NS * TR * SB;
+  static constexpr int OFF_RED = OFF_B + NS * TR * BB;
+  static constexpr int OFF_BAR = OFF_RED + 2 * W * VP * 4;
+  static constexpr int SMEM = OFF_BAR + NS * 8;
+};
+
+// Unpacks the 8 nibbles of word w into exact floats: even nibbles as 2048+q, odd ones as 128+q.
+__device__ __forceinline__ void unpack_affine(uint32_t w, float (&f)[8]) {
+  const uint32_t a12 = w << 12, a4 = w << 4, b4 = w >> 4, b12 = w >> 12;
+  f[0] = __uint_as_float((a12 & 0x0000F000u) | 0x45000000u);
+  f[1] = __uint_as_float((a12 & 0x000F0000u) | 0x43000000u);
+  f[2] = __uint_as_float((a4 & 0x0000F000u) | 0x45000000u);
+  f[3] = __uint_as_float((a4 & 0x000F0000u) | 0x43000000u);
+  f[4] = __uint_as_float((b4 & 0x0000F000u) | 0x45000000u);
+  f[5] = __uint_as_float((b4 & 0x000F0000u) | 0x43000000u);
+  f[6] = __uint_as_float((b12 & 0x0000F000u) | 0x45000000u);
+  f[7] = __uint_as_float((b12 & 0x000F0000u) | 0x43000000u);
+}
+
+// e2m1 pair -> two floats scaled by 2^-14 (half-precision bit trick of qmv_kernel.py:16-25):
+// nibble j and j+4 of w sit in the low / high 16 bits after `w >> 4j`.
+__device__ __forceinline__ void unpack_e2m1(uint32_t w, float (&f)[8]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t t = w >> (4 * j);
+    const uint32_t h2 = ((t & 0x00070007u) << 9) | ((t & 0x00080008u) << 12);
+    f[j] = __half2float(__ushort_as_half(uint16_t(h2 & 0xFFFFu)));
+    f[j + 4] = __half2float(__ushort_as_half(uint16_t(h2 >> 16)));
+  }
+}
+
+__device__ __forceinline__ float e4m3_x16k(uint32_t s) {
+  // e4m3 value * 2^14 (sign ignored): half bits (s & 0x7f) << 7 is value * 2^-8; times 2^22.
+  return __fmul_rn(__half2float(__ushort_as_half(uint16_t((s & 0x7Fu) << 7))), 4194304.0f);
+}
+
+template <int FMT, int M, int W, int TR, int NS>
+__global__ void __launch_bounds__(W * 32)
+qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
+           const uint8_t* __restrict__ sc, const uint8_t* __restrict__ bi,
+           uint16_t* __restrict__ y, int N, int ldy, unsigned* __restrict__ err) {
+  using C = QmvCfg<FMT, M, W, TR, NS>;
+  constexpr int K = C::K;
+  extern __shared__ __align__(128) unsigned char smem[];
+  float* s_red = reinterpret_cast<float*>(smem + C::OFF_RED);
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = warp * 32 + lane;  // this thread's K-chunk
+  const int r0 = int((long long)blockIdx.x * N / gridDim.x);
+  const int r1 = int((long long)(blockIdx.x + 1) * N / gridDim.x);
+  const int nrows = r1 - r0;
+  const int ntiles = (nrows + TR - 1) / TR;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < NS; ++s) mbar_init(&s_bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const uint64_t pol = policy_evict_first();
+  auto issue = [&](int t) {
+    const int s = t % NS;
+    const int rows = min(TR, nrows - t * TR);
+    const size_t row = size_t(r0) + size_t(t) * TR;
+    mbar_expect_tx(&s_bar[s], uint32_t(rows * (C::WB + C::SB + C::BB)));
+    bulk_g2s(smem + s * TR * C::WB, reinterpret_cast<const uint8_t*>(wq) + row * C::WB, rows * C::WB,
+             &s_bar[s], pol);
+    bulk_g2s(smem + C::OFF_S + s * TR * C::SB, sc + row * C::SB, rows * C::SB, &s_bar[s], pol);
+    if constexpr (FMT == FMT_AFFINE)
+      bulk_g2s(smem + C::OFF_B + s * TR * C::BB, bi + row * C::BB, rows * C::BB, &s_bar[s], pol);
+  };
+  if (tid == 0) {
+    const int pre = min(NS - 1, ntiles);
+    for (int t = 0; t < pre; ++t) issue(t);
+  }
+
+  // x prologue: this thread's 32 elements of every row m, plus the per-chunk offset sums.
+  float xv[M][32];
+  float nce[M], nco[M], xsum[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const uint16_t* xp = x + size_t(m) * K + 32 * c;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 u = *reinterpret_cast<const uint4*>(xp + 8 * q);
+      xv[m][8 * q + 0] = bflo(u.x); xv[m][8 * q + 1] = bfhi(u.x);
+      xv[m][8 * q + 2] = bflo(u.y); xv[m][8 * q + 3] = bfhi(u.y);
+      xv[m][8 * q + 4] = bflo(u.z); xv[m][8 * q + 5] = bfhi(u.z);
+      xv[m][8 * q + 6] = bflo(u.w); xv[m][8 * q + 7] = bfhi(u.w);
+    }
+    if constexpr (FMT == FMT_AFFINE) {
+      float xe = 0.0f, xo = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) { xe = __fadd_rn(xe, xv[m][j]); xo = __fadd_rn(xo, xv[m][j + 1]); }
+      nce[m] = -__fmul_rn(2048.0f, xe);
+      nco[m] = -__fmul_rn(128.0f, xo);
+      xsum[m] = __fadd_rn(xe, xo);
+    } else {
+      nce[m] = nco[m] = xsum[m] = 0.0f;
+    }
+  }
+
+  bool abort = false;
+  for (int t = 0; t < ntiles && !abort; ++t) {
+    if (tid == 0 && t + NS - 1 < ntiles) {
+      fence_proxy_async();
+      issue(t + NS - 1);
+    }
+    const int s = t % NS;
+    const bool ok = mbar_wait_bounded(&s_bar[s], uint32_t((t / NS) & 1), err);
+    const int rows = min(TR, nrows - t * TR);
+
+    float val[C::VP];
+#pragma unroll
+    for (int i = 0; i < C::VP; ++i) val[i] = 0.0f;
+    if (ok) {
+      const unsigned char* sw = smem + s * TR * C::WB;
+#pragma unroll
+      for (int r = 0; r < TR; ++r) {
+        if (r < rows) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(sw + r * C::WB + c * 16);
+          const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+          if constexpr (FMT == FMT_AFFINE) {
+            const uint16_t* ss = reinterpret_cast<const uint16_t*>(smem + C::OFF_S + s * TR * C::SB + r * C::SB);
+            const uint16_t* bb = reinterpret_cast<const uint16_t*>(smem + C::OFF_B + s * TR * C::BB + r * C::BB);
+            const float sv = bf2f(ss[c >> 1]), bv = bf2f(bb[c >> 1]);
+            float ae[M], ao[M];
+#pragma unroll
+            for (int m = 0; m < M; ++m) { ae[m] = nce[m]; ao[m] = nco[m]; }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float f[8];
+              unpack_affine(wd[q], f);
+#pragma unroll
+              for (int j = 0; j < 8; j += 2) {
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                  ae[m] = __fmaf_rn(f[j], xv[m][8 * q + j], ae[m]);
+                  ao[m] = __fmaf_rn(f[j + 1], xv[m][8 * q + j + 1], ao[m]);
+                }
+              }
+            }
+#pragma unroll
+            for (int m = 0; m < M; ++m)
+              val[r * M + m] = __fmaf_rn(bv, xsum[m], __fmul_rn(sv, __fadd_rn(ae[m], ao[m])));
+          } else {
+            const uint8_t* ss = smem + C::OFF_S + s * TR * C::SB + r * C::SB;
+            const float s0 = e4m3_x16k(ss[2 * c]), s1 = e4m3_x16k(ss[2 * c + 1]);
+            float T[2][M];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              float ae[M], ao[M];
+#pragma unroll
+              for (int m = 0; m < M; ++m) { ae[m] = 0.0f; ao[m] = 0.0f; }
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                float f[8];
+                unpack_e2m1(wd[2 * h + q], f);  // f[n] = nibble n of the word, times 2^-14
+#pragma unroll
+                for (int jj = 0; jj < 8; jj += 2) {
+#pragma unroll
+                  for (int m = 0; m < M; ++m) {
+                    ae[m] = __fmaf_rn(f[jj], xv[m][16 * h + 8 * q + jj], ae[m]);
+                    ao[m] = __fmaf_rn(f[jj + 1], xv[m][16 * h + 8 * q + jj + 1], ao[m]);
+                  }
+                }
+              }
+#pragma unroll
+              for (int m = 0; m < M; ++m) T[h][m] = __fadd_rn(ae[m], ao[m]);
+            }
+#pragma unroll
+            for (int m = 0; m < M; ++m) val[r * M + m] = __fmaf_rn(s1, T[1][m], __fmul_rn(s0, T[0][m]));
+          }
+        }
+      }
+    }
+    int idx;
+    bool owner;
+    warp_reduce_scatter<C::VP>(val, lane, idx, owner);
+    float* red = s_red + (t & 1) * W * C::VP;
+    if (owner) red[warp * C::VP + idx] = val[0];
+    abort = __syncthreads_or(!ok) != 0;
+    if (!abort && tid < rows * M) {
+      float acc = red[tid];
+#pragma unroll
+      for (int w = 1; w < W; ++w) acc = __fadd_rn(acc, red[w * C::VP + tid]);
+      const int r = tid / M, m = tid - (tid / M) * M;
+      y[size_t(m) * ldy + r0 + t * TR + r] = f2bf(acc);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------- launchers
+template <int FMT, int M, int W>
+static int launch_qmv(const void* x, const void* w, const void* s, const void* b, void* y, int N, int ldy,
+                      cudaStream_t st) {
+  constexpr int TR = (W <= 4) ? 8 : 4;
+  constexpr int NS = 4;
+  using C = QmvCfg<FMT, M, W, TR, NS>;
+  auto kern = qmv_kernel<FMT, M, W, TR, NS>;
+  static int occ = -1;
+  static std::once_flag once;
+  std::call_once(once, [&] {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess) return;
+    int o = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, W * 32, C::SMEM) != cudaSuccess) return;
+    occ = o;
+  });
+  if (occ <= 0) return QMTP_ERR_CUDA;
+  const int grid = std::max(1, std::min(N, sm_count() * occ));
+  kern<<<grid, W * 32, C::SMEM, st>>>(static_cast<const uint16_t*>(x), static_cast<const uint32_t*>(w),
+                                        static_cast<const uint8_t*>(s), static_cast<const uint8_t*>(b),
+                                        static_cast<uint16_t*>(y), N, ldy, device_error_ptr());
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+template <int FMT, int M>
+static int dispatch_w(int K, const void* x, const void* w, const void* s, const void* b, void* y, int N, int ldy,
+                      cudaStream_t st) {
+  switch (K) {
+    case 1024: return launch_qmv<FMT, M, 1>(x, w, s, b, y, N, ldy, st);
+    case 2048: return launch_qmv<FMT, M, 2>(x, w, s, b, y, N, ldy, st);
+    case 4096: return launch_qmv<FMT, M, 4>(x, w, s, b, y, N, ldy, st);
+    case 8192: return launch_qmv<FMT, M, 8>(x, w, s, b, y, N, ldy, st);
+    case 12288: return launch_qmv<FMT, M, 12>(x, w, s, b, y, N, ldy, st);
+    default: return QMTP_ERR_SHAPE;
+  }
+}
+
+template <int FMT>
+static int qmv_entry(const void* x, const void* w, const void* s, const void* b, void* y, int M, int N, int K,
+                     int ldy, void* stream) {
+  if (!x || !w || !s || !y || (FMT == FMT_AFFINE && !b)) return QMTP_ERR_ARG;
+  if (M < 1 || N < 1 || K < 1024 || K % 1024 != 0 || K > 12288 || ldy < N) return QMTP_ERR_SHAPE;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(s) || (b && !aligned16(b))) return QMTP_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint16_t* xp = static_cast<const uint16_t*>(x);
+  uint16_t* yp = static_cast<uint16_t*>(y);
+  for (int m0 = 0; m0 < M; m0 += 4) {
+    const int mm = std::min(4, M - m0);
+    const void* xm = xp + size_t(m0) * K;
+    void* ym = yp + size_t(m0) * ldy;
+    int rc;
+    switch (mm) {
+      case 1: rc = dispatch_w<FMT, 1>(K, xm, w, s, b, ym, N, ldy, st); break;
+      case 2: rc = dispatch_w<FMT, 2>(K, xm, w, s, b, ym, N, ldy, st); break;
+      case 3: rc = dispatch_w<FMT, 3>(K, xm, w, s, b, ym, N, ldy, st); break;
+      default: rc = dispatch_w<FMT, 4>(K, xm, w, s, b, ym, N, ldy, st); break;
+    }
+    if (rc != QMTP_OK) return rc;
+  }
+  return QMTP_OK;
+}
+
+// ----------------------------------------------------------------------------- quantizer
+// One warp per (row, group of 64): lane l holds elements 2l, 2l+1.  min/max are exact, so any
+// reduction order gives the oracle's values; the rest is elementwise.
+__global__ void quantize_affine_kernel(const uint16_t* __restrict__ w, uint32_t* __restrict__ wq,
+                                       uint16_t* __restrict__ sc, uint16_t* __restrict__ bi, int N, int K) {
+  const int G = K / 64;
+  const long long gid = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x / 32);
+  if (gid >= (long long)N * G) return;
+  const int lane = threadIdx.x & 31;
+  const int n = int(gid / G), g = int(gid - (long long)n * G);
+  const uint32_t pair = reinterpret_cast<const uint32_t*>(w + size_t(n) * K + size_t(g) * 64)[lane];
+  const float v0 = bflo(pair), v1 = bfhi(pair);
+  float mn = fminf(v0, v1), mx = fmaxf(v0, v1);
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, d));
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, d));
+  }
+  uint16_t sb = f2bf(__fdiv_rn(__fsub_rn(mx, mn), 15.0f));
+  if ((sb & 0x7FFFu) == 0) sb = 0x3F80;
+  const uint16_t bb = f2bf(__fadd_rn(mn, 0.0f));  // -0 -> +0
+  const float s = bf2f(sb), b = bf2f(bb);
+  float q0 = rintf(__fdiv_rn(__fsub_rn(v0, b), s));
+  float q1 = rintf(__fdiv_rn(__fsub_rn(v1, b), s));
+  q0 = fminf(fmaxf(q0, 0.0f), 15.0f);
+  q1 = fminf(fmaxf(q1, 0.0f), 15.0f);
+  // lanes 4i..4i+3 hold the 8 nibbles of word i (low nibble first)
+  uint32_t part = (uint32_t(q0) | (uint32_t(q1) << 4)) << (8 * (lane & 3));
+  part |= __shfl_xor_sync(0xFFFFFFFFu, part, 1);
+  part |= __shfl_xor_sync(0xFFFFFFFFu, part, 2);
+  if ((lane & 3) == 0) wq[(size_t(n) * K + size_t(g) * 64) / 8 + (lane >> 2)] = part;
+  if (lane == 0) {
+    sc[size_t(n) * G + g] = sb;
+    bi[size_t(n) * G + g] = bb;
+  }
+}
+
+}  // namespace qmtp
+
+using namespace qmtp;
+
+extern "C" int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const void* biases, void* y,
+                                   int M, int N, int K, int ldy, void* stream) {
+  return qmv_entry<FMT_AFFINE>(x, w, scales, biases, y, M, N, K, ldy, stream);
+}
+
+extern "C" int qmtp_qmv_nvfp4_g16(const void* x, const void* w, const void* scales, void* y, int M, int N, int K,
+                                  int ldy, void* stream) {
+  return qmv_entry<FMT_NVFP4>(x, w, scales, nullptr, y, M, N, K, ldy, stream);
+}
+
+extern "C" int qmtp_quantize_affine_g64(const void* w, void* wq, void* scales, void* biases, int N, int K,
+                                        void* stream) {
+  if (!w || !wq || !scales || !biases) return QMTP_ERR_ARG;
+  if (N < 1 || K < 64 || K % 64 != 0) return QMTP_ERR_SHAPE;
+  if (!aligned16(w) || !aligned16(wq)) return QMTP_ERR_ALIGN;
+  const long long groups = (long long)N * (K / 64);
+  const int wpb = 8;
+  const long long blocks = (groups + wpb - 1) / wpb;
+  if (blocks > 0x7FFFFFFFLL) return QMTP_ERR_SHAPE;
+  quantize_affine_kernel<<<unsigned(blocks), wpb * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(w), static_cast<uint32_t*>(wq), static_cast<uint16_t*>(scales),
+      static_cast<uint16_t*>(biases), N, K);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}

@@ -1,0 +1,101 @@
+"""ctypes binding of libqmtp.so (the C ABI declared in include/qmtp.h).
+
+The shared library sits next to this file and is built by ``qwen-mtp-mac_b200/build.py``.  There is
+no CPU or library fallback: if the library cannot be loaded, or no CUDA device is present, every
+op raises.  Arguments cross the boundary as plain device pointers, ints and the raw cudaStream_t of
+torch's current stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libqmtp.so"
+
+QMTP_OK = 0
+_ERRORS = {
+    -1: ValueError,  # QMTP_ERR_SHAPE
+    -2: ValueError,  # QMTP_ERR_ALIGN
+    -3: NotImplementedError,  # QMTP_ERR_UNSUPPORTED
+    -4: RuntimeError,  # QMTP_ERR_CUDA
+    -5: ValueError,  # QMTP_ERR_ARG
+}
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_U64 = ctypes.c_uint64
+_F = ctypes.c_float
+
+# name -> argtypes (every entry point returns int)
+SIGNATURES: dict[str, list] = {
+    "qmtp_version": [],
+    "qmtp_device_error": [ctypes.POINTER(ctypes.c_uint), _I],
+    "qmtp_qmv_affine_g64": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "qmtp_qmv_nvfp4_g16": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "qmtp_quantize_affine_g64": [_P, _P, _P, _P, _I, _I, _P],
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class LibraryUnavailable(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libqmtp.so once; raises LibraryUnavailable if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise LibraryUnavailable(
+                    f"{LIB_PATH} not built; run `python qwen-mtp-mac_b200/build.py` (no CPU fallback exists)")
+            L = ctypes.CDLL(str(LIB_PATH))
+            for name, args in SIGNATURES.items():
+                f = getattr(L, name)
+                f.argtypes = args
+                f.restype = _I
+            L.qmtp_strerror.argtypes = [_I]
+            L.qmtp_strerror.restype = ctypes.c_char_p
+            _lib = L
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return [*SIGNATURES, "qmtp_strerror"]
+
+
+def check(rc: int, what: str) -> None:
+    if rc != QMTP_OK:
+        msg = lib().qmtp_strerror(rc).decode()
+        raise _ERRORS.get(rc, RuntimeError)(f"{what}: {msg} (code {rc})")
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("qmtp ops run on CUDA tensors only (no CPU fallback)")
+        if not t.is_contiguous():
+            raise ValueError("qmtp ops need contiguous tensors")
+
+
+def stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def device_error(clear: bool = True) -> int:
+    v = ctypes.c_uint(0)
+    check(lib().qmtp_device_error(ctypes.byref(v), int(clear)), "qmtp_device_error")
+    return v.value

@@ -1,0 +1,106 @@
+"""Multi-row 4-bit quantized GEMV on B200 -- the qmv_kernel.py surface of qwen-mtp-mac.
+
+Reference: qmv_kernel.py:86-101 (``qmv_nvfp4(x, w, s, rows=None, nsg=1)``), qmv_kernel.py:104-120
+(the ``QuantizedLinear.__call__`` patch and ``install``) and MLX's
+``quantized_matmul(x, w, scales, biases, transpose=True, group_size=64, bits=4)`` for the affine
+format the B200 build is judged on.
+
+Every call runs the sm_100a kernel of libqmtp (csrc/qmv.cu).  Unlike the reference there is no
+"fall back to the library path" branch: the kernel reads each weight once for any number of rows,
+so ``install`` only records the row window for API compatibility.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+MIN_ROWS, MAX_ROWS = 3, 4  # reference defaults (qmv_kernel.py:105); informational here
+GROUP_SIZE = 64
+
+
+def _flat(x: torch.Tensor):
+    K = x.shape[-1]
+    return x.reshape(-1, K), K
+
+
+def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "affine"):
+    """``mx.quantize`` for the affine 4-bit group-64 format: bf16 [N, K] -> (wq uint32 [N, K/8],
+    scales bf16 [N, K/64], biases bf16 [N, K/64]).  Runs on the GPU (libqmtp quantizer)."""
+    if mode != "affine" or bits != 4 or group_size != 64:
+        raise NotImplementedError("only affine 4-bit group-64 quantization is implemented on the GPU")
+    _lib.require_cuda(w)
+    if w.dtype != torch.bfloat16 or w.dim() != 2:
+        raise ValueError("quantize expects a 2-D bf16 tensor")
+    N, K = w.shape
+    wq = torch.empty((N, K // 8), dtype=torch.int32, device=w.device)
+    sc = torch.empty((N, K // 64), dtype=torch.bfloat16, device=w.device)
+    bi = torch.empty((N, K // 64), dtype=torch.bfloat16, device=w.device)
+    _lib.check(_lib.lib().qmtp_quantize_affine_g64(w.data_ptr(), wq.data_ptr(), sc.data_ptr(), bi.data_ptr(),
+                                                    N, K, _lib.stream()), "quantize")
+    return wq, sc, bi
+
+
+def qmv_affine(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+               group_size: int = 64, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ dequant(w).T for the affine 4-bit group-64 format (bf16 in, bf16 out).
+    x: [..., K] bf16; w: uint32/int32 [N, K/8]; scales, biases: bf16 [N, K/64] -> [..., N]."""
+    if group_size != 64:
+        raise NotImplementedError("affine qmv is implemented for group_size=64")
+    xf, K = _flat(x)
+    N = w.shape[0]
+    M = xf.shape[0]
+    if x.dtype != torch.bfloat16:
+        raise ValueError("qmv_affine expects bf16 activations")
+    _lib.require_cuda(xf, w, scales, biases)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    _lib.check(_lib.lib().qmtp_qmv_affine_g64(xf.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                                               out.data_ptr(), M, N, K, out.shape[-1], _lib.stream()), "qmv_affine")
+    return out.reshape(*x.shape[:-1], N)
+
+
+def qmv_nvfp4(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, rows=None, nsg=1) -> torch.Tensor:
+    """Reference signature (qmv_kernel.py:86): x [..., K] bf16, w uint32 [N, K/8] e2m1 nibbles,
+    s uint8 [N, K/16] e4m3 scales -> [..., N].  ``rows``/``nsg`` were Metal tiling knobs; the B200
+    kernel picks its own tiling, so they are accepted and ignored."""
+    xf, K = _flat(x)
+    N = w.shape[0]
+    M = xf.shape[0]
+    _lib.require_cuda(xf, w, s)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    _lib.check(_lib.lib().qmtp_qmv_nvfp4_g16(xf.data_ptr(), w.data_ptr(), s.data_ptr(), out.data_ptr(), M, N, K,
+                                              N, _lib.stream()), "qmv_nvfp4")
+    return out.reshape(*x.shape[:-1], N)
+
+
+class QuantizedLinear:
+    """Bias-free 4-bit linear layer (the module the reference patches, qmv_kernel.py:108-113)."""
+
+    def __init__(self, weight, scales, biases=None, group_size=64, bits=4, mode="affine"):
+        self.weight, self.scales, self.biases = weight, scales, biases
+        self.group_size, self.bits, self.mode = group_size, bits, mode
+        self.out_features = weight.shape[0]
+        self.in_features = weight.shape[1] * 8
+
+    @classmethod
+    def from_linear(cls, w_bf16: torch.Tensor, group_size=64, bits=4, mode="affine"):
+        wq, s, b = quantize(w_bf16, group_size, bits, mode)
+        return cls(wq, s, b, group_size, bits, mode)
+
+    def __call__(self, x, out=None):
+        if self.mode == "affine":
+            return qmv_affine(x, self.weight, self.scales, self.biases, self.group_size, out=out)
+        if self.mode == "nvfp4":
+            return qmv_nvfp4(x, self.weight, self.scales)
+        raise NotImplementedError(self.mode)
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.weight, self.scales, self.biases) if t is not None)
+
+
+def install(min_rows: int = 3, max_rows: int = 4) -> None:
+    """API parity with qmv_kernel.py:116.  Records the row window; QuantizedLinear here always uses
+    the B200 kernel (there is no second, slower path to route to)."""
+    global MIN_ROWS, MAX_ROWS
+    MIN_ROWS, MAX_ROWS = min_rows, max_rows

@@ -1,0 +1,98 @@
+"""qmv kernels (libqmtp, sm_100a) against the C oracle: bit-exact (GPU)."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops
+from tests._util import affine_layer, randn_bf16, to_np, to_torch
+
+pytestmark = pytest.mark.gpu
+G = Path(__file__).resolve().parent / "golden"
+
+
+def _run_affine(x, wq, s, b, dev, ldy=None):
+    from qmtp import qmv_kernel
+
+    xt, wt, st, bt = (to_torch(a, dev) for a in (x, wq, s, b))
+    if ldy is None:
+        return to_np(qmv_kernel.qmv_affine(xt, wt, st, bt))
+    out = torch.full((x.shape[0], ldy), 7.0, dtype=torch.bfloat16, device=dev)
+    qmv_kernel.qmv_affine(xt, wt, st, bt, out=out)
+    return to_np(out)
+
+
+@pytest.mark.parametrize("K", [1024, 2048, 4096, 8192, 12288])
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+def test_qmv_affine_bit_exact(K, M, dev):
+    for N in (1, 37, 1000):
+        _, wq, s, b = affine_layer(N, K, seed=K + N)
+        x = randn_bf16((M, K), M)
+        assert np.array_equal(_run_affine(x, wq, s, b, dev), ops.qmv_affine(x, wq, s, b)), (K, M, N)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+def test_qmv_affine_config1_bit_exact(M, dev):
+    _, wq, s, b = affine_layer(12288, 4096, seed=0)
+    x = randn_bf16((M, 4096), 1)
+    assert np.array_equal(_run_affine(x, wq, s, b, dev), ops.qmv_affine(x, wq, s, b))
+
+
+def test_qmv_affine_many_rows_and_ldy(dev):
+    _, wq, s, b = affine_layer(333, 4096, seed=11)
+    x = randn_bf16((9, 4096), 12)
+    ref = ops.qmv_affine(x, wq, s, b)
+    got = _run_affine(x, wq, s, b, dev, ldy=400)
+    assert np.array_equal(got[:, :333], ref)
+    assert np.all(got[:, 333:] == ops.f32_to_bf16(np.float32([7.0]))[0])
+
+
+def test_qmv_affine_golden(dev):
+    d = np.load(G / "qmv.npz")
+    assert np.array_equal(_run_affine(d["x"], d["wq"], d["s"], d["b"], dev), d["y"])
+
+
+def test_qmv_nvfp4_bit_exact(dev):
+    from qmtp import qmv_kernel
+
+    d = np.load(G / "qmv.npz")
+    got = qmv_kernel.qmv_nvfp4(to_torch(d["x"], dev), to_torch(d["nq"], dev), to_torch(d["ns"], dev))
+    assert np.array_equal(to_np(got), d["ny"])
+    r = np.random.default_rng(3)
+    for M, K, N in ((1, 4096, 500), (3, 4096, 12288), (4, 12288, 64)):
+        nq = r.integers(0, 2 ** 32, (N, K // 8), dtype=np.uint64).astype(np.uint32)
+        ns = r.integers(54, 70, (N, K // 16), dtype=np.int64).astype(np.uint8)
+        x = randn_bf16((M, K), M + K)
+        got = qmv_kernel.qmv_nvfp4(to_torch(x, dev), to_torch(nq, dev), to_torch(ns, dev))
+        assert np.array_equal(to_np(got), ops.qmv_nvfp4(x, nq, ns)), (M, K, N)
+
+
+def test_quantize_bit_exact(dev):
+    from qmtp import qmv_kernel
+
+    w = randn_bf16((777, 4096), 21, 0.02)
+    wq, s, b = qmv_kernel.quantize(to_torch(w, dev))
+    rq, rs, rb = ops.quantize_affine(w)
+    assert np.array_equal(to_np(wq), rq) and np.array_equal(to_np(s), rs) and np.array_equal(to_np(b), rb)
+
+
+def test_qmv_rejects_bad_shapes(dev):
+    from qmtp import qmv_kernel
+
+    x = torch.zeros(2, 1000, dtype=torch.bfloat16, device=dev)
+    w = torch.zeros(8, 125, dtype=torch.int32, device=dev)
+    s = torch.zeros(8, 16, dtype=torch.bfloat16, device=dev)
+    with pytest.raises(ValueError):
+        qmv_kernel.qmv_affine(x, w, s, s)
+    xb = torch.zeros(2 * 1024 + 1, dtype=torch.bfloat16, device=dev)[1:].view(2, 1024)  # 2-byte offset
+    w = torch.zeros(8, 128, dtype=torch.int32, device=dev)
+    with pytest.raises(ValueError):
+        qmv_kernel.qmv_affine(xb, w, s, s)
+
+
+def test_no_device_error_recorded(dev):
+    from qmtp import _lib
+
+    torch.cuda.synchronize()
+    assert _lib.device_error(clear=True) == 0
