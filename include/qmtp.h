@@ -55,6 +55,12 @@ int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const 
 int qmtp_qmv_nvfp4_g16(const void* x, const void* w, const void* scales, void* y, int M, int N,
                        int K, int ldy, void* stream);
 
+/* Launch shape the qmv kernels use for (fmt 0 = affine g64, 1 = NVFP4 g16, M in 1..4, K):
+ * resident CTAs per SM, threads per CTA, dynamic shared memory, rows per pipeline stage.  The grid
+ * is min(N, SMs * ctas_per_sm).  Host-only query (first call per shape sets kernel attributes). */
+int qmtp_qmv_launch_info(int fmt, int M, int K, int* ctas_per_sm, int* threads, int* smem_bytes,
+                         int* rows_per_tile);
+
 /* Affine 4-bit group-64 quantizer (MLX mx.quantize(w, 64, 4) convention, min/max form; used by
  * the loader, qwen_ollama.py:45-50 / lm_head2.py:17):  w bf16 [N, K] -> wq uint32 [N, K/8],
  * scales, biases bf16 [N, K/64].  K % 64 == 0. */

@@ -216,26 +216,29 @@ QO_API void qo_quantize_affine(const uint16_t* w, uint32_t* wq, uint16_t* sc, ui
  * Reference op: MLX quantized_matmul(x, w, s, b, transpose=True, group_size=64, bits=4) and the
  * multi-row GEMV of qmv_kernel.py:31-75 (same weight layout; that kernel is the NVFP4 variant).
  *
- * Exact sequence.  K is cut into chunks of 32 (c = k/32); block i = chunks 32i..32i+31.
- *   x side, per (m, c):  Xe = sum_{j even} x_j, Xo = sum_{j odd} x_j  (sequential, j ascending),
- *                        Ce = 2048*Xe, Co = 128*Xo, Xc = Xe + Xo.
- *   weight side: nibble j of the chunk is read as f_j = 2048 + q_j (j even) or 128 + q_j (j odd),
- *                both exact floats (the kernel builds them with one AND/OR on the shifted word).
- *   ae = -Ce, ao = -Co; for j = 0,2,..,30: ae = fma(f_j, x_j, ae); ao = fma(f_j+1, x_j+1, ao).
- *   T = ae + ao  (= sum q_j x_j up to rounding);  P_c = fma(b_g, Xc, s_g * T), g = c/2.
+ * Exact sequence.  K is cut into chunks of 32 (c = k/32: four uint32 words w0..w3 of 8 nibbles,
+ * low nibble first); block i = chunks 32i..32i+31.  Every nibble is read as the exact value
+ * f = 128 + q (the kernel forms two of them, nibbles j and j+4, as one bf16 pair with a single
+ * AND/OR and multiplies with fma.rn.f32.bf16).  Each chunk has two accumulation lanes: lane h
+ * takes word h then word h+2; inside a word the order is j = 0, 4, 1, 5, 2, 6, 3, 7.
+ *   Sx_h = sum x over the lane's sequence (sequential fp32 adds from 0);
+ *   a_h = -(128 * Sx_h);  a_h = fma(128 + q_j, x_j, a_h) over the same sequence;
+ *   T = a_0 + a_1;  P_c = fma(b_g, Sx_0 + Sx_1, s_g * T), g = c/2.
  *   B_i = butterfly32(P_{32i..32i+31});  y = ((B_0 + B_1) + B_2) + ...;  out = bf16(y). */
 
-typedef struct { float ce, co, xc; } qo_xchunk;
+typedef struct { float sx[2]; } qo_xchunk;
+
+static const int qo_jorder[8] = {0, 4, 1, 5, 2, 6, 3, 7};
 
 static void qo_affine_xprep(const uint16_t* x, int K, float* xf, qo_xchunk* xc) {
   for (int k = 0; k < K; ++k) xf[k] = qo_bf2f(x[k]);
   for (int c = 0; c < K / 32; ++c) {
-    const float* v = xf + 32 * c;
-    float xe = 0.0f, xo = 0.0f;
-    for (int j = 0; j < 32; j += 2) { xe = xe + v[j]; xo = xo + v[j + 1]; }
-    xc[c].ce = 2048.0f * xe;
-    xc[c].co = 128.0f * xo;
-    xc[c].xc = xe + xo;
+    for (int h = 0; h < 2; ++h) {
+      float sx = 0.0f;
+      for (int wi = h; wi < 4; wi += 2)
+        for (int t = 0; t < 8; ++t) sx = sx + xf[32 * c + 8 * wi + qo_jorder[t]];
+      xc[c].sx[h] = sx;
+    }
   }
 }
 
@@ -247,20 +250,21 @@ static float qo_affine_row(const float* xf, const qo_xchunk* xc, const uint32_t*
     float P[32];
     for (int l = 0; l < 32; ++l) {
       int c = 32 * i + l;
-      const float* v = xf + 32 * c;
-      float ae = -xc[c].ce, ao = -xc[c].co;
-      for (int wd = 0; wd < 4; ++wd) {
-        uint32_t w = wrow[4 * c + wd];
-        for (int jj = 0; jj < 8; jj += 2) {
-          float fe = 2048.0f + (float)((w >> (4 * jj)) & 15u);
-          float fo = 128.0f + (float)((w >> (4 * jj + 4)) & 15u);
-          ae = fmaf(fe, v[8 * wd + jj], ae);
-          ao = fmaf(fo, v[8 * wd + jj + 1], ao);
+      float a[2];
+      for (int h = 0; h < 2; ++h) {
+        float acc = -(128.0f * xc[c].sx[h]);
+        for (int wi = h; wi < 4; wi += 2) {
+          uint32_t w = wrow[4 * c + wi];
+          for (int t = 0; t < 8; ++t) {
+            int j = qo_jorder[t];
+            acc = fmaf(128.0f + (float)((w >> (4 * j)) & 15u), xf[32 * c + 8 * wi + j], acc);
+          }
         }
+        a[h] = acc;
       }
-      float T = ae + ao;
+      float T = a[0] + a[1];
       float s = qo_bf2f(srow[c >> 1]), b = qo_bf2f(brow[c >> 1]);
-      P[l] = fmaf(b, xc[c].xc, s * T);
+      P[l] = fmaf(b, xc[c].sx[0] + xc[c].sx[1], s * T);
     }
     float B = qo_butterfly32(P);
     y = (i == 0) ? B : y + B;
@@ -338,3 +342,205 @@ QO_API int qo_qmv_nvfp4(const uint16_t* x, const uint32_t* wq, const uint8_t* sc
 /* ------------------------------------------------------------------ array helpers (tests) */
 QO_API void qo_exp_arr(const float* x, float* y, long n) { for (long i = 0; i < n; ++i) y[i] = qo_expf(x[i]); }
 QO_API void qo_log_arr(const float* x, float* y, long n) { for (long i = 0; i < n; ++i) y[i] = qo_logf(x[i]); }
+
+/* ------------------------------------------------------------------ GatedDeltaNet
+ * Lane structure of the reference kernels (gdn_kernel.py:11-64, gdn_fused.py:43-112): one
+ * simdgroup per (batch, value head, dv row); lane l owns dk elements [NP*l, NP*l+NP) (NP = Dk/32),
+ * sums its elements sequentially and the 32 lane partials are combined (here: xor butterfly). */
+
+static inline float qo_lane_dot(const float* a, const float* b, int NP, int Dk) {
+  /* sum over Dk of a*b: lane-sequential fmaf, then butterfly */
+  float P[32];
+  for (int l = 0; l < 32; ++l) {
+    float acc = 0.0f;
+    for (int i = 0; i < NP; ++i) acc = fmaf(a[NP * l + i], b[NP * l + i], acc);
+    P[l] = acc;
+  }
+  (void)Dk;
+  return qo_butterfly32(P);
+}
+
+/* One dv row of the delta rule over T tokens (state row st[Dk] updated in place).
+ *   st *= g; kv = sum st*k; delta = (v - kv)*beta; st += k*delta; o = sum st*q.
+ * Per lane and element i: st_i = st_i * g; kv = fma(st_i, k_i, kv) (interleaved, gdn_kernel.py:37-42);
+ * then st_i = fma(k_i, delta, st_i); o = fma(st_i, q_i, o) (gdn_kernel.py:45-50). */
+static void qo_gdn_row(float* st, int Dk, int T, const float* q, const float* k, int qk_stride,
+                       const float* v, int v_stride, const float* g, const float* beta, int gb_stride,
+                       float* y, int y_stride, float* mid, size_t mid_stride) {
+  int NP = Dk / 32;
+  for (int t = 0; t < T; ++t) {
+    const float* qt = q + (size_t)t * qk_stride;
+    const float* kt = k + (size_t)t * qk_stride;
+    float gt = g[(size_t)t * gb_stride], bt = beta[(size_t)t * gb_stride];
+    float P[32];
+    for (int l = 0; l < 32; ++l) {
+      float kv = 0.0f;
+      for (int i = 0; i < NP; ++i) {
+        int e = NP * l + i;
+        st[e] = st[e] * gt;
+        kv = fmaf(st[e], kt[e], kv);
+      }
+      P[l] = kv;
+    }
+    float kvm = qo_butterfly32(P);
+    float delta = (v[(size_t)t * v_stride] - kvm) * bt;
+    for (int l = 0; l < 32; ++l) {
+      float o = 0.0f;
+      for (int i = 0; i < NP; ++i) {
+        int e = NP * l + i;
+        st[e] = fmaf(kt[e], delta, st[e]);
+        o = fmaf(st[e], qt[e], o);
+      }
+      P[l] = o;
+    }
+    y[(size_t)t * y_stride] = qo_butterfly32(P);
+    if (mid && t < T - 1) memcpy(mid + (size_t)t * mid_stride, st, sizeof(float) * Dk);
+  }
+}
+
+/* gated_delta_snapshot (gdn_kernel.py:75-88): q,k bf16 [B,T,Hk,Dk]; v bf16 [B,T,Hv,Dv];
+ * g, beta fp32 [B,T,Hv]; state fp32 [B,Hv,Dv,Dk] -> y bf16 [B,T,Hv,Dv], state_out, state_mid
+ * fp32 [T-1,B,Hv,Dv,Dk]. */
+QO_API int qo_gdn_step(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,
+                       const float* beta, const float* state_in, uint16_t* y, float* state_out,
+                       float* state_mid, int B, int T, int Hk, int Hv, int Dk, int Dv) {
+  if (Dk % 32 != 0 || Hv % Hk != 0 || T < 1) return -1;
+  size_t per = (size_t)B * Hv * Dv * Dk;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int n = 0; n < B * Hv; ++n) {
+    for (int dv = 0; dv < Dv; ++dv) {
+      int b = n / Hv, hv = n % Hv, hk = hv / (Hv / Hk);
+      float* qf = (float*)malloc(sizeof(float) * (size_t)T * Dk * 2);
+      float* kf = qf + (size_t)T * Dk;
+      float* vf = (float*)malloc(sizeof(float) * T);
+      float* yf = (float*)malloc(sizeof(float) * T);
+      float* gt = (float*)malloc(sizeof(float) * T * 2);
+      float* bt = gt + T;
+      for (int t = 0; t < T; ++t) {
+        for (int e = 0; e < Dk; ++e) {
+          size_t qi = (((size_t)b * T + t) * Hk + hk) * Dk + e;
+          qf[(size_t)t * Dk + e] = qo_bf2f(q[qi]);
+          kf[(size_t)t * Dk + e] = qo_bf2f(k[qi]);
+        }
+        vf[t] = qo_bf2f(v[(((size_t)b * T + t) * Hv + hv) * Dv + dv]);
+        gt[t] = g[((size_t)b * T + t) * Hv + hv];
+        bt[t] = beta[((size_t)b * T + t) * Hv + hv];
+      }
+      size_t row = ((size_t)n * Dv + dv) * Dk;
+      float* st = state_out + row;
+      memcpy(st, state_in + row, sizeof(float) * Dk);
+      qo_gdn_row(st, Dk, T, qf, kf, Dk, vf, 1, gt, bt, 1, yf, 1, state_mid ? state_mid + row : NULL, per);
+      for (int t = 0; t < T; ++t) y[(((size_t)b * T + t) * Hv + hv) * Dv + dv] = qo_f2bf(yf[t]);
+      free(qf); free(vf); free(yf); free(gt);
+    }
+  }
+  return 0;
+}
+
+/* gdn_core (gdn_fused.py:43-112), B = 1:
+ *   win bf16 [S+KC-1, C] (C = 2*Hk*Dk + Hv*Dv), conv_w bf16 [C, KC], a, b bf16 [S, Hv] (row stride
+ *   ld_ab), A_log fp32 [Hv], dt_bias bf16 [Hv], state fp32 [Hv, Dv, Dk]
+ *   -> y fp32 [S, Hv, Dv] (bf16-rounded values), state_out, state_mid fp32 [S-1, Hv, Dv, Dk].
+ * conv: acc = fma(w_j, win_{t+j}, acc) over taps j; q = silu_bf(R(acc)) ...
+ * q/k rms: ss = lane-sequential fma(x,x) + butterfly; r = 1/sqrt(ss/Dk + 1e-6);
+ * q = R(q*r)/Dk; k = R(R(k*r) * R(1/sqrt(Dk))); g = exp(-exp(A_log) * softplus_bf(R(a + dt_bias)));
+ * beta = sigmoid_bf(b). */
+static void qo_gdn_qk_prep(const float* xin /* [Dk] conv outputs (post silu) */, int Dk, int is_q, float* out) {
+  int NP = Dk / 32;
+  float P[32];
+  for (int l = 0; l < 32; ++l) {
+    float acc = 0.0f;
+    for (int i = 0; i < NP; ++i) acc = fmaf(xin[NP * l + i], xin[NP * l + i], acc);
+    P[l] = acc;
+  }
+  float ss = qo_butterfly32(P);
+  float r = 1.0f / sqrtf(ss / (float)Dk + 1e-6f);
+  float kscale = qo_R(1.0f / sqrtf((float)Dk));
+  for (int e = 0; e < Dk; ++e) {
+    if (is_q) out[e] = qo_R(xin[e] * r) / (float)Dk;
+    else out[e] = qo_R(qo_R(xin[e] * r) * kscale);
+  }
+}
+
+static inline float qo_conv_tap(const uint16_t* conv_w, const uint16_t* win, int C, int KC, int ch, int t) {
+  float acc = 0.0f;
+  for (int j = 0; j < KC; ++j) acc = fmaf(qo_bf2f(conv_w[(size_t)ch * KC + j]), qo_bf2f(win[(size_t)(t + j) * C + ch]), acc);
+  return acc;
+}
+
+QO_API int qo_gdn_fused(const uint16_t* win, const uint16_t* conv_w, const uint16_t* a, const uint16_t* b,
+                        int ld_ab, const float* A_log, const uint16_t* dt_bias, const float* state_in,
+                        float* y, float* state_out, float* state_mid, int S, int Hk, int Hv, int Dk,
+                        int Dv, int KC) {
+  if (Dk % 32 != 0 || Hv % Hk != 0 || S < 1) return -1;
+  int C = 2 * Hk * Dk + Hv * Dv;
+  /* q/k prep per (t, hk) */
+  float* qn = (float*)malloc(sizeof(float) * (size_t)S * Hk * Dk);
+  float* kn = (float*)malloc(sizeof(float) * (size_t)S * Hk * Dk);
+  float* tmp = (float*)malloc(sizeof(float) * Dk);
+  for (int t = 0; t < S; ++t) {
+    for (int hk = 0; hk < Hk; ++hk) {
+      for (int e = 0; e < Dk; ++e) tmp[e] = qo_silu_bf(qo_R(qo_conv_tap(conv_w, win, C, KC, hk * Dk + e, t)));
+      qo_gdn_qk_prep(tmp, Dk, 1, qn + ((size_t)t * Hk + hk) * Dk);
+      for (int e = 0; e < Dk; ++e) tmp[e] = qo_silu_bf(qo_R(qo_conv_tap(conv_w, win, C, KC, Hk * Dk + hk * Dk + e, t)));
+      qo_gdn_qk_prep(tmp, Dk, 0, kn + ((size_t)t * Hk + hk) * Dk);
+    }
+  }
+  free(tmp);
+  float* gt = (float*)malloc(sizeof(float) * (size_t)S * Hv * 2);
+  float* bt = gt + (size_t)S * Hv;
+  for (int t = 0; t < S; ++t)
+    for (int hv = 0; hv < Hv; ++hv) {
+      float A = -qo_expf(A_log[hv]);
+      float sp = qo_softplus_bf(qo_R(qo_bf2f(a[(size_t)t * ld_ab + hv]) + qo_bf2f(dt_bias[hv])));
+      gt[(size_t)t * Hv + hv] = qo_expf(A * sp);
+      bt[(size_t)t * Hv + hv] = qo_sigmoid_bf(qo_bf2f(b[(size_t)t * ld_ab + hv]));
+    }
+  size_t per = (size_t)Hv * Dv * Dk;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int hv = 0; hv < Hv; ++hv) {
+    for (int dv = 0; dv < Dv; ++dv) {
+      int hk = hv / (Hv / Hk);
+      int cv = 2 * Hk * Dk + hv * Dv + dv;
+      float vf[64], yf[64];
+      float gg[64], bb[64];
+      for (int t = 0; t < S && t < 64; ++t) {
+        vf[t] = qo_silu_bf(qo_R(qo_conv_tap(conv_w, win, C, KC, cv, t)));
+        gg[t] = gt[(size_t)t * Hv + hv];
+        bb[t] = bt[(size_t)t * Hv + hv];
+      }
+      size_t row = ((size_t)hv * Dv + dv) * Dk;
+      float* st = state_out + row;
+      memcpy(st, state_in + row, sizeof(float) * Dk);
+      qo_gdn_row(st, Dk, S, qn + (size_t)hk * Dk, kn + (size_t)hk * Dk, Hk * Dk, vf, 1, gg, bb, 1, yf, 1,
+                 state_mid ? state_mid + row : NULL, per);
+      for (int t = 0; t < S; ++t) y[((size_t)t * Hv + hv) * Dv + dv] = qo_R(yf[t]);
+    }
+  }
+  free(qn); free(kn); free(gt);
+  return 0;
+}
+
+/* gdn_norm_gate (gdn_fused.py:114-129): per (token, head) row of Dv:
+ *   r = 1/sqrt(sum(y^2)/Dv + eps) (lane-sequential fma + butterfly); xn = R(w * R(y*r));
+ *   out = bf16(xn * silu_f32(z)).  y fp32 [S, H, Dv], z bf16 [S, H*Dv] (row stride ld_z). */
+QO_API void qo_gdn_norm_gate(const float* y, const uint16_t* z, int ld_z, const uint16_t* w, uint16_t* out,
+                             int S, int H, int Dv, float eps) {
+  int NP = Dv / 32;
+  for (int t = 0; t < S; ++t)
+    for (int h = 0; h < H; ++h) {
+      const float* yr = y + ((size_t)t * H + h) * Dv;
+      float P[32];
+      for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int i = 0; i < NP; ++i) acc = fmaf(yr[NP * l + i], yr[NP * l + i], acc);
+        P[l] = acc;
+      }
+      float r = 1.0f / sqrtf(qo_butterfly32(P) / (float)Dv + eps);
+      for (int e = 0; e < Dv; ++e) {
+        float xn = qo_R(qo_bf2f(w[e]) * qo_R(yr[e] * r));
+        float zz = qo_bf2f(z[(size_t)t * ld_z + (size_t)h * Dv + e]);
+        out[(size_t)t * H * Dv + (size_t)h * Dv + e] = qo_f2bf(xn * qo_silu_f32(zz));
+      }
+    }
+}

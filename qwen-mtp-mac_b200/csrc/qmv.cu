@@ -14,6 +14,7 @@
 // The fp32 operation order is the one of oracle/qmtp_oracle.c:qo_qmv_affine / qo_qmv_nvfp4.
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -37,17 +38,23 @@ struct QmvCfg {
   static constexpr int SMEM = OFF_BAR + NS * 8;
 };
 
-// Unpacks the 8 nibbles of word w into exact floats: even nibbles as 2048+q, odd ones as 128+q.
-__device__ __forceinline__ void unpack_affine(uint32_t w, float (&f)[8]) {
-  const uint32_t a12 = w << 12, a4 = w << 4, b4 = w >> 4, b12 = w >> 12;
-  f[0] = __uint_as_float((a12 & 0x0000F000u) | 0x45000000u);
-  f[1] = __uint_as_float((a12 & 0x000F0000u) | 0x43000000u);
-  f[2] = __uint_as_float((a4 & 0x0000F000u) | 0x45000000u);
-  f[3] = __uint_as_float((a4 & 0x000F0000u) | 0x43000000u);
-  f[4] = __uint_as_float((b4 & 0x0000F000u) | 0x45000000u);
-  f[5] = __uint_as_float((b4 & 0x000F0000u) | 0x43000000u);
-  f[6] = __uint_as_float((b12 & 0x0000F000u) | 0x45000000u);
-  f[7] = __uint_as_float((b12 & 0x000F0000u) | 0x43000000u);
+// (a & b) | c as one LOP3 (written out: the C++ form costs an extra logic op per value).
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// acc = fma(a.lo, x.lo, acc); acc = fma(a.hi, x.hi, acc) with bf16 operands taken from the halves
+// of 32-bit registers and an fp32 accumulator (fma.rn.f32.bf16: single rounding, = fmaf on the
+// widened values).
+__device__ __forceinline__ void fma_bf16x2(float& acc, uint32_t a, uint32_t x) {
+  asm("{\n\t.reg .b16 a0, a1, x0, x1;\n\t"
+      "mov.b32 {a0, a1}, %1;\n\t"
+      "mov.b32 {x0, x1}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, a0, x0, %0;\n\t"
+      "fma.rn.f32.bf16 %0, a1, x1, %0;\n\t}"
+      : "+f"(acc)
+      : "r"(a), "r"(x));
 }
 
 // e2m1 pair -> two floats scaled by 2^-14 (half-precision bit trick of qmv_kernel.py:16-25):
@@ -62,13 +69,28 @@ __device__ __forceinline__ void unpack_e2m1(uint32_t w, float (&f)[8]) {
   }
 }
 
+// (lo, hi) float pairs in one 64-bit register pair, for fma.rn.f32x2 (two IEEE fp32 fmas).
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 __device__ __forceinline__ float e4m3_x16k(uint32_t s) {
   // e4m3 value * 2^14 (sign ignored): half bits (s & 0x7f) << 7 is value * 2^-8; times 2^22.
   return __fmul_rn(__half2float(__ushort_as_half(uint16_t((s & 0x7Fu) << 7))), 4194304.0f);
 }
 
 template <int FMT, int M, int W, int TR, int NS>
-__global__ void __launch_bounds__(W * 32)
+__global__ void __launch_bounds__(W * 32, 1)
 qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
            const uint8_t* __restrict__ sc, const uint8_t* __restrict__ bi,
            uint16_t* __restrict__ y, int N, int ldy, unsigned* __restrict__ err) {
@@ -109,29 +131,47 @@ qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
     for (int t = 0; t < pre; ++t) issue(t);
   }
 
-  // x prologue: this thread's 32 elements of every row m, plus the per-chunk offset sums.
-  float xv[M][32];
-  float nce[M], nco[M], xsum[M];
+  // x prologue (this thread's 32 elements of every row m).  Affine: bf16 pairs
+  // xb[m][4q + j] = (x[8q + j], x[8q + j + 4]) matching the nibble pairs of word q, the lane sums
+  // Sx_h, the initial accumulators -128*Sx_h and the chunk sum.  NVFP4: (even, odd) fp32 pairs.
+  uint32_t xb[M][16];
+  uint64_t xp[FMT == FMT_AFFINE ? 1 : M][16];
+  float a0init[M][2];
+  float xsum[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) {
-    const uint16_t* xp = x + size_t(m) * K + 32 * c;
+    const uint16_t* xg = x + size_t(m) * K + 32 * c;
+    uint4 u[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint4 u = *reinterpret_cast<const uint4*>(xp + 8 * q);
-      xv[m][8 * q + 0] = bflo(u.x); xv[m][8 * q + 1] = bfhi(u.x);
-      xv[m][8 * q + 2] = bflo(u.y); xv[m][8 * q + 3] = bfhi(u.y);
-      xv[m][8 * q + 4] = bflo(u.z); xv[m][8 * q + 5] = bfhi(u.z);
-      xv[m][8 * q + 6] = bflo(u.w); xv[m][8 * q + 7] = bfhi(u.w);
-    }
+    for (int q = 0; q < 4; ++q) u[q] = *reinterpret_cast<const uint4*>(xg + 8 * q);
     if constexpr (FMT == FMT_AFFINE) {
-      float xe = 0.0f, xo = 0.0f;
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) { xe = __fadd_rn(xe, xv[m][j]); xo = __fadd_rn(xo, xv[m][j + 1]); }
-      nce[m] = -__fmul_rn(2048.0f, xe);
-      nco[m] = -__fmul_rn(128.0f, xo);
-      xsum[m] = __fadd_rn(xe, xo);
+      for (int q = 0; q < 4; ++q) {
+        xb[m][4 * q + 0] = __byte_perm(u[q].x, u[q].z, 0x5410);
+        xb[m][4 * q + 1] = __byte_perm(u[q].x, u[q].z, 0x7632);
+        xb[m][4 * q + 2] = __byte_perm(u[q].y, u[q].w, 0x5410);
+        xb[m][4 * q + 3] = __byte_perm(u[q].y, u[q].w, 0x7632);
+      }
+      float sx[2] = {0.0f, 0.0f};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sx[q & 1] = __fadd_rn(sx[q & 1], bflo(xb[m][4 * q + j]));
+          sx[q & 1] = __fadd_rn(sx[q & 1], bfhi(xb[m][4 * q + j]));
+        }
+      a0init[m][0] = -__fmul_rn(128.0f, sx[0]);
+      a0init[m][1] = -__fmul_rn(128.0f, sx[1]);
+      xsum[m] = __fadd_rn(sx[0], sx[1]);
     } else {
-      nce[m] = nco[m] = xsum[m] = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t uu[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) xp[m][4 * q + h] = pack2(bflo(uu[h]), bfhi(uu[h]));
+      }
+      a0init[m][0] = a0init[m][1] = 0.0f;
+      xsum[m] = 0.0f;
     }
   }
 
@@ -150,62 +190,65 @@ qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
     for (int i = 0; i < C::VP; ++i) val[i] = 0.0f;
     if (ok) {
       const unsigned char* sw = smem + s * TR * C::WB;
+      // All TR rows are computed (rows past the tile end read stale stage data and are dropped),
+      // so the FMA chains of different rows interleave freely.
 #pragma unroll
       for (int r = 0; r < TR; ++r) {
-        if (r < rows) {
+        if constexpr (FMT == FMT_AFFINE) {
           const uint4 wv = *reinterpret_cast<const uint4*>(sw + r * C::WB + c * 16);
           const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
-          if constexpr (FMT == FMT_AFFINE) {
-            const uint16_t* ss = reinterpret_cast<const uint16_t*>(smem + C::OFF_S + s * TR * C::SB + r * C::SB);
-            const uint16_t* bb = reinterpret_cast<const uint16_t*>(smem + C::OFF_B + s * TR * C::BB + r * C::BB);
-            const float sv = bf2f(ss[c >> 1]), bv = bf2f(bb[c >> 1]);
-            float ae[M], ao[M];
+          const uint16_t* ss = reinterpret_cast<const uint16_t*>(smem + C::OFF_S + s * TR * C::SB + r * C::SB);
+          const uint16_t* bb = reinterpret_cast<const uint16_t*>(smem + C::OFF_B + s * TR * C::BB + r * C::BB);
+          const float sv = bf2f(ss[c >> 1]), bv = bf2f(bb[c >> 1]);
+          float a[M][2];
 #pragma unroll
-            for (int m = 0; m < M; ++m) { ae[m] = nce[m]; ao[m] = nco[m]; }
+          for (int m = 0; m < M; ++m) { a[m][0] = a0init[m][0]; a[m][1] = a0init[m][1]; }
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float f[8];
-              unpack_affine(wd[q], f);
+          for (int q = 0; q < 4; ++q) {
 #pragma unroll
-              for (int j = 0; j < 8; j += 2) {
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t pr = and_or(wd[q] >> (4 * j), 0x000F000Fu, 0x43004300u);  // (128+q_j, 128+q_j+4)
 #pragma unroll
-                for (int m = 0; m < M; ++m) {
-                  ae[m] = __fmaf_rn(f[j], xv[m][8 * q + j], ae[m]);
-                  ao[m] = __fmaf_rn(f[j + 1], xv[m][8 * q + j + 1], ao[m]);
-                }
-              }
+              for (int m = 0; m < M; ++m) fma_bf16x2(a[m][q & 1], pr, xb[m][4 * q + j]);
             }
-#pragma unroll
-            for (int m = 0; m < M; ++m)
-              val[r * M + m] = __fmaf_rn(bv, xsum[m], __fmul_rn(sv, __fadd_rn(ae[m], ao[m])));
-          } else {
-            const uint8_t* ss = smem + C::OFF_S + s * TR * C::SB + r * C::SB;
-            const float s0 = e4m3_x16k(ss[2 * c]), s1 = e4m3_x16k(ss[2 * c + 1]);
-            float T[2][M];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              float ae[M], ao[M];
-#pragma unroll
-              for (int m = 0; m < M; ++m) { ae[m] = 0.0f; ao[m] = 0.0f; }
-#pragma unroll
-              for (int q = 0; q < 2; ++q) {
-                float f[8];
-                unpack_e2m1(wd[2 * h + q], f);  // f[n] = nibble n of the word, times 2^-14
-#pragma unroll
-                for (int jj = 0; jj < 8; jj += 2) {
-#pragma unroll
-                  for (int m = 0; m < M; ++m) {
-                    ae[m] = __fmaf_rn(f[jj], xv[m][16 * h + 8 * q + jj], ae[m]);
-                    ao[m] = __fmaf_rn(f[jj + 1], xv[m][16 * h + 8 * q + jj + 1], ao[m]);
-                  }
-                }
-              }
-#pragma unroll
-              for (int m = 0; m < M; ++m) T[h][m] = __fadd_rn(ae[m], ao[m]);
-            }
-#pragma unroll
-            for (int m = 0; m < M; ++m) val[r * M + m] = __fmaf_rn(s1, T[1][m], __fmul_rn(s0, T[0][m]));
           }
+#pragma unroll
+          for (int m = 0; m < M; ++m)
+            val[r * M + m] = __fmaf_rn(bv, xsum[m], __fmul_rn(sv, __fadd_rn(a[m][0], a[m][1])));
+        } else {
+          const uint4 wv = *reinterpret_cast<const uint4*>(sw + r * C::WB + c * 16);
+          const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+          const uint8_t* ss = smem + C::OFF_S + s * TR * C::SB + r * C::SB;
+          const float s0 = e4m3_x16k(ss[2 * c]), s1 = e4m3_x16k(ss[2 * c + 1]);
+          float T[2][M];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint64_t acc[M];
+#pragma unroll
+            for (int m = 0; m < M; ++m) acc[m] = pack2(0.0f, 0.0f);
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              float f[8];
+              unpack_e2m1(wd[2 * h + q], f);  // f[n] = nibble n of the word, times 2^-14
+              const uint64_t f01 = pack2(f[0], f[1]), f23 = pack2(f[2], f[3]);
+              const uint64_t f45 = pack2(f[4], f[5]), f67 = pack2(f[6], f[7]);
+#pragma unroll
+              for (int m = 0; m < M; ++m) {
+                acc[m] = ffma2(f01, xp[m][8 * h + 4 * q + 0], acc[m]);
+                acc[m] = ffma2(f23, xp[m][8 * h + 4 * q + 1], acc[m]);
+                acc[m] = ffma2(f45, xp[m][8 * h + 4 * q + 2], acc[m]);
+                acc[m] = ffma2(f67, xp[m][8 * h + 4 * q + 3], acc[m]);
+              }
+            }
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+              float ae, ao;
+              unpack2(acc[m], ae, ao);
+              T[h][m] = __fadd_rn(ae, ao);
+            }
+          }
+#pragma unroll
+          for (int m = 0; m < M; ++m) val[r * M + m] = __fmaf_rn(s1, T[1][m], __fmul_rn(s0, T[0][m]));
         }
       }
     }
@@ -226,22 +269,31 @@ qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
 }
 
 // ----------------------------------------------------------------------------- launchers
+struct QmvLaunch {
+  int grid_per_sm, block, smem, rows_per_tile, stages;
+};
+
 template <int FMT, int M, int W>
 static int launch_qmv(const void* x, const void* w, const void* s, const void* b, void* y, int N, int ldy,
-                      cudaStream_t st) {
+                      cudaStream_t st, QmvLaunch* info = nullptr) {
   constexpr int TR = (W <= 4) ? 8 : 4;
-  constexpr int NS = 4;
+  constexpr int NS = 3;
   using C = QmvCfg<FMT, M, W, TR, NS>;
   auto kern = qmv_kernel<FMT, M, W, TR, NS>;
   static int occ = -1;
   static std::once_flag once;
   std::call_once(once, [&] {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess) return;
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     int o = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, W * 32, C::SMEM) != cudaSuccess) return;
     occ = o;
   });
   if (occ <= 0) return QMTP_ERR_CUDA;
+  if (info) {
+    *info = QmvLaunch{occ, W * 32, C::SMEM, TR, NS};
+    return QMTP_OK;
+  }
   const int grid = std::max(1, std::min(N, sm_count() * occ));
   kern<<<grid, W * 32, C::SMEM, st>>>(static_cast<const uint16_t*>(x), static_cast<const uint32_t*>(w),
                                         static_cast<const uint8_t*>(s), static_cast<const uint8_t*>(b),
@@ -251,13 +303,13 @@ static int launch_qmv(const void* x, const void* w, const void* s, const void* b
 
 template <int FMT, int M>
 static int dispatch_w(int K, const void* x, const void* w, const void* s, const void* b, void* y, int N, int ldy,
-                      cudaStream_t st) {
+                      cudaStream_t st, QmvLaunch* info = nullptr) {
   switch (K) {
-    case 1024: return launch_qmv<FMT, M, 1>(x, w, s, b, y, N, ldy, st);
-    case 2048: return launch_qmv<FMT, M, 2>(x, w, s, b, y, N, ldy, st);
-    case 4096: return launch_qmv<FMT, M, 4>(x, w, s, b, y, N, ldy, st);
-    case 8192: return launch_qmv<FMT, M, 8>(x, w, s, b, y, N, ldy, st);
-    case 12288: return launch_qmv<FMT, M, 12>(x, w, s, b, y, N, ldy, st);
+    case 1024: return launch_qmv<FMT, M, 1>(x, w, s, b, y, N, ldy, st, info);
+    case 2048: return launch_qmv<FMT, M, 2>(x, w, s, b, y, N, ldy, st, info);
+    case 4096: return launch_qmv<FMT, M, 4>(x, w, s, b, y, N, ldy, st, info);
+    case 8192: return launch_qmv<FMT, M, 8>(x, w, s, b, y, N, ldy, st, info);
+    case 12288: return launch_qmv<FMT, M, 12>(x, w, s, b, y, N, ldy, st, info);
     default: return QMTP_ERR_SHAPE;
   }
 }
@@ -336,6 +388,30 @@ extern "C" int qmtp_qmv_affine_g64(const void* x, const void* w, const void* sca
 extern "C" int qmtp_qmv_nvfp4_g16(const void* x, const void* w, const void* scales, void* y, int M, int N, int K,
                                   int ldy, void* stream) {
   return qmv_entry<FMT_NVFP4>(x, w, scales, nullptr, y, M, N, K, ldy, stream);
+}
+
+extern "C" int qmtp_qmv_launch_info(int fmt, int M, int K, int* ctas_per_sm, int* threads, int* smem_bytes,
+                                    int* rows_per_tile) {
+  if (!ctas_per_sm || !threads || !smem_bytes || !rows_per_tile) return QMTP_ERR_ARG;
+  if (M < 1 || M > 4 || (fmt != 0 && fmt != 1)) return QMTP_ERR_SHAPE;
+  QmvLaunch info{};
+  int rc;
+  auto go = [&](auto fmtc) -> int {
+    constexpr int F = decltype(fmtc)::value;
+    switch (M) {
+      case 1: return dispatch_w<F, 1>(K, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
+      case 2: return dispatch_w<F, 2>(K, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
+      case 3: return dispatch_w<F, 3>(K, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
+      default: return dispatch_w<F, 4>(K, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
+    }
+  };
+  rc = fmt == 0 ? go(std::integral_constant<int, FMT_AFFINE>{}) : go(std::integral_constant<int, FMT_NVFP4>{});
+  if (rc != QMTP_OK) return rc;
+  *ctas_per_sm = info.grid_per_sm;
+  *threads = info.block;
+  *smem_bytes = info.smem;
+  *rows_per_tile = info.rows_per_tile;
+  return QMTP_OK;
 }
 
 extern "C" int qmtp_quantize_affine_g64(const void* w, void* wq, void* scales, void* biases, int N, int K,

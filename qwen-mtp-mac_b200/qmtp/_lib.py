@@ -36,6 +36,8 @@ SIGNATURES: dict[str, list] = {
     "qmtp_qmv_affine_g64": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_qmv_nvfp4_g16": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_quantize_affine_g64": [_P, _P, _P, _P, _I, _I, _P],
+    "qmtp_qmv_launch_info": [_I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                             ctypes.POINTER(_I)],
 }
 
 _lib = None
@@ -99,3 +101,9 @@ def device_error(clear: bool = True) -> int:
     v = ctypes.c_uint(0)
     check(lib().qmtp_device_error(ctypes.byref(v), int(clear)), "qmtp_device_error")
     return v.value
+
+
+def qmv_launch_info(fmt: int, M: int, K: int) -> dict:
+    vals = [ctypes.c_int(0) for _ in range(4)]
+    check(lib().qmtp_qmv_launch_info(fmt, M, K, *[ctypes.byref(v) for v in vals]), "qmv_launch_info")
+    return dict(zip(("ctas_per_sm", "threads", "smem_bytes", "rows_per_tile"), (v.value for v in vals)))

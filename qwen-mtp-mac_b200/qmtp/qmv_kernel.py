@@ -55,8 +55,12 @@ def qmv_affine(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: t
     _lib.require_cuda(xf, w, scales, biases)
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    elif out.dim() != 2 or out.shape[0] != M or out.shape[1] < N or out.dtype != torch.bfloat16:
+        raise ValueError("out must be bf16 [M, >=N]")
     _lib.check(_lib.lib().qmtp_qmv_affine_g64(xf.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
                                                out.data_ptr(), M, N, K, out.shape[-1], _lib.stream()), "qmv_affine")
+    if out.shape[-1] != N:  # caller-provided wider output (leading dimension ldy > N)
+        return out[:, :N]
     return out.reshape(*x.shape[:-1], N)
 
 
