@@ -67,6 +67,68 @@ int qmtp_qmv_launch_info(int fmt, int M, int K, int* ctas_per_sm, int* threads, 
 int qmtp_quantize_affine_g64(const void* w, void* wq, void* scales, void* biases, int N, int K,
                              void* stream);
 
+/* --------------------------------------------------------------------------------------------
+ * GatedDeltaNet recurrent step with per-token state snapshots: gdn_kernel.py:75-88
+ * gated_delta_snapshot(q, k, v, g, beta, state) -> (y, state_out, state_mid).
+ *   q, k bf16 [B, T, Hk, Dk]; v bf16 [B, T, Hv, Dv]; g, beta fp32 [B, T, Hv];
+ *   state_in fp32 [B, Hv, Dv, Dk] -> y bf16 [B, T, Hv, Dv], state_out fp32 [B, Hv, Dv, Dk],
+ *   state_mid fp32 [T-1, B, Hv, Dv, Dk] (state after tokens 1..T-1; may be NULL when T == 1).
+ *   Dk == 128, Hv % Hk == 0 (GQA: value head hv reads key head hv / (Hv/Hk)). */
+int qmtp_gdn_step(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                  const float* state_in, void* y, float* state_out, float* state_mid, int B, int T,
+                  int Hk, int Hv, int Dk, int Dv, void* stream);
+
+/* Fused GatedDeltaNet middle section, B = 1: gdn_fused.py:43-112 (gdn_core) as called by
+ * gdn_middle (gdn_fused.py:149-167).  Causal conv over the window (KC taps) + silu, q/k RMS norm
+ * (q / Dk, k * Dk^-1/2), g = exp(-exp(A_log) * softplus(a + dt_bias)), beta = sigmoid(b), delta
+ * rule with snapshots.
+ *   win bf16 [S+KC-1, C] (C = 2*Hk*Dk + Hv*Dv: conv state rows then the S new qkv rows);
+ *   conv_w bf16 [C, KC]; a, b bf16 [S, >= Hv] (row stride ld_ab); A_log fp32 [Hv];
+ *   dt_bias bf16 [Hv]; state_in fp32 [Hv, Dv, Dk]
+ *   -> y fp32 [S, Hv, Dv] (bf16-rounded values, input of the gated norm), state_out,
+ *      state_mid fp32 [S-1, Hv, Dv, Dk] when snap != 0.  Dk == 128, S <= 64. */
+int qmtp_gdn_fused(const void* win, const void* conv_w, const void* a, const void* b, int ld_ab,
+                   const float* A_log, const void* dt_bias, const float* state_in, float* y,
+                   float* state_out, float* state_mid, int S, int Hk, int Hv, int Dk, int Dv, int KC,
+                   int snap, void* stream);
+
+/* General form of qmtp_gdn_fused for graph-captured decoding: the window is read from two
+ * sources (conv rows at a device-side row offset, qkv rows with their own stride), the next
+ * window can be written out, and the state can live in a ring of slots indexed by a device int
+ * (state after token t -> slot (cur + t + 1) % ring_slots).  Rolling back to `keep` tokens is then
+ * cur = (cur + keep) % ring_slots and conv_row_off = keep, with no copy (mtp.py:136-140 restore). */
+typedef struct qmtp_gdn_args {
+  const void* conv_src;      /* bf16 rows 0..KC-2 of the window start at row *conv_row_off */
+  long long ld_conv;
+  const int* conv_row_off;   /* device int, or NULL for 0 */
+  const void* qkv;           /* bf16 [S, >= C] new conv inputs */
+  long long ld_qkv;
+  void* win_out;             /* bf16 [KC-1+S, C] or NULL */
+  const void* conv_w;
+  const void* a;
+  const void* b;
+  long long ld_ab;
+  const float* A_log;
+  const void* dt_bias;
+  const float* state_in;     /* explicit-state mode (ring == NULL) */
+  float* state_out;
+  float* state_mid;
+  float* ring;               /* ring mode: ring_slots slots of Hv*Dv*Dk floats */
+  const int* ring_cur;       /* device int: slot holding the state before token 0 */
+  int ring_slots;            /* > S */
+  float* y;                  /* fp32 [S, Hv, Dv] */
+  int S, Hk, Hv, Dk, Dv, KC, snap;
+} qmtp_gdn_args;
+
+int qmtp_gdn_fused_ex(const qmtp_gdn_args* args, void* stream);
+
+/* Gated RMS norm of gdn_fused.py:114-129 (gdn_norm_gate): per (token, head) row of Dv,
+ * out = bf16(R(w * R(y * r)) * silu_f32(z)), r = 1/sqrt(mean(y^2) + eps).
+ *   y fp32 [S, H, Dv]; z bf16 [S, >= H*Dv] (row stride ld_z); w bf16 [Dv];
+ *   out bf16 [S, >= H*Dv] (row stride ld_out).  Dv == 128. */
+int qmtp_gdn_norm_gate(const float* y, const void* z, int ld_z, const void* w, void* out, int ld_out,
+                       int S, int H, int Dv, float eps, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -137,3 +137,70 @@ def dequant_affine(wq, s, b, group_size: int = 64) -> np.ndarray:
     sf = np.repeat(bf16_to_f32(s).astype(np.float64), group_size, axis=1)
     bf = np.repeat(bf16_to_f32(b).astype(np.float64), group_size, axis=1)
     return sf * q + bf
+
+
+# ---------------------------------------------------------------- GatedDeltaNet
+def gdn_step(q, k, v, g, beta, state):
+    """C qo_gdn_step (gdn_kernel.py:11-88): returns (y bf16, state_out, state_mid [T-1,...])."""
+    q = np.ascontiguousarray(q, np.uint16)
+    k = np.ascontiguousarray(k, np.uint16)
+    v = np.ascontiguousarray(v, np.uint16)
+    g = np.ascontiguousarray(g, np.float32)
+    beta = np.ascontiguousarray(beta, np.float32)
+    state = np.ascontiguousarray(state, np.float32)
+    B, T, Hk, Dk = k.shape
+    Hv, Dv = v.shape[2:]
+    y = np.empty((B, T, Hv, Dv), np.uint16)
+    so = np.empty_like(state)
+    sm = np.empty((max(T - 1, 1),) + state.shape, np.float32)
+    rc = lib().qo_gdn_step(_p(q), _p(k), _p(v), _p(g), _p(beta), _p(state), _p(y), _p(so), _p(sm),
+                           _I(B), _I(T), _I(Hk), _I(Hv), _I(Dk), _I(Dv))
+    assert rc == 0
+    return y, so, sm
+
+
+def gdn_fused(win, conv_w, a, b, A_log, dt_bias, state, Hk, Hv, Dk, Dv, KC, snap=True):
+    """C qo_gdn_fused (gdn_fused.py:43-112), B = 1.  win bf16 [S+KC-1, C]; a, b bf16 [S, Hv];
+    state fp32 [Hv, Dv, Dk] -> (y fp32 [S, Hv, Dv], state_out, state_mid [S-1, Hv, Dv, Dk])."""
+    win = np.ascontiguousarray(win, np.uint16).reshape(-1, 2 * Hk * Dk + Hv * Dv)
+    S = win.shape[0] - (KC - 1)
+    a = np.ascontiguousarray(a, np.uint16).reshape(S, -1)
+    b = np.ascontiguousarray(b, np.uint16).reshape(S, -1)
+    conv_w = np.ascontiguousarray(conv_w, np.uint16)
+    A_log = np.ascontiguousarray(A_log, np.float32)
+    dt_bias = np.ascontiguousarray(dt_bias, np.uint16)
+    state = np.ascontiguousarray(state, np.float32).reshape(Hv, Dv, Dk)
+    y = np.empty((S, Hv, Dv), np.float32)
+    so = np.empty_like(state)
+    sm = np.empty((max(S - 1, 1), Hv, Dv, Dk), np.float32)
+    rc = lib().qo_gdn_fused(_p(win), _p(conv_w), _p(a), _p(b), _I(a.shape[1]), _p(A_log), _p(dt_bias), _p(state),
+                            _p(y), _p(so), _p(sm) if snap else None, _I(S), _I(Hk), _I(Hv), _I(Dk), _I(Dv), _I(KC))
+    assert rc == 0
+    return y, so, sm
+
+
+def gdn_norm_gate(y, z, w, eps):
+    """C qo_gdn_norm_gate (gdn_fused.py:114-129): y fp32 [S, H, Dv], z bf16 [S, H*Dv] -> bf16 [S, H*Dv]."""
+    y = np.ascontiguousarray(y, np.float32)
+    S, H, Dv = y.shape
+    z = np.ascontiguousarray(z, np.uint16).reshape(S, H * Dv)
+    w = np.ascontiguousarray(w, np.uint16)
+    out = np.empty((S, H * Dv), np.uint16)
+    lib().qo_gdn_norm_gate(_p(y), _p(z), _I(H * Dv), _p(w), _p(out), _I(S), _I(H), _I(Dv), ctypes.c_float(eps))
+    return out
+
+
+def gdn_fused_prep(win, conv_w, a, b, A_log, dt_bias, Hk, Hv, Dk, Dv, KC, **_):
+    """C qo_gdn_fused_prep: (q [S,Hk,Dk], k [S,Hk,Dk], v [S,Hv,Dv], g [S,Hv], beta [S,Hv]) as fp32."""
+    win = np.ascontiguousarray(win, np.uint16).reshape(-1, 2 * Hk * Dk + Hv * Dv)
+    S = win.shape[0] - (KC - 1)
+    a = np.ascontiguousarray(a, np.uint16).reshape(S, -1)
+    b = np.ascontiguousarray(b, np.uint16).reshape(S, -1)
+    out = [np.empty((S, Hk, Dk), np.float32), np.empty((S, Hk, Dk), np.float32), np.empty((S, Hv, Dv), np.float32),
+           np.empty((S, Hv), np.float32), np.empty((S, Hv), np.float32)]
+    rc = lib().qo_gdn_fused_prep(_p(win), _p(np.ascontiguousarray(conv_w, np.uint16)), _p(a), _p(b), _I(a.shape[1]),
+                                 _p(np.ascontiguousarray(A_log, np.float32)),
+                                 _p(np.ascontiguousarray(dt_bias, np.uint16)), *[_p(o) for o in out],
+                                 _I(S), _I(Hk), _I(Hv), _I(Dk), _I(Dv), _I(KC))
+    assert rc == 0
+    return tuple(out)

@@ -468,15 +468,13 @@ static inline float qo_conv_tap(const uint16_t* conv_w, const uint16_t* win, int
   return acc;
 }
 
-QO_API int qo_gdn_fused(const uint16_t* win, const uint16_t* conv_w, const uint16_t* a, const uint16_t* b,
-                        int ld_ab, const float* A_log, const uint16_t* dt_bias, const float* state_in,
-                        float* y, float* state_out, float* state_mid, int S, int Hk, int Hv, int Dk,
-                        int Dv, int KC) {
+/* The elementwise half of gdn_core: qn, kn fp32 [S, Hk, Dk], vn fp32 [S, Hv*Dv], g, beta fp32
+ * [S, Hv] (all values bf16-exact except g). */
+QO_API int qo_gdn_fused_prep(const uint16_t* win, const uint16_t* conv_w, const uint16_t* a, const uint16_t* b,
+                             int ld_ab, const float* A_log, const uint16_t* dt_bias, float* qn, float* kn,
+                             float* vn, float* gt, float* bt, int S, int Hk, int Hv, int Dk, int Dv, int KC) {
   if (Dk % 32 != 0 || Hv % Hk != 0 || S < 1) return -1;
   int C = 2 * Hk * Dk + Hv * Dv;
-  /* q/k prep per (t, hk) */
-  float* qn = (float*)malloc(sizeof(float) * (size_t)S * Hk * Dk);
-  float* kn = (float*)malloc(sizeof(float) * (size_t)S * Hk * Dk);
   float* tmp = (float*)malloc(sizeof(float) * Dk);
   for (int t = 0; t < S; ++t) {
     for (int hk = 0; hk < Hk; ++hk) {
@@ -485,27 +483,38 @@ QO_API int qo_gdn_fused(const uint16_t* win, const uint16_t* conv_w, const uint1
       for (int e = 0; e < Dk; ++e) tmp[e] = qo_silu_bf(qo_R(qo_conv_tap(conv_w, win, C, KC, Hk * Dk + hk * Dk + e, t)));
       qo_gdn_qk_prep(tmp, Dk, 0, kn + ((size_t)t * Hk + hk) * Dk);
     }
-  }
-  free(tmp);
-  float* gt = (float*)malloc(sizeof(float) * (size_t)S * Hv * 2);
-  float* bt = gt + (size_t)S * Hv;
-  for (int t = 0; t < S; ++t)
+    for (int cv = 0; cv < Hv * Dv; ++cv)
+      vn[(size_t)t * Hv * Dv + cv] = qo_silu_bf(qo_R(qo_conv_tap(conv_w, win, C, KC, 2 * Hk * Dk + cv, t)));
     for (int hv = 0; hv < Hv; ++hv) {
       float A = -qo_expf(A_log[hv]);
       float sp = qo_softplus_bf(qo_R(qo_bf2f(a[(size_t)t * ld_ab + hv]) + qo_bf2f(dt_bias[hv])));
       gt[(size_t)t * Hv + hv] = qo_expf(A * sp);
       bt[(size_t)t * Hv + hv] = qo_sigmoid_bf(qo_bf2f(b[(size_t)t * ld_ab + hv]));
     }
+  }
+  free(tmp);
+  return 0;
+}
+
+QO_API int qo_gdn_fused(const uint16_t* win, const uint16_t* conv_w, const uint16_t* a, const uint16_t* b,
+                        int ld_ab, const float* A_log, const uint16_t* dt_bias, const float* state_in,
+                        float* y, float* state_out, float* state_mid, int S, int Hk, int Hv, int Dk,
+                        int Dv, int KC) {
+  if (Dk % 32 != 0 || Hv % Hk != 0 || S < 1 || S > 64) return -1;
+  float* qn = (float*)malloc(sizeof(float) * (size_t)S * Hk * Dk);
+  float* kn = (float*)malloc(sizeof(float) * (size_t)S * Hk * Dk);
+  float* vn = (float*)malloc(sizeof(float) * (size_t)S * Hv * Dv);
+  float* gt = (float*)malloc(sizeof(float) * (size_t)S * Hv * 2);
+  float* bt = gt + (size_t)S * Hv;
+  qo_gdn_fused_prep(win, conv_w, a, b, ld_ab, A_log, dt_bias, qn, kn, vn, gt, bt, S, Hk, Hv, Dk, Dv, KC);
   size_t per = (size_t)Hv * Dv * Dk;
 #pragma omp parallel for collapse(2) schedule(static)
   for (int hv = 0; hv < Hv; ++hv) {
     for (int dv = 0; dv < Dv; ++dv) {
       int hk = hv / (Hv / Hk);
-      int cv = 2 * Hk * Dk + hv * Dv + dv;
-      float vf[64], yf[64];
-      float gg[64], bb[64];
-      for (int t = 0; t < S && t < 64; ++t) {
-        vf[t] = qo_silu_bf(qo_R(qo_conv_tap(conv_w, win, C, KC, cv, t)));
+      float vf[64], yf[64], gg[64], bb[64];
+      for (int t = 0; t < S; ++t) {
+        vf[t] = vn[(size_t)t * Hv * Dv + (size_t)hv * Dv + dv];
         gg[t] = gt[(size_t)t * Hv + hv];
         bb[t] = bt[(size_t)t * Hv + hv];
       }
@@ -517,7 +526,7 @@ QO_API int qo_gdn_fused(const uint16_t* win, const uint16_t* conv_w, const uint1
       for (int t = 0; t < S; ++t) y[((size_t)t * Hv + hv) * Dv + dv] = qo_R(yf[t]);
     }
   }
-  free(qn); free(kn); free(gt);
+  free(qn); free(kn); free(vn); free(gt);
   return 0;
 }
 

@@ -40,6 +40,27 @@ SIGNATURES: dict[str, list] = {
                              ctypes.POINTER(_I)],
 }
 
+
+
+class GdnArgs(ctypes.Structure):
+    """Mirror of qmtp_gdn_args (include/qmtp.h)."""
+    _fields_ = [("conv_src", _P), ("ld_conv", ctypes.c_longlong), ("conv_row_off", _P),
+                ("qkv", _P), ("ld_qkv", ctypes.c_longlong), ("win_out", _P),
+                ("conv_w", _P), ("a", _P), ("b", _P), ("ld_ab", ctypes.c_longlong),
+                ("A_log", _P), ("dt_bias", _P),
+                ("state_in", _P), ("state_out", _P), ("state_mid", _P),
+                ("ring", _P), ("ring_cur", _P), ("ring_slots", _I),
+                ("y", _P),
+                ("S", _I), ("Hk", _I), ("Hv", _I), ("Dk", _I), ("Dv", _I), ("KC", _I), ("snap", _I)]
+
+
+SIGNATURES.update({
+    "qmtp_gdn_step": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
+    "qmtp_gdn_fused": [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
+    "qmtp_gdn_fused_ex": [ctypes.POINTER(GdnArgs), _P],
+    "qmtp_gdn_norm_gate": [_P, _P, _I, _P, _P, _I, _I, _I, _I, _F, _P],
+})
+
 _lib = None
 _lock = threading.Lock()
 
