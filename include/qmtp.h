@@ -129,6 +129,33 @@ int qmtp_gdn_fused_ex(const qmtp_gdn_args* args, void* stream);
 int qmtp_gdn_norm_gate(const float* y, const void* z, int ld_z, const void* w, void* out, int ld_out,
                        int S, int H, int Dv, float eps, void* stream);
 
+/* --------------------------------------------------------------------------------------------
+ * Two-stage lm_head: lm_head2.py:23-29 TwoStageHead.__call__ (coarse quantized logits ->
+ * argpartition top-k -> take the k bf16 weight rows -> exact logits) plus the greedy argmax of
+ * engine.py:121-124.  Ties are resolved as (value descending, vocab index ascending).
+ *   h bf16 [M, K]; wq/scales/biases: affine g64 coarse head [V, K]; w_fine bf16 [V, K];
+ *   -> out_idx int32 [M, k] (candidates in that order), out_fine bf16 [M, k] (exact logits),
+ *      out_argmax int32 [M] (may be NULL), coarse_out bf16 [M, V] (may be NULL).
+ *   workspace: qmtp_lmhead2_workspace(M, V, k) bytes, 16-B aligned.  k <= 256, K % 1024 == 0. */
+size_t qmtp_lmhead2_workspace(int M, int V, int k);
+int qmtp_lmhead2(const void* h, const void* wq, const void* scales, const void* biases,
+                 const void* w_fine, int M, int V, int K, int k, int* out_idx, void* out_fine,
+                 int* out_argmax, void* coarse_out, void* workspace, size_t ws_bytes, void* stream);
+
+/* Stage 2 alone: exact top-k of bf16 rows vals [M, ld] (first V columns) and, when w_fine is
+ * given, the rescoring of the candidates against w_fine [V, K] with h [M, K] and their argmax
+ * (lm_head2.py:25-29).  workspace: qmtp_topk_workspace(M, V, k) bytes. */
+size_t qmtp_topk_workspace(int M, int V, int k);
+int qmtp_topk_rescore(const void* vals, int ld, int M, int V, int k, const void* w_fine,
+                      const void* h, int K, int* out_idx, void* out_fine, int* out_argmax,
+                      void* workspace, size_t ws_bytes, void* stream);
+
+/* Greedy token of bf16 logits rows (mtp.py:165-167 DraftHead.token / mx.argmax, ties -> lowest
+ * index): vals [M, ld] -> out int32 [M].  workspace: qmtp_argmax_workspace(M, V) bytes. */
+size_t qmtp_argmax_workspace(int M, int V);
+int qmtp_argmax_bf16(const void* vals, int ld, int M, int V, int* out, void* workspace,
+                     size_t ws_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,6 +28,8 @@ def lib():
                 L.qo_exp.restype = ctypes.c_float
                 L.qo_log.argtypes = [ctypes.c_float]
                 L.qo_log.restype = ctypes.c_float
+                L.qo_dot_bf16.argtypes = [_P, _P, _I]
+                L.qo_dot_bf16.restype = ctypes.c_float
                 _lib = L
     return _lib
 
@@ -204,3 +206,46 @@ def gdn_fused_prep(win, conv_w, a, b, A_log, dt_bias, Hk, Hv, Dk, Dv, KC, **_):
                                  _I(S), _I(Hk), _I(Hv), _I(Dk), _I(Dv), _I(KC))
     assert rc == 0
     return tuple(out)
+
+
+# ---------------------------------------------------------------- two-stage lm_head (lm_head2.py)
+def topk_bf16(vals, k):
+    v = np.ascontiguousarray(vals, np.uint16)
+    v2 = v.reshape(-1, v.shape[-1])
+    out = np.empty((v2.shape[0], k), np.int32)
+    assert lib().qo_topk_bf16(_p(v2), _I(v2.shape[0]), _I(v2.shape[1]), _I(v2.shape[1]), _I(k), _p(out)) == 0
+    return out
+
+
+def rescore_bf16(W, h, idx):
+    W = np.ascontiguousarray(W, np.uint16)
+    h = np.ascontiguousarray(h, np.uint16).reshape(-1, W.shape[1])
+    idx = np.ascontiguousarray(idx, np.int32)
+    M, k = idx.shape
+    fine = np.empty((M, k), np.uint16)
+    amax = np.empty(M, np.int32)
+    assert lib().qo_rescore_bf16(_p(W), _p(h), _p(idx), _I(M), _I(k), _I(W.shape[1]), _p(fine), _p(amax)) == 0
+    return fine, amax
+
+
+def argmax_bf16(vals):
+    v = np.ascontiguousarray(vals, np.uint16)
+    v2 = v.reshape(-1, v.shape[-1])
+    out = np.empty(v2.shape[0], np.int32)
+    lib().qo_argmax_bf16(_p(v2), _I(v2.shape[0]), _I(v2.shape[1]), _I(v2.shape[1]), _p(out))
+    return out
+
+
+def two_stage_head(h, wq, s, b, W, k=64):
+    """lm_head2.py:23-29 restated: (coarse bf16 [M,V], idx [M,k], fine bf16 [M,k], argmax [M])."""
+    coarse = qmv_affine(h, wq, s, b)
+    idx = topk_bf16(coarse, k)
+    fine, amax = rescore_bf16(W, h, idx)
+    return coarse, idx, fine, amax
+
+
+def dot_bf16(w_row, h_row) -> np.float32:
+    """C qo_dot_bf16: the fine-logit dot product in its fixed order (fp32, before bf16 rounding)."""
+    w = np.ascontiguousarray(w_row, np.uint16)
+    h = np.ascontiguousarray(h_row, np.uint16)
+    return np.float32(lib().qo_dot_bf16(_p(w), _p(h), _I(w.size)))

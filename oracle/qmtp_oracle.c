@@ -553,3 +553,74 @@ QO_API void qo_gdn_norm_gate(const float* y, const uint16_t* z, int ld_z, const 
       }
     }
 }
+
+/* ------------------------------------------------------------------ two-stage lm_head
+ * lm_head2.py:23-29.  Stage 1 is qo_qmv_affine (coarse bf16 logits).  Selection: the topk entries
+ * of a row under the total order (value descending, vocab index ascending), with bf16 values
+ * compared through the order-preserving 16-bit key below (lm_head2.py:25 argpartition leaves ties
+ * unspecified; this order resolves them).  Stage 2: fine = bf16(dot(W[idx], h)) with the dot
+ * ordered as: lane l = 0..31 takes the 8-element chunks c = l, l+32, ... ascending, fmaf over the
+ * chunk's elements ascending from 0, then the 32 lane sums are butterflied. */
+static inline uint32_t qo_bf16_key(uint16_t b) { return (b & 0x8000u) ? (uint32_t)(~b & 0xFFFFu) : (uint32_t)(b | 0x8000u); }
+
+typedef struct { uint32_t key; int32_t idx; } qo_cand;
+static int qo_cand_cmp(const void* a, const void* b) {
+  const qo_cand* x = (const qo_cand*)a; const qo_cand* y = (const qo_cand*)b;
+  if (x->key != y->key) return x->key > y->key ? -1 : 1;
+  return x->idx < y->idx ? -1 : (x->idx > y->idx ? 1 : 0);
+}
+
+QO_API int qo_topk_bf16(const uint16_t* vals, int M, int V, int ld, int k, int32_t* idx_out) {
+  if (k < 1 || k > V) return -1;
+  for (int m = 0; m < M; ++m) {
+    qo_cand* c = (qo_cand*)malloc(sizeof(qo_cand) * (size_t)V);
+    for (int i = 0; i < V; ++i) { c[i].key = qo_bf16_key(vals[(size_t)m * ld + i]); c[i].idx = i; }
+    qsort(c, (size_t)V, sizeof(qo_cand), qo_cand_cmp);
+    for (int j = 0; j < k; ++j) idx_out[(size_t)m * k + j] = c[j].idx;
+    free(c);
+  }
+  return 0;
+}
+
+QO_API float qo_dot_bf16(const uint16_t* w, const uint16_t* h, int K) {
+  float P[32];
+  for (int l = 0; l < 32; ++l) {
+    float acc = 0.0f;
+    for (int c = l; c < K / 8; c += 32)
+      for (int e = 0; e < 8; ++e) acc = fmaf(qo_bf2f(w[8 * c + e]), qo_bf2f(h[8 * c + e]), acc);
+    P[l] = acc;
+  }
+  return qo_butterfly32(P);
+}
+
+/* fine[m][j] = bf16(dot(W[idx[m][j]], h[m])) and argmax[m] = the idx with the largest fine value
+ * (ties: lowest vocab index), W bf16 [V, K]. */
+QO_API int qo_rescore_bf16(const uint16_t* W, const uint16_t* h, const int32_t* idx, int M, int k, int K,
+                           uint16_t* fine, int32_t* amax) {
+  if (K % 256 != 0) return -1;
+  for (int m = 0; m < M; ++m) {
+    uint32_t bk = 0; int32_t bi = -1;
+    for (int j = 0; j < k; ++j) {
+      int32_t v = idx[(size_t)m * k + j];
+      uint16_t f = qo_f2bf(qo_dot_bf16(W + (size_t)v * K, h + (size_t)m * K, K));
+      fine[(size_t)m * k + j] = f;
+      uint32_t key = qo_bf16_key(f);
+      if (bi < 0 || key > bk || (key == bk && v < bi)) { bk = key; bi = v; }
+    }
+    amax[m] = bi;
+  }
+  return 0;
+}
+
+/* argmax over a bf16 row (ties: lowest index). */
+QO_API int qo_argmax_bf16(const uint16_t* vals, int M, int V, int ld, int32_t* out) {
+  for (int m = 0; m < M; ++m) {
+    uint32_t bk = 0; int32_t bi = -1;
+    for (int i = 0; i < V; ++i) {
+      uint32_t key = qo_bf16_key(vals[(size_t)m * ld + i]);
+      if (bi < 0 || key > bk) { bk = key; bi = i; }
+    }
+    out[m] = bi;
+  }
+  return 0;
+}

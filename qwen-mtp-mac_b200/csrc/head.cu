@@ -1,0 +1,319 @@
+// Two-stage lm_head on B200 (lm_head2.py:14-29): coarse 4-bit logits over the full vocabulary (the
+// qmv kernel), exact top-k selection, exact bf16 rescoring of the k candidate rows, argmax.
+//
+// Selection order: value descending, vocab index ascending (argpartition leaves ties open; this
+// resolves them deterministically).  bf16 values are compared through the order-preserving 16-bit
+// key `key16`; a candidate is the 64-bit word (key16 << 32) | (0xFFFFFFFF - index), so "larger
+// word" means "better candidate" and any max/sort over these words is order-independent.
+//
+//   topk_partial  grid (G, M): block g of row m radix-selects the top k of its slice of the row
+//                 (two 8-bit histogram passes in shared memory) and writes k candidate words;
+//   topk_merge    grid (M): bitonic-sorts the G*k candidate words, keeps the first k, rescoring
+//                 each against the bf16 weight row (one warp per candidate, fixed reduction order
+//                 of oracle qo_dot_bf16), and takes the argmax of the fine logits;
+//   argmax        the same candidate words with k = 1 (draft head: argmax over the full vocab).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace qmtp {
+
+__device__ __forceinline__ uint32_t key16(uint16_t b) {
+  return (b & 0x8000u) ? uint32_t(~b & 0xFFFFu) : uint32_t(b | 0x8000u);
+}
+__device__ __forceinline__ uint64_t cand_word(uint32_t key, uint32_t idx) {
+  return (uint64_t(key) << 32) | uint64_t(0xFFFFFFFFu - idx);
+}
+__device__ __forceinline__ uint32_t cand_idx(uint64_t w) { return 0xFFFFFFFFu - uint32_t(w & 0xFFFFFFFFu); }
+
+// Block-wide exclusive prefix sum of one int per thread (blockDim.x <= 1024, multiple of 32).
+__device__ int block_excl_scan(int v, int* s_warp, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int o = __shfl_up_sync(0xFFFFFFFFu, x, d);
+    if (lane >= d) x += o;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xFFFFFFFFu, w, d);
+      if (lane >= d) w += o;
+    }
+    if (lane < nw) s_warp[lane] = w;  // inclusive per warp
+  }
+  __syncthreads();
+  total = s_warp[nw - 1];
+  const int base = warp > 0 ? s_warp[warp - 1] : 0;
+  __syncthreads();
+  return base + x - v;
+}
+
+// Finds (within the bins above `base`) the bin b where the count from the top reaches k.
+// hist[256]; warp 0 only.  Returns via s_res[0] = b, s_res[1] = count strictly above b.
+__device__ void find_bin(const int* hist, int k, int base, int* s_res) {
+  const int lane = threadIdx.x & 31;
+  int local[8], s = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) { local[i] = hist[8 * lane + i]; s += local[i]; }
+  int incl = s;  // suffix sum over lanes >= lane
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int o = __shfl_down_sync(0xFFFFFFFFu, incl, d);
+    if (lane + d < 32) incl += o;
+  }
+  const int excl = incl - s;
+  if (base + excl < k && base + incl >= k) {
+    int cum = base + excl;
+#pragma unroll
+    for (int i = 7; i >= 0; --i) {
+      if (cum + local[i] >= k) { s_res[0] = 8 * lane + i; s_res[1] = cum; break; }
+      cum += local[i];
+    }
+  }
+}
+
+// Exact top-k of n (>= k) 16-bit keys in shared memory: T and g with g < k <= g + #(key == T).
+__device__ void block_select16(const uint16_t* keys, int n, int k, int* hist, int* s_res, int& T, int& g) {
+  const int tid = threadIdx.x;
+  for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += blockDim.x) atomicAdd(&hist[keys[i] >> 8], 1);
+  __syncthreads();
+  if (tid < 32) find_bin(hist, k, 0, s_res);
+  __syncthreads();
+  const int b1 = s_res[0], g1 = s_res[1];
+  __syncthreads();
+  for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += blockDim.x) {
+    const uint32_t kk = keys[i];
+    if (int(kk >> 8) == b1) atomicAdd(&hist[kk & 255u], 1);
+  }
+  __syncthreads();
+  if (tid < 32) find_bin(hist, k, g1, s_res);
+  __syncthreads();
+  T = (b1 << 8) | s_res[0];
+  g = s_res[1];
+  __syncthreads();
+}
+
+constexpr int kTopkThreads = 256;
+
+__global__ void __launch_bounds__(kTopkThreads)
+topk_partial_kernel(const uint16_t* __restrict__ vals, long long ld, int V, int k, uint64_t* __restrict__ cand) {
+  extern __shared__ __align__(16) unsigned char sm_raw[];
+  int* hist = reinterpret_cast<int*>(sm_raw);
+  int* s_res = hist + 256;
+  int* s_warp = s_res + 4;
+  uint16_t* keys = reinterpret_cast<uint16_t*>(s_warp + 32);
+  const int G = gridDim.x, blk = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
+  const int i0 = int((long long)blk * V / G), i1 = int((long long)(blk + 1) * V / G), n = i1 - i0;
+  const uint16_t* row = vals + (long long)m * ld + i0;
+  for (int i = tid; i < n; i += blockDim.x) keys[i] = uint16_t(key16(row[i]));
+  __syncthreads();
+  int T, g;
+  block_select16(keys, n, k, hist, s_res, T, g);
+  // emit: every key > T, then the (k - g) lowest-index keys == T, each thread over a contiguous range
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int a0 = min(n, tid * per), a1 = min(n, a0 + per);
+  int cgt = 0, ceq = 0;
+  for (int i = a0; i < a1; ++i) {
+    const int kk = keys[i];
+    cgt += kk > T;
+    ceq += kk == T;
+  }
+  int tot;
+  int ogt = block_excl_scan(cgt, s_warp, tot);
+  int oeq = block_excl_scan(ceq, s_warp, tot);
+  uint64_t* out = cand + ((long long)m * G + blk) * k;
+  for (int i = a0; i < a1; ++i) {
+    const int kk = keys[i];
+    if (kk > T) {
+      out[ogt++] = cand_word(uint32_t(kk), uint32_t(i0 + i));
+    } else if (kk == T) {
+      if (oeq < k - g) out[g + oeq] = cand_word(uint32_t(kk), uint32_t(i0 + i));
+      ++oeq;
+    }
+  }
+}
+
+constexpr int kMergeThreads = 1024;
+
+// Sorts G*k candidate words of row m (descending), keeps k, rescoring + argmax.  W may be null
+// (selection only).
+__global__ void __launch_bounds__(kMergeThreads)
+topk_merge_kernel(const uint64_t* __restrict__ cand, int G, int k, int NP, const uint16_t* __restrict__ W,
+                  const uint16_t* __restrict__ h, int K, int32_t* __restrict__ out_idx,
+                  uint16_t* __restrict__ out_fine, int32_t* __restrict__ out_amax) {
+  extern __shared__ __align__(16) unsigned char sm_raw[];
+  uint64_t* s = reinterpret_cast<uint64_t*>(sm_raw);  // [NP]
+  uint64_t* fk = s + NP;                              // [k] fine candidate words
+  const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = G * k;
+  for (int i = tid; i < NP; i += blockDim.x) s[i] = i < n ? cand[(long long)m * n + i] : 0ull;
+  __syncthreads();
+  for (int size = 2; size <= NP; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < NP / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const uint64_t a = s[lo], b = s[hi];
+        if ((a < b) == desc) { s[lo] = b; s[hi] = a; }
+      }
+      __syncthreads();
+    }
+  }
+  for (int j = tid; j < k; j += blockDim.x) out_idx[(long long)m * k + j] = int32_t(cand_idx(s[j]));
+  if (!W) return;
+  const uint16_t* hr = h + (long long)m * K;
+  for (int j = warp; j < k; j += blockDim.x / 32) {
+    const uint32_t v = cand_idx(s[j]);
+    const uint16_t* wr = W + (long long)v * K;
+    float acc = 0.0f;
+    for (int c = lane; c < K / 8; c += 32) {
+      const uint4 w4 = ldg_nc_v4(wr + 8 * c);
+      const uint4 h4 = *reinterpret_cast<const uint4*>(hr + 8 * c);
+      const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w}, hh[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc = __fmaf_rn(bflo(ww[e]), bflo(hh[e]), acc);
+        acc = __fmaf_rn(bfhi(ww[e]), bfhi(hh[e]), acc);
+      }
+    }
+    acc = warp_sum(acc);
+    const uint16_t f = f2bf(acc);
+    if (lane == 0) {
+      out_fine[(long long)m * k + j] = f;
+      fk[j] = cand_word(key16(f), v);
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    uint64_t best = 0;
+    for (int j = lane; j < k; j += 32) best = max(best, fk[j]);
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) {
+      const uint64_t o = __shfl_xor_sync(0xFFFFFFFFu, best, d);
+      best = max(best, o);
+    }
+    if (lane == 0 && out_amax) out_amax[m] = int32_t(cand_idx(best));
+  }
+}
+
+// Argmax over V (per row): block maxima of candidate words, then one block per row.
+__global__ void __launch_bounds__(256)
+argmax_partial_kernel(const uint16_t* __restrict__ vals, long long ld, int V, uint64_t* __restrict__ part) {
+  const int G = gridDim.x, blk = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
+  const int i0 = int((long long)blk * V / G), i1 = int((long long)(blk + 1) * V / G);
+  const uint16_t* row = vals + (long long)m * ld;
+  uint64_t best = 0;
+  for (int i = i0 + tid; i < i1; i += blockDim.x) best = max(best, cand_word(key16(row[i]), uint32_t(i)));
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, d));
+  __shared__ uint64_t sw[8];
+  if ((tid & 31) == 0) sw[tid >> 5] = best;
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < int(blockDim.x >> 5); ++w) best = max(best, sw[w]);
+    part[(long long)m * G + blk] = best;
+  }
+}
+
+__global__ void argmax_final_kernel(const uint64_t* __restrict__ part, int G, int32_t* __restrict__ out) {
+  const int m = blockIdx.x, lane = threadIdx.x;
+  uint64_t best = 0;
+  for (int i = lane; i < G; i += 32) best = max(best, part[(long long)m * G + i]);
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, d));
+  if (lane == 0) out[m] = int32_t(cand_idx(best));
+}
+
+static int topk_blocks(int V, int k) {
+  // enough blocks to spread the selection, each slice >= k entries and <= 12288 keys (smem)
+  int G = 32;
+  while (G > 1 && V / G < k) G >>= 1;
+  while ((V + G - 1) / G > 12288) G <<= 1;
+  return G;
+}
+static int pow2_at_least(int n) {
+  int p = 1;
+  while (p < n) p <<= 1;
+  return p;
+}
+
+}  // namespace qmtp
+
+using namespace qmtp;
+
+extern "C" size_t qmtp_topk_workspace(int M, int V, int k) {
+  if (M < 1 || V < 1 || k < 1) return 0;
+  return size_t(M) * topk_blocks(V, k) * k * sizeof(uint64_t);
+}
+
+extern "C" int qmtp_topk_rescore(const void* vals, int ld, int M, int V, int k, const void* w_fine, const void* h,
+                                 int K, int* out_idx, void* out_fine, int* out_argmax, void* workspace,
+                                 size_t ws_bytes, void* stream) {
+  if (!vals || !out_idx || !workspace) return QMTP_ERR_ARG;
+  if (M < 1 || V < 1 || k < 1 || k > 256 || k > V || ld < V) return QMTP_ERR_SHAPE;
+  if (w_fine && (!h || !out_fine || K < 256 || K % 256 != 0)) return QMTP_ERR_SHAPE;
+  if (w_fine && (!aligned16(w_fine) || !aligned16(h))) return QMTP_ERR_ALIGN;
+  const int G = topk_blocks(V, k);
+  if (ws_bytes < qmtp_topk_workspace(M, V, k) || !aligned16(workspace)) return QMTP_ERR_ARG;
+  const int NP = pow2_at_least(G * k);
+  if (NP > 8192) return QMTP_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int slice = (V + G - 1) / G;
+  const size_t smemA = (256 + 4 + 32) * sizeof(int) + size_t(slice) * sizeof(uint16_t);
+  uint64_t* cand = static_cast<uint64_t*>(workspace);
+  topk_partial_kernel<<<dim3(G, M), kTopkThreads, smemA, st>>>(static_cast<const uint16_t*>(vals), ld, V, k, cand);
+  const size_t smemB = size_t(NP + k) * sizeof(uint64_t);
+  static const cudaError_t attr =
+      cudaFuncSetAttribute(topk_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
+  if (attr != cudaSuccess) return QMTP_ERR_CUDA;
+  topk_merge_kernel<<<M, kMergeThreads, smemB, st>>>(cand, G, k, NP, static_cast<const uint16_t*>(w_fine),
+                                                      static_cast<const uint16_t*>(h), K, out_idx,
+                                                      static_cast<uint16_t*>(out_fine), out_argmax);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" size_t qmtp_argmax_workspace(int M, int V) {
+  if (M < 1 || V < 1) return 0;
+  return size_t(M) * std::min(256, std::max(1, V / 1024)) * sizeof(uint64_t);
+}
+
+extern "C" int qmtp_argmax_bf16(const void* vals, int ld, int M, int V, int* out, void* workspace, size_t ws_bytes,
+                                void* stream) {
+  if (!vals || !out || !workspace) return QMTP_ERR_ARG;
+  if (M < 1 || V < 1 || ld < V) return QMTP_ERR_SHAPE;
+  if (ws_bytes < qmtp_argmax_workspace(M, V)) return QMTP_ERR_ARG;
+  const int G = std::min(256, std::max(1, V / 1024));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint64_t* part = static_cast<uint64_t*>(workspace);
+  argmax_partial_kernel<<<dim3(G, M), 256, 0, st>>>(static_cast<const uint16_t*>(vals), ld, V, part);
+  argmax_final_kernel<<<M, 32, 0, st>>>(part, G, out);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" size_t qmtp_lmhead2_workspace(int M, int V, int k) {
+  const size_t coarse = (size_t(M) * V * sizeof(uint16_t) + 255) / 256 * 256;
+  return coarse + qmtp_topk_workspace(M, V, k);
+}
+
+extern "C" int qmtp_lmhead2(const void* h, const void* wq, const void* scales, const void* biases, const void* w_fine,
+                            int M, int V, int K, int k, int* out_idx, void* out_fine, int* out_argmax,
+                            void* coarse_out, void* workspace, size_t ws_bytes, void* stream) {
+  if (!h || !wq || !scales || !biases || !w_fine || !out_idx || !out_fine || !workspace) return QMTP_ERR_ARG;
+  if (ws_bytes < qmtp_lmhead2_workspace(M, V, k)) return QMTP_ERR_ARG;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  const size_t coarse_bytes = (size_t(M) * V * sizeof(uint16_t) + 255) / 256 * 256;
+  void* coarse = coarse_out ? coarse_out : ws;
+  int rc = qmtp_qmv_affine_g64(h, wq, scales, biases, coarse, M, V, K, V, stream);
+  if (rc != QMTP_OK) return rc;
+  return qmtp_topk_rescore(coarse, V, M, V, k, w_fine, h, K, out_idx, out_fine, out_argmax, ws + coarse_bytes,
+                           ws_bytes - coarse_bytes, stream);
+}

@@ -59,7 +59,16 @@ SIGNATURES.update({
     "qmtp_gdn_fused": [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
     "qmtp_gdn_fused_ex": [ctypes.POINTER(GdnArgs), _P],
     "qmtp_gdn_norm_gate": [_P, _P, _I, _P, _P, _I, _I, _I, _I, _F, _P],
+    "qmtp_lmhead2": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
+    "qmtp_topk_rescore": [_P, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t, _P],
+    "qmtp_argmax_bf16": [_P, _I, _I, _I, _P, _P, ctypes.c_size_t, _P],
 })
+# size queries return size_t
+SIZE_QUERIES: dict[str, list] = {
+    "qmtp_lmhead2_workspace": [_I, _I, _I],
+    "qmtp_topk_workspace": [_I, _I, _I],
+    "qmtp_argmax_workspace": [_I, _I],
+}
 
 _lib = None
 _lock = threading.Lock()
@@ -84,6 +93,10 @@ def lib() -> ctypes.CDLL:
                 f = getattr(L, name)
                 f.argtypes = args
                 f.restype = _I
+            for name, args in SIZE_QUERIES.items():
+                f = getattr(L, name)
+                f.argtypes = args
+                f.restype = ctypes.c_size_t
             L.qmtp_strerror.argtypes = [_I]
             L.qmtp_strerror.restype = ctypes.c_char_p
             _lib = L
@@ -91,7 +104,7 @@ def lib() -> ctypes.CDLL:
 
 
 def exported_symbols() -> list[str]:
-    return [*SIGNATURES, "qmtp_strerror"]
+    return [*SIGNATURES, *SIZE_QUERIES, "qmtp_strerror"]
 
 
 def check(rc: int, what: str) -> None:
