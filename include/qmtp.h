@@ -55,6 +55,11 @@ int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const 
 int qmtp_qmv_nvfp4_g16(const void* x, const void* w, const void* scales, void* y, int M, int N,
                        int K, int ldy, void* stream);
 
+/* qmtp_qmv_affine_g64 with a residual epilogue: y = bf16(res + bf16(x . W^T)) (the bf16 residual
+ * add of a decoder layer fused into the projection; res may alias y).  res bf16 [M, ldy]. */
+int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void* scales, const void* biases,
+                            void* y, const void* res, int M, int N, int K, int ldy, void* stream);
+
 /* Launch shape the qmv kernels use for (fmt 0 = affine g64, 1 = NVFP4 g16, M in 1..4, K):
  * resident CTAs per SM, threads per CTA, dynamic shared memory, rows per pipeline stage.  The grid
  * is min(N, SMs * ctas_per_sm).  Host-only query (first call per shape sets kernel attributes). */
@@ -104,6 +109,7 @@ typedef struct qmtp_gdn_args {
   const void* qkv;           /* bf16 [S, >= C] new conv inputs */
   long long ld_qkv;
   void* win_out;             /* bf16 [KC-1+S, C] or NULL */
+  const int* win_out_row_off;/* device int: win_out starts *win_out_row_off rows later (NULL: 0) */
   const void* conv_w;
   const void* a;
   const void* b;
@@ -155,6 +161,66 @@ int qmtp_topk_rescore(const void* vals, int ld, int M, int V, int k, const void*
 size_t qmtp_argmax_workspace(int M, int V);
 int qmtp_argmax_bf16(const void* vals, int ld, int M, int V, int* out, void* workspace,
                      size_t ws_bytes, void* stream);
+
+/* --------------------------------------------------------------------------------------------
+ * Decoder ops of the synthetic Qwen3.5 model (mtp.py:143-153 backbone, mtp.py:35-45 MTP layer;
+ * layer structure of mlx-lm qwen3_5, cross-checked with transformers' Qwen3.5).  Positions may come
+ * from a device int (pos_ptr, + pos_add + row), so the calls can sit in a replayed CUDA graph. */
+
+/* Quantized embedding gather (affine g64 rows): out[t] = bf16(fma(s, q, b)) of row tokens[t]. */
+int qmtp_embed(const int* tokens, int T, const void* wq, const void* scales, const void* biases, int V,
+               int D, void* out, int ld_out, void* stream);
+
+/* RMSNorm (mx.fast.rms_norm): out = bf16(w * bf16(x * r)), r = 1/sqrt(mean(x^2) + eps), D % 1024 == 0.
+ * Row m reads x row (*row_sel + m) when row_sel != NULL. */
+int qmtp_rmsnorm(const void* x, int ld_x, const int* row_sel, const void* w, float eps, void* out,
+                 int ld_out, int M, int D, void* stream);
+
+/* Gated-attention input prep (Dh 256, rotary 64): per-head q/k RMS norm, rotate-half RoPE from the
+ * cos/sin tables [max_pos][32], q and gate out [S, nq, Dh], k and v appended to the caches
+ * [nkv, max_pos, Dh] at position *pos_ptr + pos_add + s. */
+int qmtp_attn_prep(const void* qkv, int ld, int S, int nq, int nkv, int Dh, int rotary, const void* qn_w,
+                   const void* kn_w, float eps, const float* cos_t, const float* sin_t, const int* pos_ptr,
+                   int pos_add, void* q_out, void* gate_out, void* k_cache, void* v_cache, int max_pos,
+                   void* stream);
+
+/* Causal decode attention over the caches (query s sees keys 0..pos+s) with the sigmoid output
+ * gate: out bf16 [S, nq*Dh] = bf16(attn * sigmoid(gate)).  Dh 256. */
+int qmtp_attention(const void* q, const void* gate, const void* k_cache, const void* v_cache, int max_pos,
+                   int S, int nq, int nkv, int Dh, const int* pos_ptr, int pos_add, void* out,
+                   void* stream);
+
+/* SwiGLU of mlx-lm's MLP: out [S, I] = bf16(silu(gate) * up), gu [S, ld] = (gate | up) columns. */
+int qmtp_swiglu(const void* gu, int ld, int S, int I, void* out, void* stream);
+
+/* Control block of the device-side speculative loop (int32 [QMTP_CTRL_SIZE]). */
+#define QMTP_CTRL_SLOT 0      /* GatedDeltaNet state ring slot before the next verify */
+#define QMTP_CTRL_CONV_ROW 1  /* row of the conv state inside the [2 * win_rows, C] window buffer */
+#define QMTP_CTRL_WOUT_ROW 2  /* row where the next window is written */
+#define QMTP_CTRL_WPAR 3      /* window buffer parity */
+#define QMTP_CTRL_POS 4       /* tokens in the trunk KV caches */
+#define QMTP_CTRL_MPOS 5      /* committed entries of the MTP KV cache */
+#define QMTP_CTRL_KEEP 6      /* tokens kept by the last verify (1..k+1) */
+#define QMTP_CTRL_SEL 7       /* KEEP - 1 */
+#define QMTP_CTRL_NOUT 8      /* tokens emitted so far */
+#define QMTP_CTRL_CYCLES 9    /* verify cycles */
+#define QMTP_CTRL_ACC0 10     /* accepted-draft counters per draft position */
+#define QMTP_CTRL_EMIT0 20    /* tokens emitted by the last cycle (KEEP of them) */
+#define QMTP_CTRL_MAX_K 8
+#define QMTP_CTRL_SIZE 32
+
+/* Greedy verification + rollback bookkeeping (mtp.py:275-294, engine.py:121-128, mtp.py:136-140):
+ * a = verify argmax [k+1], in = [t, d_1..d_k]; keep = 1 + leading drafts equal to a; appends
+ * a[0..keep) to out_tokens (forced_keep > 0: keep = forced_keep, nothing emitted, prefill);
+ * advances POS, the state-ring slot and the conv window by keep. */
+int qmtp_mtp_accept(const int* a, const int* in, int k, int* ctrl, int* out_tokens, int out_cap,
+                    int ring_slots, int win_rows, int forced_keep, void* stream);
+
+/* MPOS += KEEP (the MTP cache keeps the real pairs of this cycle; mtp.py:291-294). */
+int qmtp_mtp_advance(int* ctrl, void* stream);
+
+/* Next verify input: in = [a[SEL], drafts[0..k)]. */
+int qmtp_next_tokens(const int* a, const int* drafts, int k, const int* ctrl, int* in, void* stream);
 
 #ifdef __cplusplus
 }

@@ -624,3 +624,189 @@ QO_API int qo_argmax_bf16(const uint16_t* vals, int M, int V, int ld, int32_t* o
   }
   return 0;
 }
+
+/* ------------------------------------------------------------------ decoder ops
+ * Sums of squares for RMS norms have two fixed trees:
+ *   wide (D % 1024 == 0): 32-element contiguous chunk partials (fmaf from 0), butterfly over each
+ *        block of 32 chunks, blocks added in order (the qmv reduction tree);
+ *   head (D % 32 == 0, D <= 1024): lane l sums elements [l*D/32, (l+1)*D/32) (fmaf from 0), butterfly.
+ * RMSNorm (mx.fast.rms_norm, as restated in gdn_fused.py:123-126): r = 1/sqrt(ss/D + eps),
+ * y = R(w * R(x * r)). */
+static float qo_sumsq_wide(const float* x, int D) {
+  float y = 0.0f;
+  for (int i = 0; i < D / 1024; ++i) {
+    float P[32];
+    for (int l = 0; l < 32; ++l) {
+      float acc = 0.0f;
+      for (int e = 0; e < 32; ++e) { float v = x[1024 * i + 32 * l + e]; acc = fmaf(v, v, acc); }
+      P[l] = acc;
+    }
+    float B = qo_butterfly32(P);
+    y = (i == 0) ? B : y + B;
+  }
+  return y;
+}
+static float qo_sumsq_head(const float* x, int D) {
+  int NP = D / 32;
+  float P[32];
+  for (int l = 0; l < 32; ++l) {
+    float acc = 0.0f;
+    for (int e = 0; e < NP; ++e) { float v = x[NP * l + e]; acc = fmaf(v, v, acc); }
+    P[l] = acc;
+  }
+  return qo_butterfly32(P);
+}
+
+/* x bf16 [M, D] (row stride ld_x) -> out bf16 [M, D] (row stride ld_o); wide tree if D % 1024 == 0
+ * else head tree.  w bf16 [D]. */
+QO_API void qo_rmsnorm(const uint16_t* x, int ld_x, const uint16_t* w, float eps, uint16_t* out, int ld_o, int M, int D) {
+  float* xf = (float*)malloc(sizeof(float) * D);
+  for (int m = 0; m < M; ++m) {
+    for (int e = 0; e < D; ++e) xf[e] = qo_bf2f(x[(size_t)m * ld_x + e]);
+    float ss = (D % 1024 == 0) ? qo_sumsq_wide(xf, D) : qo_sumsq_head(xf, D);
+    float r = 1.0f / sqrtf(ss / (float)D + eps);
+    for (int e = 0; e < D; ++e) out[(size_t)m * ld_o + e] = qo_f2bf(qo_bf2f(w[e]) * qo_R(xf[e] * r));
+  }
+  free(xf);
+}
+
+/* Quantized embedding gather (nn.QuantizedEmbedding): out[t] = bf16(fma(s, q, b)) of row tok[t]. */
+QO_API void qo_embed(const int32_t* tok, int T, const uint32_t* wq, const uint16_t* sc, const uint16_t* bi, int D,
+                     uint16_t* out) {
+  int G = D / 64;
+  for (int t = 0; t < T; ++t) {
+    size_t r = (size_t)tok[t];
+    for (int e = 0; e < D; ++e) {
+      uint32_t q = (wq[(r * D + e) / 8] >> (4 * (e % 8))) & 15u;
+      out[(size_t)t * D + e] = qo_f2bf(fmaf(qo_bf2f(sc[r * G + e / 64]), (float)q, qo_bf2f(bi[r * G + e / 64])));
+    }
+  }
+}
+
+/* Gated attention input prep (hf:modeling_qwen3_5.py:647-668 structure; MLX-style rounding):
+ * for token s of the S rows of qkv (row stride ld): q heads [nq][2*Dh] (query then gate),
+ * k [nkv][Dh], v [nkv][Dh] after the q part.  q, k: per-head RMS norm (head tree) with weights
+ * qn_w / kn_w, then partial rotate-half RoPE on the first R dims with cos/sin tables [pos][R/2]:
+ *   o_i = R(x_i*c - x_{i+R/2}*s),  o_{i+R/2} = R(x_{i+R/2}*c + x_i*s)   (products rounded, then sum).
+ * Outputs: qo bf16 [S, nq, Dh], gate bf16 [S, nq, Dh], k/v written into the caches
+ * kc/vc [nkv, max_pos, Dh] at position pos0 + s. */
+QO_API void qo_attn_prep(const uint16_t* qkv, int ld, int S, int nq, int nkv, int Dh, int R, const uint16_t* qn_w,
+                         const uint16_t* kn_w, float eps, const float* cos_t, const float* sin_t, int pos0,
+                         uint16_t* qo, uint16_t* gate, uint16_t* kc, uint16_t* vc, int max_pos) {
+  float* x = (float*)malloc(sizeof(float) * Dh);
+  uint16_t* tmp = (uint16_t*)malloc(sizeof(uint16_t) * Dh);
+  int half = R / 2;
+  for (int s = 0; s < S; ++s) {
+    const uint16_t* row = qkv + (size_t)s * ld;
+    int pos = pos0 + s;
+    const float* c = cos_t + (size_t)pos * half;
+    const float* sn = sin_t + (size_t)pos * half;
+    for (int hh = 0; hh < nq + nkv; ++hh) {
+      int isq = hh < nq;
+      const uint16_t* src = isq ? row + (size_t)hh * 2 * Dh : row + (size_t)nq * 2 * Dh + (size_t)(hh - nq) * Dh;
+      for (int e = 0; e < Dh; ++e) x[e] = qo_bf2f(src[e]);
+      float r = 1.0f / sqrtf(qo_sumsq_head(x, Dh) / (float)Dh + eps);
+      const uint16_t* w = isq ? qn_w : kn_w;
+      for (int e = 0; e < Dh; ++e) x[e] = qo_bf2f(qo_f2bf(qo_bf2f(w[e]) * qo_R(x[e] * r)));
+      for (int e = 0; e < Dh; ++e) tmp[e] = qo_f2bf(x[e]);
+      for (int i = 0; i < half; ++i) {
+        float a = x[i] * c[i], b = x[i + half] * sn[i];
+        float a2 = x[i + half] * c[i], b2 = x[i] * sn[i];
+        tmp[i] = qo_f2bf(a - b);
+        tmp[i + half] = qo_f2bf(a2 + b2);
+      }
+      if (isq) {
+        memcpy(qo + ((size_t)s * nq + hh) * Dh, tmp, sizeof(uint16_t) * Dh);
+        memcpy(gate + ((size_t)s * nq + hh) * Dh, src + Dh, sizeof(uint16_t) * Dh);
+      } else {
+        int kh = hh - nq;
+        memcpy(kc + ((size_t)kh * max_pos + pos) * Dh, tmp, sizeof(uint16_t) * Dh);
+        memcpy(vc + ((size_t)kh * max_pos + pos) * Dh, row + (size_t)nq * 2 * Dh + (size_t)nkv * Dh + (size_t)kh * Dh,
+               sizeof(uint16_t) * Dh);
+      }
+    }
+  }
+  free(x); free(tmp);
+}
+
+/* Decode attention with the sigmoid output gate.  Query s (position pos0 + s) of head h attends
+ * keys 0..pos0+s of kv head h / (nq/nkv).  Keys are dealt to NW = 8 splits (key j -> split j % 8):
+ *   score_j = dot(q, k_j) (head tree: lane l takes Dh/32 contiguous dims, fmaf, butterfly) * Dh^-1/2
+ *   per split w: m_w = max score; e_j = exp(score_j - m_w); den_w = sum e_j; num_w[d] = sum
+ *   fma(e_j, v_jd, .) (keys ascending, from 0);
+ *   M = max m_w; c_w = exp(m_w - M); den = sum_w fma(c_w, den_w, .); num_d likewise (w ascending);
+ *   o_d = R(num_d / den); out_d = R(o_d * sigmoid_bf(gate_d)). */
+QO_API void qo_attention(const uint16_t* q, const uint16_t* gate, const uint16_t* kc, const uint16_t* vc, int max_pos,
+                         int S, int nq, int nkv, int Dh, int pos0, uint16_t* out) {
+  const int NW = 8;
+  float scale = 1.0f / sqrtf((float)Dh);
+  int grp = nq / nkv;
+  float* qf = (float*)malloc(sizeof(float) * Dh);
+  float* kf = (float*)malloc(sizeof(float) * Dh);
+  float* num = (float*)malloc(sizeof(float) * NW * Dh);
+  float* acc = (float*)malloc(sizeof(float) * Dh);
+  for (int s = 0; s < S; ++s)
+    for (int h = 0; h < nq; ++h) {
+      int L = pos0 + s + 1, kh = h / grp;
+      for (int e = 0; e < Dh; ++e) qf[e] = qo_bf2f(q[((size_t)s * nq + h) * Dh + e]);
+      float* sc = (float*)malloc(sizeof(float) * L);
+      for (int j = 0; j < L; ++j) {
+        const uint16_t* kr = kc + ((size_t)kh * max_pos + j) * Dh;
+        int NP = Dh / 32;
+        float P[32];
+        for (int l = 0; l < 32; ++l) {
+          float a = 0.0f;
+          for (int e = 0; e < NP; ++e) a = fmaf(qf[NP * l + e], qo_bf2f(kr[NP * l + e]), a);
+          P[l] = a;
+        }
+        sc[j] = qo_butterfly32(P) * scale;
+      }
+      float mw[8], den[8];
+      int nonempty[8];
+      for (int w = 0; w < NW; ++w) {
+        nonempty[w] = w < L;
+        mw[w] = -INFINITY; den[w] = 0.0f;
+        for (int d = 0; d < Dh; ++d) num[w * Dh + d] = 0.0f;
+        if (!nonempty[w]) continue;
+        for (int j = w; j < L; j += NW) mw[w] = sc[j] > mw[w] ? sc[j] : mw[w];
+        for (int j = w; j < L; j += NW) {
+          float e = qo_expf(sc[j] - mw[w]);
+          den[w] = den[w] + e;
+          const uint16_t* vr = vc + ((size_t)kh * max_pos + j) * Dh;
+          for (int d = 0; d < Dh; ++d) num[w * Dh + d] = fmaf(e, qo_bf2f(vr[d]), num[w * Dh + d]);
+        }
+      }
+      float M = -INFINITY;
+      for (int w = 0; w < NW; ++w) if (nonempty[w] && mw[w] > M) M = mw[w];
+      float dsum = 0.0f;
+      for (int d = 0; d < Dh; ++d) acc[d] = 0.0f;
+      for (int w = 0; w < NW; ++w) {
+        if (!nonempty[w]) continue;
+        float cw = qo_expf(mw[w] - M);
+        dsum = fmaf(cw, den[w], dsum);
+        for (int d = 0; d < Dh; ++d) acc[d] = fmaf(cw, num[w * Dh + d], acc[d]);
+      }
+      for (int d = 0; d < Dh; ++d) {
+        float o = qo_R(acc[d] / dsum);
+        float gt = qo_bf2f(gate[((size_t)s * nq + h) * Dh + d]);
+        out[(size_t)s * nq * Dh + (size_t)h * Dh + d] = qo_f2bf(o * qo_sigmoid_bf(gt));
+      }
+      free(sc);
+    }
+  free(qf); free(kf); free(num); free(acc);
+}
+
+/* SwiGLU (mlx-lm MLP: down(silu(gate(x)) * up(x))): act = R(silu_bf(g) * u); gu bf16 [S, 2I]
+ * (gate columns then up columns, row stride ld) -> out bf16 [S, I]. */
+QO_API void qo_swiglu(const uint16_t* gu, int ld, int S, int I, uint16_t* out) {
+  for (int s = 0; s < S; ++s)
+    for (int i = 0; i < I; ++i) {
+      float g = qo_bf2f(gu[(size_t)s * ld + i]), u = qo_bf2f(gu[(size_t)s * ld + I + i]);
+      out[(size_t)s * I + i] = qo_f2bf(qo_silu_bf(g) * u);
+    }
+}
+
+/* bf16 residual add: out = R(a + b). */
+QO_API void qo_add_bf16(const uint16_t* a, const uint16_t* b, uint16_t* out, long n) {
+  for (long i = 0; i < n; ++i) out[i] = qo_f2bf(qo_bf2f(a[i]) + qo_bf2f(b[i]));
+}

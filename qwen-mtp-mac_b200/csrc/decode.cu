@@ -1,0 +1,389 @@
+// Decoder glue kernels for the synthetic Qwen3.5 model and the device-side speculative-decoding
+// control of mtp.py:241-303.  Every position, length and rollback index is read from a device
+// control block (qmtp_ctrl_*), so one verify + draft cycle can be captured once in a CUDA graph
+// and replayed with one host read of the emitted tokens per cycle.
+//
+// Arithmetic (fixed fp32 sequences, bit-identical to oracle/qmtp_oracle.c):
+//   rmsnorm     wide tree (D % 1024 == 0: thread c owns the 32-element chunk c) or head tree
+//   attn_prep   q/k head RMS norm (head tree), partial rotate-half RoPE, KV-cache append
+//   attention   keys dealt to 8 splits (one warp each), two-pass softmax per split, fixed merge,
+//               output gate R(o * sigmoid_bf(gate))
+//   swiglu      R(silu_bf(g) * u)
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace qmtp {
+
+// ----------------------------------------------------------------------------- embedding
+__global__ void embed_kernel(const int32_t* __restrict__ tok, const uint32_t* __restrict__ wq,
+                             const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, int D,
+                             uint16_t* __restrict__ out, long long ld_out, int V, unsigned* err) {
+  const int t = blockIdx.x;
+  const int r = tok[t];
+  if (r < 0 || r >= V) {
+    if (threadIdx.x == 0) atomicOr(err, DEVERR_BADARG);
+    return;
+  }
+  const int G = D / 64;
+  for (int w = threadIdx.x; w < D / 8; w += blockDim.x) {
+    const uint32_t word = wq[size_t(r) * (D / 8) + w];
+    const int g = (8 * w) / 64;
+    const float s = bf2f(sc[size_t(r) * G + g]), b = bf2f(bi[size_t(r) * G + g]);
+    uint16_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = f2bf(__fmaf_rn(s, float((word >> (4 * j)) & 15u), b));
+    *reinterpret_cast<uint4*>(out + t * ld_out + 8 * w) =
+        make_uint4(o[0] | (uint32_t(o[1]) << 16), o[2] | (uint32_t(o[3]) << 16), o[4] | (uint32_t(o[5]) << 16),
+                   o[6] | (uint32_t(o[7]) << 16));
+  }
+}
+
+// ----------------------------------------------------------------------------- RMSNorm
+// Wide tree: blockDim = D/32 threads, thread c owns elements [32c, 32c+32).
+__global__ void rmsnorm_wide_kernel(const uint16_t* __restrict__ x, long long ld_x, const int* __restrict__ row_sel,
+                                    const uint16_t* __restrict__ w, float eps, uint16_t* __restrict__ out,
+                                    long long ld_o, int D) {
+  __shared__ float s_blk[32];
+  __shared__ float s_r;
+  const int m = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
+  const long long row = row_sel ? (long long)(*row_sel) + m : m;
+  const uint16_t* xr = x + row * ld_x + 32 * c;
+  float v[32];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 u = *reinterpret_cast<const uint4*>(xr + 8 * q);
+    const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) { v[8 * q + 2 * h] = bflo(uu[h]); v[8 * q + 2 * h + 1] = bfhi(uu[h]); }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) ss = __fmaf_rn(v[e], v[e], ss);
+  ss = warp_sum(ss);
+  if (lane == 0) s_blk[warp] = ss;
+  __syncthreads();
+  if (c == 0) {
+    float t = s_blk[0];
+    for (int i = 1; i < int(blockDim.x >> 5); ++i) t = __fadd_rn(t, s_blk[i]);
+    s_r = rsqrt_rn(__fadd_rn(__fdiv_rn(t, float(D)), eps));
+  }
+  __syncthreads();
+  const float r = s_r;
+  uint16_t* orow = out + (long long)m * ld_o + 32 * c;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 wu = *reinterpret_cast<const uint4*>(w + 32 * c + 8 * q);
+    const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const uint16_t lo = f2bf(__fmul_rn(bflo(ww[h]), R(__fmul_rn(v[8 * q + 2 * h], r))));
+      const uint16_t hi = f2bf(__fmul_rn(bfhi(ww[h]), R(__fmul_rn(v[8 * q + 2 * h + 1], r))));
+      o[h] = lo | (uint32_t(hi) << 16);
+    }
+    *reinterpret_cast<uint4*>(orow + 8 * q) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ----------------------------------------------------------------------------- attention prep
+// One warp per (token s, head hh) with hh < nq query heads, then nkv key heads; Dh == 256,
+// lane l owns dims [8l, 8l+8); RoPE pairs (i, i + R/2) for i < R/2 (R == 64: lanes 0..7).
+__global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld, int S, int nq, int nkv,
+                                 const uint16_t* __restrict__ qn_w, const uint16_t* __restrict__ kn_w, float eps,
+                                 const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                 const int* __restrict__ pos_ptr, int pos_add, uint16_t* __restrict__ qo,
+                                 uint16_t* __restrict__ gate, uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
+                                 int max_pos, unsigned* err) {
+  constexpr int Dh = 256, NP = 8, RH = 32;  // rotary half
+  const int lane = threadIdx.x & 31;
+  const int wid = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (wid >= S * (nq + nkv)) return;
+  const int s = wid / (nq + nkv), hh = wid - s * (nq + nkv);
+  const int pos = (pos_ptr ? *pos_ptr : 0) + pos_add + s;
+  if (pos < 0 || pos >= max_pos) {
+    if (lane == 0) atomicOr(err, DEVERR_BADARG);
+    return;
+  }
+  const bool isq = hh < nq;
+  const uint16_t* row = qkv + (long long)s * ld;
+  const uint16_t* src = isq ? row + (long long)hh * 2 * Dh : row + (long long)nq * 2 * Dh + (long long)(hh - nq) * Dh;
+  float x[NP];
+  {
+    const uint4 u = *reinterpret_cast<const uint4*>(src + NP * lane);
+    const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) { x[2 * h] = bflo(uu[h]); x[2 * h + 1] = bfhi(uu[h]); }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int e = 0; e < NP; ++e) ss = __fmaf_rn(x[e], x[e], ss);
+  ss = warp_sum(ss);
+  const float r = rsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(Dh)), eps));
+  const uint16_t* wn = isq ? qn_w : kn_w;
+#pragma unroll
+  for (int e = 0; e < NP; ++e) x[e] = R(__fmul_rn(bf2f(wn[NP * lane + e]), R(__fmul_rn(x[e], r))));
+  // rotate-half over dims [0, 64): lane l (< 8) pairs with lane l ^ 4
+  float o[NP];
+#pragma unroll
+  for (int e = 0; e < NP; ++e) {
+    const float partner = __shfl_xor_sync(0xFFFFFFFFu, x[e], 4);
+    o[e] = x[e];
+    if (lane < 8) {
+      const int d = NP * lane + e;          // this lane's dim
+      const int i = d < RH ? d : d - RH;    // frequency index
+      const float c = cos_t[(long long)pos * RH + i], sn = sin_t[(long long)pos * RH + i];
+      if (d < RH) o[e] = __fsub_rn(__fmul_rn(x[e], c), __fmul_rn(partner, sn));
+      else o[e] = __fadd_rn(__fmul_rn(x[e], c), __fmul_rn(partner, sn));
+    }
+  }
+  uint32_t pk[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) pk[h] = f2bf(o[2 * h]) | (uint32_t(f2bf(o[2 * h + 1])) << 16);
+  const uint4 packed = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  if (isq) {
+    *reinterpret_cast<uint4*>(qo + ((long long)s * nq + hh) * Dh + NP * lane) = packed;
+    *reinterpret_cast<uint4*>(gate + ((long long)s * nq + hh) * Dh + NP * lane) =
+        *reinterpret_cast<const uint4*>(src + Dh + NP * lane);
+  } else {
+    const int kh = hh - nq;
+    *reinterpret_cast<uint4*>(kc + ((long long)kh * max_pos + pos) * Dh + NP * lane) = packed;
+    *reinterpret_cast<uint4*>(vc + ((long long)kh * max_pos + pos) * Dh + NP * lane) =
+        *reinterpret_cast<const uint4*>(row + (long long)nq * 2 * Dh + (long long)nkv * Dh + (long long)kh * Dh +
+                                        NP * lane);
+  }
+}
+
+// ----------------------------------------------------------------------------- attention
+// grid (nq, S); 8 warps = 8 key splits; Dh == 256 (lane owns 8 dims); scores in shared memory.
+constexpr int kAttnSplits = 8;
+
+__global__ void __launch_bounds__(kAttnSplits * 32)
+attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ gate, const uint16_t* __restrict__ kc,
+                 const uint16_t* __restrict__ vc, int max_pos, int nq, int nkv, const int* __restrict__ pos_ptr,
+                 int pos_add, uint16_t* __restrict__ out, unsigned* err) {
+  constexpr int Dh = 256, NP = 8;
+  extern __shared__ __align__(16) float sm[];
+  float* s_num = sm;                              // [8][Dh]
+  float* s_m = s_num + kAttnSplits * Dh;          // [8]
+  float* s_den = s_m + kAttnSplits;               // [8]
+  float* s_sc = s_den + kAttnSplits;              // [8][max_pos/8 + 1]
+  const int h = blockIdx.x, s = blockIdx.y, S = gridDim.y;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int L = (pos_ptr ? *pos_ptr : 0) + pos_add + s + 1;
+  const int stride_sc = max_pos / kAttnSplits + 1;
+  if (L < 1 || L > max_pos) {
+    if (threadIdx.x == 0) atomicOr(err, DEVERR_BADARG);
+    return;
+  }
+  const int kh = h / (nq / nkv);
+  float qf[NP];
+  {
+    const uint4 u = *reinterpret_cast<const uint4*>(q + ((long long)s * nq + h) * Dh + NP * lane);
+    const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) { qf[2 * e] = bflo(uu[e]); qf[2 * e + 1] = bfhi(uu[e]); }
+  }
+  const float scale = rsqrt_rn(float(Dh));
+  // pass 1: scores and split max
+  float mw = __int_as_float(0xFF800000);
+  int n = 0;
+  for (int j = w; j < L; j += kAttnSplits, ++n) {
+    const uint4 u = *reinterpret_cast<const uint4*>(kc + ((long long)kh * max_pos + j) * Dh + NP * lane);
+    const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+    float acc = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc = __fmaf_rn(qf[2 * e], bflo(uu[e]), acc);
+      acc = __fmaf_rn(qf[2 * e + 1], bfhi(uu[e]), acc);
+    }
+    const float sc = __fmul_rn(warp_sum(acc), scale);
+    if (lane == 0) s_sc[w * stride_sc + n] = sc;
+    mw = sc > mw ? sc : mw;
+  }
+  __syncwarp();
+  // pass 2: exp, denominator, numerator (this lane's 8 dims)
+  float den = 0.0f, num[NP];
+#pragma unroll
+  for (int e = 0; e < NP; ++e) num[e] = 0.0f;
+  n = 0;
+  for (int j = w; j < L; j += kAttnSplits, ++n) {
+    const float e_ = q_expf(__fsub_rn(s_sc[w * stride_sc + n], mw));
+    den = __fadd_rn(den, e_);
+    const uint4 u = *reinterpret_cast<const uint4*>(vc + ((long long)kh * max_pos + j) * Dh + NP * lane);
+    const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      num[2 * e] = __fmaf_rn(e_, bflo(uu[e]), num[2 * e]);
+      num[2 * e + 1] = __fmaf_rn(e_, bfhi(uu[e]), num[2 * e + 1]);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < NP; ++e) s_num[w * Dh + NP * lane + e] = num[e];
+  if (lane == 0) { s_m[w] = mw; s_den[w] = den; }
+  __syncthreads();
+  // merge: thread d owns output dim d
+  const int d = threadIdx.x;
+  float M = __int_as_float(0xFF800000);
+  for (int ww = 0; ww < kAttnSplits; ++ww)
+    if (ww < L && s_m[ww] > M) M = s_m[ww];
+  float dsum = 0.0f, acc = 0.0f;
+  for (int ww = 0; ww < kAttnSplits; ++ww) {
+    if (ww >= L) continue;
+    const float cw = q_expf(__fsub_rn(s_m[ww], M));
+    dsum = __fmaf_rn(cw, s_den[ww], dsum);
+    acc = __fmaf_rn(cw, s_num[ww * Dh + d], acc);
+  }
+  const float o = R(__fdiv_rn(acc, dsum));
+  const float gt = bf2f(gate[((long long)s * nq + h) * Dh + d]);
+  out[(long long)s * nq * Dh + (long long)h * Dh + d] = f2bf(__fmul_rn(o, sigmoid_bf(gt)));
+  (void)S;
+}
+
+// ----------------------------------------------------------------------------- SwiGLU
+__global__ void swiglu_kernel(const uint16_t* __restrict__ gu, long long ld, int I, uint16_t* __restrict__ out) {
+  const int s = blockIdx.y;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < I; i += gridDim.x * blockDim.x) {
+    const float g = bf2f(gu[(long long)s * ld + i]), u = bf2f(gu[(long long)s * ld + I + i]);
+    out[(long long)s * I + i] = f2bf(__fmul_rn(silu_bf(g), u));
+  }
+}
+
+// ----------------------------------------------------------------------------- control
+// Greedy acceptance (mtp.py:275-294 / engine.py:121-128): a = verify argmax [k+1], in = [t, d_1..d_k].
+// keep = 1 + #leading drafts equal to a; emits a[0..keep); rollback bookkeeping for the next cycle.
+__global__ void accept_kernel(const int32_t* __restrict__ a, const int32_t* __restrict__ in, int k,
+                              int* __restrict__ ctrl, int32_t* __restrict__ out_tokens, int out_cap, int ring_slots,
+                              int win_rows, int forced_keep) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int n_acc = 0;
+  if (forced_keep > 0) {
+    n_acc = forced_keep - 1;
+  } else {
+    while (n_acc < k && a[n_acc] == in[1 + n_acc]) {
+      ctrl[QMTP_CTRL_ACC0 + n_acc] += 1;
+      ++n_acc;
+    }
+  }
+  const int keep = n_acc + 1;
+  int nout = ctrl[QMTP_CTRL_NOUT];
+  if (forced_keep <= 0) {
+    for (int i = 0; i < keep; ++i) {
+      ctrl[QMTP_CTRL_EMIT0 + i] = a[i];
+      if (nout < out_cap) out_tokens[nout++] = a[i];
+    }
+    ctrl[QMTP_CTRL_NOUT] = nout;
+    ctrl[QMTP_CTRL_CYCLES] += 1;
+  }
+  ctrl[QMTP_CTRL_KEEP] = keep;
+  ctrl[QMTP_CTRL_SEL] = keep - 1;
+  ctrl[QMTP_CTRL_POS] += keep;
+  ctrl[QMTP_CTRL_SLOT] = (ctrl[QMTP_CTRL_SLOT] + keep) % ring_slots;
+  const int par = ctrl[QMTP_CTRL_WPAR] ^ 1;  // the window just written becomes the previous one
+  ctrl[QMTP_CTRL_WPAR] = par;
+  ctrl[QMTP_CTRL_CONV_ROW] = par * win_rows + keep;
+  ctrl[QMTP_CTRL_WOUT_ROW] = (par ^ 1) * win_rows;
+}
+
+// MTP cache bookkeeping between the two draft steps: MPOS += keep (mtp.py:291-294: the k-1 chained
+// entries of the previous cycle are trimmed, the keep real pairs are committed).
+__global__ void mtp_advance_kernel(int* __restrict__ ctrl) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) ctrl[QMTP_CTRL_MPOS] += ctrl[QMTP_CTRL_KEEP];
+}
+
+// Next verify input [t, d1, d2]: t = a[keep-1].
+__global__ void next_tokens_kernel(const int32_t* __restrict__ a, const int32_t* __restrict__ drafts, int k,
+                                   const int* __restrict__ ctrl, int32_t* __restrict__ in) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  in[0] = a[ctrl[QMTP_CTRL_SEL]];
+  for (int i = 0; i < k; ++i) in[1 + i] = drafts[i];
+}
+
+}  // namespace qmtp
+
+using namespace qmtp;
+
+extern "C" int qmtp_embed(const int* tokens, int T, const void* wq, const void* scales, const void* biases, int V,
+                          int D, void* out, int ld_out, void* stream) {
+  if (!tokens || !wq || !scales || !biases || !out) return QMTP_ERR_ARG;
+  if (T < 1 || D % 64 != 0 || ld_out < D || ld_out % 8 != 0) return QMTP_ERR_SHAPE;
+  if (!aligned16(out)) return QMTP_ERR_ALIGN;
+  embed_kernel<<<T, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      tokens, static_cast<const uint32_t*>(wq), static_cast<const uint16_t*>(scales),
+      static_cast<const uint16_t*>(biases), D, static_cast<uint16_t*>(out), ld_out, V, device_error_ptr());
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_rmsnorm(const void* x, int ld_x, const int* row_sel, const void* w, float eps, void* out,
+                            int ld_out, int M, int D, void* stream) {
+  if (!x || !w || !out) return QMTP_ERR_ARG;
+  if (M < 1 || D % 1024 != 0 || D > 32768 || ld_x < D || ld_out < D || ld_x % 8 || ld_out % 8) return QMTP_ERR_SHAPE;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return QMTP_ERR_ALIGN;
+  rmsnorm_wide_kernel<<<M, D / 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(x), ld_x, row_sel, static_cast<const uint16_t*>(w), eps,
+      static_cast<uint16_t*>(out), ld_out, D);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_attn_prep(const void* qkv, int ld, int S, int nq, int nkv, int Dh, int rotary, const void* qn_w,
+                              const void* kn_w, float eps, const float* cos_t, const float* sin_t, const int* pos_ptr,
+                              int pos_add, void* q_out, void* gate_out, void* k_cache, void* v_cache, int max_pos,
+                              void* stream) {
+  if (!qkv || !qn_w || !kn_w || !cos_t || !sin_t || !q_out || !gate_out || !k_cache || !v_cache) return QMTP_ERR_ARG;
+  if (Dh != 256 || rotary != 64 || S < 1 || nq < 1 || nkv < 1 || nq % nkv || ld % 8) return QMTP_ERR_UNSUPPORTED;
+  const int warps = S * (nq + nkv), wpb = 8;
+  attn_prep_kernel<<<(warps + wpb - 1) / wpb, wpb * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(qkv), ld, S, nq, nkv, static_cast<const uint16_t*>(qn_w),
+      static_cast<const uint16_t*>(kn_w), eps, cos_t, sin_t, pos_ptr, pos_add, static_cast<uint16_t*>(q_out),
+      static_cast<uint16_t*>(gate_out), static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), max_pos,
+      device_error_ptr());
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_attention(const void* q, const void* gate, const void* k_cache, const void* v_cache, int max_pos,
+                              int S, int nq, int nkv, int Dh, const int* pos_ptr, int pos_add, void* out,
+                              void* stream) {
+  if (!q || !gate || !k_cache || !v_cache || !out) return QMTP_ERR_ARG;
+  if (Dh != 256 || S < 1 || nq < 1 || nkv < 1 || nq % nkv || max_pos < 8) return QMTP_ERR_UNSUPPORTED;
+  const size_t smem = (size_t(kAttnSplits) * 256 + 2 * kAttnSplits + size_t(kAttnSplits) * (max_pos / kAttnSplits + 1)) *
+                      sizeof(float);
+  if (smem > 200 * 1024) return QMTP_ERR_SHAPE;
+  static const cudaError_t attr =
+      cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (attr != cudaSuccess) return QMTP_ERR_CUDA;
+  attention_kernel<<<dim3(nq, S), kAttnSplits * 32, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(gate), static_cast<const uint16_t*>(k_cache),
+      static_cast<const uint16_t*>(v_cache), max_pos, nq, nkv, pos_ptr, pos_add, static_cast<uint16_t*>(out),
+      device_error_ptr());
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_swiglu(const void* gu, int ld, int S, int I, void* out, void* stream) {
+  if (!gu || !out) return QMTP_ERR_ARG;
+  if (S < 1 || I < 1 || ld < 2 * I) return QMTP_ERR_SHAPE;
+  swiglu_kernel<<<dim3(std::min((I + 255) / 256, 64), S), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(gu), ld, I, static_cast<uint16_t*>(out));
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_mtp_accept(const int* a, const int* in, int k, int* ctrl, int* out_tokens, int out_cap,
+                               int ring_slots, int win_rows, int forced_keep, void* stream) {
+  if (!a || !in || !ctrl || !out_tokens) return QMTP_ERR_ARG;
+  if (k < 1 || k > QMTP_CTRL_MAX_K || ring_slots < k + 2 || forced_keep > k + 1 || QMTP_CTRL_EMIT0 + k + 1 > QMTP_CTRL_SIZE)
+    return QMTP_ERR_SHAPE;
+  accept_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a, in, k, ctrl, out_tokens, out_cap, ring_slots,
+                                                                  win_rows, forced_keep);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_mtp_advance(int* ctrl, void* stream) {
+  if (!ctrl) return QMTP_ERR_ARG;
+  mtp_advance_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(ctrl);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_next_tokens(const int* a, const int* drafts, int k, const int* ctrl, int* in, void* stream) {
+  if (!a || !drafts || !ctrl || !in) return QMTP_ERR_ARG;
+  next_tokens_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a, drafts, k, ctrl, in);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}

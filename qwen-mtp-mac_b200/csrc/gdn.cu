@@ -111,7 +111,7 @@ gdn_fused_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
   }
   // window for the next step: q/k channels by the first CTA of their key head, v channels by owner
   if (A.win_out) {
-    uint16_t* wo = static_cast<uint16_t*>(A.win_out);
+    uint16_t* wo = static_cast<uint16_t*>(A.win_out) + (long long)(A.win_out_row_off ? *A.win_out_row_off : 0) * C;
     const int R_ = KC - 1 + S;
     if (dv0 == 0 && hv % (Hv / Hk) == 0) {
       for (int idx = tid; idx < R_ * 2 * Dk; idx += blockDim.x) {
@@ -287,6 +287,7 @@ extern "C" int qmtp_gdn_fused(const void* win, const void* conv_w, const void* a
   A.qkv = static_cast<const uint16_t*>(win) + (long long)(KC - 1) * C;
   A.ld_qkv = C;
   A.win_out = nullptr;
+  A.win_out_row_off = nullptr;
   A.conv_w = conv_w;
   A.a = a;
   A.b = b;

@@ -93,7 +93,8 @@ template <int FMT, int M, int W, int TR, int NS>
 __global__ void __launch_bounds__(W * 32, 1)
 qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
            const uint8_t* __restrict__ sc, const uint8_t* __restrict__ bi,
-           uint16_t* __restrict__ y, int N, int ldy, unsigned* __restrict__ err) {
+           uint16_t* __restrict__ y, const uint16_t* __restrict__ res, int N, int ldy,
+           unsigned* __restrict__ err) {
   using C = QmvCfg<FMT, M, W, TR, NS>;
   constexpr int K = C::K;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -263,7 +264,10 @@ qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
 #pragma unroll
       for (int w = 1; w < W; ++w) acc = __fadd_rn(acc, red[w * C::VP + tid]);
       const int r = tid / M, m = tid - (tid / M) * M;
-      y[size_t(m) * ldy + r0 + t * TR + r] = f2bf(acc);
+      const size_t o = size_t(m) * ldy + r0 + t * TR + r;
+      uint16_t out = f2bf(acc);
+      if (res) out = f2bf(__fadd_rn(bf2f(res[o]), bf2f(out)));  // residual: R(res + R(x.W))
+      y[o] = out;
     }
   }
 }
@@ -274,8 +278,8 @@ struct QmvLaunch {
 };
 
 template <int FMT, int M, int W>
-static int launch_qmv(const void* x, const void* w, const void* s, const void* b, void* y, int N, int ldy,
-                      cudaStream_t st, QmvLaunch* info = nullptr) {
+static int launch_qmv(const void* x, const void* w, const void* s, const void* b, void* y, const void* res, int N,
+                      int ldy, cudaStream_t st, QmvLaunch* info = nullptr) {
   constexpr int TR = (W <= 4) ? 8 : 4;
   constexpr int NS = 3;
   using C = QmvCfg<FMT, M, W, TR, NS>;
@@ -297,26 +301,27 @@ static int launch_qmv(const void* x, const void* w, const void* s, const void* b
   const int grid = std::max(1, std::min(N, sm_count() * occ));
   kern<<<grid, W * 32, C::SMEM, st>>>(static_cast<const uint16_t*>(x), static_cast<const uint32_t*>(w),
                                         static_cast<const uint8_t*>(s), static_cast<const uint8_t*>(b),
-                                        static_cast<uint16_t*>(y), N, ldy, device_error_ptr());
+                                        static_cast<uint16_t*>(y), static_cast<const uint16_t*>(res), N, ldy,
+                                        device_error_ptr());
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 
 template <int FMT, int M>
-static int dispatch_w(int K, const void* x, const void* w, const void* s, const void* b, void* y, int N, int ldy,
-                      cudaStream_t st, QmvLaunch* info = nullptr) {
+static int dispatch_w(int K, const void* x, const void* w, const void* s, const void* b, void* y, const void* res,
+                      int N, int ldy, cudaStream_t st, QmvLaunch* info = nullptr) {
   switch (K) {
-    case 1024: return launch_qmv<FMT, M, 1>(x, w, s, b, y, N, ldy, st, info);
-    case 2048: return launch_qmv<FMT, M, 2>(x, w, s, b, y, N, ldy, st, info);
-    case 4096: return launch_qmv<FMT, M, 4>(x, w, s, b, y, N, ldy, st, info);
-    case 8192: return launch_qmv<FMT, M, 8>(x, w, s, b, y, N, ldy, st, info);
-    case 12288: return launch_qmv<FMT, M, 12>(x, w, s, b, y, N, ldy, st, info);
+    case 1024: return launch_qmv<FMT, M, 1>(x, w, s, b, y, res, N, ldy, st, info);
+    case 2048: return launch_qmv<FMT, M, 2>(x, w, s, b, y, res, N, ldy, st, info);
+    case 4096: return launch_qmv<FMT, M, 4>(x, w, s, b, y, res, N, ldy, st, info);
+    case 8192: return launch_qmv<FMT, M, 8>(x, w, s, b, y, res, N, ldy, st, info);
+    case 12288: return launch_qmv<FMT, M, 12>(x, w, s, b, y, res, N, ldy, st, info);
     default: return QMTP_ERR_SHAPE;
   }
 }
 
 template <int FMT>
-static int qmv_entry(const void* x, const void* w, const void* s, const void* b, void* y, int M, int N, int K,
-                     int ldy, void* stream) {
+static int qmv_entry(const void* x, const void* w, const void* s, const void* b, void* y, const void* res, int M,
+                     int N, int K, int ldy, void* stream) {
   if (!x || !w || !s || !y || (FMT == FMT_AFFINE && !b)) return QMTP_ERR_ARG;
   if (M < 1 || N < 1 || K < 1024 || K % 1024 != 0 || K > 12288 || ldy < N) return QMTP_ERR_SHAPE;
   if (!aligned16(x) || !aligned16(w) || !aligned16(s) || (b && !aligned16(b))) return QMTP_ERR_ALIGN;
@@ -327,12 +332,13 @@ static int qmv_entry(const void* x, const void* w, const void* s, const void* b,
     const int mm = std::min(4, M - m0);
     const void* xm = xp + size_t(m0) * K;
     void* ym = yp + size_t(m0) * ldy;
+    const void* rm = res ? static_cast<const uint16_t*>(res) + size_t(m0) * ldy : nullptr;
     int rc;
     switch (mm) {
-      case 1: rc = dispatch_w<FMT, 1>(K, xm, w, s, b, ym, N, ldy, st); break;
-      case 2: rc = dispatch_w<FMT, 2>(K, xm, w, s, b, ym, N, ldy, st); break;
-      case 3: rc = dispatch_w<FMT, 3>(K, xm, w, s, b, ym, N, ldy, st); break;
-      default: rc = dispatch_w<FMT, 4>(K, xm, w, s, b, ym, N, ldy, st); break;
+      case 1: rc = dispatch_w<FMT, 1>(K, xm, w, s, b, ym, rm, N, ldy, st); break;
+      case 2: rc = dispatch_w<FMT, 2>(K, xm, w, s, b, ym, rm, N, ldy, st); break;
+      case 3: rc = dispatch_w<FMT, 3>(K, xm, w, s, b, ym, rm, N, ldy, st); break;
+      default: rc = dispatch_w<FMT, 4>(K, xm, w, s, b, ym, rm, N, ldy, st); break;
     }
     if (rc != QMTP_OK) return rc;
   }
@@ -382,12 +388,18 @@ using namespace qmtp;
 
 extern "C" int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const void* biases, void* y,
                                    int M, int N, int K, int ldy, void* stream) {
-  return qmv_entry<FMT_AFFINE>(x, w, scales, biases, y, M, N, K, ldy, stream);
+  return qmv_entry<FMT_AFFINE>(x, w, scales, biases, y, nullptr, M, N, K, ldy, stream);
+}
+
+extern "C" int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void* scales, const void* biases, void* y,
+                                       const void* res, int M, int N, int K, int ldy, void* stream) {
+  if (!res) return QMTP_ERR_ARG;
+  return qmv_entry<FMT_AFFINE>(x, w, scales, biases, y, res, M, N, K, ldy, stream);
 }
 
 extern "C" int qmtp_qmv_nvfp4_g16(const void* x, const void* w, const void* scales, void* y, int M, int N, int K,
                                   int ldy, void* stream) {
-  return qmv_entry<FMT_NVFP4>(x, w, scales, nullptr, y, M, N, K, ldy, stream);
+  return qmv_entry<FMT_NVFP4>(x, w, scales, nullptr, y, nullptr, M, N, K, ldy, stream);
 }
 
 extern "C" int qmtp_qmv_launch_info(int fmt, int M, int K, int* ctas_per_sm, int* threads, int* smem_bytes,
@@ -399,10 +411,10 @@ extern "C" int qmtp_qmv_launch_info(int fmt, int M, int K, int* ctas_per_sm, int
   auto go = [&](auto fmtc) -> int {
     constexpr int F = decltype(fmtc)::value;
     switch (M) {
-      case 1: return dispatch_w<F, 1>(K, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
-      case 2: return dispatch_w<F, 2>(K, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
-      case 3: return dispatch_w<F, 3>(K, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
-      default: return dispatch_w<F, 4>(K, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
+      case 1: return dispatch_w<F, 1>(K, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
+      case 2: return dispatch_w<F, 2>(K, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
+      case 3: return dispatch_w<F, 3>(K, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
+      default: return dispatch_w<F, 4>(K, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
     }
   };
   rc = fmt == 0 ? go(std::integral_constant<int, FMT_AFFINE>{}) : go(std::integral_constant<int, FMT_NVFP4>{});

@@ -45,7 +45,7 @@ SIGNATURES: dict[str, list] = {
 class GdnArgs(ctypes.Structure):
     """Mirror of qmtp_gdn_args (include/qmtp.h)."""
     _fields_ = [("conv_src", _P), ("ld_conv", ctypes.c_longlong), ("conv_row_off", _P),
-                ("qkv", _P), ("ld_qkv", ctypes.c_longlong), ("win_out", _P),
+                ("qkv", _P), ("ld_qkv", ctypes.c_longlong), ("win_out", _P), ("win_out_row_off", _P),
                 ("conv_w", _P), ("a", _P), ("b", _P), ("ld_ab", ctypes.c_longlong),
                 ("A_log", _P), ("dt_bias", _P),
                 ("state_in", _P), ("state_out", _P), ("state_mid", _P),
@@ -62,7 +62,21 @@ SIGNATURES.update({
     "qmtp_lmhead2": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     "qmtp_topk_rescore": [_P, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t, _P],
     "qmtp_argmax_bf16": [_P, _I, _I, _I, _P, _P, ctypes.c_size_t, _P],
+    "qmtp_qmv_affine_g64_res": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "qmtp_embed": [_P, _I, _P, _P, _P, _I, _I, _P, _I, _P],
+    "qmtp_rmsnorm": [_P, _I, _P, _P, _F, _P, _I, _I, _I, _P],
+    "qmtp_attn_prep": [_P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P],
+    "qmtp_attention": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P, _P],
+    "qmtp_swiglu": [_P, _I, _I, _I, _P, _P],
+    "qmtp_mtp_accept": [_P, _P, _I, _P, _P, _I, _I, _I, _I, _P],
+    "qmtp_mtp_advance": [_P, _P],
+    "qmtp_next_tokens": [_P, _P, _I, _P, _P, _P],
 })
+
+# control block layout (include/qmtp.h QMTP_CTRL_*)
+CTRL = dict(SLOT=0, CONV_ROW=1, WOUT_ROW=2, WPAR=3, POS=4, MPOS=5, KEEP=6, SEL=7, NOUT=8, CYCLES=9, ACC0=10,
+            EMIT0=20)
+CTRL_SIZE = 32
 # size queries return size_t
 SIZE_QUERIES: dict[str, list] = {
     "qmtp_lmhead2_workspace": [_I, _I, _I],

@@ -1,0 +1,329 @@
+"""Greedy MTP speculative decoding on B200 -- the mtp.py surface of qwen-mtp-mac.
+
+Reference: mtp.py:143-153 ``backbone``, mtp.py:199-209 ``mtp_step``, mtp.py:212-226 ``draft_chain``
+(chain="pre"), mtp.py:136-140 ``restore``, mtp.py:241-303 ``generate_mtp`` (greedy, fixed k,
+bb_hidden="pre") and the greedy branch of engine.py:121-128.
+
+B200 design.  Everything a cycle needs lives on the device: the GatedDeltaNet states in a ring of
+k+2 slots per layer (the state after each verify token is a slot, so ``restore`` is a slot index),
+the conv windows in two buffers per layer (the next conv state is a row offset), the KV caches with
+device-side lengths, and a control block (include/qmtp.h QMTP_CTRL_*) updated by the accept kernel.
+One verify + draft cycle is therefore a fixed sequence of launches, captured once as a CUDA graph
+and replayed; the host reads the control block (emitted tokens) once per cycle, as the reference
+evaluates once per cycle (mtp.py:276).  The prompt runs through the same verify-shaped step in
+chunks of k+1 tokens; every op is batch-invariant, so this equals one pass over the prompt.
+"""
+from __future__ import annotations
+
+import ctypes
+import time
+
+import numpy as np
+import torch
+
+from . import _lib
+from .lm_head2 import TwoStageHead
+from .model import ModelArgs, Weights, rope_tables
+
+C = _lib.CTRL
+
+
+class MTPDecoder:
+    """Device state + launch sequence of one greedy MTP decoding session (batch 1)."""
+
+    def __init__(self, args: ModelArgs, W: Weights, k: int = 2, max_tokens: int = 1024, device="cuda"):
+        self.a, self.W, self.k = args, W, k
+        self.S = k + 1
+        self.dev = torch.device(device)
+        a, S, dev = args, self.S, self.dev
+        self.L = _lib.lib()
+        bf, f32, i32 = torch.bfloat16, torch.float32, torch.int32
+        z = lambda *shape, dtype=bf: torch.zeros(shape, dtype=dtype, device=dev)
+        self.ctrl = z(_lib.CTRL_SIZE, dtype=i32)
+        self.ctrl_host = torch.zeros(_lib.CTRL_SIZE, dtype=i32).pin_memory()
+        self.tokens_in = z(S, dtype=i32)
+        self.a_tok = z(S, dtype=i32)
+        self.drafts = z(max(k, 1), dtype=i32)
+        self.m_tok = z(S, dtype=i32)
+        self.out_cap = max_tokens + S + 8
+        self.out_tokens = z(self.out_cap, dtype=i32)
+        self.cos, self.sin = rope_tables(a, dev)
+        # activations
+        H = a.hidden
+        self.h, self.xn, self.hn = z(S, H), z(S, H), z(S, H)
+        self.proj = z(S, max(a.gdn_proj, a.attn_proj))
+        self.ygdn = z(S, a.lin_hv, a.lin_dv, dtype=f32)
+        self.gdn_out = z(S, a.lin_hv * a.lin_dv)
+        self.att_out = z(S, a.n_heads * a.head_dim)
+        self.qb, self.gb = z(S, a.n_heads, a.head_dim), z(S, a.n_heads, a.head_dim)
+        self.gu, self.act = z(S, 2 * a.intermediate), z(S, a.intermediate)
+        self.memb, self.mcat, self.mx, self.mxn = z(S, H), z(S, 2 * H), z(S, H), z(1, H)
+        self.dlogits = z(1, a.vocab)
+        self.fine, self.idx = z(S, 64), z(S, 64, dtype=i32)
+        self.argmax_ws = torch.empty(self.L.qmtp_argmax_workspace(1, a.vocab), dtype=torch.uint8, device=dev)
+        # recurrent / cache state
+        self.lin_ids = [i for i in range(a.layers) if a.is_linear(i)]
+        self.att_ids = [i for i in range(a.layers) if not a.is_linear(i)]
+        self.slots = k + 2
+        self.win_rows = a.conv_k - 1 + S
+        self.ring = {i: z(self.slots, a.lin_hv, a.lin_dv, a.lin_dk, dtype=f32) for i in self.lin_ids}
+        self.win = {i: z(2 * self.win_rows, a.conv_dim) for i in self.lin_ids}
+        self.kv = {i: (z(a.n_kv, a.max_pos, a.head_dim), z(a.n_kv, a.max_pos, a.head_dim)) for i in self.att_ids}
+        self.mkv = (z(a.n_kv, a.max_pos, a.head_dim), z(a.n_kv, a.max_pos, a.head_dim))
+        self.head = TwoStageHead(W["lm_head"], 64, W["lm_head_q"])
+        self._gdn_args = {}
+        for i in self.lin_ids:
+            self._gdn_args[i] = self._make_gdn_args(i)
+        self.graph = None
+
+    # ------------------------------------------------------------------ helpers
+    def _cp(self, slot: int) -> int:
+        return self.ctrl.data_ptr() + 4 * slot
+
+    def _st(self):
+        return _lib.stream()
+
+    def _chk(self, rc, what):
+        if rc != 0:
+            _lib.check(rc, what)
+
+    def _qmv(self, x, lin, y, M, res=None, ldy=None, ldx=None):
+        ldy = ldy or lin.out_features
+        if res is None:
+            rc = self.L.qmtp_qmv_affine_g64(x.data_ptr(), lin.weight.data_ptr(), lin.scales.data_ptr(),
+                                            lin.biases.data_ptr(), y.data_ptr(), M, lin.out_features,
+                                            lin.in_features, ldy, self._st())
+        else:
+            rc = self.L.qmtp_qmv_affine_g64_res(x.data_ptr(), lin.weight.data_ptr(), lin.scales.data_ptr(),
+                                                lin.biases.data_ptr(), y.data_ptr(), res.data_ptr(), M,
+                                                lin.out_features, lin.in_features, ldy, self._st())
+        self._chk(rc, "qmv")
+
+    def _norm(self, x, w, out, M, ld_x=None, ld_o=None, row_sel=None):
+        H = w.shape[0]
+        self._chk(self.L.qmtp_rmsnorm(x.data_ptr(), ld_x or H, row_sel, w.data_ptr(), self.a.eps, out.data_ptr(),
+                                      ld_o or H, M, H, self._st()), "rmsnorm")
+
+    def _make_gdn_args(self, i):
+        a, L = self.a, self.W[f"layers.{i}"]
+        Cd, Z, ldp = a.conv_dim, a.lin_hv * a.lin_dv, self.proj.shape[1]
+        p = self.proj.data_ptr()
+        return _lib.GdnArgs(
+            conv_src=self.win[i].data_ptr(), ld_conv=Cd, conv_row_off=self._cp(C["CONV_ROW"]),
+            qkv=p, ld_qkv=ldp, win_out=self.win[i].data_ptr(), win_out_row_off=self._cp(C["WOUT_ROW"]),
+            conv_w=L["conv1d"].data_ptr(), a=p + 2 * (Cd + Z + a.lin_hv), b=p + 2 * (Cd + Z), ld_ab=ldp,
+            A_log=L["A_log"].data_ptr(), dt_bias=L["dt_bias"].data_ptr(), state_in=None, state_out=None,
+            state_mid=None, ring=self.ring[i].data_ptr(), ring_cur=self._cp(C["SLOT"]), ring_slots=self.slots,
+            y=self.ygdn.data_ptr(), S=self.S, Hk=a.lin_hk, Hv=a.lin_hv, Dk=a.lin_dk, Dv=a.lin_dv, KC=a.conv_k,
+            snap=1)
+
+    # ------------------------------------------------------------------ layers
+    def _attn_layer(self, L, x, rows, kc, vc, pos_slot):
+        """Gated attention block: x (pre-norm residual stream, [rows, H]) += o_proj(attn(...))."""
+        a = self.a
+        self._qmv(self.xn, L["qkv_proj"], self.proj, rows, ldy=self.proj.shape[1])
+        self._chk(self.L.qmtp_attn_prep(self.proj.data_ptr(), self.proj.shape[1], rows, a.n_heads, a.n_kv,
+                                        a.head_dim, a.rotary_dim, L["q_norm"].data_ptr(), L["k_norm"].data_ptr(),
+                                        a.eps, self.cos.data_ptr(), self.sin.data_ptr(), self._cp(pos_slot), 0,
+                                        self.qb.data_ptr(), self.gb.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                        a.max_pos, self._st()), "attn_prep")
+        self._chk(self.L.qmtp_attention(self.qb.data_ptr(), self.gb.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                        a.max_pos, rows, a.n_heads, a.n_kv, a.head_dim, self._cp(pos_slot), 0,
+                                        self.att_out.data_ptr(), self._st()), "attention")
+        self._qmv(self.att_out, L["o_proj"], x, rows, res=x)
+
+    def _mlp(self, L, x, rows):
+        a = self.a
+        self._norm(x, L["post_ln"], self.xn, rows)
+        self._qmv(self.xn, L["gate_up"], self.gu, rows)
+        self._chk(self.L.qmtp_swiglu(self.gu.data_ptr(), 2 * a.intermediate, rows, a.intermediate,
+                                     self.act.data_ptr(), self._st()), "swiglu")
+        self._qmv(self.act, L["down"], x, rows, res=x)
+
+    def backbone(self):
+        """mtp.py:143-153 on the k+1 verify tokens in self.tokens_in: h (pre-norm) and hn (post-norm)."""
+        a, W, S = self.a, self.W, self.S
+        E = W["embed"]
+        self._chk(self.L.qmtp_embed(self.tokens_in.data_ptr(), S, E.weight.data_ptr(), E.scales.data_ptr(),
+                                    E.biases.data_ptr(), a.vocab, a.hidden, self.h.data_ptr(), a.hidden,
+                                    self._st()), "embed")
+        for i in range(a.layers):
+            L = W[f"layers.{i}"]
+            self._norm(self.h, L["input_ln"], self.xn, S)
+            if a.is_linear(i):
+                self._qmv(self.xn, L["in_proj"], self.proj, S, ldy=self.proj.shape[1])
+                self._chk(self.L.qmtp_gdn_fused_ex(ctypes.byref(self._gdn_args[i]), self._st()), "gdn")
+                Z = a.lin_hv * a.lin_dv
+                self._chk(self.L.qmtp_gdn_norm_gate(self.ygdn.data_ptr(), self.proj.data_ptr() + 2 * a.conv_dim,
+                                                    self.proj.shape[1], L["norm"].data_ptr(),
+                                                    self.gdn_out.data_ptr(), Z, S, a.lin_hv, a.lin_dv, a.eps,
+                                                    self._st()), "norm_gate")
+                self._qmv(self.gdn_out, L["out_proj"], self.h, S, res=self.h)
+            else:
+                kc, vc = self.kv[i]
+                self._attn_layer(L, self.h, S, kc, vc, C["POS"])
+            self._mlp(L, self.h, S)
+        self._norm(self.h, W["norm"], self.hn, S)
+
+    def _head(self):
+        self.head.select(self.hn, out=(self.idx, self.fine, self.a_tok))
+
+    def mtp_step(self, hidden, hidden_sel, tok, rows, out_sel, draft_out, with_draft=True):
+        """mtp.py:199-209 for `rows` (hidden, token) pairs at MTP positions MPOS + r: the MTP layer
+        output lands in self.mx; the draft token of row out_sel (device int, or row 0) goes to
+        draft_out (DraftHead.token = argmax of the full-vocab 4-bit head, mtp.py:165-167)."""
+        a, M = self.a, self.W["mtp"]
+        H = a.hidden
+        E = self.W["embed"]
+        self._chk(self.L.qmtp_embed(tok, rows, E.weight.data_ptr(), E.scales.data_ptr(), E.biases.data_ptr(),
+                                    a.vocab, H, self.memb.data_ptr(), H, self._st()), "embed")
+        self._norm(self.memb, M["pre_fc_norm_embedding"], self.mcat, rows, ld_o=2 * H)
+        self._chk(self.L.qmtp_rmsnorm(hidden.data_ptr(), H, hidden_sel, M["pre_fc_norm_hidden"].data_ptr(), a.eps,
+                                      self.mcat.data_ptr() + 2 * H, 2 * H, rows, H, self._st()), "rmsnorm")
+        self._qmv(self.mcat, M["fc"], self.mx, rows)
+        Ly = M["layer"]
+        self._norm(self.mx, Ly["input_ln"], self.xn, rows)
+        self._attn_layer(Ly, self.mx, rows, self.mkv[0], self.mkv[1], C["MPOS"])
+        self._mlp(Ly, self.mx, rows)
+        if not with_draft:
+            return
+        self._chk(self.L.qmtp_rmsnorm(self.mx.data_ptr(), H, out_sel, M["norm"].data_ptr(), a.eps,
+                                      self.mxn.data_ptr(), H, 1, H, self._st()), "rmsnorm")
+        self._qmv(self.mxn, self.W["lm_head_q"], self.dlogits, 1)
+        self._chk(self.L.qmtp_argmax_bf16(self.dlogits.data_ptr(), a.vocab, 1, a.vocab, draft_out,
+                                          self.argmax_ws.data_ptr(), self.argmax_ws.numel(), self._st()), "argmax")
+
+    def _accept(self, forced_keep=0):
+        self._chk(self.L.qmtp_mtp_accept(self.a_tok.data_ptr(), self.tokens_in.data_ptr(), self.k, self.ctrl.data_ptr(),
+                                         self.out_tokens.data_ptr(), self.out_cap, self.slots, self.win_rows,
+                                         forced_keep, self._st()), "accept")
+
+    def _draft_chain(self, hidden, tok):
+        """mtp.py:212-226, k drafts, chain on the MTP's own pre-norm output (chain="pre")."""
+        sel = self._cp(C["SEL"])
+        self.mtp_step(hidden, None, tok, self.S, sel, self.drafts.data_ptr())
+        self._chk(self.L.qmtp_mtp_advance(self.ctrl.data_ptr(), self._st()), "advance")
+        for j in range(1, self.k):
+            # the chained step reads the previous step's output row: row SEL after the first step, 0 after
+            hsel = sel if j == 1 else None
+            self.mtp_step(self.mx, hsel, self.drafts.data_ptr() + 4 * (j - 1), 1, None,
+                          self.drafts.data_ptr() + 4 * j)
+        self._chk(self.L.qmtp_next_tokens(self.a_tok.data_ptr(), self.drafts.data_ptr(), self.k, self.ctrl.data_ptr(),
+                                          self.tokens_in.data_ptr(), self._st()), "next_tokens")
+
+    def cycle(self):
+        """One verify + accept + draft cycle (mtp.py:268-294), device-side only."""
+        self.backbone()
+        self._head()
+        self._accept()
+        self._draft_chain(self.h, self.a_tok.data_ptr())
+        self.ctrl_host.copy_(self.ctrl, non_blocking=True)
+
+    # ------------------------------------------------------------------ session
+    def reset(self):
+        self.ctrl.zero_()
+        self.ctrl[C["WOUT_ROW"]] = self.win_rows
+        for i in self.lin_ids:
+            self.win[i].zero_()
+            self.ring[i][0].zero_()
+
+    def prefill(self, prompt_ids) -> int:
+        """Runs the prompt (mtp.py:258-263) in chunks of k+1 and leaves [t, d1..dk] in tokens_in."""
+        p = [int(x) for x in prompt_ids]
+        S = self.S
+        self.reset()
+        n_chunks = (len(p) + S - 1) // S
+        for c in range(n_chunks):
+            chunk = p[c * S:(c + 1) * S]
+            n = len(chunk)
+            self.tokens_in.copy_(torch.tensor(chunk + [0] * (S - n), dtype=torch.int32))
+            self.backbone()
+            last = c == n_chunks - 1
+            if last:
+                self._norm_head_rows()
+            self._accept(forced_keep=n)
+            nxt = p[c * S + 1:c * S + 1 + n]
+            self.m_tok.copy_(torch.tensor(nxt + [0] * (S - len(nxt)), dtype=torch.int32))
+            if last:  # the pair of the last prompt position is (h, t): t is the verify argmax of that row
+                self.m_tok[n - 1:n].copy_(self.a_tok[n - 1:n])
+                self._draft_chain(self.h, self.m_tok.data_ptr())
+            else:
+                self.mtp_step(self.h, None, self.m_tok.data_ptr(), S, None, self.drafts.data_ptr(), with_draft=False)
+                self._chk(self.L.qmtp_mtp_advance(self.ctrl.data_ptr(), self._st()), "advance")
+        return int(self.tokens_in[0].item())
+
+    def _norm_head_rows(self):
+        self._head()
+
+    def capture(self):
+        """Captures cycle() as a CUDA graph (after one eager warm-up cycle elsewhere)."""
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self.cycle()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.graph = g
+        return g
+
+    def run_cycle(self):
+        """One cycle; returns the tokens it emitted (read from the pinned copy of the control block)."""
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self.cycle()
+        torch.cuda.current_stream(self.dev).synchronize()
+        h = self.ctrl_host.tolist()
+        keep = h[C["KEEP"]]
+        return h[C["EMIT0"]:C["EMIT0"] + keep]
+
+
+def generate_mtp(dec: MTPDecoder, prompt_ids, max_tokens, eos=(), use_graph=True, draft_override=None):
+    """mtp.py:241-303 (greedy, k fixed): returns (tokens, stats).  tok/s excludes the prefill, as the
+    reference does (mtp.py:264,295).  draft_override(cycle) -> k tokens or None replaces the drafts a
+    cycle verifies (test hook for the acceptance / rollback paths)."""
+    t = dec.prefill(prompt_ids)
+    if use_graph and dec.graph is None:
+        # capture needs the library's one-time kernel setup done: warm up on a scratch copy of state
+        snap = _snapshot(dec)
+        dec.run_cycle()
+        _restore(dec, snap)
+        dec.capture()
+        _restore(dec, snap)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    out = [t]
+    k = dec.k
+    cycles = 0
+    while len(out) < max_tokens and out[-1] not in eos:
+        if draft_override is not None:
+            o = draft_override(cycles)
+            if o is not None:
+                dec.tokens_in[1:].copy_(torch.tensor([int(v) for v in o], dtype=torch.int32))
+        out += dec.run_cycle()
+        cycles += 1
+    dt = time.perf_counter() - t0
+    for i, tok in enumerate(out):
+        if tok in eos:
+            out = out[:i + 1]
+            break
+    out = out[:max_tokens]
+    ctrl = dec.ctrl.tolist()
+    acc = [ctrl[C["ACC0"] + i] for i in range(k)]
+    stats = {"tps": (len(out) - 1) / dt if dt > 0 else 0.0, "tok_ciclo": (len(out) - 1) / max(cycles, 1),
+             "acept": [n / max(cycles, 1) for n in acc], "borradores_ciclo": float(k), "cycles": cycles,
+             "seconds": dt}
+    return out, stats
+
+
+def _snapshot(dec: MTPDecoder):
+    """Copies every piece of mutable device state (used around the warm-up cycle before capture)."""
+    bufs = [dec.ctrl, dec.tokens_in, dec.a_tok, dec.drafts, dec.out_tokens, dec.mkv[0], dec.mkv[1]]
+    bufs += [dec.ring[i] for i in dec.lin_ids] + [dec.win[i] for i in dec.lin_ids]
+    bufs += [t for i in dec.att_ids for t in dec.kv[i]]
+    return [(b, b.clone()) for b in bufs]
+
+
+def _restore(dec: MTPDecoder, snap):
+    for b, c in snap:
+        b.copy_(c)
