@@ -1,0 +1,329 @@
+"""Benchmark of the B200 decode hot path: greedy MTP speculative decoding.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one verify cycle of mtp.py:268-294 on the synthetic Qwen3.5-9B-shaped model (32 layers,
+3:1 GatedDeltaNet : gated attention, 4-bit affine g64 weights, two-stage lm_head, 1-layer MTP head,
+k = 2 drafts, batch 1) after a 512-token uniform-random prompt.  Prints one JSON line on rank 0.
+
+  value      tokens emitted per second over K graph replays, device-timed with CUDA events (the
+             replays run back to back, no host round trip);
+  e2e        the same tokens/s through qmtp.mtp.generate_mtp, the call a user makes: one replay,
+             stream sync and 128-byte control-block read per cycle, as the reference's loop does;
+  roofline   the 4-bit GEMV (qmv) kernels: algorithmic bytes of every qmv launch of one cycle over
+             their CUDA-event durations, against the measured HBM copy peak;
+  cpu_baseline  the C oracle (oracle/) running the same decode cycles from the GPU's post-prefill
+             state on the host cores (bounded sample), with a token-for-token parity check.
+
+--impl reference: the reference's CPU path restated by the oracle (the reference itself is MLX +
+Metal and cannot run here), full-size weights, a short prompt, W + K cycles on all host cores.
+Multi-GPU: replicas (batch-1 decoding does not shard); every rank decodes its own prompt.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "qwen-mtp-mac_b200")]
+
+METRIC = "MTP greedy decode tok/s (batch 1); qmv/GDN achieved HBM GB/s vs roofline"
+PROMPT_LEN, K_DRAFTS = 512, 2
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def _traffic_ratio():
+    """DRAM bytes / algorithmic bytes of the qmv kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "qmv_affine_g64_head_M3.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_ratio:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) during the timed region: median SM MHz and active throttle reasons."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.f = None
+
+    def __enter__(self):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.f.flush()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in Path(self.f.name).read_text().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        finally:
+            os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "", 1).isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "", 1).isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------------ our arm
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from qmtp import _lib
+    from qmtp import model as qm
+    from qmtp.mtp import MTPDecoder, _restore, _snapshot, export_state, generate_mtp
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = qm.ModelArgs(max_pos=2048)
+    t_build = time.time()
+    W = qm.synthetic_weights(cfg, seed=0, device=dev)
+    torch.cuda.synchronize()
+    t_build = time.time() - t_build
+    rng = np.random.default_rng(1000 + rank)
+    prompt = rng.integers(0, cfg.vocab, PROMPT_LEN).tolist()
+    K, Wu = args.steps, args.warmup
+    dec = MTPDecoder(cfg, W, k=K_DRAFTS, max_tokens=Wu + 3 * K + 64, device=dev)
+
+    # ---- prefill, one eager cycle (library setup), capture
+    t = dec.prefill(prompt)
+    post_prefill = export_state(dec) if (rank == 0 and world == 1 and args.cpu_cycles > 0) else None
+    snap = _snapshot(dec)
+    dec.launches = 0
+    dec.run_cycle()
+    launches_per_cycle = dec.launches
+    # roofline: per-launch CUDA events around every qmv of a few eager cycles
+    dec.prof = []
+    for _ in range(3):
+        dec.run_cycle()
+    torch.cuda.synchronize()
+    prof = [(b, e0.elapsed_time(e1), shp) for b, e0, e1, shp in dec.prof]
+    dec.prof = None
+    _restore(dec, snap)
+    dec.capture()
+    _restore(dec, snap)
+    # warm-up replays (their tokens are the first W cycles of the generation)
+    for _ in range(Wu):
+        dec.run_cycle()
+    n0 = int(dec.ctrl[_lib.CTRL["NOUT"]])
+
+    # ---- timed region: K back-to-back graph replays
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(K):
+            dec.graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    n1 = int(dec.ctrl[_lib.CTRL["NOUT"]])
+    tokens = n1 - n0
+    gpu_stream = dec.out_tokens[:n1].tolist()  # every token decoded after the prompt (warm-up + timed)
+    clocks = clk.summary()
+    if world > 1:
+        tt = torch.tensor([elapsed_ms, float(tokens)], dtype=torch.float64, device=dev)
+        mx = tt.clone()
+        dist.all_reduce(mx[:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(tt[1:], op=dist.ReduceOp.SUM)
+        elapsed_ms, tokens_all = float(mx[0]), float(tt[1])
+    else:
+        tokens_all = float(tokens)
+    value = tokens_all / (elapsed_ms / 1e3)
+
+    # ---- e2e: the public generate_mtp call (per-cycle host sync + control-block read)
+    gen_tokens = min(256, Wu + K)
+    out, st = generate_mtp(dec, prompt, gen_tokens, use_graph=True)
+    e2e_tps = st["tps"]
+    if world > 1:
+        e = torch.tensor([st["seconds"], float(len(out) - 1)], dtype=torch.float64, device=dev)
+        dist.all_reduce(e[:1], op=dist.ReduceOp.MAX)
+        tot = e[1:].clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        e2e_tps = float(tot[0]) / float(e[0])
+
+    peak, peak_kind = _peaks()
+    qbytes = sum(b for b, _, _ in prof)
+    qms = sum(ms for _, ms, _ in prof)
+    achieved = qbytes / (qms / 1e3) / 1e9
+    ratio = _traffic_ratio()
+    n_cycles_prof = 3
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                "traffic": None if ratio is None else round(ratio * qbytes / len(prof)),
+                "kernel": "qmv_affine_g64 (all 4-bit projections + coarse head of a cycle)",
+                "bytes_per_cycle": qbytes // n_cycles_prof, "qmv_ms_per_cycle": round(qms / n_cycles_prof, 4),
+                "launches_per_cycle": len(prof) // n_cycles_prof}
+
+    res = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": Wu,
+           "ms_per_step": round(elapsed_ms / K, 4), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": "config4: synthetic Qwen3.5-9B-shaped hybrid decoder (32 layers, 3:1 GDN:attention, "
+                                  "4-bit affine g64), 1-layer MTP head, greedy MTP decode k=2, batch 1, "
+                                  f"{PROMPT_LEN}-token uniform random prompt",
+                      "step": "one verify cycle (verify 3 tokens + accept/rollback + 2 draft steps)",
+                      "prompt_tokens": PROMPT_LEN, "drafts": K_DRAFTS, "parallelism": f"replicas x{world}",
+                      "l2": "weights ~7.5 GB per cycle >> 126 MB L2 (no flush needed)",
+                      "weights_build_s": round(t_build, 1)},
+           "e2e": {"value": round(e2e_tps, 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 4 * _lib.CTRL_SIZE, "tokens": len(out)},
+           "roofline": roofline, "clocks": clocks, "gpu_launches": launches_per_cycle * K,
+           "stats": {"tokens_timed": int(tokens_all), "tok_per_cycle": round(tokens / K, 4),
+                     "acceptance": st["acept"], "first_token": t}}
+
+    # ---- CPU oracle on a bounded sample of the same decode, from the same post-prefill state
+    if post_prefill is not None:
+        res["cpu_baseline"] = cpu_baseline_from_state(cfg, W, post_prefill, gpu_stream, args.cpu_cycles)
+    if world > 1:
+        dist.barrier()
+        dec.graph = None
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+def cpu_baseline_from_state(cfg, W, state, gpu_tokens, cycles):
+    import numpy as np
+
+    from oracle import model as om
+    from qmtp import model as qm
+
+    threads = os.cpu_count() or 1
+    t0 = time.time()
+    Wn = qm.to_numpy(W)
+    ocfg = om.ModelArgs(**{k: getattr(cfg, k) for k in om.ModelArgs.__dataclass_fields__})
+    orc = om.OracleModel(ocfg, Wn)
+    layers, mtp, pending = state
+    cache, mcache = orc.load_state(layers, mtp)
+    copy_s = time.time() - t0
+    out, st = orc.decode(cache, mcache, pending[0], pending[1:], max_tokens=10 ** 6, k=K_DRAFTS, max_cycles=cycles)
+    got = out[1:]
+    ref = gpu_tokens[:len(got)]
+    return {"value": round(st["tps"], 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{cycles} decode cycles of the full-size model from the GPU's post-prefill state "
+                      f"({st['tokens']} tokens, {st['seconds']:.1f} s; weights/state copy {copy_s:.1f} s not timed)",
+            "parity": {"cycles": cycles, "tokens": len(got), "identical": got == ref}}
+
+
+# ------------------------------------------------------------------------------ reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import model as om
+
+    threads = os.cpu_count() or 1
+    cfg = om.ModelArgs(max_pos=2048)
+    t0 = time.time()
+    Wn = om.synthetic_weights_fast(cfg, seed=0)
+    build_s = time.time() - t0
+    orc = om.OracleModel(cfg, Wn)
+    prompt = np.random.default_rng(1000).integers(0, cfg.vocab, args.ref_prompt).astype(np.int32)
+    t1 = time.time()
+    cache, mcache, t, drafts = orc.prefill(prompt, K_DRAFTS)
+    prefill_s = time.time() - t1
+    Wu, K = args.warmup, args.steps
+    _, st = orc.decode(cache, mcache, t, drafts, 10 ** 6, k=K_DRAFTS, max_cycles=Wu)
+    t_next, d_next = st["next"]
+    _, st2 = orc.decode(cache, mcache, t_next, d_next, 10 ** 6, k=K_DRAFTS, max_cycles=K)
+    v = st2["tps"]
+    res = {"metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+           "steps": K, "warmup": Wu, "ms_per_step": round(st2["seconds"] * 1e3 / max(st2["cycles"], 1), 2),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "impl": "reference",
+           "config": {"workload": "config4 (same model shapes, 4-bit affine g64, k=2, batch 1) on the host CPU",
+                      "prompt_tokens": int(args.ref_prompt), "weights": "synthetic_weights_fast (timing-equivalent)",
+                      "weights_build_s": round(build_s, 1), "prefill_s": round(prefill_s, 1)},
+           "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                            "sample": f"{args.ref_prompt}-token prompt, {Wu} warm-up + {K} timed decode cycles "
+                                      f"({st2['tokens']} tokens) of the oracle restatement (MLX reference not runnable)"},
+           "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-cycles", type=int, default=3, help="oracle cycles for cpu_baseline (0 = skip)")
+    ap.add_argument("--ref-prompt", type=int, default=16)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        args.steps = 3 if args.steps is None else args.steps
+        args.warmup = 1 if args.warmup is None else args.warmup
+        args.steps = min(args.steps, 12)
+        args.warmup = min(args.warmup, 3)
+        run_reference(args)
+    else:
+        args.steps = 253 if args.steps is None else args.steps
+        args.warmup = 3 if args.warmup is None else max(args.warmup, 0)
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -254,16 +254,18 @@ class OracleModel:
             out.append(int(self.head(hn)[0]))
         return out
 
-    def generate_mtp(self, prompt_ids, max_tokens, eos=(), k=2, time_it=False, max_cycles=None,
-                     draft_override=None):
-        """draft_override(cycle) -> list of k tokens or None: replaces the drafts a cycle verifies
-        (test hook to exercise acceptance and rollback; the MTP caches still follow the computed drafts)."""
+    def prefill(self, prompt_ids, k=2):
+        """mtp.py:258-263: prompt pass, first token t, first drafts; returns (cache, mcache, h, t, drafts)."""
         cache = self.make_cache()
         mcache = self._kv()
         p = np.int32(prompt_ids)
         h, hn = self.backbone(p, cache)
         t = int(self.head(hn[-1:])[0])
         drafts = self.draft_chain(h, np.concatenate([p[1:], np.int32([t])]), mcache, k)
+        return cache, mcache, t, drafts
+
+    def decode(self, cache, mcache, t, drafts, max_tokens, eos=(), k=2, max_cycles=None, draft_override=None):
+        """The verify loop of mtp.py:268-294 from a given state; returns (out tokens incl. t, stats)."""
         t0 = time.perf_counter()
         out = [t]
         cycles = verified = 0
@@ -303,8 +305,26 @@ class OracleModel:
         out = out[:max_tokens]
         stats = {"tps": (len(out) - 1) / dt if dt > 0 else 0.0, "tok_ciclo": (len(out) - 1) / max(cycles, 1),
                  "acept": [n / max(cycles, 1) for n in acc_pos], "borradores_ciclo": verified / max(cycles, 1),
-                 "cycles": cycles, "seconds": dt}
+                 "cycles": cycles, "seconds": dt, "tokens": max(len(out) - 1, 0), "next": (t, drafts)}
         return out, stats
+
+    def load_state(self, layers, mtp):
+        """Caches from exported engine state (qmtp.mtp.export_state): lets the decode loop start
+        from the B200 engine's post-prefill state (full-size CPU samples without a CPU prefill)."""
+        cache = []
+        for entry in layers:
+            if entry[0] == "gdn":
+                cache.append(GDNCache(entry[1].copy(), entry[2].astype(np.float32).copy()))
+            else:
+                cache.append(KVCache(entry[1].copy(), entry[2].copy(), int(entry[3])))
+        return cache, KVCache(mtp[0].copy(), mtp[1].copy(), int(mtp[2]))
+
+    def generate_mtp(self, prompt_ids, max_tokens, eos=(), k=2, max_cycles=None, draft_override=None):
+        """mtp.py:241-303 (greedy, fixed k).  draft_override(cycle) -> list of k tokens or None
+        replaces the drafts a cycle verifies (test hook for acceptance and rollback; the MTP caches
+        still follow the computed drafts)."""
+        cache, mcache, t, drafts = self.prefill(prompt_ids, k)
+        return self.decode(cache, mcache, t, drafts, max_tokens, eos, k, max_cycles, draft_override)
 
     # -- mtp.py:136-140
     def restore(self, c: GDNCache, keep: int) -> None:
@@ -343,6 +363,46 @@ def synthetic_weights(args: ModelArgs, seed: int = 0, std: float = 0.02) -> dict
         W[f"layers.{i}"] = L
     W["norm"] = ones(a.hidden)
     W["lm_head"] = bf((a.vocab, a.hidden))
+    W["lm_head_q"] = ops.quantize_affine(W["lm_head"])
+    W["mtp"] = {"pre_fc_norm_embedding": ones(a.hidden), "pre_fc_norm_hidden": ones(a.hidden),
+                "fc": lin(a.hidden, 2 * a.hidden), "norm": ones(a.hidden),
+                "layer": {"input_ln": ones(a.hidden), "post_ln": ones(a.hidden),
+                          "qkv_proj": lin(a.attn_proj, a.hidden), "q_norm": ones(a.head_dim),
+                          "k_norm": ones(a.head_dim), "o_proj": lin(a.hidden, a.n_heads * a.head_dim),
+                          "gate_up": lin(2 * a.intermediate, a.hidden), "down": lin(a.hidden, a.intermediate)}}
+    return W
+
+
+def synthetic_weights_fast(args: ModelArgs, seed: int = 0, std: float = 0.02) -> dict:
+    """Full-size random weights for CPU timing runs: packed nibbles drawn uniformly and per-group
+    scales / biases with the magnitudes an N(0, std) group quantizes to ((max-min)/15 ~ 0.3*std,
+    min ~ -2.5*std); the bf16 lm_head is N(0, std) and its coarse copy is quantized from it.  Same
+    shapes, formats and per-token work as synthetic_weights, generated in seconds."""
+    rng = np.random.default_rng(seed)
+
+    def lin(n, k):
+        wq = rng.integers(0, 2 ** 32, (n, k // 8), dtype=np.uint32)
+        s = ops.f32_to_bf16((0.3 * std + 0.03 * std * rng.standard_normal((n, k // 64))).astype(np.float32))
+        b = ops.f32_to_bf16((-2.5 * std + 0.25 * std * rng.standard_normal((n, k // 64))).astype(np.float32))
+        return wq, s, b
+
+    ones = lambda n: ops.f32_to_bf16(np.ones(n, np.float32))
+    bf = lambda shape, sc: ops.f32_to_bf16(rng.standard_normal(shape, dtype=np.float32) * np.float32(sc))
+    a = args
+    W = {"embed": lin(a.vocab, a.hidden)}
+    for i in range(a.layers):
+        L = {"input_ln": ones(a.hidden), "post_ln": ones(a.hidden), "gate_up": lin(2 * a.intermediate, a.hidden),
+             "down": lin(a.hidden, a.intermediate)}
+        if a.is_linear(i):
+            L.update(in_proj=lin(a.gdn_proj, a.hidden), conv1d=bf((a.conv_dim, a.conv_k), 1.0 / np.sqrt(a.conv_k)),
+                     A_log=np.log(rng.uniform(1, 16, a.lin_hv)).astype(np.float32), dt_bias=bf((a.lin_hv,), 1.0),
+                     norm=ones(a.lin_dv), out_proj=lin(a.hidden, a.lin_hv * a.lin_dv))
+        else:
+            L.update(qkv_proj=lin(a.attn_proj, a.hidden), q_norm=ones(a.head_dim), k_norm=ones(a.head_dim),
+                     o_proj=lin(a.hidden, a.n_heads * a.head_dim))
+        W[f"layers.{i}"] = L
+    W["norm"] = ones(a.hidden)
+    W["lm_head"] = bf((a.vocab, a.hidden), std)
     W["lm_head_q"] = ops.quantize_affine(W["lm_head"])
     W["mtp"] = {"pre_fc_norm_embedding": ones(a.hidden), "pre_fc_norm_hidden": ones(a.hidden),
                 "fc": lin(a.hidden, 2 * a.hidden), "norm": ones(a.hidden),

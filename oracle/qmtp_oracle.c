@@ -500,7 +500,7 @@ QO_API int qo_gdn_fused(const uint16_t* win, const uint16_t* conv_w, const uint1
                         int ld_ab, const float* A_log, const uint16_t* dt_bias, const float* state_in,
                         float* y, float* state_out, float* state_mid, int S, int Hk, int Hv, int Dk,
                         int Dv, int KC) {
-  if (Dk % 32 != 0 || Hv % Hk != 0 || S < 1 || S > 64) return -1;
+  if (Dk % 32 != 0 || Hv % Hk != 0 || S < 1) return -1;
   float* qn = (float*)malloc(sizeof(float) * (size_t)S * Hk * Dk);
   float* kn = (float*)malloc(sizeof(float) * (size_t)S * Hk * Dk);
   float* vn = (float*)malloc(sizeof(float) * (size_t)S * Hv * Dv);
@@ -512,7 +512,8 @@ QO_API int qo_gdn_fused(const uint16_t* win, const uint16_t* conv_w, const uint1
   for (int hv = 0; hv < Hv; ++hv) {
     for (int dv = 0; dv < Dv; ++dv) {
       int hk = hv / (Hv / Hk);
-      float vf[64], yf[64], gg[64], bb[64];
+      float* vf = (float*)malloc(sizeof(float) * (size_t)S * 4);
+      float *yf = vf + S, *gg = vf + 2 * S, *bb = vf + 3 * S;
       for (int t = 0; t < S; ++t) {
         vf[t] = vn[(size_t)t * Hv * Dv + (size_t)hv * Dv + dv];
         gg[t] = gt[(size_t)t * Hv + hv];
@@ -524,6 +525,7 @@ QO_API int qo_gdn_fused(const uint16_t* win, const uint16_t* conv_w, const uint1
       qo_gdn_row(st, Dk, S, qn + (size_t)hk * Dk, kn + (size_t)hk * Dk, Hk * Dk, vf, 1, gg, bb, 1, yf, 1,
                  state_mid ? state_mid + row : NULL, per);
       for (int t = 0; t < S; ++t) y[((size_t)t * Hv + hv) * Dv + dv] = qo_R(yf[t]);
+      free(vf);
     }
   }
   free(qn); free(kn); free(vn); free(gt);

@@ -60,6 +60,8 @@ class MTPDecoder:
         self.memb, self.mcat, self.mx, self.mxn = z(S, H), z(S, 2 * H), z(S, H), z(1, H)
         self.dlogits = z(1, a.vocab)
         self.fine, self.idx = z(S, 64), z(S, 64, dtype=i32)
+        self.coarse = z(S, a.vocab)
+        self.topk_ws = torch.empty(self.L.qmtp_topk_workspace(S, a.vocab, 64), dtype=torch.uint8, device=dev)
         self.argmax_ws = torch.empty(self.L.qmtp_argmax_workspace(1, a.vocab), dtype=torch.uint8, device=dev)
         # recurrent / cache state
         self.lin_ids = [i for i in range(a.layers) if a.is_linear(i)]
@@ -75,6 +77,8 @@ class MTPDecoder:
         for i in self.lin_ids:
             self._gdn_args[i] = self._make_gdn_args(i)
         self.graph = None
+        self.launches = 0      # kernels launched by the library calls of this decoder
+        self.prof = None       # list of (bytes, start event, end event, shape) while profiling qmv
 
     # ------------------------------------------------------------------ helpers
     def _cp(self, slot: int) -> int:
@@ -83,12 +87,21 @@ class MTPDecoder:
     def _st(self):
         return _lib.stream()
 
+    _KERNELS = {"rmsnorm": 1, "attn_prep": 1, "attention": 1, "swiglu": 1, "embed": 1, "gdn": 1, "norm_gate": 1,
+                "accept": 1, "advance": 1, "next_tokens": 1, "argmax": 2}
+
     def _chk(self, rc, what):
+        self.launches += self._KERNELS.get(what, 0)
         if rc != 0:
             _lib.check(rc, what)
 
     def _qmv(self, x, lin, y, M, res=None, ldy=None, ldx=None):
         ldy = ldy or lin.out_features
+        N, K = lin.out_features, lin.in_features
+        self.launches += (M + 3) // 4
+        if self.prof is not None:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
         if res is None:
             rc = self.L.qmtp_qmv_affine_g64(x.data_ptr(), lin.weight.data_ptr(), lin.scales.data_ptr(),
                                             lin.biases.data_ptr(), y.data_ptr(), M, lin.out_features,
@@ -98,6 +111,11 @@ class MTPDecoder:
                                                 lin.biases.data_ptr(), y.data_ptr(), res.data_ptr(), M,
                                                 lin.out_features, lin.in_features, ldy, self._st())
         self._chk(rc, "qmv")
+        if self.prof is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            nbytes = N * K // 2 + N * (K // 64) * 4 + M * K * 2 + M * N * 2 * (2 if res is not None else 1)
+            self.prof.append((nbytes, e0, e1, (M, N, K)))
 
     def _norm(self, x, w, out, M, ld_x=None, ld_o=None, row_sel=None):
         H = w.shape[0]
@@ -166,7 +184,14 @@ class MTPDecoder:
         self._norm(self.h, W["norm"], self.hn, S)
 
     def _head(self):
-        self.head.select(self.hn, out=(self.idx, self.fine, self.a_tok))
+        """Two-stage head (lm_head2.py:23-29) + greedy argmax: coarse qmv, then selection/rescoring."""
+        a = self.a
+        self._qmv(self.hn, self.W["lm_head_q"], self.coarse, self.S)
+        self.launches += 2
+        self._chk(self.L.qmtp_topk_rescore(self.coarse.data_ptr(), a.vocab, self.S, a.vocab, 64,
+                                           self.W["lm_head"].data_ptr(), self.hn.data_ptr(), a.hidden,
+                                           self.idx.data_ptr(), self.fine.data_ptr(), self.a_tok.data_ptr(),
+                                           self.topk_ws.data_ptr(), self.topk_ws.numel(), self._st()), "head")
 
     def mtp_step(self, hidden, hidden_sel, tok, rows, out_sel, draft_out, with_draft=True):
         """mtp.py:199-209 for `rows` (hidden, token) pairs at MTP positions MPOS + r: the MTP layer
@@ -327,3 +352,25 @@ def _snapshot(dec: MTPDecoder):
 def _restore(dec: MTPDecoder, snap):
     for b, c in snap:
         b.copy_(c)
+
+
+def export_state(dec: MTPDecoder):
+    """The decoding state as host arrays in the layout of a reference-style cache: per layer either
+    (conv_state bf16 [KC-1, C], state fp32 [Hv, Dv, Dk]) or (k, v bf16 [nkv, max_pos, Dh], length),
+    the MTP cache (k, v, length), and the pending verify input [t, d1..dk]."""
+    def bits(t):
+        t = t.detach().contiguous().cpu()
+        return t.view(torch.int16).numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.numpy()
+
+    ctrl = dec.ctrl.tolist()
+    a = dec.a
+    layers = []
+    for i in range(a.layers):
+        if a.is_linear(i):
+            r = ctrl[C["CONV_ROW"]]
+            layers.append(("gdn", bits(dec.win[i][r:r + a.conv_k - 1]), bits(dec.ring[i][ctrl[C["SLOT"]]])))
+        else:
+            layers.append(("attn", bits(dec.kv[i][0]), bits(dec.kv[i][1]), ctrl[C["POS"]]))
+    mtp = (bits(dec.mkv[0]), bits(dec.mkv[1]), ctrl[C["MPOS"]])
+    pending = dec.tokens_in.tolist()
+    return layers, mtp, pending
