@@ -1,4 +1,4 @@
-"""Benchmark of the B200 decode hot path: greedy MTP speculative decoding.
+"""Benchmark of the B200 decode hot path: greedy MTP speculative decoding (the config-4 workload).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
