@@ -148,6 +148,20 @@ int qmtp_lmhead2(const void* h, const void* wq, const void* scales, const void* 
                  const void* w_fine, int M, int V, int K, int k, int* out_idx, void* out_fine,
                  int* out_argmax, void* coarse_out, void* workspace, size_t ws_bytes, void* stream);
 
+/* The two-stage head of qmtp_lmhead2 for callers that cannot allocate device memory (a plugin
+ * living inside another framework's memory pool, code that may run during stream capture, a
+ * serving loop that must not synchronise the device through cudaMalloc).  This entry point has no
+ * counterpart in the reference.  It takes no workspace: it uses a scratch area that is a static
+ * __device__ array of the library (2 MiB + 64 KiB on every GPU that loads the library, until exit).
+ * Limits: M <= 4 rows, V <= 262144, k <= 64 (larger requests return QMTP_ERR_SHAPE).  The first
+ * call on a device looks up the scratch address on that device; make it before any stream
+ * capture.  All calls share the one scratch area, so calls that can overlap on the GPU (different
+ * streams, or concurrent host threads) race; serialise them.  Results are identical to
+ * qmtp_lmhead2. */
+int qmtp_lmhead2_noalloc(const void* h, const void* wq, const void* scales, const void* biases,
+                         const void* w_fine, int M, int V, int K, int k, int* out_idx, void* out_fine,
+                         int* out_argmax, void* stream);
+
 /* Stage 2 alone: exact top-k of bf16 rows vals [M, ld] (first V columns) and, when w_fine is
  * given, the rescoring of the candidates against w_fine [V, K] with h [M, K] and their argmax
  * (lm_head2.py:25-29).  workspace: qmtp_topk_workspace(M, V, k) bytes. */

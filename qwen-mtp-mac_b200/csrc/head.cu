@@ -13,6 +13,7 @@
 //                 of oracle qo_dot_bf16), and takes the argmax of the fine logits;
 //   argmax        the same candidate words with k = 1 (draft head: argmax over the full vocab).
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -316,4 +317,51 @@ extern "C" int qmtp_lmhead2(const void* h, const void* wq, const void* scales, c
   if (rc != QMTP_OK) return rc;
   return qmtp_topk_rescore(coarse, V, M, V, k, w_fine, h, K, out_idx, out_fine, out_argmax, ws + coarse_bytes,
                            ws_bytes - coarse_bytes, stream);
+}
+
+// ----------------------------------------------------------------------------- no-allocation head
+// Some callers cannot allocate device memory at all: a plugin whose host framework owns every byte
+// of the GPU through its own pool (a cudaMalloc would go around that pool and its budget), a call
+// site that may sit inside a stream capture (cudaMalloc is not allowed while a stream is being
+// captured), or a serving loop that must not pay the device-wide synchronisation a cudaMalloc can
+// cause.  qmtp_lmhead2_noalloc serves them with a scratch area that is part of the library image:
+// the static array below, which every GPU that loads the library holds until the process exits.
+namespace qmtp {
+constexpr int kNoAllocMaxRows = 4;
+constexpr int kNoAllocMaxVocab = 262144;
+constexpr int kNoAllocMaxK = 64;
+constexpr size_t kNoAllocBytes = size_t(kNoAllocMaxRows) * kNoAllocMaxVocab * sizeof(uint16_t)  // coarse logits
+                                 + size_t(kNoAllocMaxRows) * 32 * kNoAllocMaxK * sizeof(uint64_t);  // candidates
+static __device__ __align__(256) unsigned char g_lmhead2_scratch[kNoAllocBytes];
+
+// Device address of the scratch on the current device.  The name g_lmhead2_scratch in host code is
+// only a host-side stand-in, never a device address, so the address is looked up once per device
+// (with that device current) and cached.
+static int noalloc_scratch(void** out) {
+  static std::once_flag once[64];
+  static void* ptr[64];
+  static cudaError_t err[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QMTP_ERR_CUDA;
+  std::call_once(once[dev], [&] { err[dev] = cudaGetSymbolAddress(&ptr[dev], g_lmhead2_scratch); });
+  if (err[dev] != cudaSuccess || !ptr[dev]) return QMTP_ERR_CUDA;
+  *out = ptr[dev];
+  return QMTP_OK;
+}
+}  // namespace qmtp
+
+extern "C" int qmtp_lmhead2_noalloc(const void* h, const void* wq, const void* scales, const void* biases,
+                                    const void* w_fine, int M, int V, int K, int k, int* out_idx, void* out_fine,
+                                    int* out_argmax, void* stream) {
+  if (M < 1 || M > kNoAllocMaxRows || V < 1 || V > kNoAllocMaxVocab || k < 1 || k > kNoAllocMaxK)
+    return QMTP_ERR_SHAPE;
+  const size_t need = qmtp_lmhead2_workspace(M, V, k);
+  if (need == 0 || need > kNoAllocBytes) return QMTP_ERR_SHAPE;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != QMTP_OK) return rc;
+  // Nothing in the scratch has to start at zero: the coarse logits of all M rows and every
+  // candidate slot are written before they are read, within the call.
+  return qmtp_lmhead2(h, wq, scales, biases, w_fine, M, V, K, k, out_idx, out_fine, out_argmax, nullptr, scratch,
+                      kNoAllocBytes, stream);
 }

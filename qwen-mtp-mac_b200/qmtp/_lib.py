@@ -63,6 +63,7 @@ SIGNATURES.update({
     "qmtp_topk_rescore": [_P, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t, _P],
     "qmtp_argmax_bf16": [_P, _I, _I, _I, _P, _P, ctypes.c_size_t, _P],
     "qmtp_qmv_affine_g64_res": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "qmtp_lmhead2_noalloc": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P],
     "qmtp_embed": [_P, _I, _P, _P, _P, _I, _I, _P, _I, _P],
     "qmtp_rmsnorm": [_P, _I, _P, _P, _F, _P, _I, _I, _I, _P],
     "qmtp_attn_prep": [_P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P],
