@@ -140,7 +140,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     t_build = time.time() - t_build
     rng = np.random.default_rng(1000 + rank)
-    prompt = rng.integers(0, cfg.vocab, PROMPT_LEN).tolist()
+    prompt = rng.integers(0, cfg.vocab, args.prompt).tolist()
     K, Wu = args.steps, args.warmup
     dec = MTPDecoder(cfg, W, k=K_DRAFTS, max_tokens=Wu + 3 * K + 64, device=dev)
 
@@ -172,10 +172,12 @@ def run_ours(args):
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("timed")
         ev0.record()
         for _ in range(K):
             dec.graph.replay()
         ev1.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     elapsed_ms = ev0.elapsed_time(ev1)
     n1 = int(dec.ctrl[_lib.CTRL["NOUT"]])
@@ -221,9 +223,9 @@ def run_ours(args):
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
            "config": {"workload": "config4: synthetic Qwen3.5-9B-shaped hybrid decoder (32 layers, 3:1 GDN:attention, "
                                   "4-bit affine g64), 1-layer MTP head, greedy MTP decode k=2, batch 1, "
-                                  f"{PROMPT_LEN}-token uniform random prompt",
+                                  f"{args.prompt}-token uniform random prompt",
                       "step": "one verify cycle (verify 3 tokens + accept/rollback + 2 draft steps)",
-                      "prompt_tokens": PROMPT_LEN, "drafts": K_DRAFTS, "parallelism": f"replicas x{world}",
+                      "prompt_tokens": args.prompt, "drafts": K_DRAFTS, "parallelism": f"replicas x{world}",
                       "l2": "weights ~7.5 GB per cycle >> 126 MB L2 (no flush needed)",
                       "weights_build_s": round(t_build, 1)},
            "e2e": {"value": round(e2e_tps, 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
@@ -264,6 +266,86 @@ def cpu_baseline_from_state(cfg, W, state, gpu_tokens, cycles):
             "sample": f"{cycles} decode cycles of the full-size model from the GPU's post-prefill state "
                       f"({st['tokens']} tokens, {st['seconds']:.1f} s; weights/state copy {copy_s:.1f} s not timed)",
             "parity": {"cycles": cycles, "tokens": len(got), "identical": got == ref}}
+
+
+# ------------------------------------------------------------------------------ single kernels
+def run_kernel(args):
+    """Standalone timing of one kernel at a BASELINE config shape (graph-captured launches, weights
+    rotated over enough copies to exceed L2).  Used for the ncu captures and the per-kernel numbers."""
+    import numpy as np
+    import torch
+
+    from qmtp import _lib, qmv_kernel
+    from qmtp.gdn_fused import gdn_core
+    from qmtp.lm_head2 import TwoStageHead
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    peak, peak_kind = _peaks()
+    K, Wu = args.steps, args.warmup
+    if args.kernel == "qmv":
+        N, Kd, M = (int(v) for v in args.shape.split(","))
+        copies = max(1, -(-300_000_000 // (N * Kd // 2)))  # > 2x L2 of weights in rotation
+        Ls = [qmv_kernel.quantize((torch.randn(N, Kd, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+              for _ in range(copies)]
+        x = torch.randn(M, Kd, generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        nbytes = N * Kd // 2 + N * (Kd // 64) * 4 + M * Kd * 2 + M * N * 2
+        run = lambda i: qmv_kernel.qmv_affine(x, *Ls[i % copies], out=y)
+        unit_bytes = nbytes
+        label = f"qmv affine g64 N={N} K={Kd} M={M}"
+    elif args.kernel == "gdn":
+        S, Hk, Hv, D, KC = 3, 16, 32, 128, 4
+        Cd = 2 * Hk * D + Hv * D
+        copies = 16
+        states = [torch.randn(1, Hv, D, D, generator=g, device=dev) * 0.1 for _ in range(copies)]
+        win = torch.randn(1, S + KC - 1, Cd, generator=g, device=dev).to(torch.bfloat16)
+        ab = torch.randn(1, S, 2 * Hv, generator=g, device=dev).to(torch.bfloat16)
+
+        class Layer:
+            num_k_heads, num_v_heads, head_k_dim, head_v_dim, conv_kernel_size = Hk, Hv, D, D, KC
+            conv1d_weight = (torch.randn(Cd, KC, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+            A_log = torch.log(torch.rand(Hv, generator=g, device=dev) * 15 + 1)
+            dt_bias = torch.randn(Hv, generator=g, device=dev).to(torch.bfloat16)
+
+        run = lambda i: gdn_core(Layer, win, ab[..., :Hv], ab[..., Hv:], states[i % copies], snap=True)
+        unit_bytes = Hv * D * D * 4 * (1 + S) + (S + KC - 1) * Cd * 2 + S * Hv * D * 4
+        label = "GatedDeltaNet fused verify step T=3 (snapshots)"
+    else:  # head
+        V, D, M = 248320, 4096, 3
+        W = (torch.randn(V, D, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        head = TwoStageHead(W, 64)
+        h = torch.randn(M, D, generator=g, device=dev).to(torch.bfloat16)
+        outs = (torch.empty(M, 64, dtype=torch.int32, device=dev), torch.empty(M, 64, dtype=torch.bfloat16, device=dev),
+                torch.empty(M, dtype=torch.int32, device=dev))
+        run = lambda i: head.select(h, out=outs)
+        unit_bytes = V * D // 2 + V * (D // 64) * 4 + M * 64 * D * 2 + M * D * 2
+        label = "two-stage lm_head V=248320 D=4096 M=3 k=64"
+    for i in range(max(Wu, 3)):
+        run(i)
+    torch.cuda.synchronize()
+    s_ = torch.cuda.Stream()
+    s_.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s_):
+        for i in range(K):
+            run(i)
+    torch.cuda.current_stream().wait_stream(s_)
+    graph.replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        ev0.record()
+        graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    us = ev0.elapsed_time(ev1) * 1e3 / K
+    gbs = unit_bytes / (us * 1e-6) / 1e9
+    print(json.dumps({"kernel": args.kernel, "workload": label, "us_per_call": round(us, 3),
+                      "bytes_per_call": unit_bytes, "achieved_GBps": round(gbs, 1), "peak": peak,
+                      "peak_kind": peak_kind, "frac": round(gbs / peak, 4), "calls": K, "clocks": clk.summary(),
+                      "device_error": _lib.device_error()}), flush=True)
 
 
 # ------------------------------------------------------------------------------ reference arm
@@ -312,7 +394,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-cycles", type=int, default=3, help="oracle cycles for cpu_baseline (0 = skip)")
     ap.add_argument("--ref-prompt", type=int, default=16)
+    ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens (ours)")
+    ap.add_argument("--kernel", default=None, choices=["qmv", "gdn", "head"],
+                    help="time one kernel at a config shape instead of the decode loop")
+    ap.add_argument("--shape", default="12288,4096,3", help="qmv: N,K,M")
     args = ap.parse_args()
+    if args.kernel:
+        args.steps = 50 if args.steps is None else args.steps
+        args.warmup = 3 if args.warmup is None else args.warmup
+        run_kernel(args)
+        return
     if args.impl == "reference":
         args.steps = 3 if args.steps is None else args.steps
         args.warmup = 1 if args.warmup is None else args.warmup
