@@ -19,6 +19,8 @@ namespace qmtp {
 __global__ void embed_kernel(const int32_t* __restrict__ tok, const uint32_t* __restrict__ wq,
                              const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, int D,
                              uint16_t* __restrict__ out, long long ld_out, int V, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const int r = tok[t];
   if (r < 0 || r >= V) {
@@ -44,6 +46,8 @@ __global__ void embed_kernel(const int32_t* __restrict__ tok, const uint32_t* __
 __global__ void rmsnorm_wide_kernel(const uint16_t* __restrict__ x, long long ld_x, const int* __restrict__ row_sel,
                                     const uint16_t* __restrict__ w, float eps, uint16_t* __restrict__ out,
                                     long long ld_o, int D) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float s_blk[32];
   __shared__ float s_r;
   const int m = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
@@ -95,6 +99,8 @@ __global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld,
                                  const int* __restrict__ pos_ptr, int pos_add, uint16_t* __restrict__ qo,
                                  uint16_t* __restrict__ gate, uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
                                  int max_pos, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int Dh = 256, NP = 8, RH = 32;  // rotary half
   const int lane = threadIdx.x & 31;
   const int wid = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
@@ -162,6 +168,8 @@ __global__ void __launch_bounds__(kAttnSplits * 32)
 attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ gate, const uint16_t* __restrict__ kc,
                  const uint16_t* __restrict__ vc, int max_pos, int nq, int nkv, const int* __restrict__ pos_ptr,
                  int pos_add, uint16_t* __restrict__ out, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int Dh = 256, NP = 8;
   extern __shared__ __align__(16) float sm[];
   float* s_num = sm;                              // [8][Dh]
@@ -242,6 +250,8 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
 
 // ----------------------------------------------------------------------------- SwiGLU
 __global__ void swiglu_kernel(const uint16_t* __restrict__ gu, long long ld, int I, uint16_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int s = blockIdx.y;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < I; i += gridDim.x * blockDim.x) {
     const float g = bf2f(gu[(long long)s * ld + i]), u = bf2f(gu[(long long)s * ld + I + i]);
@@ -255,6 +265,8 @@ __global__ void swiglu_kernel(const uint16_t* __restrict__ gu, long long ld, int
 __global__ void accept_kernel(const int32_t* __restrict__ a, const int32_t* __restrict__ in, int k,
                               int* __restrict__ ctrl, int32_t* __restrict__ out_tokens, int out_cap, int ring_slots,
                               int win_rows, int forced_keep) {
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   int n_acc = 0;
   if (forced_keep > 0) {
@@ -288,12 +300,16 @@ __global__ void accept_kernel(const int32_t* __restrict__ a, const int32_t* __re
 // MTP cache bookkeeping between the two draft steps: MPOS += keep (mtp.py:291-294: the k-1 chained
 // entries of the previous cycle are trimmed, the keep real pairs are committed).
 __global__ void mtp_advance_kernel(int* __restrict__ ctrl) {
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x == 0 && blockIdx.x == 0) ctrl[QMTP_CTRL_MPOS] += ctrl[QMTP_CTRL_KEEP];
 }
 
 // Next verify input [t, d1, d2]: t = a[keep-1].
 __global__ void next_tokens_kernel(const int32_t* __restrict__ a, const int32_t* __restrict__ drafts, int k,
                                    const int* __restrict__ ctrl, int32_t* __restrict__ in) {
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   in[0] = a[ctrl[QMTP_CTRL_SEL]];
   for (int i = 0; i < k; ++i) in[1 + i] = drafts[i];
@@ -308,7 +324,7 @@ extern "C" int qmtp_embed(const int* tokens, int T, const void* wq, const void* 
   if (!tokens || !wq || !scales || !biases || !out) return QMTP_ERR_ARG;
   if (T < 1 || D % 64 != 0 || ld_out < D || ld_out % 8 != 0) return QMTP_ERR_SHAPE;
   if (!aligned16(out)) return QMTP_ERR_ALIGN;
-  embed_kernel<<<T, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(embed_kernel, dim3(T), dim3(128), 0, static_cast<cudaStream_t>(stream), 
       tokens, static_cast<const uint32_t*>(wq), static_cast<const uint16_t*>(scales),
       static_cast<const uint16_t*>(biases), D, static_cast<uint16_t*>(out), ld_out, V, device_error_ptr());
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
@@ -319,7 +335,7 @@ extern "C" int qmtp_rmsnorm(const void* x, int ld_x, const int* row_sel, const v
   if (!x || !w || !out) return QMTP_ERR_ARG;
   if (M < 1 || D % 1024 != 0 || D > 32768 || ld_x < D || ld_out < D || ld_x % 8 || ld_out % 8) return QMTP_ERR_SHAPE;
   if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return QMTP_ERR_ALIGN;
-  rmsnorm_wide_kernel<<<M, D / 32, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(rmsnorm_wide_kernel, dim3(M), dim3(D / 32), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const uint16_t*>(x), ld_x, row_sel, static_cast<const uint16_t*>(w), eps,
       static_cast<uint16_t*>(out), ld_out, D);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
@@ -332,7 +348,7 @@ extern "C" int qmtp_attn_prep(const void* qkv, int ld, int S, int nq, int nkv, i
   if (!qkv || !qn_w || !kn_w || !cos_t || !sin_t || !q_out || !gate_out || !k_cache || !v_cache) return QMTP_ERR_ARG;
   if (Dh != 256 || rotary != 64 || S < 1 || nq < 1 || nkv < 1 || nq % nkv || ld % 8) return QMTP_ERR_UNSUPPORTED;
   const int warps = S * (nq + nkv), wpb = 8;
-  attn_prep_kernel<<<(warps + wpb - 1) / wpb, wpb * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(attn_prep_kernel, dim3((warps + wpb - 1) / wpb), dim3(wpb * 32), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const uint16_t*>(qkv), ld, S, nq, nkv, static_cast<const uint16_t*>(qn_w),
       static_cast<const uint16_t*>(kn_w), eps, cos_t, sin_t, pos_ptr, pos_add, static_cast<uint16_t*>(q_out),
       static_cast<uint16_t*>(gate_out), static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), max_pos,
@@ -351,7 +367,7 @@ extern "C" int qmtp_attention(const void* q, const void* gate, const void* k_cac
   static const cudaError_t attr =
       cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (attr != cudaSuccess) return QMTP_ERR_CUDA;
-  attention_kernel<<<dim3(nq, S), kAttnSplits * 32, smem, static_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(attention_kernel, dim3(dim3(nq, S)), dim3(kAttnSplits * 32), smem, static_cast<cudaStream_t>(stream), 
       static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(gate), static_cast<const uint16_t*>(k_cache),
       static_cast<const uint16_t*>(v_cache), max_pos, nq, nkv, pos_ptr, pos_add, static_cast<uint16_t*>(out),
       device_error_ptr());
@@ -361,7 +377,7 @@ extern "C" int qmtp_attention(const void* q, const void* gate, const void* k_cac
 extern "C" int qmtp_swiglu(const void* gu, int ld, int S, int I, void* out, void* stream) {
   if (!gu || !out) return QMTP_ERR_ARG;
   if (S < 1 || I < 1 || ld < 2 * I) return QMTP_ERR_SHAPE;
-  swiglu_kernel<<<dim3(std::min((I + 255) / 256, 64), S), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(swiglu_kernel, dim3(dim3(std::min((I + 255) / 256, 64), S)), dim3(256), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const uint16_t*>(gu), ld, I, static_cast<uint16_t*>(out));
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
@@ -371,19 +387,19 @@ extern "C" int qmtp_mtp_accept(const int* a, const int* in, int k, int* ctrl, in
   if (!a || !in || !ctrl || !out_tokens) return QMTP_ERR_ARG;
   if (k < 1 || k > QMTP_CTRL_MAX_K || ring_slots < k + 2 || forced_keep > k + 1 || QMTP_CTRL_EMIT0 + k + 1 > QMTP_CTRL_SIZE)
     return QMTP_ERR_SHAPE;
-  accept_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a, in, k, ctrl, out_tokens, out_cap, ring_slots,
+  launch_kernel(accept_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), a, in, k, ctrl, out_tokens, out_cap, ring_slots,
                                                                   win_rows, forced_keep);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 
 extern "C" int qmtp_mtp_advance(int* ctrl, void* stream) {
   if (!ctrl) return QMTP_ERR_ARG;
-  mtp_advance_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(ctrl);
+  launch_kernel(mtp_advance_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), ctrl);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 
 extern "C" int qmtp_next_tokens(const int* a, const int* drafts, int k, const int* ctrl, int* in, void* stream) {
   if (!a || !drafts || !ctrl || !in) return QMTP_ERR_ARG;
-  next_tokens_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a, drafts, k, ctrl, in);
+  launch_kernel(next_tokens_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), a, drafts, k, ctrl, in);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }

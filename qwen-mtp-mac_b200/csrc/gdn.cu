@@ -17,6 +17,8 @@ gdn_step_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, 
                 const float* __restrict__ g, const float* __restrict__ beta, const float* __restrict__ state_in,
                 uint16_t* __restrict__ y, float* __restrict__ state_out, float* __restrict__ state_mid, int B,
                 int T, int Hk, int Hv, int Dv) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int Dk = NP * 32;
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;  // (b*Hv + hv)*Dv + dv
@@ -68,6 +70,8 @@ constexpr int kFusedDVB = kFusedWarps * kFusedRPW;   // dv rows per CTA
 template <int NP>
 __global__ void __launch_bounds__(kFusedWarps * 32)
 gdn_fused_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int Dk = NP * 32;
   extern __shared__ __align__(16) float sm[];
   const int S = A.S, KC = A.KC, Hk = A.Hk, Hv = A.Hv, Dv = A.Dv;
@@ -213,6 +217,8 @@ __global__ void __launch_bounds__(256)
 gdn_norm_gate_kernel(const float* __restrict__ y, const uint16_t* __restrict__ z, long long ld_z,
                      const uint16_t* __restrict__ w, uint16_t* __restrict__ out, long long ld_out, int S, int H,
                      float eps) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int Dv = NP * 32;
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;  // t*H + h
@@ -248,7 +254,7 @@ extern "C" int qmtp_gdn_step(const void* q, const void* k, const void* v, const 
   const int wpb = 8;
   const long long blocks = (rows + wpb - 1) / wpb;
   if (blocks > 0x7FFFFFFF) return QMTP_ERR_SHAPE;
-  gdn_step_kernel<4><<<unsigned(blocks), wpb * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(gdn_step_kernel<4>, dim3(unsigned(blocks)), dim3(wpb * 32), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k), static_cast<const uint16_t*>(v), g, beta,
       state_in, static_cast<uint16_t*>(y), state_out, T > 1 ? state_mid : nullptr, B, T, Hk, Hv, Dv);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
@@ -270,7 +276,7 @@ extern "C" int qmtp_gdn_fused_ex(const qmtp_gdn_args* args, void* stream) {
     if (p && !aligned16(p)) return QMTP_ERR_ALIGN;
   const size_t smem = size_t(A.S) * (2 * 128 + kFusedDVB + 2) * sizeof(float);
   dim3 grid(A.Hv, (A.Dv + kFusedDVB - 1) / kFusedDVB);
-  gdn_fused_kernel<4><<<grid, kFusedWarps * 32, smem, static_cast<cudaStream_t>(stream)>>>(A, device_error_ptr());
+  launch_kernel(gdn_fused_kernel<4>, dim3(grid), dim3(kFusedWarps * 32), smem, static_cast<cudaStream_t>(stream), A, device_error_ptr());
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 
@@ -316,7 +322,7 @@ extern "C" int qmtp_gdn_norm_gate(const float* y, const void* z, int ld_z, const
   if (!y || !z || !w || !out) return QMTP_ERR_ARG;
   if (S < 1 || H < 1 || Dv != 128 || ld_z < H * Dv || ld_out < H * Dv) return QMTP_ERR_SHAPE;
   const int rows = S * H, wpb = 8;
-  gdn_norm_gate_kernel<4><<<(rows + wpb - 1) / wpb, wpb * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(gdn_norm_gate_kernel<4>, dim3((rows + wpb - 1) / wpb), dim3(wpb * 32), 0, static_cast<cudaStream_t>(stream), 
       y, static_cast<const uint16_t*>(z), ld_z, static_cast<const uint16_t*>(w), static_cast<uint16_t*>(out), ld_out,
       S, H, eps);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;

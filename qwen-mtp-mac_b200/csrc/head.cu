@@ -107,6 +107,8 @@ constexpr int kTopkThreads = 256;
 
 __global__ void __launch_bounds__(kTopkThreads)
 topk_partial_kernel(const uint16_t* __restrict__ vals, long long ld, int V, int k, uint64_t* __restrict__ cand) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char sm_raw[];
   int* hist = reinterpret_cast<int*>(sm_raw);
   int* s_res = hist + 256;
@@ -151,6 +153,8 @@ __global__ void __launch_bounds__(kMergeThreads)
 topk_merge_kernel(const uint64_t* __restrict__ cand, int G, int k, int NP, const uint16_t* __restrict__ W,
                   const uint16_t* __restrict__ h, int K, int32_t* __restrict__ out_idx,
                   uint16_t* __restrict__ out_fine, int32_t* __restrict__ out_amax) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char sm_raw[];
   uint64_t* s = reinterpret_cast<uint64_t*>(sm_raw);  // [NP]
   uint64_t* fk = s + NP;                              // [k] fine candidate words
@@ -209,6 +213,8 @@ topk_merge_kernel(const uint64_t* __restrict__ cand, int G, int k, int NP, const
 // Argmax over V (per row): block maxima of candidate words, then one block per row.
 __global__ void __launch_bounds__(256)
 argmax_partial_kernel(const uint16_t* __restrict__ vals, long long ld, int V, uint64_t* __restrict__ part) {
+  pdl_trigger();
+  pdl_wait();
   const int G = gridDim.x, blk = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
   const int i0 = int((long long)blk * V / G), i1 = int((long long)(blk + 1) * V / G);
   const uint16_t* row = vals + (long long)m * ld;
@@ -226,6 +232,8 @@ argmax_partial_kernel(const uint16_t* __restrict__ vals, long long ld, int V, ui
 }
 
 __global__ void argmax_final_kernel(const uint64_t* __restrict__ part, int G, int32_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x, lane = threadIdx.x;
   uint64_t best = 0;
   for (int i = lane; i < G; i += 32) best = max(best, part[(long long)m * G + i]);
@@ -271,12 +279,12 @@ extern "C" int qmtp_topk_rescore(const void* vals, int ld, int M, int V, int k, 
   const int slice = (V + G - 1) / G;
   const size_t smemA = (256 + 4 + 32) * sizeof(int) + size_t(slice) * sizeof(uint16_t);
   uint64_t* cand = static_cast<uint64_t*>(workspace);
-  topk_partial_kernel<<<dim3(G, M), kTopkThreads, smemA, st>>>(static_cast<const uint16_t*>(vals), ld, V, k, cand);
+  launch_kernel(topk_partial_kernel, dim3(dim3(G, M)), dim3(kTopkThreads), smemA, st, static_cast<const uint16_t*>(vals), ld, V, k, cand);
   const size_t smemB = size_t(NP + k) * sizeof(uint64_t);
   static const cudaError_t attr =
       cudaFuncSetAttribute(topk_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
   if (attr != cudaSuccess) return QMTP_ERR_CUDA;
-  topk_merge_kernel<<<M, kMergeThreads, smemB, st>>>(cand, G, k, NP, static_cast<const uint16_t*>(w_fine),
+  launch_kernel(topk_merge_kernel, dim3(M), dim3(kMergeThreads), smemB, st, cand, G, k, NP, static_cast<const uint16_t*>(w_fine),
                                                       static_cast<const uint16_t*>(h), K, out_idx,
                                                       static_cast<uint16_t*>(out_fine), out_argmax);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
@@ -295,8 +303,8 @@ extern "C" int qmtp_argmax_bf16(const void* vals, int ld, int M, int V, int* out
   const int G = std::min(256, std::max(1, V / 1024));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint64_t* part = static_cast<uint64_t*>(workspace);
-  argmax_partial_kernel<<<dim3(G, M), 256, 0, st>>>(static_cast<const uint16_t*>(vals), ld, V, part);
-  argmax_final_kernel<<<M, 32, 0, st>>>(part, G, out);
+  launch_kernel(argmax_partial_kernel, dim3(dim3(G, M)), dim3(256), 0, st, static_cast<const uint16_t*>(vals), ld, V, part);
+  launch_kernel(argmax_final_kernel, dim3(M), dim3(32), 0, st, part, G, out);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 

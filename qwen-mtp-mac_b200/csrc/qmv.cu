@@ -131,6 +131,10 @@ qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
     const int pre = min(NS - 1, ntiles);
     for (int t = 0; t < pre; ++t) issue(t);
   }
+  // The weights are constant: their first tiles are fetched while the previous kernel may still
+  // run; everything below reads or writes activations and waits for it.
+  pdl_trigger();
+  pdl_wait();
 
   // x prologue (this thread's 32 elements of every row m).  Affine: bf16 pairs
   // xb[m][4q + j] = (x[8q + j], x[8q + j + 4]) matching the nibble pairs of word q, the lane sums
@@ -299,7 +303,7 @@ static int launch_qmv(const void* x, const void* w, const void* s, const void* b
     return QMTP_OK;
   }
   const int grid = std::max(1, std::min(N, sm_count() * occ));
-  kern<<<grid, W * 32, C::SMEM, st>>>(static_cast<const uint16_t*>(x), static_cast<const uint32_t*>(w),
+  launch_kernel(kern, dim3(grid), dim3(W * 32), C::SMEM, st, static_cast<const uint16_t*>(x), static_cast<const uint32_t*>(w),
                                         static_cast<const uint8_t*>(s), static_cast<const uint8_t*>(b),
                                         static_cast<uint16_t*>(y), static_cast<const uint16_t*>(res), N, ldy,
                                         device_error_ptr());
@@ -350,6 +354,8 @@ static int qmv_entry(const void* x, const void* w, const void* s, const void* b,
 // reduction order gives the oracle's values; the rest is elementwise.
 __global__ void quantize_affine_kernel(const uint16_t* __restrict__ w, uint32_t* __restrict__ wq,
                                        uint16_t* __restrict__ sc, uint16_t* __restrict__ bi, int N, int K) {
+  pdl_trigger();
+  pdl_wait();
   const int G = K / 64;
   const long long gid = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x / 32);
   if (gid >= (long long)N * G) return;
@@ -435,7 +441,7 @@ extern "C" int qmtp_quantize_affine_g64(const void* w, void* wq, void* scales, v
   const int wpb = 8;
   const long long blocks = (groups + wpb - 1) / wpb;
   if (blocks > 0x7FFFFFFFLL) return QMTP_ERR_SHAPE;
-  quantize_affine_kernel<<<unsigned(blocks), wpb * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(quantize_affine_kernel, dim3(unsigned(blocks)), dim3(wpb * 32), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const uint16_t*>(w), static_cast<uint32_t*>(wq), static_cast<uint16_t*>(scales),
       static_cast<uint16_t*>(biases), N, K);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;

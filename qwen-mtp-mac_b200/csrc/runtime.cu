@@ -1,4 +1,5 @@
 // Library-wide runtime pieces: error text, version, the device error word, device properties.
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -33,6 +34,14 @@ int sm_count() {
     count[dev] = c > 0 ? c : 1;
   });
   return count[dev];
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("QMTP_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 }  // namespace qmtp
