@@ -312,6 +312,29 @@ def run_kernel(args):
         run = lambda i: gdn_core(Layer, win, ab[..., :Hv], ab[..., Hv:], states[i % copies], snap=True)
         unit_bytes = Hv * D * D * 4 * (1 + S) + (S + KC - 1) * Cd * 2 + S * Hv * D * 4
         label = "GatedDeltaNet fused verify step T=3 (snapshots)"
+    elif args.kernel == "moe":
+        from qmtp import moe
+
+        mode = args.shape if args.shape in ("mxfp4", "nvfp4") else "mxfp4"
+        E, H, I, T, TOPK, NSH = 66, 2048, 1408, 256, 6, 2
+        copies = 2  # 2 x ~303 MB of expert weights in rotation (> 2x L2)
+        layers = []
+        for _ in range(copies):
+            wts = []
+            for shape in ((E, I, H), (E, I, H), (E, H, I)):
+                w = (torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+                wts.extend(moe.quantize(w, mode))
+                del w
+            layers.append(wts)
+        x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+        idx, sc = moe.route(torch.randn(T, E - NSH, generator=g, device=dev), TOPK, NSH)
+        y = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        run = lambda i: moe.moe_decode(x, *layers[i % copies], idx, sc, limit=None, mode=mode, out=y)
+        G = 32 if mode == "mxfp4" else 16
+        wbytes = E * 3 * H * I * (0.5 + 1 / G)
+        unit_bytes = int(wbytes + T * H * 2 * 2 + idx.numel() * 8)
+        flops = 2.0 * T * (TOPK + NSH) * 3 * H * I
+        label = f"MoE config5 {mode}: T={T} E={E - NSH}+{NSH} top{TOPK} H={H} I={I}"
     else:  # head
         V, D, M = 248320, 4096, 3
         W = (torch.randn(V, D, generator=g, device=dev) * 0.02).to(torch.bfloat16)
@@ -342,7 +365,10 @@ def run_kernel(args):
         torch.cuda.synchronize()
     us = ev0.elapsed_time(ev1) * 1e3 / K
     gbs = unit_bytes / (us * 1e-6) / 1e9
-    print(json.dumps({"kernel": args.kernel, "workload": label, "us_per_call": round(us, 3),
+    extra = {}
+    if args.kernel == "moe":
+        extra = {"tflops": round(flops / (us * 1e-6) / 1e12, 1)}
+    print(json.dumps({**extra, "kernel": args.kernel, "workload": label, "us_per_call": round(us, 3),
                       "bytes_per_call": unit_bytes, "achieved_GBps": round(gbs, 1), "peak": peak,
                       "peak_kind": peak_kind, "frac": round(gbs / peak, 4), "calls": K, "clocks": clk.summary(),
                       "device_error": _lib.device_error()}), flush=True)
@@ -395,7 +421,7 @@ def main():
     ap.add_argument("--cpu-cycles", type=int, default=3, help="oracle cycles for cpu_baseline (0 = skip)")
     ap.add_argument("--ref-prompt", type=int, default=16)
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens (ours)")
-    ap.add_argument("--kernel", default=None, choices=["qmv", "gdn", "head"],
+    ap.add_argument("--kernel", default=None, choices=["qmv", "gdn", "head", "moe"],
                     help="time one kernel at a config shape instead of the decode loop")
     ap.add_argument("--shape", default="12288,4096,3", help="qmv: N,K,M")
     args = ap.parse_args()

@@ -207,6 +207,40 @@ int qmtp_attention(const void* q, const void* gate, const void* k_cache, const v
 /* SwiGLU of mlx-lm's MLP: out [S, I] = bf16(silu(gate) * up), gu [S, ld] = (gate | up) columns. */
 int qmtp_swiglu(const void* gu, int ld, int S, int I, void* out, void* stream);
 
+/* ---------------------------------------------------------------- MXFP4 / NVFP4 MoE
+ * Replaces experiments/deepseek_moe/kernels.py:133-155 (moe_decode, batch 1) with the batched
+ * decode of T tokens.  Weight layout as the reference (kernels.py:3-5): w uint32 [E, N, K/8],
+ * 8 e2m1 nibbles per word, low nibble = lowest k; scales uint8 [E, N, K/G].
+ * fmt 0 = MXFP4 (e8m0 scale per 32, kernels.py:31-32), fmt 1 = NVFP4 (e4m3 per 16, sign ignored
+ * as qmv_kernel.py:26-28). */
+#define QMTP_FP4_MXFP4 0
+#define QMTP_FP4_NVFP4 1
+
+/* Quantizes bf16 w [N, K] (K % G == 0) into (wq, scales); OCP MX rule for MXFP4, e4m3(amax/6) for
+ * NVFP4, round-to-nearest-even e2m1 codes.  (The reference draws random bits instead,
+ * bench_moe.py:24-31; the quantizer is this library's.) */
+int qmtp_quantize_fp4(int fmt, const void* w, long long N, int K, void* wq, void* scales, void* stream);
+
+/* Router (bench_moe.py:40-42 builds idx / scores the same way): logits fp32 [T, E] -> top_k experts by
+ * logit (ties to the lower id), weights softmax-renormalised over the chosen k times routed_scale,
+ * then n_shared shared experts E .. E+n_shared-1 with weight 1.  idx int32 / scores fp32
+ * [T, top_k + n_shared].  E <= 1024, top_k + n_shared <= 16. */
+int qmtp_moe_route(const void* logits, int T, int E, int top_k, int n_shared, float routed_scale, void* idx,
+                   void* scores, void* stream);
+
+/* Device workspace (bytes) of qmtp_moe for T tokens, S slots per token, E experts, hidden H, FFN I. */
+size_t qmtp_moe_workspace(int T, int S, int E, int H, int I);
+
+/* y bf16 [T, H] = sum_j scores[t,j] * Wd[e] (silu(min(Wg[e] x_t, L)) * clamp(Wu[e] x_t, -L, L)),
+ * e = idx[t, j] (kernels.py:35-107).  x bf16 [T, H]; wg, wu [E, I, H/8]; wd [E, H, I/8]; limit = +inf
+ * disables the clamp.  H, I multiples of 128; T*S <= 65535; E <= 1024; scale rows of one 128-row
+ * tile must fit the kernel's scale buffers (H <= 4096 MXFP4 / 2048 NVFP4).  All pointers 16-B
+ * aligned, workspace 256-B aligned.  An expert id outside [0, E) raises the device error word and
+ * its slot contributes nothing. */
+int qmtp_moe(int fmt, const void* x, const void* wg, const void* sg, const void* wu, const void* su, const void* wd,
+             const void* sd, const void* idx, const void* scores, void* y, int T, int S, int E, int H, int I,
+             float limit, void* workspace, size_t ws_bytes, void* stream);
+
 /* Control block of the device-side speculative loop (int32 [QMTP_CTRL_SIZE]). */
 #define QMTP_CTRL_SLOT 0      /* GatedDeltaNet state ring slot before the next verify */
 #define QMTP_CTRL_CONV_ROW 1  /* row of the conv state inside the [2 * win_rows, C] window buffer */

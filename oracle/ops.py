@@ -249,3 +249,61 @@ def dot_bf16(w_row, h_row) -> np.float32:
     w = np.ascontiguousarray(w_row, np.uint16)
     h = np.ascontiguousarray(h_row, np.uint16)
     return np.float32(lib().qo_dot_bf16(_p(w), _p(h), _I(w.size)))
+
+
+# ---------------------------------------------------------------- MXFP4 / NVFP4 MoE (experiments/deepseek_moe)
+FP4_FORMATS = {"mxfp4": (0, 32), "nvfp4": (1, 16)}
+
+
+def quantize_fp4(w_bf16, mode: str = "mxfp4"):
+    """C qo_quantize_fp4: bf16 [..., N, K] -> (w uint32 [..., N, K/8], scales uint8 [..., N, K/G])."""
+    fmt, G = FP4_FORMATS[mode]
+    w = np.ascontiguousarray(w_bf16, dtype=np.uint16)
+    lead, K = w.shape[:-1], w.shape[-1]
+    N = int(np.prod(lead))
+    wq = np.empty(lead + (K // 8,), np.uint32)
+    s = np.empty(lead + (K // G,), np.uint8)
+    assert lib().qo_quantize_fp4(_I(fmt), _p(w), ctypes.c_long(N), _I(K), _p(wq), _p(s)) == 0
+    return wq, s
+
+
+def dequant_fp4(wq, s, mode: str = "mxfp4") -> np.ndarray:
+    fmt, _ = FP4_FORMATS[mode]
+    wq = np.ascontiguousarray(wq, np.uint32)
+    s = np.ascontiguousarray(s, np.uint8)
+    K = wq.shape[-1] * 8
+    N = int(np.prod(wq.shape[:-1]))
+    out = np.empty(wq.shape[:-1] + (K,), np.float32)
+    lib().qo_dequant_fp4(_I(fmt), _p(wq), _p(s), ctypes.c_long(N), _I(K), _p(out))
+    return out
+
+
+def moe_route(logits, top_k: int = 6, n_shared: int = 2, routed_scale: float = 1.0):
+    """C qo_moe_route: fp32 [T, E] -> (idx int32 [T, top_k+n_shared], scores fp32)."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    T, E = lg.shape
+    S = top_k + n_shared
+    idx = np.empty((T, S), np.int32)
+    sc = np.empty((T, S), np.float32)
+    lib().qo_moe_route(_p(lg), _I(T), _I(E), _I(top_k), _I(n_shared), ctypes.c_float(routed_scale), _p(idx), _p(sc))
+    return idx, sc
+
+
+def moe(x_bf16, wg, sg, wu, su, wd, sd, idx, scores, mode: str = "mxfp4", limit=None):
+    """C qo_moe (experiments/deepseek_moe/kernels.py:35-107 for T tokens): (y bf16 [T,H], y fp32 [T,H])."""
+    fmt, _ = FP4_FORMATS[mode]
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    x = x.reshape(-1, x.shape[-1])
+    T, H = x.shape
+    idx = np.ascontiguousarray(idx, np.int32).reshape(T, -1)
+    scores = np.ascontiguousarray(scores, np.float32).reshape(T, -1)
+    E, I = wg.shape[0], wg.shape[1]
+    arrs = [np.ascontiguousarray(a) for a in (wg, sg, wu, su, wd, sd)]
+    yb = np.empty((T, H), np.uint16)
+    yf = np.empty((T, H), np.float32)
+    lim = np.float32(np.inf if limit is None else limit)
+    rc = lib().qo_moe(_I(fmt), _p(x), *[_p(a) for a in arrs], _p(idx), _p(scores), _I(T), _I(idx.shape[1]), _I(E),
+                      _I(H), _I(I), ctypes.c_float(lim), _p(yf), _p(yb))
+    if rc != 0:
+        raise ValueError(f"qo_moe: rc {rc}")
+    return yb, yf

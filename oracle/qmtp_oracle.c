@@ -812,3 +812,184 @@ QO_API void qo_swiglu(const uint16_t* gu, int ld, int S, int I, uint16_t* out) {
 QO_API void qo_add_bf16(const uint16_t* a, const uint16_t* b, uint16_t* out, long n) {
   for (long i = 0; i < n; ++i) out[i] = qo_f2bf(qo_bf2f(a[i]) + qo_bf2f(b[i]));
 }
+
+/* ------------------------------------------------------------------ MXFP4 / NVFP4 MoE
+ * Weight format (experiments/deepseek_moe/kernels.py:3-5, qmv_kernel.py:7-9): uint32 [N, K/8],
+ * 8 e2m1 nibbles per word, low nibble = lowest k; scales uint8 [N, K/G]:
+ *   fmt 0 MXFP4: G = 32, e8m0 scale 2^(s-127)          (kernels.py:31-32 e8m0_scale)
+ *   fmt 1 NVFP4: G = 16, e4m3 scale, sign bit ignored   (qmv_kernel.py:26-28 e4m3_scale)
+ *
+ * Quantizers.  The reference never quantizes (its bench draws random bits, bench_moe.py:24-31),
+ * so the quantizer is this library's own, written from the OCP Microscaling spec v1.0 (sec. 6.3):
+ *   MXFP4: s = clamp(floor(log2(amax)) - 2 + 127, 0, 254) (amax = 0 -> s = 0), v = w * 2^(127-s);
+ *   NVFP4: scale = e4m3_rne(amax / 6) saturated to 448, v = w / scale (scale 0 -> all codes 0);
+ *   code = e2m1 round-to-nearest-even of v, saturated at 6; a zero magnitude is coded +0.
+ * NaN / Inf weights are not supported. */
+static inline uint32_t qo_e2m1_code(float v) {
+  float a = fabsf(v);
+  uint32_t c = 0;
+  if (a > 0.25f) c = 1;
+  if (a >= 0.75f) c = 2;
+  if (a > 1.25f) c = 3;
+  if (a >= 1.75f) c = 4;
+  if (a > 2.5f) c = 5;
+  if (a >= 3.5f) c = 6;
+  if (a > 5.0f) c = 7;
+  if (c && signbit(v)) c |= 8u;
+  return c;
+}
+static inline uint32_t qo_e4m3_code(float f) { /* f >= 0 */
+  if (!(f > 0.0f)) return 0;
+  if (f > 448.0f) return 0x7E;
+  int e = ilogbf(f);
+  if (e < -6) return (uint32_t)rintf(f * 512.0f); /* subnormal grid 2^-9 (8 -> code 8 = 2^-6) */
+  uint32_t m = (uint32_t)rintf((ldexpf(f, -e) - 1.0f) * 8.0f);
+  if (m == 8) { m = 0; e += 1; }
+  uint32_t c = ((uint32_t)(e + 7) << 3) | m;
+  return c > 0x7E ? 0x7E : c;
+}
+QO_API int qo_quantize_fp4(int fmt, const uint16_t* w, long N, int K, uint32_t* wq, uint8_t* sc) {
+  const int G = fmt == 0 ? 32 : 16;
+  if ((fmt != 0 && fmt != 1) || K % G) return -1;
+  for (long n = 0; n < N; ++n)
+    for (int g = 0; g < K / G; ++g) {
+      const uint16_t* wr = w + n * K + (long)g * G;
+      float amax = 0.0f;
+      for (int i = 0; i < G; ++i) amax = fmaxf(amax, fabsf(qo_bf2f(wr[i])));
+      uint32_t s;
+      float mul = 0.0f, div = 0.0f;
+      if (fmt == 0) {
+        int se = amax > 0.0f ? ilogbf(amax) - 2 + 127 : 0;
+        s = (uint32_t)(se < 0 ? 0 : se > 254 ? 254 : se);
+        mul = s == 0 ? qo_asf(0x7F000000u) : qo_asf((254u - s) << 23); /* 2^(127-s) */
+      } else {
+        s = qo_e4m3_code(amax / 6.0f);
+        div = qo_e4m3(s);
+      }
+      sc[n * (K / G) + g] = (uint8_t)s;
+      for (int i = 0; i < G; i += 8) {
+        uint32_t word = 0;
+        for (int j = 0; j < 8; ++j) {
+          float x = qo_bf2f(wr[i + j]);
+          float v = fmt == 0 ? x * mul : (div > 0.0f ? x / div : 0.0f);
+          word |= qo_e2m1_code(v) << (4 * j);
+        }
+        wq[n * (K / 8) + (g * G + i) / 8] = word;
+      }
+    }
+  return 0;
+}
+
+/* Dequantize one row of K weights (exact in fp32). */
+static void qo_fp4_row(int fmt, const uint32_t* wrow, const uint8_t* srow, int K, float* out) {
+  const int G = fmt == 0 ? 32 : 16;
+  for (int k = 0; k < K; ++k) {
+    float s = fmt == 0 ? qo_e8m0(srow[k / G]) : qo_e4m3(srow[k / G]);
+    out[k] = qo_e2m1((wrow[k / 8] >> (4 * (k % 8))) & 15u) * s;
+  }
+}
+QO_API void qo_dequant_fp4(int fmt, const uint32_t* wq, const uint8_t* sc, long N, int K, float* out) {
+  const int G = fmt == 0 ? 32 : 16;
+  for (long n = 0; n < N; ++n) qo_fp4_row(fmt, wq + n * (K / 8), sc + n * (K / G), K, out + n * K);
+}
+
+/* Router: softmax over E routed logits, top-k, renormalised over the chosen k (DeepSeek
+ * norm_topk_prob), times routed_scale; then n_shared shared experts (ids E .. E+n_shared-1) with
+ * score 1.0, as bench_moe.py:41-42 builds idx / scores.  The renormalised weight of expert i is
+ * exp(l_i - l_max) / sum_{j in topk} exp(l_j - l_max): the full softmax denominator cancels, so it
+ * is computed that way.  Order of selection: larger logit first, ties to the lower expert id; a NaN
+ * logit ranks below every number.  Fixed fp32 sequence: d_j = l_j - l_top (j in selection
+ * order), e_j = exp(d_j), sum = ((e_0 + e_1) + e_2) ..., w_j = (e_j / sum) * routed_scale. */
+static inline uint32_t qo_logit_key(float f) {
+  if (f != f) return 0;
+  uint32_t u = qo_asu(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+QO_API void qo_moe_route(const float* logits, int T, int E, int top_k, int n_shared, float routed_scale,
+                         int32_t* idx, float* scores) {
+  const int S = top_k + n_shared;
+  for (int t = 0; t < T; ++t) {
+    const float* l = logits + (long)t * E;
+    int32_t* id = idx + (long)t * S;
+    float* sc = scores + (long)t * S;
+    for (int j = 0; j < top_k; ++j) {
+      int best = -1;
+      uint32_t bk = 0;
+      for (int e = 0; e < E; ++e) {
+        int taken = 0;
+        for (int q = 0; q < j; ++q) taken |= id[q] == e;
+        if (taken) continue;
+        uint32_t k = qo_logit_key(l[e]);
+        if (best < 0 || k > bk) { best = e; bk = k; }
+      }
+      id[j] = best;
+    }
+    float ex[64];
+    float sum = 0.0f;
+    for (int j = 0; j < top_k; ++j) {
+      ex[j] = qo_expf(l[id[j]] - l[id[0]]);
+      sum = j == 0 ? ex[0] : sum + ex[j];
+    }
+    for (int j = 0; j < top_k; ++j) sc[j] = (ex[j] / sum) * routed_scale;
+    for (int j = 0; j < n_shared; ++j) { id[top_k + j] = E + j; sc[top_k + j] = 1.0f; }
+  }
+}
+
+/* Expert FFN, restating experiments/deepseek_moe/kernels.py:35-107 for T tokens:
+ *   h[t,j,i] = fp32( silu(min(g, L)) * clamp(u, -L, L) ),  g = Wg[e] x_t, u = Wu[e] x_t  (e = idx[t,j])
+ *   y[t,n]   = sum_j scores[t,j] * (Wd[e] h[t,j])[n]
+ * The dots and the weighted sum are evaluated in double (more accurate than the fp32 lane sums of
+ * the reference); h is rounded to fp32 as the reference stores it (kernels.py:146).  limit = +inf
+ * disables the clamp.  y_f32 gets the sum rounded to fp32, y_bf16 its RNE bf16.
+ * Weights: wg, wu [E, I, H/8] / scales [E, I, H/G]; wd [E, H, I/8] / [E, H, I/G]. */
+QO_API int qo_moe(int fmt, const uint16_t* x, const uint32_t* wg, const uint8_t* sg, const uint32_t* wu,
+                  const uint8_t* su, const uint32_t* wd, const uint8_t* sd, const int32_t* idx, const float* scores,
+                  int T, int S, int E, int H, int I, float limit, float* y_f32, uint16_t* y_bf16) {
+  const int G = fmt == 0 ? 32 : 16;
+  if (H % G || I % G || H % 8 || I % 8 || H > 8192 || I > 8192) return -1;
+  for (long i = 0; i < (long)T * S; ++i)
+    if (idx[i] < 0 || idx[i] >= E) return -2;
+  double* yacc = (double*)calloc((size_t)T * H, sizeof(double));
+  double* xd = (double*)malloc((size_t)T * H * sizeof(double));
+  int* list = (int*)malloc((size_t)T * S * sizeof(int));
+  float* h = (float*)malloc((size_t)T * S * I * sizeof(float));
+  for (long i = 0; i < (long)T * H; ++i) xd[i] = qo_bf2f(x[i]);
+  for (int e = 0; e < E; ++e) {
+    int n = 0;
+    for (int i = 0; i < T * S; ++i)
+      if (idx[i] == e) list[n++] = i;
+    if (!n) continue;
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < I; ++r) {
+      float rg[8192], ru[8192];
+      qo_fp4_row(fmt, wg + ((long)e * I + r) * (H / 8), sg + ((long)e * I + r) * (H / G), H, rg);
+      qo_fp4_row(fmt, wu + ((long)e * I + r) * (H / 8), su + ((long)e * I + r) * (H / G), H, ru);
+      for (int q = 0; q < n; ++q) {
+        const double* xt = xd + (long)(list[q] / S) * H;
+        double g = 0.0, u = 0.0;
+        for (int k = 0; k < H; ++k) { g += rg[k] * xt[k]; u += ru[k] * xt[k]; }
+        g = g < limit ? g : limit;
+        u = u < -limit ? -limit : (u > limit ? limit : u);
+        h[(long)q * I + r] = (float)(g / (1.0 + exp(-g)) * u);
+      }
+    }
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < H; ++r) {
+      float rd[8192];
+      qo_fp4_row(fmt, wd + ((long)e * H + r) * (I / 8), sd + ((long)e * H + r) * (I / G), I, rd);
+      for (int q = 0; q < n; ++q) {
+        double a = 0.0;
+        const float* hq = h + (long)q * I;
+        for (int k = 0; k < I; ++k) a += (double)rd[k] * hq[k];
+        yacc[(long)(list[q] / S) * H + r] += (double)scores[list[q]] * a;
+      }
+    }
+  }
+  for (long i = 0; i < (long)T * H; ++i) {
+    float f = (float)yacc[i];
+    if (y_f32) y_f32[i] = f;
+    if (y_bf16) y_bf16[i] = qo_f2bf(f);
+  }
+  free(yacc); free(xd); free(list); free(h);
+  return 0;
+}

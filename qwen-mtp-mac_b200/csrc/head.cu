@@ -27,33 +27,6 @@ __device__ __forceinline__ uint64_t cand_word(uint32_t key, uint32_t idx) {
 }
 __device__ __forceinline__ uint32_t cand_idx(uint64_t w) { return 0xFFFFFFFFu - uint32_t(w & 0xFFFFFFFFu); }
 
-// Block-wide exclusive prefix sum of one int per thread (blockDim.x <= 1024, multiple of 32).
-__device__ int block_excl_scan(int v, int* s_warp, int& total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  int x = v;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    const int o = __shfl_up_sync(0xFFFFFFFFu, x, d);
-    if (lane >= d) x += o;
-  }
-  if (lane == 31) s_warp[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int w = lane < nw ? s_warp[lane] : 0;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const int o = __shfl_up_sync(0xFFFFFFFFu, w, d);
-      if (lane >= d) w += o;
-    }
-    if (lane < nw) s_warp[lane] = w;  // inclusive per warp
-  }
-  __syncthreads();
-  total = s_warp[nw - 1];
-  const int base = warp > 0 ? s_warp[warp - 1] : 0;
-  __syncthreads();
-  return base + x - v;
-}
-
 // Finds (within the bins above `base`) the bin b where the count from the top reaches k.
 // hist[256]; warp 0 only.  Returns via s_res[0] = b, s_res[1] = count strictly above b.
 __device__ void find_bin(const int* hist, int k, int base, int* s_res) {

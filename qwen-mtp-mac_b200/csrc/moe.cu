@@ -1,0 +1,835 @@
+// MXFP4 / NVFP4 mixture-of-experts decode on B200: the batched form of moe_decode
+// (experiments/deepseek_moe/kernels.py:133-155) for T concurrent tokens.
+//
+//   h[t,j] = silu(min(Wg[e] x_t, L)) * clamp(Wu[e] x_t, -L, L)          e = idx[t,j]  (kernels.py:35-74)
+//   y[t]   = sum_j scores[t,j] * Wd[e] h[t,j]                                          (kernels.py:76-107)
+//
+// Weights keep the reference layout: uint32 [E, N, K/8] (8 e2m1 nibbles, low nibble = lowest k) and
+// uint8 scales [E, N, K/G] (MXFP4: e8m0, G = 32; NVFP4: e4m3 with the sign ignored, G = 16).
+//
+// Pipeline (one stream, each kernel a programmatic dependent of the previous one):
+//   moe_group    one CTA: stable counting sort of the T*S (token, slot) entries by expert, cut into
+//                token tiles of <= 64 entries; writes the tile table.
+//   moe_gather   per tile: the tile's token rows of x as a bf16 operand image (canonical K-major
+//                core-matrix layout of the tensor core, 128 K per chunk) in HBM.
+//   moe_gemm<GU> persistent, one CTA per SM; a unit = (tile, 128 weight rows).  Warp roles:
+//                  warp 0      TMA producer: weight tiles (2-D, 64-B swizzle), operand-image chunks
+//                              and the unit's scales (1-D bulk copies);
+//                  warp 1      tcgen05.mma issuer (M = 128, N = tile tokens, K = 16 per instruction),
+//                              A operand read from TMEM, B operand from shared memory;
+//                  warps 4-11  dequantizers: packed e2m1 + scale -> exact bf16, tcgen05.st into TMEM;
+//                  warps 12-15 epilogue: accumulators -> SwiGLU h (gate/up) or fp32 partials (down).
+//                gate/up writes h split as hi = bf16(h), lo = bf16(h - hi) (h to ~16 significant bits,
+//                the reference keeps h in fp32, kernels.py:146) straight into the down operand image;
+//                down multiplies the same weights by hi and lo and writes per-entry fp32 partials.
+//   moe_combine  y[t] = sum_j scores[t,j] * partial[t,j] in slot order, rounded to bf16.
+//
+// Dequantization is exact: e2m1 magnitudes are placed as bf16 subnormal-or-normal encodings of
+// v * 2^-126 (exponent low bits + top mantissa bit) and multiplied by the bf16 value 2^126 * scale
+// with one mul.rn.bf16x2 per element pair (two multiplies when that factor exceeds bf16 range).  The
+// eight nibbles of a word are laid out as element pairs (0,4), (1,5), (2,6), (3,7): the operand image
+// of the activations uses the same permutation of every 8 consecutive k, so the products are unchanged.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace qmtp {
+namespace moe {
+
+constexpr int kRows = 128;              // weight rows per unit (MMA M)
+constexpr int kChunk = 128;             // K per pipeline stage
+constexpr int kMaxTok = 64;             // entries per token tile (MMA N <= 64)
+constexpr int kStages = 4;
+constexpr int kWBytes = kRows * kChunk / 2;  // packed bytes of one 128 x 128 weight tile
+constexpr int kThreads = 512;
+constexpr unsigned kTmemCols = 512;
+
+struct Tile {
+  int expert, entry0, ntok, nt, row0, pad0, pad1, pad2;
+};
+
+template <bool GU>
+struct Cfg {
+  static constexpr int NMAT = GU ? 2 : 1;
+  static constexpr int BSTAGE = GU ? kMaxTok * 256 : kMaxTok * 512;  // operand-image bytes per stage
+  static constexpr int STAGE = NMAT * kWBytes + BSTAGE;
+  static constexpr int SCALE_BUF = GU ? 32768 : 16384;
+  static constexpr int NA = GU ? 2 : 4;           // TMEM A stages
+  static constexpr int ACOLS = GU ? 128 : 64;     // TMEM columns of one A stage (all matrices)
+  static constexpr int ACC_STRIDE = GU ? 128 : 64;
+  static constexpr int A_BASE = 2 * ACC_STRIDE;   // accumulators double-buffered below the A stages
+  static constexpr int SMEM = kStages * STAGE + 2 * SCALE_BUF + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(A_BASE + NA * ACOLS <= (int)kTmemCols, "TMEM budget");
+};
+
+// --------------------------------------------------------------------------- exact fp4 -> bf16
+// Scale byte -> bf16x2 multipliers.  Fast path: mult = 2^126 * scale fits bf16.  Slow path (rare):
+// multiply by 2^126 first, then by mult2 = scale.
+struct Mult {
+  uint32_t m, m2;
+  bool slow;
+};
+__device__ __forceinline__ Mult mult_e8m0(uint32_t s) {
+  Mult r;
+  r.slow = s > 128u;
+  r.m = ((s + 126u) << 7) * 0x00010001u;
+  r.m2 = (s << 7) * 0x00010001u;
+  return r;
+}
+__device__ __forceinline__ Mult mult_e4m3(uint32_t s) {
+  const uint32_t c = s & 0x7Fu;
+  const float f = c >= 8u ? __uint_as_float((c << 20) + (120u << 23)) : __fmul_rn(float(c), 0.001953125f);
+  Mult r;
+  r.slow = c >= 0x48u;  // e4m3 >= 4: 2^126 * scale overflows bf16
+  r.m = (r.slow ? 0u : (__float_as_uint(__fmul_rn(f, 0x1p126f)) >> 16)) * 0x00010001u;
+  r.m2 = (__float_as_uint(f) >> 16) * 0x00010001u;
+  return r;
+}
+// One word (8 nibbles) -> 4 bf16x2: pairs (0,4), (1,5), (2,6), (3,7).
+__device__ __forceinline__ void fp4_word(uint32_t w, const Mult& mu, uint32_t* r) {
+  const uint32_t y = w >> 8;
+  const uint32_t m0 = ((w & 0x000F000Fu) * 0x1040u) & 0x81C081C0u;
+  const uint32_t m1 = ((w & 0x00F000F0u) * 0x0104u) & 0x81C081C0u;
+  const uint32_t m2 = ((y & 0x000F000Fu) * 0x1040u) & 0x81C081C0u;
+  const uint32_t m3 = ((y & 0x00F000F0u) * 0x0104u) & 0x81C081C0u;
+  if (!mu.slow) {
+    r[0] = mul_bf16x2(m0, mu.m);
+    r[1] = mul_bf16x2(m1, mu.m);
+    r[2] = mul_bf16x2(m2, mu.m);
+    r[3] = mul_bf16x2(m3, mu.m);
+  } else {
+    const uint32_t p126 = 0x7E807E80u;
+    r[0] = mul_bf16x2(mul_bf16x2(m0, p126), mu.m2);
+    r[1] = mul_bf16x2(mul_bf16x2(m1, p126), mu.m2);
+    r[2] = mul_bf16x2(mul_bf16x2(m2, p126), mu.m2);
+    r[3] = mul_bf16x2(mul_bf16x2(m3, p126), mu.m2);
+  }
+}
+// Position of element k (0..7) of a word inside its permuted 8-group.
+__host__ __device__ __forceinline__ int perm8(int k) { return ((k & 3) << 1) | (k >> 2); }
+
+// --------------------------------------------------------------------------- quantizer
+// Bit-identical to the C oracle's qo_quantize_fp4 (OCP MX v1.0 sec. 6.3 for MXFP4; e4m3(amax/6)
+// scale for NVFP4).  One thread per group.
+__device__ __forceinline__ uint32_t e2m1_code(float v) {
+  const float a = fabsf(v);
+  uint32_t c = 0;
+  if (a > 0.25f) c = 1;
+  if (a >= 0.75f) c = 2;
+  if (a > 1.25f) c = 3;
+  if (a >= 1.75f) c = 4;
+  if (a > 2.5f) c = 5;
+  if (a >= 3.5f) c = 6;
+  if (a > 5.0f) c = 7;
+  if (c && (__float_as_uint(v) >> 31)) c |= 8u;
+  return c;
+}
+__device__ __forceinline__ int ilogb_pos(float f) {  // f > 0, finite
+  const uint32_t u = __float_as_uint(f);
+  const int e = int((u >> 23) & 0xFFu);
+  if (e) return e - 127;
+  return (31 - __clz(int(u & 0x7FFFFFu))) - 149;
+}
+__device__ __forceinline__ float e4m3_value(uint32_t s) {
+  const uint32_t c = s & 0x7Fu;
+  return c >= 8u ? __uint_as_float((c << 20) + (120u << 23)) : __fmul_rn(float(c), 0.001953125f);
+}
+__device__ __forceinline__ uint32_t e4m3_code(float f) {
+  if (!(f > 0.0f)) return 0;
+  if (f > 448.0f) return 0x7E;
+  int e = ilogb_pos(f);
+  if (e < -6) return uint32_t(rintf(__fmul_rn(f, 512.0f)));
+  const float mant = __uint_as_float((__float_as_uint(f) & 0x7FFFFFu) | 0x3F800000u);
+  uint32_t m = uint32_t(rintf(__fmul_rn(__fsub_rn(mant, 1.0f), 8.0f)));
+  if (m == 8u) { m = 0; e += 1; }
+  const uint32_t c = (uint32_t(e + 7) << 3) | m;
+  return c > 0x7Eu ? 0x7Eu : c;
+}
+__global__ void quantize_fp4_kernel(int fmt, const uint16_t* __restrict__ w, long long N, int K,
+                                    uint32_t* __restrict__ wq, uint8_t* __restrict__ sc) {
+  pdl_wait();
+  pdl_trigger();
+  const int G = fmt == 0 ? 32 : 16;
+  const int gpr = K / G;
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= N * gpr) return;
+  const long long n = gid / gpr;
+  const int g = int(gid % gpr);
+  const uint16_t* wr = w + n * K + (long long)g * G;
+  float v[32];
+  float amax = 0.0f;
+  for (int i = 0; i < G; ++i) {
+    v[i] = bf2f(wr[i]);
+    amax = fmaxf(amax, fabsf(v[i]));
+  }
+  uint32_t s;
+  float mul = 0.0f, div = 0.0f;
+  if (fmt == 0) {
+    int se = amax > 0.0f ? ilogb_pos(amax) - 2 + 127 : 0;
+    s = uint32_t(se < 0 ? 0 : se > 254 ? 254 : se);
+    mul = s == 0 ? __uint_as_float(0x7F000000u) : __uint_as_float((254u - s) << 23);
+  } else {
+    s = e4m3_code(__fdiv_rn(amax, 6.0f));
+    div = e4m3_value(s);
+  }
+  sc[n * gpr + g] = uint8_t(s);
+  for (int i = 0; i < G; i += 8) {
+    uint32_t word = 0;
+    for (int j = 0; j < 8; ++j) {
+      const float x = v[i + j];
+      const float q = fmt == 0 ? __fmul_rn(x, mul) : (div > 0.0f ? __fdiv_rn(x, div) : 0.0f);
+      word |= e2m1_code(q) << (4 * j);
+    }
+    wq[n * (K / 8) + (g * G + i) / 8] = word;
+  }
+}
+
+// --------------------------------------------------------------------------- router
+// One warp per token: top-k of E <= 1024 logits (larger first, ties to the lower id, NaN lowest),
+// weights = softmax over the chosen k (the oracle's qo_moe_route sequence), then shared experts.
+__device__ __forceinline__ uint32_t logit_key(float f) {
+  if (f != f) return 0;
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__global__ void moe_route_kernel(const float* __restrict__ logits, int T, int E, int top_k, int n_shared,
+                                 float routed_scale, int32_t* __restrict__ idx, float* __restrict__ scores) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const float* l = logits + (long long)t * E;
+  uint64_t cand[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int e = lane + 32 * i;
+    cand[i] = e < E ? (uint64_t(logit_key(l[e])) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(e)) : 0ull;
+  }
+  const int S = top_k + n_shared;
+  int sel[16];
+  for (int j = 0; j < top_k; ++j) {
+    uint64_t best = 0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) best = cand[i] > best ? cand[i] : best;
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) {
+      const uint64_t o = __shfl_xor_sync(0xFFFFFFFFu, best, d);
+      best = o > best ? o : best;
+    }
+    const int e = int(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu));
+    sel[j] = e;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (lane + 32 * i == e) cand[i] = 0ull;
+  }
+  if (lane == 0) {
+    float ex[16];
+    float sum = 0.0f;
+    const float top = l[sel[0]];
+    for (int j = 0; j < top_k; ++j) {
+      ex[j] = q_expf(__fsub_rn(l[sel[j]], top));
+      sum = j == 0 ? ex[0] : __fadd_rn(sum, ex[j]);
+    }
+    for (int j = 0; j < top_k; ++j) {
+      idx[(long long)t * S + j] = sel[j];
+      scores[(long long)t * S + j] = __fmul_rn(__fdiv_rn(ex[j], sum), routed_scale);
+    }
+    for (int j = 0; j < n_shared; ++j) {
+      idx[(long long)t * S + top_k + j] = E + j;
+      scores[(long long)t * S + top_k + j] = 1.0f;
+    }
+  }
+}
+
+// --------------------------------------------------------------------------- grouping
+// One CTA of 1024 threads.  Entry i = t*S + j.  Warp w owns a contiguous segment of entries; within
+// a warp, peers with the same expert are ranked by lane (match_any); a per-(warp, expert) count
+// table turns that into a stable global order: pos = offset[e] + before[w][e] + rank.  So experts
+// are laid out in id order and, within an expert, entries in (token, slot) order.
+__global__ void __launch_bounds__(1024) moe_group_kernel(const int32_t* __restrict__ idx, int n, int S, int E,
+                                                         int32_t* __restrict__ entry_pos,
+                                                         int32_t* __restrict__ sorted_tok,
+                                                         int32_t* __restrict__ rank_tmp, Tile* __restrict__ tiles,
+                                                         int32_t* __restrict__ counters, unsigned* err) {
+  extern __shared__ uint16_t cnt16[];  // [32][E]
+  __shared__ int s_warp[32];
+  __shared__ int s_eoff[1024];
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < 32 * E; i += blockDim.x) cnt16[i] = 0;
+  __syncthreads();
+  const int L = (n + 31) / 32;
+  const int seg0 = min(n, warp * L), seg1 = min(n, seg0 + L);
+  for (int b = seg0; b < seg1; b += 32) {
+    const int i = b + lane;
+    int e = -1;
+    if (i < seg1) {
+      e = idx[i];
+      if (e < 0 || e >= E) {
+        if (err) atomicOr(err, DEVERR_BADARG);
+        e = -1;
+      }
+    }
+    const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    int base = 0;
+    if (e >= 0) base = cnt16[warp * E + e];
+    __syncwarp();
+    if (e >= 0 && rank == 0) cnt16[warp * E + e] = uint16_t(base + __popc(peers));
+    __syncwarp();
+    if (i < seg1) rank_tmp[i] = e >= 0 ? base + rank : -1;
+  }
+  __syncthreads();
+  int cnt = 0;
+  if (tid < E) {
+    for (int w = 0; w < 32; ++w) {
+      const int c = cnt16[w * E + tid];
+      cnt16[w * E + tid] = uint16_t(cnt);
+      cnt += c;
+    }
+  }
+  const int ntile = (cnt + kMaxTok - 1) / kMaxTok;
+  const int last = cnt - kMaxTok * (ntile - 1);
+  const int prow = ntile ? kMaxTok * (ntile - 1) + ((last + 15) & ~15) : 0;
+  int tot_e, tot_t, tot_r;
+  const int eoff = block_excl_scan(cnt, s_warp, tot_e);
+  const int etile = block_excl_scan(ntile, s_warp, tot_t);
+  const int erow = block_excl_scan(prow, s_warp, tot_r);
+  if (tid < E) {
+    s_eoff[tid] = eoff;
+    for (int j = 0; j < ntile; ++j) {
+      Tile tl;
+      tl.expert = tid;
+      tl.entry0 = eoff + kMaxTok * j;
+      tl.ntok = min(kMaxTok, cnt - kMaxTok * j);
+      tl.nt = (tl.ntok + 15) & ~15;
+      tl.row0 = erow + kMaxTok * j;
+      tl.pad0 = tl.pad1 = tl.pad2 = 0;
+      tiles[etile + j] = tl;
+    }
+  }
+  if (tid == 0) {
+    counters[0] = tot_t;
+    counters[1] = tot_r;
+    counters[2] = tot_e;
+  }
+  __syncthreads();
+  for (int b = seg0; b < seg1; b += 32) {
+    const int i = b + lane;
+    if (i < seg1) {
+      const int r = rank_tmp[i];
+      if (r >= 0) {
+        const int e = idx[i];
+        const int pos = s_eoff[e] + cnt16[warp * E + e] + r;
+        entry_pos[i] = pos;
+        sorted_tok[pos] = i / S;
+      } else {
+        entry_pos[i] = -1;
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------- operand image of x
+// Tile image: K/128 chunks of nt x 128 bf16; inside a chunk, core matrix (k8, row8) at
+// ((k8 * nt/8) + row8) * 128 bytes, row r & 7 at 16 B steps, k permuted by perm8 inside each 8-group.
+// One 16-B unit per thread iteration, in image order (coalesced stores).
+__global__ void moe_gather_kernel(const uint16_t* __restrict__ x, int H, const Tile* __restrict__ tiles,
+                                  const int32_t* __restrict__ counters, const int32_t* __restrict__ sorted_tok,
+                                  uint8_t* __restrict__ ximg) {
+  pdl_wait();
+  pdl_trigger();
+  if (int(blockIdx.x) >= counters[0]) return;
+  const Tile tl = tiles[blockIdx.x];
+  const int nt8 = tl.nt >> 3;
+  const int units = tl.nt * (H >> 3);
+  uint8_t* base = ximg + (size_t)tl.row0 * H * 2;
+  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+    const int r7 = u & 7;
+    int v = u >> 3;
+    const int rg = v % nt8;
+    v /= nt8;  // v = chunk * 16 + k8
+    const int r = rg * 8 + r7;
+    uint4 o = make_uint4(0u, 0u, 0u, 0u);
+    if (r < tl.ntok) {
+      const int tok = sorted_tok[tl.entry0 + r];
+      const uint4 in = *reinterpret_cast<const uint4*>(x + (size_t)tok * H + (size_t)v * 8);
+      o.x = __byte_perm(in.x, in.z, 0x5410);  // (e0, e4)
+      o.y = __byte_perm(in.x, in.z, 0x7632);  // (e1, e5)
+      o.z = __byte_perm(in.y, in.w, 0x5410);  // (e2, e6)
+      o.w = __byte_perm(in.y, in.w, 0x7632);  // (e3, e7)
+    }
+    *reinterpret_cast<uint4*>(base + (size_t)u * 16) = o;
+  }
+}
+
+// --------------------------------------------------------------------------- grouped GEMM
+struct GemmArgs {
+  const uint8_t* sa;    // scales of matrix 0 (gate or down), [E*R, KS]
+  const uint8_t* sb;    // scales of matrix 1 (up), gate/up only
+  const uint8_t* bimg;  // operand images: x (gate/up) or h hi|lo (down)
+  const Tile* tiles;
+  const int32_t* counters;
+  uint8_t* himg;        // gate/up output: h operand images for down
+  float* yp;            // down output: per-entry fp32 partials [n, R]
+  int K;                // reduction length
+  int R;                // weight rows per expert
+  int KS;               // scale bytes per weight row
+  int fmt;              // 0 MXFP4, 1 NVFP4
+  float limit;          // SwiGLU clamp (+inf = off)
+  int h_rows;           // gate/up: K of the down GEMM (= R)
+  unsigned* err;        // library device error word
+};
+
+struct Bars {
+  uint64_t full[kStages], empty[kStages];
+  uint64_t afull[4], aempty[4];
+  uint64_t sfull[2], sempty[2];
+  uint64_t accfull[2], accempty[2];
+  uint64_t drain;
+  uint32_t tmem;
+  int abort;
+};
+
+template <bool GU>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1, GemmArgs a) {
+  using C = Cfg<GU>;
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = dsm;
+  uint8_t* sbufs = dsm + kStages * C::STAGE;
+  Bars* bars = reinterpret_cast<Bars*>(sbufs + 2 * C::SCALE_BUF);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  unsigned* err = a.err;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 8 + 1);
+    }
+    for (int s = 0; s < C::NA; ++s) {
+      mbar_init(&bars->afull[s], 8);
+      mbar_init(&bars->aempty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->sfull[s], 1);
+      mbar_init(&bars->sempty[s], 8);
+      mbar_init(&bars->accfull[s], 1);
+      mbar_init(&bars->accempty[s], 4);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&bars->tmem, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem;
+  volatile int* abort_flag = &bars->abort;
+
+  pdl_wait();
+  pdl_trigger();
+  const int RT = a.R / kRows;
+  const int total = a.counters[0] * RT;
+  const int nchunk = a.K / kChunk;
+  const uint32_t sbytes = uint32_t(kRows * a.KS);
+
+  if (warp == 0) {
+    // ----------------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first(), pol_b = policy_evict_last();
+      int it = 0, lu = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lu) {
+        const Tile tl = a.tiles[u / RT];
+        const int rt = u % RT;
+        const int row = tl.expert * a.R + rt * kRows;
+        const int sb = lu & 1;
+        if (!(ok = mbar_wait_bounded(&bars->sempty[sb], ((lu >> 1) & 1) ^ 1, err))) break;
+        mbar_expect_tx(&bars->sfull[sb], sbytes * C::NMAT);
+        bulk_g2s(sbufs + sb * C::SCALE_BUF, a.sa + (size_t)row * a.KS, sbytes, &bars->sfull[sb], pol_w);
+        if (GU) bulk_g2s(sbufs + sb * C::SCALE_BUF + sbytes, a.sb + (size_t)row * a.KS, sbytes, &bars->sfull[sb], pol_w);
+        const uint32_t bbytes = uint32_t(tl.nt * (GU ? 256 : 512));
+        const uint8_t* bsrc = a.bimg + (size_t)tl.row0 * a.K * (GU ? 2 : 4);
+        for (int c = 0; c < nchunk; ++c, ++it) {
+          const int s = it % kStages;
+          if (*abort_flag || !(ok = mbar_wait_bounded(&bars->empty[s], ((it / kStages) & 1) ^ 1, err))) { ok = false; break; }
+          uint8_t* st = stages + s * C::STAGE;
+          mbar_expect_tx(&bars->full[s], uint32_t(C::NMAT * kWBytes) + bbytes);
+          tma_load_2d(st, &tm0, c * (kChunk / 2), row, &bars->full[s], pol_w);
+          if (GU) tma_load_2d(st + kWBytes, &tm1, c * (kChunk / 2), row, &bars->full[s], pol_w);
+          bulk_g2s(st + C::NMAT * kWBytes, bsrc + (size_t)c * bbytes, bbytes, &bars->full[s], pol_b);
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        // let every copy already issued land before the CTA leaves
+        for (int k = 1; k <= kStages && it - k >= 0; ++k) {
+          const int j = it - k;
+          mbar_wait_bounded(&bars->full[j % kStages], (j / kStages) & 1, err, 1u << 20);
+        }
+        for (int k = 1; k <= 2 && lu - k >= 0; ++k) {
+          const int j = lu - k;
+          mbar_wait_bounded(&bars->sfull[j & 1], (j >> 1) & 1, err, 1u << 20);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int it = 0, lu = 0;
+      bool ok = true, issued = false;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lu) {
+        const Tile tl = a.tiles[u / RT];
+        const int d = lu & 1;
+        const uint32_t idesc = umma_idesc_bf16(128, tl.nt);
+        const uint32_t lbo = uint32_t(tl.nt / 8) * 128u;
+        if (!(ok = mbar_wait_bounded(&bars->accempty[d], ((lu >> 1) & 1) ^ 1, err))) break;
+        tc_fence_after();
+        const uint32_t dacc = tmem + uint32_t(d * C::ACC_STRIDE);
+        for (int c = 0; c < nchunk; ++c, ++it) {
+          const int s = it % kStages, ap = it % C::NA;
+          if (*abort_flag || !mbar_wait_bounded(&bars->full[s], (it / kStages) & 1, err) ||
+              !mbar_wait_bounded(&bars->afull[ap], (it / C::NA) & 1, err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sB = smem_u32(stages + s * C::STAGE + C::NMAT * kWBytes);
+          const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS);
+#pragma unroll
+          for (int ks = 0; ks < kChunk / 16; ++ks) {
+            const uint32_t acc = (c | ks) != 0;
+            const uint64_t bd = umma_desc(sB + uint32_t(ks) * 2u * lbo, lbo, 128u);
+            if (GU) {
+              umma_bf16_ts(dacc, aA + ks * 8, bd, idesc, acc);
+              umma_bf16_ts(dacc + 64, aA + 64 + ks * 8, bd, idesc, acc);
+            } else {
+              const uint64_t bl = umma_desc(sB + uint32_t(tl.nt) * 256u + uint32_t(ks) * 2u * lbo, lbo, 128u);
+              umma_bf16_ts(dacc, aA + ks * 8, bd, idesc, acc);
+              umma_bf16_ts(dacc, aA + ks * 8, bl, idesc, 1u);
+            }
+          }
+          issued = true;
+          umma_commit(&bars->empty[s]);
+          umma_commit(&bars->aempty[ap]);
+          if (c == nchunk - 1) umma_commit(&bars->accfull[d]);
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      if (issued) {  // every MMA issued has completed before TMEM is released
+        umma_commit(&bars->drain);
+        mbar_wait_bounded(&bars->drain, 0, err);
+      }
+    }
+  } else if (warp >= 4 && warp < 12) {
+    // ----------------------------------------------------------------- dequantizers
+    const int dw = warp - 4, q = dw & 3, part = dw >> 2;  // part: matrix (gate/up) or K half (down)
+    const int r = q * 32 + lane;
+    const int sw = (r >> 1) & 3;
+    const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
+    int it = 0, lu = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++lu) {
+      const int sb = lu & 1;
+      if (*abort_flag || !mbar_wait_bounded(&bars->sfull[sb], (lu >> 1) & 1, err)) { *abort_flag = 1; break; }
+      const uint8_t* srow = sbufs + sb * C::SCALE_BUF + (GU ? part * int(sbytes) : 0) + r * a.KS;
+      bool ok = true;
+      for (int c = 0; c < nchunk; ++c, ++it) {
+        const int s = it % kStages, ap = it % C::NA;
+        if (*abort_flag || !mbar_wait_bounded(&bars->full[s], (it / kStages) & 1, err)) { ok = false; break; }
+        const uint8_t* wt = stages + s * C::STAGE + (GU ? part * kWBytes : 0) + r * 64;
+        constexpr int NCH = GU ? 4 : 2;  // 32-element chunks handled by this thread per stage
+        const int ch0 = GU ? 0 : 2 * part;
+        uint4 wv[NCH];
+#pragma unroll
+        for (int j = 0; j < NCH; ++j)
+          wv[j] = *reinterpret_cast<const uint4*>(wt + 16 * ((ch0 + j) ^ sw));
+        uint32_t sc0, sc1;  // scale bytes of this stage
+        if (a.fmt == 0) {
+          sc0 = *reinterpret_cast<const uint32_t*>(srow + 4 * c);
+          sc1 = 0;
+        } else {
+          const uint2 t2 = *reinterpret_cast<const uint2*>(srow + 8 * c);
+          sc0 = t2.x;
+          sc1 = t2.y;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bars->empty[s]);
+          if (c == nchunk - 1) mbar_arrive(&bars->sempty[sb]);
+        }
+        if (!mbar_wait_bounded(&bars->aempty[ap], ((it / C::NA) & 1) ^ 1, err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t acol = uint32_t(C::A_BASE + ap * C::ACOLS + (GU ? part * 64 : part * 32));
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) {
+          const int ch = ch0 + j;
+          uint32_t out[16];
+          if (a.fmt == 0) {
+            const Mult mu = mult_e8m0((sc0 >> (8 * ch)) & 0xFFu);
+            fp4_word(wv[j].x, mu, out);
+            fp4_word(wv[j].y, mu, out + 4);
+            fp4_word(wv[j].z, mu, out + 8);
+            fp4_word(wv[j].w, mu, out + 12);
+          } else {
+            const uint32_t sw2 = ch < 2 ? sc0 : sc1;
+            const Mult m0 = mult_e4m3((sw2 >> (16 * (ch & 1))) & 0xFFu);
+            const Mult m1 = mult_e4m3((sw2 >> (16 * (ch & 1) + 8)) & 0xFFu);
+            fp4_word(wv[j].x, m0, out);
+            fp4_word(wv[j].y, m0, out + 4);
+            fp4_word(wv[j].z, m1, out + 8);
+            fp4_word(wv[j].w, m1, out + 12);
+          }
+          tmem_st16(lane_base + acol + uint32_t(j * 16), out);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->afull[ap]);
+      }
+      if (!ok) { *abort_flag = 1; break; }
+    }
+  } else if (warp >= 12) {
+    // ----------------------------------------------------------------- epilogue
+    const int q = warp & 3, r = q * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
+    int lu = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++lu) {
+      const Tile tl = a.tiles[u / RT];
+      const int rt = u % RT;
+      const int d = lu & 1;
+      if (*abort_flag || !mbar_wait_bounded(&bars->accfull[d], (lu >> 1) & 1, err)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const uint32_t dacc = lane_base + uint32_t(d * C::ACC_STRIDE);
+      if (GU) {
+        // this row is k = rt*128 + r of the down GEMM: chunk rt, permuted position p
+        const int p = (r & ~7) | perm8(r & 7);
+        const int nt8 = tl.nt >> 3;
+        uint8_t* hb = a.himg + (size_t)tl.row0 * a.h_rows * 4 + (size_t)rt * tl.nt * 512;
+        for (int cg = 0; cg < tl.nt / 16; ++cg) {
+          uint32_t g[16], v[16];
+          tmem_ld16(dacc + uint32_t(cg * 16), g);
+          tmem_ld16(dacc + 64u + uint32_t(cg * 16), v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = cg * 16 + i;
+            float hv = 0.0f;
+            if (n < tl.ntok) {
+              const float gv = fminf(__uint_as_float(g[i]), a.limit);
+              const float uv = fmaxf(fminf(__uint_as_float(v[i]), a.limit), -a.limit);
+              hv = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, q_expf(-gv))), uv);
+            }
+            const uint16_t hi = f2bf(hv);
+            const uint16_t lo = f2bf(__fsub_rn(hv, bf2f(hi)));
+            const int off = ((p >> 3) * nt8 + (n >> 3)) * 128 + (n & 7) * 16 + (p & 7) * 2;
+            *reinterpret_cast<uint16_t*>(hb + off) = hi;
+            *reinterpret_cast<uint16_t*>(hb + tl.nt * 256 + off) = lo;
+          }
+        }
+      } else {
+        float* yrow = a.yp + (size_t)tl.entry0 * a.R + rt * kRows + r;
+        for (int cg = 0; cg < tl.nt / 16; ++cg) {
+          uint32_t v[16];
+          tmem_ld16(dacc + uint32_t(cg * 16), v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = cg * 16 + i;
+            if (n < tl.ntok) yrow[(size_t)n * a.R] = __uint_as_float(v[i]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->accempty[d]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// --------------------------------------------------------------------------- combine
+__global__ void moe_combine_kernel(const float* __restrict__ yp, const int32_t* __restrict__ entry_pos,
+                                   const float* __restrict__ scores, int S, int H, uint16_t* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  for (int n = threadIdx.x * 4; n < H; n += blockDim.x * 4) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int j = 0; j < S; ++j) {
+      const int pos = entry_pos[(size_t)t * S + j];
+      if (pos < 0) continue;
+      const float w = scores[(size_t)t * S + j];
+      const float4 v = *reinterpret_cast<const float4*>(yp + (size_t)pos * H + n);
+      acc[0] = __fmaf_rn(w, v.x, acc[0]);
+      acc[1] = __fmaf_rn(w, v.y, acc[1]);
+      acc[2] = __fmaf_rn(w, v.z, acc[2]);
+      acc[3] = __fmaf_rn(w, v.w, acc[3]);
+    }
+    uint2 o;
+    o.x = uint32_t(f2bf(acc[0])) | (uint32_t(f2bf(acc[1])) << 16);
+    o.y = uint32_t(f2bf(acc[2])) | (uint32_t(f2bf(acc[3])) << 16);
+    *reinterpret_cast<uint2*>(y + (size_t)t * H + n) = o;
+  }
+}
+
+// --------------------------------------------------------------------------- host side
+struct Workspace {
+  size_t entry_pos, sorted_tok, rank_tmp, tiles, counters, ximg, himg, yp, total;
+  int max_tiles, max_rows;
+};
+inline size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
+inline Workspace layout(int T, int S, int E, int H, int I) {
+  Workspace w;
+  const size_t n = size_t(T) * S;
+  w.max_tiles = int(E + (n + kMaxTok - 1) / kMaxTok);
+  w.max_rows = int(n + 15 * size_t(w.max_tiles));
+  size_t o = 0;
+  w.entry_pos = o; o = up256(o + n * 4);
+  w.sorted_tok = o; o = up256(o + n * 4);
+  w.rank_tmp = o; o = up256(o + n * 4);
+  w.tiles = o; o = up256(o + size_t(w.max_tiles) * sizeof(Tile));
+  w.counters = o; o = up256(o + 16);
+  w.ximg = o; o = up256(o + size_t(w.max_rows) * H * 2);
+  w.himg = o; o = up256(o + size_t(w.max_rows) * I * 4);
+  w.yp = o; o = up256(o + n * H * 4);
+  w.total = o;
+  return w;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+// Packed weights [rows, K/2 bytes] as a uint8 2-D tensor; box = 64 bytes (128 k) x 128 rows, 64-B swizzle.
+bool weight_map(CUtensorMap* m, const void* base, long long rows, int K) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cuuint64_t(K / 2), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(K / 2)};
+  cuuint32_t box[2] = {uint32_t(kChunk / 2), uint32_t(kRows)};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool GU>
+cudaError_t launch_gemm(const CUtensorMap& m0, const CUtensorMap& m1, const GemmArgs& a, int grid,
+                        cudaStream_t st) {
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute(moe_gemm_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<GU>::SMEM);
+  });
+  if (attr != cudaSuccess) return attr;
+  return launch_kernel(moe_gemm_kernel<GU>, dim3(grid), dim3(kThreads), Cfg<GU>::SMEM, st, m0, m1, a);
+}
+
+}  // namespace moe
+}  // namespace qmtp
+
+using namespace qmtp;
+using namespace qmtp::moe;
+
+extern "C" int qmtp_quantize_fp4(int fmt, const void* w, long long N, int K, void* wq, void* scales, void* stream) {
+  if (fmt != 0 && fmt != 1) return QMTP_ERR_ARG;
+  const int G = fmt == 0 ? 32 : 16;
+  if (!w || !wq || !scales) return QMTP_ERR_ARG;
+  if (N <= 0 || K <= 0 || K % G) return QMTP_ERR_SHAPE;
+  const long long groups = N * (K / G);
+  QMTP_CUDA_TRY(launch_kernel(quantize_fp4_kernel, dim3(unsigned((groups + 255) / 256)), dim3(256), 0,
+                              static_cast<cudaStream_t>(stream), fmt, static_cast<const uint16_t*>(w), N, K,
+                              static_cast<uint32_t*>(wq), static_cast<uint8_t*>(scales)));
+  return QMTP_OK;
+}
+
+extern "C" int qmtp_moe_route(const void* logits, int T, int E, int top_k, int n_shared, float routed_scale, void* idx,
+                              void* scores, void* stream) {
+  if (!logits || !idx || !scores) return QMTP_ERR_ARG;
+  if (T <= 0 || E <= 0 || E > 1024 || top_k <= 0 || top_k > E || n_shared < 0 || top_k + n_shared > 16)
+    return QMTP_ERR_SHAPE;
+  QMTP_CUDA_TRY(launch_kernel(moe_route_kernel, dim3(unsigned((T + 7) / 8)), dim3(256), 0,
+                              static_cast<cudaStream_t>(stream), static_cast<const float*>(logits), T, E, top_k,
+                              n_shared, routed_scale, static_cast<int32_t*>(idx), static_cast<float*>(scores)));
+  return QMTP_OK;
+}
+
+extern "C" size_t qmtp_moe_workspace(int T, int S, int E, int H, int I) {
+  if (T <= 0 || S <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
+  return layout(T, S, E, H, I).total;
+}
+
+extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_, const void* wu, const void* su_,
+                        const void* wd, const void* sd_, const void* idx_, const void* scores_, void* y_, int T, int S,
+                        int E, int H, int I, float limit, void* workspace, size_t ws_bytes, void* stream_) {
+  if (fmt != 0 && fmt != 1) return QMTP_ERR_ARG;
+  if (!x_ || !wg || !sg_ || !wu || !su_ || !wd || !sd_ || !idx_ || !scores_ || !y_ || !workspace) return QMTP_ERR_ARG;
+  if (T <= 0 || S <= 0 || E <= 0 || E > 1024 || (long long)T * S > 65535) return QMTP_ERR_SHAPE;
+  if (H <= 0 || I <= 0 || H % kRows || I % kRows) return QMTP_ERR_SHAPE;
+  const int G = fmt == 0 ? 32 : 16;
+  const int KS_gu = H / G, KS_dn = I / G;
+  if (2 * kRows * KS_gu > Cfg<true>::SCALE_BUF || kRows * KS_dn > Cfg<false>::SCALE_BUF) return QMTP_ERR_UNSUPPORTED;
+  if (!aligned16(x_) || !aligned16(wg) || !aligned16(wu) || !aligned16(wd) || !aligned16(sg_) || !aligned16(su_) ||
+      !aligned16(sd_) || !aligned16(y_) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return QMTP_ERR_ALIGN;
+  const Workspace L = layout(T, S, E, H, I);
+  if (ws_bytes < L.total) return QMTP_ERR_SHAPE;
+  const auto* x = static_cast<const uint16_t*>(x_);
+  const auto* sg = static_cast<const uint8_t*>(sg_);
+  const auto* su = static_cast<const uint8_t*>(su_);
+  const auto* sd = static_cast<const uint8_t*>(sd_);
+  const auto* idx = static_cast<const int32_t*>(idx_);
+  const auto* scores = static_cast<const float*>(scores_);
+  auto* y = static_cast<uint16_t*>(y_);
+  auto stream = static_cast<cudaStream_t>(stream_);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  auto* entry_pos = reinterpret_cast<int32_t*>(ws + L.entry_pos);
+  auto* sorted_tok = reinterpret_cast<int32_t*>(ws + L.sorted_tok);
+  auto* rank_tmp = reinterpret_cast<int32_t*>(ws + L.rank_tmp);
+  auto* tiles = reinterpret_cast<Tile*>(ws + L.tiles);
+  auto* counters = reinterpret_cast<int32_t*>(ws + L.counters);
+  uint8_t* ximg = ws + L.ximg;
+  uint8_t* himg = ws + L.himg;
+  auto* yp = reinterpret_cast<float*>(ws + L.yp);
+
+  CUtensorMap mg, mu, md;
+  if (!weight_map(&mg, wg, (long long)E * I, H) || !weight_map(&mu, wu, (long long)E * I, H) ||
+      !weight_map(&md, wd, (long long)E * H, I))
+    return QMTP_ERR_CUDA;
+
+  const int n = T * S;
+  static std::once_flag once;
+  static cudaError_t gattr = cudaSuccess;
+  std::call_once(once, [] {
+    gattr = cudaFuncSetAttribute(moe_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 32 * 1024 * 2);
+  });
+  QMTP_CUDA_TRY(gattr);
+  unsigned* err = device_error_ptr();
+  QMTP_CUDA_TRY(launch_kernel(moe_group_kernel, dim3(1), dim3(1024), size_t(32) * E * 2, stream, idx, n, S, E,
+                              entry_pos, sorted_tok, rank_tmp, tiles, counters, err));
+  QMTP_CUDA_TRY(launch_kernel(moe_gather_kernel, dim3(unsigned(L.max_tiles)), dim3(256), 0, stream, x, H,
+                              (const Tile*)tiles, (const int32_t*)counters, (const int32_t*)sorted_tok, ximg));
+  const int grid = sm_count();
+  GemmArgs gu{sg, su, ximg, tiles, counters, himg, nullptr, H, I, KS_gu, fmt, limit, I, err};
+  QMTP_CUDA_TRY(launch_gemm<true>(mg, mu, gu, grid, stream));
+  GemmArgs dn{sd, nullptr, himg, tiles, counters, nullptr, yp, I, H, KS_dn, fmt, limit, 0, err};
+  QMTP_CUDA_TRY(launch_gemm<false>(md, md, dn, grid, stream));
+  QMTP_CUDA_TRY(launch_kernel(moe_combine_kernel, dim3(unsigned(T)), dim3(256), 0, stream, (const float*)yp,
+                              (const int32_t*)entry_pos, scores, S, H, y));
+  return QMTP_OK;
+}

@@ -72,6 +72,9 @@ SIGNATURES.update({
     "qmtp_mtp_accept": [_P, _P, _I, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_mtp_advance": [_P, _P],
     "qmtp_next_tokens": [_P, _P, _I, _P, _P, _P],
+    "qmtp_quantize_fp4": [_I, _P, ctypes.c_longlong, _I, _P, _P, _P],
+    "qmtp_moe_route": [_P, _I, _I, _I, _I, _F, _P, _P, _P],
+    "qmtp_moe": [_I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, ctypes.c_size_t, _P],
 })
 
 # control block layout (include/qmtp.h QMTP_CTRL_*)
@@ -83,6 +86,7 @@ SIZE_QUERIES: dict[str, list] = {
     "qmtp_lmhead2_workspace": [_I, _I, _I],
     "qmtp_topk_workspace": [_I, _I, _I],
     "qmtp_argmax_workspace": [_I, _I],
+    "qmtp_moe_workspace": [_I, _I, _I, _I, _I],
 }
 
 _lib = None
