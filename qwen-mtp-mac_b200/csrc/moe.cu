@@ -46,6 +46,7 @@ constexpr int kStages = 4;
 constexpr int kWBytes = kRows * kChunk / 2;  // packed bytes of one 128 x 128 weight tile
 constexpr int kThreads = 512;
 constexpr unsigned kTmemCols = 512;
+constexpr uint32_t kWaitPolls = 1u << 20;  // bound of every mbarrier wait (normal waits end in microseconds)
 
 struct Tile {
   int expert, entry0, ntok, nt, row0, pad0, pad1, pad2;
@@ -451,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int rt = u % RT;
         const int row = tl.expert * a.R + rt * kRows;
         const int sb = lu & 1;
-        if (!(ok = mbar_wait_bounded(&bars->sempty[sb], ((lu >> 1) & 1) ^ 1, err))) break;
+        if (!(ok = mbar_wait_bounded(&bars->sempty[sb], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
         mbar_expect_tx(&bars->sfull[sb], sbytes * C::NMAT);
         bulk_g2s(sbufs + sb * C::SCALE_BUF, a.sa + (size_t)row * a.KS, sbytes, &bars->sfull[sb], pol_w);
         if (GU) bulk_g2s(sbufs + sb * C::SCALE_BUF + sbytes, a.sb + (size_t)row * a.KS, sbytes, &bars->sfull[sb], pol_w);
@@ -459,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* bsrc = a.bimg + (size_t)tl.row0 * a.K * (GU ? 2 : 4);
         for (int c = 0; c < nchunk; ++c, ++it) {
           const int s = it % kStages;
-          if (*abort_flag || !(ok = mbar_wait_bounded(&bars->empty[s], ((it / kStages) & 1) ^ 1, err))) { ok = false; break; }
+          if (*abort_flag || !(ok = mbar_wait_bounded(&bars->empty[s], ((it / kStages) & 1) ^ 1, err, kWaitPolls))) { ok = false; break; }
           uint8_t* st = stages + s * C::STAGE;
           mbar_expect_tx(&bars->full[s], uint32_t(C::NMAT * kWBytes) + bbytes);
           tma_load_2d(st, &tm0, c * (kChunk / 2), row, &bars->full[s], pol_w);
@@ -490,13 +491,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int d = lu & 1;
         const uint32_t idesc = umma_idesc_bf16(128, tl.nt);
         const uint32_t lbo = uint32_t(tl.nt / 8) * 128u;
-        if (!(ok = mbar_wait_bounded(&bars->accempty[d], ((lu >> 1) & 1) ^ 1, err))) break;
+        if (!(ok = mbar_wait_bounded(&bars->accempty[d], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
         tc_fence_after();
         const uint32_t dacc = tmem + uint32_t(d * C::ACC_STRIDE);
         for (int c = 0; c < nchunk; ++c, ++it) {
           const int s = it % kStages, ap = it % C::NA;
-          if (*abort_flag || !mbar_wait_bounded(&bars->full[s], (it / kStages) & 1, err) ||
-              !mbar_wait_bounded(&bars->afull[ap], (it / C::NA) & 1, err)) { ok = false; break; }
+          if (*abort_flag || !mbar_wait_bounded(&bars->full[s], (it / kStages) & 1, err, kWaitPolls) ||
+              !mbar_wait_bounded(&bars->afull[ap], (it / C::NA) & 1, err, kWaitPolls)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sB = smem_u32(stages + s * C::STAGE + C::NMAT * kWBytes);
           const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS);
@@ -522,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) *abort_flag = 1;
       if (issued) {  // every MMA issued has completed before TMEM is released
         umma_commit(&bars->drain);
-        mbar_wait_bounded(&bars->drain, 0, err);
+        mbar_wait_bounded(&bars->drain, 0, err, kWaitPolls);
       }
     }
   } else if (warp >= 4 && warp < 12) {
@@ -534,12 +535,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0, lu = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++lu) {
       const int sb = lu & 1;
-      if (*abort_flag || !mbar_wait_bounded(&bars->sfull[sb], (lu >> 1) & 1, err)) { *abort_flag = 1; break; }
+      if (*abort_flag || !mbar_wait_bounded(&bars->sfull[sb], (lu >> 1) & 1, err, kWaitPolls)) { *abort_flag = 1; break; }
       const uint8_t* srow = sbufs + sb * C::SCALE_BUF + (GU ? part * int(sbytes) : 0) + r * a.KS;
       bool ok = true;
       for (int c = 0; c < nchunk; ++c, ++it) {
         const int s = it % kStages, ap = it % C::NA;
-        if (*abort_flag || !mbar_wait_bounded(&bars->full[s], (it / kStages) & 1, err)) { ok = false; break; }
+        if (*abort_flag || !mbar_wait_bounded(&bars->full[s], (it / kStages) & 1, err, kWaitPolls)) { ok = false; break; }
         const uint8_t* wt = stages + s * C::STAGE + (GU ? part * kWBytes : 0) + r * 64;
         constexpr int NCH = GU ? 4 : 2;  // 32-element chunks handled by this thread per stage
         const int ch0 = GU ? 0 : 2 * part;
@@ -561,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&bars->empty[s]);
           if (c == nchunk - 1) mbar_arrive(&bars->sempty[sb]);
         }
-        if (!mbar_wait_bounded(&bars->aempty[ap], ((it / C::NA) & 1) ^ 1, err)) { ok = false; break; }
+        if (!mbar_wait_bounded(&bars->aempty[ap], ((it / C::NA) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
         tc_fence_after();
         const uint32_t acol = uint32_t(C::A_BASE + ap * C::ACOLS + (GU ? part * 64 : part * 32));
 #pragma unroll
@@ -601,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Tile tl = a.tiles[u / RT];
       const int rt = u % RT;
       const int d = lu & 1;
-      if (*abort_flag || !mbar_wait_bounded(&bars->accfull[d], (lu >> 1) & 1, err)) { *abort_flag = 1; break; }
+      if (*abort_flag || !mbar_wait_bounded(&bars->accfull[d], (lu >> 1) & 1, err, kWaitPolls)) { *abort_flag = 1; break; }
       tc_fence_after();
       const uint32_t dacc = lane_base + uint32_t(d * C::ACC_STRIDE);
       if (GU) {
@@ -821,7 +822,7 @@ extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_
   QMTP_CUDA_TRY(gattr);
   unsigned* err = device_error_ptr();
   QMTP_CUDA_TRY(launch_kernel(moe_group_kernel, dim3(1), dim3(1024), size_t(32) * E * 2, stream, idx, n, S, E,
-                              entry_pos, sorted_tok, rank_tmp, tiles, counters, err));
+                              entry_pos, sorted_tok, rank_tmp, tiles, counters, err, kWaitPolls));
   QMTP_CUDA_TRY(launch_kernel(moe_gather_kernel, dim3(unsigned(L.max_tiles)), dim3(256), 0, stream, x, H,
                               (const Tile*)tiles, (const int32_t*)counters, (const int32_t*)sorted_tok, ximg));
   const int grid = sm_count();
