@@ -233,7 +233,7 @@ size_t qmtp_moe_workspace(int T, int S, int E, int H, int I);
 
 /* y bf16 [T, H] = sum_j scores[t,j] * Wd[e] (silu(min(Wg[e] x_t, L)) * clamp(Wu[e] x_t, -L, L)),
  * e = idx[t, j] (kernels.py:35-107).  x bf16 [T, H]; wg, wu [E, I, H/8]; wd [E, H, I/8]; limit = +inf
- * disables the clamp.  H, I multiples of 128; T*S <= 65535; E <= 1024; scale rows of one 128-row
+ * disables the clamp.  H, I multiples of 128; S <= 16; T*S <= 65535; E <= 1024; scale rows of one 128-row
  * tile must fit the kernel's scale buffers (H <= 4096 MXFP4 / 2048 NVFP4).  All pointers 16-B
  * aligned, workspace 256-B aligned.  An expert id outside [0, E) raises the device error word and
  * its slot contributes nothing. */

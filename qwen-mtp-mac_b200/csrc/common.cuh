@@ -265,6 +265,28 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes or about `ns`
+// nanoseconds pass, so a waiting warp takes no issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// Bounded sleeping wait: at most `limit` polls of up to 1 us each; on timeout records DEVERR_TIMEOUT.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, unsigned* err,
+                                                uint32_t limit = (1u << 20)) {
+  for (uint32_t it = 0; it < limit; ++it)
+    if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
+  if (err) atomicOr(err, DEVERR_TIMEOUT);
+  return false;
+}
+
 // ----------------------------------------------------------------------------- loads
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 r;

@@ -349,7 +349,8 @@ __global__ void moe_gather_kernel(const uint16_t* __restrict__ x, int H, const T
   const int nt8 = tl.nt >> 3;
   const int units = tl.nt * (H >> 3);
   uint8_t* base = ximg + (size_t)tl.row0 * H * 2;
-  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+  const int step = blockDim.x * gridDim.y;
+  for (int u = blockIdx.y * blockDim.x + threadIdx.x; u < units; u += step) {
     const int r7 = u & 7;
     int v = u >> 3;
     const int rg = v % nt8;
@@ -452,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int rt = u % RT;
         const int row = tl.expert * a.R + rt * kRows;
         const int sb = lu & 1;
-        if (!(ok = mbar_wait_bounded(&bars->sempty[sb], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
+        if (!(ok = mbar_wait_sleep(&bars->sempty[sb], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
         mbar_expect_tx(&bars->sfull[sb], sbytes * C::NMAT);
         bulk_g2s(sbufs + sb * C::SCALE_BUF, a.sa + (size_t)row * a.KS, sbytes, &bars->sfull[sb], pol_w);
         if (GU) bulk_g2s(sbufs + sb * C::SCALE_BUF + sbytes, a.sb + (size_t)row * a.KS, sbytes, &bars->sfull[sb], pol_w);
@@ -460,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* bsrc = a.bimg + (size_t)tl.row0 * a.K * (GU ? 2 : 4);
         for (int c = 0; c < nchunk; ++c, ++it) {
           const int s = it % kStages;
-          if (*abort_flag || !(ok = mbar_wait_bounded(&bars->empty[s], ((it / kStages) & 1) ^ 1, err, kWaitPolls))) { ok = false; break; }
+          if (*abort_flag || !(ok = mbar_wait_sleep(&bars->empty[s], ((it / kStages) & 1) ^ 1, err, kWaitPolls))) { ok = false; break; }
           uint8_t* st = stages + s * C::STAGE;
           mbar_expect_tx(&bars->full[s], uint32_t(C::NMAT * kWBytes) + bbytes);
           tma_load_2d(st, &tm0, c * (kChunk / 2), row, &bars->full[s], pol_w);
@@ -473,11 +474,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // let every copy already issued land before the CTA leaves
         for (int k = 1; k <= kStages && it - k >= 0; ++k) {
           const int j = it - k;
-          mbar_wait_bounded(&bars->full[j % kStages], (j / kStages) & 1, err, 1u << 20);
+          mbar_wait_sleep(&bars->full[j % kStages], (j / kStages) & 1, err, 1u << 20);
         }
         for (int k = 1; k <= 2 && lu - k >= 0; ++k) {
           const int j = lu - k;
-          mbar_wait_bounded(&bars->sfull[j & 1], (j >> 1) & 1, err, 1u << 20);
+          mbar_wait_sleep(&bars->sfull[j & 1], (j >> 1) & 1, err, 1u << 20);
         }
       }
     }
@@ -491,13 +492,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int d = lu & 1;
         const uint32_t idesc = umma_idesc_bf16(128, tl.nt);
         const uint32_t lbo = uint32_t(tl.nt / 8) * 128u;
-        if (!(ok = mbar_wait_bounded(&bars->accempty[d], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
+        if (!(ok = mbar_wait_sleep(&bars->accempty[d], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
         tc_fence_after();
         const uint32_t dacc = tmem + uint32_t(d * C::ACC_STRIDE);
         for (int c = 0; c < nchunk; ++c, ++it) {
           const int s = it % kStages, ap = it % C::NA;
-          if (*abort_flag || !mbar_wait_bounded(&bars->full[s], (it / kStages) & 1, err, kWaitPolls) ||
-              !mbar_wait_bounded(&bars->afull[ap], (it / C::NA) & 1, err, kWaitPolls)) { ok = false; break; }
+          if (*abort_flag || !mbar_wait_sleep(&bars->full[s], (it / kStages) & 1, err, kWaitPolls) ||
+              !mbar_wait_sleep(&bars->afull[ap], (it / C::NA) & 1, err, kWaitPolls)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sB = smem_u32(stages + s * C::STAGE + C::NMAT * kWBytes);
           const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS);
@@ -523,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) *abort_flag = 1;
       if (issued) {  // every MMA issued has completed before TMEM is released
         umma_commit(&bars->drain);
-        mbar_wait_bounded(&bars->drain, 0, err, kWaitPolls);
+        mbar_wait_sleep(&bars->drain, 0, err, kWaitPolls);
       }
     }
   } else if (warp >= 4 && warp < 12) {
@@ -535,12 +536,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0, lu = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++lu) {
       const int sb = lu & 1;
-      if (*abort_flag || !mbar_wait_bounded(&bars->sfull[sb], (lu >> 1) & 1, err, kWaitPolls)) { *abort_flag = 1; break; }
+      if (*abort_flag || !mbar_wait_sleep(&bars->sfull[sb], (lu >> 1) & 1, err, kWaitPolls)) { *abort_flag = 1; break; }
       const uint8_t* srow = sbufs + sb * C::SCALE_BUF + (GU ? part * int(sbytes) : 0) + r * a.KS;
       bool ok = true;
       for (int c = 0; c < nchunk; ++c, ++it) {
         const int s = it % kStages, ap = it % C::NA;
-        if (*abort_flag || !mbar_wait_bounded(&bars->full[s], (it / kStages) & 1, err, kWaitPolls)) { ok = false; break; }
+        if (*abort_flag || !mbar_wait_sleep(&bars->full[s], (it / kStages) & 1, err, kWaitPolls)) { ok = false; break; }
         const uint8_t* wt = stages + s * C::STAGE + (GU ? part * kWBytes : 0) + r * 64;
         constexpr int NCH = GU ? 4 : 2;  // 32-element chunks handled by this thread per stage
         const int ch0 = GU ? 0 : 2 * part;
@@ -562,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&bars->empty[s]);
           if (c == nchunk - 1) mbar_arrive(&bars->sempty[sb]);
         }
-        if (!mbar_wait_bounded(&bars->aempty[ap], ((it / C::NA) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
+        if (!mbar_wait_sleep(&bars->aempty[ap], ((it / C::NA) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
         tc_fence_after();
         const uint32_t acol = uint32_t(C::A_BASE + ap * C::ACOLS + (GU ? part * 64 : part * 32));
 #pragma unroll
@@ -602,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Tile tl = a.tiles[u / RT];
       const int rt = u % RT;
       const int d = lu & 1;
-      if (*abort_flag || !mbar_wait_bounded(&bars->accfull[d], (lu >> 1) & 1, err, kWaitPolls)) { *abort_flag = 1; break; }
+      if (*abort_flag || !mbar_wait_sleep(&bars->accfull[d], (lu >> 1) & 1, err, kWaitPolls)) { *abort_flag = 1; break; }
       tc_fence_after();
       const uint32_t dacc = lane_base + uint32_t(d * C::ACC_STRIDE);
       if (GU) {
@@ -661,17 +662,26 @@ __global__ void moe_combine_kernel(const float* __restrict__ yp, const int32_t* 
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
-  for (int n = threadIdx.x * 4; n < H; n += blockDim.x * 4) {
+  int pos[16];
+  float w[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    pos[j] = j < S ? entry_pos[(size_t)t * S + j] : -1;
+    w[j] = j < S ? scores[(size_t)t * S + j] : 0.0f;
+  }
+  for (int n = (blockIdx.y * blockDim.x + threadIdx.x) * 4; n < H; n += blockDim.x * gridDim.y * 4) {
+    float4 v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      v[j] = pos[j] >= 0 ? *reinterpret_cast<const float4*>(yp + (size_t)pos[j] * H + n) : make_float4(0.f, 0.f, 0.f, 0.f);
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int j = 0; j < S; ++j) {
-      const int pos = entry_pos[(size_t)t * S + j];
-      if (pos < 0) continue;
-      const float w = scores[(size_t)t * S + j];
-      const float4 v = *reinterpret_cast<const float4*>(yp + (size_t)pos * H + n);
-      acc[0] = __fmaf_rn(w, v.x, acc[0]);
-      acc[1] = __fmaf_rn(w, v.y, acc[1]);
-      acc[2] = __fmaf_rn(w, v.z, acc[2]);
-      acc[3] = __fmaf_rn(w, v.w, acc[3]);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (pos[j] < 0) continue;
+      acc[0] = __fmaf_rn(w[j], v[j].x, acc[0]);
+      acc[1] = __fmaf_rn(w[j], v[j].y, acc[1]);
+      acc[2] = __fmaf_rn(w[j], v[j].z, acc[2]);
+      acc[3] = __fmaf_rn(w[j], v[j].w, acc[3]);
     }
     uint2 o;
     o.x = uint32_t(f2bf(acc[0])) | (uint32_t(f2bf(acc[1])) << 16);
@@ -780,7 +790,7 @@ extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_
                         int E, int H, int I, float limit, void* workspace, size_t ws_bytes, void* stream_) {
   if (fmt != 0 && fmt != 1) return QMTP_ERR_ARG;
   if (!x_ || !wg || !sg_ || !wu || !su_ || !wd || !sd_ || !idx_ || !scores_ || !y_ || !workspace) return QMTP_ERR_ARG;
-  if (T <= 0 || S <= 0 || E <= 0 || E > 1024 || (long long)T * S > 65535) return QMTP_ERR_SHAPE;
+  if (T <= 0 || S <= 0 || S > 16 || E <= 0 || E > 1024 || (long long)T * S > 65535) return QMTP_ERR_SHAPE;
   if (H <= 0 || I <= 0 || H % kRows || I % kRows) return QMTP_ERR_SHAPE;
   const int G = fmt == 0 ? 32 : 16;
   const int KS_gu = H / G, KS_dn = I / G;
@@ -822,15 +832,15 @@ extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_
   QMTP_CUDA_TRY(gattr);
   unsigned* err = device_error_ptr();
   QMTP_CUDA_TRY(launch_kernel(moe_group_kernel, dim3(1), dim3(1024), size_t(32) * E * 2, stream, idx, n, S, E,
-                              entry_pos, sorted_tok, rank_tmp, tiles, counters, err, kWaitPolls));
-  QMTP_CUDA_TRY(launch_kernel(moe_gather_kernel, dim3(unsigned(L.max_tiles)), dim3(256), 0, stream, x, H,
+                              entry_pos, sorted_tok, rank_tmp, tiles, counters, err));
+  QMTP_CUDA_TRY(launch_kernel(moe_gather_kernel, dim3(unsigned(L.max_tiles), 8), dim3(256), 0, stream, x, H,
                               (const Tile*)tiles, (const int32_t*)counters, (const int32_t*)sorted_tok, ximg));
   const int grid = sm_count();
   GemmArgs gu{sg, su, ximg, tiles, counters, himg, nullptr, H, I, KS_gu, fmt, limit, I, err};
   QMTP_CUDA_TRY(launch_gemm<true>(mg, mu, gu, grid, stream));
   GemmArgs dn{sd, nullptr, himg, tiles, counters, nullptr, yp, I, H, KS_dn, fmt, limit, 0, err};
   QMTP_CUDA_TRY(launch_gemm<false>(md, md, dn, grid, stream));
-  QMTP_CUDA_TRY(launch_kernel(moe_combine_kernel, dim3(unsigned(T)), dim3(256), 0, stream, (const float*)yp,
+  QMTP_CUDA_TRY(launch_kernel(moe_combine_kernel, dim3(unsigned(T), unsigned((H + 1023) / 1024)), dim3(256), 0, stream, (const float*)yp,
                               (const int32_t*)entry_pos, scores, S, H, y));
   return QMTP_OK;
 }
