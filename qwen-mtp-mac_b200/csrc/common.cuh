@@ -311,6 +311,10 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t smem_addr, uint32_t lbo, 
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
+// Instruction descriptor, kind::f16 with f16 A/B, fp32 accumulator, both operands K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
+  return (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
 // Byte offset of element (r, k) in a [R x Kt] bf16 tile stored as SWIZZLE_NONE K-major core matrices,
 // core matrices ordered K-chunk-major: (k/8) * (R/8) + r/8.  Then lbo = (R/8)*128, sbo = 128.
 __host__ __device__ constexpr uint32_t cm_offset(int r, int k, int R) {

@@ -10,25 +10,29 @@
 // Pipeline (one stream, each kernel a programmatic dependent of the previous one):
 //   moe_group    one CTA: stable counting sort of the T*S (token, slot) entries by expert, cut into
 //                token tiles of <= 64 entries; writes the tile table.
-//   moe_gather   per tile: the tile's token rows of x as a bf16 operand image (canonical K-major
-//                core-matrix layout of the tensor core, 128 K per chunk) in HBM.
+//   moe_gather   per tile row: the token's x as an f16 operand image (canonical K-major core-matrix
+//                layout of the tensor core, 128 K per chunk), scaled by a per-token power of two.
 //   moe_gemm<GU> persistent, one CTA per SM; a unit = (tile, 128 weight rows).  Warp roles:
-//                  warp 0      TMA producer: weight tiles (2-D, 64-B swizzle), operand-image chunks
-//                              and the unit's scales (1-D bulk copies);
+//                  warp 0      TMA producer of the weight ring (2-D, 64-B swizzle) and the unit's scales;
+//                  warp 2      producer of the operand-image ring (1-D bulk copies);
 //                  warp 1      tcgen05.mma issuer (M = 128, N = tile tokens, K = 16 per instruction),
 //                              A operand read from TMEM, B operand from shared memory;
-//                  warps 4-11  dequantizers: packed e2m1 + scale -> exact bf16, tcgen05.st into TMEM;
-//                  warps 12-15 epilogue: accumulators -> SwiGLU h (gate/up) or fp32 partials (down).
+//                  warps 4-19  dequantizers: packed e2m1 + scale -> f16 (gate/up) or bf16 (down) in
+//                              registers, tcgen05.st into TMEM;
+//                  warps 20-23 epilogue: accumulators -> SwiGLU h (gate/up) or fp32 partials (down).
 //                gate/up writes h split as hi = bf16(h), lo = bf16(h - hi) (h to ~16 significant bits,
 //                the reference keeps h in fp32, kernels.py:146) straight into the down operand image;
 //                down multiplies the same weights by hi and lo and writes per-entry fp32 partials.
 //   moe_combine  y[t] = sum_j scores[t,j] * partial[t,j] in slot order, rounded to bf16.
 //
-// Dequantization is exact: e2m1 magnitudes are placed as bf16 subnormal-or-normal encodings of
-// v * 2^-126 (exponent low bits + top mantissa bit) and multiplied by the bf16 value 2^126 * scale
-// with one mul.rn.bf16x2 per element pair (two multiplies when that factor exceeds bf16 range).  The
-// eight nibbles of a word are laid out as element pairs (0,4), (1,5), (2,6), (3,7): the operand image
-// of the activations uses the same permutation of every 8 consecutive k, so the products are unchanged.
+// Dequantization.  gate/up uses f16 operands: each byte of a word goes through the hardware
+// e2m1x2 -> f16x2 conversion and one f16x2 multiply by the block factor (no integer bit work, which
+// keeps the dequantizers off the integer pipe).  NVFP4 factors (e4m3 * 2^-8) are always exact in f16;
+// MXFP4 factors are taken relative to the row's largest scale so they fit f16, and the epilogue
+// restores the row's power of two.  down uses bf16 operands (h needs bf16's range): e2m1 magnitudes
+// are placed as bf16 encodings of v * 2^-126 and multiplied by 2^126 * scale with one mul.rn.bf16x2
+// per element pair (two multiplies when that factor exceeds bf16 range); its nibbles are laid out as
+// pairs (0,4), (1,5), (2,6), (3,7), and the h operand image uses the same permutation of every 8 k.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -39,14 +43,19 @@
 namespace qmtp {
 namespace moe {
 
-constexpr int kRows = 128;              // weight rows per unit (MMA M)
-constexpr int kChunk = 128;             // K per pipeline stage
-constexpr int kMaxTok = 64;             // entries per token tile (MMA N <= 64)
-constexpr int kStages = 4;
+constexpr int kRows = 128;                   // weight rows per unit (MMA M)
+constexpr int kChunk = 128;                  // K per pipeline stage
+constexpr int kMaxTok = 64;                  // entries per token tile (MMA N <= 64)
 constexpr int kWBytes = kRows * kChunk / 2;  // packed bytes of one 128 x 128 weight tile
-constexpr int kThreads = 512;
+constexpr int kMaxW = 8;                     // weight ring stages (upper bound; chosen per launch)
+constexpr int kNB = 3;                       // operand-image ring stages
+constexpr int kDQ = 4;                       // dequantizing warps per TMEM lane quarter
+constexpr int kNDQ = 4 * kDQ;
+constexpr int kWarps = 4 + kNDQ + 4;         // 4 control warps, dequantizers, 4 epilogue warps
+constexpr int kThreads = kWarps * 32;
 constexpr unsigned kTmemCols = 512;
-constexpr uint32_t kWaitPolls = 1u << 20;  // bound of every mbarrier wait (normal waits end in microseconds)
+constexpr uint32_t kWaitPolls = 1u << 20;    // bound of every mbarrier wait (normal waits end in microseconds)
+constexpr int kSmemMax = 227 * 1024;
 
 struct Tile {
   int expert, entry0, ntok, nt, row0, pad0, pad1, pad2;
@@ -55,16 +64,35 @@ struct Tile {
 template <bool GU>
 struct Cfg {
   static constexpr int NMAT = GU ? 2 : 1;
+  static constexpr int WSTAGE = NMAT * kWBytes;
   static constexpr int BSTAGE = GU ? kMaxTok * 256 : kMaxTok * 512;  // operand-image bytes per stage
-  static constexpr int STAGE = NMAT * kWBytes + BSTAGE;
-  static constexpr int SCALE_BUF = GU ? 32768 : 16384;
-  static constexpr int NA = GU ? 2 : 4;           // TMEM A stages
-  static constexpr int ACOLS = GU ? 128 : 64;     // TMEM columns of one A stage (all matrices)
+  static constexpr int NA = GU ? 2 : 4;            // TMEM A stages
+  static constexpr int ACOLS = GU ? 128 : 64;      // TMEM columns of one A stage (all matrices)
   static constexpr int ACC_STRIDE = GU ? 128 : 64;
-  static constexpr int A_BASE = 2 * ACC_STRIDE;   // accumulators double-buffered below the A stages
-  static constexpr int SMEM = kStages * STAGE + 2 * SCALE_BUF + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int A_BASE = 2 * ACC_STRIDE;    // accumulators double-buffered below the A stages
   static_assert(A_BASE + NA * ACOLS <= (int)kTmemCols, "TMEM budget");
 };
+
+// Shared-memory map of one GEMM CTA (host and device compute it the same way).
+struct SmemMap {
+  int w, b, s, rs, bars, total;
+};
+__host__ __device__ inline SmemMap smem_map(bool gu, int nw, int sbuf) {
+  SmemMap m;
+  int o = 0;
+  m.w = o;
+  o += nw * (gu ? 2 * kWBytes : kWBytes);
+  m.b = o;
+  o += kNB * (gu ? kMaxTok * 256 : kMaxTok * 512);
+  m.s = o;
+  o += 2 * sbuf;
+  m.rs = o;
+  o += 2 * 2 * kRows * 4;  // row exponents [unit parity][matrix][row]
+  m.bars = o;
+  o += 512;
+  m.total = o + 1024;  // alignment slack
+  return m;
+}
 
 // --------------------------------------------------------------------------- exact fp4 -> bf16
 // Scale byte -> bf16x2 multipliers.  Fast path: mult = 2^126 * scale fits bf16.  Slow path (rare):
@@ -77,7 +105,7 @@ __device__ __forceinline__ Mult mult_e8m0(uint32_t s) {
   Mult r;
   r.slow = s > 128u;
   r.m = ((s + 126u) << 7) * 0x00010001u;
-  r.m2 = (s << 7) * 0x00010001u;
+  r.m2 = (s == 0 ? 0x0040u : s << 7) * 0x00010001u;  // 2^(s-127); s = 0 is the bf16 subnormal 2^-127
   return r;
 }
 __device__ __forceinline__ Mult mult_e4m3(uint32_t s) {
@@ -89,26 +117,51 @@ __device__ __forceinline__ Mult mult_e4m3(uint32_t s) {
   r.m2 = (__float_as_uint(f) >> 16) * 0x00010001u;
   return r;
 }
-// One word (8 nibbles) -> 4 bf16x2: pairs (0,4), (1,5), (2,6), (3,7).
-__device__ __forceinline__ void fp4_word(uint32_t w, const Mult& mu, uint32_t* r) {
+// One word (8 nibbles) -> 4 bf16x2: pairs (0,4), (1,5), (2,6), (3,7).  `fast`: one multiply by
+// 2^126 * scale; `wide`: multiply by 2^126 first, then by the scale (every scale byte).
+__device__ __forceinline__ void fp4_word_mags(uint32_t w, uint32_t (&m)[4]) {
   const uint32_t y = w >> 8;
-  const uint32_t m0 = ((w & 0x000F000Fu) * 0x1040u) & 0x81C081C0u;
-  const uint32_t m1 = ((w & 0x00F000F0u) * 0x0104u) & 0x81C081C0u;
-  const uint32_t m2 = ((y & 0x000F000Fu) * 0x1040u) & 0x81C081C0u;
-  const uint32_t m3 = ((y & 0x00F000F0u) * 0x0104u) & 0x81C081C0u;
-  if (!mu.slow) {
-    r[0] = mul_bf16x2(m0, mu.m);
-    r[1] = mul_bf16x2(m1, mu.m);
-    r[2] = mul_bf16x2(m2, mu.m);
-    r[3] = mul_bf16x2(m3, mu.m);
-  } else {
-    const uint32_t p126 = 0x7E807E80u;
-    r[0] = mul_bf16x2(mul_bf16x2(m0, p126), mu.m2);
-    r[1] = mul_bf16x2(mul_bf16x2(m1, p126), mu.m2);
-    r[2] = mul_bf16x2(mul_bf16x2(m2, p126), mu.m2);
-    r[3] = mul_bf16x2(mul_bf16x2(m3, p126), mu.m2);
-  }
+  m[0] = ((w & 0x000F000Fu) * 0x1040u) & 0x81C081C0u;
+  m[1] = ((w & 0x00F000F0u) * 0x0104u) & 0x81C081C0u;
+  m[2] = ((y & 0x000F000Fu) * 0x1040u) & 0x81C081C0u;
+  m[3] = ((y & 0x00F000F0u) * 0x0104u) & 0x81C081C0u;
 }
+__device__ __forceinline__ void fp4_word_fast(uint32_t w, uint32_t mult, uint32_t* r) {
+  uint32_t m[4];
+  fp4_word_mags(w, m);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) r[i] = mul_bf16x2(m[i], mult);
+}
+__device__ __forceinline__ void fp4_word_wide(uint32_t w, uint32_t scale, uint32_t* r) {
+  uint32_t m[4];
+  fp4_word_mags(w, m);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) r[i] = mul_bf16x2(mul_bf16x2(m[i], 0x7E807E80u), scale);
+}
+// f16 path (gate/up): hardware e2m1x2 -> f16x2 conversion of each byte (element pair (2b, 2b+1), low
+// nibble in the low half), then one f16x2 multiply by the scale factor.  Natural k order.
+__device__ __forceinline__ void fp4_word_f16(uint32_t w, uint32_t mult, uint32_t* r) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t.reg .b32 t0, t1, t2, t3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 t0, b0;\n\tcvt.rn.f16x2.e2m1x2 t1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 t2, b2;\n\tcvt.rn.f16x2.e2m1x2 t3, b3;\n\t"
+      "mul.rn.f16x2 %0, t0, %5;\n\tmul.rn.f16x2 %1, t1, %5;\n\t"
+      "mul.rn.f16x2 %2, t2, %5;\n\tmul.rn.f16x2 %3, t3, %5;\n\t}"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(w), "r"(mult));
+}
+// f16 factor of an MXFP4 block (scale byte s) inside a row whose largest scale byte is smax:
+// 2^(s - smax + 13), so |e2m1 * factor| <= 6 * 2^13 fits f16; the row's outputs are multiplied by
+// 2^(smax - 140) in the epilogue.  Blocks 2^28 or more below the row's largest become f16 subnormal.
+__device__ __forceinline__ uint32_t mult_mx_f16(uint32_t s, int smax) {
+  const int me = int(s) - smax + 28;  // biased f16 exponent of the factor
+  const uint32_t bits = me >= 1 ? uint32_t(me) << 10 : (me >= -9 ? 1u << (me + 9) : 0u);
+  return bits * 0x00010001u;
+}
+// NVFP4 factor: e4m3 magnitude as f16 bits (s & 0x7f) << 7 = scale * 2^-8 (qmv_kernel.py:26-28 trick);
+// outputs are multiplied by 2^8 in the epilogue.  e2m1 * e4m3 * 2^-8 is always exact in f16.
+__device__ __forceinline__ uint32_t mult_nv_f16(uint32_t s) { return ((s & 0x7Fu) << 7) * 0x00010001u; }
+
 // Position of element k (0..7) of a word inside its permuted 8-group.
 __host__ __device__ __forceinline__ int perm8(int k) { return ((k & 3) << 1) | (k >> 2); }
 
@@ -133,6 +186,9 @@ __device__ __forceinline__ int ilogb_pos(float f) {  // f > 0, finite
   const int e = int((u >> 23) & 0xFFu);
   if (e) return e - 127;
   return (31 - __clz(int(u & 0x7FFFFFu))) - 149;
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  return uint32_t(__half_as_ushort(__float2half_rn(lo))) | (uint32_t(__half_as_ushort(__float2half_rn(hi))) << 16);
 }
 __device__ __forceinline__ float e4m3_value(uint32_t s) {
   const uint32_t c = s & 0x7Fu;
@@ -336,93 +392,125 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const int32_t* __restri
 }
 
 // --------------------------------------------------------------------------- operand image of x
-// Tile image: K/128 chunks of nt x 128 bf16; inside a chunk, core matrix (k8, row8) at
-// ((k8 * nt/8) + row8) * 128 bytes, row r & 7 at 16 B steps, k permuted by perm8 inside each 8-group.
-// One 16-B unit per thread iteration, in image order (coalesced stores).
+// Tile image (f16, natural k order): K/128 chunks of nt x 128; inside a chunk, core matrix (k8, row8)
+// at ((k8 * nt/8) + row8) * 128 bytes, row r & 7 at 16-B steps.  One warp per tile row.  Each token row
+// is scaled by 2^-k (k = max(0, ilogb(max|x|) - 14)) so every value fits f16; k goes to xsh[entry]
+// and the gate/up epilogue multiplies by 2^k.  bf16 -> f16 is exact for |x| >= 2^-17 after scaling.
 __global__ void moe_gather_kernel(const uint16_t* __restrict__ x, int H, const Tile* __restrict__ tiles,
                                   const int32_t* __restrict__ counters, const int32_t* __restrict__ sorted_tok,
-                                  uint8_t* __restrict__ ximg) {
+                                  uint8_t* __restrict__ ximg, int32_t* __restrict__ xsh) {
   pdl_wait();
   pdl_trigger();
   if (int(blockIdx.x) >= counters[0]) return;
   const Tile tl = tiles[blockIdx.x];
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= tl.nt) return;
   const int nt8 = tl.nt >> 3;
-  const int units = tl.nt * (H >> 3);
-  uint8_t* base = ximg + (size_t)tl.row0 * H * 2;
-  const int step = blockDim.x * gridDim.y;
-  for (int u = blockIdx.y * blockDim.x + threadIdx.x; u < units; u += step) {
-    const int r7 = u & 7;
-    int v = u >> 3;
-    const int rg = v % nt8;
-    v /= nt8;  // v = chunk * 16 + k8
-    const int r = rg * 8 + r7;
-    uint4 o = make_uint4(0u, 0u, 0u, 0u);
-    if (r < tl.ntok) {
-      const int tok = sorted_tok[tl.entry0 + r];
-      const uint4 in = *reinterpret_cast<const uint4*>(x + (size_t)tok * H + (size_t)v * 8);
-      o.x = __byte_perm(in.x, in.z, 0x5410);  // (e0, e4)
-      o.y = __byte_perm(in.x, in.z, 0x7632);  // (e1, e5)
-      o.z = __byte_perm(in.y, in.w, 0x5410);  // (e2, e6)
-      o.w = __byte_perm(in.y, in.w, 0x7632);  // (e3, e7)
-    }
-    *reinterpret_cast<uint4*>(base + (size_t)u * 16) = o;
+  uint8_t* base = ximg + (size_t)tl.row0 * H * 2 + (size_t)(row >> 3) * 128 + (row & 7) * 16;
+  const int units = H >> 3;
+  if (row >= tl.ntok) {
+    for (int u = lane; u < units; u += 32)
+      *reinterpret_cast<uint4*>(base + (size_t)u * nt8 * 128) = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)sorted_tok[tl.entry0 + row] * H);
+  float amax = 0.0f;
+  for (int u = lane; u < units; u += 32) {
+    const uint4 v = xr[u];
+    amax = fmaxf(amax, fmaxf(fmaxf(fmaxf(fabsf(bflo(v.x)), fabsf(bfhi(v.x))), fmaxf(fabsf(bflo(v.y)), fabsf(bfhi(v.y)))),
+                             fmaxf(fmaxf(fabsf(bflo(v.z)), fabsf(bfhi(v.z))), fmaxf(fabsf(bflo(v.w)), fabsf(bfhi(v.w))))));
+  }
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, d));
+  const int k = (amax > 0.0f && amax <= 3.4e38f) ? max(0, ilogb_pos(amax) - 14) : 0;
+  const float sc = __uint_as_float(uint32_t(127 - k) << 23);
+  if (lane == 0) xsh[tl.entry0 + row] = k;
+  for (int u = lane; u < units; u += 32) {
+    const uint4 v = xr[u];
+    uint4 o;
+    o.x = pack_half2(__fmul_rn(bflo(v.x), sc), __fmul_rn(bfhi(v.x), sc));
+    o.y = pack_half2(__fmul_rn(bflo(v.y), sc), __fmul_rn(bfhi(v.y), sc));
+    o.z = pack_half2(__fmul_rn(bflo(v.z), sc), __fmul_rn(bfhi(v.z), sc));
+    o.w = pack_half2(__fmul_rn(bflo(v.w), sc), __fmul_rn(bfhi(v.w), sc));
+    *reinterpret_cast<uint4*>(base + (size_t)u * nt8 * 128) = o;
   }
 }
 
 // --------------------------------------------------------------------------- grouped GEMM
 struct GemmArgs {
-  const uint8_t* sa;    // scales of matrix 0 (gate or down), [E*R, KS]
-  const uint8_t* sb;    // scales of matrix 1 (up), gate/up only
-  const uint8_t* bimg;  // operand images: x (gate/up) or h hi|lo (down)
+  const uint8_t* sa;      // down: scales [E*R, KS] (1-D bulk copy per unit); gate/up uses tensor maps
+  const uint8_t* bimg;    // operand images: x (gate/up, f16) or h hi|lo (down, bf16)
   const Tile* tiles;
   const int32_t* counters;
-  uint8_t* himg;        // gate/up output: h operand images for down
-  float* yp;            // down output: per-entry fp32 partials [n, R]
-  int K;                // reduction length
-  int R;                // weight rows per expert
-  int KS;               // scale bytes per weight row
-  int fmt;              // 0 MXFP4, 1 NVFP4
-  float limit;          // SwiGLU clamp (+inf = off)
-  int h_rows;           // gate/up: K of the down GEMM (= R)
-  unsigned* err;        // library device error word
+  const int32_t* xsh;     // gate/up: per-entry exponent of the activation downscale
+  uint8_t* himg;          // gate/up output: h operand images for down
+  float* yp;              // down output: per-entry fp32 partials [n, R]
+  int K;                  // reduction length
+  int R;                  // weight rows per expert
+  int KS;                 // scale bytes per weight row
+  int fmt;                // 0 MXFP4, 1 NVFP4
+  float limit;            // SwiGLU clamp (+inf = off)
+  int h_rows;             // gate/up: K of the down GEMM (= R)
+  int nw;                 // weight ring stages
+  int sbuf;               // bytes of one scale buffer
+  unsigned* err;          // library device error word
 };
 
 struct Bars {
-  uint64_t full[kStages], empty[kStages];
+  uint64_t wfull[kMaxW], wempty[kMaxW];
+  uint64_t bfull[kNB], bempty[kNB];
   uint64_t afull[4], aempty[4];
   uint64_t sfull[2], sempty[2];
   uint64_t accfull[2], accempty[2];
+  uint64_t rsfull[2], rsempty[2];
   uint64_t drain;
   uint32_t tmem;
   int abort;
 };
+static_assert(sizeof(Bars) <= 512, "barrier block");
 
+// Warp roles: 0 weight/scale producer, 1 MMA issuer, 2 operand-image producer, 3 idle,
+// 4 .. 4+kNDQ-1 dequantizers (lane quarter dw & 3, sub-task dw >> 2), last 4 epilogue.
+// Gate/up (GU): f16 MMA; dequantizer sub-task = (matrix, half of the 4 32-element chunks of a stage).
+// Down: bf16 MMA; sub-task = one chunk.
 template <bool GU>
 __global__ void __launch_bounds__(kThreads, 1)
-    moe_gemm_kernel(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1, GemmArgs a) {
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ CUtensorMap tw1,
+                    const __grid_constant__ CUtensorMap ts0, const __grid_constant__ CUtensorMap ts1, GemmArgs a) {
   using C = Cfg<GU>;
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* stages = dsm;
-  uint8_t* sbufs = dsm + kStages * C::STAGE;
-  Bars* bars = reinterpret_cast<Bars*>(sbufs + 2 * C::SCALE_BUF);
+  const SmemMap map = smem_map(GU, a.nw, a.sbuf);
+  uint8_t* wring = dsm + map.w;
+  uint8_t* bring = dsm + map.b;
+  uint8_t* sbufs = dsm + map.s;
+  int* rsx = reinterpret_cast<int*>(dsm + map.rs);  // [2][2][128]
+  Bars* bars = reinterpret_cast<Bars*>(dsm + map.bars);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   unsigned* err = a.err;
+  const int NW = a.nw;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->empty[s], 8 + 1);
+    for (int s = 0; s < NW; ++s) {
+      mbar_init(&bars->wfull[s], 1);
+      mbar_init(&bars->wempty[s], kNDQ);
+    }
+    for (int s = 0; s < kNB; ++s) {
+      mbar_init(&bars->bfull[s], 1);
+      mbar_init(&bars->bempty[s], 1);
     }
     for (int s = 0; s < C::NA; ++s) {
-      mbar_init(&bars->afull[s], 8);
+      mbar_init(&bars->afull[s], kNDQ);
       mbar_init(&bars->aempty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->sfull[s], 1);
-      mbar_init(&bars->sempty[s], 8);
+      mbar_init(&bars->sempty[s], kNDQ);
       mbar_init(&bars->accfull[s], 1);
       mbar_init(&bars->accempty[s], 4);
+      mbar_init(&bars->rsfull[s], kNDQ);
+      mbar_init(&bars->rsempty[s], 4);
     }
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
@@ -440,45 +528,73 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int RT = a.R / kRows;
   const int total = a.counters[0] * RT;
   const int nchunk = a.K / kChunk;
-  const uint32_t sbytes = uint32_t(kRows * a.KS);
+  const int KS = a.KS;
 
   if (warp == 0) {
-    // ----------------------------------------------------------------- producer
+    // ----------------------------------------------------------------- weight + scale producer
     if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first(), pol_b = policy_evict_last();
+      const uint64_t pol_w = policy_evict_first();
       int it = 0, lu = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lu) {
         const Tile tl = a.tiles[u / RT];
-        const int rt = u % RT;
-        const int row = tl.expert * a.R + rt * kRows;
+        const int row = tl.expert * a.R + (u % RT) * kRows;
         const int sb = lu & 1;
-        if (!(ok = mbar_wait_sleep(&bars->sempty[sb], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
-        mbar_expect_tx(&bars->sfull[sb], sbytes * C::NMAT);
-        bulk_g2s(sbufs + sb * C::SCALE_BUF, a.sa + (size_t)row * a.KS, sbytes, &bars->sfull[sb], pol_w);
-        if (GU) bulk_g2s(sbufs + sb * C::SCALE_BUF + sbytes, a.sb + (size_t)row * a.KS, sbytes, &bars->sfull[sb], pol_w);
-        const uint32_t bbytes = uint32_t(tl.nt * (GU ? 256 : 512));
-        const uint8_t* bsrc = a.bimg + (size_t)tl.row0 * a.K * (GU ? 2 : 4);
+        if (*abort_flag || !(ok = mbar_wait_sleep(&bars->sempty[sb], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
+        uint8_t* sdst = sbufs + sb * a.sbuf;
+        if (GU) {
+          mbar_expect_tx(&bars->sfull[sb], uint32_t(2 * kRows * KS));
+          for (int m = 0; m < 2; ++m)
+            for (int bx = 0; bx < KS / 16; ++bx)
+              tma_load_2d(sdst + m * kRows * KS + bx * (kRows * 16), m ? (const void*)&ts1 : (const void*)&ts0,
+                          bx * 16, row, &bars->sfull[sb], pol_w);
+        } else {
+          mbar_expect_tx(&bars->sfull[sb], uint32_t(kRows * KS));
+          bulk_g2s(sdst, a.sa + (size_t)row * KS, uint32_t(kRows * KS), &bars->sfull[sb], pol_w);
+        }
         for (int c = 0; c < nchunk; ++c, ++it) {
-          const int s = it % kStages;
-          if (*abort_flag || !(ok = mbar_wait_sleep(&bars->empty[s], ((it / kStages) & 1) ^ 1, err, kWaitPolls))) { ok = false; break; }
-          uint8_t* st = stages + s * C::STAGE;
-          mbar_expect_tx(&bars->full[s], uint32_t(C::NMAT * kWBytes) + bbytes);
-          tma_load_2d(st, &tm0, c * (kChunk / 2), row, &bars->full[s], pol_w);
-          if (GU) tma_load_2d(st + kWBytes, &tm1, c * (kChunk / 2), row, &bars->full[s], pol_w);
-          bulk_g2s(st + C::NMAT * kWBytes, bsrc + (size_t)c * bbytes, bbytes, &bars->full[s], pol_b);
+          const int s = it % NW;
+          if (*abort_flag || !mbar_wait_sleep(&bars->wempty[s], ((it / NW) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
+          uint8_t* st = wring + s * C::WSTAGE;
+          mbar_expect_tx(&bars->wfull[s], uint32_t(C::WSTAGE));
+          tma_load_2d(st, &tw0, c * (kChunk / 2), row, &bars->wfull[s], pol_w);
+          if (GU) tma_load_2d(st + kWBytes, &tw1, c * (kChunk / 2), row, &bars->wfull[s], pol_w);
         }
       }
       if (!ok) {
         *abort_flag = 1;
-        // let every copy already issued land before the CTA leaves
-        for (int k = 1; k <= kStages && it - k >= 0; ++k) {
+        for (int k = 1; k <= NW && it - k >= 0; ++k) {
           const int j = it - k;
-          mbar_wait_sleep(&bars->full[j % kStages], (j / kStages) & 1, err, 1u << 20);
+          mbar_wait_sleep(&bars->wfull[j % NW], (j / NW) & 1, err, kWaitPolls);
         }
         for (int k = 1; k <= 2 && lu - k >= 0; ++k) {
           const int j = lu - k;
-          mbar_wait_sleep(&bars->sfull[j & 1], (j >> 1) & 1, err, 1u << 20);
+          mbar_wait_sleep(&bars->sfull[j & 1], (j >> 1) & 1, err, kWaitPolls);
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // ----------------------------------------------------------------- operand-image producer
+    if (lane == 0) {
+      const uint64_t pol_b = policy_evict_last();
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const Tile tl = a.tiles[u / RT];
+        const uint32_t bbytes = uint32_t(tl.nt * (GU ? 256 : 512));
+        const uint8_t* bsrc = a.bimg + (size_t)tl.row0 * a.K * (GU ? 2 : 4);
+        for (int c = 0; c < nchunk; ++c, ++it) {
+          const int s = it % kNB;
+          if (*abort_flag || !mbar_wait_sleep(&bars->bempty[s], ((it / kNB) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
+          mbar_expect_tx(&bars->bfull[s], bbytes);
+          bulk_g2s(bring + s * C::BSTAGE, bsrc + (size_t)c * bbytes, bbytes, &bars->bfull[s], pol_b);
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        for (int k = 1; k <= kNB && it - k >= 0; ++k) {
+          const int j = it - k;
+          mbar_wait_sleep(&bars->bfull[j % kNB], (j / kNB) & 1, err, kWaitPolls);
         }
       }
     }
@@ -490,17 +606,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lu) {
         const Tile tl = a.tiles[u / RT];
         const int d = lu & 1;
-        const uint32_t idesc = umma_idesc_bf16(128, tl.nt);
+        const uint32_t idesc = GU ? umma_idesc_f16(128, tl.nt) : umma_idesc_bf16(128, tl.nt);
         const uint32_t lbo = uint32_t(tl.nt / 8) * 128u;
-        if (!(ok = mbar_wait_sleep(&bars->accempty[d], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
+        if (*abort_flag || !(ok = mbar_wait_sleep(&bars->accempty[d], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
         tc_fence_after();
         const uint32_t dacc = tmem + uint32_t(d * C::ACC_STRIDE);
         for (int c = 0; c < nchunk; ++c, ++it) {
-          const int s = it % kStages, ap = it % C::NA;
-          if (*abort_flag || !mbar_wait_sleep(&bars->full[s], (it / kStages) & 1, err, kWaitPolls) ||
+          const int s = it % kNB, ap = it % C::NA;
+          if (*abort_flag || !mbar_wait_sleep(&bars->bfull[s], (it / kNB) & 1, err, kWaitPolls) ||
               !mbar_wait_sleep(&bars->afull[ap], (it / C::NA) & 1, err, kWaitPolls)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sB = smem_u32(stages + s * C::STAGE + C::NMAT * kWBytes);
+          const uint32_t sB = smem_u32(bring + s * C::BSTAGE);
           const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS);
 #pragma unroll
           for (int ks = 0; ks < kChunk / 16; ++ks) {
@@ -516,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           issued = true;
-          umma_commit(&bars->empty[s]);
+          umma_commit(&bars->bempty[s]);
           umma_commit(&bars->aempty[ap]);
           if (c == nchunk - 1) umma_commit(&bars->accfull[d]);
         }
@@ -527,74 +643,114 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait_sleep(&bars->drain, 0, err, kWaitPolls);
       }
     }
-  } else if (warp >= 4 && warp < 12) {
+  } else if (warp >= 4 && warp < 4 + kNDQ) {
     // ----------------------------------------------------------------- dequantizers
-    const int dw = warp - 4, q = dw & 3, part = dw >> 2;  // part: matrix (gate/up) or K half (down)
+    const int dw = warp - 4, q = dw & 3, sub = dw >> 2;
+    const int mat = GU ? sub >> 1 : 0;
+    const int ch0 = GU ? 2 * (sub & 1) : sub;  // first 32-element chunk of the stage handled here
+    constexpr int NCH = GU ? 2 : 1;
     const int r = q * 32 + lane;
     const int sw = (r >> 1) & 3;
     const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
     int it = 0, lu = 0;
-    for (int u = blockIdx.x; u < total; u += gridDim.x, ++lu) {
-      const int sb = lu & 1;
-      if (*abort_flag || !mbar_wait_sleep(&bars->sfull[sb], (lu >> 1) & 1, err, kWaitPolls)) { *abort_flag = 1; break; }
-      const uint8_t* srow = sbufs + sb * C::SCALE_BUF + (GU ? part * int(sbytes) : 0) + r * a.KS;
-      bool ok = true;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lu) {
+      const int sb = lu & 1, d = lu & 1;
+      if (*abort_flag || !mbar_wait_sleep(&bars->sfull[sb], (lu >> 1) & 1, err, kWaitPolls)) { ok = false; break; }
+      const uint8_t* sbase = sbufs + sb * a.sbuf;
+      int smax = 0;
+      if (GU) {
+        // this row's largest e8m0 byte (MXFP4), published with the NVFP4 constant for the epilogue
+        int e_row = 8;
+        if (a.fmt == 0) {
+          uint32_t m = 0;
+          const uint8_t* rowp = sbase + mat * kRows * KS + r * 16;
+          for (int bx = 0; bx < KS / 16; ++bx) {
+            const uint4 v = *reinterpret_cast<const uint4*>(rowp + bx * (kRows * 16));
+            m = __vmaxu4(m, __vmaxu4(__vmaxu4(v.x, v.y), __vmaxu4(v.z, v.w)));
+          }
+          smax = int(max(max(m & 0xFFu, (m >> 8) & 0xFFu), max((m >> 16) & 0xFFu, m >> 24)));
+          e_row = smax - 140;
+        }
+        if (!mbar_wait_sleep(&bars->rsempty[d], ((lu >> 1) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
+        if ((sub & 1) == 0) rsx[(d * 2 + mat) * kRows + r] = e_row;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->rsfull[d]);
+      }
       for (int c = 0; c < nchunk; ++c, ++it) {
-        const int s = it % kStages, ap = it % C::NA;
-        if (*abort_flag || !mbar_wait_sleep(&bars->full[s], (it / kStages) & 1, err, kWaitPolls)) { ok = false; break; }
-        const uint8_t* wt = stages + s * C::STAGE + (GU ? part * kWBytes : 0) + r * 64;
-        constexpr int NCH = GU ? 4 : 2;  // 32-element chunks handled by this thread per stage
-        const int ch0 = GU ? 0 : 2 * part;
+        const int s = it % NW, ap = it % C::NA;
+        if (*abort_flag || !mbar_wait_sleep(&bars->wfull[s], (it / NW) & 1, err, kWaitPolls)) { ok = false; break; }
+        const uint8_t* wt = wring + s * C::WSTAGE + mat * kWBytes + r * 64;
         uint4 wv[NCH];
 #pragma unroll
-        for (int j = 0; j < NCH; ++j)
-          wv[j] = *reinterpret_cast<const uint4*>(wt + 16 * ((ch0 + j) ^ sw));
-        uint32_t sc0, sc1;  // scale bytes of this stage
-        if (a.fmt == 0) {
-          sc0 = *reinterpret_cast<const uint32_t*>(srow + 4 * c);
-          sc1 = 0;
+        for (int j = 0; j < NCH; ++j) wv[j] = *reinterpret_cast<const uint4*>(wt + 16 * ((ch0 + j) ^ sw));
+        uint32_t sc;  // scale bytes of this thread's chunks, lowest chunk in the low byte(s)
+        if (GU) {
+          if (a.fmt == 0)
+            sc = *reinterpret_cast<const uint16_t*>(sbase + mat * kRows * KS + (c >> 2) * (kRows * 16) + r * 16 +
+                                                    4 * (c & 3) + ch0);
+          else
+            sc = *reinterpret_cast<const uint32_t*>(sbase + mat * kRows * KS + (c >> 1) * (kRows * 16) + r * 16 +
+                                                    8 * (c & 1) + 2 * ch0);
         } else {
-          const uint2 t2 = *reinterpret_cast<const uint2*>(srow + 8 * c);
-          sc0 = t2.x;
-          sc1 = t2.y;
+          if (a.fmt == 0)
+            sc = sbase[r * KS + 4 * c + ch0];
+          else
+            sc = *reinterpret_cast<const uint16_t*>(sbase + r * KS + 8 * c + 2 * ch0);
         }
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&bars->empty[s]);
+          mbar_arrive(&bars->wempty[s]);
           if (c == nchunk - 1) mbar_arrive(&bars->sempty[sb]);
         }
         if (!mbar_wait_sleep(&bars->aempty[ap], ((it / C::NA) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t acol = uint32_t(C::A_BASE + ap * C::ACOLS + (GU ? part * 64 : part * 32));
 #pragma unroll
         for (int j = 0; j < NCH; ++j) {
-          const int ch = ch0 + j;
           uint32_t out[16];
-          if (a.fmt == 0) {
-            const Mult mu = mult_e8m0((sc0 >> (8 * ch)) & 0xFFu);
-            fp4_word(wv[j].x, mu, out);
-            fp4_word(wv[j].y, mu, out + 4);
-            fp4_word(wv[j].z, mu, out + 8);
-            fp4_word(wv[j].w, mu, out + 12);
+          if (GU) {
+            uint32_t m0, m1;
+            if (a.fmt == 0) {
+              m0 = m1 = mult_mx_f16((sc >> (8 * j)) & 0xFFu, smax);
+            } else {
+              m0 = mult_nv_f16((sc >> (16 * j)) & 0xFFu);
+              m1 = mult_nv_f16((sc >> (16 * j + 8)) & 0xFFu);
+            }
+            fp4_word_f16(wv[j].x, m0, out);
+            fp4_word_f16(wv[j].y, m0, out + 4);
+            fp4_word_f16(wv[j].z, m1, out + 8);
+            fp4_word_f16(wv[j].w, m1, out + 12);
+            tmem_st16(lane_base + uint32_t(C::A_BASE + ap * C::ACOLS + mat * 64 + (ch0 + j) * 16), out);
           } else {
-            const uint32_t sw2 = ch < 2 ? sc0 : sc1;
-            const Mult m0 = mult_e4m3((sw2 >> (16 * (ch & 1))) & 0xFFu);
-            const Mult m1 = mult_e4m3((sw2 >> (16 * (ch & 1) + 8)) & 0xFFu);
-            fp4_word(wv[j].x, m0, out);
-            fp4_word(wv[j].y, m0, out + 4);
-            fp4_word(wv[j].z, m1, out + 8);
-            fp4_word(wv[j].w, m1, out + 12);
+            Mult m0, m1;
+            if (a.fmt == 0) {
+              m0 = m1 = mult_e8m0(sc & 0xFFu);
+            } else {
+              m0 = mult_e4m3(sc & 0xFFu);
+              m1 = mult_e4m3((sc >> 8) & 0xFFu);
+            }
+            if (!__any_sync(0xFFFFFFFFu, m0.slow || m1.slow)) {
+              fp4_word_fast(wv[j].x, m0.m, out);
+              fp4_word_fast(wv[j].y, m0.m, out + 4);
+              fp4_word_fast(wv[j].z, m1.m, out + 8);
+              fp4_word_fast(wv[j].w, m1.m, out + 12);
+            } else {
+              fp4_word_wide(wv[j].x, m0.m2, out);
+              fp4_word_wide(wv[j].y, m0.m2, out + 4);
+              fp4_word_wide(wv[j].z, m1.m2, out + 8);
+              fp4_word_wide(wv[j].w, m1.m2, out + 12);
+            }
+            tmem_st16(lane_base + uint32_t(C::A_BASE + ap * C::ACOLS + (ch0 + j) * 16), out);
           }
-          tmem_st16(lane_base + acol + uint32_t(j * 16), out);
         }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->afull[ap]);
       }
-      if (!ok) { *abort_flag = 1; break; }
     }
-  } else if (warp >= 12) {
+    if (!ok) *abort_flag = 1;
+  } else if (warp >= 4 + kNDQ) {
     // ----------------------------------------------------------------- epilogue
     const int q = warp & 3, r = q * 32 + lane;
     const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
@@ -604,9 +760,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int rt = u % RT;
       const int d = lu & 1;
       if (*abort_flag || !mbar_wait_sleep(&bars->accfull[d], (lu >> 1) & 1, err, kWaitPolls)) { *abort_flag = 1; break; }
+      if (GU && !mbar_wait_sleep(&bars->rsfull[d], (lu >> 1) & 1, err, kWaitPolls)) { *abort_flag = 1; break; }
       tc_fence_after();
       const uint32_t dacc = lane_base + uint32_t(d * C::ACC_STRIDE);
       if (GU) {
+        const float fg = ldexpf(1.0f, rsx[(d * 2 + 0) * kRows + r]);
+        const float fu = ldexpf(1.0f, rsx[(d * 2 + 1) * kRows + r]);
         // this row is k = rt*128 + r of the down GEMM: chunk rt, permuted position p
         const int p = (r & ~7) | perm8(r & 7);
         const int nt8 = tl.nt >> 3;
@@ -621,8 +780,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n = cg * 16 + i;
             float hv = 0.0f;
             if (n < tl.ntok) {
-              const float gv = fminf(__uint_as_float(g[i]), a.limit);
-              const float uv = fmaxf(fminf(__uint_as_float(v[i]), a.limit), -a.limit);
+              const float tf = ldexpf(1.0f, a.xsh[tl.entry0 + n]);
+              const float gv = fminf(__fmul_rn(__fmul_rn(__uint_as_float(g[i]), fg), tf), a.limit);
+              const float uv = fmaxf(fminf(__fmul_rn(__fmul_rn(__uint_as_float(v[i]), fu), tf), a.limit), -a.limit);
               hv = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, q_expf(-gv))), uv);
             }
             const uint16_t hi = f2bf(hv);
@@ -647,7 +807,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->accempty[d]);
+      if (lane == 0) {
+        mbar_arrive(&bars->accempty[d]);
+        if (GU) mbar_arrive(&bars->rsempty[d]);
+      }
     }
   }
   tc_fence_before();
@@ -692,7 +855,7 @@ __global__ void moe_combine_kernel(const float* __restrict__ yp, const int32_t* 
 
 // --------------------------------------------------------------------------- host side
 struct Workspace {
-  size_t entry_pos, sorted_tok, rank_tmp, tiles, counters, ximg, himg, yp, total;
+  size_t entry_pos, sorted_tok, rank_tmp, xsh, tiles, counters, ximg, himg, yp, total;
   int max_tiles, max_rows;
 };
 inline size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -705,6 +868,7 @@ inline Workspace layout(int T, int S, int E, int H, int I) {
   w.entry_pos = o; o = up256(o + n * 4);
   w.sorted_tok = o; o = up256(o + n * 4);
   w.rank_tmp = o; o = up256(o + n * 4);
+  w.xsh = o; o = up256(o + n * 4);
   w.tiles = o; o = up256(o + size_t(w.max_tiles) * sizeof(Tile));
   w.counters = o; o = up256(o + 16);
   w.ximg = o; o = up256(o + size_t(w.max_rows) * H * 2);
@@ -726,29 +890,42 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   });
   return fn;
 }
-// Packed weights [rows, K/2 bytes] as a uint8 2-D tensor; box = 64 bytes (128 k) x 128 rows, 64-B swizzle.
-bool weight_map(CUtensorMap* m, const void* base, long long rows, int K) {
+// uint8 2-D tensor [rows, cols] with row pitch `cols` bytes; box = bw bytes x 128 rows.
+bool byte_map(CUtensorMap* m, const void* base, long long rows, long long cols, int bw, CUtensorMapSwizzle swz) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[2] = {cuuint64_t(K / 2), cuuint64_t(rows)};
-  cuuint64_t strides[1] = {cuuint64_t(K / 2)};
-  cuuint32_t box[2] = {uint32_t(kChunk / 2), uint32_t(kRows)};
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols)};
+  cuuint32_t box[2] = {uint32_t(bw), uint32_t(kRows)};
   cuuint32_t es[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// Packed weights [rows, K/2 bytes]: box = 64 bytes (128 k) x 128 rows, 64-B swizzle.
+bool weight_map(CUtensorMap* m, const void* base, long long rows, int K) {
+  return byte_map(m, base, rows, K / 2, kChunk / 2, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+// Weight-ring depth: as many stages as fit next to the operand ring and the two scale buffers.
+template <bool GU>
+int ring_stages(int sbuf) {
+  for (int nw = kMaxW; nw >= 2; --nw)
+    if (smem_map(GU, nw, sbuf).total <= kSmemMax) return nw;
+  return 0;
 }
 
 template <bool GU>
-cudaError_t launch_gemm(const CUtensorMap& m0, const CUtensorMap& m1, const GemmArgs& a, int grid,
-                        cudaStream_t st) {
+cudaError_t launch_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& s0, const CUtensorMap& s1,
+                        const GemmArgs& a, int grid, cudaStream_t st) {
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(moe_gemm_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<GU>::SMEM);
+    attr = cudaFuncSetAttribute(moe_gemm_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
   });
   if (attr != cudaSuccess) return attr;
-  return launch_kernel(moe_gemm_kernel<GU>, dim3(grid), dim3(kThreads), Cfg<GU>::SMEM, st, m0, m1, a);
+  const size_t smem = size_t(smem_map(GU, a.nw, a.sbuf).total);
+  return launch_kernel(moe_gemm_kernel<GU>, dim3(grid), dim3(kThreads), smem, st, w0, w1, s0, s1, a);
 }
 
 }  // namespace moe
@@ -794,15 +971,16 @@ extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_
   if (H <= 0 || I <= 0 || H % kRows || I % kRows) return QMTP_ERR_SHAPE;
   const int G = fmt == 0 ? 32 : 16;
   const int KS_gu = H / G, KS_dn = I / G;
-  if (2 * kRows * KS_gu > Cfg<true>::SCALE_BUF || kRows * KS_dn > Cfg<false>::SCALE_BUF) return QMTP_ERR_UNSUPPORTED;
+  if (KS_gu % 16) return QMTP_ERR_UNSUPPORTED;  // gate/up scales are staged in 16-byte TMA boxes
+  const int sbuf_gu = (2 * kRows * KS_gu + 1023) & ~1023, sbuf_dn = (kRows * KS_dn + 1023) & ~1023;
+  const int nw_gu = ring_stages<true>(sbuf_gu), nw_dn = ring_stages<false>(sbuf_dn);
+  if (nw_gu < 2 || nw_dn < 2) return QMTP_ERR_UNSUPPORTED;
   if (!aligned16(x_) || !aligned16(wg) || !aligned16(wu) || !aligned16(wd) || !aligned16(sg_) || !aligned16(su_) ||
       !aligned16(sd_) || !aligned16(y_) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return QMTP_ERR_ALIGN;
   const Workspace L = layout(T, S, E, H, I);
   if (ws_bytes < L.total) return QMTP_ERR_SHAPE;
   const auto* x = static_cast<const uint16_t*>(x_);
-  const auto* sg = static_cast<const uint8_t*>(sg_);
-  const auto* su = static_cast<const uint8_t*>(su_);
   const auto* sd = static_cast<const uint8_t*>(sd_);
   const auto* idx = static_cast<const int32_t*>(idx_);
   const auto* scores = static_cast<const float*>(scores_);
@@ -812,15 +990,18 @@ extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_
   auto* entry_pos = reinterpret_cast<int32_t*>(ws + L.entry_pos);
   auto* sorted_tok = reinterpret_cast<int32_t*>(ws + L.sorted_tok);
   auto* rank_tmp = reinterpret_cast<int32_t*>(ws + L.rank_tmp);
+  auto* xsh = reinterpret_cast<int32_t*>(ws + L.xsh);
   auto* tiles = reinterpret_cast<Tile*>(ws + L.tiles);
   auto* counters = reinterpret_cast<int32_t*>(ws + L.counters);
   uint8_t* ximg = ws + L.ximg;
   uint8_t* himg = ws + L.himg;
   auto* yp = reinterpret_cast<float*>(ws + L.yp);
 
-  CUtensorMap mg, mu, md;
+  CUtensorMap mg, mu, md, msg, msu;
   if (!weight_map(&mg, wg, (long long)E * I, H) || !weight_map(&mu, wu, (long long)E * I, H) ||
-      !weight_map(&md, wd, (long long)E * H, I))
+      !weight_map(&md, wd, (long long)E * H, I) ||
+      !byte_map(&msg, sg_, (long long)E * I, KS_gu, 16, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !byte_map(&msu, su_, (long long)E * I, KS_gu, 16, CU_TENSOR_MAP_SWIZZLE_NONE))
     return QMTP_ERR_CUDA;
 
   const int n = T * S;
@@ -833,14 +1014,14 @@ extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_
   unsigned* err = device_error_ptr();
   QMTP_CUDA_TRY(launch_kernel(moe_group_kernel, dim3(1), dim3(1024), size_t(32) * E * 2, stream, idx, n, S, E,
                               entry_pos, sorted_tok, rank_tmp, tiles, counters, err));
-  QMTP_CUDA_TRY(launch_kernel(moe_gather_kernel, dim3(unsigned(L.max_tiles), 8), dim3(256), 0, stream, x, H,
-                              (const Tile*)tiles, (const int32_t*)counters, (const int32_t*)sorted_tok, ximg));
+  QMTP_CUDA_TRY(launch_kernel(moe_gather_kernel, dim3(unsigned(L.max_tiles), kMaxTok / 8), dim3(256), 0, stream, x, H,
+                              (const Tile*)tiles, (const int32_t*)counters, (const int32_t*)sorted_tok, ximg, xsh));
   const int grid = sm_count();
-  GemmArgs gu{sg, su, ximg, tiles, counters, himg, nullptr, H, I, KS_gu, fmt, limit, I, err};
-  QMTP_CUDA_TRY(launch_gemm<true>(mg, mu, gu, grid, stream));
-  GemmArgs dn{sd, nullptr, himg, tiles, counters, nullptr, yp, I, H, KS_dn, fmt, limit, 0, err};
-  QMTP_CUDA_TRY(launch_gemm<false>(md, md, dn, grid, stream));
-  QMTP_CUDA_TRY(launch_kernel(moe_combine_kernel, dim3(unsigned(T), unsigned((H + 1023) / 1024)), dim3(256), 0, stream, (const float*)yp,
-                              (const int32_t*)entry_pos, scores, S, H, y));
+  GemmArgs gu{nullptr, ximg, tiles, counters, xsh, himg, nullptr, H, I, KS_gu, fmt, limit, I, nw_gu, sbuf_gu, err};
+  QMTP_CUDA_TRY(launch_gemm<true>(mg, mu, msg, msu, gu, grid, stream));
+  GemmArgs dn{sd, himg, tiles, counters, nullptr, nullptr, yp, I, H, KS_dn, fmt, limit, 0, nw_dn, sbuf_dn, err};
+  QMTP_CUDA_TRY(launch_gemm<false>(md, md, md, md, dn, grid, stream));
+  QMTP_CUDA_TRY(launch_kernel(moe_combine_kernel, dim3(unsigned(T), unsigned((H + 1023) / 1024)), dim3(256), 0, stream,
+                              (const float*)yp, (const int32_t*)entry_pos, scores, S, H, y));
   return QMTP_OK;
 }
