@@ -439,7 +439,8 @@ __global__ void moe_gather_kernel(const uint16_t* __restrict__ x, int H, const T
 
 // --------------------------------------------------------------------------- grouped GEMM
 struct GemmArgs {
-  const uint8_t* sa;      // down: scales [E*R, KS] (1-D bulk copy per unit); gate/up uses tensor maps
+  const uint8_t* sa;      // scales of matrix 0 [E*R, KS] (1-D bulk copies when not staged by tensor maps)
+  const uint8_t* sb;      // gate/up: scales of matrix 1
   const uint8_t* bimg;    // operand images: x (gate/up, f16) or h hi|lo (down, bf16)
   const Tile* tiles;
   const int32_t* counters;
@@ -454,6 +455,7 @@ struct GemmArgs {
   int h_rows;             // gate/up: K of the down GEMM (= R)
   int nw;                 // weight ring stages
   int sbuf;               // bytes of one scale buffer
+  int sbox;               // gate/up: scales staged in 16-byte TMA boxes (KS % 16 == 0), else as rows
   unsigned* err;          // library device error word
 };
 
@@ -544,10 +546,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* sdst = sbufs + sb * a.sbuf;
         if (GU) {
           mbar_expect_tx(&bars->sfull[sb], uint32_t(2 * kRows * KS));
-          for (int m = 0; m < 2; ++m)
-            for (int bx = 0; bx < KS / 16; ++bx)
-              tma_load_2d(sdst + m * kRows * KS + bx * (kRows * 16), m ? (const void*)&ts1 : (const void*)&ts0,
-                          bx * 16, row, &bars->sfull[sb], pol_w);
+          if (a.sbox) {
+            for (int m = 0; m < 2; ++m)
+              for (int bx = 0; bx < KS / 16; ++bx)
+                tma_load_2d(sdst + m * kRows * KS + bx * (kRows * 16), m ? (const void*)&ts1 : (const void*)&ts0,
+                            bx * 16, row, &bars->sfull[sb], pol_w);
+          } else {
+            bulk_g2s(sdst, a.sa + (size_t)row * KS, uint32_t(kRows * KS), &bars->sfull[sb], pol_w);
+            bulk_g2s(sdst + kRows * KS, a.sb + (size_t)row * KS, uint32_t(kRows * KS), &bars->sfull[sb], pol_w);
+          }
         } else {
           mbar_expect_tx(&bars->sfull[sb], uint32_t(kRows * KS));
           bulk_g2s(sdst, a.sa + (size_t)row * KS, uint32_t(kRows * KS), &bars->sfull[sb], pol_w);
@@ -664,10 +671,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         int e_row = 8;
         if (a.fmt == 0) {
           uint32_t m = 0;
-          const uint8_t* rowp = sbase + mat * kRows * KS + r * 16;
-          for (int bx = 0; bx < KS / 16; ++bx) {
-            const uint4 v = *reinterpret_cast<const uint4*>(rowp + bx * (kRows * 16));
-            m = __vmaxu4(m, __vmaxu4(__vmaxu4(v.x, v.y), __vmaxu4(v.z, v.w)));
+          if (a.sbox) {
+            const uint8_t* rowp = sbase + mat * kRows * KS + r * 16;
+            for (int bx = 0; bx < KS / 16; ++bx) {
+              const uint4 v = *reinterpret_cast<const uint4*>(rowp + bx * (kRows * 16));
+              m = __vmaxu4(m, __vmaxu4(__vmaxu4(v.x, v.y), __vmaxu4(v.z, v.w)));
+            }
+          } else {
+            const uint8_t* rowp = sbase + mat * kRows * KS + r * KS;
+            for (int j = 0; j < KS; j += 4) m = __vmaxu4(m, *reinterpret_cast<const uint32_t*>(rowp + j));
           }
           smax = int(max(max(m & 0xFFu, (m >> 8) & 0xFFu), max((m >> 16) & 0xFFu, m >> 24)));
           e_row = smax - 140;
@@ -686,12 +698,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < NCH; ++j) wv[j] = *reinterpret_cast<const uint4*>(wt + 16 * ((ch0 + j) ^ sw));
         uint32_t sc;  // scale bytes of this thread's chunks, lowest chunk in the low byte(s)
         if (GU) {
-          if (a.fmt == 0)
-            sc = *reinterpret_cast<const uint16_t*>(sbase + mat * kRows * KS + (c >> 2) * (kRows * 16) + r * 16 +
-                                                    4 * (c & 3) + ch0);
-          else
-            sc = *reinterpret_cast<const uint32_t*>(sbase + mat * kRows * KS + (c >> 1) * (kRows * 16) + r * 16 +
-                                                    8 * (c & 1) + 2 * ch0);
+          // byte j of this row: 16-byte boxes ((j / 16) * 2048 + r * 16 + j % 16) or rows of KS bytes
+          const int j = a.fmt == 0 ? 4 * c + ch0 : 8 * c + 2 * ch0;
+          const uint8_t* sp = sbase + mat * kRows * KS + (a.sbox ? (j >> 4) * (kRows * 16) + r * 16 + (j & 15) : r * KS + j);
+          sc = a.fmt == 0 ? uint32_t(*reinterpret_cast<const uint16_t*>(sp)) : *reinterpret_cast<const uint32_t*>(sp);
         } else {
           if (a.fmt == 0)
             sc = sbase[r * KS + 4 * c + ch0];
@@ -971,7 +981,7 @@ extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_
   if (H <= 0 || I <= 0 || H % kRows || I % kRows) return QMTP_ERR_SHAPE;
   const int G = fmt == 0 ? 32 : 16;
   const int KS_gu = H / G, KS_dn = I / G;
-  if (KS_gu % 16) return QMTP_ERR_UNSUPPORTED;  // gate/up scales are staged in 16-byte TMA boxes
+  const int sbox = KS_gu % 16 == 0;  // gate/up scales in 16-byte TMA boxes (conflict-light reads), else rows
   const int sbuf_gu = (2 * kRows * KS_gu + 1023) & ~1023, sbuf_dn = (kRows * KS_dn + 1023) & ~1023;
   const int nw_gu = ring_stages<true>(sbuf_gu), nw_dn = ring_stages<false>(sbuf_dn);
   if (nw_gu < 2 || nw_dn < 2) return QMTP_ERR_UNSUPPORTED;
@@ -1000,9 +1010,10 @@ extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_
   CUtensorMap mg, mu, md, msg, msu;
   if (!weight_map(&mg, wg, (long long)E * I, H) || !weight_map(&mu, wu, (long long)E * I, H) ||
       !weight_map(&md, wd, (long long)E * H, I) ||
-      !byte_map(&msg, sg_, (long long)E * I, KS_gu, 16, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !byte_map(&msu, su_, (long long)E * I, KS_gu, 16, CU_TENSOR_MAP_SWIZZLE_NONE))
+      (sbox && (!byte_map(&msg, sg_, (long long)E * I, KS_gu, 16, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+                !byte_map(&msu, su_, (long long)E * I, KS_gu, 16, CU_TENSOR_MAP_SWIZZLE_NONE))))
     return QMTP_ERR_CUDA;
+  if (!sbox) msg = msu = mg;  // unused
 
   const int n = T * S;
   static std::once_flag once;
@@ -1017,9 +1028,10 @@ extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_
   QMTP_CUDA_TRY(launch_kernel(moe_gather_kernel, dim3(unsigned(L.max_tiles), kMaxTok / 8), dim3(256), 0, stream, x, H,
                               (const Tile*)tiles, (const int32_t*)counters, (const int32_t*)sorted_tok, ximg, xsh));
   const int grid = sm_count();
-  GemmArgs gu{nullptr, ximg, tiles, counters, xsh, himg, nullptr, H, I, KS_gu, fmt, limit, I, nw_gu, sbuf_gu, err};
+  GemmArgs gu{static_cast<const uint8_t*>(sg_), static_cast<const uint8_t*>(su_), ximg, tiles, counters, xsh, himg,
+              nullptr, H, I, KS_gu, fmt, limit, I, nw_gu, sbuf_gu, sbox, err};
   QMTP_CUDA_TRY(launch_gemm<true>(mg, mu, msg, msu, gu, grid, stream));
-  GemmArgs dn{sd, himg, tiles, counters, nullptr, nullptr, yp, I, H, KS_dn, fmt, limit, 0, nw_dn, sbuf_dn, err};
+  GemmArgs dn{sd, nullptr, himg, tiles, counters, nullptr, nullptr, yp, I, H, KS_dn, fmt, limit, 0, nw_dn, sbuf_dn, 0, err};
   QMTP_CUDA_TRY(launch_gemm<false>(md, md, md, md, dn, grid, stream));
   QMTP_CUDA_TRY(launch_kernel(moe_combine_kernel, dim3(unsigned(T), unsigned((H + 1023) / 1024)), dim3(256), 0, stream,
                               (const float*)yp, (const int32_t*)entry_pos, scores, S, H, y));
