@@ -48,7 +48,7 @@ constexpr int kChunk = 128;                  // K per pipeline stage
 constexpr int kMaxTok = 64;                  // entries per token tile (MMA N <= 64)
 constexpr int kWBytes = kRows * kChunk / 2;  // packed bytes of one 128 x 128 weight tile
 constexpr int kMaxW = 8;                     // weight ring stages (upper bound; chosen per launch)
-constexpr int kNB = 3;                       // operand-image ring stages
+constexpr int kNB = 4;                       // operand-image ring stages (= depth of the stage-done ring)
 constexpr int kDQ = 4;                       // dequantizing warps per TMEM lane quarter
 constexpr int kNDQ = 4 * kDQ;
 constexpr int kWarps = 4 + kNDQ + 4;         // 4 control warps, dequantizers, 4 epilogue warps
@@ -66,10 +66,13 @@ struct Cfg {
   static constexpr int NMAT = GU ? 2 : 1;
   static constexpr int WSTAGE = NMAT * kWBytes;
   static constexpr int BSTAGE = GU ? kMaxTok * 256 : kMaxTok * 512;  // operand-image bytes per stage
-  static constexpr int NA = GU ? 2 : 4;            // TMEM A stages
-  static constexpr int ACOLS = GU ? 128 : 64;      // TMEM columns of one A stage (all matrices)
-  static constexpr int ACC_STRIDE = GU ? 128 : 64;
-  static constexpr int A_BASE = 2 * ACC_STRIDE;    // accumulators double-buffered below the A stages
+  // TMEM: two accumulator buffers of 128 columns (gate | up, or the hi | lo halves of N = 2*nt for down),
+  // then four A slots of 64 columns (gate/up: one half-chunk of K = 64 per slot, 32 columns per matrix;
+  // down: one chunk of K = 128 per slot).
+  static constexpr int NA = 4;
+  static constexpr int ACOLS = 64;
+  static constexpr int ACC_STRIDE = 128;
+  static constexpr int A_BASE = 2 * ACC_STRIDE;
   static_assert(A_BASE + NA * ACOLS <= (int)kTmemCols, "TMEM budget");
 };
 
@@ -461,8 +464,9 @@ struct GemmArgs {
 
 struct Bars {
   uint64_t wfull[kMaxW], wempty[kMaxW];
-  uint64_t bfull[kNB], bempty[kNB];
-  uint64_t afull[4], aempty[4];
+  uint64_t bfull[kNB];
+  uint64_t sdone[kNB];  // stage done: all MMAs of K-chunk `it` completed (frees its operand slot and A slots)
+  uint64_t afull[4];
   uint64_t sfull[2], sempty[2];
   uint64_t accfull[2], accempty[2];
   uint64_t rsfull[2], rsempty[2];
@@ -472,10 +476,30 @@ struct Bars {
 };
 static_assert(sizeof(Bars) <= 512, "barrier block");
 
+__device__ __forceinline__ void umma_ts_first(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts_acc(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 1, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc)
+      : "memory");
+}
+
 // Warp roles: 0 weight/scale producer, 1 MMA issuer, 2 operand-image producer, 3 idle,
 // 4 .. 4+kNDQ-1 dequantizers (lane quarter dw & 3, sub-task dw >> 2), last 4 epilogue.
-// Gate/up (GU): f16 MMA; dequantizer sub-task = (matrix, half of the 4 32-element chunks of a stage).
-// Down: bf16 MMA; sub-task = one chunk.
+// Pacing: the MMA issuer is the critical resource (a kind::f16 MMA costs ~45 cycles for N <= 64), so
+// everything else runs ahead of it: the weight ring by up to nw chunks, the operand ring by kNB chunks,
+// and the dequantizers by two chunks (gate/up: K-chunk `it` uses A slots 2*(it%2) + {0,1}, one per half
+// of K, and is written once chunk it-2 is done; down: chunk `it` uses slot it%4, written once chunk it-4
+// is done).  One commit per chunk (sdone) releases both its operand slot and its A slots.
+// Gate/up: f16 MMA, dequantizer sub-task = (matrix, chunk j of each K half).  Down: bf16 MMA with
+// N = 2*nt (hi rows then lo rows of h), sub-task = one 32-element chunk.
 template <bool GU>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tw0, const __grid_constant__ CUtensorMap tw1,
@@ -500,12 +524,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < kNB; ++s) {
       mbar_init(&bars->bfull[s], 1);
-      mbar_init(&bars->bempty[s], 1);
+      mbar_init(&bars->sdone[s], 1);
     }
-    for (int s = 0; s < C::NA; ++s) {
-      mbar_init(&bars->afull[s], kNDQ);
-      mbar_init(&bars->aempty[s], 1);
-    }
+    for (int s = 0; s < C::NA; ++s) mbar_init(&bars->afull[s], kNDQ);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->sfull[s], 1);
       mbar_init(&bars->sempty[s], kNDQ);
@@ -531,6 +552,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total = a.counters[0] * RT;
   const int nchunk = a.K / kChunk;
   const int KS = a.KS;
+  // chunk j done <=> phase (j / kNB) of sdone[j % kNB] completed
+  auto wait_done = [&](int j) -> bool {
+    return j < 0 || mbar_wait_sleep(&bars->sdone[j % kNB], (j / kNB) & 1, err, kWaitPolls);
+  };
 
   if (warp == 0) {
     // ----------------------------------------------------------------- weight + scale producer
@@ -592,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* bsrc = a.bimg + (size_t)tl.row0 * a.K * (GU ? 2 : 4);
         for (int c = 0; c < nchunk; ++c, ++it) {
           const int s = it % kNB;
-          if (*abort_flag || !mbar_wait_sleep(&bars->bempty[s], ((it / kNB) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
+          if (*abort_flag || !wait_done(it - kNB)) { ok = false; break; }
           mbar_expect_tx(&bars->bfull[s], bbytes);
           bulk_g2s(bring + s * C::BSTAGE, bsrc + (size_t)c * bbytes, bbytes, &bars->bfull[s], pol_b);
         }
@@ -613,34 +638,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lu) {
         const Tile tl = a.tiles[u / RT];
         const int d = lu & 1;
-        const uint32_t idesc = GU ? umma_idesc_f16(128, tl.nt) : umma_idesc_bf16(128, tl.nt);
-        const uint32_t lbo = uint32_t(tl.nt / 8) * 128u;
+        const int N = GU ? tl.nt : 2 * tl.nt;
+        const uint32_t idesc = GU ? umma_idesc_f16(128, N) : umma_idesc_bf16(128, N);
+        const uint32_t lbo = uint32_t(N / 8) * 128u;
         if (*abort_flag || !(ok = mbar_wait_sleep(&bars->accempty[d], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
         tc_fence_after();
         const uint32_t dacc = tmem + uint32_t(d * C::ACC_STRIDE);
         for (int c = 0; c < nchunk; ++c, ++it) {
-          const int s = it % kNB, ap = it % C::NA;
-          if (*abort_flag || !mbar_wait_sleep(&bars->bfull[s], (it / kNB) & 1, err, kWaitPolls) ||
-              !mbar_wait_sleep(&bars->afull[ap], (it / C::NA) & 1, err, kWaitPolls)) { ok = false; break; }
-          tc_fence_after();
+          const int s = it % kNB;
+          if (*abort_flag || !mbar_wait_sleep(&bars->bfull[s], (it / kNB) & 1, err, kWaitPolls)) { ok = false; break; }
           const uint32_t sB = smem_u32(bring + s * C::BSTAGE);
-          const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS);
+          if (GU) {
+            for (int h = 0; h < 2; ++h) {
+              const int ai = 2 * it + h, ap = ai % C::NA;
+              if (!mbar_wait_sleep(&bars->afull[ap], (ai / C::NA) & 1, err, kWaitPolls)) { ok = false; break; }
+              tc_fence_after();
+              const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS);
 #pragma unroll
-          for (int ks = 0; ks < kChunk / 16; ++ks) {
-            const uint32_t acc = (c | ks) != 0;
-            const uint64_t bd = umma_desc(sB + uint32_t(ks) * 2u * lbo, lbo, 128u);
-            if (GU) {
-              umma_bf16_ts(dacc, aA + ks * 8, bd, idesc, acc);
-              umma_bf16_ts(dacc + 64, aA + 64 + ks * 8, bd, idesc, acc);
-            } else {
-              const uint64_t bl = umma_desc(sB + uint32_t(tl.nt) * 256u + uint32_t(ks) * 2u * lbo, lbo, 128u);
-              umma_bf16_ts(dacc, aA + ks * 8, bd, idesc, acc);
-              umma_bf16_ts(dacc, aA + ks * 8, bl, idesc, 1u);
+              for (int j = 0; j < 4; ++j) {
+                const uint64_t bd = umma_desc(sB + uint32_t(4 * h + j) * 2u * lbo, lbo, 128u);
+                if (c == 0 && h == 0 && j == 0) {
+                  umma_ts_first(dacc, aA, bd, idesc);
+                  umma_ts_first(dacc + 64, aA + 32, bd, idesc);
+                } else {
+                  umma_ts_acc(dacc, aA + j * 8, bd, idesc);
+                  umma_ts_acc(dacc + 64, aA + 32 + j * 8, bd, idesc);
+                }
+              }
+            }
+            if (!ok) break;
+          } else {
+            const int ap = it % C::NA;
+            if (!mbar_wait_sleep(&bars->afull[ap], (it / C::NA) & 1, err, kWaitPolls)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS);
+#pragma unroll
+            for (int ks = 0; ks < kChunk / 16; ++ks) {
+              const uint64_t bd = umma_desc(sB + uint32_t(ks) * 2u * lbo, lbo, 128u);
+              if (c == 0 && ks == 0)
+                umma_ts_first(dacc, aA, bd, idesc);
+              else
+                umma_ts_acc(dacc, aA + ks * 8, bd, idesc);
             }
           }
           issued = true;
-          umma_commit(&bars->bempty[s]);
-          umma_commit(&bars->aempty[ap]);
+          umma_commit(&bars->sdone[s]);
           if (c == nchunk - 1) umma_commit(&bars->accfull[d]);
         }
       }
@@ -654,8 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ----------------------------------------------------------------- dequantizers
     const int dw = warp - 4, q = dw & 3, sub = dw >> 2;
     const int mat = GU ? sub >> 1 : 0;
-    const int ch0 = GU ? 2 * (sub & 1) : sub;  // first 32-element chunk of the stage handled here
-    constexpr int NCH = GU ? 2 : 1;
+    const int jj = sub & 1;  // gate/up: chunk jj of each K half (chunks jj and 2 + jj of the stage)
     const int r = q * 32 + lane;
     const int sw = (r >> 1) & 3;
     const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
@@ -685,78 +726,101 @@ __global__ void __launch_bounds__(kThreads, 1)
           e_row = smax - 140;
         }
         if (!mbar_wait_sleep(&bars->rsempty[d], ((lu >> 1) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
-        if ((sub & 1) == 0) rsx[(d * 2 + mat) * kRows + r] = e_row;
+        if (jj == 0) rsx[(d * 2 + mat) * kRows + r] = e_row;
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->rsfull[d]);
       }
       for (int c = 0; c < nchunk; ++c, ++it) {
-        const int s = it % NW, ap = it % C::NA;
+        const int s = it % NW;
         if (*abort_flag || !mbar_wait_sleep(&bars->wfull[s], (it / NW) & 1, err, kWaitPolls)) { ok = false; break; }
         const uint8_t* wt = wring + s * C::WSTAGE + mat * kWBytes + r * 64;
-        uint4 wv[NCH];
-#pragma unroll
-        for (int j = 0; j < NCH; ++j) wv[j] = *reinterpret_cast<const uint4*>(wt + 16 * ((ch0 + j) ^ sw));
-        uint32_t sc;  // scale bytes of this thread's chunks, lowest chunk in the low byte(s)
         if (GU) {
-          // byte j of this row: 16-byte boxes ((j / 16) * 2048 + r * 16 + j % 16) or rows of KS bytes
-          const int j = a.fmt == 0 ? 4 * c + ch0 : 8 * c + 2 * ch0;
-          const uint8_t* sp = sbase + mat * kRows * KS + (a.sbox ? (j >> 4) * (kRows * 16) + r * 16 + (j & 15) : r * KS + j);
-          sc = a.fmt == 0 ? uint32_t(*reinterpret_cast<const uint16_t*>(sp)) : *reinterpret_cast<const uint32_t*>(sp);
-        } else {
-          if (a.fmt == 0)
-            sc = sbase[r * KS + 4 * c + ch0];
-          else
-            sc = *reinterpret_cast<const uint16_t*>(sbase + r * KS + 8 * c + 2 * ch0);
-        }
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&bars->wempty[s]);
-          if (c == nchunk - 1) mbar_arrive(&bars->sempty[sb]);
-        }
-        if (!mbar_wait_sleep(&bars->aempty[ap], ((it / C::NA) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
-        tc_fence_after();
+          const uint4 w0 = *reinterpret_cast<const uint4*>(wt + 16 * (jj ^ sw));
+          const uint4 w1 = *reinterpret_cast<const uint4*>(wt + 16 * ((2 + jj) ^ sw));
+          // this row's scale bytes of the stage: MXFP4 4 (one per chunk), NVFP4 8 (two per chunk)
+          const int j0 = a.fmt == 0 ? 4 * c : 8 * c;
+          const uint8_t* sp = sbase + mat * kRows * KS + (a.sbox ? (j0 >> 4) * (kRows * 16) + r * 16 + (j0 & 15) : r * KS + j0);
+          uint32_t s0, s1;
+          if (a.fmt == 0) {
+            s0 = *reinterpret_cast<const uint32_t*>(sp);
+            s1 = 0;
+          } else {
+            const uint2 t2 = *reinterpret_cast<const uint2*>(sp);
+            s0 = t2.x;
+            s1 = t2.y;
+          }
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&bars->wempty[s]);
+            if (c == nchunk - 1) mbar_arrive(&bars->sempty[sb]);
+          }
+          if (!wait_done(it - 2)) { ok = false; break; }  // A slots of chunk it-2 are free again
+          tc_fence_after();
 #pragma unroll
-        for (int j = 0; j < NCH; ++j) {
-          uint32_t out[16];
-          if (GU) {
+          for (int h = 0; h < 2; ++h) {
+            const int ch = 2 * h + jj;
+            const uint4 wv = h ? w1 : w0;
             uint32_t m0, m1;
             if (a.fmt == 0) {
-              m0 = m1 = mult_mx_f16((sc >> (8 * j)) & 0xFFu, smax);
+              m0 = m1 = mult_mx_f16((s0 >> (8 * ch)) & 0xFFu, smax);
             } else {
-              m0 = mult_nv_f16((sc >> (16 * j)) & 0xFFu);
-              m1 = mult_nv_f16((sc >> (16 * j + 8)) & 0xFFu);
+              const uint32_t sw2 = ch < 2 ? s0 : s1;
+              m0 = mult_nv_f16((sw2 >> (16 * (ch & 1))) & 0xFFu);
+              m1 = mult_nv_f16((sw2 >> (16 * (ch & 1) + 8)) & 0xFFu);
             }
-            fp4_word_f16(wv[j].x, m0, out);
-            fp4_word_f16(wv[j].y, m0, out + 4);
-            fp4_word_f16(wv[j].z, m1, out + 8);
-            fp4_word_f16(wv[j].w, m1, out + 12);
-            tmem_st16(lane_base + uint32_t(C::A_BASE + ap * C::ACOLS + mat * 64 + (ch0 + j) * 16), out);
-          } else {
-            Mult m0, m1;
-            if (a.fmt == 0) {
-              m0 = m1 = mult_e8m0(sc & 0xFFu);
-            } else {
-              m0 = mult_e4m3(sc & 0xFFu);
-              m1 = mult_e4m3((sc >> 8) & 0xFFu);
-            }
-            if (!__any_sync(0xFFFFFFFFu, m0.slow || m1.slow)) {
-              fp4_word_fast(wv[j].x, m0.m, out);
-              fp4_word_fast(wv[j].y, m0.m, out + 4);
-              fp4_word_fast(wv[j].z, m1.m, out + 8);
-              fp4_word_fast(wv[j].w, m1.m, out + 12);
-            } else {
-              fp4_word_wide(wv[j].x, m0.m2, out);
-              fp4_word_wide(wv[j].y, m0.m2, out + 4);
-              fp4_word_wide(wv[j].z, m1.m2, out + 8);
-              fp4_word_wide(wv[j].w, m1.m2, out + 12);
-            }
-            tmem_st16(lane_base + uint32_t(C::A_BASE + ap * C::ACOLS + (ch0 + j) * 16), out);
+            uint32_t out[16];
+            fp4_word_f16(wv.x, m0, out);
+            fp4_word_f16(wv.y, m0, out + 4);
+            fp4_word_f16(wv.z, m1, out + 8);
+            fp4_word_f16(wv.w, m1, out + 12);
+            const int ap = (2 * it + h) % C::NA;
+            tmem_st16(lane_base + uint32_t(C::A_BASE + ap * C::ACOLS + mat * 32 + jj * 16), out);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->afull[ap]);
           }
+        } else {
+          const int ch = sub;
+          const uint4 wv = *reinterpret_cast<const uint4*>(wt + 16 * (ch ^ sw));
+          uint32_t sc;
+          if (a.fmt == 0)
+            sc = sbase[r * KS + 4 * c + ch];
+          else
+            sc = *reinterpret_cast<const uint16_t*>(sbase + r * KS + 8 * c + 2 * ch);
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&bars->wempty[s]);
+            if (c == nchunk - 1) mbar_arrive(&bars->sempty[sb]);
+          }
+          if (!wait_done(it - C::NA)) { ok = false; break; }  // A slot of chunk it-4 is free again
+          tc_fence_after();
+          Mult m0, m1;
+          if (a.fmt == 0) {
+            m0 = m1 = mult_e8m0(sc & 0xFFu);
+          } else {
+            m0 = mult_e4m3(sc & 0xFFu);
+            m1 = mult_e4m3((sc >> 8) & 0xFFu);
+          }
+          uint32_t out[16];
+          if (!__any_sync(0xFFFFFFFFu, m0.slow || m1.slow)) {
+            fp4_word_fast(wv.x, m0.m, out);
+            fp4_word_fast(wv.y, m0.m, out + 4);
+            fp4_word_fast(wv.z, m1.m, out + 8);
+            fp4_word_fast(wv.w, m1.m, out + 12);
+          } else {
+            fp4_word_wide(wv.x, m0.m2, out);
+            fp4_word_wide(wv.y, m0.m2, out + 4);
+            fp4_word_wide(wv.z, m1.m2, out + 8);
+            fp4_word_wide(wv.w, m1.m2, out + 12);
+          }
+          const int ap = it % C::NA;
+          tmem_st16(lane_base + uint32_t(C::A_BASE + ap * C::ACOLS + ch * 16), out);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->afull[ap]);
         }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->afull[ap]);
       }
     }
     if (!ok) *abort_flag = 1;
@@ -776,10 +840,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (GU) {
         const float fg = ldexpf(1.0f, rsx[(d * 2 + 0) * kRows + r]);
         const float fu = ldexpf(1.0f, rsx[(d * 2 + 1) * kRows + r]);
-        // this row is k = rt*128 + r of the down GEMM: chunk rt, permuted position p
+        // this row is k = rt*128 + r of the down GEMM: chunk rt, permuted position p; the down operand
+        // chunk is [2*nt x 128]: rows 0..nt-1 carry hi(h), rows nt..2nt-1 carry lo(h)
         const int p = (r & ~7) | perm8(r & 7);
-        const int nt8 = tl.nt >> 3;
-        uint8_t* hb = a.himg + (size_t)tl.row0 * a.h_rows * 4 + (size_t)rt * tl.nt * 512;
+        const int n8 = (2 * tl.nt) >> 3;
+        uint8_t* hb = a.himg + (size_t)tl.row0 * a.h_rows * 4 + (size_t)rt * tl.nt * 512 + (p >> 3) * n8 * 128 + (p & 7) * 2;
         for (int cg = 0; cg < tl.nt / 16; ++cg) {
           uint32_t g[16], v[16];
           tmem_ld16(dacc + uint32_t(cg * 16), g);
@@ -797,21 +862,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const uint16_t hi = f2bf(hv);
             const uint16_t lo = f2bf(__fsub_rn(hv, bf2f(hi)));
-            const int off = ((p >> 3) * nt8 + (n >> 3)) * 128 + (n & 7) * 16 + (p & 7) * 2;
-            *reinterpret_cast<uint16_t*>(hb + off) = hi;
-            *reinterpret_cast<uint16_t*>(hb + tl.nt * 256 + off) = lo;
+            const int rl = n + tl.nt;
+            *reinterpret_cast<uint16_t*>(hb + (n >> 3) * 128 + (n & 7) * 16) = hi;
+            *reinterpret_cast<uint16_t*>(hb + (rl >> 3) * 128 + (rl & 7) * 16) = lo;
           }
         }
       } else {
         float* yrow = a.yp + (size_t)tl.entry0 * a.R + rt * kRows + r;
         for (int cg = 0; cg < tl.nt / 16; ++cg) {
-          uint32_t v[16];
-          tmem_ld16(dacc + uint32_t(cg * 16), v);
+          uint32_t vh[16], vl[16];
+          tmem_ld16(dacc + uint32_t(cg * 16), vh);
+          tmem_ld16(dacc + uint32_t(tl.nt + cg * 16), vl);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int n = cg * 16 + i;
-            if (n < tl.ntok) yrow[(size_t)n * a.R] = __uint_as_float(v[i]);
+            if (n < tl.ntok) yrow[(size_t)n * a.R] = __fadd_rn(__uint_as_float(vh[i]), __uint_as_float(vl[i]));
           }
         }
       }
