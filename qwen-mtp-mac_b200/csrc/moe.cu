@@ -476,28 +476,30 @@ struct Bars {
 };
 static_assert(sizeof(Bars) <= 512, "barrier block");
 
+// MMA issue without a "memory" clobber: the operands are ordered by the barrier waits (volatile asm with
+// clobbers) and tcgen05 fences around the issue loop; a clobber here would make the compiler reload
+// values from memory between consecutive MMAs and roughly double the issue time.
 __device__ __forceinline__ void umma_ts_first(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 0, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-      "r"(a), "l"(b), "r"(idesc)
-      : "memory");
+      "r"(a), "l"(b), "r"(idesc));
 }
 __device__ __forceinline__ void umma_ts_acc(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 1, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-      "r"(a), "l"(b), "r"(idesc)
-      : "memory");
+      "r"(a), "l"(b), "r"(idesc));
 }
 
-// Warp roles: 0 weight/scale producer, 1 MMA issuer, 2 operand-image producer, 3 idle,
+// Warp roles: 0 weight/scale producer, 1 and 3 MMA issuers, 2 operand-image producer,
 // 4 .. 4+kNDQ-1 dequantizers (lane quarter dw & 3, sub-task dw >> 2), last 4 epilogue.
-// Pacing: the MMA issuer is the critical resource (a kind::f16 MMA costs ~45 cycles for N <= 64), so
-// everything else runs ahead of it: the weight ring by up to nw chunks, the operand ring by kNB chunks,
+// Pacing: MMA issue is the critical resource (a kind::f16 MMA costs its issuing thread ~50 cycles for
+// N <= 64, whatever the operand sizes; two issuing threads double the rate), so everything else runs
+// ahead of it: the weight ring by up to nw chunks, the operand ring by kNB chunks,
 // and the dequantizers by two chunks (gate/up: K-chunk `it` uses A slots 2*(it%2) + {0,1}, one per half
 // of K, and is written once chunk it-2 is done; down: chunk `it` uses slot it%4, written once chunk it-4
-// is done).  One commit per chunk (sdone) releases both its operand slot and its A slots.
+// is done).  One commit per chunk and issuer (sdone, count 2) releases its operand slot and A slots.
 // Gate/up: f16 MMA, dequantizer sub-task = (matrix, chunk j of each K half).  Down: bf16 MMA with
 // N = 2*nt (hi rows then lo rows of h), sub-task = one 32-element chunk.
 template <bool GU>
@@ -524,18 +526,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < kNB; ++s) {
       mbar_init(&bars->bfull[s], 1);
-      mbar_init(&bars->sdone[s], 1);
+      mbar_init(&bars->sdone[s], 2);  // one commit from each MMA issuer
     }
     for (int s = 0; s < C::NA; ++s) mbar_init(&bars->afull[s], kNDQ);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->sfull[s], 1);
       mbar_init(&bars->sempty[s], kNDQ);
-      mbar_init(&bars->accfull[s], 1);
+      mbar_init(&bars->accfull[s], 2);
       mbar_init(&bars->accempty[s], 4);
       mbar_init(&bars->rsfull[s], kNDQ);
       mbar_init(&bars->rsempty[s], 4);
     }
-    mbar_init(&bars->drain, 1);
+    mbar_init(&bars->drain, 2);
     bars->abort = 0;
     fence_mbar_init();
   }
@@ -630,41 +632,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    // ----------------------------------------------------------------- MMA issuer
+  } else if (warp == 1 || warp == 3) {
+    // ----------------------------------------------------------------- MMA issuers
+    // A tcgen05.mma costs its issuing thread ~50 cycles, so two threads on different schedulers issue:
+    // gate/up: issuer 0 the gate MMAs, issuer 1 the up MMAs; down: issuer 0 multiplies by the hi rows of
+    // the operand chunk, issuer 1 by the lo rows, into the two halves of the accumulator.
     if (lane == 0) {
+      const int iss = warp == 1 ? 0 : 1;
       int it = 0, lu = 0;
       bool ok = true, issued = false;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lu) {
         const Tile tl = a.tiles[u / RT];
         const int d = lu & 1;
-        const int N = GU ? tl.nt : 2 * tl.nt;
-        const uint32_t idesc = GU ? umma_idesc_f16(128, N) : umma_idesc_bf16(128, N);
-        const uint32_t lbo = uint32_t(N / 8) * 128u;
+        const int nt = tl.nt;
+        const uint32_t idesc = GU ? umma_idesc_f16(128, nt) : umma_idesc_bf16(128, nt);
+        // K-direction stride of the operand chunk: nt rows (gate/up) or 2*nt rows (down, hi then lo)
+        const uint32_t lbo = uint32_t((GU ? nt : 2 * nt) / 8) * 128u;
+        const uint32_t boff = GU ? 0u : uint32_t(iss * (nt / 8) * 128);
         if (*abort_flag || !(ok = mbar_wait_sleep(&bars->accempty[d], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
         tc_fence_after();
-        const uint32_t dacc = tmem + uint32_t(d * C::ACC_STRIDE);
+        const uint32_t dacc = tmem + uint32_t(d * C::ACC_STRIDE + (GU ? iss * 64 : iss * nt));
         for (int c = 0; c < nchunk; ++c, ++it) {
           const int s = it % kNB;
           if (*abort_flag || !mbar_wait_sleep(&bars->bfull[s], (it / kNB) & 1, err, kWaitPolls)) { ok = false; break; }
-          const uint32_t sB = smem_u32(bring + s * C::BSTAGE);
+          // descriptor of k-step 0 of this issuer's operand rows; k-step ks starts ks * 2 * lbo bytes later
+          // (the start-address field holds address / 16 and stays below 2^14 for every smem address)
+          const uint64_t bd0 = umma_desc(smem_u32(bring + s * C::BSTAGE) + boff, lbo, 128u);
+          const uint64_t kstep = uint64_t((2u * lbo) >> 4);
           if (GU) {
             for (int h = 0; h < 2; ++h) {
               const int ai = 2 * it + h, ap = ai % C::NA;
               if (!mbar_wait_sleep(&bars->afull[ap], (ai / C::NA) & 1, err, kWaitPolls)) { ok = false; break; }
               tc_fence_after();
-              const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint64_t bd = umma_desc(sB + uint32_t(4 * h + j) * 2u * lbo, lbo, 128u);
-                if (c == 0 && h == 0 && j == 0) {
-                  umma_ts_first(dacc, aA, bd, idesc);
-                  umma_ts_first(dacc + 64, aA + 32, bd, idesc);
-                } else {
-                  umma_ts_acc(dacc, aA + j * 8, bd, idesc);
-                  umma_ts_acc(dacc + 64, aA + 32 + j * 8, bd, idesc);
-                }
-              }
+              const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS + iss * 32);
+              const uint64_t bh = bd0 + uint64_t(4 * h) * kstep;
+              if (c == 0 && h == 0)
+                umma_ts_first(dacc, aA, bh, idesc);
+              else
+                umma_ts_acc(dacc, aA, bh, idesc);
+              umma_ts_acc(dacc, aA + 8, bh + kstep, idesc);
+              umma_ts_acc(dacc, aA + 16, bh + 2 * kstep, idesc);
+              umma_ts_acc(dacc, aA + 24, bh + 3 * kstep, idesc);
             }
             if (!ok) break;
           } else {
@@ -672,14 +680,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait_sleep(&bars->afull[ap], (it / C::NA) & 1, err, kWaitPolls)) { ok = false; break; }
             tc_fence_after();
             const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS);
+            if (c == 0)
+              umma_ts_first(dacc, aA, bd0, idesc);
+            else
+              umma_ts_acc(dacc, aA, bd0, idesc);
 #pragma unroll
-            for (int ks = 0; ks < kChunk / 16; ++ks) {
-              const uint64_t bd = umma_desc(sB + uint32_t(ks) * 2u * lbo, lbo, 128u);
-              if (c == 0 && ks == 0)
-                umma_ts_first(dacc, aA, bd, idesc);
-              else
-                umma_ts_acc(dacc, aA + ks * 8, bd, idesc);
-            }
+            for (int ks = 1; ks < kChunk / 16; ++ks) umma_ts_acc(dacc, aA + ks * 8, bd0 + uint64_t(ks) * kstep, idesc);
           }
           issued = true;
           umma_commit(&bars->sdone[s]);
@@ -687,10 +693,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) *abort_flag = 1;
-      if (issued) {  // every MMA issued has completed before TMEM is released
-        umma_commit(&bars->drain);
-        mbar_wait_sleep(&bars->drain, 0, err, kWaitPolls);
-      }
+      // every MMA issued has completed before TMEM is released (both issuers arrive on `drain`)
+      if (issued) umma_commit(&bars->drain);
+      else mbar_arrive(&bars->drain);
+      mbar_wait_sleep(&bars->drain, 0, err, kWaitPolls);
     }
   } else if (warp >= 4 && warp < 4 + kNDQ) {
     // ----------------------------------------------------------------- dequantizers
