@@ -287,6 +287,26 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
   return false;
 }
 
+// Bounded wait with back-off: a failed poll puts the thread to sleep for about `ns` nanoseconds, so
+// warps that run ahead of the critical one take no issue slots while they wait.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, unsigned* err, uint32_t ns,
+                                                  uint32_t limit = (1u << 22)) {
+  for (uint32_t it = 0; it < limit; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    __nanosleep(ns);
+  }
+  if (err) atomicOr(err, DEVERR_TIMEOUT);
+  return false;
+}
+// Bounded tight wait for the thread on the critical path (no sleep between polls).
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, unsigned* err,
+                                               uint32_t limit = (1u << 26)) {
+  for (uint32_t it = 0; it < limit; ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  if (err) atomicOr(err, DEVERR_TIMEOUT);
+  return false;
+}
+
 // ----------------------------------------------------------------------------- loads
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 r;

@@ -556,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int KS = a.KS;
   // chunk j done <=> phase (j / kNB) of sdone[j % kNB] completed
   auto wait_done = [&](int j) -> bool {
-    return j < 0 || mbar_wait_sleep(&bars->sdone[j % kNB], (j / kNB) & 1, err, kWaitPolls);
+    return j < 0 || mbar_wait_backoff(&bars->sdone[j % kNB], (j / kNB) & 1, err, 64);
   };
 
   if (warp == 0) {
@@ -569,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Tile tl = a.tiles[u / RT];
         const int row = tl.expert * a.R + (u % RT) * kRows;
         const int sb = lu & 1;
-        if (*abort_flag || !(ok = mbar_wait_sleep(&bars->sempty[sb], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
+        if (*abort_flag || !(ok = mbar_wait_backoff(&bars->sempty[sb], ((lu >> 1) & 1) ^ 1, err, 128))) break;
         uint8_t* sdst = sbufs + sb * a.sbuf;
         if (GU) {
           mbar_expect_tx(&bars->sfull[sb], uint32_t(2 * kRows * KS));
@@ -588,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int c = 0; c < nchunk; ++c, ++it) {
           const int s = it % NW;
-          if (*abort_flag || !mbar_wait_sleep(&bars->wempty[s], ((it / NW) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
+          if (*abort_flag || !mbar_wait_backoff(&bars->wempty[s], ((it / NW) & 1) ^ 1, err, 128)) { ok = false; break; }
           uint8_t* st = wring + s * C::WSTAGE;
           mbar_expect_tx(&bars->wfull[s], uint32_t(C::WSTAGE));
           tma_load_2d(st, &tw0, c * (kChunk / 2), row, &bars->wfull[s], pol_w);
@@ -599,11 +599,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
         for (int k = 1; k <= NW && it - k >= 0; ++k) {
           const int j = it - k;
-          mbar_wait_sleep(&bars->wfull[j % NW], (j / NW) & 1, err, kWaitPolls);
+          mbar_wait_backoff(&bars->wfull[j % NW], (j / NW) & 1, err, 128);
         }
         for (int k = 1; k <= 2 && lu - k >= 0; ++k) {
           const int j = lu - k;
-          mbar_wait_sleep(&bars->sfull[j & 1], (j >> 1) & 1, err, kWaitPolls);
+          mbar_wait_backoff(&bars->sfull[j & 1], (j >> 1) & 1, err, 128);
         }
       }
     }
@@ -628,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
         for (int k = 1; k <= kNB && it - k >= 0; ++k) {
           const int j = it - k;
-          mbar_wait_sleep(&bars->bfull[j % kNB], (j / kNB) & 1, err, kWaitPolls);
+          mbar_wait_backoff(&bars->bfull[j % kNB], (j / kNB) & 1, err, 128);
         }
       }
     }
@@ -649,12 +649,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // K-direction stride of the operand chunk: nt rows (gate/up) or 2*nt rows (down, hi then lo)
         const uint32_t lbo = uint32_t((GU ? nt : 2 * nt) / 8) * 128u;
         const uint32_t boff = GU ? 0u : uint32_t(iss * (nt / 8) * 128);
-        if (*abort_flag || !(ok = mbar_wait_sleep(&bars->accempty[d], ((lu >> 1) & 1) ^ 1, err, kWaitPolls))) break;
+        if (*abort_flag || !(ok = mbar_wait_backoff(&bars->accempty[d], ((lu >> 1) & 1) ^ 1, err, 32))) break;
         tc_fence_after();
         const uint32_t dacc = tmem + uint32_t(d * C::ACC_STRIDE + (GU ? iss * 64 : iss * nt));
         for (int c = 0; c < nchunk; ++c, ++it) {
           const int s = it % kNB;
-          if (*abort_flag || !mbar_wait_sleep(&bars->bfull[s], (it / kNB) & 1, err, kWaitPolls)) { ok = false; break; }
+          if (*abort_flag || !mbar_wait_spin(&bars->bfull[s], (it / kNB) & 1, err)) { ok = false; break; }
           // descriptor of k-step 0 of this issuer's operand rows; k-step ks starts ks * 2 * lbo bytes later
           // (the start-address field holds address / 16 and stays below 2^14 for every smem address)
           const uint64_t bd0 = umma_desc(smem_u32(bring + s * C::BSTAGE) + boff, lbo, 128u);
@@ -662,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (GU) {
             for (int h = 0; h < 2; ++h) {
               const int ai = 2 * it + h, ap = ai % C::NA;
-              if (!mbar_wait_sleep(&bars->afull[ap], (ai / C::NA) & 1, err, kWaitPolls)) { ok = false; break; }
+              if (!mbar_wait_spin(&bars->afull[ap], (ai / C::NA) & 1, err)) { ok = false; break; }
               tc_fence_after();
               const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS + iss * 32);
               const uint64_t bh = bd0 + uint64_t(4 * h) * kstep;
@@ -677,7 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
           } else {
             const int ap = it % C::NA;
-            if (!mbar_wait_sleep(&bars->afull[ap], (it / C::NA) & 1, err, kWaitPolls)) { ok = false; break; }
+            if (!mbar_wait_spin(&bars->afull[ap], (it / C::NA) & 1, err)) { ok = false; break; }
             tc_fence_after();
             const uint32_t aA = tmem + uint32_t(C::A_BASE + ap * C::ACOLS);
             if (c == 0)
@@ -696,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // every MMA issued has completed before TMEM is released (both issuers arrive on `drain`)
       if (issued) umma_commit(&bars->drain);
       else mbar_arrive(&bars->drain);
-      mbar_wait_sleep(&bars->drain, 0, err, kWaitPolls);
+      mbar_wait_backoff(&bars->drain, 0, err, 64);
     }
   } else if (warp >= 4 && warp < 4 + kNDQ) {
     // ----------------------------------------------------------------- dequantizers
@@ -710,7 +710,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lu) {
       const int sb = lu & 1, d = lu & 1;
-      if (*abort_flag || !mbar_wait_sleep(&bars->sfull[sb], (lu >> 1) & 1, err, kWaitPolls)) { ok = false; break; }
+      if (*abort_flag || !mbar_wait_backoff(&bars->sfull[sb], (lu >> 1) & 1, err, 64)) { ok = false; break; }
       const uint8_t* sbase = sbufs + sb * a.sbuf;
       int smax = 0;
       if (GU) {
@@ -731,14 +731,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           smax = int(max(max(m & 0xFFu, (m >> 8) & 0xFFu), max((m >> 16) & 0xFFu, m >> 24)));
           e_row = smax - 140;
         }
-        if (!mbar_wait_sleep(&bars->rsempty[d], ((lu >> 1) & 1) ^ 1, err, kWaitPolls)) { ok = false; break; }
+        if (!mbar_wait_backoff(&bars->rsempty[d], ((lu >> 1) & 1) ^ 1, err, 64)) { ok = false; break; }
         if (jj == 0) rsx[(d * 2 + mat) * kRows + r] = e_row;
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->rsfull[d]);
       }
       for (int c = 0; c < nchunk; ++c, ++it) {
         const int s = it % NW;
-        if (*abort_flag || !mbar_wait_sleep(&bars->wfull[s], (it / NW) & 1, err, kWaitPolls)) { ok = false; break; }
+        if (*abort_flag || !mbar_wait_backoff(&bars->wfull[s], (it / NW) & 1, err, 64)) { ok = false; break; }
         const uint8_t* wt = wring + s * C::WSTAGE + mat * kWBytes + r * 64;
         if (GU) {
           const uint4 w0 = *reinterpret_cast<const uint4*>(wt + 16 * (jj ^ sw));
@@ -839,8 +839,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Tile tl = a.tiles[u / RT];
       const int rt = u % RT;
       const int d = lu & 1;
-      if (*abort_flag || !mbar_wait_sleep(&bars->accfull[d], (lu >> 1) & 1, err, kWaitPolls)) { *abort_flag = 1; break; }
-      if (GU && !mbar_wait_sleep(&bars->rsfull[d], (lu >> 1) & 1, err, kWaitPolls)) { *abort_flag = 1; break; }
+      if (*abort_flag || !mbar_wait_backoff(&bars->accfull[d], (lu >> 1) & 1, err, 256)) { *abort_flag = 1; break; }
+      if (GU && !mbar_wait_backoff(&bars->rsfull[d], (lu >> 1) & 1, err, 256)) { *abort_flag = 1; break; }
       tc_fence_after();
       const uint32_t dacc = lane_base + uint32_t(d * C::ACC_STRIDE);
       if (GU) {
