@@ -374,6 +374,67 @@ def run_kernel(args):
                       "device_error": _lib.device_error()}), flush=True)
 
 
+def run_moe_ep(args):
+    """Config 5 expert-parallel over WORLD_SIZE GPUs (launched by torch.distributed.run): every rank holds
+    256 tokens, 64/G routed experts and both shared experts; one step = one MoE layer (route -> all-to-all
+    dispatch -> local experts -> all-to-all back -> shared experts -> combine).  Device time per step is
+    the max over ranks (CUDA events, all-reduce MAX)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from qmtp import _lib, moe
+    from qmtp.moe_ep import ExpertParallelMoE, local_expert_table
+
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    mode = args.shape if args.shape in ("mxfp4", "nvfp4") else "mxfp4"
+    E_R, NSH, H, I, T, TOPK = 64, 2, 2048, 1408, 256, 6
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    full = []
+    for shape in ((E_R + NSH, I, H), (E_R + NSH, I, H), (E_R + NSH, H, I)):
+        w = (torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        full.extend(moe.quantize(w, mode))
+        del w
+    loc = local_expert_table(*full, E_R, NSH, rank, world)
+    del full
+    torch.cuda.empty_cache()
+    gt = torch.Generator(device=dev)
+    gt.manual_seed(1000 + rank)
+    x = torch.randn((T, H), generator=gt, device=dev).to(torch.bfloat16)
+    idx, sc = moe.route(torch.randn((T, E_R), generator=gt, device=dev), TOPK, NSH)
+    layer = ExpertParallelMoE(E_R, NSH, lambda xr, e: moe.experts(xr, *loc, e, limit=None, mode=mode),
+                              lambda tab, ro, s_: moe.combine(tab, ro, s_))
+    for _ in range(max(args.warmup, 3)):
+        layer(x, idx, sc)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        layer(x, idx, sc)
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    dist.barrier()
+    Gs = 32 if mode == "mxfp4" else 16
+    wbytes = (E_R // world + NSH) * 3 * H * I * (0.5 + 1 / Gs)
+    if rank == 0:
+        us = float(ms.item()) * 1e3
+        print(json.dumps({"kernel": "moe_ep", "workload": f"MoE config5 {mode} expert-parallel: {world} GPUs x T={T}",
+                          "n_gpus": world, "us_per_layer": round(us, 2), "tokens_per_s": round(world * T / (us * 1e-6), 1),
+                          "local_weight_bytes": int(wbytes), "local_weight_GBps": round(wbytes / (us * 1e-6) / 1e9, 1),
+                          "steps": args.steps, "scaling": "weak", "device_error": _lib.device_error()}), flush=True)
+    dist.destroy_process_group()
+
+
 # ------------------------------------------------------------------------------ reference arm
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
@@ -428,7 +489,10 @@ def main():
     if args.kernel:
         args.steps = 50 if args.steps is None else args.steps
         args.warmup = 3 if args.warmup is None else args.warmup
-        run_kernel(args)
+        if args.kernel == "moe" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            run_moe_ep(args)
+        else:
+            run_kernel(args)
         return
     if args.impl == "reference":
         args.steps = 3 if args.steps is None else args.steps

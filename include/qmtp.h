@@ -241,6 +241,18 @@ int qmtp_moe(int fmt, const void* x, const void* wg, const void* sg, const void*
              const void* sd, const void* idx, const void* scores, void* y, int T, int S, int E, int H, int I,
              float limit, void* workspace, size_t ws_bytes, void* stream);
 
+/* Expert-parallel building blocks.  qmtp_moe_experts: partial[r] (fp32 [n, H]) = Wd[e] (silu(min(Wg[e] x_r, L)) *
+ * clamp(Wu[e] x_r, -L, L)) for each row r with expert e = expert[r] (int32 [n]), i.e. one (token, slot) entry per
+ * row without the routing weight; rows keep their input order.  Same limits as qmtp_moe (S = 1); the workspace is
+ * qmtp_moe_workspace(n, 1, E, H, I).
+ * qmtp_moe_combine: y[t] (bf16) = sum_j scores[t, j] * partials[row_of[t, j]] (fp32 [*, H]) in slot order j;
+ * row_of < 0 skips a slot.  H % 4 == 0, S <= 16. */
+int qmtp_moe_experts(int fmt, const void* x, const void* wg, const void* sg, const void* wu, const void* su,
+                     const void* wd, const void* sd, const void* expert, void* partial, int n, int E, int H, int I,
+                     float limit, void* workspace, size_t ws_bytes, void* stream);
+int qmtp_moe_combine(const void* partials, const void* row_of, const void* scores, int T, int S, int H, void* y,
+                     void* stream);
+
 /* Control block of the device-side speculative loop (int32 [QMTP_CTRL_SIZE]). */
 #define QMTP_CTRL_SLOT 0      /* GatedDeltaNet state ring slot before the next verify */
 #define QMTP_CTRL_CONV_ROW 1  /* row of the conv state inside the [2 * win_rows, C] window buffer */

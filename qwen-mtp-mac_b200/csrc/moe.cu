@@ -450,6 +450,7 @@ struct GemmArgs {
   const int32_t* xsh;     // gate/up: per-entry exponent of the activation downscale
   uint8_t* himg;          // gate/up output: h operand images for down
   float* yp;              // down output: per-entry fp32 partials [n, R]
+  const int32_t* out_row; // down: optional row of yp for each sorted entry (nullptr = the entry itself)
   int K;                  // reduction length
   int R;                  // weight rows per expert
   int KS;                 // scale bytes per weight row
@@ -874,7 +875,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        float* yrow = a.yp + (size_t)tl.entry0 * a.R + rt * kRows + r;
+        float* ycol = a.yp + rt * kRows + r;
         for (int cg = 0; cg < tl.nt / 16; ++cg) {
           uint32_t vh[16], vl[16];
           tmem_ld16(dacc + uint32_t(cg * 16), vh);
@@ -883,7 +884,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int n = cg * 16 + i;
-            if (n < tl.ntok) yrow[(size_t)n * a.R] = __fadd_rn(__uint_as_float(vh[i]), __uint_as_float(vl[i]));
+            if (n < tl.ntok) {
+              const int e = tl.entry0 + n;
+              const size_t row = size_t(a.out_row ? a.out_row[e] : e);
+              ycol[row * a.R] = __fadd_rn(__uint_as_float(vh[i]), __uint_as_float(vl[i]));
+            }
           }
         }
       }
@@ -1044,11 +1049,15 @@ extern "C" size_t qmtp_moe_workspace(int T, int S, int E, int H, int I) {
   return layout(T, S, E, H, I).total;
 }
 
-extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_, const void* wu, const void* su_,
-                        const void* wd, const void* sd_, const void* idx_, const void* scores_, void* y_, int T, int S,
-                        int E, int H, int I, float limit, void* workspace, size_t ws_bytes, void* stream_) {
+// Shared body of qmtp_moe (y = combined bf16 output) and qmtp_moe_experts (yp_out = fp32 partial of
+// every (row, slot) entry with S == 1, written in input row order; no combine).
+static int moe_run(int fmt, const void* x_, const void* wg, const void* sg_, const void* wu, const void* su_,
+                   const void* wd, const void* sd_, const void* idx_, const void* scores_, void* y_, float* yp_out,
+                   int T, int S, int E, int H, int I, float limit, void* workspace, size_t ws_bytes, void* stream_) {
   if (fmt != 0 && fmt != 1) return QMTP_ERR_ARG;
-  if (!x_ || !wg || !sg_ || !wu || !su_ || !wd || !sd_ || !idx_ || !scores_ || !y_ || !workspace) return QMTP_ERR_ARG;
+  if (!x_ || !wg || !sg_ || !wu || !su_ || !wd || !sd_ || !idx_ || !workspace) return QMTP_ERR_ARG;
+  if (!yp_out && (!scores_ || !y_)) return QMTP_ERR_ARG;
+  if (yp_out && S != 1) return QMTP_ERR_SHAPE;
   if (T <= 0 || S <= 0 || S > 16 || E <= 0 || E > 1024 || (long long)T * S > 65535) return QMTP_ERR_SHAPE;
   if (H <= 0 || I <= 0 || H % kRows || I % kRows) return QMTP_ERR_SHAPE;
   const int G = fmt == 0 ? 32 : 16;
@@ -1058,7 +1067,8 @@ extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_
   const int nw_gu = ring_stages<true>(sbuf_gu), nw_dn = ring_stages<false>(sbuf_dn);
   if (nw_gu < 2 || nw_dn < 2) return QMTP_ERR_UNSUPPORTED;
   if (!aligned16(x_) || !aligned16(wg) || !aligned16(wu) || !aligned16(wd) || !aligned16(sg_) || !aligned16(su_) ||
-      !aligned16(sd_) || !aligned16(y_) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+      !aligned16(sd_) || (y_ && !aligned16(y_)) || (yp_out && !aligned16(yp_out)) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return QMTP_ERR_ALIGN;
   const Workspace L = layout(T, S, E, H, I);
   if (ws_bytes < L.total) return QMTP_ERR_SHAPE;
@@ -1101,11 +1111,40 @@ extern "C" int qmtp_moe(int fmt, const void* x_, const void* wg, const void* sg_
                               (const Tile*)tiles, (const int32_t*)counters, (const int32_t*)sorted_tok, ximg, xsh));
   const int grid = sm_count();
   GemmArgs gu{static_cast<const uint8_t*>(sg_), static_cast<const uint8_t*>(su_), ximg, tiles, counters, xsh, himg,
-              nullptr, H, I, KS_gu, fmt, limit, I, nw_gu, sbuf_gu, sbox, err};
+              nullptr, nullptr, H, I, KS_gu, fmt, limit, I, nw_gu, sbuf_gu, sbox, err};
   QMTP_CUDA_TRY(launch_gemm<true>(mg, mu, msg, msu, gu, grid, stream));
-  GemmArgs dn{sd, nullptr, himg, tiles, counters, nullptr, nullptr, yp, I, H, KS_dn, fmt, limit, 0, nw_dn, sbuf_dn, 0, err};
+  GemmArgs dn{sd, nullptr, himg, tiles, counters, nullptr, nullptr, yp_out ? yp_out : yp,
+              yp_out ? (const int32_t*)sorted_tok : nullptr, I, H, KS_dn, fmt, limit, 0, nw_dn, sbuf_dn, 0, err};
   QMTP_CUDA_TRY(launch_gemm<false>(md, md, md, md, dn, grid, stream));
-  QMTP_CUDA_TRY(launch_kernel(moe_combine_kernel, dim3(unsigned(T), unsigned((H + 1023) / 1024)), dim3(256), 0, stream,
-                              (const float*)yp, (const int32_t*)entry_pos, scores, S, H, y));
+  if (!yp_out)
+    QMTP_CUDA_TRY(launch_kernel(moe_combine_kernel, dim3(unsigned(T), unsigned((H + 1023) / 1024)), dim3(256), 0,
+                                stream, (const float*)yp, (const int32_t*)entry_pos, scores, S, H, y));
+  return QMTP_OK;
+}
+
+extern "C" int qmtp_moe(int fmt, const void* x, const void* wg, const void* sg, const void* wu, const void* su,
+                        const void* wd, const void* sd, const void* idx, const void* scores, void* y, int T, int S,
+                        int E, int H, int I, float limit, void* workspace, size_t ws_bytes, void* stream) {
+  return moe_run(fmt, x, wg, sg, wu, su, wd, sd, idx, scores, y, nullptr, T, S, E, H, I, limit, workspace, ws_bytes,
+                 stream);
+}
+
+extern "C" int qmtp_moe_experts(int fmt, const void* x, const void* wg, const void* sg, const void* wu, const void* su,
+                                const void* wd, const void* sd, const void* expert, void* partial, int n, int E, int H,
+                                int I, float limit, void* workspace, size_t ws_bytes, void* stream) {
+  if (!partial) return QMTP_ERR_ARG;
+  return moe_run(fmt, x, wg, sg, wu, su, wd, sd, expert, nullptr, nullptr, static_cast<float*>(partial), n, 1, E, H, I,
+                 limit, workspace, ws_bytes, stream);
+}
+
+extern "C" int qmtp_moe_combine(const void* partials, const void* row_of, const void* scores, int T, int S, int H,
+                                void* y, void* stream) {
+  if (!partials || !row_of || !scores || !y) return QMTP_ERR_ARG;
+  if (T <= 0 || S <= 0 || S > 16 || H <= 0 || H % 4) return QMTP_ERR_SHAPE;
+  if (!aligned16(partials) || (reinterpret_cast<uintptr_t>(y) & 7u)) return QMTP_ERR_ALIGN;
+  QMTP_CUDA_TRY(launch_kernel(moe_combine_kernel, dim3(unsigned(T), unsigned((H + 1023) / 1024)), dim3(256), 0,
+                              static_cast<cudaStream_t>(stream), static_cast<const float*>(partials),
+                              static_cast<const int32_t*>(row_of), static_cast<const float*>(scores), S, H,
+                              static_cast<uint16_t*>(y)));
   return QMTP_OK;
 }

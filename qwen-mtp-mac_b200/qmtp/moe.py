@@ -109,3 +109,40 @@ def moe_decode(x, wg, sg, wu, su, wd, sd, idx, scores, *, limit=10.0, nsg=1, row
     _lib.check(_lib.lib().qmtp_moe(fmt, x2.data_ptr(), *[t.data_ptr() for t in ts], idx2.data_ptr(), sc2.data_ptr(),
                                    y.data_ptr(), T, S, E, H, I, lim, _aligned(ws), need, _lib.stream()), "qmtp_moe")
     return y.reshape(x.shape)
+
+
+def experts(x_rows: torch.Tensor, wg, sg, wu, su, wd, sd, expert: torch.Tensor, *, limit=None,
+            mode: str = "mxfp4", out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-row expert FFN without the routing weight: fp32 [n, H], row r through expert[r].
+
+    The expert-parallel building block (the rows a rank received for its local experts)."""
+    fmt, G = _mode(mode)
+    _lib.require_cuda(x_rows)
+    H = x_rows.shape[-1]
+    x2 = x_rows.reshape(-1, H).contiguous()
+    n = x2.shape[0]
+    e = expert.reshape(n).to(torch.int32).contiguous()
+    E, I = wg.shape[0], wg.shape[1]
+    y = out if out is not None else torch.empty((n, H), dtype=torch.float32, device=x_rows.device)
+    if n == 0:
+        return y
+    ws = _workspace(x_rows.device, n, 1, E, H, I)
+    need = _lib.lib().qmtp_moe_workspace(n, 1, E, H, I)
+    lim = math.inf if limit is None else float(limit)
+    ts = [t.contiguous() for t in (wg, sg, wu, su, wd, sd)]
+    _lib.check(_lib.lib().qmtp_moe_experts(fmt, x2.data_ptr(), *[t.data_ptr() for t in ts], e.data_ptr(), y.data_ptr(),
+                                           n, E, H, I, lim, _aligned(ws), need, _lib.stream()), "qmtp_moe_experts")
+    return y
+
+
+def combine(partials: torch.Tensor, row_of: torch.Tensor, scores: torch.Tensor, out: torch.Tensor | None = None):
+    """y[t] = sum_j scores[t, j] * partials[row_of[t, j]] in slot order (fp32 sum, bf16 result)."""
+    _lib.require_cuda(partials)
+    T, S = row_of.shape
+    H = partials.shape[-1]
+    y = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16, device=partials.device)
+    r = row_of.to(torch.int32).contiguous()
+    sc = scores.to(torch.float32).contiguous()
+    _lib.check(_lib.lib().qmtp_moe_combine(partials.data_ptr(), r.data_ptr(), sc.data_ptr(), T, S, H, y.data_ptr(),
+                                           _lib.stream()), "qmtp_moe_combine")
+    return y
