@@ -50,6 +50,17 @@ int qmtp_device_error(unsigned* out, int clear);
 int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const void* biases,
                         void* y, int M, int N, int K, int ldy, void* stream);
 
+/* qmv with the producer of x fused into its load (each row of x at x + m * ldx, elements):
+ *   pre 0: none;
+ *   pre 1: RMSNorm over the K features, x <- bf16(pre_w * bf16(x * rsqrt(mean(x^2) + eps)))
+ *          (bit-identical to qmtp_rmsnorm followed by qmtp_qmv_affine_g64);
+ *   pre 2: SwiGLU, x <- bf16(silu(gate) * up) with gate = row[0:K], up = row[K:2K]
+ *          (bit-identical to qmtp_swiglu followed by qmtp_qmv_affine_g64).
+ * res != NULL adds the bf16 residual as qmtp_qmv_affine_g64_res does. ldx % 8 == 0. */
+int qmtp_qmv_affine_g64_ex(const void* x, long long ldx, int pre, const void* pre_w, float eps, const void* w,
+                           const void* scales, const void* biases, void* y, const void* res, int M, int N, int K,
+                           int ldy, void* stream);
+
 /* Multi-row 4-bit GEMV, NVFP4 (e2m1 nibbles, e4m3 scale per 16): qmv_kernel.py:86-101 qmv_nvfp4.
  *   x bf16 [M, K]; w uint32 [N, K/8]; scales uint8 [N, K/16]; y bf16 [M, ldy]. K % 1024 == 0. */
 int qmtp_qmv_nvfp4_g16(const void* x, const void* w, const void* scales, void* y, int M, int N,

@@ -21,6 +21,11 @@
 namespace qmtp {
 
 enum QFmt { FMT_AFFINE = 0, FMT_NVFP4 = 1 };
+// x prologue applied while the x chunk is loaded (the op whose output the GEMV consumes, fused):
+//   PRE_RMSNORM: x <- bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) over the full row of K (decode.cu
+//                rmsnorm_wide_kernel, same chunk ownership and reduction order, so bit-identical);
+//   PRE_SWIGLU:  x <- bf16(silu_bf(gate) * up) with gate = x[:, 0:K], up = x[:, K:2K] (swiglu_kernel).
+enum QPre { PRE_NONE = 0, PRE_RMSNORM = 1, PRE_SWIGLU = 2 };
 
 template <int FMT, int M, int W, int TR, int NS>
 struct QmvCfg {
@@ -35,7 +40,8 @@ struct QmvCfg {
   static constexpr int OFF_B = OFF_S + NS * TR * SB;
   static constexpr int OFF_RED = OFF_B + NS * TR * BB;
   static constexpr int OFF_BAR = OFF_RED + 2 * W * VP * 4;
-  static constexpr int SMEM = OFF_BAR + NS * 8;
+  static constexpr int OFF_PRE = OFF_BAR + NS * 8;                 // per-(row, warp) sums of squares
+  static constexpr int SMEM = OFF_PRE + 4 * 16 * 4;
 };
 
 // (a & b) | c as one LOP3 (written out: the C++ form costs an extra logic op per value).
@@ -89,12 +95,12 @@ __device__ __forceinline__ float e4m3_x16k(uint32_t s) {
   return __fmul_rn(__half2float(__ushort_as_half(uint16_t((s & 0x7Fu) << 7))), 4194304.0f);
 }
 
-template <int FMT, int M, int W, int TR, int NS>
+template <int FMT, int M, int W, int TR, int NS, int PRE>
 __global__ void __launch_bounds__(W * 32, 1)
 qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
            const uint8_t* __restrict__ sc, const uint8_t* __restrict__ bi,
            uint16_t* __restrict__ y, const uint16_t* __restrict__ res, int N, int ldy,
-           unsigned* __restrict__ err) {
+           unsigned* __restrict__ err, long long ldx, const uint16_t* __restrict__ pre_w, float eps) {
   using C = QmvCfg<FMT, M, W, TR, NS>;
   constexpr int K = C::K;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -144,11 +150,79 @@ qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
   float a0init[M][2];
   float xsum[M];
 #pragma unroll
+  // fused prologue ops: this thread's 32 x values of every row (row m at x + m * ldx)
+  uint4 xin[M][4];
+#pragma unroll
   for (int m = 0; m < M; ++m) {
-    const uint16_t* xg = x + size_t(m) * K + 32 * c;
+    const uint16_t* xg = x + size_t(m) * size_t(ldx) + 32 * c;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) xin[m][q] = *reinterpret_cast<const uint4*>(xg + 8 * q);
+  }
+  if constexpr (PRE == PRE_SWIGLU) {
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const uint16_t* ug = x + size_t(m) * size_t(ldx) + K + 32 * c;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 uv = *reinterpret_cast<const uint4*>(ug + 8 * q);
+        const uint32_t gg[4] = {xin[m][q].x, xin[m][q].y, xin[m][q].z, xin[m][q].w};
+        const uint32_t uu[4] = {uv.x, uv.y, uv.z, uv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const uint16_t lo = f2bf(__fmul_rn(silu_bf(bflo(gg[h])), bflo(uu[h])));
+          const uint16_t hi = f2bf(__fmul_rn(silu_bf(bfhi(gg[h])), bfhi(uu[h])));
+          o[h] = lo | (uint32_t(hi) << 16);
+        }
+        xin[m][q] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  if constexpr (PRE == PRE_RMSNORM) {
+    float* s_pre = reinterpret_cast<float*>(smem + C::OFF_PRE);  // [M][W]
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t uu[4] = {xin[m][q].x, xin[m][q].y, xin[m][q].z, xin[m][q].w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          ss = __fmaf_rn(bflo(uu[h]), bflo(uu[h]), ss);
+          ss = __fmaf_rn(bfhi(uu[h]), bfhi(uu[h]), ss);
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) s_pre[m * W + warp] = ss;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      float t = s_pre[m * W];
+#pragma unroll
+      for (int w = 1; w < W; ++w) t = __fadd_rn(t, s_pre[m * W + w]);
+      const float r = rsqrt_rn(__fadd_rn(__fdiv_rn(t, float(K)), eps));
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 wu = *reinterpret_cast<const uint4*>(pre_w + 32 * c + 8 * q);
+        const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
+        const uint32_t uu[4] = {xin[m][q].x, xin[m][q].y, xin[m][q].z, xin[m][q].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const uint16_t lo = f2bf(__fmul_rn(bflo(ww[h]), R(__fmul_rn(bflo(uu[h]), r))));
+          const uint16_t hi = f2bf(__fmul_rn(bfhi(ww[h]), R(__fmul_rn(bfhi(uu[h]), r))));
+          o[h] = lo | (uint32_t(hi) << 16);
+        }
+        xin[m][q] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
     uint4 u[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) u[q] = *reinterpret_cast<const uint4*>(xg + 8 * q);
+    for (int q = 0; q < 4; ++q) u[q] = xin[m][q];
     if constexpr (FMT == FMT_AFFINE) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -281,13 +355,13 @@ struct QmvLaunch {
   int grid_per_sm, block, smem, rows_per_tile, stages;
 };
 
-template <int FMT, int M, int W>
+template <int FMT, int M, int W, int PRE>
 static int launch_qmv(const void* x, const void* w, const void* s, const void* b, void* y, const void* res, int N,
-                      int ldy, cudaStream_t st, QmvLaunch* info = nullptr) {
+                      int ldy, cudaStream_t st, QmvLaunch* info, long long ldx, const void* pre_w, float eps) {
   constexpr int TR = (W <= 4) ? 8 : 4;
   constexpr int NS = 3;
   using C = QmvCfg<FMT, M, W, TR, NS>;
-  auto kern = qmv_kernel<FMT, M, W, TR, NS>;
+  auto kern = qmv_kernel<FMT, M, W, TR, NS, PRE>;
   static int occ = -1;
   static std::once_flag once;
   std::call_once(once, [&] {
@@ -306,43 +380,70 @@ static int launch_qmv(const void* x, const void* w, const void* s, const void* b
   launch_kernel(kern, dim3(grid), dim3(W * 32), C::SMEM, st, static_cast<const uint16_t*>(x), static_cast<const uint32_t*>(w),
                                         static_cast<const uint8_t*>(s), static_cast<const uint8_t*>(b),
                                         static_cast<uint16_t*>(y), static_cast<const uint16_t*>(res), N, ldy,
-                                        device_error_ptr());
+                                        device_error_ptr(), ldx, static_cast<const uint16_t*>(pre_w), eps);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 
-template <int FMT, int M>
-static int dispatch_w(int K, const void* x, const void* w, const void* s, const void* b, void* y, const void* res,
-                      int N, int ldy, cudaStream_t st, QmvLaunch* info = nullptr) {
+struct QmvArgs {
+  const void *x, *w, *s, *b;
+  void* y;
+  const void* res;
+  int N, ldy;
+  long long ldx;
+  const void* pre_w;
+  float eps;
+};
+
+template <int FMT, int M, int PRE>
+static int dispatch_w(int K, const QmvArgs& a, cudaStream_t st, QmvLaunch* info = nullptr) {
+#define QMTP_QMV_W(WW) launch_qmv<FMT, M, WW, PRE>(a.x, a.w, a.s, a.b, a.y, a.res, a.N, a.ldy, st, info, a.ldx, a.pre_w, a.eps)
   switch (K) {
-    case 1024: return launch_qmv<FMT, M, 1>(x, w, s, b, y, res, N, ldy, st, info);
-    case 2048: return launch_qmv<FMT, M, 2>(x, w, s, b, y, res, N, ldy, st, info);
-    case 4096: return launch_qmv<FMT, M, 4>(x, w, s, b, y, res, N, ldy, st, info);
-    case 8192: return launch_qmv<FMT, M, 8>(x, w, s, b, y, res, N, ldy, st, info);
-    case 12288: return launch_qmv<FMT, M, 12>(x, w, s, b, y, res, N, ldy, st, info);
+    case 1024: return QMTP_QMV_W(1);
+    case 2048: return QMTP_QMV_W(2);
+    case 4096: return QMTP_QMV_W(4);
+    case 8192: return QMTP_QMV_W(8);
+    case 12288: return QMTP_QMV_W(12);
     default: return QMTP_ERR_SHAPE;
+  }
+#undef QMTP_QMV_W
+}
+
+template <int FMT, int PRE>
+static int dispatch_m(int M, int K, const QmvArgs& a, cudaStream_t st, QmvLaunch* info = nullptr) {
+  switch (M) {
+    case 1: return dispatch_w<FMT, 1, PRE>(K, a, st, info);
+    case 2: return dispatch_w<FMT, 2, PRE>(K, a, st, info);
+    case 3: return dispatch_w<FMT, 3, PRE>(K, a, st, info);
+    default: return dispatch_w<FMT, 4, PRE>(K, a, st, info);
   }
 }
 
 template <int FMT>
 static int qmv_entry(const void* x, const void* w, const void* s, const void* b, void* y, const void* res, int M,
-                     int N, int K, int ldy, void* stream) {
+                     int N, int K, int ldy, void* stream, int pre = PRE_NONE, long long ldx = 0,
+                     const void* pre_w = nullptr, float eps = 0.0f) {
   if (!x || !w || !s || !y || (FMT == FMT_AFFINE && !b)) return QMTP_ERR_ARG;
   if (M < 1 || N < 1 || K < 1024 || K % 1024 != 0 || K > 12288 || ldy < N) return QMTP_ERR_SHAPE;
-  if (!aligned16(x) || !aligned16(w) || !aligned16(s) || (b && !aligned16(b))) return QMTP_ERR_ALIGN;
+  if (ldx == 0) ldx = pre == PRE_SWIGLU ? 2LL * K : K;
+  if (ldx < (pre == PRE_SWIGLU ? 2LL * K : K) || ldx % 8) return QMTP_ERR_SHAPE;
+  if (pre != PRE_NONE && FMT != FMT_AFFINE) return QMTP_ERR_UNSUPPORTED;
+  if (pre == PRE_RMSNORM && !pre_w) return QMTP_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(s) || (b && !aligned16(b)) || (pre_w && !aligned16(pre_w)))
+    return QMTP_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint16_t* xp = static_cast<const uint16_t*>(x);
   uint16_t* yp = static_cast<uint16_t*>(y);
   for (int m0 = 0; m0 < M; m0 += 4) {
     const int mm = std::min(4, M - m0);
-    const void* xm = xp + size_t(m0) * K;
-    void* ym = yp + size_t(m0) * ldy;
-    const void* rm = res ? static_cast<const uint16_t*>(res) + size_t(m0) * ldy : nullptr;
+    QmvArgs a{xp + size_t(m0) * size_t(ldx), w, s, b, yp + size_t(m0) * ldy,
+              res ? static_cast<const uint16_t*>(res) + size_t(m0) * ldy : nullptr, N, ldy, ldx, pre_w, eps};
     int rc;
-    switch (mm) {
-      case 1: rc = dispatch_w<FMT, 1>(K, xm, w, s, b, ym, rm, N, ldy, st); break;
-      case 2: rc = dispatch_w<FMT, 2>(K, xm, w, s, b, ym, rm, N, ldy, st); break;
-      case 3: rc = dispatch_w<FMT, 3>(K, xm, w, s, b, ym, rm, N, ldy, st); break;
-      default: rc = dispatch_w<FMT, 4>(K, xm, w, s, b, ym, rm, N, ldy, st); break;
+    if constexpr (FMT == FMT_AFFINE) {
+      rc = pre == PRE_RMSNORM ? dispatch_m<FMT, PRE_RMSNORM>(mm, K, a, st)
+         : pre == PRE_SWIGLU  ? dispatch_m<FMT, PRE_SWIGLU>(mm, K, a, st)
+                              : dispatch_m<FMT, PRE_NONE>(mm, K, a, st);
+    } else {
+      rc = dispatch_m<FMT, PRE_NONE>(mm, K, a, st);
     }
     if (rc != QMTP_OK) return rc;
   }
@@ -403,6 +504,13 @@ extern "C" int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void*
   return qmv_entry<FMT_AFFINE>(x, w, scales, biases, y, res, M, N, K, ldy, stream);
 }
 
+extern "C" int qmtp_qmv_affine_g64_ex(const void* x, long long ldx, int pre, const void* pre_w, float eps,
+                                      const void* w, const void* scales, const void* biases, void* y, const void* res,
+                                      int M, int N, int K, int ldy, void* stream) {
+  if (pre < PRE_NONE || pre > PRE_SWIGLU) return QMTP_ERR_ARG;
+  return qmv_entry<FMT_AFFINE>(x, w, scales, biases, y, res, M, N, K, ldy, stream, pre, ldx, pre_w, eps);
+}
+
 extern "C" int qmtp_qmv_nvfp4_g16(const void* x, const void* w, const void* scales, void* y, int M, int N, int K,
                                   int ldy, void* stream) {
   return qmv_entry<FMT_NVFP4>(x, w, scales, nullptr, y, nullptr, M, N, K, ldy, stream);
@@ -416,12 +524,8 @@ extern "C" int qmtp_qmv_launch_info(int fmt, int M, int K, int* ctas_per_sm, int
   int rc;
   auto go = [&](auto fmtc) -> int {
     constexpr int F = decltype(fmtc)::value;
-    switch (M) {
-      case 1: return dispatch_w<F, 1>(K, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
-      case 2: return dispatch_w<F, 2>(K, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
-      case 3: return dispatch_w<F, 3>(K, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
-      default: return dispatch_w<F, 4>(K, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 0, &info);
-    }
+    const QmvArgs a{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, K, nullptr, 0.0f};
+    return dispatch_m<F, PRE_NONE>(M, K, a, 0, &info);
   };
   rc = fmt == 0 ? go(std::integral_constant<int, FMT_AFFINE>{}) : go(std::integral_constant<int, FMT_NVFP4>{});
   if (rc != QMTP_OK) return rc;

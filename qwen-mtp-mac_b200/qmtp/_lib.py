@@ -35,6 +35,7 @@ SIGNATURES: dict[str, list] = {
     "qmtp_device_error": [ctypes.POINTER(ctypes.c_uint), _I],
     "qmtp_qmv_affine_g64": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_qmv_nvfp4_g16": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "qmtp_qmv_affine_g64_ex": [_P, ctypes.c_longlong, _I, _P, _F, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_quantize_affine_g64": [_P, _P, _P, _P, _I, _I, _P],
     "qmtp_qmv_launch_info": [_I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
                              ctypes.POINTER(_I)],
