@@ -136,9 +136,9 @@ class MTPDecoder:
 
     # ------------------------------------------------------------------ layers
     def _attn_layer(self, L, x, rows, kc, vc, pos_slot):
-        """Gated attention block: x (pre-norm residual stream, [rows, H]) += o_proj(attn(input_ln(x)))."""
+        """Gated attention block: x (pre-norm residual stream, [rows, H]) += o_proj(attn(...))."""
         a = self.a
-        self._qmv(x, L["qkv_proj"], self.proj, rows, ldy=self.proj.shape[1], pre=1, pre_w=L["input_ln"])
+        self._qmv(self.xn, L["qkv_proj"], self.proj, rows, ldy=self.proj.shape[1])
         self._chk(self.L.qmtp_attn_prep(self.proj.data_ptr(), self.proj.shape[1], rows, a.n_heads, a.n_kv,
                                         a.head_dim, a.rotary_dim, L["q_norm"].data_ptr(), L["k_norm"].data_ptr(),
                                         a.eps, self.cos.data_ptr(), self.sin.data_ptr(), self._cp(pos_slot), 0,
@@ -150,10 +150,12 @@ class MTPDecoder:
         self._qmv(self.att_out, L["o_proj"], x, rows, res=x)
 
     def _mlp(self, L, x, rows):
-        """x += down(swiglu(gate_up(post_ln(x)))): the norm and SwiGLU are fused into the two GEMVs."""
         a = self.a
-        self._qmv(x, L["gate_up"], self.gu, rows, pre=1, pre_w=L["post_ln"])
-        self._qmv(self.gu, L["down"], x, rows, res=x, pre=2, ldx=2 * a.intermediate)
+        self._norm(x, L["post_ln"], self.xn, rows)
+        self._qmv(self.xn, L["gate_up"], self.gu, rows)
+        self._chk(self.L.qmtp_swiglu(self.gu.data_ptr(), 2 * a.intermediate, rows, a.intermediate,
+                                     self.act.data_ptr(), self._st()), "swiglu")
+        self._qmv(self.act, L["down"], x, rows, res=x)
 
     def backbone(self):
         """mtp.py:143-153 on the k+1 verify tokens in self.tokens_in: h (pre-norm) and hn (post-norm)."""
@@ -164,8 +166,9 @@ class MTPDecoder:
                                     self._st()), "embed")
         for i in range(a.layers):
             L = W[f"layers.{i}"]
+            self._norm(self.h, L["input_ln"], self.xn, S)
             if a.is_linear(i):
-                self._qmv(self.h, L["in_proj"], self.proj, S, ldy=self.proj.shape[1], pre=1, pre_w=L["input_ln"])
+                self._qmv(self.xn, L["in_proj"], self.proj, S, ldy=self.proj.shape[1])
                 self._chk(self.L.qmtp_gdn_fused_ex(ctypes.byref(self._gdn_args[i]), self._st()), "gdn")
                 Z = a.lin_hv * a.lin_dv
                 self._chk(self.L.qmtp_gdn_norm_gate(self.ygdn.data_ptr(), self.proj.data_ptr() + 2 * a.conv_dim,
@@ -203,6 +206,7 @@ class MTPDecoder:
                                       self.mcat.data_ptr() + 2 * H, 2 * H, rows, H, self._st()), "rmsnorm")
         self._qmv(self.mcat, M["fc"], self.mx, rows)
         Ly = M["layer"]
+        self._norm(self.mx, Ly["input_ln"], self.xn, rows)
         self._attn_layer(Ly, self.mx, rows, self.mkv[0], self.mkv[1], C["MPOS"])
         self._mlp(Ly, self.mx, rows)
         if not with_draft:
