@@ -50,16 +50,52 @@ int qmtp_device_error(unsigned* out, int clear);
 int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const void* biases,
                         void* y, int M, int N, int K, int ldy, void* stream);
 
-/* qmv with the producer of x fused into its load (each row of x at x + m * ldx, elements):
- *   pre 0: none;
- *   pre 1: RMSNorm over the K features, x <- bf16(pre_w * bf16(x * rsqrt(mean(x^2) + eps)))
- *          (bit-identical to qmtp_rmsnorm followed by qmtp_qmv_affine_g64);
- *   pre 2: SwiGLU, x <- bf16(silu(gate) * up) with gate = row[0:K], up = row[K:2K]
- *          (bit-identical to qmtp_swiglu followed by qmtp_qmv_affine_g64).
- * res != NULL adds the bf16 residual as qmtp_qmv_affine_g64_res does. ldx % 8 == 0. */
-int qmtp_qmv_affine_g64_ex(const void* x, long long ldx, int pre, const void* pre_w, float eps, const void* w,
-                           const void* scales, const void* biases, void* y, const void* res, int M, int N, int K,
-                           int ldy, void* stream);
+/* qmtp_qmv_affine_g64 with the ops around a decoder projection fused in (one launch, every
+ * option bit-identical to the separate kernels it replaces):
+ *   x rows at x + m * ldx (elements; 0 = K, or 2K with pre = SWIGLU), ldx % 8 == 0;
+ *   pre  QMTP_QMV_PRE_RMSNORM: x <- bf16(pre_w * bf16(x * rsqrt(mean(x^2) + pre_eps))) over the K
+ *          features while x is loaded (qmtp_rmsnorm then qmv); every CTA repeats the row statistics;
+ *        QMTP_QMV_PRE_SWIGLU: x <- bf16(silu(gate) * up), gate = row[0:K], up = row[K:2K] (qmtp_swiglu then
+ *          qmv); every CTA repeats the activation for the whole row;
+ *   res  != NULL: y = bf16(res + bf16(x . W^T)) as qmtp_qmv_affine_g64_res;
+ *   epi  QMTP_QMV_EPI_SWIGLU: w/scales/biases hold 2N rows [gate | up]; y[m][j] = bf16(silu(g_j) * u_j)
+ *          with g, u the bf16 projections (qmv over 2N rows then qmtp_swiglu), each element once;
+ *        QMTP_QMV_EPI_NORM: after y is complete, norm_y[m] = RMSNorm(y[m]) with weight norm_w and
+ *          norm_eps (qmv then qmtp_rmsnorm); needs N % 1024 == 0, N <= K, ld_norm >= N and `sync`,
+ *          a device uint32 that is 0 before the call (the kernel leaves it 0); calls that share a
+ *          `sync` word must not run concurrently;
+ *   prefetch[i], prefetch_bytes[i]: up to four device byte ranges a later kernel reads; the launch
+ *          pulls them into L2 while it streams its own weights (a hint: NULL / 0 entries, unaligned
+ *          starts are ignored, sizes are rounded down to 16 bytes).
+ * pre and epi are exclusive; epi = SWIGLU excludes res. */
+#define QMTP_QMV_PRE_NONE 0
+#define QMTP_QMV_PRE_RMSNORM 1
+#define QMTP_QMV_PRE_SWIGLU 2
+#define QMTP_QMV_EPI_NONE 0
+#define QMTP_QMV_EPI_SWIGLU 1
+#define QMTP_QMV_EPI_NORM 2
+typedef struct qmtp_qmv_args {
+  const void* x;
+  long long ldx;
+  const void* w;
+  const void* scales;
+  const void* biases;
+  void* y;
+  const void* res;
+  int M, N, K, ldy;
+  int pre;
+  const void* pre_w;
+  float pre_eps;
+  int epi;
+  void* norm_y;
+  const void* norm_w;
+  long long ld_norm;
+  float norm_eps;
+  unsigned* sync;
+  const void* prefetch[4];
+  long long prefetch_bytes[4];
+} qmtp_qmv_args;
+int qmtp_qmv_ex(const qmtp_qmv_args* args, void* stream);
 
 /* Multi-row 4-bit GEMV, NVFP4 (e2m1 nibbles, e4m3 scale per 16): qmv_kernel.py:86-101 qmv_nvfp4.
  *   x bf16 [M, K]; w uint32 [N, K/8]; scales uint8 [N, K/16]; y bf16 [M, ldy]. K % 1024 == 0. */

@@ -26,6 +26,39 @@ enum QFmt { FMT_AFFINE = 0, FMT_NVFP4 = 1 };
 //                rmsnorm_wide_kernel, same chunk ownership and reduction order, so bit-identical);
 //   PRE_SWIGLU:  x <- bf16(silu_bf(gate) * up) with gate = x[:, 0:K], up = x[:, K:2K] (swiglu_kernel).
 enum QPre { PRE_NONE = 0, PRE_RMSNORM = 1, PRE_SWIGLU = 2 };
+// Epilogues (the op that consumes y, fused where it costs each output element once):
+//   EPI_SWIGLU: the weight rows are [gate (N) | up (N)]; a CTA owns gate rows [r0, r1) and the up rows
+//               N + [r0, r1), so y[m][j] = bf16(silu_bf(bf16(g)) * bf16(u)) (swiglu_kernel's sequence);
+//   EPI_NORM:   after the last output is written, the CTA that finishes last RMS-normalises the M
+//               rows of y into norm_y (rmsnorm_wide_kernel's chunk ownership and reduction order).
+enum QEpi { EPI_NONE = 0, EPI_SWIGLU = 1, EPI_NORM = 2 };
+
+// Up to four byte ranges that later kernels read, prefetched into L2 while this kernel streams
+// its own weights (the CTAs split every range evenly).  Ranges are 16-byte aligned multiples of 16.
+struct QPf {
+  const uint8_t* p[4];
+  unsigned long long n[4];
+};
+
+struct QmvParams {
+  const uint16_t* x;
+  long long ldx;
+  const uint32_t* wq;
+  const uint8_t* sc;
+  const uint8_t* bi;
+  uint16_t* y;
+  const uint16_t* res;
+  int N, ldy;
+  unsigned* err;
+  const uint16_t* pre_w;
+  float eps;
+  uint16_t* norm_y;        // EPI_NORM output rows (stride ldn), weight norm_w, epsilon norm_eps
+  const uint16_t* norm_w;
+  long long ldn;
+  float norm_eps;
+  unsigned* sync;          // EPI_NORM arrival counter: 0 before the launch, reset to 0 by the last CTA
+  QPf pf;
+};
 
 template <int FMT, int M, int W, int TR, int NS>
 struct QmvCfg {
@@ -41,8 +74,27 @@ struct QmvCfg {
   static constexpr int OFF_RED = OFF_B + NS * TR * BB;
   static constexpr int OFF_BAR = OFF_RED + 2 * W * VP * 4;
   static constexpr int OFF_PRE = OFF_BAR + NS * 8;                 // per-(row, warp) sums of squares
-  static constexpr int SMEM = OFF_PRE + 4 * 16 * 4;
+  static constexpr int OFF_FLAG = OFF_PRE + 4 * 16 * 4;           // norm factors [4] + last-CTA flag
+  static constexpr int SMEM = OFF_FLAG + 32;
 };
+
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// This CTA's share of the prefetch ranges (contiguous 16-byte-aligned slices, 64 KB per request).
+__device__ __forceinline__ void issue_prefetch(const QPf& pf) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const unsigned long long n = pf.n[i];
+    if (n == 0) continue;
+    const unsigned long long per = ((n + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+    const unsigned long long beg = per * blockIdx.x;
+    const unsigned long long end = min(beg + per, n);
+    for (unsigned long long o = beg; o < end; o += 65536ull)
+      prefetch_l2(pf.p[i] + o, uint32_t(min(65536ull, end - o)));
+  }
+}
 
 // (a & b) | c as one LOP3 (written out: the C++ form costs an extra logic op per value).
 __device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
@@ -95,14 +147,25 @@ __device__ __forceinline__ float e4m3_x16k(uint32_t s) {
   return __fmul_rn(__half2float(__ushort_as_half(uint16_t((s & 0x7Fu) << 7))), 4194304.0f);
 }
 
-template <int FMT, int M, int W, int TR, int NS, int PRE>
-__global__ void __launch_bounds__(W * 32, 1)
-qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
-           const uint8_t* __restrict__ sc, const uint8_t* __restrict__ bi,
-           uint16_t* __restrict__ y, const uint16_t* __restrict__ res, int N, int ldy,
-           unsigned* __restrict__ err, long long ldx, const uint16_t* __restrict__ pre_w, float eps) {
+template <int FMT, int M, int W, int TR, int NS, int PRE, int EPI>
+__global__ void __launch_bounds__(W * 32, 1) qmv_kernel(const __grid_constant__ QmvParams p) {
   using C = QmvCfg<FMT, M, W, TR, NS>;
   constexpr int K = C::K;
+  // output rows per tile: with EPI_SWIGLU a tile holds HT gate rows (stage rows 0..HT-1) and the
+  // matching HT up rows (stage rows HT..TR-1)
+  constexpr int HT = EPI == EPI_SWIGLU ? TR / 2 : TR;
+  static_assert(EPI != EPI_SWIGLU || TR % 2 == 0, "swiglu tiles pair rows");
+  const uint16_t* __restrict__ x = p.x;
+  const uint32_t* __restrict__ wq = p.wq;
+  const uint8_t* __restrict__ sc = p.sc;
+  const uint8_t* __restrict__ bi = p.bi;
+  uint16_t* __restrict__ y = p.y;
+  const uint16_t* __restrict__ res = p.res;
+  const int N = p.N, ldy = p.ldy;
+  unsigned* __restrict__ err = p.err;
+  const long long ldx = p.ldx;
+  const uint16_t* __restrict__ pre_w = p.pre_w;
+  const float eps = p.eps;
   extern __shared__ __align__(128) unsigned char smem[];
   float* s_red = reinterpret_cast<float*>(smem + C::OFF_RED);
   uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -112,7 +175,7 @@ qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
   const int r0 = int((long long)blockIdx.x * N / gridDim.x);
   const int r1 = int((long long)(blockIdx.x + 1) * N / gridDim.x);
   const int nrows = r1 - r0;
-  const int ntiles = (nrows + TR - 1) / TR;
+  const int ntiles = (nrows + HT - 1) / HT;
 
   if (tid == 0) {
 #pragma unroll
@@ -122,16 +185,20 @@ qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
   __syncthreads();
 
   const uint64_t pol = policy_evict_first();
+  auto issue_rows = [&](int s, int slot, size_t row, int rows) {
+    bulk_g2s(smem + (s * TR + slot) * C::WB, reinterpret_cast<const uint8_t*>(wq) + row * C::WB, rows * C::WB,
+             &s_bar[s], pol);
+    bulk_g2s(smem + C::OFF_S + (s * TR + slot) * C::SB, sc + row * C::SB, rows * C::SB, &s_bar[s], pol);
+    if constexpr (FMT == FMT_AFFINE)
+      bulk_g2s(smem + C::OFF_B + (s * TR + slot) * C::BB, bi + row * C::BB, rows * C::BB, &s_bar[s], pol);
+  };
   auto issue = [&](int t) {
     const int s = t % NS;
-    const int rows = min(TR, nrows - t * TR);
-    const size_t row = size_t(r0) + size_t(t) * TR;
-    mbar_expect_tx(&s_bar[s], uint32_t(rows * (C::WB + C::SB + C::BB)));
-    bulk_g2s(smem + s * TR * C::WB, reinterpret_cast<const uint8_t*>(wq) + row * C::WB, rows * C::WB,
-             &s_bar[s], pol);
-    bulk_g2s(smem + C::OFF_S + s * TR * C::SB, sc + row * C::SB, rows * C::SB, &s_bar[s], pol);
-    if constexpr (FMT == FMT_AFFINE)
-      bulk_g2s(smem + C::OFF_B + s * TR * C::BB, bi + row * C::BB, rows * C::BB, &s_bar[s], pol);
+    const int rows = min(HT, nrows - t * HT);
+    const size_t row = size_t(r0) + size_t(t) * HT;
+    mbar_expect_tx(&s_bar[s], uint32_t((EPI == EPI_SWIGLU ? 2 : 1) * rows * (C::WB + C::SB + C::BB)));
+    issue_rows(s, 0, row, rows);
+    if constexpr (EPI == EPI_SWIGLU) issue_rows(s, HT, row + size_t(N), rows);
   };
   if (tid == 0) {
     const int pre = min(NS - 1, ntiles);
@@ -262,7 +329,9 @@ qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
     }
     const int s = t % NS;
     const bool ok = mbar_wait_bounded(&s_bar[s], uint32_t((t / NS) & 1), err);
-    const int rows = min(TR, nrows - t * TR);
+    const int rows = min(HT, nrows - t * HT);
+    // L2 prefetch for the following kernels once this CTA's own stream is flowing
+    if (t == 0 && tid == 0) issue_prefetch(p.pf);
 
     float val[C::VP];
 #pragma unroll
@@ -342,11 +411,83 @@ qmv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ wq,
 #pragma unroll
       for (int w = 1; w < W; ++w) acc = __fadd_rn(acc, red[w * C::VP + tid]);
       const int r = tid / M, m = tid - (tid / M) * M;
-      const size_t o = size_t(m) * ldy + r0 + t * TR + r;
-      uint16_t out = f2bf(acc);
-      if (res) out = f2bf(__fadd_rn(bf2f(res[o]), bf2f(out)));  // residual: R(res + R(x.W))
+      const size_t o = size_t(m) * ldy + r0 + t * HT + r;
+      uint16_t out;
+      if constexpr (EPI == EPI_SWIGLU) {
+        const int tu = tid + HT * M;  // value (r + HT, m): the up row paired with gate row r
+        float au = red[tu];
+#pragma unroll
+        for (int w = 1; w < W; ++w) au = __fadd_rn(au, red[w * C::VP + tu]);
+        out = f2bf(__fmul_rn(silu_bf(bf2f(f2bf(acc))), bf2f(f2bf(au))));
+      } else {
+        out = f2bf(acc);
+        if (res) out = f2bf(__fadd_rn(bf2f(res[o]), bf2f(out)));  // residual: R(res + R(x.W))
+      }
       y[o] = out;
     }
+  }
+
+  if constexpr (EPI == EPI_NORM) {
+    // Publish this CTA's outputs and count arrivals (threadfence-reduction pattern, no waiting):
+    // the CTA that arrives last sees every row of y and normalises it.
+    float* s_blk = reinterpret_cast<float*>(smem + C::OFF_PRE);  // [M][16] per-warp sums of squares
+    unsigned* s_last = reinterpret_cast<unsigned*>(smem + C::OFF_FLAG + 16);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) *s_last = (atomicAdd(p.sync, 1u) == gridDim.x - 1) ? 1u : 0u;
+    __syncthreads();
+    if (*s_last == 0u) return;
+    __threadfence();
+    // rmsnorm_wide_kernel over D = N features: thread c < D/32 owns elements [32c, 32c + 32).
+    const int nthr = N / 32;
+    uint32_t v[M][16];
+    uint4 wn[4];
+    if (tid < nthr) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) wn[q] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + 32 * tid + 8 * q));
+#pragma unroll
+      for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 u = __ldcg(reinterpret_cast<const uint4*>(y + size_t(m) * ldy + 32 * tid + 8 * q));
+          v[m][4 * q] = u.x; v[m][4 * q + 1] = u.y; v[m][4 * q + 2] = u.z; v[m][4 * q + 3] = u.w;
+        }
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          ss = __fmaf_rn(bflo(v[m][e]), bflo(v[m][e]), ss);
+          ss = __fmaf_rn(bfhi(v[m][e]), bfhi(v[m][e]), ss);
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) s_blk[m * 16 + warp] = ss;
+      }
+    }
+    __syncthreads();
+    if (tid < nthr) {
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        // every thread forms the row factor itself (same sequence as the block's thread 0)
+        float t = s_blk[m * 16];
+        for (int i = 1; i < nthr / 32; ++i) t = __fadd_rn(t, s_blk[m * 16 + i]);
+        const float r = rsqrt_rn(__fadd_rn(__fdiv_rn(t, float(N)), p.norm_eps));
+        uint16_t* orow = p.norm_y + size_t(m) * size_t(p.ldn) + 32 * tid;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t ww[4] = {wn[q].x, wn[q].y, wn[q].z, wn[q].w};
+          uint32_t o[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const uint16_t lo = f2bf(__fmul_rn(bflo(ww[h]), R(__fmul_rn(bflo(v[m][4 * q + h]), r))));
+            const uint16_t hi = f2bf(__fmul_rn(bfhi(ww[h]), R(__fmul_rn(bfhi(v[m][4 * q + h]), r))));
+            o[h] = lo | (uint32_t(hi) << 16);
+          }
+          *reinterpret_cast<uint4*>(orow + 8 * q) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+    }
+    if (tid == 0) *p.sync = 0u;  // ready for the next launch on this counter
   }
 }
 
@@ -355,13 +496,12 @@ struct QmvLaunch {
   int grid_per_sm, block, smem, rows_per_tile, stages;
 };
 
-template <int FMT, int M, int W, int PRE>
-static int launch_qmv(const void* x, const void* w, const void* s, const void* b, void* y, const void* res, int N,
-                      int ldy, cudaStream_t st, QmvLaunch* info, long long ldx, const void* pre_w, float eps) {
+template <int FMT, int M, int W, int PRE, int EPI>
+static int launch_qmv(const QmvParams& p, cudaStream_t st, QmvLaunch* info) {
   constexpr int TR = (W <= 4) ? 8 : 4;
   constexpr int NS = 3;
   using C = QmvCfg<FMT, M, W, TR, NS>;
-  auto kern = qmv_kernel<FMT, M, W, TR, NS, PRE>;
+  auto kern = qmv_kernel<FMT, M, W, TR, NS, PRE, EPI>;
   static int occ = -1;
   static std::once_flag once;
   std::call_once(once, [&] {
@@ -376,58 +516,55 @@ static int launch_qmv(const void* x, const void* w, const void* s, const void* b
     *info = QmvLaunch{occ, W * 32, C::SMEM, TR, NS};
     return QMTP_OK;
   }
-  const int grid = std::max(1, std::min(N, sm_count() * occ));
-  launch_kernel(kern, dim3(grid), dim3(W * 32), C::SMEM, st, static_cast<const uint16_t*>(x), static_cast<const uint32_t*>(w),
-                                        static_cast<const uint8_t*>(s), static_cast<const uint8_t*>(b),
-                                        static_cast<uint16_t*>(y), static_cast<const uint16_t*>(res), N, ldy,
-                                        device_error_ptr(), ldx, static_cast<const uint16_t*>(pre_w), eps);
+  const int grid = std::max(1, std::min(p.N, sm_count() * occ));
+  launch_kernel(kern, dim3(grid), dim3(W * 32), C::SMEM, st, p);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 
-struct QmvArgs {
-  const void *x, *w, *s, *b;
-  void* y;
-  const void* res;
-  int N, ldy;
-  long long ldx;
-  const void* pre_w;
-  float eps;
-};
-
-template <int FMT, int M, int PRE>
-static int dispatch_w(int K, const QmvArgs& a, cudaStream_t st, QmvLaunch* info = nullptr) {
-#define QMTP_QMV_W(WW) launch_qmv<FMT, M, WW, PRE>(a.x, a.w, a.s, a.b, a.y, a.res, a.N, a.ldy, st, info, a.ldx, a.pre_w, a.eps)
+template <int FMT, int M, int PRE, int EPI>
+static int dispatch_w(int K, const QmvParams& p, cudaStream_t st, QmvLaunch* info = nullptr) {
   switch (K) {
-    case 1024: return QMTP_QMV_W(1);
-    case 2048: return QMTP_QMV_W(2);
-    case 4096: return QMTP_QMV_W(4);
-    case 8192: return QMTP_QMV_W(8);
-    case 12288: return QMTP_QMV_W(12);
+    case 1024: return launch_qmv<FMT, M, 1, PRE, EPI>(p, st, info);
+    case 2048: return launch_qmv<FMT, M, 2, PRE, EPI>(p, st, info);
+    case 4096: return launch_qmv<FMT, M, 4, PRE, EPI>(p, st, info);
+    case 8192: return launch_qmv<FMT, M, 8, PRE, EPI>(p, st, info);
+    case 12288: return launch_qmv<FMT, M, 12, PRE, EPI>(p, st, info);
     default: return QMTP_ERR_SHAPE;
   }
-#undef QMTP_QMV_W
 }
 
-template <int FMT, int PRE>
-static int dispatch_m(int M, int K, const QmvArgs& a, cudaStream_t st, QmvLaunch* info = nullptr) {
+template <int FMT, int PRE, int EPI>
+static int dispatch_m(int M, int K, const QmvParams& p, cudaStream_t st, QmvLaunch* info = nullptr) {
   switch (M) {
-    case 1: return dispatch_w<FMT, 1, PRE>(K, a, st, info);
-    case 2: return dispatch_w<FMT, 2, PRE>(K, a, st, info);
-    case 3: return dispatch_w<FMT, 3, PRE>(K, a, st, info);
-    default: return dispatch_w<FMT, 4, PRE>(K, a, st, info);
+    case 1: return dispatch_w<FMT, 1, PRE, EPI>(K, p, st, info);
+    case 2: return dispatch_w<FMT, 2, PRE, EPI>(K, p, st, info);
+    case 3: return dispatch_w<FMT, 3, PRE, EPI>(K, p, st, info);
+    default: return dispatch_w<FMT, 4, PRE, EPI>(K, p, st, info);
   }
 }
 
+// All public qmv entry points land here.  N is the number of output columns (with EPI_SWIGLU the
+// weight matrix holds 2N rows).
 template <int FMT>
 static int qmv_entry(const void* x, const void* w, const void* s, const void* b, void* y, const void* res, int M,
                      int N, int K, int ldy, void* stream, int pre = PRE_NONE, long long ldx = 0,
-                     const void* pre_w = nullptr, float eps = 0.0f) {
+                     const void* pre_w = nullptr, float eps = 0.0f, int epi = EPI_NONE, void* norm_y = nullptr,
+                     const void* norm_w = nullptr, long long ldn = 0, float norm_eps = 0.0f,
+                     unsigned* sync = nullptr, const QPf* pf = nullptr) {
   if (!x || !w || !s || !y || (FMT == FMT_AFFINE && !b)) return QMTP_ERR_ARG;
   if (M < 1 || N < 1 || K < 1024 || K % 1024 != 0 || K > 12288 || ldy < N) return QMTP_ERR_SHAPE;
   if (ldx == 0) ldx = pre == PRE_SWIGLU ? 2LL * K : K;
   if (ldx < (pre == PRE_SWIGLU ? 2LL * K : K) || ldx % 8) return QMTP_ERR_SHAPE;
-  if (pre != PRE_NONE && FMT != FMT_AFFINE) return QMTP_ERR_UNSUPPORTED;
+  if ((pre != PRE_NONE || epi != EPI_NONE) && FMT != FMT_AFFINE) return QMTP_ERR_UNSUPPORTED;
+  if (pre != PRE_NONE && epi != EPI_NONE) return QMTP_ERR_UNSUPPORTED;
   if (pre == PRE_RMSNORM && !pre_w) return QMTP_ERR_ARG;
+  if (epi == EPI_SWIGLU && res) return QMTP_ERR_UNSUPPORTED;
+  if (epi == EPI_NORM) {
+    if (!norm_y || !norm_w || !sync) return QMTP_ERR_ARG;
+    // the normalising CTA has K/32 threads and covers D = N with N/32 of them
+    if (N % 1024 != 0 || N > K || ldy % 8 || ldn < N || ldn % 8) return QMTP_ERR_SHAPE;
+    if (!aligned16(y) || !aligned16(norm_y) || !aligned16(norm_w)) return QMTP_ERR_ALIGN;
+  }
   if (!aligned16(x) || !aligned16(w) || !aligned16(s) || (b && !aligned16(b)) || (pre_w && !aligned16(pre_w)))
     return QMTP_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -435,15 +572,34 @@ static int qmv_entry(const void* x, const void* w, const void* s, const void* b,
   uint16_t* yp = static_cast<uint16_t*>(y);
   for (int m0 = 0; m0 < M; m0 += 4) {
     const int mm = std::min(4, M - m0);
-    QmvArgs a{xp + size_t(m0) * size_t(ldx), w, s, b, yp + size_t(m0) * ldy,
-              res ? static_cast<const uint16_t*>(res) + size_t(m0) * ldy : nullptr, N, ldy, ldx, pre_w, eps};
+    QmvParams p{};
+    p.x = xp + size_t(m0) * size_t(ldx);
+    p.ldx = ldx;
+    p.wq = static_cast<const uint32_t*>(w);
+    p.sc = static_cast<const uint8_t*>(s);
+    p.bi = static_cast<const uint8_t*>(b);
+    p.y = yp + size_t(m0) * ldy;
+    p.res = res ? static_cast<const uint16_t*>(res) + size_t(m0) * ldy : nullptr;
+    p.N = N;
+    p.ldy = ldy;
+    p.err = device_error_ptr();
+    p.pre_w = static_cast<const uint16_t*>(pre_w);
+    p.eps = eps;
+    p.norm_y = norm_y ? static_cast<uint16_t*>(norm_y) + size_t(m0) * size_t(ldn) : nullptr;
+    p.norm_w = static_cast<const uint16_t*>(norm_w);
+    p.ldn = ldn;
+    p.norm_eps = norm_eps;
+    p.sync = sync;
+    if (pf && m0 == 0) p.pf = *pf;
     int rc;
     if constexpr (FMT == FMT_AFFINE) {
-      rc = pre == PRE_RMSNORM ? dispatch_m<FMT, PRE_RMSNORM>(mm, K, a, st)
-         : pre == PRE_SWIGLU  ? dispatch_m<FMT, PRE_SWIGLU>(mm, K, a, st)
-                              : dispatch_m<FMT, PRE_NONE>(mm, K, a, st);
+      rc = pre == PRE_RMSNORM ? dispatch_m<FMT, PRE_RMSNORM, EPI_NONE>(mm, K, p, st)
+         : pre == PRE_SWIGLU  ? dispatch_m<FMT, PRE_SWIGLU, EPI_NONE>(mm, K, p, st)
+         : epi == EPI_SWIGLU  ? dispatch_m<FMT, PRE_NONE, EPI_SWIGLU>(mm, K, p, st)
+         : epi == EPI_NORM    ? dispatch_m<FMT, PRE_NONE, EPI_NORM>(mm, K, p, st)
+                              : dispatch_m<FMT, PRE_NONE, EPI_NONE>(mm, K, p, st);
     } else {
-      rc = dispatch_m<FMT, PRE_NONE>(mm, K, a, st);
+      rc = dispatch_m<FMT, PRE_NONE, EPI_NONE>(mm, K, p, st);
     }
     if (rc != QMTP_OK) return rc;
   }
@@ -504,11 +660,20 @@ extern "C" int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void*
   return qmv_entry<FMT_AFFINE>(x, w, scales, biases, y, res, M, N, K, ldy, stream);
 }
 
-extern "C" int qmtp_qmv_affine_g64_ex(const void* x, long long ldx, int pre, const void* pre_w, float eps,
-                                      const void* w, const void* scales, const void* biases, void* y, const void* res,
-                                      int M, int N, int K, int ldy, void* stream) {
-  if (pre < PRE_NONE || pre > PRE_SWIGLU) return QMTP_ERR_ARG;
-  return qmv_entry<FMT_AFFINE>(x, w, scales, biases, y, res, M, N, K, ldy, stream, pre, ldx, pre_w, eps);
+extern "C" int qmtp_qmv_ex(const qmtp_qmv_args* a, void* stream) {
+  if (!a) return QMTP_ERR_ARG;
+  if (a->pre < PRE_NONE || a->pre > PRE_SWIGLU || a->epi < EPI_NONE || a->epi > EPI_NORM) return QMTP_ERR_ARG;
+  QPf pf{};
+  for (int i = 0; i < 4; ++i) {
+    const long long n = a->prefetch_bytes[i] & ~15LL;
+    if (a->prefetch[i] && n > 0 && aligned16(a->prefetch[i])) {
+      pf.p[i] = static_cast<const uint8_t*>(a->prefetch[i]);
+      pf.n[i] = static_cast<unsigned long long>(n);
+    }
+  }
+  return qmv_entry<FMT_AFFINE>(a->x, a->w, a->scales, a->biases, a->y, a->res, a->M, a->N, a->K, a->ldy, stream,
+                               a->pre, a->ldx, a->pre_w, a->pre_eps, a->epi, a->norm_y, a->norm_w, a->ld_norm,
+                               a->norm_eps, a->sync, &pf);
 }
 
 extern "C" int qmtp_qmv_nvfp4_g16(const void* x, const void* w, const void* scales, void* y, int M, int N, int K,
@@ -524,8 +689,9 @@ extern "C" int qmtp_qmv_launch_info(int fmt, int M, int K, int* ctas_per_sm, int
   int rc;
   auto go = [&](auto fmtc) -> int {
     constexpr int F = decltype(fmtc)::value;
-    const QmvArgs a{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, K, nullptr, 0.0f};
-    return dispatch_m<F, PRE_NONE>(M, K, a, 0, &info);
+    QmvParams p{};
+    p.N = 1;
+    return dispatch_m<F, PRE_NONE, EPI_NONE>(M, K, p, 0, &info);
   };
   rc = fmt == 0 ? go(std::integral_constant<int, FMT_AFFINE>{}) : go(std::integral_constant<int, FMT_NVFP4>{});
   if (rc != QMTP_OK) return rc;

@@ -35,7 +35,6 @@ SIGNATURES: dict[str, list] = {
     "qmtp_device_error": [ctypes.POINTER(ctypes.c_uint), _I],
     "qmtp_qmv_affine_g64": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_qmv_nvfp4_g16": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
-    "qmtp_qmv_affine_g64_ex": [_P, ctypes.c_longlong, _I, _P, _F, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_quantize_affine_g64": [_P, _P, _P, _P, _I, _I, _P],
     "qmtp_qmv_launch_info": [_I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
                              ctypes.POINTER(_I)],
@@ -55,7 +54,21 @@ class GdnArgs(ctypes.Structure):
                 ("S", _I), ("Hk", _I), ("Hv", _I), ("Dk", _I), ("Dv", _I), ("KC", _I), ("snap", _I)]
 
 
+class QmvArgs(ctypes.Structure):
+    """Mirror of qmtp_qmv_args (include/qmtp.h)."""
+    _fields_ = [("x", _P), ("ldx", ctypes.c_longlong), ("w", _P), ("scales", _P), ("biases", _P),
+                ("y", _P), ("res", _P), ("M", _I), ("N", _I), ("K", _I), ("ldy", _I),
+                ("pre", _I), ("pre_w", _P), ("pre_eps", _F),
+                ("epi", _I), ("norm_y", _P), ("norm_w", _P), ("ld_norm", ctypes.c_longlong), ("norm_eps", _F),
+                ("sync", _P), ("prefetch", _P * 4), ("prefetch_bytes", ctypes.c_longlong * 4)]
+
+
+QMV_PRE_NONE, QMV_PRE_RMSNORM, QMV_PRE_SWIGLU = 0, 1, 2
+QMV_EPI_NONE, QMV_EPI_SWIGLU, QMV_EPI_NORM = 0, 1, 2
+
+
 SIGNATURES.update({
+    "qmtp_qmv_ex": [ctypes.POINTER(QmvArgs), _P],
     "qmtp_gdn_step": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
     "qmtp_gdn_fused": [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
     "qmtp_gdn_fused_ex": [ctypes.POINTER(GdnArgs), _P],
