@@ -193,37 +193,65 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
     for (int e = 0; e < 4; ++e) { qf[2 * e] = bflo(uu[e]); qf[2 * e + 1] = bfhi(uu[e]); }
   }
   const float scale = rsqrt_rn(float(Dh));
-  // pass 1: scores and split max
+  // pass 1: scores and split max.  Keys are taken kU at a time so their loads overlap; every score
+  // is still lane-sequential fmas + warp_sum, and the split max is taken in key order.
+  constexpr int kU = 16;
   float mw = __int_as_float(0xFF800000);
-  int n = 0;
-  for (int j = w; j < L; j += kAttnSplits, ++n) {
-    const uint4 u = *reinterpret_cast<const uint4*>(kc + ((long long)kh * max_pos + j) * Dh + NP * lane);
-    const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
-    float acc = 0.0f;
+  for (int n0 = 0; w + kAttnSplits * n0 < L; n0 += kU) {
+    uint4 kr[kU];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      acc = __fmaf_rn(qf[2 * e], bflo(uu[e]), acc);
-      acc = __fmaf_rn(qf[2 * e + 1], bfhi(uu[e]), acc);
+    for (int u = 0; u < kU; ++u) {
+      const int j = w + kAttnSplits * (n0 + u);
+      if (j < L) kr[u] = *reinterpret_cast<const uint4*>(kc + ((long long)kh * max_pos + j) * Dh + NP * lane);
     }
-    const float sc = __fmul_rn(warp_sum(acc), scale);
-    if (lane == 0) s_sc[w * stride_sc + n] = sc;
-    mw = sc > mw ? sc : mw;
+    float acc[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const uint32_t uu[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
+      acc[u] = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[u] = __fmaf_rn(qf[2 * e], bflo(uu[e]), acc[u]);
+        acc[u] = __fmaf_rn(qf[2 * e + 1], bfhi(uu[e]), acc[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int j = w + kAttnSplits * (n0 + u);
+      if (j >= L) break;
+      const float sc = __fmul_rn(warp_sum(acc[u]), scale);
+      if (lane == 0) s_sc[w * stride_sc + n0 + u] = sc;
+      mw = sc > mw ? sc : mw;
+    }
   }
   __syncwarp();
-  // pass 2: exp, denominator, numerator (this lane's 8 dims)
+  // pass 2: exp, denominator, numerator (this lane's 8 dims), sequential in key order per split;
+  // the value rows and exponentials of kU keys are fetched ahead of the accumulation chains.
   float den = 0.0f, num[NP];
 #pragma unroll
   for (int e = 0; e < NP; ++e) num[e] = 0.0f;
-  n = 0;
-  for (int j = w; j < L; j += kAttnSplits, ++n) {
-    const float e_ = q_expf(__fsub_rn(s_sc[w * stride_sc + n], mw));
-    den = __fadd_rn(den, e_);
-    const uint4 u = *reinterpret_cast<const uint4*>(vc + ((long long)kh * max_pos + j) * Dh + NP * lane);
-    const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+  for (int n0 = 0; w + kAttnSplits * n0 < L; n0 += kU) {
+    uint4 vr[kU];
+    float ex[kU];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      num[2 * e] = __fmaf_rn(e_, bflo(uu[e]), num[2 * e]);
-      num[2 * e + 1] = __fmaf_rn(e_, bfhi(uu[e]), num[2 * e + 1]);
+    for (int u = 0; u < kU; ++u) {
+      const int j = w + kAttnSplits * (n0 + u);
+      if (j < L) {
+        vr[u] = *reinterpret_cast<const uint4*>(vc + ((long long)kh * max_pos + j) * Dh + NP * lane);
+        ex[u] = q_expf(__fsub_rn(s_sc[w * stride_sc + n0 + u], mw));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int j = w + kAttnSplits * (n0 + u);
+      if (j >= L) break;
+      den = __fadd_rn(den, ex[u]);
+      const uint32_t uu[4] = {vr[u].x, vr[u].y, vr[u].z, vr[u].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        num[2 * e] = __fmaf_rn(ex[u], bflo(uu[e]), num[2 * e]);
+        num[2 * e + 1] = __fmaf_rn(ex[u], bfhi(uu[e]), num[2 * e + 1]);
+      }
     }
   }
 #pragma unroll
