@@ -161,10 +161,30 @@ __global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld,
 }
 
 // ----------------------------------------------------------------------------- attention
-// grid (nq, S); 8 warps = 8 key splits; Dh == 256 (lane owns 8 dims); scores in shared memory.
+// One thread-block cluster of kAttnSplits CTAs per (query head, token); CTA rank w owns key split w
+// (keys j = w, w + 8, ...).  Dh == 256.  Per CTA: scores (8 warps, lane owns 8 dims, warp_sum) ->
+// split max -> exponentials -> den (one sequential chain) and num[d] (thread d, keys ascending) in
+// shared memory.  Rank 0 then merges the 8 splits in order through distributed shared memory.
 constexpr int kAttnSplits = 8;
+constexpr int kAttnBatch = 8;   // keys a warp fetches at once in the score pass
 
-__global__ void __launch_bounds__(kAttnSplits * 32)
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem(const float* local, uint32_t rank) {
+  uint32_t la = static_cast<uint32_t>(__cvta_generic_to_shared(local)), ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(256)
 attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ gate, const uint16_t* __restrict__ kc,
                  const uint16_t* __restrict__ vc, int max_pos, int nq, int nkv, const int* __restrict__ pos_ptr,
                  int pos_add, uint16_t* __restrict__ out, unsigned* err) {
@@ -172,19 +192,20 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
   pdl_wait();
   constexpr int Dh = 256, NP = 8;
   extern __shared__ __align__(16) float sm[];
-  float* s_num = sm;                              // [8][Dh]
-  float* s_m = s_num + kAttnSplits * Dh;          // [8]
-  float* s_den = s_m + kAttnSplits;               // [8]
-  float* s_sc = s_den + kAttnSplits;              // [8][max_pos/8 + 1]
-  const int h = blockIdx.x, s = blockIdx.y, S = gridDim.y;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float* s_num = sm;                 // [Dh] this split's numerator
+  float* s_md = s_num + Dh;          // [2] split max, denominator
+  float* s_red = s_md + 2;           // [8] per-warp maxima
+  float* s_sc = s_red + 8;           // [max_pos / 8 + 1] scores, then exponentials
+  const int w = int(cluster_rank());  // key split
+  const int h = blockIdx.x / kAttnSplits, s = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int L = (pos_ptr ? *pos_ptr : 0) + pos_add + s + 1;
-  const int stride_sc = max_pos / kAttnSplits + 1;
-  if (L < 1 || L > max_pos) {
-    if (threadIdx.x == 0) atomicOr(err, DEVERR_BADARG);
+  if (L < 1 || L > max_pos) {  // uniform over the cluster: every CTA leaves before any barrier
+    if (tid == 0 && w == 0) atomicOr(err, DEVERR_BADARG);
     return;
   }
   const int kh = h / (nq / nkv);
+  const int nk = w < L ? (L - w + kAttnSplits - 1) / kAttnSplits : 0;  // keys of this split
   float qf[NP];
   {
     const uint4 u = *reinterpret_cast<const uint4*>(q + ((long long)s * nq + h) * Dh + NP * lane);
@@ -193,20 +214,21 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
     for (int e = 0; e < 4; ++e) { qf[2 * e] = bflo(uu[e]); qf[2 * e + 1] = bfhi(uu[e]); }
   }
   const float scale = rsqrt_rn(float(Dh));
-  // pass 1: scores and split max.  Keys are taken kU at a time so their loads overlap; every score
-  // is still lane-sequential fmas + warp_sum, and the split max is taken in key order.
-  constexpr int kU = 16;
-  float mw = __int_as_float(0xFF800000);
-  for (int n0 = 0; w + kAttnSplits * n0 < L; n0 += kU) {
-    uint4 kr[kU];
+  // scores: warp `warp` takes split-local keys n = warp, warp + 8, ...; a score is lane-sequential
+  // fmas over the lane's 8 dims + warp_sum (independent per key, so any distribution gives the
+  // same values); the max is exact, hence order-free
+  float mx = __int_as_float(0xFF800000);
+  for (int n0 = warp; n0 < nk; n0 += 8 * kAttnBatch) {
+    uint4 kr[kAttnBatch];
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int j = w + kAttnSplits * (n0 + u);
-      if (j < L) kr[u] = *reinterpret_cast<const uint4*>(kc + ((long long)kh * max_pos + j) * Dh + NP * lane);
+    for (int u = 0; u < kAttnBatch; ++u) {
+      const int n = n0 + 8 * u;
+      if (n < nk)
+        kr[u] = *reinterpret_cast<const uint4*>(kc + ((long long)kh * max_pos + w + kAttnSplits * n) * Dh + NP * lane);
     }
-    float acc[kU];
+    float acc[kAttnBatch];
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
+    for (int u = 0; u < kAttnBatch; ++u) {
       const uint32_t uu[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
       acc[u] = 0.0f;
 #pragma unroll
@@ -216,64 +238,68 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
       }
     }
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int j = w + kAttnSplits * (n0 + u);
-      if (j >= L) break;
-      const float sc = __fmul_rn(warp_sum(acc[u]), scale);
-      if (lane == 0) s_sc[w * stride_sc + n0 + u] = sc;
-      mw = sc > mw ? sc : mw;
-    }
-  }
-  __syncwarp();
-  // pass 2: exp, denominator, numerator (this lane's 8 dims), sequential in key order per split;
-  // the value rows and exponentials of kU keys are fetched ahead of the accumulation chains.
-  float den = 0.0f, num[NP];
+    for (int d = 16; d >= 1; d >>= 1)
 #pragma unroll
-  for (int e = 0; e < NP; ++e) num[e] = 0.0f;
-  for (int n0 = 0; w + kAttnSplits * n0 < L; n0 += kU) {
-    uint4 vr[kU];
-    float ex[kU];
+      for (int u = 0; u < kAttnBatch; ++u) acc[u] = __fadd_rn(acc[u], __shfl_xor_sync(0xFFFFFFFFu, acc[u], d));
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int j = w + kAttnSplits * (n0 + u);
-      if (j < L) {
-        vr[u] = *reinterpret_cast<const uint4*>(vc + ((long long)kh * max_pos + j) * Dh + NP * lane);
-        ex[u] = q_expf(__fsub_rn(s_sc[w * stride_sc + n0 + u], mw));
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int j = w + kAttnSplits * (n0 + u);
-      if (j >= L) break;
-      den = __fadd_rn(den, ex[u]);
-      const uint32_t uu[4] = {vr[u].x, vr[u].y, vr[u].z, vr[u].w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        num[2 * e] = __fmaf_rn(ex[u], bflo(uu[e]), num[2 * e]);
-        num[2 * e + 1] = __fmaf_rn(ex[u], bfhi(uu[e]), num[2 * e + 1]);
+    for (int u = 0; u < kAttnBatch; ++u) {
+      const int n = n0 + 8 * u;
+      if (n < nk) {
+        const float sc = __fmul_rn(acc[u], scale);
+        if (lane == 0) s_sc[n] = sc;
+        mx = sc > mx ? sc : mx;
       }
     }
   }
-#pragma unroll
-  for (int e = 0; e < NP; ++e) s_num[w * Dh + NP * lane + e] = num[e];
-  if (lane == 0) { s_m[w] = mw; s_den[w] = den; }
+  if (lane == 0) s_red[warp] = mx;
   __syncthreads();
-  // merge: thread d owns output dim d
-  const int d = threadIdx.x;
-  float M = __int_as_float(0xFF800000);
-  for (int ww = 0; ww < kAttnSplits; ++ww)
-    if (ww < L && s_m[ww] > M) M = s_m[ww];
-  float dsum = 0.0f, acc = 0.0f;
-  for (int ww = 0; ww < kAttnSplits; ++ww) {
-    if (ww >= L) continue;
-    const float cw = q_expf(__fsub_rn(s_m[ww], M));
-    dsum = __fmaf_rn(cw, s_den[ww], dsum);
-    acc = __fmaf_rn(cw, s_num[ww * Dh + d], acc);
+  float mw = s_red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) mw = s_red[i] > mw ? s_red[i] : mw;
+  // exponentials (parallel), then the two sequential chains of the split
+  for (int n = tid; n < nk; n += 256) s_sc[n] = q_expf(__fsub_rn(s_sc[n], mw));
+  __syncthreads();
+  if (tid == 0) {
+    float den = 0.0f;
+    for (int n = 0; n < nk; ++n) den = __fadd_rn(den, s_sc[n]);
+    s_md[0] = mw;
+    s_md[1] = den;
   }
-  const float o = R(__fdiv_rn(acc, dsum));
-  const float gt = bf2f(gate[((long long)s * nq + h) * Dh + d]);
-  out[(long long)s * nq * Dh + (long long)h * Dh + d] = f2bf(__fmul_rn(o, sigmoid_bf(gt)));
-  (void)S;
+  {
+    const int d = tid;
+    float num = 0.0f;
+    const uint16_t* vb = vc + ((long long)kh * max_pos + w) * Dh + d;
+    for (int n0 = 0; n0 < nk; n0 += 16) {
+      uint16_t v16[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        if (n0 + u < nk) v16[u] = vb[(long long)kAttnSplits * (n0 + u) * Dh];
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        if (n0 + u < nk) num = __fmaf_rn(s_sc[n0 + u], bf2f(v16[u]), num);
+    }
+    s_num[d] = num;
+  }
+  cluster_sync_all();  // every split's (max, den, num) is visible to rank 0
+  if (w == 0) {
+    const int d = tid;
+    const int nsplit = L < kAttnSplits ? L : kAttnSplits;
+    float M = __int_as_float(0xFF800000);
+    for (int ww = 0; ww < nsplit; ++ww) {
+      const float m = ld_dsmem(s_md, ww);
+      if (m > M) M = m;
+    }
+    float dsum = 0.0f, acc = 0.0f;
+    for (int ww = 0; ww < nsplit; ++ww) {
+      const float cw = q_expf(__fsub_rn(ld_dsmem(s_md, ww), M));
+      dsum = __fmaf_rn(cw, ld_dsmem(s_md + 1, ww), dsum);
+      acc = __fmaf_rn(cw, ld_dsmem(s_num + d, ww), acc);
+    }
+    const float o = R(__fdiv_rn(acc, dsum));
+    const float gt = bf2f(gate[((long long)s * nq + h) * Dh + d]);
+    out[(long long)s * nq * Dh + (long long)h * Dh + d] = f2bf(__fmul_rn(o, sigmoid_bf(gt)));
+  }
+  cluster_sync_all();  // rank 0 has read the other CTAs' shared memory before they exit
 }
 
 // ----------------------------------------------------------------------------- SwiGLU
@@ -389,16 +415,28 @@ extern "C" int qmtp_attention(const void* q, const void* gate, const void* k_cac
                               void* stream) {
   if (!q || !gate || !k_cache || !v_cache || !out) return QMTP_ERR_ARG;
   if (Dh != 256 || S < 1 || nq < 1 || nkv < 1 || nq % nkv || max_pos < 8) return QMTP_ERR_UNSUPPORTED;
-  const size_t smem = (size_t(kAttnSplits) * 256 + 2 * kAttnSplits + size_t(kAttnSplits) * (max_pos / kAttnSplits + 1)) *
-                      sizeof(float);
+  const size_t smem = (size_t(Dh) + 2 + 8 + size_t(max_pos / kAttnSplits + 1)) * sizeof(float);
   if (smem > 200 * 1024) return QMTP_ERR_SHAPE;
   static const cudaError_t attr =
       cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (attr != cudaSuccess) return QMTP_ERR_CUDA;
-  launch_kernel(attention_kernel, dim3(dim3(nq, S)), dim3(kAttnSplits * 32), smem, static_cast<cudaStream_t>(stream), 
-      static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(gate), static_cast<const uint16_t*>(k_cache),
-      static_cast<const uint16_t*>(v_cache), max_pos, nq, nkv, pos_ptr, pos_add, static_cast<uint16_t*>(out),
-      device_error_ptr());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(nq * kAttnSplits), unsigned(S));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = kAttnSplits;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  cudaLaunchKernelEx(&cfg, attention_kernel, static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(gate),
+                     static_cast<const uint16_t*>(k_cache), static_cast<const uint16_t*>(v_cache), max_pos, nq, nkv,
+                     pos_ptr, pos_add, static_cast<uint16_t*>(out), device_error_ptr());
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 
