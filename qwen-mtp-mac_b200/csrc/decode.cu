@@ -265,36 +265,50 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
     s_md[0] = mw;
     s_md[1] = den;
   }
-  {
-    const int d = tid;
-    float num = 0.0f;
-    const uint16_t* vb = vc + ((long long)kh * max_pos + w) * Dh + d;
-    for (int n0 = 0; n0 < nk; n0 += 16) {
-      uint16_t v16[16];
+  if (tid < Dh / 2) {
+    // thread t owns dims 2t, 2t+1: one 32-bit load per key, 32 keys in flight per batch
+    float num0 = 0.0f, num1 = 0.0f;
+    const uint32_t* vb = reinterpret_cast<const uint32_t*>(vc + ((long long)kh * max_pos + w) * Dh) + tid;
+    for (int n0 = 0; n0 < nk; n0 += 32) {
+      uint32_t v2[32];
 #pragma unroll
-      for (int u = 0; u < 16; ++u)
-        if (n0 + u < nk) v16[u] = vb[(long long)kAttnSplits * (n0 + u) * Dh];
+      for (int u = 0; u < 32; ++u)
+        if (n0 + u < nk) v2[u] = vb[(long long)kAttnSplits * (n0 + u) * (Dh / 2)];
 #pragma unroll
-      for (int u = 0; u < 16; ++u)
-        if (n0 + u < nk) num = __fmaf_rn(s_sc[n0 + u], bf2f(v16[u]), num);
+      for (int u = 0; u < 32; ++u)
+        if (n0 + u < nk) {
+          const float e = s_sc[n0 + u];
+          num0 = __fmaf_rn(e, bflo(v2[u]), num0);
+          num1 = __fmaf_rn(e, bfhi(v2[u]), num1);
+        }
     }
-    s_num[d] = num;
+    s_num[2 * tid] = num0;
+    s_num[2 * tid + 1] = num1;
   }
   cluster_sync_all();  // every split's (max, den, num) is visible to rank 0
   if (w == 0) {
     const int d = tid;
     const int nsplit = L < kAttnSplits ? L : kAttnSplits;
+    float mm[kAttnSplits], dd[kAttnSplits], nn[kAttnSplits];
+#pragma unroll
+    for (int ww = 0; ww < kAttnSplits; ++ww)
+      if (ww < nsplit) {
+        mm[ww] = ld_dsmem(s_md, ww);
+        dd[ww] = ld_dsmem(s_md + 1, ww);
+        nn[ww] = ld_dsmem(s_num + d, ww);
+      }
     float M = __int_as_float(0xFF800000);
-    for (int ww = 0; ww < nsplit; ++ww) {
-      const float m = ld_dsmem(s_md, ww);
-      if (m > M) M = m;
-    }
+#pragma unroll
+    for (int ww = 0; ww < kAttnSplits; ++ww)
+      if (ww < nsplit && mm[ww] > M) M = mm[ww];
     float dsum = 0.0f, acc = 0.0f;
-    for (int ww = 0; ww < nsplit; ++ww) {
-      const float cw = q_expf(__fsub_rn(ld_dsmem(s_md, ww), M));
-      dsum = __fmaf_rn(cw, ld_dsmem(s_md + 1, ww), dsum);
-      acc = __fmaf_rn(cw, ld_dsmem(s_num + d, ww), acc);
-    }
+#pragma unroll
+    for (int ww = 0; ww < kAttnSplits; ++ww)
+      if (ww < nsplit) {
+        const float cw = q_expf(__fsub_rn(mm[ww], M));
+        dsum = __fmaf_rn(cw, dd[ww], dsum);
+        acc = __fmaf_rn(cw, nn[ww], acc);
+      }
     const float o = R(__fdiv_rn(acc, dsum));
     const float gt = bf2f(gate[((long long)s * nq + h) * Dh + d]);
     out[(long long)s * nq * Dh + (long long)h * Dh + d] = f2bf(__fmul_rn(o, sigmoid_bf(gt)));
