@@ -83,6 +83,7 @@ class MTPDecoder:
         self.graph = None
         self.launches = 0      # kernels launched by the library calls of this decoder
         self.prof = None       # list of (bytes, start event, end event, shape) while profiling qmv
+        self.qmv_log = None    # list of the _qmv argument tuples of a cycle while recording
 
     # ------------------------------------------------------------------ helpers
     def _cp(self, slot: int) -> int:
@@ -103,6 +104,8 @@ class MTPDecoder:
         """4-bit GEMV y = x . W^T (+ res), one qmtp_qmv_ex launch per 4 rows."""
         N, K = lin.out_features, lin.in_features
         ldy = ldy or N
+        if self.qmv_log is not None:
+            self.qmv_log.append((x, lin, y, M, res, ldy))
         self.launches += (M + 3) // 4
         if self.prof is not None:
             e0 = torch.cuda.Event(enable_timing=True)
