@@ -95,18 +95,51 @@ gdn_fused_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
     return silu_bf(R(acc));
   };
 
-  // phase 1: conv + silu of this head's q / k channels and of the CTA's v channels; gates
-  for (int idx = tid; idx < S * 2 * Dk; idx += blockDim.x) {
-    const int t = idx / (2 * Dk), rem = idx - t * 2 * Dk, isk = rem / Dk, e = rem - isk * Dk;
-    qk[idx] = conv(t, isk * Hk * Dk + hk * Dk + e);
+  // The state rows of phase 3 do not depend on phases 1-2: fetch them first so their latency
+  // overlaps the convolution.
+  const size_t per = size_t(Hv) * Dv * Dk;
+  const float* sin = A.state_in;
+  int cur = 0;
+  if (A.ring) {
+    cur = *A.ring_cur;
+    if (cur < 0 || cur >= A.ring_slots) {
+      if (tid == 0) atomicOr(err, DEVERR_BADARG);
+      return;
+    }
+    sin = A.ring + size_t(cur) * per;
   }
-  for (int idx = tid; idx < S * kFusedDVB; idx += blockDim.x) {
+  float st[kFusedRPW][NP];
+#pragma unroll
+  for (int rr = 0; rr < kFusedRPW; ++rr) {
+    const int dv = dv0 + warp * kFusedRPW + rr;
+    if (dv < Dv) {
+      const float4 s4 = *reinterpret_cast<const float4*>(sin + (size_t(hv) * Dv + dv) * Dk + NP * lane);
+      st[rr][0] = s4.x; st[rr][1] = s4.y; st[rr][2] = s4.z; st[rr][3] = s4.w;
+    }
+  }
+
+  // phase 1: conv + silu of this head's q / k channels and of the CTA's v channels; gates.
+  // q / k: a thread per channel over the tokens (the loads of consecutive tokens overlap).
+  for (int cc = tid; cc < 2 * Dk; cc += blockDim.x) {
+    const int isk = cc / Dk, e = cc - isk * Dk, ch = isk * Hk * Dk + hk * Dk + e;
+    int t = 0;
+    for (; t + 4 <= S; t += 4) {
+      float o[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) o[u] = conv(t + u, ch);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) qk[(t + u) * 2 * Dk + cc] = o[u];
+    }
+    for (; t < S; ++t) qk[t * 2 * Dk + cc] = conv(t, ch);
+  }
+  // v channels from the last warps and the gates from warp 5, so no warp carries all three parts
+  for (int idx = int(blockDim.x) - 1 - tid; idx < S * kFusedDVB && idx >= 0; idx += blockDim.x) {
     const int t = idx / kFusedDVB, d = idx - t * kFusedDVB;
     vs[idx] = (dv0 + d < Dv) ? conv(t, 2 * Hk * Dk + hv * Dv + dv0 + d) : 0.0f;
   }
   const uint16_t* av = static_cast<const uint16_t*>(A.a);
   const uint16_t* bv = static_cast<const uint16_t*>(A.b);
-  for (int t = tid; t < S; t += blockDim.x) {
+  for (int t = tid - 160; t >= 0 && t < S; t += blockDim.x) {
     const float Aneg = -q_expf(A.A_log[hv]);
     const float dtb = bf2f(static_cast<const uint16_t*>(A.dt_bias)[hv]);
     const float sp = softplus_bf(R(__fadd_rn(bf2f(av[(long long)t * A.ld_ab + hv]), dtb)));
@@ -117,8 +150,12 @@ gdn_fused_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
   if (A.win_out) {
     uint16_t* wo = static_cast<uint16_t*>(A.win_out) + (long long)(A.win_out_row_off ? *A.win_out_row_off : 0) * C;
     const int R_ = KC - 1 + S;
-    if (dv0 == 0 && hv % (Hv / Hk) == 0) {
-      for (int idx = tid; idx < R_ * 2 * Dk; idx += blockDim.x) {
+    {
+      // the q/k channels of key head hk are shared by its rep x gridDim.y CTAs: each writes a slice
+      const int rep = Hv / Hk, nsl = rep * int(gridDim.y), j = (hv - hk * rep) * int(gridDim.y) + int(blockIdx.y);
+      const int E = R_ * 2 * Dk, per_sl = (E + nsl - 1) / nsl;
+      const int i1 = min(E, (j + 1) * per_sl);
+      for (int idx = j * per_sl + tid; idx < i1; idx += blockDim.x) {
         const int r = idx / (2 * Dk), rem = idx - r * 2 * Dk, isk = rem / Dk, e = rem - isk * Dk;
         const int ch = isk * Hk * Dk + hk * Dk + e;
         wo[(long long)r * C + ch] = win(r, ch);
@@ -151,26 +188,6 @@ gdn_fused_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
   __syncthreads();
 
   // phase 3: the delta rule for this warp's dv rows, states in registers
-  const size_t per = size_t(Hv) * Dv * Dk;
-  const float* sin = A.state_in;
-  int cur = 0;
-  if (A.ring) {
-    cur = *A.ring_cur;
-    if (cur < 0 || cur >= A.ring_slots) {
-      if (tid == 0) atomicOr(err, DEVERR_BADARG);
-      return;
-    }
-    sin = A.ring + size_t(cur) * per;
-  }
-  float st[kFusedRPW][NP];
-#pragma unroll
-  for (int rr = 0; rr < kFusedRPW; ++rr) {
-    const int dv = dv0 + warp * kFusedRPW + rr;
-    if (dv < Dv) {
-      const float4 s4 = *reinterpret_cast<const float4*>(sin + (size_t(hv) * Dv + dv) * Dk + NP * lane);
-      st[rr][0] = s4.x; st[rr][1] = s4.y; st[rr][2] = s4.z; st[rr][3] = s4.w;
-    }
-  }
   for (int t = 0; t < S; ++t) {
     const float4 q4 = *reinterpret_cast<const float4*>(qk + (t * 2 + 0) * Dk + NP * lane);
     const float4 k4 = *reinterpret_cast<const float4*>(qk + (t * 2 + 1) * Dk + NP * lane);
