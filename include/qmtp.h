@@ -239,7 +239,7 @@ int qmtp_rmsnorm(const void* x, int ld_x, const int* row_sel, const void* w, flo
 
 /* Gated-attention input prep (Dh 256, rotary 64): per-head q/k RMS norm, rotate-half RoPE from the
  * cos/sin tables [max_pos][32], q and gate out [S, nq, Dh], k and v appended to the caches
- * [nkv, max_pos, Dh] at position *pos_ptr + pos_add + s. */
+ * [nkv, max_pos, Dh] at position *pos_ptr + pos_add + s.  qkv, qn_w, kn_w 16-byte aligned. */
 int qmtp_attn_prep(const void* qkv, int ld, int S, int nq, int nkv, int Dh, int rotary, const void* qn_w,
                    const void* kn_w, float eps, const float* cos_t, const float* sin_t, const int* pos_ptr,
                    int pos_add, void* q_out, void* gate_out, void* k_cache, void* v_cache, int max_pos,

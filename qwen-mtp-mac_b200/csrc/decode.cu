@@ -47,10 +47,13 @@ __global__ void rmsnorm_wide_kernel(const uint16_t* __restrict__ x, long long ld
                                     const uint16_t* __restrict__ w, float eps, uint16_t* __restrict__ out,
                                     long long ld_o, int D) {
   pdl_trigger();
-  pdl_wait();
   __shared__ float s_blk[32];
   __shared__ float s_r;
   const int m = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
+  uint4 wq4[4];  // the norm weight is constant: fetched while the previous kernel may still run
+#pragma unroll
+  for (int q = 0; q < 4; ++q) wq4[q] = *reinterpret_cast<const uint4*>(w + 32 * c + 8 * q);
+  pdl_wait();
   const long long row = row_sel ? (long long)(*row_sel) + m : m;
   const uint16_t* xr = x + row * ld_x + 32 * c;
   float v[32];
@@ -77,8 +80,7 @@ __global__ void rmsnorm_wide_kernel(const uint16_t* __restrict__ x, long long ld
   uint16_t* orow = out + (long long)m * ld_o + 32 * c;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const uint4 wu = *reinterpret_cast<const uint4*>(w + 32 * c + 8 * q);
-    const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
+    const uint32_t ww[4] = {wq4[q].x, wq4[q].y, wq4[q].z, wq4[q].w};
     uint32_t o[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
@@ -100,12 +102,14 @@ __global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld,
                                  uint16_t* __restrict__ gate, uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
                                  int max_pos, unsigned* err) {
   pdl_trigger();
-  pdl_wait();
   constexpr int Dh = 256, NP = 8, RH = 32;  // rotary half
   const int lane = threadIdx.x & 31;
   const int wid = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (wid >= S * (nq + nkv)) return;
   const int s = wid / (nq + nkv), hh = wid - s * (nq + nkv);
+  // the q / k norm weights are constant: fetched while the previous kernel may still run
+  const uint4 wn4 = *reinterpret_cast<const uint4*>((hh < nq ? qn_w : kn_w) + NP * lane);
+  pdl_wait();
   const int pos = (pos_ptr ? *pos_ptr : 0) + pos_add + s;
   if (pos < 0 || pos >= max_pos) {
     if (lane == 0) atomicOr(err, DEVERR_BADARG);
@@ -126,9 +130,12 @@ __global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld,
   for (int e = 0; e < NP; ++e) ss = __fmaf_rn(x[e], x[e], ss);
   ss = warp_sum(ss);
   const float r = rsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(Dh)), eps));
-  const uint16_t* wn = isq ? qn_w : kn_w;
+  {
+    const uint32_t wv[4] = {wn4.x, wn4.y, wn4.z, wn4.w};
 #pragma unroll
-  for (int e = 0; e < NP; ++e) x[e] = R(__fmul_rn(bf2f(wn[NP * lane + e]), R(__fmul_rn(x[e], r))));
+    for (int e = 0; e < NP; ++e)
+      x[e] = R(__fmul_rn((e & 1) ? bfhi(wv[e >> 1]) : bflo(wv[e >> 1]), R(__fmul_rn(x[e], r))));
+  }
   // rotate-half over dims [0, 64): lane l (< 8) pairs with lane l ^ 4
   float o[NP];
 #pragma unroll
@@ -415,6 +422,7 @@ extern "C" int qmtp_attn_prep(const void* qkv, int ld, int S, int nq, int nkv, i
                               void* stream) {
   if (!qkv || !qn_w || !kn_w || !cos_t || !sin_t || !q_out || !gate_out || !k_cache || !v_cache) return QMTP_ERR_ARG;
   if (Dh != 256 || rotary != 64 || S < 1 || nq < 1 || nkv < 1 || nq % nkv || ld % 8) return QMTP_ERR_UNSUPPORTED;
+  if (!aligned16(qkv) || !aligned16(qn_w) || !aligned16(kn_w)) return QMTP_ERR_ALIGN;
   const int warps = S * (nq + nkv), wpb = 8;
   launch_kernel(attn_prep_kernel, dim3((warps + wpb - 1) / wpb), dim3(wpb * 32), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const uint16_t*>(qkv), ld, S, nq, nkv, static_cast<const uint16_t*>(qn_w),

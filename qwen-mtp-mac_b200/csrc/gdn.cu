@@ -235,14 +235,19 @@ gdn_norm_gate_kernel(const float* __restrict__ y, const uint16_t* __restrict__ z
                      const uint16_t* __restrict__ w, uint16_t* __restrict__ out, long long ld_out, int S, int H,
                      float eps) {
   pdl_trigger();
-  pdl_wait();
   constexpr int Dv = NP * 32;
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;  // t*H + h
   if (row >= S * H) return;
   const int t = row / H, h = row - t * H;
+  float wv[NP];  // the norm weight is constant: fetched while the previous kernel may still run
+#pragma unroll
+  for (int i = 0; i < NP; ++i) wv[i] = bf2f(w[NP * lane + i]);
+  pdl_wait();
   const float* yr = y + size_t(row) * Dv + NP * lane;
-  float yv[NP];
+  float yv[NP], zv[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) zv[i] = bf2f(z[(long long)t * ld_z + (long long)h * Dv + NP * lane + i]);
   float ss = 0.0f;
 #pragma unroll
   for (int i = 0; i < NP; ++i) { yv[i] = yr[i]; ss = __fmaf_rn(yv[i], yv[i], ss); }
@@ -251,9 +256,8 @@ gdn_norm_gate_kernel(const float* __restrict__ y, const uint16_t* __restrict__ z
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
     const int e = NP * lane + i;
-    const float xn = R(__fmul_rn(bf2f(w[e]), R(__fmul_rn(yv[i], r))));
-    const float zz = bf2f(z[(long long)t * ld_z + (long long)h * Dv + e]);
-    out[(long long)t * ld_out + (long long)h * Dv + e] = f2bf(__fmul_rn(xn, silu_f32(zz)));
+    const float xn = R(__fmul_rn(wv[i], R(__fmul_rn(yv[i], r))));
+    out[(long long)t * ld_out + (long long)h * Dv + e] = f2bf(__fmul_rn(xn, silu_f32(zv[i])));
   }
 }
 
