@@ -172,9 +172,14 @@ __global__ void __launch_bounds__(W * 32, 1) qmv_kernel(const __grid_constant__ 
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c = warp * 32 + lane;  // this thread's K-chunk
-  const int r0 = int((long long)blockIdx.x * N / gridDim.x);
-  const int r1 = int((long long)(blockIdx.x + 1) * N / gridDim.x);
-  const int nrows = r1 - r0;
+  // whole tiles per CTA (only the last tile of the matrix can be partial), so no CTA computes the
+  // unused rows of a partial tile of its own
+  const int ntot = (N + HT - 1) / HT;
+  const int t0 = int((long long)blockIdx.x * ntot / gridDim.x);
+  const int t1 = int((long long)(blockIdx.x + 1) * ntot / gridDim.x);
+  const int r0 = t0 * HT;
+  const int r1 = min(N, t1 * HT);
+  const int nrows = max(0, r1 - r0);
   const int ntiles = (nrows + HT - 1) / HT;
 
   if (tid == 0) {
@@ -216,7 +221,6 @@ __global__ void __launch_bounds__(W * 32, 1) qmv_kernel(const __grid_constant__ 
   uint64_t xp[FMT == FMT_AFFINE ? 1 : M][16];
   float a0init[M][2];
   float xsum[M];
-#pragma unroll
   // fused prologue ops: this thread's 32 x values of every row (row m at x + m * ldx)
   uint4 xin[M][4];
 #pragma unroll
