@@ -119,23 +119,44 @@ gdn_fused_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
   }
 
   // phase 1: conv + silu of this head's q / k channels and of the CTA's v channels; gates.
-  // q / k: a thread per channel over the tokens (the loads of consecutive tokens overlap).
-  for (int cc = tid; cc < 2 * Dk; cc += blockDim.x) {
-    const int isk = cc / Dk, e = cc - isk * Dk, ch = isk * Hk * Dk + hk * Dk + e;
-    int t = 0;
-    for (; t + 4 <= S; t += 4) {
-      float o[4];
+  // A thread takes a channel over all tokens.  For the decode shape (KC == 4, S <= 4) the channel's
+  // window column and taps are fetched with independent loads first, then the S outputs are formed
+  // from registers (same fma sequence as conv()).
+  constexpr int kFastKC = 4, kFastS = 4;
+  const bool fast = KC == kFastKC && S <= kFastS;
+  auto conv_channel = [&](int ch, float* dst, int stride) {
+    if (fast) {
+      float wv[kFastKC - 1 + kFastS], cw[kFastKC];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) o[u] = conv(t + u, ch);
+      for (int r = 0; r < kFastKC - 1 + kFastS; ++r)
+        if (r < kFastKC - 1 + S)
+          wv[r] = bf2f(r < kFastKC - 1 ? conv_src[(long long)(off + r) * A.ld_conv + ch]
+                                      : qkv[(long long)(r - (kFastKC - 1)) * A.ld_qkv + ch]);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) qk[(t + u) * 2 * Dk + cc] = o[u];
+      for (int j = 0; j < kFastKC; ++j) cw[j] = bf2f(conv_w[(long long)ch * kFastKC + j]);
+#pragma unroll
+      for (int t = 0; t < kFastS; ++t)
+        if (t < S) {
+          float acc = 0.0f;
+#pragma unroll
+          for (int j = 0; j < kFastKC; ++j) acc = __fmaf_rn(cw[j], wv[t + j], acc);
+          dst[t * stride] = silu_bf(R(acc));
+        }
+    } else {
+      for (int t = 0; t < S; ++t) dst[t * stride] = conv(t, ch);
     }
-    for (; t < S; ++t) qk[t * 2 * Dk + cc] = conv(t, ch);
+  };
+  for (int cc = tid; cc < 2 * Dk; cc += blockDim.x) {
+    const int isk = cc / Dk, e = cc - isk * Dk;
+    conv_channel(isk * Hk * Dk + hk * Dk + e, qk + cc, 2 * Dk);
   }
-  // v channels from the last warps and the gates from warp 5, so no warp carries all three parts
-  for (int idx = int(blockDim.x) - 1 - tid; idx < S * kFusedDVB && idx >= 0; idx += blockDim.x) {
-    const int t = idx / kFusedDVB, d = idx - t * kFusedDVB;
-    vs[idx] = (dv0 + d < Dv) ? conv(t, 2 * Hk * Dk + hv * Dv + dv0 + d) : 0.0f;
+  // v channels from the last warp and the gates from warp 5, so no warp carries all three parts
+  for (int d = int(blockDim.x) - 1 - tid; d >= 0 && d < kFusedDVB; d += blockDim.x) {
+    if (dv0 + d < Dv) {
+      conv_channel(2 * Hk * Dk + hv * Dv + dv0 + d, vs + d, kFusedDVB);
+    } else {
+      for (int t = 0; t < S; ++t) vs[t * kFusedDVB + d] = 0.0f;
+    }
   }
   const uint16_t* av = static_cast<const uint16_t*>(A.a);
   const uint16_t* bv = static_cast<const uint16_t*>(A.b);
