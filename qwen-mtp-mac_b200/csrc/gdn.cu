@@ -73,6 +73,7 @@ gdn_fused_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
   pdl_trigger();
   pdl_wait();
   constexpr int Dk = NP * 32;
+  static_assert((Dk & (Dk - 1)) == 0, "the 1/Dk multiplications need a power of two");
   extern __shared__ __align__(16) float sm[];
   const int S = A.S, KC = A.KC, Hk = A.Hk, Hv = A.Hv, Dv = A.Dv;
   float* qk = sm;                          // [S][2][Dk]
@@ -201,10 +202,11 @@ gdn_fused_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
 #pragma unroll
     for (int i = 0; i < NP; ++i) { xv[i] = xr[i]; ss = __fmaf_rn(xv[i], xv[i], ss); }
     ss = warp_sum(ss);
-    const float r = rsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(Dk)), 1e-6f));
+    // Dk is a power of two: x / Dk and x * (1 / Dk) are the same correctly rounded value
+    const float r = rsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / float(Dk)), 1e-6f));
 #pragma unroll
     for (int i = 0; i < NP; ++i)
-      xr[i] = (p & 1) ? R(__fmul_rn(R(__fmul_rn(xv[i], r)), kscale)) : __fdiv_rn(R(__fmul_rn(xv[i], r)), float(Dk));
+      xr[i] = (p & 1) ? R(__fmul_rn(R(__fmul_rn(xv[i], r)), kscale)) : __fmul_rn(R(__fmul_rn(xv[i], r)), 1.0f / float(Dk));
   }
   __syncthreads();
 
@@ -257,6 +259,7 @@ gdn_norm_gate_kernel(const float* __restrict__ y, const uint16_t* __restrict__ z
                      float eps) {
   pdl_trigger();
   constexpr int Dv = NP * 32;
+  static_assert((Dv & (Dv - 1)) == 0, "the 1/Dv multiplications need a power of two");
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;  // t*H + h
   if (row >= S * H) return;
@@ -273,7 +276,7 @@ gdn_norm_gate_kernel(const float* __restrict__ y, const uint16_t* __restrict__ z
 #pragma unroll
   for (int i = 0; i < NP; ++i) { yv[i] = yr[i]; ss = __fmaf_rn(yv[i], yv[i], ss); }
   ss = warp_sum(ss);
-  const float r = rsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(Dv)), eps));
+  const float r = rsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / float(Dv)), eps));  // Dv: a power of two
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
     const int e = NP * lane + i;
