@@ -564,7 +564,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ----------------------------------------------------------------- weight + scale producer
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
-      int it = 0, lu = 0;
+      int it = 0, lu = 0, ws = 0;
+      uint32_t wph = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lu) {
         const Tile tl = a.tiles[u / RT];
@@ -587,9 +588,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_expect_tx(&bars->sfull[sb], uint32_t(kRows * KS));
           bulk_g2s(sdst, a.sa + (size_t)row * KS, uint32_t(kRows * KS), &bars->sfull[sb], pol_w);
         }
-        for (int c = 0; c < nchunk; ++c, ++it) {
-          const int s = it % NW;
-          if (*abort_flag || !mbar_wait_backoff(&bars->wempty[s], ((it / NW) & 1) ^ 1, err, 128)) { ok = false; break; }
+        for (int c = 0; c < nchunk; ++c, ++it, ws = ws + 1 == NW ? 0 : ws + 1, wph ^= ws == 0 ? 1u : 0u) {
+          const int s = ws;  // it % NW, phase (it / NW) & 1, kept incrementally
+          if (*abort_flag || !mbar_wait_backoff(&bars->wempty[s], wph ^ 1u, err, 128)) { ok = false; break; }
           uint8_t* st = wring + s * C::WSTAGE;
           mbar_expect_tx(&bars->wfull[s], uint32_t(C::WSTAGE));
           tma_load_2d(st, &tw0, c * (kChunk / 2), row, &bars->wfull[s], pol_w);
@@ -707,7 +708,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;
     const int sw = (r >> 1) & 3;
     const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
-    int it = 0, lu = 0;
+    int it = 0, lu = 0, ws = 0;
+    uint32_t wph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++lu) {
       const int sb = lu & 1, d = lu & 1;
@@ -737,9 +739,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->rsfull[d]);
       }
-      for (int c = 0; c < nchunk; ++c, ++it) {
-        const int s = it % NW;
-        if (*abort_flag || !mbar_wait_backoff(&bars->wfull[s], (it / NW) & 1, err, 64)) { ok = false; break; }
+      for (int c = 0; c < nchunk; ++c, ++it, ws = ws + 1 == NW ? 0 : ws + 1, wph ^= ws == 0 ? 1u : 0u) {
+        const int s = ws;  // it % NW, phase (it / NW) & 1, kept incrementally
+        if (*abort_flag || !mbar_wait_backoff(&bars->wfull[s], wph, err, 64)) { ok = false; break; }
         const uint8_t* wt = wring + s * C::WSTAGE + mat * kWBytes + r * 64;
         if (GU) {
           const uint4 w0 = *reinterpret_cast<const uint4*>(wt + 16 * (jj ^ sw));
