@@ -7,11 +7,12 @@ its own T tokens (weak scaling).  One layer:
 
   1. dispatch plan: each (token, slot) entry of a routed expert goes to the owner rank; entries are
      ordered by (destination rank, token, slot), which fixes the order of everything that follows;
-  2. all-to-all of the per-peer counts, then of the token rows (bf16) and their local expert ids;
-  3. the owner computes one fp32 partial per received row (qmtp_moe_experts);
-  4. all-to-all of the partials back to the token's rank (same split sizes, reversed);
-  5. shared experts run locally on the rank's own tokens;
-  6. y[t] = sum_j scores[t, j] * partial(t, j) in slot order (qmtp_moe_combine) -- the same sum, in
+  2. all-to-all of the per-peer counts (the layer's only host synchronisation: NCCL needs the split
+     sizes), then of the token rows (bf16) and their local expert ids;
+  3. one expert pass (qmtp_moe_experts) over the received rows followed by the rank's own
+     shared-expert rows: one fp32 partial per row;
+  4. all-to-all of the received rows' partials back to the token's rank (split sizes reversed);
+  5. y[t] = sum_j scores[t, j] * partial(t, j) in slot order (qmtp_moe_combine) -- the same sum, in
      the same order, as the single-GPU kernel's combine.
 
 The expert computation and the combine are pluggable (`compute`, `combine_fn`) so the identical
@@ -21,21 +22,6 @@ from __future__ import annotations
 
 import torch
 import torch.distributed as dist
-
-
-def plan_dispatch(idx: torch.Tensor, n_routed: int, world: int):
-    """idx int [T, S] -> (order, dest, counts): routed entries (flat t*S + j) in (dest, t, j) order."""
-    T, S = idx.shape
-    flat = idx.reshape(-1).to(torch.int64)
-    per = n_routed // world
-    routed = flat < n_routed
-    ent = torch.nonzero(routed, as_tuple=False).reshape(-1)  # ascending = (t, j) order
-    dest = torch.div(flat[ent], per, rounding_mode="floor")
-    key = dest * (T * S) + ent
-    order = ent[torch.argsort(key)]
-    dest_sorted = torch.div(flat[order], per, rounding_mode="floor")
-    counts = torch.bincount(dest_sorted, minlength=world)
-    return order, dest_sorted, counts
 
 
 class ExpertParallelMoE:
@@ -59,36 +45,42 @@ class ExpertParallelMoE:
         T, S = idx.shape
         H = x.shape[-1]
         dev = x.device
-        order, dest, counts = plan_dispatch(idx, self.n_routed, self.world)
-        tok = torch.div(order, S, rounding_mode="floor")
-        send_x = x.index_select(0, tok).contiguous()
-        send_e = (idx.reshape(-1)[order].to(torch.int64) - dest * self.per).to(torch.int32).contiguous()
-        recv_counts = torch.empty_like(counts)
-        dist.all_to_all_single(recv_counts, counts, group=self.group)
-        sc = counts.tolist()
-        rc = recv_counts.tolist()
-        recv_x = torch.empty((sum(rc), H), dtype=x.dtype, device=dev)
-        recv_e = torch.empty((sum(rc),), dtype=torch.int32, device=dev)
+        G, n_ent = self.world, T * S
+        flat = idx.reshape(-1).to(torch.int64)
+        # destination of every (t, j) entry: the owner rank of a routed expert, G for a shared one.
+        # One stable order (dest, t, j) serves the dispatch (dest < G) and the local shared rows.
+        dest = torch.where(flat < self.n_routed, torch.div(flat, self.per, rounding_mode="floor"),
+                           torch.full_like(flat, G))
+        order_all = torch.argsort(dest * n_ent + torch.arange(n_ent, device=dev))
+        counts_all = torch.zeros(G + 1, dtype=torch.int64, device=dev).scatter_add_(0, dest, torch.ones_like(dest))
+        recv_counts = torch.empty(G, dtype=torch.int64, device=dev)
+        dist.all_to_all_single(recv_counts, counts_all[:G].contiguous(), group=self.group)
+        host = torch.cat([counts_all, recv_counts]).tolist()  # the layer's one host synchronisation
+        sc, n_sh, rc = host[:G], host[G], host[G + 1:]
+        n_send, n_recv = sum(sc), sum(rc)
+        order, sh = order_all[:n_send], order_all[n_send:]
+        tok_all = torch.div(order_all, S, rounding_mode="floor")
+        send_x = x.index_select(0, tok_all[:n_send]).contiguous()
+        send_e = (flat[order] - dest[order] * self.per).to(torch.int32).contiguous()
+        # the rows this rank computes: the routed rows it receives, then its own shared-expert rows
+        rows_x = torch.empty((n_recv + n_sh, H), dtype=x.dtype, device=dev)
+        rows_e = torch.empty((n_recv + n_sh,), dtype=torch.int32, device=dev)
         # 16-bit rows travel as int32 pairs (gloo has no 16-bit all-to-all; NCCL moves bytes either way)
         wide = x.element_size() == 2 and H % 2 == 0
-        dist.all_to_all_single(recv_x.view(torch.int32) if wide else recv_x,
-                               send_x.view(torch.int32) if wide else send_x,
+        rx = rows_x[:n_recv]
+        dist.all_to_all_single(rx.view(torch.int32) if wide else rx, send_x.view(torch.int32) if wide else send_x,
                                output_split_sizes=rc, input_split_sizes=sc, group=self.group)
-        dist.all_to_all_single(recv_e, send_e, output_split_sizes=rc, input_split_sizes=sc, group=self.group)
-        part = self.compute(recv_x, recv_e).contiguous()
-        back = torch.empty((len(order), H), dtype=part.dtype, device=dev)
-        dist.all_to_all_single(back, part, output_split_sizes=sc, input_split_sizes=rc, group=self.group)
-        # shared experts on this rank's own tokens
-        flat = idx.reshape(-1).to(torch.int64)
-        sh = torch.nonzero(flat >= self.n_routed, as_tuple=False).reshape(-1)
-        sh_x = x.index_select(0, torch.div(sh, S, rounding_mode="floor")).contiguous()
-        sh_e = (flat[sh] - self.n_routed + self.per).to(torch.int32).contiguous()
-        sh_part = self.compute(sh_x, sh_e).contiguous()
-        # row of every (t, j) entry in the table [back ; sh_part]
-        row_of = torch.full((T * S,), -1, dtype=torch.int64, device=dev)
-        row_of[order] = torch.arange(len(order), device=dev)
-        row_of[sh] = len(order) + torch.arange(len(sh), device=dev)
-        table = torch.cat([back, sh_part], 0)
+        dist.all_to_all_single(rows_e[:n_recv], send_e, output_split_sizes=rc, input_split_sizes=sc,
+                               group=self.group)
+        rows_x[n_recv:] = x.index_select(0, tok_all[n_send:])
+        rows_e[n_recv:] = (flat[sh] - self.n_routed + self.per).to(torch.int32)
+        part = self.compute(rows_x, rows_e).contiguous()
+        back = torch.empty((n_send, H), dtype=part.dtype, device=dev)
+        dist.all_to_all_single(back, part[:n_recv], output_split_sizes=sc, input_split_sizes=rc, group=self.group)
+        # row of every (t, j) entry in the table [back ; own shared rows]
+        row_of = torch.empty((n_ent,), dtype=torch.int64, device=dev)
+        row_of[order_all] = torch.arange(n_ent, device=dev)
+        table = torch.cat([back, part[n_recv:]], 0)
         return self.combine_fn(table, row_of.reshape(T, S), scores)
 
 
