@@ -292,6 +292,7 @@ int qmtp_moe(int fmt, const void* x, const void* wg, const void* sg, const void*
  * clamp(Wu[e] x_r, -L, L)) for each row r with expert e = expert[r] (int32 [n]), i.e. one (token, slot) entry per
  * row without the routing weight; rows keep their input order.  Same limits as qmtp_moe (S = 1); the workspace is
  * qmtp_moe_workspace(n, 1, E, H, I).
+ * expert[r] = -1 marks an empty row: it is skipped and partial[r] is left unwritten.
  * qmtp_moe_combine: y[t] (bf16) = sum_j scores[t, j] * partials[row_of[t, j]] (fp32 [*, H]) in slot order j;
  * row_of < 0 skips a slot.  H % 4 == 0, S <= 16. */
 int qmtp_moe_experts(int fmt, const void* x, const void* wg, const void* sg, const void* wu, const void* su,
@@ -299,6 +300,26 @@ int qmtp_moe_experts(int fmt, const void* x, const void* wg, const void* sg, con
                      float limit, void* workspace, size_t ws_bytes, void* stream);
 int qmtp_moe_combine(const void* partials, const void* row_of, const void* scores, int T, int S, int H, void* y,
                      void* stream);
+
+/* Fixed-capacity dispatch of one expert-parallel MoE layer (no counterpart in the reference, whose MoE
+ * runs on one device).  `world` ranks, rank r owning routed experts [r * per, (r + 1) * per), per =
+ * n_routed / world; ids >= n_routed are shared experts, computed by every rank for its own tokens.
+ * For this rank's T tokens, idx int32 [T, S] and x bf16 [T, H]:
+ *   send_x bf16 [world * cap, H], send_e int32 [world * cap]: the rows for rank d at d * cap + p (p in
+ *     (t, j) order) with the local expert id e - d * per; unused slots have id -1;
+ *   sh_x bf16 [T * S, H], sh_e int32 [T * S]: the shared-expert rows, local id per + e - n_routed
+ *     (the layout of a rank's expert table: its routed shard, then the shared experts); unused -1;
+ *   pos int32 [T * S]: the row of entry (t, j) in the table [partials sent back by the ranks
+ *     (world * cap rows) ; this rank's expert pass over its world * cap received rows, then its shared
+ *     rows], i.e. d * cap + p for a routed entry and 2 * world * cap + q for the q-th shared entry;
+ *   counts int32 [world + 1]: entries sent to each rank, then the shared entries.
+ * Every size is fixed, so the all-to-alls of send_x / send_e and of the partials use equal splits and
+ * the layer needs no host synchronisation.  cap must cover the routed entries this rank sends to any one
+ * rank (T * S always does); an entry beyond cap, or with an invalid id, is dropped (pos = -1) and the
+ * device error word records it.  H % 8 == 0; x, send_x, sh_x 16-byte aligned. */
+int qmtp_moe_dispatch(const void* idx, int T, int S, const void* x, int H, int n_routed, int n_shared, int world,
+                      int cap, void* send_x, void* send_e, void* sh_x, void* sh_e, void* pos, void* counts,
+                      void* stream);
 
 /* Control block of the device-side speculative loop (int32 [QMTP_CTRL_SIZE]). */
 #define QMTP_CTRL_SLOT 0      /* GatedDeltaNet state ring slot before the next verify */

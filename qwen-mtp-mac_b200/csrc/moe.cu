@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const int32_t* __restri
     int e = -1;
     if (i < seg1) {
       e = idx[i];
-      if (e < 0 || e >= E) {
+      if (e < -1 || e >= E) {  // -1: an empty row (padding of a fixed-capacity dispatch), skipped
         if (err) atomicOr(err, DEVERR_BADARG);
         e = -1;
       }
@@ -942,6 +942,78 @@ __global__ void moe_combine_kernel(const float* __restrict__ yp, const int32_t* 
   }
 }
 
+// --------------------------------------------------------------------------- expert-parallel dispatch
+// Plan (one CTA of 1024 threads): entry i = (t, j), expert e = idx[i].  A routed entry (e < n_routed) goes
+// to rank d = e / per at slot p (its rank among d's entries in (t, j) order, from block scans, so the
+// placement is deterministic); a shared entry takes the next local slot q in (t, j) order.
+//   send_e[d * cap + p] = e - d * per (unused slots -1); sh_e[q] = per + e - n_routed (unused -1);
+//   pos[i] = d * cap + p, or 2 * G * cap + q for a shared entry: the entry's row in the table
+//   [partials back from the peers (G * cap rows) ; this rank's expert pass (G * cap received rows, then
+//   the shared rows)];
+//   counts[d] = entries to rank d, counts[G] = shared entries.  An entry beyond `cap` or with an invalid
+//   expert id is dropped (pos = -1) and recorded in the device error word.
+__global__ void __launch_bounds__(1024) moe_dispatch_plan_kernel(const int32_t* __restrict__ idx, int n,
+                                                                 int n_routed, int n_exp, int per, int G, int cap,
+                                                                 int32_t* __restrict__ send_e, int32_t* __restrict__ sh_e,
+                                                                 int32_t* __restrict__ pos, int32_t* __restrict__ counts,
+                                                                 unsigned* err) {
+  __shared__ int s_warp[32];
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x;
+  for (int i = tid; i < G * cap; i += blockDim.x) send_e[i] = -1;
+  for (int i = tid; i < n; i += blockDim.x) {
+    sh_e[i] = -1;
+    pos[i] = -1;  // invalid expert ids keep -1 (recorded below)
+  }
+  auto cat = [&](int e) { return (e < 0 || e >= n_exp) ? -1 : (e < n_routed ? e / per : G); };
+  const int per_thr = (n + blockDim.x - 1) / blockDim.x, i0 = min(n, tid * per_thr), i1 = min(n, i0 + per_thr);
+  bool overflow = false;
+  for (int c = 0; c <= G; ++c) {  // category c: rank c (routed) or G (shared)
+    int mine = 0;
+    for (int i = i0; i < i1; ++i) {
+      const int e = idx[i];
+      if (c == 0 && cat(e) < 0) overflow = true;
+      mine += cat(e) == c;
+    }
+    int total;
+    int slot = block_excl_scan(mine, s_warp, total);  // ends with a barrier: send_e / sh_e fills are done
+    for (int i = i0; i < i1; ++i) {
+      const int e = idx[i];
+      if (cat(e) != c) continue;
+      if (c < G) {
+        if (slot < cap) {
+          send_e[c * cap + slot] = e - c * per;
+          pos[i] = c * cap + slot;
+        } else {
+          pos[i] = -1;
+          overflow = true;
+        }
+      } else {
+        sh_e[slot] = per + e - n_routed;
+        pos[i] = 2 * G * cap + slot;
+      }
+      ++slot;
+    }
+    if (tid == 0) counts[c] = total;
+  }
+  if (overflow && err) atomicOr(err, DEVERR_BADARG);
+}
+
+// Row copies of the plan: x[t] of entry i to send_x (routed) or sh_x (shared); one CTA per entry.
+__global__ void __launch_bounds__(256) moe_dispatch_rows_kernel(const uint16_t* __restrict__ x, int S, int H, int G,
+                                                                int cap, const int32_t* __restrict__ pos,
+                                                                uint16_t* __restrict__ send_x,
+                                                                uint16_t* __restrict__ sh_x) {
+  pdl_wait();
+  pdl_trigger();
+  const int i = blockIdx.x, p = pos[i];
+  if (p < 0) return;
+  const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(i / S) * H);
+  uint4* dst = reinterpret_cast<uint4*>(p < G * cap ? send_x + (size_t)p * H : sh_x + (size_t)(p - 2 * G * cap) * H);
+  for (int k = threadIdx.x; k < H / 8; k += blockDim.x) dst[k] = src[k];
+}
+
 // --------------------------------------------------------------------------- host side
 struct Workspace {
   size_t entry_pos, sorted_tok, rank_tmp, xsh, tiles, counters, ximg, himg, yp, total;
@@ -1137,6 +1209,26 @@ extern "C" int qmtp_moe_experts(int fmt, const void* x, const void* wg, const vo
   if (!partial) return QMTP_ERR_ARG;
   return moe_run(fmt, x, wg, sg, wu, su, wd, sd, expert, nullptr, nullptr, static_cast<float*>(partial), n, 1, E, H, I,
                  limit, workspace, ws_bytes, stream);
+}
+
+extern "C" int qmtp_moe_dispatch(const void* idx, int T, int S, const void* x, int H, int n_routed, int n_shared,
+                                 int world, int cap, void* send_x, void* send_e, void* sh_x, void* sh_e, void* pos,
+                                 void* counts, void* stream) {
+  if (!idx || !x || !send_x || !send_e || !sh_x || !sh_e || !pos || !counts) return QMTP_ERR_ARG;
+  if (T <= 0 || S <= 0 || H <= 0 || H % 8 || world <= 0 || n_routed <= 0 || n_routed % world || n_shared < 0 ||
+      cap <= 0 || (long long)T * S > (1 << 20) || (long long)world * cap > (1 << 24))
+    return QMTP_ERR_SHAPE;
+  if (!aligned16(x) || !aligned16(send_x) || !aligned16(sh_x)) return QMTP_ERR_ALIGN;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int n = T * S;
+  QMTP_CUDA_TRY(launch_kernel(moe_dispatch_plan_kernel, dim3(1), dim3(1024), 0, st, static_cast<const int32_t*>(idx), n,
+                              n_routed, n_routed + n_shared, n_routed / world, world, cap, static_cast<int32_t*>(send_e),
+                              static_cast<int32_t*>(sh_e), static_cast<int32_t*>(pos), static_cast<int32_t*>(counts),
+                              device_error_ptr()));
+  QMTP_CUDA_TRY(launch_kernel(moe_dispatch_rows_kernel, dim3(unsigned(n)), dim3(256), 0, st,
+                              static_cast<const uint16_t*>(x), S, H, world, cap, static_cast<const int32_t*>(pos),
+                              static_cast<uint16_t*>(send_x), static_cast<uint16_t*>(sh_x)));
+  return QMTP_OK;
 }
 
 extern "C" int qmtp_moe_combine(const void* partials, const void* row_of, const void* scores, int T, int S, int H,

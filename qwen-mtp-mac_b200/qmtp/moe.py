@@ -146,3 +146,18 @@ def combine(partials: torch.Tensor, row_of: torch.Tensor, scores: torch.Tensor, 
     _lib.check(_lib.lib().qmtp_moe_combine(partials.data_ptr(), r.data_ptr(), sc.data_ptr(), T, S, H, y.data_ptr(),
                                            _lib.stream()), "qmtp_moe_combine")
     return y
+
+
+def dispatch(idx: torch.Tensor, x: torch.Tensor, n_routed: int, n_shared: int, world: int, cap: int,
+             send_x: torch.Tensor, send_e: torch.Tensor, sh_x: torch.Tensor, sh_e: torch.Tensor,
+             pos: torch.Tensor, counts: torch.Tensor) -> None:
+    """Fixed-capacity expert-parallel dispatch into caller buffers (qmtp_moe_dispatch): send_x
+    [world * cap, H], send_e [world * cap], sh_x [T * S, H], sh_e [T * S], pos [T * S], counts
+    [world + 1]; see include/qmtp.h for the layout."""
+    _lib.require_cuda(x)
+    T, S = idx.shape
+    H = x.shape[-1]
+    i32 = idx.to(torch.int32).contiguous()
+    _lib.check(_lib.lib().qmtp_moe_dispatch(i32.data_ptr(), T, S, x.data_ptr(), H, n_routed, n_shared, world, cap,
+                                            send_x.data_ptr(), send_e.data_ptr(), sh_x.data_ptr(), sh_e.data_ptr(),
+                                            pos.data_ptr(), counts.data_ptr(), _lib.stream()), "qmtp_moe_dispatch")

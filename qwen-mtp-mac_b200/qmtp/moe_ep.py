@@ -15,8 +15,14 @@ its own T tokens (weak scaling).  One layer:
   5. y[t] = sum_j scores[t, j] * partial(t, j) in slot order (qmtp_moe_combine) -- the same sum, in
      the same order, as the single-GPU kernel's combine.
 
-The expert computation and the combine are pluggable (`compute`, `combine_fn`) so the identical
-dispatch logic runs with the CUDA kernels on GPUs and with the C oracle in the gloo tests.
+With a fixed capacity per peer (`capacity=`) the layer makes no host synchronisation: the dispatch
+kernel (qmtp_moe_dispatch) lays the rows out in equal slots of `capacity` rows per peer (empty slots
+carry expert id -1), the all-to-alls use equal splits, and the combine reads every partial through a
+position table computed on the device.  The whole layer can then be captured in one CUDA graph.
+
+The expert computation, the combine and the fixed-capacity planner are pluggable (`compute`,
+`combine_fn`, `dispatch`) so the identical dispatch logic runs with the CUDA kernels on GPUs and with
+the C oracle in the gloo tests.
 """
 from __future__ import annotations
 
@@ -27,11 +33,12 @@ import torch.distributed as dist
 class ExpertParallelMoE:
     """One MoE layer sharded expert-parallel over the default process group (or `group`).
 
-    compute(x_rows, local_expert_ids) -> fp32 partials [n, H]: routed experts owned by this rank use
-    local ids 0 .. E/G-1; shared expert s uses local id E/G + s.
+    compute(x_rows, local_expert_ids, out=None) -> fp32 partials [n, H] (written into `out` when given):
+    routed experts owned by this rank use local ids 0 .. E/G-1, shared expert s uses local id E/G + s,
+    id -1 marks an empty row (its partial is not needed).
     combine_fn(partials, row_of [T, S], scores [T, S]) -> y [T, H]."""
 
-    def __init__(self, n_routed: int, n_shared: int, compute, combine_fn, group=None):
+    def __init__(self, n_routed: int, n_shared: int, compute, combine_fn, group=None, capacity=None, dispatch=None):
         self.n_routed, self.n_shared = n_routed, n_shared
         self.group = group
         self.world = dist.get_world_size(group)
@@ -40,8 +47,52 @@ class ExpertParallelMoE:
             raise ValueError(f"{n_routed} routed experts do not split over {self.world} ranks")
         self.per = n_routed // self.world
         self.compute, self.combine_fn = compute, combine_fn
+        # capacity=None: exact split sizes, one host synchronisation per layer.  capacity = int or
+        # callable(T, S) -> int: fixed-capacity dispatch, no host synchronisation (the layer can be
+        # captured in a CUDA graph together with its NCCL calls); it must cover the routed entries a
+        # rank sends to any one rank (T * S always does).
+        self.capacity = capacity
+        self.dispatch = dispatch  # fixed-capacity planner; None = the CUDA kernel (qmtp.moe.dispatch)
+        self._bufs = {}
 
     def __call__(self, x: torch.Tensor, idx: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
+        if self.capacity is not None:
+            return self._call_fixed(x, idx, scores)
+        return self._call_exact(x, idx, scores)
+
+    def _call_fixed(self, x: torch.Tensor, idx: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
+        T, S = idx.shape
+        H = x.shape[-1]
+        G, n, dev = self.world, T * S, x.device
+        cap = int(self.capacity(T, S) if callable(self.capacity) else self.capacity)
+        key = (T, S, H, cap, x.dtype, dev)
+        b = self._bufs.get(key)
+        if b is None:
+            b = dict(send_x=torch.empty((G * cap, H), dtype=x.dtype, device=dev),
+                     send_e=torch.empty((G * cap,), dtype=torch.int32, device=dev),
+                     rows_x=torch.empty((G * cap + n, H), dtype=x.dtype, device=dev),
+                     rows_e=torch.empty((G * cap + n,), dtype=torch.int32, device=dev),
+                     pos=torch.empty((n,), dtype=torch.int32, device=dev),
+                     counts=torch.empty((G + 1,), dtype=torch.int32, device=dev),
+                     # [partials back from the ranks ; this rank's pass: received rows, shared rows]
+                     table=torch.empty((2 * G * cap + n, H), dtype=torch.float32, device=dev))
+            self._bufs = {key: b}
+        plan = self.dispatch
+        if plan is None:
+            from .moe import dispatch as plan
+        plan(idx, x, self.n_routed, self.n_shared, G, cap, b["send_x"], b["send_e"], b["rows_x"][G * cap:],
+             b["rows_e"][G * cap:], b["pos"], b["counts"])
+        wide = x.element_size() == 2 and H % 2 == 0
+        rx, sx = b["rows_x"][:G * cap], b["send_x"]
+        dist.all_to_all_single(rx.view(torch.int32) if wide else rx, sx.view(torch.int32) if wide else sx,
+                               group=self.group)
+        dist.all_to_all_single(b["rows_e"][:G * cap], b["send_e"], group=self.group)
+        tab = b["table"]
+        self.compute(b["rows_x"], b["rows_e"], out=tab[G * cap:])
+        dist.all_to_all_single(tab[:G * cap], tab[G * cap:2 * G * cap], group=self.group)
+        return self.combine_fn(tab, b["pos"].view(T, S), scores)
+
+    def _call_exact(self, x: torch.Tensor, idx: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
         T, S = idx.shape
         H = x.shape[-1]
         dev = x.device

@@ -41,7 +41,7 @@ def _tokens(rank):
     return x, idx, sc
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, fixed):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     for p in (root, os.path.join(root, "qwen-mtp-mac_b200")):
@@ -57,13 +57,19 @@ def _worker(rank, world, port, out):
     sel = list(range(rank * per, (rank + 1) * per)) + list(range(E_R, E_R + N_SH))
     loc = [a[sel] for a in (wg, sg, wu, su, wd, sd)]
 
-    def compute(x_rows, ids):
+    def compute(x_rows, ids, out=None):
         n = x_rows.shape[0]
-        if n == 0:
-            return torch.zeros((0, H), dtype=torch.float32)
-        xb = x_rows.numpy().view(np.uint16)
-        _, yf = ops.moe(xb, *loc, ids.numpy().reshape(n, 1), np.ones((n, 1), np.float32), "mxfp4", None)
-        return torch.from_numpy(yf)
+        y = torch.zeros((n, H), dtype=torch.float32)
+        keep = (ids >= 0).nonzero().reshape(-1)  # empty rows (id -1) of a fixed-capacity dispatch
+        if len(keep):
+            xb = x_rows[keep].numpy().view(np.uint16)
+            _, yf = ops.moe(xb, *loc, ids[keep].numpy().reshape(-1, 1), np.ones((len(keep), 1), np.float32),
+                            "mxfp4", None)
+            y[keep] = torch.from_numpy(yf)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
 
     def combine(table, row_of, scores):
         tab = table.numpy()
@@ -76,20 +82,24 @@ def _worker(rank, world, port, out):
         return torch.from_numpy(ops.f32_to_bf16(y).view(np.int16))
 
     x, idx, sc = _tokens(rank)
-    layer = ExpertParallelMoE(E_R, N_SH, compute, combine)
+    from tests._moe_dispatch_ref import ref_dispatch
+    layer = ExpertParallelMoE(E_R, N_SH, compute, combine, capacity=(lambda T_, S_: T_ * S_) if fixed else None,
+                              dispatch=ref_dispatch)
     y = layer(torch.from_numpy(x.view(np.int16)), torch.from_numpy(idx), torch.from_numpy(sc))
     out[rank] = y.numpy().view(np.uint16).copy()
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_expert_parallel_matches_single_process():
+@pytest.mark.parametrize("fixed", [False, True], ids=["exact-splits", "fixed-capacity"])
+def test_expert_parallel_matches_single_process(fixed):
     from oracle import ops
 
     world = 2
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
-    mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, start_method="spawn", join=True)
+    mp.start_processes(_worker, args=(world, _free_port(), out, fixed), nprocs=world, start_method="spawn",
+                       join=True)
     layer = _layer()
     for rank in range(world):
         x, idx, sc = _tokens(rank)

@@ -23,7 +23,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, mode, out):
+def _worker(rank, world, port, mode, fixed, out):
     import sys
     import torch.distributed as dist
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -50,8 +50,10 @@ def _worker(rank, world, port, mode, out):
         gt.manual_seed(100 + rank)
         x = torch.randn((T, H), generator=gt, device=dev).to(torch.bfloat16)
         idx, sc = moe.route(torch.randn((T, E_R), generator=gt, device=dev), 6, N_SH)
-        layer = ExpertParallelMoE(E_R, N_SH, lambda xr, e: moe.experts(xr, *loc, e, limit=None, mode=mode),
-                                  lambda tab, ro, s: moe.combine(tab, ro, s))
+        layer = ExpertParallelMoE(E_R, N_SH, lambda xr, e, out=None: moe.experts(xr, *loc, e, limit=None, mode=mode,
+                                                                                 out=out),
+                                  lambda tab, ro, s: moe.combine(tab, ro, s),
+                                  capacity=(lambda T_, S_: T_ * S_) if fixed else None)
         y_ep = layer(x, idx, sc)
         y_one = moe.moe_decode(x, *wts, idx, sc, limit=None, mode=mode)
         torch.cuda.synchronize()
@@ -62,8 +64,9 @@ def _worker(rank, world, port, mode, out):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("fixed", [False, True], ids=["exact-splits", "fixed-capacity"])
 @pytest.mark.parametrize("mode", ["mxfp4", "nvfp4"])
-def test_expert_parallel_bit_identical_on_two_gpus(mode):
+def test_expert_parallel_bit_identical_on_two_gpus(mode, fixed):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -71,7 +74,8 @@ def test_expert_parallel_bit_identical_on_two_gpus(mode):
     world = 2
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
-    mp.start_processes(_worker, args=(world, _free_port(), mode, out), nprocs=world, start_method="spawn", join=True)
+    mp.start_processes(_worker, args=(world, _free_port(), mode, fixed, out), nprocs=world, start_method="spawn",
+                       join=True)
     for r in range(world):
         same, diff = out[r]
         assert same, (r, diff)
