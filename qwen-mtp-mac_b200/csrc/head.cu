@@ -153,14 +153,24 @@ topk_merge_kernel(const uint64_t* __restrict__ cand, int G, int k, int NP, const
     const uint32_t v = cand_idx(s[j]);
     const uint16_t* wr = W + (long long)v * K;
     float acc = 0.0f;
-    for (int c = lane; c < K / 8; c += 32) {
-      const uint4 w4 = ldg_nc_v4(wr + 8 * c);
-      const uint4 h4 = *reinterpret_cast<const uint4*>(hr + 8 * c);
-      const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w}, hh[4] = {h4.x, h4.y, h4.z, h4.w};
+    // the weight row's chunks of this lane (c = lane, lane + 32, ...) are fetched 8 at a time before
+    // the fma chain consumes them in ascending order (h is small and stays in L1)
+    constexpr int kB = 8;
+    for (int c0 = lane; c0 < K / 8; c0 += 32 * kB) {
+      uint4 w4[kB];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        acc = __fmaf_rn(bflo(ww[e]), bflo(hh[e]), acc);
-        acc = __fmaf_rn(bfhi(ww[e]), bfhi(hh[e]), acc);
+      for (int u = 0; u < kB; ++u)
+        if (c0 + 32 * u < K / 8) w4[u] = ldg_nc_v4(wr + 8 * (c0 + 32 * u));
+#pragma unroll
+      for (int u = 0; u < kB; ++u) {
+        if (c0 + 32 * u >= K / 8) break;
+        const uint4 h4 = *reinterpret_cast<const uint4*>(hr + 8 * (c0 + 32 * u));
+        const uint32_t ww[4] = {w4[u].x, w4[u].y, w4[u].z, w4[u].w}, hh[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc = __fmaf_rn(bflo(ww[e]), bflo(hh[e]), acc);
+          acc = __fmaf_rn(bfhi(ww[e]), bfhi(hh[e]), acc);
+        }
       }
     }
     acc = warp_sum(acc);
