@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -430,10 +431,15 @@ def run_moe_ep(args):
     gt.manual_seed(1000 + rank)
     x = torch.randn((T, H), generator=gt, device=dev).to(torch.bfloat16)
     idx, sc = moe.route(torch.randn((T, E_R), generator=gt, device=dev), TOPK, NSH)
-    # fixed capacity: a rank sends at most T * TOPK routed rows to any one peer, so nothing is dropped
+    # fixed capacity: a rank sends at most T * TOPK routed rows to any one peer; a slot of `factor` times
+    # the average load T * TOPK / G keeps the all-to-alls near the real traffic, and any row it would
+    # drop is reported through the device error word (printed below)
+    cap = T * TOPK
+    if args.ep_capacity_factor > 0:
+        cap = min(cap, int(math.ceil(args.ep_capacity_factor * T * TOPK / world)))
     layer = ExpertParallelMoE(E_R, NSH,
                               lambda xr, e, out=None: moe.experts(xr, *loc, e, limit=None, mode=mode, out=out),
-                              lambda tab, ro, s_: moe.combine(tab, ro, s_), capacity=T * TOPK)
+                              lambda tab, ro, s_: moe.combine(tab, ro, s_), capacity=cap)
     for _ in range(max(args.warmup, 3)):
         layer(x, idx, sc)
     torch.cuda.synchronize()
@@ -459,6 +465,8 @@ def run_moe_ep(args):
     del graph  # a graph holding NCCL calls goes before the process group
     ms = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=dev)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    derr = torch.tensor([_lib.device_error()], dtype=torch.int64, device=dev)  # includes dispatch overflow
+    dist.all_reduce(derr, op=dist.ReduceOp.MAX)
     dist.barrier()
     Gs = 32 if mode == "mxfp4" else 16
     wbytes = (E_R // world + NSH) * 3 * H * I * (0.5 + 1 / Gs)
@@ -468,8 +476,9 @@ def run_moe_ep(args):
                           "n_gpus": world, "us_per_layer": round(us, 2), "tokens_per_s": round(world * T / (us * 1e-6), 1),
                           "local_weight_bytes": int(wbytes), "local_weight_GBps": round(wbytes / (us * 1e-6) / 1e9, 1),
                           "steps": args.steps, "scaling": "weak",
-                          "dispatch": f"fixed capacity {T * TOPK} rows per peer, no host sync, one CUDA graph per layer",
-                          "device_error": _lib.device_error()}), flush=True)
+                          "dispatch": f"fixed capacity {cap} rows per peer (exact bound {T * TOPK}), no host sync, "
+                                      "one CUDA graph per layer",
+                          "device_error": int(derr.item())}), flush=True)
     dist.destroy_process_group()
 
 
@@ -523,6 +532,9 @@ def main():
     ap.add_argument("--kernel", default=None, choices=["qmv", "gdn", "head", "moe"],
                     help="time one kernel at a config shape instead of the decode loop")
     ap.add_argument("--shape", default="12288,4096,3", help="qmv: N,K,M")
+    ap.add_argument("--ep-capacity-factor", type=float, default=2.0,
+                    help="expert-parallel MoE: rows per peer slot = factor x the average load T*TOPK/G, at most "
+                         "the exact bound T*TOPK (0 = exact bound); an overflow shows as device_error != 0")
     args = ap.parse_args()
     if args.kernel:
         args.steps = 50 if args.steps is None else args.steps
