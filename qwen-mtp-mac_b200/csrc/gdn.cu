@@ -211,19 +211,76 @@ gdn_fused_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
   __syncthreads();
 
   // phase 3: the delta rule for this warp's dv rows, states in registers
+  auto snapshot_dst = [&](int t) -> float* {
+    if (A.ring) return (A.snap || t == S - 1) ? A.ring + size_t((cur + t + 1) % A.ring_slots) * per : nullptr;
+    if (t == S - 1) return A.state_out;
+    return (A.snap && A.state_mid) ? A.state_mid + size_t(t) * per : nullptr;
+  };
+  if (S <= kFastS) {
+    // decode shape: the tokens unrolled; only the k.state sums chain from token to token, the
+    // q.state sums of all tokens are reduced together at the end (same operations, shorter chain)
+    float op[kFastS][kFusedRPW];
+#pragma unroll
+    for (int t = 0; t < kFastS; ++t) {
+      if (t >= S) break;
+      const float4 q4 = *reinterpret_cast<const float4*>(qk + (t * 2 + 0) * Dk + NP * lane);
+      const float4 k4 = *reinterpret_cast<const float4*>(qk + (t * 2 + 1) * Dk + NP * lane);
+      const float qf[4] = {q4.x, q4.y, q4.z, q4.w}, kf[4] = {k4.x, k4.y, k4.z, k4.w};
+      const float gt = gs[t], bt = bs[t];
+      float* dst = snapshot_dst(t);
+      float kv[kFusedRPW];
+#pragma unroll
+      for (int rr = 0; rr < kFusedRPW; ++rr) {
+        kv[rr] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          st[rr][i] = __fmul_rn(st[rr][i], gt);
+          kv[rr] = __fmaf_rn(st[rr][i], kf[i], kv[rr]);
+        }
+      }
+#pragma unroll
+      for (int d = 16; d >= 1; d >>= 1)
+#pragma unroll
+        for (int rr = 0; rr < kFusedRPW; ++rr) kv[rr] = __fadd_rn(kv[rr], __shfl_xor_sync(0xFFFFFFFFu, kv[rr], d));
+#pragma unroll
+      for (int rr = 0; rr < kFusedRPW; ++rr) {
+        const int dv = dv0 + warp * kFusedRPW + rr;
+        const float delta = dv < Dv ? __fmul_rn(__fsub_rn(vs[t * kFusedDVB + dv - dv0], kv[rr]), bt) : 0.0f;
+        op[t][rr] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          st[rr][i] = __fmaf_rn(kf[i], delta, st[rr][i]);
+          op[t][rr] = __fmaf_rn(st[rr][i], qf[i], op[t][rr]);
+        }
+        if (dst && dv < Dv)
+          *reinterpret_cast<float4*>(dst + (size_t(hv) * Dv + dv) * Dk + NP * lane) =
+              make_float4(st[rr][0], st[rr][1], st[rr][2], st[rr][3]);
+      }
+    }
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1)
+#pragma unroll
+      for (int t = 0; t < kFastS; ++t)
+#pragma unroll
+        for (int rr = 0; rr < kFusedRPW; ++rr)
+          if (t < S) op[t][rr] = __fadd_rn(op[t][rr], __shfl_xor_sync(0xFFFFFFFFu, op[t][rr], d));
+    if (lane == 0) {
+#pragma unroll
+      for (int t = 0; t < kFastS; ++t)
+#pragma unroll
+        for (int rr = 0; rr < kFusedRPW; ++rr) {
+          const int dv = dv0 + warp * kFusedRPW + rr;
+          if (t < S && dv < Dv) A.y[(size_t(t) * Hv + hv) * Dv + dv] = R(op[t][rr]);
+        }
+    }
+    return;
+  }
   for (int t = 0; t < S; ++t) {
     const float4 q4 = *reinterpret_cast<const float4*>(qk + (t * 2 + 0) * Dk + NP * lane);
     const float4 k4 = *reinterpret_cast<const float4*>(qk + (t * 2 + 1) * Dk + NP * lane);
     const float qf[4] = {q4.x, q4.y, q4.z, q4.w}, kf[4] = {k4.x, k4.y, k4.z, k4.w};
     const float gt = gs[t], bt = bs[t];
-    float* dst = nullptr;
-    if (A.ring) {
-      if (A.snap || t == S - 1) dst = A.ring + size_t((cur + t + 1) % A.ring_slots) * per;
-    } else if (t == S - 1) {
-      dst = A.state_out;
-    } else if (A.snap && A.state_mid) {
-      dst = A.state_mid + size_t(t) * per;
-    }
+    float* dst = snapshot_dst(t);
 #pragma unroll
     for (int rr = 0; rr < kFusedRPW; ++rr) {
       const int dv = dv0 + warp * kFusedRPW + rr;
