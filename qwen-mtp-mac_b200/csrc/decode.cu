@@ -399,7 +399,9 @@ extern "C" int qmtp_embed(const int* tokens, int T, const void* wq, const void* 
   if (!tokens || !wq || !scales || !biases || !out) return QMTP_ERR_ARG;
   if (T < 1 || D % 64 != 0 || ld_out < D || ld_out % 8 != 0) return QMTP_ERR_SHAPE;
   if (!aligned16(out)) return QMTP_ERR_ALIGN;
-  launch_kernel(embed_kernel, dim3(T), dim3(128), 0, static_cast<cudaStream_t>(stream), 
+  // one packed word per thread (D / 8 threads up to 1024), so a row costs one round trip to memory
+  const int threads = std::min(1024, std::max(32, ((D / 8 + 31) / 32) * 32));
+  launch_kernel(embed_kernel, dim3(T), dim3(threads), 0, static_cast<cudaStream_t>(stream), 
       tokens, static_cast<const uint32_t*>(wq), static_cast<const uint16_t*>(scales),
       static_cast<const uint16_t*>(biases), D, static_cast<uint16_t*>(out), ld_out, V, device_error_ptr());
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;

@@ -202,6 +202,7 @@ argmax_partial_kernel(const uint16_t* __restrict__ vals, long long ld, int V, ui
   const int i0 = int((long long)blk * V / G), i1 = int((long long)(blk + 1) * V / G);
   const uint16_t* row = vals + (long long)m * ld;
   uint64_t best = 0;
+#pragma unroll 4
   for (int i = i0 + tid; i < i1; i += blockDim.x) best = max(best, cand_word(key16(row[i]), uint32_t(i)));
 #pragma unroll
   for (int d = 16; d >= 1; d >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, d));
