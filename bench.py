@@ -307,16 +307,30 @@ def run_kernel(args):
     peak, peak_kind = _peaks()
     K, Wu = args.steps, args.warmup
     if args.kernel == "qmv":
-        N, Kd, M = (int(v) for v in args.shape.split(","))
+        parts = args.shape.split(",")
+        N, Kd, M = (int(v) for v in parts[:3])
+        fmt = parts[3] if len(parts) > 3 else "affine"
         copies = max(1, -(-300_000_000 // (N * Kd // 2)))  # > 2x L2 of weights in rotation
-        Ls = [qmv_kernel.quantize((torch.randn(N, Kd, generator=g, device=dev) * 0.02).to(torch.bfloat16))
-              for _ in range(copies)]
         x = torch.randn(M, Kd, generator=g, device=dev).to(torch.bfloat16)
         y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-        nbytes = N * Kd // 2 + N * (Kd // 64) * 4 + M * Kd * 2 + M * N * 2
-        run = lambda i: qmv_kernel.qmv_affine(x, *Ls[i % copies], out=y)
+        if fmt == "nvfp4":
+            from qmtp import moe
+
+            Ls = []
+            for _ in range(copies):
+                wq_, s_ = moe.quantize((torch.randn(1, N, Kd, generator=g, device=dev) * 0.02).to(torch.bfloat16),
+                                       "nvfp4")
+                Ls.append((wq_[0], s_[0]))
+            nbytes = N * Kd // 2 + N * (Kd // 16) + M * Kd * 2 + M * N * 2
+            run = lambda i: qmv_kernel.qmv_nvfp4(x, *Ls[i % copies])
+            label = f"qmv NVFP4 g16 N={N} K={Kd} M={M}"
+        else:
+            Ls = [qmv_kernel.quantize((torch.randn(N, Kd, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+                  for _ in range(copies)]
+            nbytes = N * Kd // 2 + N * (Kd // 64) * 4 + M * Kd * 2 + M * N * 2
+            run = lambda i: qmv_kernel.qmv_affine(x, *Ls[i % copies], out=y)
+            label = f"qmv affine g64 N={N} K={Kd} M={M}"
         unit_bytes = nbytes
-        label = f"qmv affine g64 N={N} K={Kd} M={M}"
     elif args.kernel == "gdn":
         S, Hk, Hv, D, KC = 3, 16, 32, 128, 4
         Cd = 2 * Hk * D + Hv * D
@@ -531,7 +545,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens (ours)")
     ap.add_argument("--kernel", default=None, choices=["qmv", "gdn", "head", "moe"],
                     help="time one kernel at a config shape instead of the decode loop")
-    ap.add_argument("--shape", default="12288,4096,3", help="qmv: N,K,M")
+    ap.add_argument("--shape", default="12288,4096,3", help="qmv: N,K,M[,affine|nvfp4]")
     ap.add_argument("--ep-capacity-factor", type=float, default=2.0,
                     help="expert-parallel MoE: rows per peer slot = factor x the average load T*TOPK/G, at most "
                          "the exact bound T*TOPK (0 = exact bound); an overflow shows as device_error != 0")
