@@ -115,18 +115,6 @@ __device__ __forceinline__ void fma_bf16x2(float& acc, uint32_t a, uint32_t x) {
       : "r"(a), "r"(x));
 }
 
-// e2m1 pair -> two floats scaled by 2^-14 (half-precision bit trick of qmv_kernel.py:16-25):
-// nibble j and j+4 of w sit in the low / high 16 bits after `w >> 4j`.
-__device__ __forceinline__ void unpack_e2m1(uint32_t w, float (&f)[8]) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t t = w >> (4 * j);
-    const uint32_t h2 = ((t & 0x00070007u) << 9) | ((t & 0x00080008u) << 12);
-    f[j] = __half2float(__ushort_as_half(uint16_t(h2 & 0xFFFFu)));
-    f[j + 4] = __half2float(__ushort_as_half(uint16_t(h2 >> 16)));
-  }
-}
-
 // (lo, hi) float pairs in one 64-bit register pair, for fma.rn.f32x2 (two IEEE fp32 fmas).
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
   uint64_t r;
@@ -140,6 +128,23 @@ __device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
+}
+
+// e2m1 nibble pairs -> exact fp32 values, unscaled: the hardware e2m1x2 -> f16x2 conversion of
+// each byte (nibble 2b in the low half, 2b+1 in the high half; signed, zero exact), then f16 -> f32.
+// p[b] = (nibble 2b, nibble 2b+1) as a (lo, hi) pair for fma.rn.f32x2.
+__device__ __forceinline__ void e2m1_pairs(uint32_t w, uint64_t (&p)[4]) {
+  uint32_t h[4];
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
+#pragma unroll
+  for (int b = 0; b < 4; ++b)
+    p[b] = pack2(__half2float(__ushort_as_half(uint16_t(h[b] & 0xFFFFu))),
+                 __half2float(__ushort_as_half(uint16_t(h[b] >> 16))));
 }
 
 __device__ __forceinline__ float e4m3_x16k(uint32_t s) {
@@ -216,7 +221,7 @@ __global__ void __launch_bounds__(W * 32, 1) qmv_kernel(const __grid_constant__ 
 
   // x prologue (this thread's 32 elements of every row m).  Affine: bf16 pairs
   // xb[m][4q + j] = (x[8q + j], x[8q + j + 4]) matching the nibble pairs of word q, the lane sums
-  // Sx_h, the initial accumulators -128*Sx_h and the chunk sum.  NVFP4: (even, odd) fp32 pairs.
+  // Sx_h, the initial accumulators -128*Sx_h and the chunk sum.  NVFP4: (even, odd) fp32 pairs times 2^-14.
   uint32_t xb[M][16];
   uint64_t xp[FMT == FMT_AFFINE ? 1 : M][16];
   float a0init[M][2];
@@ -315,10 +320,15 @@ __global__ void __launch_bounds__(W * 32, 1) qmv_kernel(const __grid_constant__ 
       xsum[m] = __fadd_rn(sx[0], sx[1]);
     } else {
 #pragma unroll
+      // The reference scales the weights (half-bit e2m1 decode = value * 2^-14, qmv_kernel.py:16-25);
+      // here x carries the 2^-14 instead.  x * 2^-14 is exact for every bf16 x (its lowest set bit
+      // is >= 2^-133, the scaled one >= 2^-147 > 2^-149), so e2m1 * (x * 2^-14) is the same exact
+      // product as (e2m1 * 2^-14) * x and every fma rounds identically.
       for (int q = 0; q < 4; ++q) {
         const uint32_t uu[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
 #pragma unroll
-        for (int h = 0; h < 4; ++h) xp[m][4 * q + h] = pack2(bflo(uu[h]), bfhi(uu[h]));
+        for (int h = 0; h < 4; ++h)
+          xp[m][4 * q + h] = pack2(__fmul_rn(bflo(uu[h]), 0x1p-14f), __fmul_rn(bfhi(uu[h]), 0x1p-14f));
       }
       a0init[m][0] = a0init[m][1] = 0.0f;
       xsum[m] = 0.0f;
@@ -380,16 +390,12 @@ __global__ void __launch_bounds__(W * 32, 1) qmv_kernel(const __grid_constant__ 
             for (int m = 0; m < M; ++m) acc[m] = pack2(0.0f, 0.0f);
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
-              float f[8];
-              unpack_e2m1(wd[2 * h + q], f);  // f[n] = nibble n of the word, times 2^-14
-              const uint64_t f01 = pack2(f[0], f[1]), f23 = pack2(f[2], f[3]);
-              const uint64_t f45 = pack2(f[4], f[5]), f67 = pack2(f[6], f[7]);
+              uint64_t f[4];
+              e2m1_pairs(wd[2 * h + q], f);  // f[b] = nibbles (2b, 2b+1) of the word
 #pragma unroll
               for (int m = 0; m < M; ++m) {
-                acc[m] = ffma2(f01, xp[m][8 * h + 4 * q + 0], acc[m]);
-                acc[m] = ffma2(f23, xp[m][8 * h + 4 * q + 1], acc[m]);
-                acc[m] = ffma2(f45, xp[m][8 * h + 4 * q + 2], acc[m]);
-                acc[m] = ffma2(f67, xp[m][8 * h + 4 * q + 3], acc[m]);
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[m] = ffma2(f[b], xp[m][8 * h + 4 * q + b], acc[m]);
               }
             }
 #pragma unroll

@@ -68,6 +68,27 @@ def test_qmv_nvfp4_bit_exact(dev):
         assert np.array_equal(to_np(got), ops.qmv_nvfp4(x, nq, ns)), (M, K, N)
 
 
+def test_qmv_nvfp4_extreme_x_bit_exact(dev):
+    """Activations over bf16's whole finite range (subnormals, tiny and huge normals, zeros): the
+    kernel moves the reference's 2^-14 weight scale onto x, which must stay exact everywhere."""
+    from qmtp import qmv_kernel
+
+    r = np.random.default_rng(21)
+    for M, K, N in ((2, 1024, 300), (1, 4096, 200)):
+        sign = r.integers(0, 2, (M, K)).astype(np.uint16) << 15
+        man = r.integers(0, 128, (M, K)).astype(np.uint16)
+        kind = r.integers(0, 4, (M, K))
+        exp = np.where(kind == 0, 0,                                     # subnormal / zero
+              np.where(kind == 1, r.integers(1, 12, (M, K)),              # just above 2^-126
+              np.where(kind == 2, r.integers(110, 140, (M, K)),           # ordinary magnitudes
+                       r.integers(200, 227, (M, K))))).astype(np.uint16)  # up to 2^99
+        x = sign | (exp << 7) | man
+        nq = r.integers(0, 2 ** 32, (N, K // 8), dtype=np.uint64).astype(np.uint32)
+        ns = r.integers(40, 90, (N, K // 16), dtype=np.int64).astype(np.uint8)
+        got = qmv_kernel.qmv_nvfp4(to_torch(x, dev), to_torch(nq, dev), to_torch(ns, dev))
+        assert np.array_equal(to_np(got), ops.qmv_nvfp4(x, nq, ns)), (M, K, N)
+
+
 def test_quantize_bit_exact(dev):
     from qmtp import qmv_kernel
 
