@@ -143,7 +143,7 @@ def run_ours(args):
     rng = np.random.default_rng(1000 + rank)
     prompt = rng.integers(0, cfg.vocab, args.prompt).tolist()
     K, Wu = args.steps, args.warmup
-    dec = MTPDecoder(cfg, W, k=K_DRAFTS, max_tokens=Wu + 3 * K + 64, device=dev)
+    dec = MTPDecoder(cfg, W, k=K_DRAFTS, max_tokens=Wu + 3 * K + 64, device=dev, fuse_norm=args.fuse_norm)
 
     # ---- prefill, one eager cycle (library setup), capture
     t = dec.prefill(prompt)
@@ -543,6 +543,8 @@ def main():
     ap.add_argument("--cpu-cycles", type=int, default=3, help="oracle cycles for cpu_baseline (0 = skip)")
     ap.add_argument("--ref-prompt", type=int, default=16)
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens (ours)")
+    ap.add_argument("--fuse-norm", action="store_true",
+                    help="decoder runs the layer RMSNorms inside the consuming projections (bit-identical)")
     ap.add_argument("--kernel", default=None, choices=["qmv", "gdn", "head", "moe"],
                     help="time one kernel at a config shape instead of the decode loop")
     ap.add_argument("--shape", default="12288,4096,3", help="qmv: N,K,M[,affine|nvfp4]")

@@ -31,8 +31,14 @@ C = _lib.CTRL
 class MTPDecoder:
     """Device state + launch sequence of one greedy MTP decoding session (batch 1)."""
 
-    def __init__(self, args: ModelArgs, W: Weights, k: int = 2, max_tokens: int = 1024, device="cuda"):
+    def __init__(self, args: ModelArgs, W: Weights, k: int = 2, max_tokens: int = 1024, device="cuda",
+                 fuse_norm: bool = False):
         self.a, self.W, self.k = args, W, k
+        # fuse_norm: the input / post-attention RMSNorms run in the x prologue of the projection that
+        # consumes them (qmtp_qmv_ex PRE_RMSNORM, bit-identical to the separate kernel).  Off by default:
+        # every CTA of the projection then normalises the whole row again, which costs more than the
+        # separate launch it saves (config 4 on B200: 277 against 292 tok/s).
+        self.fuse_norm = fuse_norm
         self.S = k + 1
         self.dev = torch.device(device)
         a, S, dev = args, self.S, self.dev
@@ -100,12 +106,13 @@ class MTPDecoder:
         if rc != 0:
             _lib.check(rc, what)
 
-    def _qmv(self, x, lin, y, M, res=None, ldy=None):
-        """4-bit GEMV y = x . W^T (+ res), one qmtp_qmv_ex launch per 4 rows."""
+    def _qmv(self, x, lin, y, M, res=None, ldy=None, pre_w=None):
+        """4-bit GEMV y = x . W^T (+ res), one qmtp_qmv_ex launch per 4 rows; with pre_w, x is first
+        RMS-normalised with that weight (the decoder's fused norm)."""
         N, K = lin.out_features, lin.in_features
         ldy = ldy or N
         if self.qmv_log is not None:
-            self.qmv_log.append((x, lin, y, M, res, ldy))
+            self.qmv_log.append((x, lin, y, M, res, ldy, pre_w))
         self.launches += (M + 3) // 4
         if self.prof is not None:
             e0 = torch.cuda.Event(enable_timing=True)
@@ -115,6 +122,10 @@ class MTPDecoder:
         a.w, a.scales, a.biases = lin.weight.data_ptr(), lin.scales.data_ptr(), lin.biases.data_ptr()
         a.y, a.res = y.data_ptr(), (res.data_ptr() if res is not None else None)
         a.M, a.N, a.K, a.ldy = M, N, K, ldy
+        if pre_w is not None:
+            a.pre, a.pre_w, a.pre_eps = _lib.QMV_PRE_RMSNORM, pre_w.data_ptr(), self.a.eps
+        else:
+            a.pre, a.pre_w = _lib.QMV_PRE_NONE, None
         self._chk(self.L.qmtp_qmv_ex(ctypes.byref(a), self._st()), "qmv")
         if self.prof is not None:
             e1 = torch.cuda.Event(enable_timing=True)
@@ -141,10 +152,12 @@ class MTPDecoder:
             snap=1)
 
     # ------------------------------------------------------------------ layers
-    def _attn_layer(self, L, x, rows, kc, vc, pos_slot):
-        """Gated attention block: x (pre-norm residual stream, [rows, H]) += o_proj(attn(...))."""
+    def _attn_layer(self, L, x, rows, kc, vc, pos_slot, xin=None, pre_w=None):
+        """Gated attention block: x (pre-norm residual stream, [rows, H]) += o_proj(attn(...)); the
+        projection input is xin (default: the normalised rows in self.xn), RMS-normalised by pre_w if given."""
         a = self.a
-        self._qmv(self.xn, L["qkv_proj"], self.proj, rows, ldy=self.proj.shape[1])
+        self._qmv(self.xn if xin is None else xin, L["qkv_proj"], self.proj, rows, ldy=self.proj.shape[1],
+                  pre_w=pre_w)
         self._chk(self.L.qmtp_attn_prep(self.proj.data_ptr(), self.proj.shape[1], rows, a.n_heads, a.n_kv,
                                         a.head_dim, a.rotary_dim, L["q_norm"].data_ptr(), L["k_norm"].data_ptr(),
                                         a.eps, self.cos.data_ptr(), self.sin.data_ptr(), self._cp(pos_slot), 0,
@@ -157,8 +170,11 @@ class MTPDecoder:
 
     def _mlp(self, L, x, rows):
         a = self.a
-        self._norm(x, L["post_ln"], self.xn, rows)
-        self._qmv(self.xn, L["gate_up"], self.gu, rows)
+        if self.fuse_norm:
+            self._qmv(x, L["gate_up"], self.gu, rows, pre_w=L["post_ln"])
+        else:
+            self._norm(x, L["post_ln"], self.xn, rows)
+            self._qmv(self.xn, L["gate_up"], self.gu, rows)
         self._chk(self.L.qmtp_swiglu(self.gu.data_ptr(), 2 * a.intermediate, rows, a.intermediate,
                                      self.act.data_ptr(), self._st()), "swiglu")
         self._qmv(self.act, L["down"], x, rows, res=x)
@@ -172,9 +188,13 @@ class MTPDecoder:
                                     self._st()), "embed")
         for i in range(a.layers):
             L = W[f"layers.{i}"]
-            self._norm(self.h, L["input_ln"], self.xn, S)
+            if self.fuse_norm:
+                xin, pw = self.h, L["input_ln"]
+            else:
+                self._norm(self.h, L["input_ln"], self.xn, S)
+                xin, pw = self.xn, None
             if a.is_linear(i):
-                self._qmv(self.xn, L["in_proj"], self.proj, S, ldy=self.proj.shape[1])
+                self._qmv(xin, L["in_proj"], self.proj, S, ldy=self.proj.shape[1], pre_w=pw)
                 self._chk(self.L.qmtp_gdn_fused_ex(ctypes.byref(self._gdn_args[i]), self._st()), "gdn")
                 Z = a.lin_hv * a.lin_dv
                 self._chk(self.L.qmtp_gdn_norm_gate(self.ygdn.data_ptr(), self.proj.data_ptr() + 2 * a.conv_dim,
@@ -184,7 +204,7 @@ class MTPDecoder:
                 self._qmv(self.gdn_out, L["out_proj"], self.h, S, res=self.h)
             else:
                 kc, vc = self.kv[i]
-                self._attn_layer(L, self.h, S, kc, vc, C["POS"])
+                self._attn_layer(L, self.h, S, kc, vc, C["POS"], xin=xin, pre_w=pw)
             self._mlp(L, self.h, S)
         self._norm(self.h, W["norm"], self.hn, S)
 
@@ -212,8 +232,12 @@ class MTPDecoder:
                                       self.mcat.data_ptr() + 2 * H, 2 * H, rows, H, self._st()), "rmsnorm")
         self._qmv(self.mcat, M["fc"], self.mx, rows)
         Ly = M["layer"]
-        self._norm(self.mx, Ly["input_ln"], self.xn, rows)
-        self._attn_layer(Ly, self.mx, rows, self.mkv[0], self.mkv[1], C["MPOS"])
+        if self.fuse_norm:
+            self._attn_layer(Ly, self.mx, rows, self.mkv[0], self.mkv[1], C["MPOS"], xin=self.mx,
+                             pre_w=Ly["input_ln"])
+        else:
+            self._norm(self.mx, Ly["input_ln"], self.xn, rows)
+            self._attn_layer(Ly, self.mx, rows, self.mkv[0], self.mkv[1], C["MPOS"])
         self._mlp(Ly, self.mx, rows)
         if not with_draft:
             return

@@ -60,3 +60,22 @@ def test_config4_loop_shape_on_small_model(small_pair):
     ref, _ = orc.generate_mtp(p, 256)
     out, st = generate_mtp(_decoder(W), p, 256, use_graph=True)
     assert len(out) == 256 and out == ref
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_fused_norm_stream_matches_oracle(small_pair, use_graph):
+    """Decoder with the input / post-attention RMSNorms fused into the projections' x prologue."""
+    from qmtp import model as qm
+    from qmtp.mtp import MTPDecoder, generate_mtp
+
+    orc, W = small_pair
+    p = prompt(34, seed=2)
+    g = orc.generate_greedy(p, 45)
+    ref, rst = orc.generate_mtp(p, 45, draft_override=greedy_overrides(g, om.SMALL.vocab))
+    dec = MTPDecoder(qm.SMALL, W, k=2, max_tokens=300, fuse_norm=True)
+    out, st = generate_mtp(dec, p, 45, use_graph=use_graph, draft_override=greedy_overrides(g, om.SMALL.vocab))
+    assert out == ref and st["acept"] == rst["acept"]
+    ref2, _ = orc.generate_mtp(p, 30)
+    out2, _ = generate_mtp(MTPDecoder(qm.SMALL, W, k=2, max_tokens=300, fuse_norm=True), p, 30,
+                           use_graph=use_graph)
+    assert out2 == ref2
