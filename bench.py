@@ -124,7 +124,7 @@ def run_ours(args):
 
     from qmtp import _lib
     from qmtp import model as qm
-    from qmtp.mtp import MTPDecoder, _restore, _snapshot, export_state, generate_mtp
+    from qmtp.mtp import MTPDecoder, Sampling, _restore, _snapshot, export_state, generate_mtp
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -143,7 +143,10 @@ def run_ours(args):
     rng = np.random.default_rng(1000 + rank)
     prompt = rng.integers(0, cfg.vocab, args.prompt).tolist()
     K, Wu = args.steps, args.warmup
-    dec = MTPDecoder(cfg, W, k=K_DRAFTS, max_tokens=Wu + 3 * K + 64, device=dev, fuse_norm=args.fuse_norm)
+    sp = (Sampling(args.temperature, args.top_k, args.top_p, args.min_p, args.seed) if args.temperature > 0
+          else None)
+    dec = MTPDecoder(cfg, W, k=K_DRAFTS, max_tokens=Wu + 3 * K + 64, device=dev, fuse_norm=args.fuse_norm,
+                     sampling=sp)
 
     # ---- prefill, one eager cycle (library setup), capture
     t = dec.prefill(prompt)
@@ -244,12 +247,16 @@ def run_ours(args):
            "ms_per_step": round(elapsed_ms / K, 4), "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
            "config": {"workload": "config4: synthetic Qwen3.5-9B-shaped hybrid decoder (32 layers, 3:1 GDN:attention, "
-                                  "4-bit affine g64), 1-layer MTP head, greedy MTP decode k=2, batch 1, "
-                                  f"{args.prompt}-token uniform random prompt",
+                                  "4-bit affine g64), 1-layer MTP head, "
+                                  + ("greedy" if sp is None else "exact speculative sampling")
+                                  + f" MTP decode k=2, batch 1, {args.prompt}-token uniform random prompt",
                       "step": "one verify cycle (verify 3 tokens + accept/rollback + 2 draft steps)",
                       "prompt_tokens": args.prompt, "drafts": K_DRAFTS, "parallelism": f"replicas x{world}",
                       "l2": "weights ~7.5 GB per cycle >> 126 MB L2 (no flush needed)",
-                      "weights_build_s": round(t_build, 1)},
+                      "weights_build_s": round(t_build, 1),
+                      **({} if sp is None else {"sampling": {"temperature": sp.temperature, "top_k": sp.top_k,
+                                                             "top_p": sp.top_p, "min_p": sp.min_p,
+                                                             "seed": sp.seed, "head_candidates": dec.K}})},
            "e2e": {"value": round(e2e_tps, 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 4 * _lib.CTRL_SIZE, "tokens": len(out)},
            "roofline": roofline, "clocks": clocks, "gpu_launches": launches_per_cycle * K,
@@ -258,7 +265,7 @@ def run_ours(args):
 
     # ---- CPU oracle on a bounded sample of the same decode, from the same post-prefill state
     if post_prefill is not None:
-        res["cpu_baseline"] = cpu_baseline_from_state(cfg, W, post_prefill, gpu_stream, args.cpu_cycles)
+        res["cpu_baseline"] = cpu_baseline_from_state(cfg, W, post_prefill, gpu_stream, args.cpu_cycles, sp)
     if world > 1:
         dist.barrier()
         dec.graph = None
@@ -267,7 +274,7 @@ def run_ours(args):
         print(json.dumps(res), flush=True)
 
 
-def cpu_baseline_from_state(cfg, W, state, gpu_tokens, cycles):
+def cpu_baseline_from_state(cfg, W, state, gpu_tokens, cycles, sampling=None):
     import numpy as np
 
     from oracle import model as om
@@ -281,7 +288,9 @@ def cpu_baseline_from_state(cfg, W, state, gpu_tokens, cycles):
     layers, mtp, pending = state
     cache, mcache = orc.load_state(layers, mtp)
     copy_s = time.time() - t0
-    out, st = orc.decode(cache, mcache, pending[0], pending[1:], max_tokens=10 ** 6, k=K_DRAFTS, max_cycles=cycles)
+    # with sampling, the first verify cycle after the prompt uses Philox call counter 1 (0 drew the first token)
+    out, st = orc.decode(cache, mcache, pending[0], pending[1:], max_tokens=10 ** 6, k=K_DRAFTS, max_cycles=cycles,
+                         sampling=sampling, rng_ctr=1)
     got = out[1:]
     ref = gpu_tokens[:len(got)]
     return {"value": round(st["tps"], 4), "unit": "tok/s", "cores": threads, "kind": "port",
@@ -543,6 +552,12 @@ def main():
     ap.add_argument("--cpu-cycles", type=int, default=3, help="oracle cycles for cpu_baseline (0 = skip)")
     ap.add_argument("--ref-prompt", type=int, default=16)
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens (ours)")
+    ap.add_argument("--temperature", type=float, default=0.0,
+                    help="> 0: exact speculative sampling instead of greedy (engine.py:91-152)")
+    ap.add_argument("--top-k", type=int, default=0)
+    ap.add_argument("--top-p", type=float, default=1.0)
+    ap.add_argument("--min-p", type=float, default=0.0)
+    ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--fuse-norm", action="store_true",
                     help="decoder runs the layer RMSNorms inside the consuming projections (bit-identical)")
     ap.add_argument("--kernel", default=None, choices=["qmv", "gdn", "head", "moe"],

@@ -335,6 +335,9 @@ int qmtp_moe_dispatch(const void* idx, int T, int S, const void* x, int H, int n
 #define QMTP_CTRL_ACC0 10     /* accepted-draft counters per draft position */
 #define QMTP_CTRL_EMIT0 20    /* tokens emitted by the last cycle (KEEP of them) */
 #define QMTP_CTRL_MAX_K 8
+#define QMTP_CTRL_RNG 29      /* sampling: calls of qmtp_sample so far (the Philox call counter) */
+#define QMTP_CTRL_SEED_LO 30  /* sampling: Philox key, low word (set by the caller) */
+#define QMTP_CTRL_SEED_HI 31  /* sampling: Philox key, high word */
 #define QMTP_CTRL_SIZE 32
 
 /* Greedy verification + rollback bookkeeping (mtp.py:275-294, engine.py:121-128, mtp.py:136-140):
@@ -349,6 +352,28 @@ int qmtp_mtp_advance(int* ctrl, void* stream);
 
 /* Next verify input: in = [a[SEL], drafts[0..k)]. */
 int qmtp_next_tokens(const int* a, const int* drafts, int k, const int* ctrl, int* in, void* stream);
+
+/* Sampling parameters (engine.py:29-35 Sampling): temperature > 0; top_k 0 = off; top_p in (0, 1],
+ * 1 = off; min_p in [0, 1], 0 = off. */
+typedef struct {
+  float temperature;
+  int top_k;
+  float top_p;
+  float min_p;
+} qmtp_sampling;
+
+/* Exact speculative sampling over the two-stage head's candidates (engine.py:91-152: Engine._dist,
+ * _sample_first, _verify).  idx int32 / fine bf16 [rows, ld]: K <= 256 candidates per row (vocabulary
+ * ids and exact logits, as qmtp_topk_rescore writes them).
+ *   first_row < 0 (verify): drafts[0..k); draft i is accepted with probability p_i(d_i), else a token
+ *     is drawn from p_i without d_i and the cycle stops; all accepted -> a bonus draw from row k.
+ *     out[0..n_acc] = the emitted tokens (accepted drafts, then the drawn token), so a following
+ *     qmtp_mtp_accept(out, [t, drafts]) counts n_acc and commits n_acc + 1 tokens.
+ *   first_row >= 0: one draw from that row into out[first_row] (the first token after a prompt).
+ * Random numbers: Philox4x32-10 keyed by ctrl[QMTP_CTRL_SEED_LO/HI], counter (ctrl[QMTP_CTRL_RNG],
+ * row, use, 0); every call increments ctrl[QMTP_CTRL_RNG].  V = vocabulary size (top_k >= V is off). */
+int qmtp_sample(const int* idx, const void* fine, int K, int ld, const int* drafts, int k, int first_row,
+                const qmtp_sampling* sp, int V, int* ctrl, int* out, void* stream);
 
 #ifdef __cplusplus
 }

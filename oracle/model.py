@@ -218,6 +218,23 @@ class OracleModel:
         _, idx, fine, amax = ops.two_stage_head(hn, wq, s, b, self.W["lm_head"], k)
         return amax
 
+    def candidates(self, hn, K):
+        """Two-stage head candidates (vocabulary ids int32 [M, K], exact logits bf16 [M, K])."""
+        wq, s, b = self.W["lm_head_q"]
+        _, idx, fine, _ = ops.two_stage_head(hn, wq, s, b, self.W["lm_head"], K)
+        return idx, fine
+
+    def _sample(self, hn, sp, ctr, drafts=None):
+        """engine.py:110-152 through the C sampler: first token (drafts None) or a verify decision."""
+        K = sampling_k(sp)
+        idx, fine = self.candidates(hn, K)
+        seed = int(sp.seed or 0)
+        kw = dict(temperature=sp.temperature, top_k=sp.top_k, top_p=sp.top_p, min_p=sp.min_p, V=self.a.vocab,
+                  seed=seed, ctr=ctr)
+        if drafts is None:
+            return ops.sample(idx, fine, None, first_row=idx.shape[0] - 1, **kw)
+        return ops.sample(idx, fine, drafts, **kw)
+
     def draft_token(self, xn):
         """Draft head: full-vocabulary 4-bit head (bench_ab.py:24 DRAFT_HEAD, engine.py:46-48) + argmax."""
         return ops.argmax_bf16(qmv(xn, self.W["lm_head_q"]))
@@ -254,18 +271,22 @@ class OracleModel:
             out.append(int(self.head(hn)[0]))
         return out
 
-    def prefill(self, prompt_ids, k=2):
-        """mtp.py:258-263: prompt pass, first token t, first drafts; returns (cache, mcache, h, t, drafts)."""
+    def prefill(self, prompt_ids, k=2, sampling=None):
+        """mtp.py:258-263: prompt pass, first token t, first drafts; returns (cache, mcache, h, t, drafts).
+        With sampling (temperature > 0) the first token is drawn (engine.py:110-115, call counter 0)."""
         cache = self.make_cache()
         mcache = self._kv()
         p = np.int32(prompt_ids)
         h, hn = self.backbone(p, cache)
-        t = int(self.head(hn[-1:])[0])
+        t = int(self._sample(hn[-1:], sampling, 0)) if _sampled(sampling) else int(self.head(hn[-1:])[0])
         drafts = self.draft_chain(h, np.concatenate([p[1:], np.int32([t])]), mcache, k)
         return cache, mcache, t, drafts
 
-    def decode(self, cache, mcache, t, drafts, max_tokens, eos=(), k=2, max_cycles=None, draft_override=None):
-        """The verify loop of mtp.py:268-294 from a given state; returns (out tokens incl. t, stats)."""
+    def decode(self, cache, mcache, t, drafts, max_tokens, eos=(), k=2, max_cycles=None, draft_override=None,
+               sampling=None, rng_ctr=1):
+        """The verify loop of mtp.py:268-294 from a given state; returns (out tokens incl. t, stats).
+        With sampling (temperature > 0) each cycle decides by exact speculative sampling (engine.py:
+        121-152) with call counter rng_ctr, rng_ctr + 1, ..."""
         t0 = time.perf_counter()
         out = [t]
         cycles = verified = 0
@@ -279,11 +300,17 @@ class OracleModel:
                 if o is not None:
                     drafts = [int(v) for v in o]
             h, hn = self.backbone(np.int32([t] + drafts), cache, snap=True)
-            av = [int(v) for v in self.head(hn)]
-            n_acc = 0
-            while n_acc < k and av[n_acc] == drafts[n_acc]:
-                acc_pos[n_acc] += 1
-                n_acc += 1
+            if _sampled(sampling):
+                n_acc, av = self._sample(hn, sampling, rng_ctr, drafts)
+                rng_ctr += 1
+                for i in range(n_acc):
+                    acc_pos[i] += 1
+            else:
+                av = [int(v) for v in self.head(hn)]
+                n_acc = 0
+                while n_acc < k and av[n_acc] == drafts[n_acc]:
+                    acc_pos[n_acc] += 1
+                    n_acc += 1
             cycles += 1
             verified += k
             keep = n_acc + 1
@@ -319,12 +346,13 @@ class OracleModel:
                 cache.append(KVCache(entry[1].copy(), entry[2].copy(), int(entry[3])))
         return cache, KVCache(mtp[0].copy(), mtp[1].copy(), int(mtp[2]))
 
-    def generate_mtp(self, prompt_ids, max_tokens, eos=(), k=2, max_cycles=None, draft_override=None):
-        """mtp.py:241-303 (greedy, fixed k).  draft_override(cycle) -> list of k tokens or None
-        replaces the drafts a cycle verifies (test hook for acceptance and rollback; the MTP caches
-        still follow the computed drafts)."""
-        cache, mcache, t, drafts = self.prefill(prompt_ids, k)
-        return self.decode(cache, mcache, t, drafts, max_tokens, eos, k, max_cycles, draft_override)
+    def generate_mtp(self, prompt_ids, max_tokens, eos=(), k=2, max_cycles=None, draft_override=None,
+                     sampling=None):
+        """mtp.py:241-303 (fixed k; greedy, or sampled when sampling.temperature > 0).
+        draft_override(cycle) -> list of k tokens or None replaces the drafts a cycle verifies (test
+        hook for acceptance and rollback; the MTP caches still follow the computed drafts)."""
+        cache, mcache, t, drafts = self.prefill(prompt_ids, k, sampling)
+        return self.decode(cache, mcache, t, drafts, max_tokens, eos, k, max_cycles, draft_override, sampling)
 
     # -- mtp.py:136-140
     def restore(self, c: GDNCache, keep: int) -> None:
@@ -332,6 +360,17 @@ class OracleModel:
         n_keep = self.a.conv_k - 1
         c.conv = win[keep:keep + n_keep].copy()
         c.state = mids[keep - 1].copy() if keep - 1 < mids.shape[0] else c.state
+
+
+def _sampled(sp) -> bool:
+    return sp is not None and sp.temperature > 0
+
+
+def sampling_k(sp) -> int:
+    """lm_head2.py:32-36 k_for: head candidates for a sampling configuration."""
+    if sp is None or sp.temperature <= 0 or 0 < sp.top_k <= 32:
+        return 64
+    return 256 if sp.top_k <= 0 else min(4 * sp.top_k, 2048)
 
 
 # ------------------------------------------------------------------ synthetic weights

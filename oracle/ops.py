@@ -307,3 +307,35 @@ def moe(x_bf16, wg, sg, wu, su, wd, sd, idx, scores, mode: str = "mxfp4", limit=
     if rc != 0:
         raise ValueError(f"qo_moe: rc {rc}")
     return yb, yf
+
+
+# ---------------------------------------------------------------- speculative sampling (T > 0)
+def philox4x32_10(ctr, key) -> np.ndarray:
+    """C qo_philox4x32_10: Philox4x32-10 of a 4-word counter under a 2-word key."""
+    c = np.ascontiguousarray(ctr, np.uint32)
+    k = np.ascontiguousarray(key, np.uint32)
+    o = np.empty(4, np.uint32)
+    lib().qo_philox4x32_10(_p(c), _p(k), _p(o))
+    return o
+
+
+def sample(idx, fine, drafts, temperature, top_k=0, top_p=1.0, min_p=0.0, V=None, seed=0, ctr=0, first_row=-1):
+    """C qo_sample over candidate rows idx int32 [R, K] / fine bf16 [R, K]: verify mode (first_row < 0)
+    returns (n_acc, emitted tokens); first mode returns the token drawn from row first_row."""
+    idx = np.ascontiguousarray(idx, np.int32)
+    fine = np.ascontiguousarray(fine, np.uint16)
+    R, K = idx.shape
+    d = np.ascontiguousarray(drafts if drafts is not None else [], np.int32)
+    k = int(d.size)
+    out = np.zeros(max(k + 1, 1), np.int32)
+    f = lib().qo_sample
+    f.restype = ctypes.c_int
+    n = f(_p(idx), _p(fine), _I(K), _I(K), _p(d) if k else None, _I(k), _I(first_row), ctypes.c_float(temperature),
+          _I(top_k), ctypes.c_float(top_p), ctypes.c_float(min_p), _I(V if V is not None else 1 << 30),
+          ctypes.c_uint32(seed & 0xFFFFFFFF), ctypes.c_uint32((seed >> 32) & 0xFFFFFFFF), ctypes.c_uint32(ctr),
+          _p(out))
+    if n < 0:
+        raise ValueError("qo_sample: bad arguments")
+    if first_row >= 0:
+        return int(out[0])
+    return n, [int(v) for v in out[:n + 1]]

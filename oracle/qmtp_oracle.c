@@ -993,3 +993,131 @@ QO_API int qo_moe(int fmt, const uint16_t* x, const uint32_t* wg, const uint8_t*
   free(yacc); free(xd); free(list); free(h);
   return 0;
 }
+
+/* ------------------------------------------------------------------ speculative sampling (T > 0)
+ * engine.py:91-152 (Engine._dist / _sample_first / _verify) restated with a fixed operation order
+ * and a counter-based generator, so the CUDA sampler (csrc/sample.cu) makes the same decisions.
+ *
+ * Random numbers: Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as easy as
+ * 1, 2, 3", SC 2011): 10 rounds of two 32x32->64 multiplies, Weyl key schedule.  A uniform is the
+ * top 24 bits of output word 0 times 2^-24 (exact in fp32, in [0, 1)).  Counter = (call counter,
+ * row, use (0: accept test, 1: categorical draw), 0), key = the 64-bit seed. */
+QO_API void qo_philox4x32_10(const uint32_t* ctr_in, const uint32_t* key_in, uint32_t* out) {
+  uint32_t c[4] = {ctr_in[0], ctr_in[1], ctr_in[2], ctr_in[3]}, k0 = key_in[0], k1 = key_in[1];
+  for (int r = 0; r < 10; ++r) {
+    if (r > 0) { k0 += 0x9E3779B9u; k1 += 0xBB67AE85u; }
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c[0], p1 = (uint64_t)0xCD9E8D57u * c[2];
+    const uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0, hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+    const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+    c[0] = n0; c[1] = lo1; c[2] = n2; c[3] = lo0;
+  }
+  memcpy(out, c, sizeof c);
+}
+static float qo_uniform(uint32_t seed_lo, uint32_t seed_hi, uint32_t ctr, uint32_t row, uint32_t use) {
+  const uint32_t c[4] = {ctr, row, use, 0u}, k[2] = {seed_lo, seed_hi};
+  uint32_t o[4];
+  qo_philox4x32_10(c, k, o);
+  return (float)(o[0] >> 8) * (1.0f / 16777216.0f);
+}
+
+typedef struct { float l; int32_t i; } qo_scand;
+/* candidates ordered by exact logit descending, then vocabulary index ascending */
+static int qo_scand_cmp(const void* a, const void* b) {
+  const qo_scand *x = (const qo_scand*)a, *y = (const qo_scand*)b;
+  if (x->l > y->l) return -1;
+  if (x->l < y->l) return 1;
+  return (x->i < y->i) ? -1 : (x->i > y->i);
+}
+
+/* Engine._dist (engine.py:92-108) over one row's K candidates (the two-stage head leaves every
+ * other logit at -inf): temperature, top_k, log-softmax, top_p on the sorted exclusive cumsum,
+ * min_p, renormalisation.  Leaves the kept candidates sorted in c[0..n) and p[0..n). */
+static int qo_dist(const int32_t* idx, const uint16_t* fine, int K, float T, int top_k, float top_p, float min_p,
+                   int V, qo_scand* c, float* p) {
+  for (int j = 0; j < K; ++j) { c[j].l = qo_bf2f(fine[j]); c[j].i = idx[j]; }
+  qsort(c, (size_t)K, sizeof(qo_scand), qo_scand_cmp);
+  int n = K;
+  if (top_k > 0 && top_k < V && top_k < n) n = top_k;
+  float z[2048], lp[2048];
+  for (int j = 0; j < n; ++j) z[j] = c[j].l / T;
+  const float m = z[0];
+  float s = 0.0f;
+  for (int j = 0; j < n; ++j) s = s + qo_expf(z[j] - m);
+  const float L = m + qo_logf(s);
+  for (int j = 0; j < n; ++j) lp[j] = z[j] - L;
+  if (top_p < 1.0f) {
+    float acc = 0.0f;
+    int np_ = n;
+    for (int j = 0; j < n; ++j) {
+      const float q = qo_expf(lp[j]);
+      const float inc = acc + q;
+      if (!(inc - q < top_p)) { np_ = j; break; }
+      acc = inc;
+    }
+    n = np_;
+  }
+  if (min_p > 0.0f) {
+    const float thr = lp[0] + qo_logf(min_p);
+    int nm = n;
+    for (int j = 0; j < n; ++j)
+      if (!(lp[j] >= thr)) { nm = j; break; }
+    n = nm;
+  }
+  float s2 = 0.0f;
+  for (int j = 0; j < n; ++j) { p[j] = qo_expf(lp[j] - lp[0]); s2 = s2 + p[j]; }
+  for (int j = 0; j < n; ++j) p[j] = p[j] / s2;
+  return n;
+}
+
+/* categorical draw by inverse CDF over the kept candidates, skipping vocabulary id `excl` */
+static int32_t qo_draw(const qo_scand* c, const float* p, int n, int32_t excl, float u) {
+  float tot = 0.0f;
+  for (int j = 0; j < n; ++j)
+    if (c[j].i != excl) tot = tot + p[j];
+  const float r = u * tot;
+  float acc = 0.0f;
+  int32_t last = c[0].i;
+  for (int j = 0; j < n; ++j) {
+    if (c[j].i == excl) continue;
+    acc = acc + p[j];
+    last = c[j].i;
+    if (acc > r) return c[j].i;
+  }
+  return last;
+}
+
+/* mode verify (first_row < 0): rows 0..k of [*, ld] candidates against drafts[0..k) (engine.py:
+ * 121-152): accept draft i with probability p_i(d_i), else draw from p_i without d_i and stop; all
+ * accepted -> draw the bonus token from row k.  Writes the emitted tokens to out (n_acc + 1 of
+ * them) and returns n_acc.  Mode first (first_row >= 0, engine.py:110-115): one draw from that row
+ * into out[0] (its uniform uses counter row 0, wherever the row sits); returns 0.  K <= 2048; T > 0. */
+QO_API int qo_sample(const int32_t* idx, const uint16_t* fine, int K, int ld, const int32_t* drafts, int k,
+                     int first_row, float T, int top_k, float top_p, float min_p, int V, uint32_t seed_lo,
+                     uint32_t seed_hi, uint32_t ctr, int32_t* out) {
+  if (K < 1 || K > 2048 || !(T > 0.0f)) return -1;
+  qo_scand c[2048];
+  float p[2048];
+  if (first_row >= 0) {
+    const int n = qo_dist(idx + (size_t)first_row * ld, fine + (size_t)first_row * ld, K, T, top_k, top_p, min_p,
+                          V, c, p);
+    out[0] = qo_draw(c, p, n, -1, qo_uniform(seed_lo, seed_hi, ctr, 0u, 1u));  /* counter row 0 */
+    return 0;
+  }
+  for (int i = 0; i <= k; ++i) {
+    const int n = qo_dist(idx + (size_t)i * ld, fine + (size_t)i * ld, K, T, top_k, top_p, min_p, V, c, p);
+    if (i == k) {
+      out[k] = qo_draw(c, p, n, -1, qo_uniform(seed_lo, seed_hi, ctr, (uint32_t)k, 1u));
+      return k;
+    }
+    float pd = 0.0f;
+    for (int j = 0; j < n; ++j)
+      if (c[j].i == drafts[i]) pd = p[j];
+    if (qo_uniform(seed_lo, seed_hi, ctr, (uint32_t)i, 0u) < pd) {
+      out[i] = drafts[i];
+      continue;
+    }
+    out[i] = qo_draw(c, p, n, drafts[i], qo_uniform(seed_lo, seed_hi, ctr, (uint32_t)i, 1u));
+    return i;
+  }
+  return k;
+}

@@ -96,7 +96,18 @@ SIGNATURES.update({
 
 # control block layout (include/qmtp.h QMTP_CTRL_*)
 CTRL = dict(SLOT=0, CONV_ROW=1, WOUT_ROW=2, WPAR=3, POS=4, MPOS=5, KEEP=6, SEL=7, NOUT=8, CYCLES=9, ACC0=10,
-            EMIT0=20)
+            EMIT0=20, RNG=29, SEED_LO=30, SEED_HI=31)
+
+
+class SamplingArgs(ctypes.Structure):
+    """Mirror of qmtp_sampling (include/qmtp.h)."""
+    _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_int), ("top_p", ctypes.c_float),
+                ("min_p", ctypes.c_float)]
+
+
+SIGNATURES["qmtp_sample"] = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                             ctypes.c_int, ctypes.c_int, ctypes.POINTER(SamplingArgs), ctypes.c_int,
+                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
 CTRL_SIZE = 32
 # size queries return size_t
 SIZE_QUERIES: dict[str, list] = {

@@ -17,23 +17,45 @@ from __future__ import annotations
 
 import ctypes
 import time
+from dataclasses import dataclass
 
 import numpy as np
 import torch
 
 from . import _lib
-from .lm_head2 import TwoStageHead
+from .lm_head2 import TwoStageHead, k_for
 from .model import ModelArgs, Weights, rope_tables
 
 C = _lib.CTRL
 
 
+@dataclass
+class Sampling:
+    """engine.py:29-35: temperature 0 is greedy; top_k 0, top_p 1 and min_p 0 are off.  seed keys the
+    counter-based generator (None: 0), so a seeded request replays exactly."""
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    min_p: float = 0.0
+    seed: int | None = None
+
+
 class MTPDecoder:
-    """Device state + launch sequence of one greedy MTP decoding session (batch 1)."""
+    """Device state + launch sequence of one MTP decoding session (batch 1; greedy or sampled)."""
 
     def __init__(self, args: ModelArgs, W: Weights, k: int = 2, max_tokens: int = 1024, device="cuda",
-                 fuse_norm: bool = False):
+                 fuse_norm: bool = False, sampling: Sampling | None = None):
         self.a, self.W, self.k = args, W, k
+        # sampling with temperature > 0: exact speculative sampling (engine.py:91-152) over the
+        # k_for(sampling) candidates of the two-stage head (lm_head2.py:32-36); otherwise greedy
+        self.sp = sampling if sampling is not None and sampling.temperature > 0 else None
+        self.K = k_for(self.sp)
+        if self.K > 256:
+            raise NotImplementedError(f"top_k = {sampling.top_k} needs {self.K} head candidates; this build "
+                                      "selects at most 256 (top_k <= 64, or top_k = 0)")
+        if self.sp is not None:
+            self._sargs = _lib.SamplingArgs(float(self.sp.temperature), int(self.sp.top_k), float(self.sp.top_p),
+                                            float(self.sp.min_p))
         # fuse_norm: the input / post-attention RMSNorms run in the x prologue of the projection that
         # consumes them (qmtp_qmv_ex PRE_RMSNORM, bit-identical to the separate kernel).  Off by default:
         # every CTA of the projection then normalises the whole row again, which costs more than the
@@ -65,9 +87,9 @@ class MTPDecoder:
         self.gu, self.act = z(S, 2 * a.intermediate), z(S, a.intermediate)
         self.memb, self.mcat, self.mx, self.mxn = z(S, H), z(S, 2 * H), z(S, H), z(1, H)
         self.dlogits = z(1, a.vocab)
-        self.fine, self.idx = z(S, 64), z(S, 64, dtype=i32)
+        self.fine, self.idx = z(S, self.K), z(S, self.K, dtype=i32)
         self.coarse = z(S, a.vocab)
-        self.topk_ws = torch.empty(self.L.qmtp_topk_workspace(S, a.vocab, 64), dtype=torch.uint8, device=dev)
+        self.topk_ws = torch.empty(self.L.qmtp_topk_workspace(S, a.vocab, self.K), dtype=torch.uint8, device=dev)
         self.argmax_ws = torch.empty(self.L.qmtp_argmax_workspace(1, a.vocab), dtype=torch.uint8, device=dev)
         # recurrent / cache state
         self.lin_ids = [i for i in range(a.layers) if a.is_linear(i)]
@@ -213,7 +235,7 @@ class MTPDecoder:
         a = self.a
         self._qmv(self.hn, self.W["lm_head_q"], self.coarse, self.S)
         self.launches += 2
-        self._chk(self.L.qmtp_topk_rescore(self.coarse.data_ptr(), a.vocab, self.S, a.vocab, 64,
+        self._chk(self.L.qmtp_topk_rescore(self.coarse.data_ptr(), a.vocab, self.S, a.vocab, self.K,
                                            self.W["lm_head"].data_ptr(), self.hn.data_ptr(), a.hidden,
                                            self.idx.data_ptr(), self.fine.data_ptr(), self.a_tok.data_ptr(),
                                            self.topk_ws.data_ptr(), self.topk_ws.numel(), self._st()), "head")
@@ -247,6 +269,15 @@ class MTPDecoder:
         self._chk(self.L.qmtp_argmax_bf16(self.dlogits.data_ptr(), a.vocab, 1, a.vocab, draft_out,
                                           self.argmax_ws.data_ptr(), self.argmax_ws.numel(), self._st()), "argmax")
 
+    def _sample(self, first_row=-1):
+        """Sampling mode: the emitted tokens (verify) or the first token (first_row) over a_tok."""
+        self.launches += 1
+        rc = self.L.qmtp_sample(self.idx.data_ptr(), self.fine.data_ptr(), self.K, self.K,
+                                self.tokens_in.data_ptr() + 4, self.k, first_row, ctypes.byref(self._sargs),
+                                self.a.vocab, self.ctrl.data_ptr(), self.a_tok.data_ptr(), self._st())
+        if rc != 0:
+            _lib.check(rc, "sample")
+
     def _accept(self, forced_keep=0):
         self._chk(self.L.qmtp_mtp_accept(self.a_tok.data_ptr(), self.tokens_in.data_ptr(), self.k, self.ctrl.data_ptr(),
                                          self.out_tokens.data_ptr(), self.out_cap, self.slots, self.win_rows,
@@ -269,6 +300,8 @@ class MTPDecoder:
         """One verify + accept + draft cycle (mtp.py:268-294), device-side only."""
         self.backbone()
         self._head()
+        if self.sp is not None:
+            self._sample()
         self._accept()
         self._draft_chain(self.h, self.a_tok.data_ptr())
         self.ctrl_host.copy_(self.ctrl, non_blocking=True)
@@ -277,6 +310,11 @@ class MTPDecoder:
     def reset(self):
         self.ctrl.zero_()
         self.ctrl[C["WOUT_ROW"]] = self.win_rows
+        if self.sp is not None:
+            seed = int(self.sp.seed or 0) & 0xFFFFFFFFFFFFFFFF
+            lo, hi = seed & 0xFFFFFFFF, seed >> 32
+            self.ctrl[C["SEED_LO"]] = lo - (1 << 32) if lo >= 1 << 31 else lo
+            self.ctrl[C["SEED_HI"]] = hi - (1 << 32) if hi >= 1 << 31 else hi
         for i in self.lin_ids:
             self.win[i].zero_()
             self.ring[i][0].zero_()
@@ -295,6 +333,8 @@ class MTPDecoder:
             last = c == n_chunks - 1
             if last:
                 self._norm_head_rows()
+                if self.sp is not None:  # the first token is drawn from the last prompt row (engine.py:110-115)
+                    self._sample(first_row=n - 1)
             self._accept(forced_keep=n)
             nxt = p[c * S + 1:c * S + 1 + n]
             self.m_tok.copy_(torch.tensor(nxt + [0] * (S - len(nxt)), dtype=torch.int32))
