@@ -79,6 +79,9 @@ class MTPDecoder:
         # activations
         H = a.hidden
         self.h, self.xn, self.hn = z(S, H), z(S, H), z(S, H)
+        self.lasth = z(1, H)   # last hidden row of a kept prompt prefix (its MTP pair is still owed)
+        self.prefix = None     # kept prompt-prefix state (prefill(prefix_len=...))
+        self.cached_tokens = 0
         self.proj = z(S, max(a.gdn_proj, a.attn_proj))
         self.ygdn = z(S, a.lin_hv, a.lin_dv, dtype=f32)
         self.gdn_out = z(S, a.lin_hv * a.lin_dv)
@@ -319,32 +322,84 @@ class MTPDecoder:
             self.win[i].zero_()
             self.ring[i][0].zero_()
 
-    def prefill(self, prompt_ids) -> int:
-        """Runs the prompt (mtp.py:258-263) in chunks of k+1 and leaves [t, d1..dk] in tokens_in."""
+    def prefill(self, prompt_ids, prefix_len: int = 0) -> int:
+        """Runs the prompt (mtp.py:258-263) in chunks of k+1 and leaves [t, d1..dk] in tokens_in.
+
+        prefix_len (engine.py:52-88, 160-172): the first prefix_len tokens are a reusable prefix, e.g.
+        the conversation so far without the generation prompt.  The state after them is kept on the
+        device (GatedDeltaNet state and conv window, control block, the last hidden row; the KV caches
+        only grow, so their entries before the prefix stay valid), and a later prompt that starts with
+        the same tokens resumes from it instead of running them again.  A prompt that does not share
+        the kept prefix drops it.  The prompt after the prefix is never empty."""
         p = [int(x) for x in prompt_ids]
+        if not p:
+            raise ValueError("empty prompt")
+        prefix_len = max(0, min(int(prefix_len), len(p) - 1))
+        snap = self.prefix
+        if snap is not None and len(snap["ids"]) <= prefix_len and p[:len(snap["ids"])] == snap["ids"]:
+            self._restore_prefix(snap)
+            start, pending = len(snap["ids"]), True
+        else:
+            self.prefix = None
+            self.reset()
+            start, pending = 0, False
+        self.cached_tokens = start
+        if prefix_len > start:
+            self._prefill_part(p[start:prefix_len], pending, final=False)
+            self._take_prefix(p[:prefix_len])
+            start, pending = prefix_len, True
+        return self._prefill_part(p[start:], pending, final=True)
+
+    def _prefill_part(self, toks, pending: bool, final: bool):
+        """Prompt tokens appended to the current state.  pending: the MTP pair (last hidden row of the
+        previous part, first token of this one) is still owed.  A non-final part leaves the pair of its
+        last row pending (its next token is not known yet) and keeps that row in self.lasth."""
         S = self.S
-        self.reset()
-        n_chunks = (len(p) + S - 1) // S
+        if pending:
+            self.m_tok[0:1].fill_(toks[0])
+            self.mtp_step(self.lasth, None, self.m_tok.data_ptr(), 1, None, self.drafts.data_ptr(), with_draft=False)
+            self.ctrl[C["MPOS"]] += 1
+        n_chunks = (len(toks) + S - 1) // S
         for c in range(n_chunks):
-            chunk = p[c * S:(c + 1) * S]
+            chunk = toks[c * S:(c + 1) * S]
             n = len(chunk)
             self.tokens_in.copy_(torch.tensor(chunk + [0] * (S - n), dtype=torch.int32))
             self.backbone()
             last = c == n_chunks - 1
-            if last:
+            if last and final:
                 self._norm_head_rows()
                 if self.sp is not None:  # the first token is drawn from the last prompt row (engine.py:110-115)
                     self._sample(first_row=n - 1)
             self._accept(forced_keep=n)
-            nxt = p[c * S + 1:c * S + 1 + n]
+            nxt = toks[c * S + 1:c * S + 1 + n]
             self.m_tok.copy_(torch.tensor(nxt + [0] * (S - len(nxt)), dtype=torch.int32))
-            if last:  # the pair of the last prompt position is (h, t): t is the verify argmax of that row
+            if last and final:  # the pair of the last prompt position is (h, t): t is the verify argmax of that row
                 self.m_tok[n - 1:n].copy_(self.a_tok[n - 1:n])
                 self._draft_chain(self.h, self.m_tok.data_ptr())
+            elif last:
+                if n > 1:
+                    self.mtp_step(self.h, None, self.m_tok.data_ptr(), n - 1, None, self.drafts.data_ptr(),
+                                  with_draft=False)
+                    self.ctrl[C["MPOS"]] += n - 1
+                self.lasth.copy_(self.h[n - 1:n])
             else:
                 self.mtp_step(self.h, None, self.m_tok.data_ptr(), S, None, self.drafts.data_ptr(), with_draft=False)
                 self._chk(self.L.qmtp_mtp_advance(self.ctrl.data_ptr(), self._st()), "advance")
-        return int(self.tokens_in[0].item())
+        return int(self.tokens_in[0].item()) if final else None
+
+    def _take_prefix(self, ids):
+        cur = int(self.ctrl[C["SLOT"]].item())
+        self.prefix = {"ids": list(ids), "ctrl": self.ctrl.clone(), "lasth": self.lasth.clone(),
+                       "state": {i: self.ring[i][cur].clone() for i in self.lin_ids},
+                       "win": {i: self.win[i].clone() for i in self.lin_ids}}
+
+    def _restore_prefix(self, snap):
+        self.ctrl.copy_(snap["ctrl"])
+        cur = int(snap["ctrl"][C["SLOT"]].item())
+        for i in self.lin_ids:
+            self.ring[i][cur].copy_(snap["state"][i])
+            self.win[i].copy_(snap["win"][i])
+        self.lasth.copy_(snap["lasth"])
 
     def _norm_head_rows(self):
         self._head()
@@ -372,11 +427,13 @@ class MTPDecoder:
         return h[C["EMIT0"]:C["EMIT0"] + keep]
 
 
-def generate_mtp(dec: MTPDecoder, prompt_ids, max_tokens, eos=(), use_graph=True, draft_override=None):
+def generate_mtp(dec: MTPDecoder, prompt_ids, max_tokens, eos=(), use_graph=True, draft_override=None,
+                 prefix_len=0):
     """mtp.py:241-303 (greedy, k fixed): returns (tokens, stats).  tok/s excludes the prefill, as the
     reference does (mtp.py:264,295).  draft_override(cycle) -> k tokens or None replaces the drafts a
-    cycle verifies (test hook for the acceptance / rollback paths)."""
-    t = dec.prefill(prompt_ids)
+    cycle verifies (test hook for the acceptance / rollback paths).  prefix_len: see MTPDecoder.prefill
+    (stats["cached_tokens"] = prompt tokens resumed from the kept prefix)."""
+    t = dec.prefill(prompt_ids, prefix_len)
     if use_graph and dec.graph is None:
         # capture needs the library's one-time kernel setup done: warm up on a scratch copy of state
         snap = _snapshot(dec)
@@ -406,7 +463,7 @@ def generate_mtp(dec: MTPDecoder, prompt_ids, max_tokens, eos=(), use_graph=True
     acc = [ctrl[C["ACC0"] + i] for i in range(k)]
     stats = {"tps": (len(out) - 1) / dt if dt > 0 else 0.0, "tok_ciclo": (len(out) - 1) / max(cycles, 1),
              "acept": [n / max(cycles, 1) for n in acc], "borradores_ciclo": float(k), "cycles": cycles,
-             "seconds": dt}
+             "seconds": dt, "cached_tokens": dec.cached_tokens}
     return out, stats
 
 
