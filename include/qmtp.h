@@ -102,6 +102,11 @@ int qmtp_qmv_ex(const qmtp_qmv_args* args, void* stream);
 int qmtp_qmv_nvfp4_g16(const void* x, const void* w, const void* scales, void* y, int M, int N,
                        int K, int ldy, void* stream);
 
+/* qmtp_qmv_nvfp4_g16 with a residual epilogue, y = bf16(res + bf16(x . W^T)) (res [M, ldy], may be y):
+ * the decoder's o_proj / out_proj / down projections of an NVFP4 checkpoint. */
+int qmtp_qmv_nvfp4_g16_res(const void* x, const void* w, const void* scales, void* y, const void* res, int M,
+                           int N, int K, int ldy, void* stream);
+
 /* qmtp_qmv_affine_g64 with a residual epilogue: y = bf16(res + bf16(x . W^T)) (the bf16 residual
  * add of a decoder layer fused into the projection; res may alias y).  res bf16 [M, ldy]. */
 int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void* scales, const void* biases,
@@ -231,6 +236,11 @@ int qmtp_argmax_bf16(const void* vals, int ld, int M, int V, int* out, void* wor
 /* Quantized embedding gather (affine g64 rows): out[t] = bf16(fma(s, q, b)) of row tokens[t]. */
 int qmtp_embed(const int* tokens, int T, const void* wq, const void* scales, const void* biases, int V,
                int D, void* out, int ld_out, void* stream);
+
+/* Quantized embedding gather, NVFP4 rows (the embed_tokens of an NVFP4 checkpoint, qwen_ollama.py:50-51):
+ * out[t][e] = bf16(e2m1(q) * e4m3(scale of 16)); wq uint32 [V, D/8], scales uint8 [V, D/16]. */
+int qmtp_embed_nvfp4(const int* tokens, int T, const void* wq, const void* scales, int V, int D, void* out,
+                     int ld_out, void* stream);
 
 /* RMSNorm (mx.fast.rms_norm): out = bf16(w * bf16(x * r)), r = 1/sqrt(mean(x^2) + eps), D % 1024 == 0.
  * Row m reads x row (*row_sel + m) when row_sel != NULL. */

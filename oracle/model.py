@@ -91,9 +91,17 @@ def rmsnorm(x, w, eps):
     return out.reshape(x.shape)
 
 
-def embed(tokens, wq, s, b, D):
+def embed(tokens, *lin_and_d):
+    """embed(tokens, wq, s, b, D) for an affine-g64 table, embed(tokens, wq, s, D) for NVFP4."""
+    D = lin_and_d[-1]
     tok = _c(tokens, np.int32).ravel()
     out = np.empty((tok.size, D), np.uint16)
+    if len(lin_and_d) == 3:
+        wq, s = lin_and_d[:2]
+        ops.lib().qo_embed_nvfp4(_P(tok.ctypes.data), _I(tok.size), _P(_c(wq, np.uint32).ctypes.data),
+                                 _P(_c(s, np.uint8).ctypes.data), _I(D), _P(out.ctypes.data))
+        return out
+    wq, s, b = lin_and_d[:3]
     ops.lib().qo_embed(_P(tok.ctypes.data), _I(tok.size), _P(_c(wq, np.uint32).ctypes.data),
                        _P(_c(s, np.uint16).ctypes.data), _P(_c(b, np.uint16).ctypes.data), _I(D),
                        _P(out.ctypes.data))
@@ -108,6 +116,9 @@ def add(a, b):
 
 
 def qmv(x, lin):
+    """lin = (wq, scales, biases) affine g64, or (wq, scales) NVFP4 g16."""
+    if len(lin) == 2:
+        return ops.qmv_nvfp4(x, lin[0], lin[1])
     return ops.qmv_affine(x, lin[0], lin[1], lin[2])
 
 

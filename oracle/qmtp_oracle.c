@@ -685,6 +685,17 @@ QO_API void qo_embed(const int32_t* tok, int T, const uint32_t* wq, const uint16
   }
 }
 
+/* NVFP4 embedding rows: bf16(e2m1(q) * e4m3(scale)), the product exact in fp32. */
+QO_API void qo_embed_nvfp4(const int32_t* tok, int T, const uint32_t* wq, const uint8_t* sc, int D, uint16_t* out) {
+  for (int t = 0; t < T; ++t) {
+    size_t r = (size_t)tok[t];
+    for (int e = 0; e < D; ++e) {
+      uint32_t q = (wq[(r * D + e) / 8] >> (4 * (e % 8))) & 15u;
+      out[(size_t)t * D + e] = qo_f2bf(qo_e2m1(q) * qo_e4m3(sc[r * (D / 16) + e / 16]));
+    }
+  }
+}
+
 /* Gated attention input prep (hf:modeling_qwen3_5.py:647-668 structure; MLX-style rounding):
  * for token s of the S rows of qkv (row stride ld): q heads [nq][2*Dh] (query then gate),
  * k [nkv][Dh], v [nkv][Dh] after the q part.  q, k: per-head RMS norm (head tree) with weights

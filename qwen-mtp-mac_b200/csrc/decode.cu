@@ -41,6 +41,41 @@ __global__ void embed_kernel(const int32_t* __restrict__ tok, const uint32_t* __
   }
 }
 
+// NVFP4 rows: out = bf16(e2m1(q) * e4m3(scale of 16)), the product exact in fp32 (2 x 4 significant bits);
+// e4m3 is read as in qmv_kernel.py:26-28 (sign ignored; exponent 15 with mantissa 7 is 480).
+__device__ __forceinline__ float e4m3_unsigned(uint32_t s) {
+  const uint32_t e = (s >> 3) & 15u, m = s & 7u;
+  if (e == 0) return __fmul_rn(float(m), 0.001953125f);
+  return __uint_as_float((e + 120u) << 23 | (m << 20));
+}
+__global__ void embed_nvfp4_kernel(const int32_t* __restrict__ tok, const uint32_t* __restrict__ wq,
+                                   const uint8_t* __restrict__ sc, int D, uint16_t* __restrict__ out,
+                                   long long ld_out, int V, unsigned* err) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int r = tok[t];
+  if (r < 0 || r >= V) {
+    if (threadIdx.x == 0) atomicOr(err, DEVERR_BADARG);
+    return;
+  }
+  for (int w = threadIdx.x; w < D / 8; w += blockDim.x) {
+    const uint32_t word = wq[size_t(r) * (D / 8) + w];
+    const float s = e4m3_unsigned(sc[size_t(r) * (D / 16) + w / 2]);
+    uint16_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t q = (word >> (4 * j)) & 15u;
+      const uint32_t mg = q & 7u;  // e2m1 magnitude: 0, .5, 1, 1.5, 2, 3, 4, 6
+      const float v = mg < 2u ? 0.5f * float(mg) : __uint_as_float((((mg >> 1) + 126u) << 23) | ((mg & 1u) << 22));
+      o[j] = f2bf(__fmul_rn(q & 8u ? -v : v, s));
+    }
+    *reinterpret_cast<uint4*>(out + t * ld_out + 8 * w) =
+        make_uint4(o[0] | (uint32_t(o[1]) << 16), o[2] | (uint32_t(o[3]) << 16), o[4] | (uint32_t(o[5]) << 16),
+                   o[6] | (uint32_t(o[7]) << 16));
+  }
+}
+
 // ----------------------------------------------------------------------------- RMSNorm
 // Wide tree: blockDim = D/32 threads, thread c owns elements [32c, 32c+32).
 __global__ void rmsnorm_wide_kernel(const uint16_t* __restrict__ x, long long ld_x, const int* __restrict__ row_sel,
@@ -404,6 +439,18 @@ extern "C" int qmtp_embed(const int* tokens, int T, const void* wq, const void* 
   launch_kernel(embed_kernel, dim3(T), dim3(threads), 0, static_cast<cudaStream_t>(stream), 
       tokens, static_cast<const uint32_t*>(wq), static_cast<const uint16_t*>(scales),
       static_cast<const uint16_t*>(biases), D, static_cast<uint16_t*>(out), ld_out, V, device_error_ptr());
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_embed_nvfp4(const int* tokens, int T, const void* wq, const void* scales, int V, int D, void* out,
+                                int ld_out, void* stream) {
+  if (!tokens || !wq || !scales || !out) return QMTP_ERR_ARG;
+  if (T < 1 || D % 64 != 0 || ld_out < D || ld_out % 8 != 0) return QMTP_ERR_SHAPE;
+  if (!aligned16(out)) return QMTP_ERR_ALIGN;
+  const int threads = std::min(1024, std::max(32, ((D / 8 + 31) / 32) * 32));
+  launch_kernel(embed_nvfp4_kernel, dim3(T), dim3(threads), 0, static_cast<cudaStream_t>(stream), tokens,
+                static_cast<const uint32_t*>(wq), static_cast<const uint8_t*>(scales), D,
+                static_cast<uint16_t*>(out), ld_out, V, device_error_ptr());
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 

@@ -691,6 +691,11 @@ extern "C" int qmtp_qmv_nvfp4_g16(const void* x, const void* w, const void* scal
   return qmv_entry<FMT_NVFP4>(x, w, scales, nullptr, y, nullptr, M, N, K, ldy, stream);
 }
 
+extern "C" int qmtp_qmv_nvfp4_g16_res(const void* x, const void* w, const void* scales, void* y, const void* res,
+                                      int M, int N, int K, int ldy, void* stream) {
+  return qmv_entry<FMT_NVFP4>(x, w, scales, nullptr, y, res, M, N, K, ldy, stream);
+}
+
 extern "C" int qmtp_qmv_launch_info(int fmt, int M, int K, int* ctas_per_sm, int* threads, int* smem_bytes,
                                     int* rows_per_tile) {
   if (!ctas_per_sm || !threads || !smem_bytes || !rows_per_tile) return QMTP_ERR_ARG;

@@ -79,6 +79,8 @@ SIGNATURES.update({
     "qmtp_qmv_affine_g64_res": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_lmhead2_noalloc": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P],
     "qmtp_embed": [_P, _I, _P, _P, _P, _I, _I, _P, _I, _P],
+    "qmtp_embed_nvfp4": [_P, _I, _P, _P, _I, _I, _P, _I, _P],
+    "qmtp_qmv_nvfp4_g16_res": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_rmsnorm": [_P, _I, _P, _P, _F, _P, _I, _I, _I, _P],
     "qmtp_attn_prep": [_P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P],
     "qmtp_attention": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P, _P],

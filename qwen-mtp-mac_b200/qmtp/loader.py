@@ -11,12 +11,12 @@ What the reference does at load time, restated for this engine's weight layout:
   zero-centred RMSNorms store ``w - 1``; every 1-D MTP tensor gets ``+ 1`` (``load_mtp_tensors``).
 * ``mtp.py:35-57`` / mlx-lm ``qwen3_5``: the module names of the trunk and of the MTP layer.
 
-The decoder serves 4-bit affine group-64 linears (the MLX ``quantize(w, 64, 4)`` format: uint32
-words of 8 nibbles, bf16 scales and biases per 64 inputs).  A checkpoint linear that is already in
-that format is used as stored; a bf16 linear is quantized on the GPU at load time (the reference
-quantizes the MTP head the same way, ``mtp.py:67-68``).  Linears in another quantized format
-(NVFP4 ``uint8`` scales without biases, other group sizes) are rejected with an error: this
-decoder's projections run the affine kernel only.
+The decoder serves two 4-bit linear formats: affine group 64 (the MLX ``quantize(w, 64, 4)``
+format: uint32 words of 8 nibbles, bf16 scales and biases per 64 inputs) and NVFP4 (the same nibble
+words holding e2m1 values, one e4m3 ``uint8`` scale per 16 inputs, no biases; the format of the Ollama
+``qwen3.5:9b-mlx`` blobs, qwen_ollama.py:20).  A checkpoint linear in either format is used as stored;
+a bf16 linear is quantized to affine g64 on the GPU at load time (the reference quantizes the MTP head
+at load too, ``mtp.py:67-68``).  Other quantized formats are rejected with an error.
 
 Projections that read the same input are concatenated along the output rows, as ``qmtp.model``
 documents: GatedDeltaNet ``[in_proj_qkv | in_proj_z | in_proj_b | in_proj_a]``, attention
@@ -165,7 +165,7 @@ def _bf16_array(v: np.ndarray, name: str) -> np.ndarray:
 
 
 def _linear(t: dict, name: str, n: int, k: int):
-    """(wq, scales, biases) for an affine-g64 linear, or Bf16Linear for a bf16 one."""
+    """(wq, scales, biases) for an affine-g64 linear, (wq, scales) for an NVFP4 one, or Bf16Linear."""
     w = t.get(name + ".weight")
     if w is None:
         raise KeyError(f"missing tensor {name}.weight")
@@ -175,10 +175,14 @@ def _linear(t: dict, name: str, n: int, k: int):
         if w.shape != (n, k):
             raise ValueError(f"{name}.weight: shape {w.shape}, expected {(n, k)}")
         return Bf16Linear(w)
-    if b is None or s.dtype != np.uint16 or b.dtype != np.uint16:
-        raise NotImplementedError(f"{name}: quantized with a format other than affine 4-bit group 64 "
-                                  "(e.g. NVFP4); this decoder's projections run the affine kernel")
     w = w.view(np.uint32) if w.dtype in (np.int32, np.uint32) else None
+    if b is None and s.dtype == np.uint8 and s.shape == (n, k // 16):
+        if w is None or w.shape != (n, k // 8):
+            raise ValueError(f"{name}: NVFP4 nibbles must be uint32 [{n}, {k // 8}]")
+        return (w, s)
+    if b is None or s.dtype != np.uint16 or b.dtype != np.uint16:
+        raise NotImplementedError(f"{name}: quantized with a format other than affine 4-bit group 64 or "
+                                  "NVFP4 group 16")
     if w is None or w.shape != (n, k // 8) or s.shape != (n, k // 64) or b.shape != (n, k // 64):
         raise ValueError(f"{name}: affine g64 tensors must be uint32 [{n}, {k // 8}] and bf16 [{n}, {k // 64}]")
     return (w, s, b)
@@ -186,11 +190,11 @@ def _linear(t: dict, name: str, n: int, k: int):
 
 def _concat(parts, name):
     """Row-wise concatenation of linears of one input (all quantized or all bf16)."""
-    if all(isinstance(p, tuple) for p in parts):
-        return tuple(np.concatenate([p[i] for p in parts], axis=0) for i in range(3))
+    if all(isinstance(p, tuple) for p in parts) and len({len(p) for p in parts}) == 1:
+        return tuple(np.concatenate([p[i] for p in parts], axis=0) for i in range(len(parts[0])))
     if all(isinstance(p, Bf16Linear) for p in parts):
         return Bf16Linear(np.concatenate([p.w for p in parts], axis=0))
-    raise NotImplementedError(f"{name}: mixed bf16 and quantized projections of one input")
+    raise NotImplementedError(f"{name}: projections of one input in different formats")
 
 
 def _vec(t: dict, name: str, n: int, plus_one: bool = False, dtype=np.uint16) -> np.ndarray:
@@ -284,7 +288,8 @@ def trunk_layout(tensors: dict, a: ModelArgs, hf_norms: bool = False) -> dict:
 
 
 def load_mtp_tensors(tensors: dict) -> dict:
-    """mtp.py:61-66: ``mtp.*`` tensors with the prefix removed and ``+ 1`` on every 1-D tensor."""
+    """mtp.py:61-66: ``mtp.*`` tensors with the prefix removed and ``+ 1`` on every 1-D tensor
+    (``.weight.scale`` is renamed ``.scales`` as for the trunk)."""
     out = {}
     for k, v in tensors.items():
         if not k.startswith("mtp."):
@@ -292,7 +297,7 @@ def load_mtp_tensors(tensors: dict) -> dict:
         v = np.asarray(v)
         if v.ndim == 1:
             v = _bf16_add_one(_bf16_array(v, k))
-        out[k[len("mtp."):]] = v
+        out[k[len("mtp."):].replace(".weight.scale", ".scales")] = v
     if not out:
         raise KeyError("no mtp.* tensors")
     return out

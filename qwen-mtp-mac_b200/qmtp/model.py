@@ -146,6 +146,8 @@ def from_numpy(Wn: dict, device="cuda") -> Weights:
     def conv(v):
         if isinstance(v, dict):
             return {k: conv(x) for k, x in v.items()}
+        if isinstance(v, tuple) and len(v) == 2:  # NVFP4: (uint32 nibbles, uint8 e4m3 scales per 16)
+            return QuantizedLinear(t(v[0]), t(v[1]), None, group_size=16, mode="nvfp4")
         if isinstance(v, tuple):
             return QuantizedLinear(*(t(x) for x in v))
         return t(v)
@@ -168,6 +170,8 @@ def to_numpy(W: dict) -> dict:
         if isinstance(v, dict):
             return {k: conv(x) for k, x in v.items()}
         if isinstance(v, QuantizedLinear):
+            if v.mode == "nvfp4":
+                return (n(v.weight), n(v.scales))
             return (n(v.weight), n(v.scales), n(v.biases))
         return n(v)
 

@@ -131,13 +131,33 @@ class MTPDecoder:
         if rc != 0:
             _lib.check(rc, what)
 
+    def _embed(self, tok, rows, out):
+        """Embedding rows of device token ids (affine g64 or NVFP4 table) into out [rows, hidden]."""
+        a, E = self.a, self.W["embed"]
+        if E.mode == "nvfp4":
+            rc = self.L.qmtp_embed_nvfp4(tok, rows, E.weight.data_ptr(), E.scales.data_ptr(), a.vocab, a.hidden,
+                                         out.data_ptr(), a.hidden, self._st())
+        else:
+            rc = self.L.qmtp_embed(tok, rows, E.weight.data_ptr(), E.scales.data_ptr(), E.biases.data_ptr(), a.vocab,
+                                   a.hidden, out.data_ptr(), a.hidden, self._st())
+        self._chk(rc, "embed")
+
     def _qmv(self, x, lin, y, M, res=None, ldy=None, pre_w=None):
         """4-bit GEMV y = x . W^T (+ res), one qmtp_qmv_ex launch per 4 rows; with pre_w, x is first
-        RMS-normalised with that weight (the decoder's fused norm)."""
+        RMS-normalised with that weight (the decoder's fused norm).  NVFP4 layers (an NVFP4 checkpoint)
+        run qmtp_qmv_nvfp4_g16_res."""
         N, K = lin.out_features, lin.in_features
         ldy = ldy or N
         if self.qmv_log is not None:
             self.qmv_log.append((x, lin, y, M, res, ldy, pre_w))
+        if lin.mode == "nvfp4":
+            if pre_w is not None:
+                raise NotImplementedError("fuse_norm runs the affine kernel's prologue; NVFP4 layers have none")
+            self.launches += (M + 3) // 4
+            self._chk(self.L.qmtp_qmv_nvfp4_g16_res(x.data_ptr(), lin.weight.data_ptr(), lin.scales.data_ptr(),
+                                                    y.data_ptr(), res.data_ptr() if res is not None else None,
+                                                    M, N, K, ldy, self._st()), "qmv")
+            return
         self.launches += (M + 3) // 4
         if self.prof is not None:
             e0 = torch.cuda.Event(enable_timing=True)
@@ -207,10 +227,7 @@ class MTPDecoder:
     def backbone(self):
         """mtp.py:143-153 on the k+1 verify tokens in self.tokens_in: h (pre-norm) and hn (post-norm)."""
         a, W, S = self.a, self.W, self.S
-        E = W["embed"]
-        self._chk(self.L.qmtp_embed(self.tokens_in.data_ptr(), S, E.weight.data_ptr(), E.scales.data_ptr(),
-                                    E.biases.data_ptr(), a.vocab, a.hidden, self.h.data_ptr(), a.hidden,
-                                    self._st()), "embed")
+        self._embed(self.tokens_in.data_ptr(), S, self.h)
         for i in range(a.layers):
             L = W[f"layers.{i}"]
             if self.fuse_norm:
@@ -249,9 +266,7 @@ class MTPDecoder:
         draft_out (DraftHead.token = argmax of the full-vocab 4-bit head, mtp.py:165-167)."""
         a, M = self.a, self.W["mtp"]
         H = a.hidden
-        E = self.W["embed"]
-        self._chk(self.L.qmtp_embed(tok, rows, E.weight.data_ptr(), E.scales.data_ptr(), E.biases.data_ptr(),
-                                    a.vocab, H, self.memb.data_ptr(), H, self._st()), "embed")
+        self._embed(tok, rows, self.memb)
         self._norm(self.memb, M["pre_fc_norm_embedding"], self.mcat, rows, ld_o=2 * H)
         self._chk(self.L.qmtp_rmsnorm(hidden.data_ptr(), H, hidden_sel, M["pre_fc_norm_hidden"].data_ptr(), a.eps,
                                       self.mcat.data_ptr() + 2 * H, 2 * H, rows, H, self._st()), "rmsnorm")

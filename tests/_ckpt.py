@@ -23,7 +23,7 @@ def minus_one(w):
     return ops.f32_to_bf16(f.astype(np.float32))
 
 
-def checkpoint(Wn, a, hf_norms=True, prefix="model.language_model."):
+def checkpoint(Wn, a, hf_norms=True, prefix="model.language_model.", scale_suffix=".scales"):
     """(trunk tensors, mtp tensors, names of bf16 tensors).  Quantized linears keep their triples
     (``.weight`` uint32, ``.scales`` / ``.biases`` bf16); the MTP tensors carry raw-HF norms (w - 1)."""
     T, M, bf = {}, {}, set()
@@ -34,8 +34,12 @@ def checkpoint(Wn, a, hf_norms=True, prefix="model.language_model."):
             bf.add(name)
 
     def lin(d, name, trip, r0=None, r1=None):
-        w, s, b = trip
         sl = slice(r0, r1)
+        if len(trip) == 2:  # NVFP4 (Ollama blobs name the scales ".weight.scale")
+            put(d, name + ".weight", trip[0][sl], False)
+            put(d, name + (".weight.scale" if scale_suffix != ".scales" else ".scales"), trip[1][sl], False)
+            return
+        w, s, b = trip
         put(d, name + ".weight", w[sl], False)
         put(d, name + ".scales", s[sl], True)
         put(d, name + ".biases", b[sl], True)
@@ -86,3 +90,24 @@ def checkpoint(Wn, a, hf_norms=True, prefix="model.language_model."):
     lin(M, "mtp.fc", m["fc"])
     block(M, "mtp.layers.0.", m["layer"], True)
     return T, M, bf
+
+
+def dequant(trip):
+    """bf16 bits of s * q + b for an affine-g64 triple (the dense weight a bf16 checkpoint holds)."""
+    wq, s, b = trip
+    n, k8 = wq.shape
+    q = ((wq[:, :, None] >> (4 * np.arange(8, dtype=np.uint32))) & 15).reshape(n, 8 * k8).astype(np.float32)
+    sf = np.repeat(ops.bf16_to_f32(s), 64, axis=1)
+    bf = np.repeat(ops.bf16_to_f32(b), 64, axis=1)
+    return ops.f32_to_bf16((sf * q + bf).astype(np.float32))
+
+
+def to_nvfp4(Wn):
+    """The oracle weights with every linear except the lm_head copies re-quantized to NVFP4 g16."""
+    def conv(k, v):
+        if isinstance(v, dict):
+            return {kk: conv(kk, x) for kk, x in v.items()}
+        if isinstance(v, tuple) and k != "lm_head_q":
+            return ops.quantize_fp4(dequant(v), "nvfp4")
+        return v
+    return {k: conv(k, v) for k, v in Wn.items()}

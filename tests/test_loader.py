@@ -92,7 +92,7 @@ def _eq(got, want, path="W"):
         for k in want:
             _eq(got[k], want[k], f"{path}.{k}")
     elif isinstance(want, tuple):
-        assert isinstance(got, tuple) and len(got) == 3, path
+        assert isinstance(got, tuple) and len(got) == len(want), path
         for g, w in zip(got, want):
             assert g.dtype == w.dtype and np.array_equal(g, w), path
     else:
@@ -137,10 +137,27 @@ def test_rejects_other_quantized_formats(small_weights):
     T, _, _ = _ckpt.checkpoint(small_weights, a)
     T = L.sanitize_names(T)
     n = "layers.0.mlp.down_proj"
-    T[n + ".scales"] = np.zeros((a.hidden, a.intermediate // 16), np.uint8)  # NVFP4: e4m3 bytes, no biases
+    T[n + ".scales"] = np.zeros((a.hidden, a.intermediate // 32), np.uint8)  # MXFP4-shaped scales: not served
     del T[n + ".biases"]
     with pytest.raises(NotImplementedError):
         L.trunk_layout(T, L.args_from_config(_ckpt.config_dict(a)))
+
+
+def test_nvfp4_checkpoint_layout(tmp_path, small_weights):
+    """An NVFP4 checkpoint (Ollama scale names) reassembles into (nibbles, scales) pairs."""
+    L = _loader()
+    a = om.SMALL
+    Wq = _ckpt.to_nvfp4(small_weights)
+    T, M, bf = _ckpt.checkpoint(Wq, a, scale_suffix=".weight.scale")
+    assert any(k.endswith(".weight.scale") for k in T)
+    L.write_safetensors(tmp_path / "t.safetensors", T, bf16=[k for k in T if k in bf])
+    args = L.args_from_config(_ckpt.config_dict(a))
+    W = L.trunk_layout(L.sanitize_names(L.read_safetensors(tmp_path / "t.safetensors")), args, hf_norms=True)
+    W["mtp"] = L.mtp_layout(L.load_mtp_tensors(M), args)
+    del W["lm_head_q"]
+    want = dict(Wq)
+    del want["lm_head_q"]
+    _eq(W, want)
 
 
 def test_ollama_manifest(tmp_path):
@@ -162,3 +179,16 @@ def test_ollama_manifest(tmp_path):
     c, tensors, jsons = L.ollama_checkpoint("9b-mlx", root)
     assert c == cfg and len(tensors) == 2 and set(jsons) == {"config.json", "tok.json"}
     assert all(p.read_text() in ("x", "y") for p in tensors)
+
+
+def test_oracle_nvfp4_embedding():
+    """qo_embed_nvfp4 = bf16(e2m1(q) * e4m3(s)) with the reference's decoders (qmv_kernel.py:16-29)."""
+    r = np.random.default_rng(9)
+    V, D = 50, 128
+    wq = r.integers(0, 2 ** 32, (V, D // 8), dtype=np.uint64).astype(np.uint32)
+    sc = r.integers(0, 256, (V, D // 16), dtype=np.int64).astype(np.uint8)
+    tok = np.int32([3, 0, 49, 3])
+    e2m1, e4m3, _ = ops.decode_tables()
+    q = ((wq[:, :, None] >> (4 * np.arange(8, dtype=np.uint32))) & 15).reshape(V, D)
+    want = ops.f32_to_bf16((e2m1[q] * np.repeat(e4m3[sc], 16, axis=1)).astype(np.float32))[tok]
+    assert np.array_equal(om.embed(tok, wq, sc, D), want)
