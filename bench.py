@@ -137,7 +137,7 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     cfg = qm.ModelArgs(max_pos=2048)
     t_build = time.time()
-    W = qm.synthetic_weights(cfg, seed=0, device=dev)
+    W = qm.synthetic_weights(cfg, seed=0, device=dev, fmt=args.weights)
     torch.cuda.synchronize()
     t_build = time.time() - t_build
     rng = np.random.default_rng(1000 + rank)
@@ -238,7 +238,8 @@ def run_ours(args):
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "traffic": None if ratio is None else round(ratio * qbytes / len(prof)),
-                "kernel": "qmv_affine_g64 (all 4-bit projections + coarse head of a cycle)",
+                "kernel": ("qmv_affine_g64" if args.weights == "affine" else "qmv_nvfp4_g16 (trunk) + qmv_affine_g64 (coarse head)")
+                          + " (all 4-bit projections + coarse head of a cycle)",
                 "bytes_per_cycle": qbytes, "qmv_ms_per_cycle": round(qmv_ms_cycle, 4),
                 "launches_per_cycle": len(prof),
                 "timing": "the cycle's projections alone in a CUDA graph, back-to-back replays"}
@@ -247,7 +248,8 @@ def run_ours(args):
            "ms_per_step": round(elapsed_ms / K, 4), "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
            "config": {"workload": "config4: synthetic Qwen3.5-9B-shaped hybrid decoder (32 layers, 3:1 GDN:attention, "
-                                  "4-bit affine g64), 1-layer MTP head, "
+                                  + ("4-bit affine g64" if args.weights == "affine" else "4-bit NVFP4 g16")
+                                  + "), 1-layer MTP head, "
                                   + ("greedy" if sp is None else "exact speculative sampling")
                                   + f" MTP decode k=2, batch 1, {args.prompt}-token uniform random prompt",
                       "step": "one verify cycle (verify 3 tokens + accept/rollback + 2 draft steps)",
@@ -552,6 +554,8 @@ def main():
     ap.add_argument("--cpu-cycles", type=int, default=3, help="oracle cycles for cpu_baseline (0 = skip)")
     ap.add_argument("--ref-prompt", type=int, default=16)
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens (ours)")
+    ap.add_argument("--weights", default="affine", choices=["affine", "nvfp4"],
+                    help="decode: 4-bit format of the linears (affine g64 = config 4; nvfp4 = the Ollama blobs' format)")
     ap.add_argument("--temperature", type=float, default=0.0,
                     help="> 0: exact speculative sampling instead of greedy (engine.py:91-152)")
     ap.add_argument("--top-k", type=int, default=0)

@@ -89,9 +89,11 @@ def _randn_bf16(shape, gen, std, device):
     return (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std).to(torch.bfloat16)
 
 
-def synthetic_weights(args: ModelArgs, seed: int = 0, std: float = 0.02, device="cuda") -> Weights:
+def synthetic_weights(args: ModelArgs, seed: int = 0, std: float = 0.02, device="cuda", fmt: str = "affine") -> Weights:
     """Random-init weights generated and quantized on the GPU (torch CUDA RNG, libqmtp quantizer).
-    Linear weights N(0, std); norm weights 1; conv N(0, 1/KC); A_log = log U(1, 16); dt_bias N(0, 1)."""
+    Linear weights N(0, std); norm weights 1; conv N(0, 1/KC); A_log = log U(1, 16); dt_bias N(0, 1).
+    fmt "nvfp4": the linears and the embedding in NVFP4 g16 (the Ollama checkpoint's format); the
+    lm_head stays bf16 with its affine g64 coarse copy."""
     device = torch.device(device)
     g = torch.Generator(device=device)
     g.manual_seed(seed)
@@ -100,7 +102,13 @@ def synthetic_weights(args: ModelArgs, seed: int = 0, std: float = 0.02, device=
 
     def lin(n, k):
         w = _randn_bf16((n, k), g, std, device)
-        q = QuantizedLinear.from_linear(w)
+        if fmt == "nvfp4":
+            from .moe import quantize as quantize_fp4
+
+            wq, sc = quantize_fp4(w[None], "nvfp4")
+            q = QuantizedLinear(wq[0], sc[0], None, group_size=16, mode="nvfp4")
+        else:
+            q = QuantizedLinear.from_linear(w)
         del w
         return q
 

@@ -150,32 +150,33 @@ class MTPDecoder:
         ldy = ldy or N
         if self.qmv_log is not None:
             self.qmv_log.append((x, lin, y, M, res, ldy, pre_w))
-        if lin.mode == "nvfp4":
-            if pre_w is not None:
-                raise NotImplementedError("fuse_norm runs the affine kernel's prologue; NVFP4 layers have none")
-            self.launches += (M + 3) // 4
-            self._chk(self.L.qmtp_qmv_nvfp4_g16_res(x.data_ptr(), lin.weight.data_ptr(), lin.scales.data_ptr(),
-                                                    y.data_ptr(), res.data_ptr() if res is not None else None,
-                                                    M, N, K, ldy, self._st()), "qmv")
-            return
+        nv = lin.mode == "nvfp4"
+        if nv and pre_w is not None:
+            raise NotImplementedError("fuse_norm runs the affine kernel's prologue; NVFP4 layers have none")
         self.launches += (M + 3) // 4
         if self.prof is not None:
             e0 = torch.cuda.Event(enable_timing=True)
             e0.record()
-        a = self._qa
-        a.x, a.ldx = x.data_ptr(), K
-        a.w, a.scales, a.biases = lin.weight.data_ptr(), lin.scales.data_ptr(), lin.biases.data_ptr()
-        a.y, a.res = y.data_ptr(), (res.data_ptr() if res is not None else None)
-        a.M, a.N, a.K, a.ldy = M, N, K, ldy
-        if pre_w is not None:
-            a.pre, a.pre_w, a.pre_eps = _lib.QMV_PRE_RMSNORM, pre_w.data_ptr(), self.a.eps
+        if nv:
+            self._chk(self.L.qmtp_qmv_nvfp4_g16_res(x.data_ptr(), lin.weight.data_ptr(), lin.scales.data_ptr(),
+                                                    y.data_ptr(), res.data_ptr() if res is not None else None,
+                                                    M, N, K, ldy, self._st()), "qmv")
         else:
-            a.pre, a.pre_w = _lib.QMV_PRE_NONE, None
-        self._chk(self.L.qmtp_qmv_ex(ctypes.byref(a), self._st()), "qmv")
+            a = self._qa
+            a.x, a.ldx = x.data_ptr(), K
+            a.w, a.scales, a.biases = lin.weight.data_ptr(), lin.scales.data_ptr(), lin.biases.data_ptr()
+            a.y, a.res = y.data_ptr(), (res.data_ptr() if res is not None else None)
+            a.M, a.N, a.K, a.ldy = M, N, K, ldy
+            if pre_w is not None:
+                a.pre, a.pre_w, a.pre_eps = _lib.QMV_PRE_RMSNORM, pre_w.data_ptr(), self.a.eps
+            else:
+                a.pre, a.pre_w = _lib.QMV_PRE_NONE, None
+            self._chk(self.L.qmtp_qmv_ex(ctypes.byref(a), self._st()), "qmv")
         if self.prof is not None:
             e1 = torch.cuda.Event(enable_timing=True)
             e1.record()
-            nbytes = N * K // 2 + N * (K // 64) * 4 + M * K * 2 + M * N * 2 * (2 if res is not None else 1)
+            scale_bytes = N * (K // 16) if nv else N * (K // 64) * 4
+            nbytes = N * K // 2 + scale_bytes + M * K * 2 + M * N * 2 * (2 if res is not None else 1)
             self.prof.append((nbytes, e0, e1, (M, N, K)))
 
     def _norm(self, x, w, out, M, ld_x=None, ld_o=None, row_sel=None):
