@@ -339,3 +339,18 @@ def sample(idx, fine, drafts, temperature, top_k=0, top_p=1.0, min_p=0.0, V=None
     if first_row >= 0:
         return int(out[0])
     return n, [int(v) for v in out[:n + 1]]
+
+
+def sample_dist(idx, fine, temperature, top_k=0, top_p=1.0, min_p=0.0, V=None):
+    """C qo_sample_dist: (kept vocabulary ids in order, their probabilities) of one candidate row."""
+    idx = np.ascontiguousarray(idx, np.int32).ravel()
+    fine = np.ascontiguousarray(fine, np.uint16).ravel()
+    K = idx.size
+    oi, op = np.empty(K, np.int32), np.empty(K, np.float32)
+    f = lib().qo_sample_dist
+    f.restype = ctypes.c_int
+    n = f(_p(idx), _p(fine), _I(K), ctypes.c_float(temperature), _I(top_k), ctypes.c_float(top_p),
+          ctypes.c_float(min_p), _I(V if V is not None else 1 << 30), _p(oi), _p(op))
+    if n < 0:
+        raise ValueError("qo_sample_dist: bad arguments")
+    return oi[:n], op[:n]

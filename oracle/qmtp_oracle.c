@@ -1132,3 +1132,14 @@ QO_API int qo_sample(const int32_t* idx, const uint16_t* fine, int K, int ld, co
   }
   return k;
 }
+
+/* Engine._dist of one row for tests: the kept candidates (sorted) and their probabilities; returns n. */
+QO_API int qo_sample_dist(const int32_t* idx, const uint16_t* fine, int K, float T, int top_k, float top_p,
+                          float min_p, int V, int32_t* out_idx, float* out_p) {
+  if (K < 1 || K > 2048 || !(T > 0.0f)) return -1;
+  qo_scand c[2048];
+  float p[2048];
+  const int n = qo_dist(idx, fine, K, T, top_k, top_p, min_p, V, c, p);
+  for (int j = 0; j < n; ++j) { out_idx[j] = c[j].i; out_p[j] = p[j]; }
+  return n;
+}

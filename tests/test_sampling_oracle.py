@@ -84,3 +84,26 @@ def test_sampling_is_deterministic_per_seed_and_counter():
     a = [ops.sample(idx, fine, d, seed=7, ctr=c, **kw) for c in range(50)]
     assert a == [ops.sample(idx, fine, d, seed=7, ctr=c, **kw) for c in range(50)]
     assert a != [ops.sample(idx, fine, d, seed=8, ctr=c, **kw) for c in range(50)]
+
+
+@pytest.mark.parametrize("sp", [dict(temperature=0.7, top_k=20, top_p=0.9), dict(temperature=1.0, top_p=0.5),
+                                dict(temperature=1.0, min_p=0.1)])
+def test_distribution_is_valid(sp):
+    """tests/test_kernels.py:129-139 of the reference on the restated Engine._dist (1000 candidates x 3
+    rows of N(0, 9) logits): probabilities sum to 1, top_k / top_p / min_p hold."""
+    rng = np.random.default_rng(7)
+    for row in range(3):
+        fine = ops.f32_to_bf16((rng.standard_normal(1000) * 3).astype(np.float32))
+        idx = np.arange(1000, dtype=np.int32)
+        kept, p = ops.sample_dist(idx, fine, V=1000, **sp)
+        assert abs(float(p.astype(np.float64).sum()) - 1.0) <= 1e-4
+        assert np.all(np.diff(p) <= 0)  # sorted by probability
+        if sp.get("top_k"):
+            assert len(kept) <= sp["top_k"]
+        if sp.get("min_p"):
+            assert float(p.min()) >= sp["min_p"] * float(p[0]) * (1 - 1e-5)
+        # the kept set and probabilities of an independent float64 restatement
+        lf = ops.bf16_to_f32(fine).astype(np.float64)
+        p64 = _dist64(lf, sp["temperature"], sp.get("top_k", 0), sp.get("top_p", 1.0), sp.get("min_p", 0.0))
+        assert set(kept.tolist()) == set(np.flatnonzero(p64 > 0).tolist())
+        assert np.allclose(p, p64[kept], rtol=1e-5, atol=1e-7)
