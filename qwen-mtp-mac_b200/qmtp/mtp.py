@@ -1,8 +1,9 @@
-"""Greedy MTP speculative decoding on B200 -- the mtp.py surface of qwen-mtp-mac.
+"""MTP speculative decoding on B200 -- the mtp.py / engine.py surface of qwen-mtp-mac.
 
 Reference: mtp.py:143-153 ``backbone``, mtp.py:199-209 ``mtp_step``, mtp.py:212-226 ``draft_chain``
-(chain="pre"), mtp.py:136-140 ``restore``, mtp.py:241-303 ``generate_mtp`` (greedy, fixed k,
-bb_hidden="pre") and the greedy branch of engine.py:121-128.
+(chain="pre"), mtp.py:136-140 ``restore``, mtp.py:241-303 ``generate_mtp`` (fixed k, bb_hidden="pre"),
+engine.py:121-128 (greedy verify), engine.py:91-152 (exact speculative sampling, ``Sampling``) and
+engine.py:52-88 (prompt-prefix state cache, ``prefill(prompt, prefix_len)``).
 
 B200 design.  Everything a cycle needs lives on the device: the GatedDeltaNet states in a ring of
 k+2 slots per layer (the state after each verify token is a slot, so ``restore`` is a slot index),
