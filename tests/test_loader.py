@@ -192,3 +192,38 @@ def test_oracle_nvfp4_embedding():
     q = ((wq[:, :, None] >> (4 * np.arange(8, dtype=np.uint32))) & 15).reshape(V, D)
     want = ops.f32_to_bf16((e2m1[q] * np.repeat(e4m3[sc], 16, axis=1)).astype(np.float32))[tok]
     assert np.array_equal(om.embed(tok, wq, sc, D), want)
+
+
+def test_loader_error_paths(small_weights):
+    """Missing or unusable tensors fail with a clear error instead of loading something else."""
+    L = _loader()
+    a = om.SMALL
+    args = L.args_from_config(_ckpt.config_dict(a))
+    T, _, _ = _ckpt.checkpoint(small_weights, a)
+    T = L.sanitize_names(T)
+    for mutate, exc in [(lambda t: t.pop("lm_head.weight"), KeyError),                  # tied embeddings
+                        (lambda t: t.update({"lm_head.scales": np.zeros(1, np.uint16)}), NotImplementedError),
+                        (lambda t: t.pop("layers.0.linear_attn.A_log"), KeyError),
+                        (lambda t: t.update({"layers.0.linear_attn.conv1d.weight": np.zeros((3, 4), np.uint16)}),
+                         ValueError),
+                        (lambda t: t.update({"layers.3.self_attn.k_proj.weight":
+                                             np.zeros((7, a.hidden // 8), np.uint32)}), ValueError)]:
+        t = dict(T)
+        mutate(t)
+        with pytest.raises(exc):
+            L.trunk_layout(t, args)
+
+
+def test_config_variants():
+    """Top-level config (no text_config), rope_scaling instead of rope_parameters, no layer_types."""
+    L = _loader()
+    from qmtp import model as qm
+
+    c = dict(_ckpt.config_dict(om.SMALL)["text_config"])
+    rope = c.pop("rope_parameters")
+    c.pop("layer_types")
+    c["rope_scaling"] = rope
+    assert L.args_from_config(c, max_pos=1024) == qm.SMALL
+    c.pop("rope_scaling")
+    c["rope_theta"], c["partial_rotary_factor"] = om.SMALL.rope_theta, 0.25
+    assert L.args_from_config(c, max_pos=1024) == qm.SMALL
