@@ -51,9 +51,9 @@ def _peaks():
     return 6650.0, "fallback"
 
 
-def _traffic_ratio():
+def _traffic_ratio(summary="qmv_affine_g64_inproj_M3.md"):
     """DRAM bytes / algorithmic bytes of the qmv kernel from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "qmv_affine_g64_inproj_M3.md"
+    p = ROOT / "profiles" / summary
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -234,7 +234,7 @@ def run_ours(args):
     peak, peak_kind = _peaks()
     qbytes = sum(b for b, _ in prof)
     achieved = qbytes / (qmv_ms_cycle / 1e3) / 1e9
-    ratio = _traffic_ratio()
+    ratio = _traffic_ratio("qmv_affine_g64_inproj_M3.md" if args.weights == "affine" else "qmv_nvfp4_g16_head_M1.md")
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "traffic": None if ratio is None else round(ratio * qbytes / len(prof)),
