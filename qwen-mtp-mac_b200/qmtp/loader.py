@@ -360,6 +360,25 @@ def load(files: Iterable, config: dict, mtp_files: Iterable = (), hf_norms: bool
     return a, to_device(Wn, device)
 
 
+def checkpoint_dir(path):
+    """(config dict, safetensors files) of a Hugging Face / MLX model directory: the shards named by
+    model.safetensors.index.json (weight_map), else every *.safetensors file in the directory."""
+    d = Path(path).expanduser()
+    config = json.loads((d / "config.json").read_text())
+    index = d / "model.safetensors.index.json"
+    if index.exists():
+        shards = sorted(set(json.loads(index.read_text())["weight_map"].values()))
+        files = [d / f for f in shards]
+        missing = [str(f) for f in files if not f.exists()]
+        if missing:
+            raise FileNotFoundError(f"shards named by the index are missing: {missing}")
+    else:
+        files = sorted(d.glob("*.safetensors"))
+    if not files:
+        raise FileNotFoundError(f"{d}: no safetensors files")
+    return config, files
+
+
 # ----------------------------------------------------------------------------------- Ollama
 def ollama_checkpoint(tag: str = "9b-mlx", root="~/.ollama/models", model: str = "qwen3.5"):
     """qwen_ollama.py:22-28: (config dict, tensor blob paths, {json name: path}) of an Ollama model."""

@@ -227,3 +227,18 @@ def test_config_variants():
     c.pop("rope_scaling")
     c["rope_theta"], c["partial_rotary_factor"] = om.SMALL.rope_theta, 0.25
     assert L.args_from_config(c, max_pos=1024) == qm.SMALL
+
+
+def test_checkpoint_dir(tmp_path):
+    L = _loader()
+    cfg = _ckpt.config_dict(om.SMALL)
+    (tmp_path / "config.json").write_text(json.dumps(cfg))
+    for n in ("b.safetensors", "a.safetensors"):
+        L.write_safetensors(tmp_path / n, {"x": np.zeros(2, np.float32)})
+    c, files = L.checkpoint_dir(tmp_path)
+    assert c == cfg and [f.name for f in files] == ["a.safetensors", "b.safetensors"]
+    (tmp_path / "model.safetensors.index.json").write_text(json.dumps({"weight_map": {"x": "b.safetensors"}}))
+    assert [f.name for f in L.checkpoint_dir(tmp_path)[1]] == ["b.safetensors"]
+    (tmp_path / "model.safetensors.index.json").write_text(json.dumps({"weight_map": {"x": "c.safetensors"}}))
+    with pytest.raises(FileNotFoundError):
+        L.checkpoint_dir(tmp_path)
