@@ -8,7 +8,7 @@ k = 2 drafts, batch 1) after a 512-token uniform-random prompt.  Prints one JSON
 
   value      tokens emitted per second over K graph replays, device-timed with CUDA events (the
              replays run back to back, no host round trip);
-  e2e        the same tokens/s through qmtp.mtp.generate_mtp, the call a user makes: one replay,
+  e2e        the same tokens/s through qmtp.mtp.decode_mtp, the call a user makes: one replay,
              stream sync and 128-byte control-block read per cycle, as the reference's loop does;
   roofline   the 4-bit GEMV (qmv) kernels: algorithmic bytes of every qmv launch of one cycle over
              their CUDA-event durations, against the measured HBM copy peak;
@@ -124,7 +124,7 @@ def run_ours(args):
 
     from qmtp import _lib
     from qmtp import model as qm
-    from qmtp.mtp import MTPDecoder, Sampling, _restore, _snapshot, export_state, generate_mtp
+    from qmtp.mtp import MTPDecoder, Sampling, _restore, _snapshot, export_state, decode_mtp
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -145,7 +145,7 @@ def run_ours(args):
     K, Wu = args.steps, args.warmup
     sp = (Sampling(args.temperature, args.top_k, args.top_p, args.min_p, args.seed) if args.temperature > 0
           else None)
-    dec = MTPDecoder(cfg, W, k=K_DRAFTS, max_tokens=Wu + 3 * K + 64, device=dev, fuse_norm=args.fuse_norm,
+    dec = MTPDecoder(cfg, W, k=K_DRAFTS, max_tokens=Wu + 3 * K + 64, device=dev,
                      sampling=sp)
 
     # ---- prefill, one eager cycle (library setup), capture
@@ -220,9 +220,9 @@ def run_ours(args):
         tokens_all = float(tokens)
     value = tokens_all / (elapsed_ms / 1e3)
 
-    # ---- e2e: the public generate_mtp call (per-cycle host sync + control-block read)
+    # ---- e2e: the public decode_mtp call (per-cycle host sync + control-block read)
     gen_tokens = min(256, Wu + K)
-    out, st = generate_mtp(dec, prompt, gen_tokens, use_graph=True)
+    out, st = decode_mtp(dec, prompt, gen_tokens, use_graph=True)
     e2e_tps = st["tps"]
     if world > 1:
         e = torch.tensor([st["seconds"], float(len(out) - 1)], dtype=torch.float64, device=dev)
@@ -339,8 +339,10 @@ def run_kernel(args):
             Ls = [qmv_kernel.quantize((torch.randn(N, Kd, generator=g, device=dev) * 0.02).to(torch.bfloat16))
                   for _ in range(copies)]
             nbytes = N * Kd // 2 + N * (Kd // 64) * 4 + M * Kd * 2 + M * N * 2
-            run = lambda i: qmv_kernel.qmv_affine(x, *Ls[i % copies], out=y)
-            label = f"qmv affine g64 N={N} K={Kd} M={M}"
+            ws = qmv_kernel.workspace(N, Kd, dev)
+            split = fmt != "affine-whole"
+            run = lambda i: qmv_kernel.qmv_affine(x, *Ls[i % copies], out=y, ws=ws, split=split)
+            label = f"qmv affine g64 N={N} K={Kd} M={M}" + ("" if split else " (whole tiles)")
         unit_bytes = nbytes
     elif args.kernel == "gdn":
         S, Hk, Hv, D, KC = 3, 16, 32, 128, 4
@@ -562,11 +564,9 @@ def main():
     ap.add_argument("--top-p", type=float, default=1.0)
     ap.add_argument("--min-p", type=float, default=0.0)
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--fuse-norm", action="store_true",
-                    help="decoder runs the layer RMSNorms inside the consuming projections (bit-identical)")
     ap.add_argument("--kernel", default=None, choices=["qmv", "gdn", "head", "moe"],
                     help="time one kernel at a config shape instead of the decode loop")
-    ap.add_argument("--shape", default="12288,4096,3", help="qmv: N,K,M[,affine|nvfp4]")
+    ap.add_argument("--shape", default="12288,4096,3", help="qmv: N,K,M[,affine|affine-whole|nvfp4]")
     ap.add_argument("--ep-capacity-factor", type=float, default=2.0,
                     help="expert-parallel MoE: rows per peer slot = factor x the average load T*TOPK/G, at most "
                          "the exact bound T*TOPK (0 = exact bound); an overflow shows as device_error != 0")

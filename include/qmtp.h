@@ -42,60 +42,42 @@ int qmtp_device_error(unsigned* out, int clear);
 /* --------------------------------------------------------------------------------------------
  * Multi-row 4-bit GEMV, affine group 64 (MLX quantized_matmul(x, w, scales, biases, transpose=True,
  * group_size=64, bits=4); replaces the QuantizedLinear.__call__ route of qmv_kernel.py:104-113 and
- * the kernel qmv_nvfp4 of qmv_kernel.py:86-101 for the affine format).
+ * the kernel qmv_nvfp4 of qmv_kernel.py:86-101 for the affine format).  Runs on the tensor cores
+ * (tcgen05.mma kind::i8): every group of 64 activations is put on a block-floating-point grid
+ * (x_q = RNE(x * 2^(19-E)), E = exponent of the group's largest |x|) and each group's dot product
+ * with the 4-bit codes is an exact integer; the fp32 sequence after that is fixed (oracle
+ * qo_qmv_affine).  Results do not depend on M, on the launch shape or on the entry point.
  *   x  bf16 [M, K]; w uint32 [N, K/8] (8 nibbles per word, low nibble = lowest k);
  *   scales, biases bf16 [N, K/64]; y bf16 [M, ldy] (columns 0..N-1 written).
- *   K % 1024 == 0 and K <= 12288; any M >= 1 (processed 4 rows at a time); N >= 1.
- * Each output row is reduced in a fixed order that does not depend on M (batch-invariant). */
+ *   K % 512 == 0; any M >= 1 (processed 4 rows per launch); N >= 1.
+ * This entry point needs no workspace: each CTA computes whole tiles of rows (for small N fewer CTAs
+ * than SMs work; qmtp_qmv_affine_g64_split spreads the reduction over every SM). */
 int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const void* biases,
                         void* y, int M, int N, int K, int ldy, void* stream);
 
-/* qmtp_qmv_affine_g64 with the ops around a decoder projection fused in (one launch, every
- * option bit-identical to the separate kernels it replaces):
- *   x rows at x + m * ldx (elements; 0 = K, or 2K with pre = SWIGLU), ldx % 8 == 0;
- *   pre  QMTP_QMV_PRE_RMSNORM: x <- bf16(pre_w * bf16(x * rsqrt(mean(x^2) + pre_eps))) over the K
- *          features while x is loaded (qmtp_rmsnorm then qmv); every CTA repeats the row statistics;
- *        QMTP_QMV_PRE_SWIGLU: x <- bf16(silu(gate) * up), gate = row[0:K], up = row[K:2K] (qmtp_swiglu then
- *          qmv); every CTA repeats the activation for the whole row;
- *   res  != NULL: y = bf16(res + bf16(x . W^T)) as qmtp_qmv_affine_g64_res;
- *   epi  QMTP_QMV_EPI_SWIGLU: w/scales/biases hold 2N rows [gate | up]; y[m][j] = bf16(silu(g_j) * u_j)
- *          with g, u the bf16 projections (qmv over 2N rows then qmtp_swiglu), each element once;
- *        QMTP_QMV_EPI_NORM: after y is complete, norm_y[m] = RMSNorm(y[m]) with weight norm_w and
- *          norm_eps (qmv then qmtp_rmsnorm); needs N % 1024 == 0, N <= K, ld_norm >= N and `sync`,
- *          a device uint32 that is 0 before the call (the kernel leaves it 0); calls that share a
- *          `sync` word must not run concurrently;
- *   prefetch[i], prefetch_bytes[i]: up to four device byte ranges a later kernel reads; the launch
- *          pulls them into L2 while it streams its own weights (a hint: NULL / 0 entries, unaligned
- *          starts are ignored, sizes are rounded down to 16 bytes).
- * pre and epi are exclusive; epi = SWIGLU excludes res. */
-#define QMTP_QMV_PRE_NONE 0
-#define QMTP_QMV_PRE_RMSNORM 1
-#define QMTP_QMV_PRE_SWIGLU 2
-#define QMTP_QMV_EPI_NONE 0
-#define QMTP_QMV_EPI_SWIGLU 1
-#define QMTP_QMV_EPI_NORM 2
-typedef struct qmtp_qmv_args {
-  const void* x;
-  long long ldx;
-  const void* w;
-  const void* scales;
-  const void* biases;
-  void* y;
-  const void* res;
-  int M, N, K, ldy;
-  int pre;
-  const void* pre_w;
-  float pre_eps;
-  int epi;
-  void* norm_y;
-  const void* norm_w;
-  long long ld_norm;
-  float norm_eps;
-  unsigned* sync;
-  const void* prefetch[4];
-  long long prefetch_bytes[4];
-} qmtp_qmv_args;
-int qmtp_qmv_ex(const qmtp_qmv_args* args, void* stream);
+/* qmtp_qmv_affine_g64 with a residual epilogue: y = bf16(res + bf16(x . W^T)) (the bf16 residual
+ * add of a decoder layer fused into the projection; res may alias y).  res bf16 [M, ldy]. */
+int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void* scales, const void* biases,
+                            void* y, const void* res, int M, int N, int K, int ldy, void* stream);
+
+/* Bytes of the workspace qmtp_qmv_affine_g64_split needs for an N x K matrix (any M): 64 KiB of tile
+ * arrival counters (always at the start, so matrices of any shape can share one workspace) plus the
+ * slice partials.  0 if N x K is not supported (K % 512 != 0, or N above 2^20 rows). */
+size_t qmtp_qmv_workspace(int N, int K);
+
+/* qmtp_qmv_affine_g64 (+ optional residual, res may be NULL) with tiles shared between CTAs: a
+ * tile's 512-k slices may be computed by different CTAs, and the CTA that finishes a tile's last
+ * share adds the slice partials in order, so every SM streams weights even for N = 4096.  Same bits
+ * as qmtp_qmv_affine_g64.  x rows at x + m * ldx (elements; 0 = K).  workspace: 256-byte aligned,
+ * >= qmtp_qmv_workspace(N, K) bytes, ZERO-FILLED before its first use; every launch leaves its
+ * arrival counters at zero again.  Launches that may run concurrently need separate workspaces. */
+int qmtp_qmv_affine_g64_split(const void* x, long long ldx, const void* w, const void* scales,
+                              const void* biases, void* y, const void* res, int M, int N, int K, int ldy,
+                              void* workspace, size_t ws_bytes, void* stream);
+
+/* Tiling the affine kernel picks for an N x K matrix (split != 0: the _split entry point): weight
+ * rows per tile, CTAs, work units (tile x 512-k slice).  Host-only query. */
+int qmtp_qmv_plan(int N, int K, int split, int* rows_per_tile, int* grid, int* units);
 
 /* Multi-row 4-bit GEMV, NVFP4 (e2m1 nibbles, e4m3 scale per 16): qmv_kernel.py:86-101 qmv_nvfp4.
  *   x bf16 [M, K]; w uint32 [N, K/8]; scales uint8 [N, K/16]; y bf16 [M, ldy]. K % 1024 == 0. */
@@ -106,17 +88,6 @@ int qmtp_qmv_nvfp4_g16(const void* x, const void* w, const void* scales, void* y
  * the decoder's o_proj / out_proj / down projections of an NVFP4 checkpoint. */
 int qmtp_qmv_nvfp4_g16_res(const void* x, const void* w, const void* scales, void* y, const void* res, int M,
                            int N, int K, int ldy, void* stream);
-
-/* qmtp_qmv_affine_g64 with a residual epilogue: y = bf16(res + bf16(x . W^T)) (the bf16 residual
- * add of a decoder layer fused into the projection; res may alias y).  res bf16 [M, ldy]. */
-int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void* scales, const void* biases,
-                            void* y, const void* res, int M, int N, int K, int ldy, void* stream);
-
-/* Launch shape the qmv kernels use for (fmt 0 = affine g64, 1 = NVFP4 g16, M in 1..4, K):
- * resident CTAs per SM, threads per CTA, dynamic shared memory, rows per pipeline stage.  The grid
- * is min(N, SMs * ctas_per_sm).  Host-only query (first call per shape sets kernel attributes). */
-int qmtp_qmv_launch_info(int fmt, int M, int K, int* ctas_per_sm, int* threads, int* smem_bytes,
-                         int* rows_per_tile);
 
 /* Affine 4-bit group-64 quantizer (MLX mx.quantize(w, 64, 4) convention, min/max form; used by
  * the loader, qwen_ollama.py:45-50 / lm_head2.py:17):  w bf16 [N, K] -> wq uint32 [N, K/8],
@@ -194,7 +165,7 @@ int qmtp_gdn_norm_gate(const float* y, const void* z, int ld_z, const void* w, v
  *   h bf16 [M, K]; wq/scales/biases: affine g64 coarse head [V, K]; w_fine bf16 [V, K];
  *   -> out_idx int32 [M, k] (candidates in that order), out_fine bf16 [M, k] (exact logits),
  *      out_argmax int32 [M] (may be NULL), coarse_out bf16 [M, V] (may be NULL).
- *   workspace: qmtp_lmhead2_workspace(M, V, k) bytes, 16-B aligned.  k <= 256, K % 1024 == 0. */
+ *   workspace: qmtp_lmhead2_workspace(M, V, k) bytes, 16-B aligned.  k <= 256, K % 512 == 0. */
 size_t qmtp_lmhead2_workspace(int M, int V, int k);
 int qmtp_lmhead2(const void* h, const void* wq, const void* scales, const void* biases,
                  const void* w_fine, int M, int V, int K, int k, int* out_idx, void* out_fine,
@@ -206,10 +177,11 @@ int qmtp_lmhead2(const void* h, const void* wq, const void* scales, const void* 
  * counterpart in the reference.  It takes no workspace: it uses a scratch area that is a static
  * __device__ array of the library (2 MiB + 64 KiB on every GPU that loads the library, until exit).
  * Limits: M <= 4 rows, V <= 262144, k <= 64 (larger requests return QMTP_ERR_SHAPE).  The first
- * call on a device looks up the scratch address on that device; make it before any stream
- * capture.  All calls share the one scratch area, so calls that can overlap on the GPU (different
- * streams, or concurrent host threads) race; serialise them.  Results are identical to
- * qmtp_lmhead2. */
+ * call in a CUDA context looks up the scratch address there (cudaGetSymbolAddress) and caches it
+ * for that context; make that first call before any stream capture.  A failed lookup is not cached,
+ * and a new context (after cudaDeviceReset) gets a fresh lookup.  All calls share the one scratch
+ * area, so calls that can overlap on the GPU (different streams, or concurrent host threads) race;
+ * serialise them.  Results are identical to qmtp_lmhead2. */
 int qmtp_lmhead2_noalloc(const void* h, const void* wq, const void* scales, const void* biases,
                          const void* w_fine, int M, int V, int K, int k, int* out_idx, void* out_fine,
                          int* out_argmax, void* stream);

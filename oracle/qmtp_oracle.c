@@ -212,83 +212,133 @@ QO_API void qo_quantize_affine(const uint16_t* w, uint32_t* wq, uint16_t* sc, ui
 }
 
 /* ------------------------------------------------------------------ qmv, affine 4-bit g64
- * y[m,n] = sum_k x[m,k] * (s[n,k/64] * q[n,k] + b[n,k/64]), K % 1024 == 0.
+ * y[m,n] = sum_k x[m,k] * (s[n,k/64] * q[n,k] + b[n,k/64]), K % 512 == 0.
  * Reference op: MLX quantized_matmul(x, w, s, b, transpose=True, group_size=64, bits=4) and the
  * multi-row GEMV of qmv_kernel.py:31-75 (same weight layout; that kernel is the NVFP4 variant).
  *
- * Exact sequence.  K is cut into chunks of 32 (c = k/32: four uint32 words w0..w3 of 8 nibbles,
- * low nibble first); block i = chunks 32i..32i+31.  Every nibble is read as the exact value
- * f = 128 + q (the kernel forms two of them, nibbles j and j+4, as one bf16 pair with a single
- * AND/OR and multiplies with fma.rn.f32.bf16).  Each chunk has two accumulation lanes: lane h
- * takes word h then word h+2; inside a word the order is j = 0, 4, 1, 5, 2, 6, 3, 7.
- *   Sx_h = sum x over the lane's sequence (sequential fp32 adds from 0);
- *   a_h = -(128 * Sx_h);  a_h = fma(128 + q_j, x_j, a_h) over the same sequence;
- *   T = a_0 + a_1;  P_c = fma(b_g, Sx_0 + Sx_1, s_g * T), g = c/2.
- *   B_i = butterfly32(P_{32i..32i+31});  y = ((B_0 + B_1) + B_2) + ...;  out = bf16(y). */
+ * Exact sequence (block floating point per group of 64 activations, exact integer group sums):
+ *   per token m and group g (k in [64g, 64g+64)):
+ *     any x non-finite -> c = xf = NaN (the output row becomes NaN); all x zero -> c = xf = 0;
+ *     else E = floor(log2(max|x|)), x_q = RNE(x * 2^(19-E)) (an integer, |x_q| < 2^20),
+ *     c = 2^(E-19) as fp32 (0 below 2^-149), xf = float(sum_k x_q) * c;
+ *   per row n:  S_g = sum_k q[n,k] * x_q[k]  (exact integer, |S_g| < 2^31);
+ *     slice j = groups 8j..8j+7: H_0 = chain over groups 8j..8j+3, H_1 over 8j+4..8j+7, each from 0:
+ *       H = fma(float(S_g), s_g * c_g, H);  H = fma(b_g, xf_g, H);
+ *     P_j = H_0 + H_1;  y = ((P_0 + P_1) + P_2) + ...;  out = bf16(y).
+ * The tensor-core kernel forms S_g from three signed byte limbs of x_q with kind::i8 MMAs; the
+ * integer sums are exact, so their order does not matter.  Compared with MLX's fp32 sums this
+ * rounds each group's dot product once instead of once per partial sum (x_q is exact for every
+ * element >= 2^-12 of its group's maximum). */
 
-typedef struct { float sx[2]; } qo_xchunk;
+static inline float qo_pow2(int k) {
+  if (k >= -126) return qo_asf((uint32_t)(k + 127) << 23);
+  if (k >= -149) return qo_asf(1u << (k + 149));
+  return 0.0f;
+}
 
-static const int qo_jorder[8] = {0, 4, 1, 5, 2, 6, 3, 7};
+/* |x| of bf16 magnitude bits a on the grid 2^(E-19), round half to even. */
+static inline int32_t qo_grid_mag(uint32_t a, int E) {
+  int ef = (int)(a >> 7);
+  int sig = ef ? (int)(128u | (a & 127u)) : (int)(a & 127u);
+  int ex = ef ? ef - 134 : -133;
+  int sh = ex + 19 - E;
+  if (sh >= 0) return sig << sh;
+  int r = -sh;
+  if (r > 8) return 0;
+  int m = sig >> r, rem = sig & ((1 << r) - 1), half = 1 << (r - 1);
+  if (rem > half || (rem == half && (m & 1))) ++m;
+  return m;
+}
 
-static void qo_affine_xprep(const uint16_t* x, int K, float* xf, qo_xchunk* xc) {
-  for (int k = 0; k < K; ++k) xf[k] = qo_bf2f(x[k]);
-  for (int c = 0; c < K / 32; ++c) {
-    for (int h = 0; h < 2; ++h) {
-      float sx = 0.0f;
-      for (int wi = h; wi < 4; wi += 2)
-        for (int t = 0; t < 8; ++t) sx = sx + xf[32 * c + 8 * wi + qo_jorder[t]];
-      xc[c].sx[h] = sx;
+/* One token row: x_q [K], c and xf per group [K/64]. */
+static void qo_affine_xgroups(const uint16_t* x, int K, int32_t* xq, float* c, float* xf) {
+  for (int g = 0; g < K / 64; ++g) {
+    const uint16_t* xg = x + 64 * g;
+    uint32_t amax = 0;
+    int nf = 0;
+    for (int e = 0; e < 64; ++e) {
+      uint32_t a = xg[e] & 0x7FFFu;
+      if (a >= 0x7F80u) nf = 1;
+      if (a > amax) amax = a;
     }
+    if (nf || amax == 0) {
+      for (int e = 0; e < 64; ++e) xq[64 * g + e] = 0;
+      c[g] = xf[g] = nf ? qo_asf(0x7FC00000u) : 0.0f;
+      continue;
+    }
+    int ef = (int)(amax >> 7);
+    int E;
+    if (ef) {
+      E = ef - 127;
+    } else {
+      int l = 0;
+      while ((amax & 127u) >> (l + 1)) ++l;
+      E = -133 + l;
+    }
+    int32_t sum = 0;
+    for (int e = 0; e < 64; ++e) {
+      int32_t mag = qo_grid_mag(xg[e] & 0x7FFFu, E);
+      int32_t v = (xg[e] & 0x8000u) ? -mag : mag;
+      xq[64 * g + e] = v;
+      sum += v;
+    }
+    c[g] = qo_pow2(E - 19);
+    xf[g] = (float)sum * c[g];
   }
 }
 
-static float qo_affine_row(const float* xf, const qo_xchunk* xc, const uint32_t* wrow,
+static float qo_affine_row(const int32_t* xq, const float* c, const float* xf, const uint8_t* qrow,
                            const uint16_t* srow, const uint16_t* brow, int K) {
-  int NC = K / 32;
+  int NSL = K / 512;
   float y = 0.0f;
-  for (int i = 0; i < NC / 32; ++i) {
-    float P[32];
-    for (int l = 0; l < 32; ++l) {
-      int c = 32 * i + l;
-      float a[2];
-      for (int h = 0; h < 2; ++h) {
-        float acc = -(128.0f * xc[c].sx[h]);
-        for (int wi = h; wi < 4; wi += 2) {
-          uint32_t w = wrow[4 * c + wi];
-          for (int t = 0; t < 8; ++t) {
-            int j = qo_jorder[t];
-            acc = fmaf(128.0f + (float)((w >> (4 * j)) & 15u), xf[32 * c + 8 * wi + j], acc);
-          }
-        }
-        a[h] = acc;
+  for (int sl = 0; sl < NSL; ++sl) {
+    float H[2] = {0.0f, 0.0f};
+    for (int h = 0; h < 2; ++h) {
+      for (int gi = 0; gi < 4; ++gi) {
+        int g = 8 * sl + 4 * h + gi;
+        const uint8_t* qg = qrow + 64 * g;
+        const int32_t* xg = xq + 64 * g;
+        int32_t S = 0; /* exact: every partial sum is below 64 * 15 * 2^20 < 2^31 */
+        for (int e = 0; e < 64; ++e) S += (int32_t)qg[e] * xg[e];
+        float t = (float)S;
+        float s = qo_bf2f(srow[g]), b = qo_bf2f(brow[g]);
+        H[h] = fmaf(t, s * c[g], H[h]);
+        H[h] = fmaf(b, xf[g], H[h]);
       }
-      float T = a[0] + a[1];
-      float s = qo_bf2f(srow[c >> 1]), b = qo_bf2f(brow[c >> 1]);
-      P[l] = fmaf(b, xc[c].sx[0] + xc[c].sx[1], s * T);
     }
-    float B = qo_butterfly32(P);
-    y = (i == 0) ? B : y + B;
+    float P = H[0] + H[1];
+    y = (sl == 0) ? P : y + P;
   }
   return y;
 }
 
 QO_API int qo_qmv_affine(const uint16_t* x, const uint32_t* wq, const uint16_t* sc,
                          const uint16_t* bi, uint16_t* y, int M, int N, int K) {
-  if (K % 1024 != 0 || M < 1 || N < 1) return -1;
-  float* xf = (float*)malloc(sizeof(float) * (size_t)M * K);
-  qo_xchunk* xc = (qo_xchunk*)malloc(sizeof(qo_xchunk) * (size_t)M * (K / 32));
-  for (int m = 0; m < M; ++m) qo_affine_xprep(x + (size_t)m * K, K, xf + (size_t)m * K, xc + (size_t)m * (K / 32));
+  if (K % 512 != 0 || K < 512 || M < 1 || N < 1) return -1;
   int G = K / 64;
-#pragma omp parallel for schedule(static)
-  for (int n = 0; n < N; ++n) {
-    for (int m = 0; m < M; ++m) {
-      float v = qo_affine_row(xf + (size_t)m * K, xc + (size_t)m * (K / 32), wq + (size_t)n * (K / 8),
-                              sc + (size_t)n * G, bi + (size_t)n * G, K);
-      y[(size_t)m * N + n] = qo_f2bf(v);
+  int32_t* xq = (int32_t*)malloc(sizeof(int32_t) * (size_t)M * K);
+  float* c = (float*)malloc(sizeof(float) * (size_t)M * G);
+  float* xf = (float*)malloc(sizeof(float) * (size_t)M * G);
+  for (int m = 0; m < M; ++m)
+    qo_affine_xgroups(x + (size_t)m * K, K, xq + (size_t)m * K, c + (size_t)m * G, xf + (size_t)m * G);
+#pragma omp parallel
+  {
+    uint8_t* qrow = (uint8_t*)malloc((size_t)K);
+#pragma omp for schedule(static)
+    for (int n = 0; n < N; ++n) {
+      const uint32_t* wrow = wq + (size_t)n * (K / 8);
+      for (int k = 0; k < K; ++k) qrow[k] = (uint8_t)((wrow[k >> 3] >> (4 * (k & 7))) & 15u);
+      for (int m = 0; m < M; ++m) {
+        float v = qo_affine_row(xq + (size_t)m * K, c + (size_t)m * G, xf + (size_t)m * G, qrow,
+                                sc + (size_t)n * G, bi + (size_t)n * G, K);
+        y[(size_t)m * N + n] = qo_f2bf(v);
+      }
     }
+    free(qrow);
   }
+  free(xq);
+  free(c);
   free(xf);
-  free(xc);
   return 0;
 }
 

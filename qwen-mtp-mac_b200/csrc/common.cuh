@@ -7,9 +7,12 @@
 // bit-identical to it.  exp/log below are this library's own (Cody-Waite reduction, Taylor /
 // atanh series), not CUDA's math library, for the same reason.
 #pragma once
-#include <cstdint>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <cstdint>
 
 #include "../../include/qmtp.h"
 
@@ -46,7 +49,12 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 // ----------------------------------------------------------------------------- errors
 enum : unsigned { DEVERR_TIMEOUT = 1u, DEVERR_BADARG = 2u };
 unsigned* device_error_ptr();  // per-device address of the library's device error word
+// Device address of a __device__ symbol in the current context (cached per context; QMTP_ERR_CUDA if
+// the lookup fails, which is not cached).
+int symbol_address(const void* symbol, void** out);
 int sm_count();                 // SMs of the current device (cached)
+// cuTensorMapEncodeTiled from the driver (resolved once through the runtime; nullptr if unavailable).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 #define QMTP_CUDA_TRY(expr)                          \
   do {                                               \

@@ -326,20 +326,11 @@ constexpr size_t kNoAllocBytes = size_t(kNoAllocMaxRows) * kNoAllocMaxVocab * si
                                  + size_t(kNoAllocMaxRows) * 32 * kNoAllocMaxK * sizeof(uint64_t);  // candidates
 static __device__ __align__(256) unsigned char g_lmhead2_scratch[kNoAllocBytes];
 
-// Device address of the scratch on the current device.  The name g_lmhead2_scratch in host code is
-// only a host-side stand-in, never a device address, so the address is looked up once per device
-// (with that device current) and cached.
-static int noalloc_scratch(void** out) {
-  static std::once_flag once[64];
-  static void* ptr[64];
-  static cudaError_t err[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QMTP_ERR_CUDA;
-  std::call_once(once[dev], [&] { err[dev] = cudaGetSymbolAddress(&ptr[dev], g_lmhead2_scratch); });
-  if (err[dev] != cudaSuccess || !ptr[dev]) return QMTP_ERR_CUDA;
-  *out = ptr[dev];
-  return QMTP_OK;
-}
+// Device address of the scratch in the current context.  The name g_lmhead2_scratch in host code
+// is only a host-side stand-in, never a device address, so the address is looked up with the device
+// current (cudaGetSymbolAddress) and cached per CUDA context: a context created after a
+// cudaDeviceReset gets a fresh lookup, and a failed lookup is retried by the next call.
+static int noalloc_scratch(void** out) { return symbol_address(g_lmhead2_scratch, out); }
 }  // namespace qmtp
 
 extern "C" int qmtp_lmhead2_noalloc(const void* h, const void* wq, const void* scales, const void* biases,

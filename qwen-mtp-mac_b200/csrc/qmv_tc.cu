@@ -1,0 +1,684 @@
+// 4-bit affine group-64 GEMV (qmv) on the 5th-generation tensor cores (tcgen05.mma kind::i8).
+//
+// Replaces qmv_kernel.py:31-101 (qmv_nvfp4_multi) and the MLX quantized_matmul route of
+// qmv_kernel.py:104-113 for the affine format: y[m, n] = sum_k x[m, k] * (s[n, k/64] * q[n, k] + b[n, k/64]).
+//
+// Arithmetic (the contract oracle/qmtp_oracle.c:qo_qmv_affine states):
+//   * every group of 64 activations of a token is put on a block-floating-point grid: E = exponent of
+//     the group's largest |x|, x_q = RNE(x * 2^(19-E)), an exact integer |x_q| < 2^20 (exact for every
+//     element >= 2^-12 of the group's maximum);
+//   * x_q is split into three signed bytes (x_q = l2*2^14 + l1*2^7 + l0) and the tensor core forms the
+//     exact integer sums D_l = sum_k q_k * l_k (s8 x s8 -> s32), so S = sum_k q_k x_q,k is exact;
+//   * per group: acc = fma(float(S), s * 2^(E-19), acc); acc = fma(b, float(sum x_q) * 2^(E-19), acc),
+//     two chains of four groups per slice of 512 k, slices added in order.
+// The per-group integer sums are exact, so the result does not depend on how the work is split: a
+// launch may give a CTA whole tiles or slices of a tile, and every token row is independent of the
+// others (batch-invariant).
+//
+// Design:
+//   * a tile is R <= 128 weight rows (the MMA's M); a unit of work is (tile, slice of 512 k).  CTAs
+//     take contiguous unit ranges (one CTA per SM, 216 KB of shared memory); a tile split between CTAs
+//     is finished by the CTA that arrives last (one arrival counter per tile at the start of a caller
+//     workspace, fp32 slice partials after them; no CTA ever waits for another);
+//   * warp 0: TMA producer.  Per unit, two 128-byte-wide boxes of packed nibbles (128-byte swizzle) and
+//     the unit's scales and biases land in a 4-stage ring;
+//   * warps 2-3: activation producers.  They build the B operand (the three byte limbs of every token,
+//     16 x 64 bytes per group, canonical K-major layout) and the per-group factors from x;
+//   * warps 4-7: one per TMEM lane quarter, a thread per weight row.  They unpack the nibbles of their
+//     row into bytes (two LOP3s per word) and store them into TMEM as the A operand, then read the
+//     integer accumulators back and run the fp32 chains of the contract;
+//   * warp 1: MMA issuer.  Per unit 16 MMAs (M=128, N=16, K=32, A from TMEM, B from shared memory) and
+//     one commit.  TMEM: A slots [0,256), accumulator slots [256,512), double-buffered per unit.
+// The nibble-to-byte unpacking permutes k inside each word (bytes 0,2,4,6 then 1,3,5,7); the B operand
+// is built with the same permutation, so every product pairs the right x with the right q.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace qmtp {
+namespace tq {
+
+constexpr int kMaxRows = 128;                      // MMA M: rows of a tile
+constexpr int kGpu = 8;                            // groups of 64 k per unit (one 512-k slice)
+constexpr int kBox = 128;                          // inner bytes of a weight TMA box (4 groups)
+constexpr int kWStage = 2 * kMaxRows * kBox;       // 32768: two boxes
+constexpr int kSStage = kMaxRows * 16;             // 2048: 8 bf16 per row
+constexpr int kStage = kWStage + 2 * kSStage;      // 36864
+constexpr int kNS = 4;                             // weight ring stages
+constexpr int kBGroup = 1024;                      // B image of one group: 16 rows x 64 bytes
+constexpr int kNB = 8;                             // B slots
+constexpr int kBSlot = kGpu * kBGroup;             // 8192
+constexpr int kMaxTok = 4;                         // tokens per launch (3 limbs each: 12 of 16 B rows)
+constexpr int kXSlot = kGpu * kMaxTok * 8;         // per slot: [group][token] float2 (c, xf)
+constexpr int kOffB = kNS * kStage;                // 147456
+constexpr int kOffX = kOffB + kNB * kBSlot;        // 212992
+constexpr int kOffBar = kOffX + kNB * kXSlot;      // 215040
+constexpr int kSmemUsed = kOffBar + 512;
+constexpr int kSmem = kSmemUsed + 1024;            // slack for 1024-byte alignment of the base
+constexpr int kThreads = 256;
+constexpr int kTmemCols = 512;
+constexpr int kABase = 0, kDBase = 256;
+constexpr int kMinRows = 64;                       // smallest tile the planner picks (workspace bound)
+// Split-mode workspace: arrival counters first, at a fixed place whatever the matrix, so the slice
+// partials of one shape never land on the counters of another shape sharing the workspace.
+constexpr size_t kCntBytes = 65536;                // 16384 counters: tiles of up to 1M rows
+constexpr long long kMaxSplitTiles = kCntBytes / 4;
+static_assert(kOffB % 1024 == 0 && kStage % 1024 == 0, "stage alignment");
+
+struct Bars {
+  uint64_t full[kNS], empty[kNS];
+  uint64_t afull[2], dfull[2], dempty[2];
+  uint64_t bfull[kNB], bempty[kNB];
+  uint64_t drain;
+  uint32_t tmem;
+  int abort;
+  int last;
+};
+static_assert(sizeof(Bars) <= 512, "barrier block");
+
+struct Params {
+  const uint16_t* x;
+  long long ldx;
+  uint16_t* y;
+  const uint16_t* res;
+  float* part;        // split mode: slice partials [ntiles][NSL][kMaxTok][128]
+  unsigned* cnt;      // split mode: arrival count per tile (0 between launches)
+  unsigned* err;
+  long long U;        // units = ntiles * NSL
+  int ldy, N, K, NSL, R, ntiles, whole;
+};
+
+// D (TMEM, s32) (+)= A (TMEM, s8 rows) x B (shared memory, s8, K-major).  No "memory" clobber: the
+// operands are ordered by the barrier waits and the tcgen05 fences around the issue loop.
+__device__ __forceinline__ void umma_i8(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// Instruction descriptor, kind::i8: s32 accumulator, s8 A and B, both K-major.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+// 2^k as fp32 (exact for k >= -149, 0 below).
+__device__ __forceinline__ float pow2f(int k) {
+  if (k >= -126) return __uint_as_float(uint32_t(k + 127) << 23);
+  if (k >= -149) return __uint_as_float(1u << (k + 149));
+  return 0.0f;
+}
+// |x| of bf16 bits a (sign cleared) on the grid 2^(E-19), rounded to nearest even.
+__device__ __forceinline__ int grid_mag(uint32_t a, int E) {
+  const int ef = int(a >> 7);
+  const int sig = ef ? int(128u | (a & 127u)) : int(a & 127u);
+  const int ex = ef ? ef - 134 : -133;
+  const int sh = ex + 19 - E;
+  if (sh >= 0) return sig << sh;
+  const int r = -sh;
+  if (r > 8) return 0;
+  int m = sig >> r;
+  const int rem = sig & ((1 << r) - 1), half = 1 << (r - 1);
+  if (rem > half || (rem == half && (m & 1))) ++m;
+  return m;
+}
+__device__ __forceinline__ void bar_workers() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ float ld_cg_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kThreads, 1)
+    qmv_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
+                  const __grid_constant__ CUtensorMap tb, const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smraw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(sm + kOffBar);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int NSL = p.NSL, R = p.R;
+  unsigned* err = p.err;
+
+  long long u0, u1;
+  if (p.whole) {
+    const long long T = p.ntiles;
+    u0 = (long long)blockIdx.x * T / gridDim.x * NSL;
+    u1 = (long long)(blockIdx.x + 1) * T / gridDim.x * NSL;
+  } else {
+    u0 = (long long)blockIdx.x * p.U / gridDim.x;
+    u1 = (long long)(blockIdx.x + 1) * p.U / gridDim.x;
+  }
+  const int nun = int(u1 - u0);
+  const bool cache = NSL <= kNB;  // B image of each slice built once (slot = slice); else per unit
+
+  if (tid == 0) {
+    for (int s = 0; s < kNS; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 4);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->afull[s], 4);
+      mbar_init(&bars->dfull[s], 1);
+      mbar_init(&bars->dempty[s], 4);
+    }
+    for (int s = 0; s < kNB; ++s) {
+      mbar_init(&bars->bfull[s], 2);
+      mbar_init(&bars->bempty[s], 4);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&bars->tmem, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem;
+  volatile int* abort_flag = &bars->abort;
+
+  const uint64_t pol_w = policy_evict_first();
+  auto issue = [&](int j) {
+    const long long u = u0 + j;
+    const int tile = int(u / NSL), sl = int(u % NSL);
+    const int row = tile * R;
+    const int st = j % kNS;
+    uint8_t* dst = sm + st * kStage;
+    mbar_expect_tx(&bars->full[st], uint32_t(R * (2 * kBox + 32)));
+    tma_load_2d(dst, &tw, sl * 256, row, &bars->full[st], pol_w);
+    tma_load_2d(dst + kMaxRows * kBox, &tw, sl * 256 + kBox, row, &bars->full[st], pol_w);
+    tma_load_2d(dst + kWStage, &ts, sl * 8, row, &bars->full[st], pol_w);
+    tma_load_2d(dst + kWStage + kSStage, &tb, sl * 8, row, &bars->full[st], pol_w);
+  };
+  // The weights are constant: the first stages are requested before the dependency wait.
+  const int pre = min(kNS, nun);
+  if (warp == 0 && lane == 0)
+    for (int j = 0; j < pre; ++j) issue(j);
+  pdl_trigger();
+  pdl_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int j = pre;
+      for (; j < nun; ++j) {
+        const int st = j % kNS;
+        if (*abort_flag || !mbar_wait_backoff(&bars->empty[st], ((j / kNS) & 1) ^ 1, err, 64)) break;
+        fence_proxy_async();
+        issue(j);
+      }
+      if (j < nun) {
+        *abort_flag = 1;
+        // no copy may land after the CTA exits: wait for the stages still in flight
+        for (int k = 1; k <= kNS && j - k >= 0; ++k) {
+          const int jj = j - k;
+          mbar_wait_backoff(&bars->full[jj % kNS], (jj / kNS) & 1, err, 64, 1u << 16);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(128, 16);
+      const uint32_t bsm = smem_u32(sm + kOffB);
+      bool issued = false;
+      for (int j = 0; j < nun; ++j) {
+        const int a = j & 1;
+        const long long u = u0 + j;
+        const int sl = int(u % NSL);
+        const int slot = cache ? sl : j % kNB;
+        const uint32_t bpar = cache ? 0u : uint32_t((j / kNB) & 1);
+        if (*abort_flag || !mbar_wait_spin(&bars->bfull[slot], bpar, err) ||
+            !mbar_wait_spin(&bars->afull[a], uint32_t((j >> 1) & 1), err) ||
+            !mbar_wait_spin(&bars->dempty[a], uint32_t(((j >> 1) & 1) ^ 1), err)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d0 = tmem + uint32_t(kDBase + a * 128);
+        const uint32_t a0 = tmem + uint32_t(kABase + a * 128);
+        const uint32_t b0 = bsm + uint32_t(slot * kBSlot);
+#pragma unroll
+        for (int g = 0; g < kGpu; ++g) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            umma_i8(d0 + uint32_t(g * 16), a0 + uint32_t(g * 16 + 8 * h),
+                    umma_desc(b0 + uint32_t(g * kBGroup + h * 512), 256u, 128u), idesc, uint32_t(h));
+        }
+        umma_commit(&bars->dfull[a]);
+        issued = true;
+      }
+      // every MMA issued has completed before the CTA releases TMEM
+      if (issued) {
+        umma_commit(&bars->drain);
+        mbar_wait_backoff(&bars->drain, 0, err, 64);
+      }
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------------- activation producers
+    const int tb_ = tid - 64;  // 0..63
+    const int nb = cache ? min(nun, NSL) : nun;
+    for (int j = 0; j < nb; ++j) {
+      const int sl = int((u0 + j) % NSL);
+      const int slot = cache ? sl : j % kNB;
+      if (!cache && j >= kNB) {
+        if (*abort_flag || !mbar_wait_backoff(&bars->bempty[slot], uint32_t(((j / kNB) & 1) ^ 1), err, 64)) {
+          *abort_flag = 1;
+          break;
+        }
+      }
+      uint8_t* bimg = sm + kOffB + slot * kBSlot;
+      float2* xsc = reinterpret_cast<float2*>(sm + kOffX + slot * kXSlot);
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        const int t = tb_ + 64 * i;
+        const int m = t >> 6, g = (t >> 3) & 7, li = t & 7;
+        const uint4 v = *reinterpret_cast<const uint4*>(p.x + (size_t)m * (size_t)p.ldx + (size_t)sl * 512 +
+                                                        g * 64 + li * 8);
+        const uint32_t hv[8] = {v.x & 0xFFFFu, v.x >> 16, v.y & 0xFFFFu, v.y >> 16,
+                                v.z & 0xFFFFu, v.z >> 16, v.w & 0xFFFFu, v.w >> 16};
+        uint32_t amax = 0, nf = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t a = hv[e] & 0x7FFFu;
+          nf |= a >= 0x7F80u ? 1u : 0u;
+          amax = max(amax, a);
+        }
+#pragma unroll
+        for (int d = 1; d < 8; d <<= 1) {
+          amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, d));
+          nf |= __shfl_xor_sync(0xFFFFFFFFu, nf, d);
+        }
+        const bool zero = nf || amax == 0;
+        const int ef = int(amax >> 7);
+        const int E = ef ? ef - 127 : -133 + (31 - __clz(int(amax & 127u) | 1));
+        uint32_t lo[3] = {0, 0, 0}, hi[3] = {0, 0, 0};
+        int xs = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int mag = zero ? 0 : grid_mag(hv[e] & 0x7FFFu, E);
+          const int xq = (hv[e] & 0x8000u) ? -mag : mag;
+          xs += xq;
+          const uint32_t b0 = uint32_t(xq) & 127u, b1 = uint32_t(xq >> 7) & 127u, b2 = uint32_t(xq >> 14) & 255u;
+          const int sh = 8 * (e >> 1);
+          if (e & 1) {
+            hi[0] |= b0 << sh; hi[1] |= b1 << sh; hi[2] |= b2 << sh;
+          } else {
+            lo[0] |= b0 << sh; lo[1] |= b1 << sh; lo[2] |= b2 << sh;
+          }
+        }
+#pragma unroll
+        for (int d = 1; d < 8; d <<= 1) xs += __shfl_xor_sync(0xFFFFFFFFu, xs, d);
+        // B row j = 3m + limb, k bytes p = 8li .. 8li+7 of the group (canonical K-major layout)
+        const int pb = 8 * li;
+#pragma unroll
+        for (int l = 0; l < 3; ++l) {
+          const int j = 3 * m + l;
+          const int off = g * kBGroup + ((pb >> 4) * 2 + (j >> 3)) * 128 + (j & 7) * 16 + (pb & 15);
+          *reinterpret_cast<uint2*>(bimg + off) = make_uint2(lo[l], hi[l]);
+        }
+        if (li == 0) {
+          float c, xf;
+          if (nf) {
+            c = xf = __uint_as_float(0x7FC00000u);
+          } else if (amax == 0) {
+            c = xf = 0.0f;
+          } else {
+            c = pow2f(E - 19);
+            xf = __fmul_rn(__int2float_rn(xs), c);
+          }
+          xsc[g * kMaxTok + m] = make_float2(c, xf);
+        }
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->bfull[slot]);
+    }
+  } else {
+    // ------------------------------------------------------------------- row workers
+    const int q = warp - 4;
+    const int r = 32 * q + lane;
+    const uint32_t tl = tmem + (uint32_t(32 * q) << 16);
+    const int rsw = r & 7;
+    float Y[MT];
+    bool own = false;  // this CTA holds slice 0 of the current tile (Y is the tile's running prefix)
+    int part_start = 0;
+#pragma unroll
+    for (int m = 0; m < MT; ++m) Y[m] = 0.0f;
+    uint4 sv_prev = make_uint4(0, 0, 0, 0), bv_prev = make_uint4(0, 0, 0, 0);
+    bool ok = true;
+
+    // Every worker warp runs the same sequence of epilogues and named barriers whatever happens: a wait
+    // that gives up only sets `ok` false (and the CTA's abort flag), so no warp is left at a barrier.
+    auto epilogue = [&](int jj, const uint4& sv, const uint4& bv) {
+      const int a = jj & 1;
+      const long long u = u0 + jj;
+      const int tile = int(u / NSL), sl = int(u % NSL);
+      const int slot = cache ? sl : jj % kNB;
+      const uint32_t bpar = cache ? 0u : uint32_t((jj / kNB) & 1);
+      if (ok && !*abort_flag) {
+        if (!mbar_wait_backoff(&bars->dfull[a], uint32_t((jj >> 1) & 1), err, 32) ||
+            !mbar_wait_backoff(&bars->bfull[slot], bpar, err, 32)) {
+          ok = false;
+          *abort_flag = 1;
+        }
+      } else {
+        ok = false;
+      }
+      tc_fence_after();
+      const float2* xsc = reinterpret_cast<const float2*>(sm + kOffX + slot * kXSlot);
+      const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+      float H0[MT], H1[MT];
+#pragma unroll
+      for (int m = 0; m < MT; ++m) H0[m] = H1[m] = 0.0f;
+#pragma unroll
+      for (int gp = 0; gp < 4; ++gp) {
+        uint32_t v0[16], v1[16];
+        tmem_ld16(tl + uint32_t(kDBase + a * 128 + gp * 16), v0);
+        tmem_ld16(tl + uint32_t(kDBase + a * 128 + (gp + 4) * 16), v1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int g = gp + 4 * hh;
+          const uint32_t* v = hh ? v1 : v0;
+          const float s = (g & 1) ? bfhi(sw[g >> 1]) : bflo(sw[g >> 1]);
+          const float b = (g & 1) ? bfhi(bw[g >> 1]) : bflo(bw[g >> 1]);
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            const int S = int(v[3 * m + 2]) * 16384 + int(v[3 * m + 1]) * 128 + int(v[3 * m]);
+            const float2 cx = xsc[g * kMaxTok + m];
+            float& H = hh ? H1[m] : H0[m];
+            H = __fmaf_rn(__int2float_rn(S), __fmul_rn(s, cx.x), H);
+            H = __fmaf_rn(b, cx.y, H);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && ok) {
+        mbar_arrive(&bars->dempty[a]);
+        if (!cache) mbar_arrive(&bars->bempty[slot]);
+      }
+      float P[MT];
+#pragma unroll
+      for (int m = 0; m < MT; ++m) P[m] = __fadd_rn(H0[m], H1[m]);
+      const size_t tbase = (size_t)tile * (size_t)NSL * (kMaxTok * 128);
+      if (sl == 0) {
+        own = true;
+        part_start = 0;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) Y[m] = P[m];
+      } else if (own) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) Y[m] = __fadd_rn(Y[m], P[m]);
+      } else {
+        if (jj == 0) part_start = sl;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) p.part[tbase + (size_t)sl * (kMaxTok * 128) + m * 128 + r] = P[m];
+      }
+      const bool end = sl == NSL - 1 || jj == nun - 1;
+      if (!end) return;
+      const int row = tile * R + r;
+      const bool valid = r < R && row < p.N;
+      if (own && sl == NSL - 1) {
+        // the whole tile was computed here
+        if (valid) {
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            uint16_t o = f2bf(Y[m]);
+            const size_t oi = (size_t)m * p.ldy + row;
+            if (p.res) o = f2bf(__fadd_rn(bf2f(p.res[oi]), bf2f(o)));
+            p.y[oi] = o;
+          }
+        }
+        own = false;
+        return;
+      }
+      // a split tile: publish this CTA's share; the last CTA to arrive finishes the tile
+      if (own) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) p.part[tbase + m * 128 + r] = Y[m];
+      }
+      const int contributed = sl - part_start + 1;
+      __threadfence();
+      bar_workers();
+      if (tid == 128) {
+        const unsigned old = atomicAdd(&p.cnt[tile], unsigned(contributed));
+        bars->last = (old + unsigned(contributed) == unsigned(NSL)) ? 1 : 0;
+      }
+      bar_workers();
+      if (bars->last) {
+        __threadfence();
+        // slices covered by the prefix: those of the CTA that owns unit tile * NSL
+        const long long v = (long long)tile * NSL;
+        const long long G = gridDim.x;
+        const long long owner = ((v + 1) * G + p.U - 1) / p.U - 1;
+        const long long ou1 = (owner + 1) * p.U / G;
+        const int alen = int(min(ou1, v + NSL) - v);
+        if (valid) {
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            float acc = ld_cg_f32(p.part + tbase + m * 128 + r);
+            for (int s2 = alen; s2 < NSL; ++s2)
+              acc = __fadd_rn(acc, ld_cg_f32(p.part + tbase + (size_t)s2 * (kMaxTok * 128) + m * 128 + r));
+            uint16_t o = f2bf(acc);
+            const size_t oi = (size_t)m * p.ldy + row;
+            if (p.res) o = f2bf(__fadd_rn(bf2f(p.res[oi]), bf2f(o)));
+            p.y[oi] = o;
+          }
+        }
+        if (tid == 128) p.cnt[tile] = 0u;  // ready for the next launch
+      }
+      bar_workers();
+      own = false;
+    };
+
+    for (int j = 0; j < nun; ++j) {
+      const int st = j % kNS;
+      if (ok && !*abort_flag) {
+        if (!mbar_wait_backoff(&bars->full[st], uint32_t((j / kNS) & 1), err, 32)) {
+          ok = false;
+          *abort_flag = 1;
+        }
+      } else {
+        ok = false;
+      }
+      const uint8_t* sg = sm + st * kStage;
+      const uint4 sv = *reinterpret_cast<const uint4*>(sg + kWStage + r * 16);
+      const uint4 bv = *reinterpret_cast<const uint4*>(sg + kWStage + kSStage + r * 16);
+      const int a = j & 1;
+#pragma unroll
+      for (int g = 0; g < kGpu; ++g) {
+        const uint8_t* rowp = sg + (g >> 2) * (kMaxRows * kBox) + r * kBox;
+        const int c0 = 2 * (g & 3);
+        const uint4 w0 = *reinterpret_cast<const uint4*>(rowp + 16 * (c0 ^ rsw));
+        const uint4 w1 = *reinterpret_cast<const uint4*>(rowp + 16 * ((c0 + 1) ^ rsw));
+        const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        uint32_t o[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          o[2 * i] = wd[i] & 0x0F0F0F0Fu;
+          o[2 * i + 1] = (wd[i] >> 4) & 0x0F0F0F0Fu;
+        }
+        tmem_st16(tl + uint32_t(kABase + a * 128 + g * 16), o);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && ok) {
+        mbar_arrive(&bars->empty[st]);
+        mbar_arrive(&bars->afull[a]);
+      }
+      if (j >= 1) epilogue(j - 1, sv_prev, bv_prev);
+      sv_prev = sv;
+      bv_prev = bv;
+    }
+    if (nun > 0) epilogue(nun - 1, sv_prev, bv_prev);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ----------------------------------------------------------------------------- host side
+struct Plan {
+  int R, G, ntiles, NSL, whole;
+  long long U;
+};
+
+// Rows per tile and grid: the slowest CTA's work (units x max(bytes / per-SM bandwidth, MMA issue
+// floor)) is minimised; ties go to the larger tile.
+static Plan make_plan(int N, int K, bool split, int sms) {
+  const int NSL = K / 512;
+  Plan best{};
+  double best_cost = 1e30;
+  for (int R = kMaxRows; R >= kMinRows; R -= 8) {
+    const int T = (N + R - 1) / R;
+    long long G, per;
+    if (split) {
+      const long long U = (long long)T * NSL;
+      G = std::min<long long>(sms, U);
+      per = (U + G - 1) / G;
+    } else {
+      G = std::min(sms, T);
+      per = (long long)((T + G - 1) / G) * NSL;
+    }
+    const double unit_us = std::max(R * 288.0 / 44.0e3, 0.45);
+    const double cost = double(per) * unit_us;
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = Plan{R, int(G), T, NSL, split ? 0 : 1, (long long)T * NSL};
+    }
+  }
+  return best;
+}
+
+static bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, long long inner,
+                      long long rows, int box_inner, int box_rows, CUtensorMapSwizzle swz) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(inner * esize)};
+  cuuint32_t box[2] = {uint32_t(box_inner), uint32_t(box_rows)};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int MT>
+static int launch_mt(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb, const Params& p, int G,
+                     cudaStream_t st) {
+  auto kern = qmv_tc_kernel<MT>;
+  static std::once_flag once;
+  static bool ok = false;
+  std::call_once(once, [&] {
+    ok = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) == cudaSuccess;
+  });
+  if (!ok) return QMTP_ERR_CUDA;
+  launch_kernel(kern, dim3(G), dim3(kThreads), kSmem, st, tw, ts, tb, p);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+static size_t ws_part_bytes(int N, int K) {
+  const long long T = (N + kMinRows - 1) / kMinRows;
+  return (size_t)T * (size_t)(K / 512) * kMaxTok * 128 * sizeof(float);
+}
+
+}  // namespace tq
+
+size_t qmv_tc_workspace(int N, int K) {
+  if (N < 1 || K < 512 || K % 512) return 0;
+  if ((N + tq::kMinRows - 1) / tq::kMinRows > tq::kMaxSplitTiles) return 0;
+  return tq::kCntBytes + tq::ws_part_bytes(N, K);
+}
+
+// All affine qmv entry points land here.  workspace == nullptr: whole tiles per CTA.
+int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const void* b, void* y, const void* res,
+           int M, int N, int K, int ldy, void* workspace, size_t ws_bytes, void* stream) {
+  using namespace tq;
+  if (!x || !w || !s || !b || !y) return QMTP_ERR_ARG;
+  if (M < 1 || N < 1 || K < 512 || K % 512 != 0 || ldy < N) return QMTP_ERR_SHAPE;
+  if (ldx == 0) ldx = K;
+  if (ldx < K || ldx % 8) return QMTP_ERR_SHAPE;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(s) || !aligned16(b)) return QMTP_ERR_ALIGN;
+  const bool split = workspace != nullptr;
+  if (split && (qmv_tc_workspace(N, K) == 0 || ws_bytes < qmv_tc_workspace(N, K))) return QMTP_ERR_SHAPE;
+  if (split && (reinterpret_cast<uintptr_t>(workspace) & 255u)) return QMTP_ERR_ALIGN;
+  const Plan pl = make_plan(N, K, split, sm_count());
+  CUtensorMap tw, ts, tb;
+  if (!encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, K / 2, N, kBox, pl.R, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, s, K / 64, N, 8, pl.R, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, b, K / 64, N, 8, pl.R, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return QMTP_ERR_CUDA;
+  Params p{};
+  p.ldx = ldx;
+  p.ldy = ldy;
+  p.N = N;
+  p.K = K;
+  p.NSL = pl.NSL;
+  p.R = pl.R;
+  p.ntiles = pl.ntiles;
+  p.whole = pl.whole;
+  p.U = pl.U;
+  p.err = device_error_ptr();
+  if (split) {
+    p.cnt = static_cast<unsigned*>(workspace);
+    p.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCntBytes);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int m0 = 0; m0 < M; m0 += kMaxTok) {
+    const int mm = std::min(kMaxTok, M - m0);
+    p.x = static_cast<const uint16_t*>(x) + (size_t)m0 * (size_t)ldx;
+    p.y = static_cast<uint16_t*>(y) + (size_t)m0 * (size_t)ldy;
+    p.res = res ? static_cast<const uint16_t*>(res) + (size_t)m0 * (size_t)ldy : nullptr;
+    int rc;
+    switch (mm) {
+      case 1: rc = launch_mt<1>(tw, ts, tb, p, pl.G, st); break;
+      case 2: rc = launch_mt<2>(tw, ts, tb, p, pl.G, st); break;
+      case 3: rc = launch_mt<3>(tw, ts, tb, p, pl.G, st); break;
+      default: rc = launch_mt<4>(tw, ts, tb, p, pl.G, st); break;
+    }
+    if (rc != QMTP_OK) return rc;
+  }
+  return QMTP_OK;
+}
+
+int qmv_tc_plan(int N, int K, int split, int* rows, int* grid, int* units) {
+  const tq::Plan pl = tq::make_plan(N, K, split != 0, sm_count());
+  if (rows) *rows = pl.R;
+  if (grid) *grid = pl.G;
+  if (units) *units = int(pl.U);
+  return QMTP_OK;
+}
+
+}  // namespace qmtp
+
+using namespace qmtp;
+
+extern "C" int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const void* biases, void* y,
+                                   int M, int N, int K, int ldy, void* stream) {
+  return qmv_tc(x, 0, w, scales, biases, y, nullptr, M, N, K, ldy, nullptr, 0, stream);
+}
+
+extern "C" int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void* scales, const void* biases, void* y,
+                                       const void* res, int M, int N, int K, int ldy, void* stream) {
+  if (!res) return QMTP_ERR_ARG;
+  return qmv_tc(x, 0, w, scales, biases, y, res, M, N, K, ldy, nullptr, 0, stream);
+}
+
+extern "C" size_t qmtp_qmv_workspace(int N, int K) { return qmv_tc_workspace(N, K); }
+
+extern "C" int qmtp_qmv_affine_g64_split(const void* x, long long ldx, const void* w, const void* scales,
+                                         const void* biases, void* y, const void* res, int M, int N, int K, int ldy,
+                                         void* workspace, size_t ws_bytes, void* stream) {
+  if (!workspace) return QMTP_ERR_ARG;
+  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, workspace, ws_bytes, stream);
+}
+
+extern "C" int qmtp_qmv_plan(int N, int K, int split, int* rows_per_tile, int* grid, int* units) {
+  if (N < 1 || K < 512 || K % 512) return QMTP_ERR_SHAPE;
+  return qmv_tc_plan(N, K, split, rows_per_tile, grid, units);
+}

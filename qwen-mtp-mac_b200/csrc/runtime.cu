@@ -11,16 +11,62 @@ static __device__ unsigned g_device_error;
 
 static constexpr int kMaxDevices = 64;
 
-unsigned* device_error_ptr() {
-  static std::once_flag once[kMaxDevices];
-  static unsigned* ptr[kMaxDevices];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  std::call_once(once[dev], [&] {
+// The CUDA context current on this thread (driver entry point resolved once), or nullptr.
+static CUcontext current_context() {
+  using Fn = CUresult (*)(CUcontext*);
+  static std::once_flag once;
+  static Fn fn = nullptr;
+  std::call_once(once, [] {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess) ptr[dev] = static_cast<unsigned*>(p);
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<Fn>(p);
   });
-  return ptr[dev];
+  CUcontext c = nullptr;
+  if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
+// Device addresses of __device__ symbols, cached per (context, symbol).  Keyed on the context, not
+// the device ordinal, so a context created after cudaDeviceReset gets a fresh lookup instead of a
+// stale address; failed lookups are not cached, so a call that failed (for example inside a stream
+// capture) is retried by the next call.
+int symbol_address(const void* symbol, void** out) {
+  struct Entry {
+    CUcontext ctx;
+    const void* sym;
+    void* addr;
+  };
+  static std::mutex mu;
+  static Entry table[256];
+  static int used = 0;
+  CUcontext ctx = current_context();
+  if (ctx) {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i)
+      if (table[i].ctx == ctx && table[i].sym == symbol) {
+        *out = table[i].addr;
+        return QMTP_OK;
+      }
+  }
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, symbol) != cudaSuccess || !p) {
+    cudaGetLastError();  // the failed lookup leaves no sticky error behind
+    return QMTP_ERR_CUDA;
+  }
+  if (!ctx) ctx = current_context();  // the lookup above may have created the primary context
+  if (ctx) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (used < 256) table[used++] = Entry{ctx, symbol, p};
+  }
+  *out = p;
+  return QMTP_OK;
+}
+
+unsigned* device_error_ptr() {
+  void* p = nullptr;
+  return symbol_address(&g_device_error, &p) == QMTP_OK ? static_cast<unsigned*>(p) : nullptr;
 }
 
 int sm_count() {
@@ -34,6 +80,19 @@ int sm_count() {
     count[dev] = c > 0 ? c : 1;
   });
   return count[dev];
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
 }
 
 bool pdl_enabled() {

@@ -36,8 +36,9 @@ SIGNATURES: dict[str, list] = {
     "qmtp_qmv_affine_g64": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_qmv_nvfp4_g16": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_quantize_affine_g64": [_P, _P, _P, _P, _I, _I, _P],
-    "qmtp_qmv_launch_info": [_I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
-                             ctypes.POINTER(_I)],
+    "qmtp_qmv_affine_g64_split": [_P, ctypes.c_longlong, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, ctypes.c_size_t,
+                                  _P],
+    "qmtp_qmv_plan": [_I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)],
 }
 
 
@@ -54,21 +55,7 @@ class GdnArgs(ctypes.Structure):
                 ("S", _I), ("Hk", _I), ("Hv", _I), ("Dk", _I), ("Dv", _I), ("KC", _I), ("snap", _I)]
 
 
-class QmvArgs(ctypes.Structure):
-    """Mirror of qmtp_qmv_args (include/qmtp.h)."""
-    _fields_ = [("x", _P), ("ldx", ctypes.c_longlong), ("w", _P), ("scales", _P), ("biases", _P),
-                ("y", _P), ("res", _P), ("M", _I), ("N", _I), ("K", _I), ("ldy", _I),
-                ("pre", _I), ("pre_w", _P), ("pre_eps", _F),
-                ("epi", _I), ("norm_y", _P), ("norm_w", _P), ("ld_norm", ctypes.c_longlong), ("norm_eps", _F),
-                ("sync", _P), ("prefetch", _P * 4), ("prefetch_bytes", ctypes.c_longlong * 4)]
-
-
-QMV_PRE_NONE, QMV_PRE_RMSNORM, QMV_PRE_SWIGLU = 0, 1, 2
-QMV_EPI_NONE, QMV_EPI_SWIGLU, QMV_EPI_NORM = 0, 1, 2
-
-
 SIGNATURES.update({
-    "qmtp_qmv_ex": [ctypes.POINTER(QmvArgs), _P],
     "qmtp_gdn_step": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
     "qmtp_gdn_fused": [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
     "qmtp_gdn_fused_ex": [ctypes.POINTER(GdnArgs), _P],
@@ -113,6 +100,7 @@ SIGNATURES["qmtp_sample"] = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, cty
 CTRL_SIZE = 32
 # size queries return size_t
 SIZE_QUERIES: dict[str, list] = {
+    "qmtp_qmv_workspace": [_I, _I],
     "qmtp_lmhead2_workspace": [_I, _I, _I],
     "qmtp_topk_workspace": [_I, _I, _I],
     "qmtp_argmax_workspace": [_I, _I],
@@ -186,7 +174,8 @@ def device_error(clear: bool = True) -> int:
     return v.value
 
 
-def qmv_launch_info(fmt: int, M: int, K: int) -> dict:
-    vals = [ctypes.c_int(0) for _ in range(4)]
-    check(lib().qmtp_qmv_launch_info(fmt, M, K, *[ctypes.byref(v) for v in vals]), "qmv_launch_info")
-    return dict(zip(("ctas_per_sm", "threads", "smem_bytes", "rows_per_tile"), (v.value for v in vals)))
+def qmv_plan(N: int, K: int, split: bool = True) -> dict:
+    """Tiling the affine qmv kernel picks for an N x K matrix: rows per tile, CTAs, work units."""
+    vals = [ctypes.c_int(0) for _ in range(3)]
+    check(lib().qmtp_qmv_plan(N, K, int(split), *[ctypes.byref(v) for v in vals]), "qmv_plan")
+    return dict(zip(("rows_per_tile", "grid", "units"), (v.value for v in vals)))

@@ -85,6 +85,36 @@ class Weights(dict):
     """Nested dict of device tensors / QuantizedLinear layers, same key names as the oracle's."""
 
 
+class Model:
+    """The language model handle the reference's loop functions take as ``lm`` (mtp.py:143-303):
+    configuration, weights, the two-stage head (``lm_head``, lm_head2.py:14-29) and its MTP weights
+    (``mtp``, mtp.py:35-70).  ``make_cache`` returns the device state of a decoding session (an
+    ``MTPDecoder``), which stands for the reference's trunk cache and MTP cache together."""
+
+    def __init__(self, args: ModelArgs, weights: Weights):
+        from .lm_head2 import TwoStageHead
+
+        self.args, self.weights = args, weights
+        self.mtp = weights["mtp"]
+        self.lm_head = TwoStageHead(weights["lm_head"], 64, weights["lm_head_q"])
+        self._caches: dict = {}
+
+    def make_cache(self, k: int = 2, max_tokens: int = 1024, sampling=None):
+        from .mtp import MTPDecoder
+
+        return MTPDecoder(self.args, self.weights, k=k, max_tokens=max_tokens,
+                          device=self.weights["norm"].device, sampling=sampling)
+
+    def session(self, k: int = 2, max_tokens: int = 1024):
+        """A decoder for k drafts kept on the model (reused by generate_mtp calls with the same k while
+        it has room for max_tokens)."""
+        dec = self._caches.get(k)
+        if dec is None or dec.out_cap < max_tokens + dec.S + 8:
+            dec = self.make_cache(k=k, max_tokens=max(max_tokens, 1024))
+            self._caches[k] = dec
+        return dec
+
+
 def _randn_bf16(shape, gen, std, device):
     return (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std).to(torch.bfloat16)
 

@@ -45,23 +45,12 @@ class MTPDecoder:
     """Device state + launch sequence of one MTP decoding session (batch 1; greedy or sampled)."""
 
     def __init__(self, args: ModelArgs, W: Weights, k: int = 2, max_tokens: int = 1024, device="cuda",
-                 fuse_norm: bool = False, sampling: Sampling | None = None):
+                 sampling: Sampling | None = None):
         self.a, self.W, self.k = args, W, k
         # sampling with temperature > 0: exact speculative sampling (engine.py:91-152) over the
         # k_for(sampling) candidates of the two-stage head (lm_head2.py:32-36); otherwise greedy
-        self.sp = sampling if sampling is not None and sampling.temperature > 0 else None
-        self.K = k_for(self.sp)
-        if self.K > 256:
-            raise NotImplementedError(f"top_k = {sampling.top_k} needs {self.K} head candidates; this build "
-                                      "selects at most 256 (top_k <= 64, or top_k = 0)")
-        if self.sp is not None:
-            self._sargs = _lib.SamplingArgs(float(self.sp.temperature), int(self.sp.top_k), float(self.sp.top_p),
-                                            float(self.sp.min_p))
-        # fuse_norm: the input / post-attention RMSNorms run in the x prologue of the projection that
-        # consumes them (qmtp_qmv_ex PRE_RMSNORM, bit-identical to the separate kernel).  Off by default:
-        # every CTA of the projection then normalises the whole row again, which costs more than the
-        # separate launch it saves (config 4 on B200: 277 against 292 tok/s).
-        self.fuse_norm = fuse_norm
+        self.sp, self.K, self._sargs = None, 64, None
+        self.set_sampling(sampling, _init=True)
         self.S = k + 1
         self.dev = torch.device(device)
         a, S, dev = args, self.S, self.dev
@@ -90,10 +79,13 @@ class MTPDecoder:
         self.qb, self.gb = z(S, a.n_heads, a.head_dim), z(S, a.n_heads, a.head_dim)
         self.gu, self.act = z(S, 2 * a.intermediate), z(S, a.intermediate)
         self.memb, self.mcat, self.mx, self.mxn = z(S, H), z(S, 2 * H), z(S, H), z(1, H)
+        self._hstage, self._sel, self._last_S = z(S, H), z(1, dtype=i32), None  # reference-style calls
         self.dlogits = z(1, a.vocab)
-        self.fine, self.idx = z(S, self.K), z(S, self.K, dtype=i32)
+        self.KMAX = 256
+        self.fine, self.idx = z(S, self.KMAX), z(S, self.KMAX, dtype=i32)
         self.coarse = z(S, a.vocab)
-        self.topk_ws = torch.empty(self.L.qmtp_topk_workspace(S, a.vocab, self.K), dtype=torch.uint8, device=dev)
+        self.topk_ws = torch.empty(self.L.qmtp_topk_workspace(S, a.vocab, self.KMAX), dtype=torch.uint8,
+                                   device=dev)
         self.argmax_ws = torch.empty(self.L.qmtp_argmax_workspace(1, a.vocab), dtype=torch.uint8, device=dev)
         # recurrent / cache state
         self.lin_ids = [i for i in range(a.layers) if a.is_linear(i)]
@@ -108,14 +100,32 @@ class MTPDecoder:
         self._gdn_args = {}
         for i in self.lin_ids:
             self._gdn_args[i] = self._make_gdn_args(i)
-        # Measured on B200 (config 4): the fused swiglu / norm epilogues and the L2 prefetch of
-        # qmtp_qmv_ex do not shorten this cycle (the separate glue kernels overlap through PDL), so
-        # the decoder launches plain projections.
-        self._qa = _lib.QmvArgs()
+        # split-K workspace of the affine projections (tile partials + arrival counters), sized for the
+        # largest matrix the decoder multiplies; zero-filled once, the kernel leaves the counters at zero
+        shapes = [(lin.out_features, lin.in_features) for lin in _linears(W) if lin.mode == "affine"]
+        ws = max([int(self.L.qmtp_qmv_workspace(n, k_)) for n, k_ in shapes] + [256])
+        self.qws = torch.zeros(ws, dtype=torch.uint8, device=dev)
         self.graph = None
         self.launches = 0      # kernels launched by the library calls of this decoder
         self.prof = None       # list of (bytes, start event, end event, shape) while profiling qmv
         self.qmv_log = None    # list of the _qmv argument tuples of a cycle while recording
+
+    def set_sampling(self, sampling: Sampling | None, _init: bool = False):
+        """Greedy (None or temperature 0) or exact speculative sampling with these parameters; the
+        candidate count is k_for(sampling).  A change drops the captured cycle graph (recaptured by the
+        next decode), since the sampler's parameters are part of its launches."""
+        sp = sampling if sampling is not None and sampling.temperature > 0 else None
+        K = k_for(sp)
+        if K > 256:
+            raise NotImplementedError(f"top_k = {sampling.top_k} needs {K} head candidates; this build "
+                                      "selects at most 256 (top_k <= 64, or top_k = 0)")
+        key = None if sp is None else (float(sp.temperature), int(sp.top_k), float(sp.top_p), float(sp.min_p))
+        old = None if self.sp is None else (float(self.sp.temperature), int(self.sp.top_k), float(self.sp.top_p),
+                                            float(self.sp.min_p))
+        self.sp, self.K = sp, K
+        self._sargs = None if sp is None else _lib.SamplingArgs(*key)
+        if not _init and key != old:
+            self.graph = None
 
     # ------------------------------------------------------------------ helpers
     def _cp(self, slot: int) -> int:
@@ -143,17 +153,15 @@ class MTPDecoder:
                                    a.hidden, out.data_ptr(), a.hidden, self._st())
         self._chk(rc, "embed")
 
-    def _qmv(self, x, lin, y, M, res=None, ldy=None, pre_w=None):
-        """4-bit GEMV y = x . W^T (+ res), one qmtp_qmv_ex launch per 4 rows; with pre_w, x is first
-        RMS-normalised with that weight (the decoder's fused norm).  NVFP4 layers (an NVFP4 checkpoint)
-        run qmtp_qmv_nvfp4_g16_res."""
+    def _qmv(self, x, lin, y, M, res=None, ldy=None):
+        """4-bit GEMV y = x . W^T (+ res): affine layers on the tensor-core kernel with split tiles
+        (qmtp_qmv_affine_g64_split, one launch per 4 rows), NVFP4 layers (an NVFP4 checkpoint) on
+        qmtp_qmv_nvfp4_g16_res."""
         N, K = lin.out_features, lin.in_features
         ldy = ldy or N
         if self.qmv_log is not None:
-            self.qmv_log.append((x, lin, y, M, res, ldy, pre_w))
+            self.qmv_log.append((x, lin, y, M, res, ldy))
         nv = lin.mode == "nvfp4"
-        if nv and pre_w is not None:
-            raise NotImplementedError("fuse_norm runs the affine kernel's prologue; NVFP4 layers have none")
         self.launches += (M + 3) // 4
         if self.prof is not None:
             e0 = torch.cuda.Event(enable_timing=True)
@@ -163,16 +171,10 @@ class MTPDecoder:
                                                     y.data_ptr(), res.data_ptr() if res is not None else None,
                                                     M, N, K, ldy, self._st()), "qmv")
         else:
-            a = self._qa
-            a.x, a.ldx = x.data_ptr(), K
-            a.w, a.scales, a.biases = lin.weight.data_ptr(), lin.scales.data_ptr(), lin.biases.data_ptr()
-            a.y, a.res = y.data_ptr(), (res.data_ptr() if res is not None else None)
-            a.M, a.N, a.K, a.ldy = M, N, K, ldy
-            if pre_w is not None:
-                a.pre, a.pre_w, a.pre_eps = _lib.QMV_PRE_RMSNORM, pre_w.data_ptr(), self.a.eps
-            else:
-                a.pre, a.pre_w = _lib.QMV_PRE_NONE, None
-            self._chk(self.L.qmtp_qmv_ex(ctypes.byref(a), self._st()), "qmv")
+            self._chk(self.L.qmtp_qmv_affine_g64_split(x.data_ptr(), K, lin.weight.data_ptr(), lin.scales.data_ptr(),
+                                                       lin.biases.data_ptr(), y.data_ptr(),
+                                                       res.data_ptr() if res is not None else None, M, N, K, ldy,
+                                                       self.qws.data_ptr(), self.qws.numel(), self._st()), "qmv")
         if self.prof is not None:
             e1 = torch.cuda.Event(enable_timing=True)
             e1.record()
@@ -199,12 +201,11 @@ class MTPDecoder:
             snap=1)
 
     # ------------------------------------------------------------------ layers
-    def _attn_layer(self, L, x, rows, kc, vc, pos_slot, xin=None, pre_w=None):
+    def _attn_layer(self, L, x, rows, kc, vc, pos_slot):
         """Gated attention block: x (pre-norm residual stream, [rows, H]) += o_proj(attn(...)); the
-        projection input is xin (default: the normalised rows in self.xn), RMS-normalised by pre_w if given."""
+        projection input is the normalised rows in self.xn."""
         a = self.a
-        self._qmv(self.xn if xin is None else xin, L["qkv_proj"], self.proj, rows, ldy=self.proj.shape[1],
-                  pre_w=pre_w)
+        self._qmv(self.xn, L["qkv_proj"], self.proj, rows, ldy=self.proj.shape[1])
         self._chk(self.L.qmtp_attn_prep(self.proj.data_ptr(), self.proj.shape[1], rows, a.n_heads, a.n_kv,
                                         a.head_dim, a.rotary_dim, L["q_norm"].data_ptr(), L["k_norm"].data_ptr(),
                                         a.eps, self.cos.data_ptr(), self.sin.data_ptr(), self._cp(pos_slot), 0,
@@ -217,11 +218,8 @@ class MTPDecoder:
 
     def _mlp(self, L, x, rows):
         a = self.a
-        if self.fuse_norm:
-            self._qmv(x, L["gate_up"], self.gu, rows, pre_w=L["post_ln"])
-        else:
-            self._norm(x, L["post_ln"], self.xn, rows)
-            self._qmv(self.xn, L["gate_up"], self.gu, rows)
+        self._norm(x, L["post_ln"], self.xn, rows)
+        self._qmv(self.xn, L["gate_up"], self.gu, rows)
         self._chk(self.L.qmtp_swiglu(self.gu.data_ptr(), 2 * a.intermediate, rows, a.intermediate,
                                      self.act.data_ptr(), self._st()), "swiglu")
         self._qmv(self.act, L["down"], x, rows, res=x)
@@ -232,13 +230,9 @@ class MTPDecoder:
         self._embed(self.tokens_in.data_ptr(), S, self.h)
         for i in range(a.layers):
             L = W[f"layers.{i}"]
-            if self.fuse_norm:
-                xin, pw = self.h, L["input_ln"]
-            else:
-                self._norm(self.h, L["input_ln"], self.xn, S)
-                xin, pw = self.xn, None
+            self._norm(self.h, L["input_ln"], self.xn, S)
             if a.is_linear(i):
-                self._qmv(xin, L["in_proj"], self.proj, S, ldy=self.proj.shape[1], pre_w=pw)
+                self._qmv(self.xn, L["in_proj"], self.proj, S, ldy=self.proj.shape[1])
                 self._chk(self.L.qmtp_gdn_fused_ex(ctypes.byref(self._gdn_args[i]), self._st()), "gdn")
                 Z = a.lin_hv * a.lin_dv
                 self._chk(self.L.qmtp_gdn_norm_gate(self.ygdn.data_ptr(), self.proj.data_ptr() + 2 * a.conv_dim,
@@ -248,7 +242,7 @@ class MTPDecoder:
                 self._qmv(self.gdn_out, L["out_proj"], self.h, S, res=self.h)
             else:
                 kc, vc = self.kv[i]
-                self._attn_layer(L, self.h, S, kc, vc, C["POS"], xin=xin, pre_w=pw)
+                self._attn_layer(L, self.h, S, kc, vc, C["POS"])
             self._mlp(L, self.h, S)
         self._norm(self.h, W["norm"], self.hn, S)
 
@@ -274,12 +268,8 @@ class MTPDecoder:
                                       self.mcat.data_ptr() + 2 * H, 2 * H, rows, H, self._st()), "rmsnorm")
         self._qmv(self.mcat, M["fc"], self.mx, rows)
         Ly = M["layer"]
-        if self.fuse_norm:
-            self._attn_layer(Ly, self.mx, rows, self.mkv[0], self.mkv[1], C["MPOS"], xin=self.mx,
-                             pre_w=Ly["input_ln"])
-        else:
-            self._norm(self.mx, Ly["input_ln"], self.xn, rows)
-            self._attn_layer(Ly, self.mx, rows, self.mkv[0], self.mkv[1], C["MPOS"])
+        self._norm(self.mx, Ly["input_ln"], self.xn, rows)
+        self._attn_layer(Ly, self.mx, rows, self.mkv[0], self.mkv[1], C["MPOS"])
         self._mlp(Ly, self.mx, rows)
         if not with_draft:
             return
@@ -432,6 +422,17 @@ class MTPDecoder:
         self.graph = g
         return g
 
+    def ensure_graph(self):
+        """Captures the cycle graph if there is none.  Capture needs the library's one-time kernel setup
+        done, so one eager cycle runs first on a copy of the state, which is then put back."""
+        if self.graph is not None:
+            return
+        snap = _snapshot(self)
+        self.run_cycle()
+        _restore(self, snap)
+        self.capture()
+        _restore(self, snap)
+
     def run_cycle(self):
         """One cycle; returns the tokens it emitted (read from the pinned copy of the control block)."""
         if self.graph is not None:
@@ -444,20 +445,30 @@ class MTPDecoder:
         return h[C["EMIT0"]:C["EMIT0"] + keep]
 
 
-def generate_mtp(dec: MTPDecoder, prompt_ids, max_tokens, eos=(), use_graph=True, draft_override=None,
-                 prefix_len=0):
-    """mtp.py:241-303 (greedy, k fixed): returns (tokens, stats).  tok/s excludes the prefill, as the
-    reference does (mtp.py:264,295).  draft_override(cycle) -> k tokens or None replaces the drafts a
-    cycle verifies (test hook for the acceptance / rollback paths).  prefix_len: see MTPDecoder.prefill
-    (stats["cached_tokens"] = prompt tokens resumed from the kept prefix)."""
+def _linears(W):
+    """Every 4-bit linear layer of a weight set (nested dicts of tensors and QuantizedLinear)."""
+    from .qmv_kernel import QuantizedLinear
+
+    out, todo = [], [W]
+    while todo:
+        for v in todo.pop().values():
+            if isinstance(v, QuantizedLinear):
+                out.append(v)
+            elif isinstance(v, dict):
+                todo.append(v)
+    return out
+
+
+def decode_mtp(dec: MTPDecoder, prompt_ids, max_tokens, eos=(), use_graph=True, draft_override=None,
+               prefix_len=0):
+    """The loop of mtp.py:241-303 on a decoder (greedy or the decoder's sampling, k fixed): returns
+    (tokens, stats).  tok/s excludes the prefill, as the reference does (mtp.py:264,295).
+    draft_override(cycle) -> k tokens or None replaces the drafts a cycle verifies (test hook for the
+    acceptance / rollback paths).  prefix_len: see MTPDecoder.prefill (stats["cached_tokens"] = prompt
+    tokens resumed from the kept prefix)."""
     t = dec.prefill(prompt_ids, prefix_len)
-    if use_graph and dec.graph is None:
-        # capture needs the library's one-time kernel setup done: warm up on a scratch copy of state
-        snap = _snapshot(dec)
-        dec.run_cycle()
-        _restore(dec, snap)
-        dec.capture()
-        _restore(dec, snap)
+    if use_graph:
+        dec.ensure_graph()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     out = [t]
@@ -482,6 +493,157 @@ def generate_mtp(dec: MTPDecoder, prompt_ids, max_tokens, eos=(), use_graph=True
              "acept": [n / max(cycles, 1) for n in acc], "borradores_ciclo": float(k), "cycles": cycles,
              "seconds": dt, "cached_tokens": dec.cached_tokens}
     return out, stats
+
+
+# ---------------------------------------------------------------------------------------------------
+# The reference's loop functions with its names and argument order (mtp.py:136-303), over the device
+# state of an MTPDecoder.  `lm` is a qmtp.model.Model; a "cache" (trunk or MTP) is the decoder that
+# lm.make_cache() returns.  They run eagerly, one call at a time, like the reference's; decode_mtp is
+# the graph-captured loop that generate_mtp hands the work to.
+
+
+class DraftHead:
+    """mtp.py:156-167: the cheap head that proposes drafts.  Only the full-vocabulary form exists here
+    (ids=None): the 4-bit affine copy of the lm_head, as the synthetic configuration uses."""
+
+    def __init__(self, proj, ids=None):
+        if ids is not None:
+            raise NotImplementedError("a draft head over a vocabulary subset is not built (full vocabulary only)")
+        self.proj, self.ids = proj, ids
+
+    def __call__(self, x):
+        return self.proj(x)
+
+    def token(self, logits):
+        return torch.argmax(logits, dim=-1)
+
+
+def _check_head(lm, head):
+    if head is not None and getattr(head, "proj", None) is not lm.weights["lm_head_q"]:
+        raise NotImplementedError("the draft head must be the model's 4-bit full-vocabulary head (lm_head_q)")
+
+
+def _check_mtp(lm, mtp):
+    if mtp is not None and mtp is not lm.mtp:
+        raise NotImplementedError("mtp must be the model's own MTP weights (lm.mtp)")
+
+
+def restore(cache: MTPDecoder, keep: int):
+    """mtp.py:136-140: leaves the GatedDeltaNet layers (and here the trunk KV caches too) as if only the
+    first `keep` tokens of the last backbone() step had been processed: the state is ring slot keep of
+    that step and the conv window starts at row keep."""
+    S = getattr(cache, "_last_S", None)
+    if S is None:
+        raise RuntimeError("restore() follows a backbone() step")
+    if not 1 <= keep <= S:
+        raise ValueError(f"keep must be in 1..{S}")
+    c = cache.ctrl.tolist()
+    c[C["SLOT"]] = (c[C["SLOT"]] - S + keep) % cache.slots
+    c[C["CONV_ROW"]] = c[C["CONV_ROW"]] - S + keep
+    c[C["POS"]] = c[C["POS"]] - S + keep
+    c[C["KEEP"]], c[C["SEL"]] = keep, keep - 1
+    cache.ctrl.copy_(torch.tensor(c, dtype=torch.int32))
+    cache._last_S = keep
+
+
+def backbone(lm, tokens, cache: MTPDecoder, last_only=False):
+    """mtp.py:143-153: the trunk over tokens [1, S] (S <= k+1 of the cache): returns (logits, h, hn)
+    with the two-stage head's logits (-inf outside the candidates, lm_head2.py:23-29) and the pre-/
+    post-norm hidden rows.  The step is committed (all S tokens); restore(cache, keep) rolls it back."""
+    t = torch.as_tensor(tokens, dtype=torch.int32).reshape(-1).to(cache.dev)
+    n = t.numel()
+    if not 1 <= n <= cache.S:
+        raise ValueError(f"backbone takes 1..{cache.S} tokens per step with this cache")
+    cache.tokens_in.zero_()
+    cache.tokens_in[:n].copy_(t)
+    cache.backbone()
+    cache._accept(forced_keep=n)
+    cache._last_S = n
+    h, hn = cache.h[:n].clone()[None], cache.hn[:n].clone()[None]
+    logits = lm.lm_head(hn[:, -1:] if last_only else hn)
+    return logits, h, hn
+
+
+def mtp_step(lm, mtp, hidden, tokens, mcache: MTPDecoder, head=None):
+    """mtp.py:199-209: one MTP pass over the pairs (hidden[i], tokens[i]) (the pairs are committed to
+    the MTP cache); returns (logits, x, xn) of the last pair, logits from the draft head."""
+    _check_mtp(lm, mtp)
+    _check_head(lm, head)
+    dec = mcache
+    hid = hidden.reshape(-1, dec.a.hidden)
+    tok = torch.as_tensor(tokens, dtype=torch.int32).reshape(-1).to(dec.dev)
+    n = tok.numel()
+    if hid.shape[0] != n or not 1 <= n <= dec.S:
+        raise ValueError(f"mtp_step takes 1..{dec.S} (hidden, token) pairs with this cache")
+    return _mtp_pairs(dec, hid, tok, commit=True)
+
+
+def _mtp_pairs(dec, hid, tok, commit):
+    n = tok.numel()
+    dec._hstage[:n].copy_(hid)
+    dec.m_tok[:n].copy_(tok)
+    dec._sel.fill_(n - 1)
+    dec.mtp_step(dec._hstage, None, dec.m_tok.data_ptr(), n, dec._sel.data_ptr(), dec.drafts.data_ptr())
+    if commit:
+        dec.ctrl[C["MPOS"]] += n
+    x = dec.mx[n - 1:n].clone()[None]
+    xn = dec.mxn[:1].clone()[None]
+    return dec.dlogits.clone()[None], x, xn
+
+
+def draft_chain(lm, mtp, hidden, tokens, mcache: MTPDecoder, k, head=None, chain="pre", with_probs=False):
+    """mtp.py:212-226: k drafts, the first from the real pairs (hidden, tokens) (committed to the MTP
+    cache), the next ones chained on the MTP's own pre-norm output (not committed, as the reference
+    trims them in the next cycle).  with_probs: also the draft head's probability of each draft."""
+    _check_mtp(lm, mtp)
+    _check_head(lm, head)
+    if chain != "pre":
+        raise NotImplementedError('only chain="pre" is built')
+    dec = mcache
+    hid = hidden.reshape(-1, dec.a.hidden)
+    tok = torch.as_tensor(tokens, dtype=torch.int32).reshape(-1).to(dec.dev)
+    if hid.shape[0] != tok.numel() or not 1 <= tok.numel() <= dec.S:
+        raise ValueError(f"draft_chain takes 1..{dec.S} (hidden, token) pairs with this cache")
+    drafts, probs = [], []
+    logits, x, _ = _mtp_pairs(dec, hid, tok, commit=True)
+    mpos = int(dec.ctrl[C["MPOS"]].item())
+    for i in range(k):
+        if i:
+            logits, x, _ = _mtp_pairs(dec, x[0], drafts[-1].reshape(1), commit=False)
+            dec.ctrl[C["MPOS"]] += 1  # the chained entry is visible to the next chained step
+        drafts.append(torch.argmax(logits[0, -1]).to(torch.int32).reshape(1))
+        if with_probs:
+            probs.append(torch.softmax(logits[0, -1].float(), dim=-1).max().reshape(1))
+    dec.ctrl[C["MPOS"]] = mpos
+    d = torch.cat(drafts)[None]
+    return (d, torch.cat(probs)[None]) if with_probs else d
+
+
+def n_drafts(probs, tau):
+    """mtp.py:229-238: adaptive k -- verify drafts while their cumulative probability stays above tau
+    (at least one)."""
+    n, acc = 0, 1.0
+    for p in probs:
+        acc *= p
+        if n and acc < tau:
+            break
+        n += 1
+    return n
+
+
+def generate_mtp(lm, mtp, prompt_ids, max_tokens, eos, head=None, k=1, bb_hidden="pre", chain="pre", tau=None):
+    """mtp.py:241-303 with the reference's signature: greedy MTP decoding of prompt_ids, returns
+    (tokens, stats).  Runs decode_mtp (the graph-captured loop) on the model's session for this k.
+    bb_hidden and chain must be "pre" and tau None (fixed k): the variants the build implements."""
+    _check_mtp(lm, mtp)
+    _check_head(lm, head)
+    if bb_hidden != "pre" or chain != "pre":
+        raise NotImplementedError('only bb_hidden="pre", chain="pre" are built')
+    if tau is not None:
+        raise NotImplementedError("adaptive k (tau) is not built; the verify step has a fixed k")
+    dec = lm.session(k=k, max_tokens=max_tokens)
+    dec.set_sampling(None)
+    return decode_mtp(dec, prompt_ids, max_tokens, tuple(eos))
 
 
 def _snapshot(dec: MTPDecoder):

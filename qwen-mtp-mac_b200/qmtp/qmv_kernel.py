@@ -5,9 +5,10 @@ Reference: qmv_kernel.py:86-101 (``qmv_nvfp4(x, w, s, rows=None, nsg=1)``), qmv_
 ``quantized_matmul(x, w, scales, biases, transpose=True, group_size=64, bits=4)`` for the affine
 format the B200 build is judged on.
 
-Every call runs the sm_100a kernel of libqmtp (csrc/qmv.cu).  Unlike the reference there is no
-"fall back to the library path" branch: the kernel reads each weight once for any number of rows,
-so ``install`` only records the row window for API compatibility.
+Every call runs an sm_100a kernel of libqmtp: the affine format on the tensor cores (csrc/qmv_tc.cu,
+tcgen05 kind::i8 with exact integer group sums), NVFP4 on the CUDA cores (csrc/qmv.cu).  Unlike the
+reference there is no "fall back to the library path" branch: the kernels read each weight once for
+any number of rows, so ``install`` only records the row window for API compatibility.
 """
 from __future__ import annotations
 
@@ -17,6 +18,22 @@ from . import _lib
 
 MIN_ROWS, MAX_ROWS = 3, 4  # reference defaults (qmv_kernel.py:105); informational here
 GROUP_SIZE = 64
+
+# Split-K workspaces, one per (device, stream): the kernel's tile arrival counters must not be shared by
+# launches that can run at the same time.  Zero-filled once; every launch leaves the counters at zero.
+_WS: dict = {}
+
+
+def workspace(N: int, K: int, device=None) -> torch.Tensor:
+    """The cached split-K workspace of the current stream, grown to cover an N x K matrix."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    need = int(_lib.lib().qmtp_qmv_workspace(N, K))
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=dev)
+        _WS[key] = ws
+    return ws
 
 
 def _flat(x: torch.Tensor):
@@ -42,9 +59,13 @@ def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "
 
 
 def qmv_affine(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
-               group_size: int = 64, out: torch.Tensor | None = None) -> torch.Tensor:
+               group_size: int = 64, out: torch.Tensor | None = None, res: torch.Tensor | None = None,
+               ws: torch.Tensor | None = None, split: bool = True) -> torch.Tensor:
     """y = x @ dequant(w).T for the affine 4-bit group-64 format (bf16 in, bf16 out).
-    x: [..., K] bf16; w: uint32/int32 [N, K/8]; scales, biases: bf16 [N, K/64] -> [..., N]."""
+    x: [..., K] bf16; w: uint32/int32 [N, K/8]; scales, biases: bf16 [N, K/64] -> [..., N].
+    res (bf16, same shape as out): y = bf16(res + bf16(x . W^T)), may alias out.
+    split=True (default) lets CTAs share a tile (needs a workspace: `ws`, or the cached one of the
+    current stream); split=False gives each CTA whole tiles and needs none.  Both give the same bits."""
     if group_size != 64:
         raise NotImplementedError("affine qmv is implemented for group_size=64")
     xf, K = _flat(x)
@@ -52,13 +73,27 @@ def qmv_affine(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: t
     M = xf.shape[0]
     if x.dtype != torch.bfloat16:
         raise ValueError("qmv_affine expects bf16 activations")
-    _lib.require_cuda(xf, w, scales, biases)
+    _lib.require_cuda(xf, w, scales, biases, res)
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
     elif out.dim() != 2 or out.shape[0] != M or out.shape[1] < N or out.dtype != torch.bfloat16:
         raise ValueError("out must be bf16 [M, >=N]")
-    _lib.check(_lib.lib().qmtp_qmv_affine_g64(xf.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
-                                               out.data_ptr(), M, N, K, out.shape[-1], _lib.stream()), "qmv_affine")
+    if res is not None and (res.shape != out.shape or res.dtype != torch.bfloat16):
+        raise ValueError("res must match out")
+    L = _lib.lib()
+    if split:
+        if ws is None:
+            ws = workspace(N, K, x.device)
+        rc = L.qmtp_qmv_affine_g64_split(xf.data_ptr(), K, w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                                         out.data_ptr(), _lib.ptr(res), M, N, K, out.shape[-1], ws.data_ptr(),
+                                         ws.numel() * ws.element_size(), _lib.stream())
+    elif res is not None:
+        rc = L.qmtp_qmv_affine_g64_res(xf.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                                       out.data_ptr(), res.data_ptr(), M, N, K, out.shape[-1], _lib.stream())
+    else:
+        rc = L.qmtp_qmv_affine_g64(xf.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                                   out.data_ptr(), M, N, K, out.shape[-1], _lib.stream())
+    _lib.check(rc, "qmv_affine")
     if out.shape[-1] != N:  # caller-provided wider output (leading dimension ldy > N)
         return out[:, :N]
     return out.reshape(*x.shape[:-1], N)

@@ -16,7 +16,7 @@ _dequant = _ckpt.dequant
 
 def test_loaded_checkpoint_decodes_like_the_oracle(tmp_path, dev):
     from qmtp import loader
-    from qmtp.mtp import MTPDecoder, generate_mtp
+    from qmtp.mtp import MTPDecoder, decode_mtp
 
     a = om.SMALL
     Wn = om.synthetic_weights(a, seed=3)
@@ -34,14 +34,14 @@ def test_loaded_checkpoint_decodes_like_the_oracle(tmp_path, dev):
     want["mtp"] = dict(Wn["mtp"], fc=ops.quantize_affine(dense))
     p = prompt(40, seed=7)
     ref, _ = om.OracleModel(a, want).generate_mtp(p, 30)
-    out, st = generate_mtp(MTPDecoder(args, W, k=2, max_tokens=300), p, 30)
+    out, st = decode_mtp(MTPDecoder(args, W, k=2, max_tokens=300), p, 30)
     assert out == ref
 
 
 def test_nvfp4_checkpoint_decodes_like_the_oracle(tmp_path, dev):
     """Every linear (and the embedding) in NVFP4, written with Ollama's scale names, loaded and decoded."""
     from qmtp import loader
-    from qmtp.mtp import MTPDecoder, generate_mtp
+    from qmtp.mtp import MTPDecoder, decode_mtp
 
     a = om.SMALL
     Wq = _ckpt.to_nvfp4(om.synthetic_weights(a, seed=3))
@@ -53,7 +53,7 @@ def test_nvfp4_checkpoint_decodes_like_the_oracle(tmp_path, dev):
     assert W["embed"].mode == "nvfp4" and W["layers.0"]["in_proj"].mode == "nvfp4"
     p = prompt(40, seed=8)
     ref, _ = om.OracleModel(a, Wq).generate_mtp(p, 16)
-    out, _ = generate_mtp(MTPDecoder(args, W, k=2, max_tokens=300), p, 16)
+    out, _ = decode_mtp(MTPDecoder(args, W, k=2, max_tokens=300), p, 16)
     assert out == ref
 
 

@@ -29,53 +29,34 @@ def _decoder(W, max_tokens=300):
 
 @pytest.mark.parametrize("use_graph", [False, True])
 def test_stream_matches_oracle(small_pair, use_graph):
-    from qmtp.mtp import generate_mtp
+    from qmtp.mtp import decode_mtp
 
     orc, W = small_pair
     p = prompt(40)
     ref, _ = orc.generate_mtp(p, 30)
-    out, st = generate_mtp(_decoder(W), p, 30, use_graph=use_graph)
+    out, st = decode_mtp(_decoder(W), p, 30, use_graph=use_graph)
     assert out == ref
     assert st["cycles"] >= 1
 
 
 def test_rollback_paths_match_oracle(small_pair):
-    from qmtp.mtp import generate_mtp
+    from qmtp.mtp import decode_mtp
 
     orc, W = small_pair
     p = prompt(34, seed=2)
     g = orc.generate_greedy(p, 45)
     ref, rst = orc.generate_mtp(p, 45, draft_override=greedy_overrides(g, om.SMALL.vocab))
-    out, st = generate_mtp(_decoder(W), p, 45, use_graph=True, draft_override=greedy_overrides(g, om.SMALL.vocab))
+    out, st = decode_mtp(_decoder(W), p, 45, use_graph=True, draft_override=greedy_overrides(g, om.SMALL.vocab))
     assert ref == g and out == ref
     assert st["acept"] == rst["acept"]
 
 
 def test_config4_loop_shape_on_small_model(small_pair):
     """512-token prompt, 256 generated tokens, k = 2 (the config-4 loop) on the small model."""
-    from qmtp.mtp import generate_mtp
+    from qmtp.mtp import decode_mtp
 
     orc, W = small_pair
     p = prompt(512, seed=5)
     ref, _ = orc.generate_mtp(p, 256)
-    out, st = generate_mtp(_decoder(W), p, 256, use_graph=True)
+    out, st = decode_mtp(_decoder(W), p, 256, use_graph=True)
     assert len(out) == 256 and out == ref
-
-
-@pytest.mark.parametrize("use_graph", [False, True])
-def test_fused_norm_stream_matches_oracle(small_pair, use_graph):
-    """Decoder with the input / post-attention RMSNorms fused into the projections' x prologue."""
-    from qmtp import model as qm
-    from qmtp.mtp import MTPDecoder, generate_mtp
-
-    orc, W = small_pair
-    p = prompt(34, seed=2)
-    g = orc.generate_greedy(p, 45)
-    ref, rst = orc.generate_mtp(p, 45, draft_override=greedy_overrides(g, om.SMALL.vocab))
-    dec = MTPDecoder(qm.SMALL, W, k=2, max_tokens=300, fuse_norm=True)
-    out, st = generate_mtp(dec, p, 45, use_graph=use_graph, draft_override=greedy_overrides(g, om.SMALL.vocab))
-    assert out == ref and st["acept"] == rst["acept"]
-    ref2, _ = orc.generate_mtp(p, 30)
-    out2, _ = generate_mtp(MTPDecoder(qm.SMALL, W, k=2, max_tokens=300, fuse_norm=True), p, 30,
-                           use_graph=use_graph)
-    assert out2 == ref2

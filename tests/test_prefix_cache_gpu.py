@@ -26,7 +26,7 @@ def _fresh(W, sampling=None):
 
 @pytest.mark.parametrize("sampled", [False, True])
 def test_prefix_reuse_matches_fresh_prefill(small, sampled):
-    from qmtp.mtp import Sampling, generate_mtp
+    from qmtp.mtp import Sampling, decode_mtp
 
     orc, W = small
     sp = Sampling(temperature=0.9, top_p=0.95, seed=21) if sampled else None
@@ -41,9 +41,9 @@ def test_prefix_reuse_matches_fresh_prefill(small, sampled):
              (base + ext + tails[3], 38, 38),     # resumes from the extended prefix
              (base[:20] + tails[0], 20, 0)]       # shares less than the kept prefix: fresh prefill
     for i, (p, pl, cached) in enumerate(cases):
-        out, st = generate_mtp(dec, p, 24, prefix_len=pl, use_graph=i % 2 == 0)
+        out, st = decode_mtp(dec, p, 24, prefix_len=pl, use_graph=i % 2 == 0)
         assert st["cached_tokens"] == cached, (i, st["cached_tokens"])
-        ref, _ = generate_mtp(_fresh(W, sp), p, 24)
+        ref, _ = decode_mtp(_fresh(W, sp), p, 24)
         assert out == ref, i
         if i == 1:
             want, _ = orc.generate_mtp(p, 24, sampling=sp)

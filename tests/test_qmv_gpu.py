@@ -12,40 +12,134 @@ pytestmark = pytest.mark.gpu
 G = Path(__file__).resolve().parent / "golden"
 
 
-def _run_affine(x, wq, s, b, dev, ldy=None):
+def _run_affine(x, wq, s, b, dev, ldy=None, split=True, res=None):
     from qmtp import qmv_kernel
 
     xt, wt, st, bt = (to_torch(a, dev) for a in (x, wq, s, b))
-    if ldy is None:
-        return to_np(qmv_kernel.qmv_affine(xt, wt, st, bt))
-    out = torch.full((x.shape[0], ldy), 7.0, dtype=torch.bfloat16, device=dev)
-    qmv_kernel.qmv_affine(xt, wt, st, bt, out=out)
+    rt = None if res is None else to_torch(res, dev)
+    if ldy is None and rt is None:
+        return to_np(qmv_kernel.qmv_affine(xt, wt, st, bt, split=split))
+    out = torch.full((x.shape[0], ldy or wq.shape[0]), 7.0, dtype=torch.bfloat16, device=dev)
+    if rt is not None:
+        out.copy_(rt)
+    qmv_kernel.qmv_affine(xt, wt, st, bt, out=out, res=out if rt is not None else None, split=split)
     return to_np(out)
 
 
-@pytest.mark.parametrize("K", [1024, 2048, 4096, 8192, 12288])
+@pytest.mark.parametrize("K", [512, 1024, 2048, 4096, 8192, 12288])
 @pytest.mark.parametrize("M", [1, 2, 3, 4])
 def test_qmv_affine_bit_exact(K, M, dev):
-    for N in (1, 37, 1000):
+    for N in (1, 37, 1000, 4096):
         _, wq, s, b = affine_layer(N, K, seed=K + N)
         x = randn_bf16((M, K), M)
-        assert np.array_equal(_run_affine(x, wq, s, b, dev), ops.qmv_affine(x, wq, s, b)), (K, M, N)
+        ref = ops.qmv_affine(x, wq, s, b)
+        for split in (True, False):
+            assert np.array_equal(_run_affine(x, wq, s, b, dev, split=split), ref), (K, M, N, split)
+
+
+def test_qmv_affine_shared_workspace_across_shapes(dev):
+    """One workspace serves matrices of every shape in turn (the decoder's use): the slice partials
+    of a large matrix never disturb the tile counters of a smaller one."""
+    from qmtp import qmv_kernel, _lib
+
+    ws = torch.zeros(_lib.lib().qmtp_qmv_workspace(24576, 4096), dtype=torch.uint8, device=dev)
+    cases = []
+    for N, K in ((24576, 4096), (1, 2048), (4096, 12288), (37, 4096), (12352, 4096), (5, 8192)):
+        _, wq, s, b = affine_layer(N, K, seed=N ^ K)
+        x = randn_bf16((3, K), N + 1)
+        cases.append((x, wq, s, b, ops.qmv_affine(x, wq, s, b)))
+    for _ in range(2):
+        for x, wq, s, b, ref in cases:
+            xt, wt, st, bt = (to_torch(a, dev) for a in (x, wq, s, b))
+            assert np.array_equal(to_np(qmv_kernel.qmv_affine(xt, wt, st, bt, ws=ws)), ref), wq.shape
 
 
 @pytest.mark.parametrize("M", [1, 2, 3, 4])
 def test_qmv_affine_config1_bit_exact(M, dev):
     _, wq, s, b = affine_layer(12288, 4096, seed=0)
     x = randn_bf16((M, 4096), 1)
-    assert np.array_equal(_run_affine(x, wq, s, b, dev), ops.qmv_affine(x, wq, s, b))
+    ref = ops.qmv_affine(x, wq, s, b)
+    for split in (True, False):
+        assert np.array_equal(_run_affine(x, wq, s, b, dev, split=split), ref)
+
+
+@pytest.mark.parametrize("N,K", [(12352, 4096), (4096, 4096), (4096, 12288), (24576, 4096), (10240, 4096),
+                                 (4096, 8192), (777, 12288)])
+def test_qmv_affine_decoder_shapes_split(N, K, dev):
+    """The decoder's projection shapes: split tiles (slice partials finished by the last CTA) give the
+    oracle's bits, the workspace counters return to zero, and repeated calls agree."""
+    from qmtp import qmv_kernel, _lib
+
+    _, wq, s, b = affine_layer(N, K, seed=N + K)
+    x = randn_bf16((3, K), 5)
+    ref = ops.qmv_affine(x, wq, s, b)
+    ws = torch.zeros(_lib.lib().qmtp_qmv_workspace(N, K), dtype=torch.uint8, device=dev)
+    xt, wt, st, bt = (to_torch(a, dev) for a in (x, wq, s, b))
+    for _ in range(3):
+        got = to_np(qmv_kernel.qmv_affine(xt, wt, st, bt, ws=ws))
+        assert np.array_equal(got, ref), (N, K)
+    plan = _lib.qmv_plan(N, K, True)
+    T = (N + plan["rows_per_tile"] - 1) // plan["rows_per_tile"]
+    head = ws.view(torch.int32)[:16384]
+    assert int(head.abs().sum()) == 0, "arrival counters left non-zero"
+    assert plan["units"] == T * (K // 512)
+
+
+def test_qmv_affine_residual_in_place(dev):
+    _, wq, s, b = affine_layer(4096, 12288, seed=3)
+    x = randn_bf16((3, 12288), 4)
+    res = randn_bf16((3, 4096), 6)
+    y = ops.qmv_affine(x, wq, s, b)
+    ref = ops.f32_to_bf16(ops.bf16_to_f32(res) + ops.bf16_to_f32(y))
+    for split in (True, False):
+        assert np.array_equal(_run_affine(x, wq, s, b, dev, split=split, res=res), ref)
 
 
 def test_qmv_affine_many_rows_and_ldy(dev):
     _, wq, s, b = affine_layer(333, 4096, seed=11)
     x = randn_bf16((9, 4096), 12)
     ref = ops.qmv_affine(x, wq, s, b)
-    got = _run_affine(x, wq, s, b, dev, ldy=400)
-    assert np.array_equal(got[:, :333], ref)
-    assert np.all(got[:, 333:] == ops.f32_to_bf16(np.float32([7.0]))[0])
+    for split in (True, False):
+        got = _run_affine(x, wq, s, b, dev, ldy=400, split=split)
+        assert np.array_equal(got[:, :333], ref)
+        assert np.all(got[:, 333:] == ops.f32_to_bf16(np.float32([7.0]))[0])
+
+
+def test_qmv_affine_extreme_x_bit_exact(dev):
+    """Activations over bf16's whole finite range, all-zero groups, subnormal-only groups, and a group
+    holding an infinity (its token row becomes NaN, the others are unaffected)."""
+    r = np.random.default_rng(31)
+    M, K, N = 4, 4096, 700
+    sign = r.integers(0, 2, (M, K)).astype(np.uint16) << 15
+    man = r.integers(0, 128, (M, K)).astype(np.uint16)
+    kind = r.integers(0, 4, (M, K))
+    exp = np.where(kind == 0, 0, np.where(kind == 1, r.integers(1, 12, (M, K)),
+                   np.where(kind == 2, r.integers(110, 140, (M, K)), r.integers(200, 254, (M, K))))).astype(np.uint16)
+    x = sign | (exp << 7) | man
+    x[0, 0:64] = 0
+    x[1, 512:576] = man[1, 512:576] | sign[1, 512:576]
+    x[2, 1000] = 0x7F80
+    _, wq, s, b = affine_layer(N, K, seed=8)
+    ref = ops.qmv_affine(x, wq, s, b)
+    assert np.isnan(ops.bf16_to_f32(ref[2])).all()
+    for split in (True, False):
+        assert np.array_equal(_run_affine(x, wq, s, b, dev, split=split), ref)
+
+
+def test_qmv_affine_split_ldx(dev):
+    from qmtp import _lib
+
+    N, K, ldx = 1500, 4096, 4096 + 64
+    _, wq, s, b = affine_layer(N, K, seed=12)
+    xw = randn_bf16((3, ldx), 13)
+    ref = ops.qmv_affine(np.ascontiguousarray(xw[:, :K]), wq, s, b)
+    xt, wt, st, bt = (to_torch(a, dev) for a in (xw, wq, s, b))
+    y = torch.empty((3, N), dtype=torch.bfloat16, device=dev)
+    ws = torch.zeros(_lib.lib().qmtp_qmv_workspace(N, K), dtype=torch.uint8, device=dev)
+    _lib.check(_lib.lib().qmtp_qmv_affine_g64_split(xt.data_ptr(), ldx, wt.data_ptr(), st.data_ptr(), bt.data_ptr(),
+                                                   y.data_ptr(), None, 3, N, K, N, ws.data_ptr(), ws.numel(),
+                                                   _lib.stream()), "split")
+    assert np.array_equal(to_np(y), ref)
 
 
 def test_qmv_affine_golden(dev):
@@ -104,12 +198,14 @@ def test_qmv_rejects_bad_shapes(dev):
     x = torch.zeros(2, 1000, dtype=torch.bfloat16, device=dev)
     w = torch.zeros(8, 125, dtype=torch.int32, device=dev)
     s = torch.zeros(8, 16, dtype=torch.bfloat16, device=dev)
-    with pytest.raises(ValueError):
-        qmv_kernel.qmv_affine(x, w, s, s)
+    for split in (True, False):
+        with pytest.raises(ValueError):
+            qmv_kernel.qmv_affine(x, w, s, s, split=split)
     xb = torch.zeros(2 * 1024 + 1, dtype=torch.bfloat16, device=dev)[1:].view(2, 1024)  # 2-byte offset
     w = torch.zeros(8, 128, dtype=torch.int32, device=dev)
-    with pytest.raises(ValueError):
-        qmv_kernel.qmv_affine(xb, w, s, s)
+    for split in (True, False):
+        with pytest.raises(ValueError):
+            qmv_kernel.qmv_affine(xb, w, s, s, split=split)
 
 
 def test_no_device_error_recorded(dev):

@@ -89,7 +89,7 @@ def small_pair():
 ])
 def test_sampled_stream_matches_oracle(small_pair, sp, use_graph, override):
     from qmtp import model as qm
-    from qmtp.mtp import MTPDecoder, Sampling, generate_mtp
+    from qmtp.mtp import MTPDecoder, Sampling, decode_mtp
 
     orc, W = small_pair
     p = prompt(37, seed=4)
@@ -97,7 +97,7 @@ def test_sampled_stream_matches_oracle(small_pair, sp, use_graph, override):
     s = Sampling(**sp)
     ref, rst = orc.generate_mtp(p, 40, sampling=s, draft_override=ov())
     dec = MTPDecoder(qm.SMALL, W, k=2, max_tokens=300, sampling=s)
-    out, st = generate_mtp(dec, p, 40, use_graph=use_graph, draft_override=ov())
+    out, st = decode_mtp(dec, p, 40, use_graph=use_graph, draft_override=ov())
     assert out == ref
     assert st["acept"] == rst["acept"]
     if override:

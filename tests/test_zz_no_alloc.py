@@ -57,6 +57,28 @@ def test_noalloc_head_matches_workspace_head_twice(dev):
         assert (got[0] >= 0).all() and (got[2] >= 0).all()
 
 
+def test_noalloc_head_largest_request_matches_workspace_head(dev):
+    """The largest request the scratch is sized for (M = 4, V = 262144, k = 64) against the
+    workspace head, bit for bit, twice; one vocabulary row more is refused."""
+    from qmtp import _lib
+
+    V, D, k = 262144, 512, 64
+    W, wq, s, b = _head_inputs(V, D, dev, 5)
+    ws = torch.empty(_lib.lib().qmtp_lmhead2_workspace(4, V, k), dtype=torch.uint8, device=dev)
+    for seed in (21, 22):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        h = torch.randn(4, D, generator=g, device=dev).to(torch.bfloat16)
+        ref = _run("qmtp_lmhead2", h, W, wq, s, b, k, dev, ws)
+        got = _run("qmtp_lmhead2_noalloc", h, W, wq, s, b, k, dev)
+        for r, x in zip(ref, got):
+            assert torch.equal(r, x), seed
+    W1, wq1, s1, b1 = _head_inputs(V + 1, D, dev, 6)
+    with pytest.raises(ValueError):
+        _run("qmtp_lmhead2_noalloc", h, W1, wq1, s1, b1, k, dev)
+    assert _lib.device_error() == 0
+
+
 def test_noalloc_head_rejects_sizes_beyond_its_scratch(dev):
     from qmtp import _lib
 
