@@ -16,8 +16,10 @@ k = 2 drafts, batch 1) after a 512-token uniform-random prompt.  Prints one JSON
              state on the host cores (bounded sample), with a token-for-token parity check.
 
 --impl reference: the reference's CPU path restated by the oracle (the reference itself is MLX +
-Metal and cannot run here), full-size weights, a short prompt, W + K cycles on all host cores.
-Multi-GPU: replicas (batch-1 decoding does not shard); every rank decodes its own prompt.
+Metal and cannot run here), full-size weights, the same 512-token prompt (prefilled in one oracle
+pass), W + K cycles on all host cores.
+Multi-GPU: replicas of the decode (batch-1 decoding does not shard; every rank decodes its own
+prompt), and in the same line ("moe_ep") config 5's MoE layer expert-parallel over the same ranks.
 """
 from __future__ import annotations
 
@@ -145,7 +147,8 @@ def run_ours(args):
     K, Wu = args.steps, args.warmup
     sp = (Sampling(args.temperature, args.top_k, args.top_p, args.min_p, args.seed) if args.temperature > 0
           else None)
-    dec = MTPDecoder(cfg, W, k=K_DRAFTS, max_tokens=Wu + 3 * K + 64, device=dev,
+    gen_tokens = 256  # config 4 generates 256 tokens; the e2e leg decodes all of them
+    dec = MTPDecoder(cfg, W, k=K_DRAFTS, max_tokens=max(Wu + 3 * K + 64, gen_tokens + 64), device=dev,
                      sampling=sp)
 
     # ---- prefill, one eager cycle (library setup), capture
@@ -220,8 +223,7 @@ def run_ours(args):
         tokens_all = float(tokens)
     value = tokens_all / (elapsed_ms / 1e3)
 
-    # ---- e2e: the public decode_mtp call (per-cycle host sync + control-block read)
-    gen_tokens = min(256, Wu + K)
+    # ---- e2e: the public decode_mtp call (per-cycle host sync + control-block read), config 4's 256 tokens
     out, st = decode_mtp(dec, prompt, gen_tokens, use_graph=True)
     e2e_tps = st["tps"]
     if world > 1:
@@ -260,7 +262,10 @@ def run_ours(args):
                                                              "top_p": sp.top_p, "min_p": sp.min_p,
                                                              "seed": sp.seed, "head_candidates": dec.K}})},
            "e2e": {"value": round(e2e_tps, 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
-                   "d2h_bytes_per_step": 4 * _lib.CTRL_SIZE, "tokens": len(out)},
+                   "d2h_bytes_per_step": 4 * _lib.CTRL_SIZE, "tokens": len(out),
+                   "h2d_note": "a decode cycle takes no host input: the prompt is copied once before the "
+                               "timed region and every later token is produced on the device; each cycle "
+                               "reads the 128-byte control block (emitted tokens) back to the host"},
            "roofline": roofline, "clocks": clocks, "gpu_launches": launches_per_cycle * K,
            "stats": {"tokens_timed": int(tokens_all), "tok_per_cycle": round(tokens / K, 4),
                      "acceptance": st["acept"], "first_token": t}}
@@ -269,8 +274,13 @@ def run_ours(args):
     if post_prefill is not None:
         res["cpu_baseline"] = cpu_baseline_from_state(cfg, W, post_prefill, gpu_stream, args.cpu_cycles, sp)
     if world > 1:
+        # the sharded workload of the build: config 5's MoE layer expert-parallel over the same ranks
         dist.barrier()
         dec.graph = None
+        del dec, W
+        torch.cuda.empty_cache()
+        res["moe_ep"] = moe_ep_measure(args, dev, rank, world)
+        dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res), flush=True)
@@ -433,15 +443,26 @@ def run_moe_ep(args):
     import torch
     import torch.distributed as dist
 
-    from qmtp import _lib, moe
-    from qmtp.moe_ep import ExpertParallelMoE, local_expert_table
-
     world = int(os.environ["WORLD_SIZE"])
     rank = int(os.environ["RANK"])
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    out = moe_ep_measure(args, dev, rank, world)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    dist.destroy_process_group()
+
+
+def moe_ep_measure(args, dev, rank, world):
+    """Config 5 expert-parallel layer over the initialised process group; returns the line (rank 0)."""
+    import torch
+    import torch.distributed as dist
+
+    from qmtp import _lib, moe
+    from qmtp.moe_ep import ExpertParallelMoE, local_expert_table
+
     mode = args.shape if args.shape in ("mxfp4", "nvfp4") else "mxfp4"
     E_R, NSH, H, I, T, TOPK = 64, 2, 2048, 1408, 256, 6
     g = torch.Generator(device=dev)
@@ -497,16 +518,15 @@ def run_moe_ep(args):
     dist.barrier()
     Gs = 32 if mode == "mxfp4" else 16
     wbytes = (E_R // world + NSH) * 3 * H * I * (0.5 + 1 / Gs)
-    if rank == 0:
-        us = float(ms.item()) * 1e3
-        print(json.dumps({"kernel": "moe_ep", "workload": f"MoE config5 {mode} expert-parallel: {world} GPUs x T={T}",
-                          "n_gpus": world, "us_per_layer": round(us, 2), "tokens_per_s": round(world * T / (us * 1e-6), 1),
-                          "local_weight_bytes": int(wbytes), "local_weight_GBps": round(wbytes / (us * 1e-6) / 1e9, 1),
-                          "steps": args.steps, "scaling": "weak",
-                          "dispatch": f"fixed capacity {cap} rows per peer (exact bound {T * TOPK}), no host sync, "
-                                      "one CUDA graph per layer",
-                          "device_error": int(derr.item())}), flush=True)
-    dist.destroy_process_group()
+    us = float(ms.item()) * 1e3
+    return {"kernel": "moe_ep", "workload": f"MoE config5 {mode} expert-parallel: {world} GPUs x T={T}",
+            "n_gpus": world, "us_per_layer": round(us, 2), "tokens_per_s": round(world * T / (us * 1e-6), 1),
+            "local_weight_bytes": int(wbytes), "local_weight_GBps": round(wbytes / (us * 1e-6) / 1e9, 1),
+            "steps": args.steps, "scaling": "weak",
+            "dispatch": f"fixed capacity {cap} rows per peer (exact bound {T * TOPK}), no host sync, "
+                        "one CUDA graph per layer",
+            "timing": "CUDA events around graph replays, max over ranks",
+            "device_error": int(derr.item())}
 
 
 # ------------------------------------------------------------------------------ reference arm
@@ -524,7 +544,7 @@ def run_reference(args):
     Wn = om.synthetic_weights_fast(cfg, seed=0)
     build_s = time.time() - t0
     orc = om.OracleModel(cfg, Wn)
-    prompt = np.random.default_rng(1000).integers(0, cfg.vocab, args.ref_prompt).astype(np.int32)
+    prompt = np.random.default_rng(1000).integers(0, cfg.vocab, args.prompt).astype(np.int32)
     t1 = time.time()
     cache, mcache, t, drafts = orc.prefill(prompt, K_DRAFTS)
     prefill_s = time.time() - t1
@@ -538,10 +558,10 @@ def run_reference(args):
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
            "impl": "reference",
            "config": {"workload": "config4 (same model shapes, 4-bit affine g64, k=2, batch 1) on the host CPU",
-                      "prompt_tokens": int(args.ref_prompt), "weights": "synthetic_weights_fast (timing-equivalent)",
+                      "prompt_tokens": int(args.prompt), "weights": "synthetic_weights_fast (timing-equivalent)",
                       "weights_build_s": round(build_s, 1), "prefill_s": round(prefill_s, 1)},
            "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port",
-                            "sample": f"{args.ref_prompt}-token prompt, {Wu} warm-up + {K} timed decode cycles "
+                            "sample": f"{args.prompt}-token prompt, {Wu} warm-up + {K} timed decode cycles "
                                       f"({st2['tokens']} tokens) of the oracle restatement (MLX reference not runnable)"},
            "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(res), flush=True)
@@ -554,7 +574,6 @@ def main():
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-cycles", type=int, default=3, help="oracle cycles for cpu_baseline (0 = skip)")
-    ap.add_argument("--ref-prompt", type=int, default=16)
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens (ours)")
     ap.add_argument("--weights", default="affine", choices=["affine", "nvfp4"],
                     help="decode: 4-bit format of the linears (affine g64 = config 4; nvfp4 = the Ollama blobs' format)")
@@ -582,8 +601,6 @@ def main():
     if args.impl == "reference":
         args.steps = 3 if args.steps is None else args.steps
         args.warmup = 1 if args.warmup is None else args.warmup
-        args.steps = min(args.steps, 12)
-        args.warmup = min(args.warmup, 3)
         run_reference(args)
     else:
         args.steps = 253 if args.steps is None else args.steps

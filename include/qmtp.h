@@ -96,6 +96,25 @@ int qmtp_quantize_affine_g64(const void* w, void* wq, void* scales, void* biases
                              void* stream);
 
 /* --------------------------------------------------------------------------------------------
+ * Diagnostics (no counterpart in the reference; they let the test suite reach device building blocks).
+ * qmtp_math_eval: out[i] = f(bf16 x[i]) as fp32 for the device functions every kernel shares: the
+ * library's exp and log, and the bf16 activation formulas of gdn_fused.py:22-41 (sigmoid, silu,
+ * softplus with a bf16 rounding after every op) plus the fp32 silu.  x bf16 [n], out fp32 [n]. */
+#define QMTP_MATH_EXP 0
+#define QMTP_MATH_LOG 1
+#define QMTP_MATH_SIGMOID_BF 2
+#define QMTP_MATH_SILU_BF 3
+#define QMTP_MATH_SOFTPLUS_BF 4
+#define QMTP_MATH_SILU_F32 5
+int qmtp_math_eval(int fn, const void* x, int n, float* out, void* stream);
+
+/* qmtp_wait_selftest: one kernel waits on an mbarrier phase that never completes, with the bounded
+ * wait every kernel of the library uses, limited to `limit` polls (1 .. 2^20).  The wait gives up,
+ * records bit 0 (timeout) in the device error word and writes 0 to *result (device int); the kernel
+ * returns normally.  Shows that a wait that runs out ends the kernel instead of hanging the GPU. */
+int qmtp_wait_selftest(unsigned limit, int* result, void* stream);
+
+/* --------------------------------------------------------------------------------------------
  * GatedDeltaNet recurrent step with per-token state snapshots: gdn_kernel.py:75-88
  * gated_delta_snapshot(q, k, v, g, beta, state) -> (y, state_out, state_mid).
  *   q, k bf16 [B, T, Hk, Dk]; v bf16 [B, T, Hv, Dv]; g, beta fp32 [B, T, Hv];

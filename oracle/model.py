@@ -423,6 +423,89 @@ def synthetic_weights(args: ModelArgs, seed: int = 0, std: float = 0.02) -> dict
     return W
 
 
+def synthetic_weights_seeded(args: ModelArgs, seed: int = 0, std: float = 0.02, threads: int | None = None) -> dict:
+    """Full-size seeded random-init weights, reproducible on any machine and generated in parallel:
+    the tensors are listed in a fixed order and cut into chunks of at most 2^24 elements; chunk i of
+    the list draws from np.random.default_rng(SeedSequence(seed).spawn(n)[i]).  Distributions as
+    synthetic_weights (linear N(0, std) -> affine g64 by the oracle quantizer, norms 1, conv
+    N(0, 1/KC), A_log = log U(1, 16), dt_bias N(0, 1)); the numbers differ from synthetic_weights'."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+
+    a = args
+    specs = []  # (path, kind, shape, scale)
+    ones = lambda n: ops.f32_to_bf16(np.ones(n, np.float32))
+
+    def lin(path, n, k):
+        specs.append((path, "lin", (n, k), std))
+
+    def bf(path, shape, scale):
+        specs.append((path, "bf", shape, scale))
+
+    lin(("embed",), a.vocab, a.hidden)
+    for i in range(a.layers):
+        L = f"layers.{i}"
+        lin((L, "gate_up"), 2 * a.intermediate, a.hidden)
+        lin((L, "down"), a.hidden, a.intermediate)
+        if a.is_linear(i):
+            lin((L, "in_proj"), a.gdn_proj, a.hidden)
+            bf((L, "conv1d"), (a.conv_dim, a.conv_k), 1.0 / np.sqrt(a.conv_k))
+            specs.append(((L, "A_log"), "alog", (a.lin_hv,), 0.0))
+            bf((L, "dt_bias"), (a.lin_hv,), 1.0)
+            lin((L, "out_proj"), a.hidden, a.lin_hv * a.lin_dv)
+        else:
+            lin((L, "qkv_proj"), a.attn_proj, a.hidden)
+            lin((L, "o_proj"), a.hidden, a.n_heads * a.head_dim)
+    bf(("lm_head",), (a.vocab, a.hidden), std)
+    lin(("mtp", "fc"), a.hidden, 2 * a.hidden)
+    for name, n, k in (("qkv_proj", a.attn_proj, a.hidden), ("o_proj", a.hidden, a.n_heads * a.head_dim),
+                       ("gate_up", 2 * a.intermediate, a.hidden), ("down", a.hidden, a.intermediate)):
+        lin(("mtp", "layer", name), n, k)
+
+    CH = 1 << 24
+    chunks = []  # (spec index, flat start, flat end)
+    for si, (_, _, shape, _) in enumerate(specs):
+        n = int(np.prod(shape))
+        chunks += [(si, o, min(o + CH, n)) for o in range(0, n, CH)]
+    seeds = np.random.SeedSequence(seed).spawn(len(chunks))
+    bufs = [np.empty(int(np.prod(sp[2])), np.uint16 if sp[1] != "alog" else np.float32) for sp in specs]
+
+    def fill(ci):
+        si, o0, o1 = chunks[ci]
+        _, kind, _, scale = specs[si]
+        rng = np.random.default_rng(seeds[ci])
+        if kind == "alog":
+            bufs[si][o0:o1] = np.log(rng.uniform(1, 16, o1 - o0)).astype(np.float32)
+        else:
+            bufs[si][o0:o1] = ops.f32_to_bf16(rng.standard_normal(o1 - o0, dtype=np.float32) * np.float32(scale))
+
+    with ThreadPoolExecutor(threads or os.cpu_count()) as ex:
+        list(ex.map(fill, range(len(chunks))))
+    W = {"mtp": {"layer": {}}}
+    for (path, kind, shape, _), buf in zip(specs, bufs):
+        v = buf.reshape(shape)
+        if kind == "lin":
+            v = ops.quantize_affine(v)
+        d = W
+        for key in path[:-1]:
+            d = d.setdefault(key, {})
+        d[path[-1]] = v
+    W["lm_head_q"] = ops.quantize_affine(W["lm_head"])
+    W["norm"] = ones(a.hidden)
+    for i in range(a.layers):
+        L = W[f"layers.{i}"]
+        L.update(input_ln=ones(a.hidden), post_ln=ones(a.hidden))
+        if a.is_linear(i):
+            L["norm"] = ones(a.lin_dv)
+        else:
+            L.update(q_norm=ones(a.head_dim), k_norm=ones(a.head_dim))
+    M = W["mtp"]
+    M.update(pre_fc_norm_embedding=ones(a.hidden), pre_fc_norm_hidden=ones(a.hidden), norm=ones(a.hidden))
+    M["layer"].update(input_ln=ones(a.hidden), post_ln=ones(a.hidden), q_norm=ones(a.head_dim),
+                      k_norm=ones(a.head_dim))
+    return W
+
+
 def synthetic_weights_fast(args: ModelArgs, seed: int = 0, std: float = 0.02) -> dict:
     """Full-size random weights for CPU timing runs: packed nibbles drawn uniformly and per-group
     scales / biases with the magnitudes an N(0, std) group quantizes to ((max-min)/15 ~ 0.3*std,

@@ -55,10 +55,11 @@ constexpr int kMaxTok = 4;                         // tokens per launch (3 limbs
 constexpr int kXSlot = kGpu * kMaxTok * 8;         // per slot: [group][token] float2 (c, xf)
 constexpr int kOffB = kNS * kStage;                // 147456
 constexpr int kOffX = kOffB + kNB * kBSlot;        // 212992
-constexpr int kOffBar = kOffX + kNB * kXSlot;      // 215040
+constexpr int kOffH = kOffX + kNB * kXSlot;        // 215040: chain-1 partials [2][kMaxTok][128] fp32
+constexpr int kOffBar = kOffH + 2 * kMaxTok * 128 * 4;  // 219136
 constexpr int kSmemUsed = kOffBar + 512;
 constexpr int kSmem = kSmemUsed + 1024;            // slack for 1024-byte alignment of the base
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;                      // 12 warps
 constexpr int kTmemCols = 512;
 constexpr int kABase = 0, kDBase = 256;
 constexpr int kMinRows = 64;                       // smallest tile the planner picks (workspace bound)
@@ -68,11 +69,15 @@ constexpr size_t kCntBytes = 65536;                // 16384 counters: tiles of u
 constexpr long long kMaxSplitTiles = kCntBytes / 4;
 static_assert(kOffB % 1024 == 0 && kStage % 1024 == 0, "stage alignment");
 
+// Barriers.  Per unit j: weight stage j % kNS (full / empty); A and accumulator slot a = j & 1 per
+// chain h (afull / dfull / dempty [h][a]); activation operand slot (bfull / bempty); the chain-1 partial
+// buffer j & 1 handed from the chain-1 workers to the chain-0 workers (hfull / hempty).
 struct Bars {
   uint64_t full[kNS], empty[kNS];
-  uint64_t afull[2], dfull[2], dempty[2];
+  uint64_t afull[2][2], dfull[2][2], dempty[2][2];
   uint64_t bfull[kNB], bempty[kNB];
-  uint64_t drain;
+  uint64_t hfull[2], hempty[2];
+  uint64_t drain[2];
   uint32_t tmem;
   int abort;
   int last;
@@ -87,8 +92,19 @@ struct Params {
   float* part;        // split mode: slice partials [ntiles][NSL][kMaxTok][128]
   unsigned* cnt;      // split mode: arrival count per tile (0 between launches)
   unsigned* err;
-  long long U;        // units = ntiles * NSL
+  int U;              // units = ntiles * NSL (U * gridDim.x < 2^31, checked by the host)
   int ldy, N, K, NSL, R, ntiles, whole;
+};
+
+// (tile, slice) of consecutive units, advanced without divisions.
+struct UnitCursor {
+  int tile, sl;
+  __device__ __forceinline__ void next(int NSL) {
+    if (++sl == NSL) {
+      sl = 0;
+      ++tile;
+    }
+  }
 };
 
 // D (TMEM, s32) (+)= A (TMEM, s8 rows) x B (shared memory, s8, K-major).  No "memory" clobber: the
@@ -109,27 +125,87 @@ __device__ __forceinline__ float pow2f(int k) {
   if (k >= -149) return __uint_as_float(1u << (k + 149));
   return 0.0f;
 }
-// |x| of bf16 bits a (sign cleared) on the grid 2^(E-19), rounded to nearest even.
-__device__ __forceinline__ int grid_mag(uint32_t a, int E) {
-  const int ef = int(a >> 7);
-  const int sig = ef ? int(128u | (a & 127u)) : int(a & 127u);
-  const int ex = ef ? ef - 134 : -133;
-  const int sh = ex + 19 - E;
-  if (sh >= 0) return sig << sh;
-  const int r = -sh;
-  if (r > 8) return 0;
-  int m = sig >> r;
-  const int rem = sig & ((1 << r) - 1), half = 1 << (r - 1);
-  if (rem > half || (rem == half && (m & 1))) ++m;
-  return m;
+// x * 2^(19-E) rounded to the nearest integer (ties to even).  The scaling is split into two powers
+// of two that are normal fp32 numbers; bf16 x has 8 significant bits and |x| < 2^(E+1), so both
+// products are exact whenever the result is at least 1/2 in magnitude (a product that underflows
+// belongs to an element that rounds to 0 either way), and the conversion does the one rounding.
+__device__ __forceinline__ int grid_value(uint32_t h, float s1, float s2) {
+  return __float2int_rn(__fmul_rn(__fmul_rn(bf2f(uint16_t(h)), s1), s2));
 }
-__device__ __forceinline__ void bar_workers() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-__device__ __forceinline__ float ld_cg_f32(const float* p) {
-  float v;
-  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
-  return v;
+__device__ __forceinline__ void bar_chain0() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_tmap(const void* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
+}
+__device__ __forceinline__ void release_gpu_fence() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// One activation task: 8 consecutive x of token m in group g (lane li of the group's 8 lanes) ->
+// their three byte limbs in the B image of the slot (rows 3m..3m+2, permuted k: the even k of the
+// 8 then the odd k, as the nibble unpacking orders the weights) and, from lane 0 of the group, the
+// group factors (c, xf).  All 8 lanes of a group are in one warp.
+__device__ __forceinline__ void prep_task(uint4 v, int m, int g, int li, uint8_t* bimg, float2* xsc) {
+  const uint32_t hv[8] = {v.x & 0xFFFFu, v.x >> 16, v.y & 0xFFFFu, v.y >> 16,
+                          v.z & 0xFFFFu, v.z >> 16, v.w & 0xFFFFu, v.w >> 16};
+  uint32_t amax = 0, nf = 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const uint32_t a = hv[e] & 0x7FFFu;
+    nf |= a >= 0x7F80u ? 1u : 0u;
+    amax = max(amax, a);
+  }
+#pragma unroll
+  for (int d = 1; d < 8; d <<= 1) {
+    amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, d));
+    nf |= __shfl_xor_sync(0xFFFFFFFFu, nf, d);
+  }
+  const bool zero = nf || amax == 0;
+  const int ef = int(amax >> 7);
+  const int E = ef ? ef - 127 : -133 + (31 - __clz(int(amax & 127u) | 1));
+  const int k = zero ? 0 : 19 - E;  // in [-108, 152]
+  const float s1 = pow2f(k >> 1), s2 = pow2f(k - (k >> 1));
+  uint32_t lo[3] = {0, 0, 0}, hi[3] = {0, 0, 0};
+  int xs = 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int xq = zero ? 0 : grid_value(hv[e], s1, s2);
+    xs += xq;
+    const uint32_t b0 = uint32_t(xq) & 127u, b1 = uint32_t(xq >> 7) & 127u, b2 = uint32_t(xq >> 14) & 255u;
+    const int sh = 8 * (e >> 1);
+    if (e & 1) {
+      hi[0] |= b0 << sh; hi[1] |= b1 << sh; hi[2] |= b2 << sh;
+    } else {
+      lo[0] |= b0 << sh; lo[1] |= b1 << sh; lo[2] |= b2 << sh;
+    }
+  }
+#pragma unroll
+  for (int d = 1; d < 8; d <<= 1) xs += __shfl_xor_sync(0xFFFFFFFFu, xs, d);
+  const int pb = 8 * li;
+#pragma unroll
+  for (int l = 0; l < 3; ++l) {
+    const int j = 3 * m + l;
+    const int off = g * kBGroup + ((pb >> 4) * 2 + (j >> 3)) * 128 + (j & 7) * 16 + (pb & 15);
+    *reinterpret_cast<uint2*>(bimg + off) = make_uint2(lo[l], hi[l]);
+  }
+  if (li == 0) {
+    float c, xf;
+    if (nf) {
+      c = xf = __uint_as_float(0x7FC00000u);
+    } else if (amax == 0) {
+      c = xf = 0.0f;
+    } else {
+      c = pow2f(E - 19);
+      xf = __fmul_rn(__int2float_rn(xs), c);
+    }
+    xsc[g * kMaxTok + m] = make_float2(c, xf);
+  }
 }
 
+// Warp roles (12 warps):
+//   0      TMA producer (lane 0), after the activation build;
+//   1, 3   MMA issuers of chain 0 (groups 0-3 of a unit) and chain 1 (groups 4-7), lane 0;
+//   all    first build the activation operand of every slice the CTA needs (the first weight stages
+//          are in flight meanwhile);
+//   2      in stream mode (more than 8 slices and units), builds the later slices one unit at a time;
+//   4-7    chain-0 workers, 8-11 chain-1 workers: warp w serves TMEM lane quarter w % 4, thread = row.
 template <int MT>
 __global__ void __launch_bounds__(kThreads, 1)
     qmv_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
@@ -141,33 +217,46 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int NSL = p.NSL, R = p.R;
   unsigned* err = p.err;
 
-  long long u0, u1;
+  int u0, u1;
   if (p.whole) {
-    const long long T = p.ntiles;
-    u0 = (long long)blockIdx.x * T / gridDim.x * NSL;
-    u1 = (long long)(blockIdx.x + 1) * T / gridDim.x * NSL;
+    u0 = int(blockIdx.x) * p.ntiles / int(gridDim.x) * NSL;
+    u1 = int(blockIdx.x + 1) * p.ntiles / int(gridDim.x) * NSL;
   } else {
-    u0 = (long long)blockIdx.x * p.U / gridDim.x;
-    u1 = (long long)(blockIdx.x + 1) * p.U / gridDim.x;
+    u0 = int(blockIdx.x) * p.U / int(gridDim.x);
+    u1 = int(blockIdx.x + 1) * p.U / int(gridDim.x);
   }
-  const int nun = int(u1 - u0);
-  const bool cache = NSL <= kNB;  // B image of each slice built once (slot = slice); else per unit
+  const int nun = u1 - u0;
+  const UnitCursor first{u0 / NSL, u0 % NSL};
+  // cache mode: every slice the CTA needs has its own B slot, built once up front; stream mode (more
+  // than kNB distinct slices): slot j % kNB is rebuilt for each unit
+  const bool cache = NSL <= kNB || nun <= kNB;
+  // B slot of unit j whose slice is sl
+  auto slot_of = [&](int j, int sl) { return cache ? (NSL <= kNB ? sl : j) : (j & (kNB - 1)); };
+  const int nbuild = cache ? min(nun, NSL <= kNB ? NSL : nun) : min(nun, kNB);
 
   if (tid == 0) {
+    prefetch_tmap(&tw);
+    prefetch_tmap(&ts);
+    prefetch_tmap(&tb);
     for (int s = 0; s < kNS; ++s) {
       mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->empty[s], 4);
+      mbar_init(&bars->empty[s], 8);
+    }
+    for (int h = 0; h < 2; ++h)
+      for (int s = 0; s < 2; ++s) {
+        mbar_init(&bars->afull[h][s], 4);
+        mbar_init(&bars->dfull[h][s], 1);
+        mbar_init(&bars->dempty[h][s], 4);
+      }
+    for (int s = 0; s < kNB; ++s) {
+      mbar_init(&bars->bfull[s], 2 * MT);  // one arrival per warp batch of 32 tasks
+      mbar_init(&bars->bempty[s], 8);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars->afull[s], 4);
-      mbar_init(&bars->dfull[s], 1);
-      mbar_init(&bars->dempty[s], 4);
+      mbar_init(&bars->hfull[s], 4);
+      mbar_init(&bars->hempty[s], 4);
+      mbar_init(&bars->drain[s], 1);
     }
-    for (int s = 0; s < kNB; ++s) {
-      mbar_init(&bars->bfull[s], 2);
-      mbar_init(&bars->bempty[s], 4);
-    }
-    mbar_init(&bars->drain, 1);
     bars->abort = 0;
     fence_mbar_init();
   }
@@ -179,10 +268,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = &bars->abort;
 
   const uint64_t pol_w = policy_evict_first();
-  auto issue = [&](int j) {
-    const long long u = u0 + j;
-    const int tile = int(u / NSL), sl = int(u % NSL);
-    const int row = tile * R;
+  auto issue = [&](int j, const UnitCursor& c) {
+    const int sl = c.sl;
+    const int row = c.tile * R;
     const int st = j % kNS;
     uint8_t* dst = sm + st * kStage;
     mbar_expect_tx(&bars->full[st], uint32_t(R * (2 * kBox + 32)));
@@ -193,20 +281,74 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
   // The weights are constant: the first stages are requested before the dependency wait.
   const int pre = min(kNS, nun);
+  UnitCursor pc = first;  // producer's cursor: the next unit to request
   if (warp == 0 && lane == 0)
-    for (int j = 0; j < pre; ++j) issue(j);
+    for (int j = 0; j < pre; ++j, pc.next(NSL)) issue(j, pc);
   pdl_trigger();
   pdl_wait();
+
+  // Builds the activation operand of units [j0, j0 + nb) (their slots) with `nthr` threads starting
+  // at thread `t0`: all loads first, then the tasks in slot order, one bfull arrival per warp batch.
+  auto build = [&](int j0, int nb, int t0, int nthr) {
+    const int per_slot = 64 * MT;
+    const int total = nb * per_slot;
+    const int me = tid - t0;
+    const int sbase = (first.sl + j0) % NSL;  // slice of unit j0
+    // trips per thread: up to kNB slots over all threads, or one slot over one warp
+    constexpr int kMaxIt = (kNB * 64 * MT + kThreads - 1) / kThreads > 2 * MT ? (kNB * 64 * MT + kThreads - 1) / kThreads
+                                                                                : 2 * MT;
+    uint4 v[kMaxIt];
+#pragma unroll
+    for (int i = 0; i < kMaxIt; ++i) {
+      const int t = me + i * nthr;
+      if (t < total) {
+        const int jb = t / per_slot, r = t - jb * per_slot;
+        const int sl = sbase + jb < NSL ? sbase + jb : sbase + jb - NSL;
+        const int m = r >> 6, g = (r >> 3) & 7, li = r & 7;
+        v[i] = *reinterpret_cast<const uint4*>(p.x + (size_t)m * (size_t)p.ldx + (size_t)sl * 512 + g * 64 + li * 8);
+      }
+    }
+    int cur_slot = -1;  // slot of this warp's open batch run (its bfull arrivals are owed)
+    int batches = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxIt; ++i) {
+      const int t = me + i * nthr;
+      if (t < total) {  // warp-uniform: total and nthr are multiples of 32
+        const int jb = t / per_slot, r = t - jb * per_slot;
+        const int slot = slot_of(j0 + jb, sbase + jb < NSL ? sbase + jb : sbase + jb - NSL);
+        if (slot != cur_slot && cur_slot >= 0) {
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0)
+            for (int b = 0; b < batches; ++b) mbar_arrive(&bars->bfull[cur_slot]);
+          batches = 0;
+        }
+        cur_slot = slot;
+        ++batches;
+        const int m = r >> 6, g = (r >> 3) & 7, li = r & 7;
+        prep_task(v[i], m, g, li, sm + kOffB + slot * kBSlot, reinterpret_cast<float2*>(sm + kOffX + slot * kXSlot));
+      }
+    }
+    if (cur_slot >= 0) {
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0)
+        for (int b = 0; b < batches; ++b) mbar_arrive(&bars->bfull[cur_slot]);
+    }
+  };
+
+  // every warp builds the activation operand first (the weights are still in flight)
+  build(0, nbuild, 0, kThreads);
 
   if (warp == 0) {
     // ------------------------------------------------------------------- TMA producer
     if (lane == 0) {
       int j = pre;
-      for (; j < nun; ++j) {
+      for (; j < nun; ++j, pc.next(NSL)) {
         const int st = j % kNS;
         if (*abort_flag || !mbar_wait_backoff(&bars->empty[st], ((j / kNS) & 1) ^ 1, err, 64)) break;
         fence_proxy_async();
-        issue(j);
+        issue(j, pc);
       }
       if (j < nun) {
         *abort_flag = 1;
@@ -217,148 +359,85 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------- MMA issuer
+  } else if (warp == 1 || warp == 3) {
+    // ------------------------------------------------------------------- MMA issuers (one per chain)
     if (lane == 0) {
+      const int h = warp == 1 ? 0 : 1;
       constexpr uint32_t idesc = idesc_i8(128, 16);
       const uint32_t bsm = smem_u32(sm + kOffB);
       bool issued = false;
-      for (int j = 0; j < nun; ++j) {
+      UnitCursor c = first;
+      for (int j = 0; j < nun; ++j, c.next(NSL)) {
         const int a = j & 1;
-        const long long u = u0 + j;
-        const int sl = int(u % NSL);
-        const int slot = cache ? sl : j % kNB;
+        const int slot = slot_of(j, c.sl);
         const uint32_t bpar = cache ? 0u : uint32_t((j / kNB) & 1);
         if (*abort_flag || !mbar_wait_spin(&bars->bfull[slot], bpar, err) ||
-            !mbar_wait_spin(&bars->afull[a], uint32_t((j >> 1) & 1), err) ||
-            !mbar_wait_spin(&bars->dempty[a], uint32_t(((j >> 1) & 1) ^ 1), err)) {
+            !mbar_wait_spin(&bars->afull[h][a], uint32_t((j >> 1) & 1), err) ||
+            !mbar_wait_spin(&bars->dempty[h][a], uint32_t(((j >> 1) & 1) ^ 1), err)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t d0 = tmem + uint32_t(kDBase + a * 128);
-        const uint32_t a0 = tmem + uint32_t(kABase + a * 128);
-        const uint32_t b0 = bsm + uint32_t(slot * kBSlot);
+        const uint32_t d0 = tmem + uint32_t(kDBase + a * 128 + 64 * h);
+        const uint32_t a0 = tmem + uint32_t(kABase + a * 128 + 64 * h);
+        // descriptor of the chain's first group; group gi / k-half k2 start (gi*1024 + k2*512) bytes
+        // later (the start-address field holds address / 16 and stays below 2^14)
+        const uint64_t bd = umma_desc(bsm + uint32_t(slot * kBSlot + 4 * h * kBGroup), 256u, 128u);
 #pragma unroll
-        for (int g = 0; g < kGpu; ++g) {
+        for (int gi = 0; gi < 4; ++gi) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-            umma_i8(d0 + uint32_t(g * 16), a0 + uint32_t(g * 16 + 8 * h),
-                    umma_desc(b0 + uint32_t(g * kBGroup + h * 512), 256u, 128u), idesc, uint32_t(h));
+          for (int k2 = 0; k2 < 2; ++k2)
+            umma_i8(d0 + uint32_t(gi * 16), a0 + uint32_t(gi * 16 + 8 * k2),
+                    bd + uint64_t((gi * kBGroup + k2 * 512) >> 4), idesc, uint32_t(k2));
         }
-        umma_commit(&bars->dfull[a]);
+        umma_commit(&bars->dfull[h][a]);
         issued = true;
       }
       // every MMA issued has completed before the CTA releases TMEM
       if (issued) {
-        umma_commit(&bars->drain);
-        mbar_wait_backoff(&bars->drain, 0, err, 64);
+        umma_commit(&bars->drain[h]);
+        mbar_wait_backoff(&bars->drain[h], 0, err, 64);
       }
     }
-  } else if (warp < 4) {
-    // ------------------------------------------------------------------- activation producers
-    const int tb_ = tid - 64;  // 0..63
-    const int nb = cache ? min(nun, NSL) : nun;
-    for (int j = 0; j < nb; ++j) {
-      const int sl = int((u0 + j) % NSL);
-      const int slot = cache ? sl : j % kNB;
-      if (!cache && j >= kNB) {
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------- stream-mode operand builds
+    if (!cache) {
+      for (int j = kNB; j < nun; ++j) {
+        const int slot = j % kNB;
         if (*abort_flag || !mbar_wait_backoff(&bars->bempty[slot], uint32_t(((j / kNB) & 1) ^ 1), err, 64)) {
           *abort_flag = 1;
           break;
         }
+        build(j, 1, 64, 32);
       }
-      uint8_t* bimg = sm + kOffB + slot * kBSlot;
-      float2* xsc = reinterpret_cast<float2*>(sm + kOffX + slot * kXSlot);
-#pragma unroll
-      for (int i = 0; i < MT; ++i) {
-        const int t = tb_ + 64 * i;
-        const int m = t >> 6, g = (t >> 3) & 7, li = t & 7;
-        const uint4 v = *reinterpret_cast<const uint4*>(p.x + (size_t)m * (size_t)p.ldx + (size_t)sl * 512 +
-                                                        g * 64 + li * 8);
-        const uint32_t hv[8] = {v.x & 0xFFFFu, v.x >> 16, v.y & 0xFFFFu, v.y >> 16,
-                                v.z & 0xFFFFu, v.z >> 16, v.w & 0xFFFFu, v.w >> 16};
-        uint32_t amax = 0, nf = 0;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const uint32_t a = hv[e] & 0x7FFFu;
-          nf |= a >= 0x7F80u ? 1u : 0u;
-          amax = max(amax, a);
-        }
-#pragma unroll
-        for (int d = 1; d < 8; d <<= 1) {
-          amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, d));
-          nf |= __shfl_xor_sync(0xFFFFFFFFu, nf, d);
-        }
-        const bool zero = nf || amax == 0;
-        const int ef = int(amax >> 7);
-        const int E = ef ? ef - 127 : -133 + (31 - __clz(int(amax & 127u) | 1));
-        uint32_t lo[3] = {0, 0, 0}, hi[3] = {0, 0, 0};
-        int xs = 0;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int mag = zero ? 0 : grid_mag(hv[e] & 0x7FFFu, E);
-          const int xq = (hv[e] & 0x8000u) ? -mag : mag;
-          xs += xq;
-          const uint32_t b0 = uint32_t(xq) & 127u, b1 = uint32_t(xq >> 7) & 127u, b2 = uint32_t(xq >> 14) & 255u;
-          const int sh = 8 * (e >> 1);
-          if (e & 1) {
-            hi[0] |= b0 << sh; hi[1] |= b1 << sh; hi[2] |= b2 << sh;
-          } else {
-            lo[0] |= b0 << sh; lo[1] |= b1 << sh; lo[2] |= b2 << sh;
-          }
-        }
-#pragma unroll
-        for (int d = 1; d < 8; d <<= 1) xs += __shfl_xor_sync(0xFFFFFFFFu, xs, d);
-        // B row j = 3m + limb, k bytes p = 8li .. 8li+7 of the group (canonical K-major layout)
-        const int pb = 8 * li;
-#pragma unroll
-        for (int l = 0; l < 3; ++l) {
-          const int j = 3 * m + l;
-          const int off = g * kBGroup + ((pb >> 4) * 2 + (j >> 3)) * 128 + (j & 7) * 16 + (pb & 15);
-          *reinterpret_cast<uint2*>(bimg + off) = make_uint2(lo[l], hi[l]);
-        }
-        if (li == 0) {
-          float c, xf;
-          if (nf) {
-            c = xf = __uint_as_float(0x7FC00000u);
-          } else if (amax == 0) {
-            c = xf = 0.0f;
-          } else {
-            c = pow2f(E - 19);
-            xf = __fmul_rn(__int2float_rn(xs), c);
-          }
-          xsc[g * kMaxTok + m] = make_float2(c, xf);
-        }
-      }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->bfull[slot]);
     }
-  } else {
+  } else if (warp >= 4) {
     // ------------------------------------------------------------------- row workers
-    const int q = warp - 4;
+    const int h = warp < 8 ? 0 : 1;  // chain: groups 4h .. 4h+3 of every unit
+    const int q = warp & 3;
     const int r = 32 * q + lane;
     const uint32_t tl = tmem + (uint32_t(32 * q) << 16);
     const int rsw = r & 7;
+    float* hx = reinterpret_cast<float*>(sm + kOffH);  // [2][kMaxTok][128] chain-1 partials
     float Y[MT];
-    bool own = false;  // this CTA holds slice 0 of the current tile (Y is the tile's running prefix)
+    bool own = false;  // chain 0: this CTA holds slice 0 of the current tile (Y is the tile's running prefix)
     int part_start = 0;
 #pragma unroll
     for (int m = 0; m < MT; ++m) Y[m] = 0.0f;
-    uint4 sv_prev = make_uint4(0, 0, 0, 0), bv_prev = make_uint4(0, 0, 0, 0);
+    uint2 sv_prev = make_uint2(0, 0), bv_prev = make_uint2(0, 0);
     bool ok = true;
+    UnitCursor ec = first;  // unit of the next epilogue
 
     // Every worker warp runs the same sequence of epilogues and named barriers whatever happens: a wait
     // that gives up only sets `ok` false (and the CTA's abort flag), so no warp is left at a barrier.
-    auto epilogue = [&](int jj, const uint4& sv, const uint4& bv) {
+    auto epilogue = [&](int jj, const uint2& sv, const uint2& bv) {
       const int a = jj & 1;
-      const long long u = u0 + jj;
-      const int tile = int(u / NSL), sl = int(u % NSL);
-      const int slot = cache ? sl : jj % kNB;
+      const int tile = ec.tile, sl = ec.sl;
+      ec.next(NSL);
+      const int slot = slot_of(jj, sl);
       const uint32_t bpar = cache ? 0u : uint32_t((jj / kNB) & 1);
       if (ok && !*abort_flag) {
-        if (!mbar_wait_backoff(&bars->dfull[a], uint32_t((jj >> 1) & 1), err, 32) ||
+        if (!mbar_wait_backoff(&bars->dfull[h][a], uint32_t((jj >> 1) & 1), err, 32) ||
             !mbar_wait_backoff(&bars->bfull[slot], bpar, err, 32)) {
           ok = false;
           *abort_flag = 1;
@@ -368,41 +447,64 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const float2* xsc = reinterpret_cast<const float2*>(sm + kOffX + slot * kXSlot);
-      const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
-      float H0[MT], H1[MT];
+      const uint32_t sw[2] = {sv.x, sv.y}, bw[2] = {bv.x, bv.y};
+      float H[MT];
 #pragma unroll
-      for (int m = 0; m < MT; ++m) H0[m] = H1[m] = 0.0f;
+      for (int m = 0; m < MT; ++m) H[m] = 0.0f;
 #pragma unroll
-      for (int gp = 0; gp < 4; ++gp) {
+      for (int gp = 0; gp < 2; ++gp) {
         uint32_t v0[16], v1[16];
-        tmem_ld16(tl + uint32_t(kDBase + a * 128 + gp * 16), v0);
-        tmem_ld16(tl + uint32_t(kDBase + a * 128 + (gp + 4) * 16), v1);
+        tmem_ld16(tl + uint32_t(kDBase + a * 128 + (4 * h + 2 * gp) * 16), v0);
+        tmem_ld16(tl + uint32_t(kDBase + a * 128 + (4 * h + 2 * gp + 1) * 16), v1);
         tmem_ld_wait();
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          const int g = gp + 4 * hh;
+          const int gl = 2 * gp + hh;  // group of this chain, 0..3
+          const int g = 4 * h + gl;
           const uint32_t* v = hh ? v1 : v0;
-          const float s = (g & 1) ? bfhi(sw[g >> 1]) : bflo(sw[g >> 1]);
-          const float b = (g & 1) ? bfhi(bw[g >> 1]) : bflo(bw[g >> 1]);
+          const float s = (gl & 1) ? bfhi(sw[gl >> 1]) : bflo(sw[gl >> 1]);
+          const float b = (gl & 1) ? bfhi(bw[gl >> 1]) : bflo(bw[gl >> 1]);
 #pragma unroll
           for (int m = 0; m < MT; ++m) {
             const int S = int(v[3 * m + 2]) * 16384 + int(v[3 * m + 1]) * 128 + int(v[3 * m]);
             const float2 cx = xsc[g * kMaxTok + m];
-            float& H = hh ? H1[m] : H0[m];
-            H = __fmaf_rn(__int2float_rn(S), __fmul_rn(s, cx.x), H);
-            H = __fmaf_rn(b, cx.y, H);
+            H[m] = __fmaf_rn(__int2float_rn(S), __fmul_rn(s, cx.x), H[m]);
+            H[m] = __fmaf_rn(b, cx.y, H[m]);
           }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0 && ok) {
-        mbar_arrive(&bars->dempty[a]);
+        mbar_arrive(&bars->dempty[h][a]);
         if (!cache) mbar_arrive(&bars->bempty[slot]);
+      }
+      float* hb = hx + (jj & 1) * (kMaxTok * 128);
+      if (h == 1) {
+        // hand chain 1 to the chain-0 worker of the same row
+        if (ok && !*abort_flag) {
+          if (!mbar_wait_backoff(&bars->hempty[jj & 1], uint32_t(((jj >> 1) & 1) ^ 1), err, 32)) {
+            ok = false;
+            *abort_flag = 1;
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) hb[m * 128 + r] = H[m];
+        __syncwarp();
+        if (lane == 0 && ok) mbar_arrive(&bars->hfull[jj & 1]);
+        return;
+      }
+      if (ok && !*abort_flag) {
+        if (!mbar_wait_backoff(&bars->hfull[jj & 1], uint32_t((jj >> 1) & 1), err, 32)) {
+          ok = false;
+          *abort_flag = 1;
+        }
       }
       float P[MT];
 #pragma unroll
-      for (int m = 0; m < MT; ++m) P[m] = __fadd_rn(H0[m], H1[m]);
+      for (int m = 0; m < MT; ++m) P[m] = __fadd_rn(H[m], hb[m * 128 + r]);
+      __syncwarp();
+      if (lane == 0 && ok) mbar_arrive(&bars->hempty[jj & 1]);
       const size_t tbase = (size_t)tile * (size_t)NSL * (kMaxTok * 128);
       if (sl == 0) {
         own = true;
@@ -435,33 +537,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         own = false;
         return;
       }
-      // a split tile: publish this CTA's share; the last CTA to arrive finishes the tile
+      // a split tile: publish this CTA's share; the last CTA to arrive finishes the tile.  The barrier
+      // orders every row's stores before thread 128's gpu-scope release fence and the arrival count.
       if (own) {
 #pragma unroll
         for (int m = 0; m < MT; ++m) p.part[tbase + m * 128 + r] = Y[m];
       }
       const int contributed = sl - part_start + 1;
-      __threadfence();
-      bar_workers();
+      bar_chain0();
       if (tid == 128) {
+        release_gpu_fence();
         const unsigned old = atomicAdd(&p.cnt[tile], unsigned(contributed));
         bars->last = (old + unsigned(contributed) == unsigned(NSL)) ? 1 : 0;
+        release_gpu_fence();
       }
-      bar_workers();
+      bar_chain0();
       if (bars->last) {
-        __threadfence();
         // slices covered by the prefix: those of the CTA that owns unit tile * NSL
-        const long long v = (long long)tile * NSL;
-        const long long G = gridDim.x;
-        const long long owner = ((v + 1) * G + p.U - 1) / p.U - 1;
-        const long long ou1 = (owner + 1) * p.U / G;
-        const int alen = int(min(ou1, v + NSL) - v);
+        const int v = tile * NSL;
+        const int G = int(gridDim.x);
+        const int owner = ((v + 1) * G + p.U - 1) / p.U - 1;
+        const int ou1 = (owner + 1) * p.U / G;
+        const int alen = min(ou1, v + NSL) - v;
         if (valid) {
 #pragma unroll
           for (int m = 0; m < MT; ++m) {
-            float acc = ld_cg_f32(p.part + tbase + m * 128 + r);
-            for (int s2 = alen; s2 < NSL; ++s2)
-              acc = __fadd_rn(acc, ld_cg_f32(p.part + tbase + (size_t)s2 * (kMaxTok * 128) + m * 128 + r));
+            const float* pp = p.part + tbase + m * 128 + r;
+            float acc = __ldcg(pp);
+            for (int s2 = alen; s2 < NSL; ++s2) acc = __fadd_rn(acc, __ldcg(pp + (size_t)s2 * (kMaxTok * 128)));
             uint16_t o = f2bf(acc);
             const size_t oi = (size_t)m * p.ldy + row;
             if (p.res) o = f2bf(__fadd_rn(bf2f(p.res[oi]), bf2f(o)));
@@ -470,11 +573,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (tid == 128) p.cnt[tile] = 0u;  // ready for the next launch
       }
-      bar_workers();
+      bar_chain0();
       own = false;
     };
 
+    // Iteration j: the epilogue of unit j-2, then the unpacking of unit j.  Two units of A and of
+    // accumulators are in TMEM, so unit j reuses the slots of unit j-2 and its MMAs (issued after the
+    // unpacking of j) run while this warp does the epilogue of j-1 and the unpacking of j+1.
+    uint2 sv_prev2 = make_uint2(0, 0), bv_prev2 = make_uint2(0, 0);
     for (int j = 0; j < nun; ++j) {
+      if (j >= 2) epilogue(j - 2, sv_prev2, bv_prev2);
+      sv_prev2 = sv_prev;
+      bv_prev2 = bv_prev;
       const int st = j % kNS;
       if (ok && !*abort_flag) {
         if (!mbar_wait_backoff(&bars->full[st], uint32_t((j / kNS) & 1), err, 32)) {
@@ -485,13 +595,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
       }
       const uint8_t* sg = sm + st * kStage;
-      const uint4 sv = *reinterpret_cast<const uint4*>(sg + kWStage + r * 16);
-      const uint4 bv = *reinterpret_cast<const uint4*>(sg + kWStage + kSStage + r * 16);
+      const uint2 sv = *reinterpret_cast<const uint2*>(sg + kWStage + r * 16 + 8 * h);
+      const uint2 bv = *reinterpret_cast<const uint2*>(sg + kWStage + kSStage + r * 16 + 8 * h);
       const int a = j & 1;
+      const uint8_t* rowp = sg + h * (kMaxRows * kBox) + r * kBox;  // box h holds groups 4h .. 4h+3
 #pragma unroll
-      for (int g = 0; g < kGpu; ++g) {
-        const uint8_t* rowp = sg + (g >> 2) * (kMaxRows * kBox) + r * kBox;
-        const int c0 = 2 * (g & 3);
+      for (int gl = 0; gl < 4; ++gl) {
+        const int c0 = 2 * gl;
         const uint4 w0 = *reinterpret_cast<const uint4*>(rowp + 16 * (c0 ^ rsw));
         const uint4 w1 = *reinterpret_cast<const uint4*>(rowp + 16 * ((c0 + 1) ^ rsw));
         const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
@@ -501,20 +611,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           o[2 * i] = wd[i] & 0x0F0F0F0Fu;
           o[2 * i + 1] = (wd[i] >> 4) & 0x0F0F0F0Fu;
         }
-        tmem_st16(tl + uint32_t(kABase + a * 128 + g * 16), o);
+        tmem_st16(tl + uint32_t(kABase + a * 128 + (4 * h + gl) * 16), o);
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0 && ok) {
         mbar_arrive(&bars->empty[st]);
-        mbar_arrive(&bars->afull[a]);
+        mbar_arrive(&bars->afull[h][a]);
       }
-      if (j >= 1) epilogue(j - 1, sv_prev, bv_prev);
       sv_prev = sv;
       bv_prev = bv;
     }
-    if (nun > 0) epilogue(nun - 1, sv_prev, bv_prev);
+    if (nun >= 2) epilogue(nun - 2, sv_prev2, bv_prev2);
+    if (nun >= 1) epilogue(nun - 1, sv_prev, bv_prev);
   }
 
   tc_fence_before();
@@ -528,6 +638,8 @@ struct Plan {
   int R, G, ntiles, NSL, whole;
   long long U;
 };
+// Unit indices are 32-bit in the kernel: U * grid must stay below 2^31.
+constexpr long long kMaxUnitProduct = (1LL << 31) - 1;
 
 // Rows per tile and grid: the slowest CTA's work (units x max(bytes / per-SM bandwidth, MMA issue
 // floor)) is minimised; ties go to the larger tile.
@@ -608,6 +720,7 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
   if (split && (qmv_tc_workspace(N, K) == 0 || ws_bytes < qmv_tc_workspace(N, K))) return QMTP_ERR_SHAPE;
   if (split && (reinterpret_cast<uintptr_t>(workspace) & 255u)) return QMTP_ERR_ALIGN;
   const Plan pl = make_plan(N, K, split, sm_count());
+  if (pl.U * (long long)(pl.G + 1) > kMaxUnitProduct) return QMTP_ERR_SHAPE;
   CUtensorMap tw, ts, tb;
   if (!encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, K / 2, N, kBox, pl.R, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, s, K / 64, N, 8, pl.R, CU_TENSOR_MAP_SWIZZLE_NONE) ||
@@ -622,7 +735,7 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
   p.R = pl.R;
   p.ntiles = pl.ntiles;
   p.whole = pl.whole;
-  p.U = pl.U;
+  p.U = int(pl.U);
   p.err = device_error_ptr();
   if (split) {
     p.cnt = static_cast<unsigned*>(workspace);

@@ -81,6 +81,8 @@ SIGNATURES.update({
     "qmtp_moe_experts": [_I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, ctypes.c_size_t, _P],
     "qmtp_moe_combine": [_P, _P, _P, _I, _I, _I, _P, _P],
     "qmtp_moe_dispatch": [_P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P],
+    "qmtp_math_eval": [_I, _P, _I, _P, _P],
+    "qmtp_wait_selftest": [ctypes.c_uint, _P, _P],
 })
 
 # control block layout (include/qmtp.h QMTP_CTRL_*)
