@@ -17,18 +17,23 @@
 //
 // Design:
 //   * a tile is R <= 128 weight rows (the MMA's M); a unit of work is (tile, slice of 512 k).  CTAs
-//     take contiguous unit ranges (one CTA per SM, 216 KB of shared memory); a tile split between CTAs
+//     take contiguous unit ranges (one CTA per SM, 220 KB of shared memory); a tile split between CTAs
 //     is finished by the CTA that arrives last (one arrival counter per tile at the start of a caller
 //     workspace, fp32 slice partials after them; no CTA ever waits for another);
-//   * warp 0: TMA producer.  Per unit, two 128-byte-wide boxes of packed nibbles (128-byte swizzle) and
-//     the unit's scales and biases land in a 4-stage ring;
-//   * warps 2-3: activation producers.  They build the B operand (the three byte limbs of every token,
-//     16 x 64 bytes per group, canonical K-major layout) and the per-group factors from x;
-//   * warps 4-7: one per TMEM lane quarter, a thread per weight row.  They unpack the nibbles of their
-//     row into bytes (two LOP3s per word) and store them into TMEM as the A operand, then read the
-//     integer accumulators back and run the fp32 chains of the contract;
-//   * warp 1: MMA issuer.  Per unit 16 MMAs (M=128, N=16, K=32, A from TMEM, B from shared memory) and
-//     one commit.  TMEM: A slots [0,256), accumulator slots [256,512), double-buffered per unit.
+//   * all 12 warps first build the B operand of every slice the CTA needs (the three byte limbs of every
+//     token, 16 x 64 bytes per group, canonical K-major layout) and the per-group factors from x, while
+//     the first weight stages are in flight;
+//   * warp 0 is the TMA producer: per unit, two 128-byte-wide boxes of packed nibbles (128-byte swizzle)
+//     and the unit's scales and biases land in a 4-stage ring;
+//   * the two chains of a slice (groups 0-3 and 4-7) have their own workers: warps 4-7
+//     for chain 0, warps 8-11 for chain 1.  A worker thread owns one weight row (TMEM
+//     lane quarter = warp % 4): it unpacks its row's nibbles of the chain's groups into bytes (two LOP3s
+//     per word) and stores them into TMEM as the A operand; two units later it reads the integer
+//     accumulators back and runs the chain.  The chain-1 workers hand their partial to the chain-0
+//     workers of the same rows, which add the slices in order;
+//   * warp 1 (chain 0) and warp 3 (chain 1) each issue the chain's 8 MMAs of a unit (M=128, N=16, K=32,
+//     A from TMEM, B from shared memory) and one commit.  TMEM: A slots [0,256), accumulator slots
+//     [256,512), two units in flight.
 // The nibble-to-byte unpacking permutes k inside each word (bytes 0,2,4,6 then 1,3,5,7); the B operand
 // is built with the same permutation, so every product pairs the right x with the right q.
 #include <cuda.h>
@@ -132,11 +137,46 @@ __device__ __forceinline__ float pow2f(int k) {
 __device__ __forceinline__ int grid_value(uint32_t h, float s1, float s2) {
   return __float2int_rn(__fmul_rn(__fmul_rn(bf2f(uint16_t(h)), s1), s2));
 }
+// The first NC (<= 12) accumulator columns of a lane quarter (32x32b shape): only the 3 * MT limb
+// columns of a group are read.  Completion is awaited by the caller (tmem_ld_wait).
+__device__ __forceinline__ void tmem_ld_x1(uint32_t taddr, uint32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v[0]) : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_x4(uint32_t taddr, uint32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
+}
+template <int NC>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* v) {
+  static_assert(NC >= 1 && NC <= 12, "at most 12 accumulator columns");
+  if constexpr (NC <= 4) {
+    tmem_ld_x4(taddr, v);
+  } else if constexpr (NC <= 8) {
+    tmem_ld_x8(taddr, v);
+  } else if constexpr (NC == 9) {
+    tmem_ld_x8(taddr, v);
+    tmem_ld_x1(taddr + 8u, v + 8);
+  } else {
+    tmem_ld_x8(taddr, v);
+    tmem_ld_x4(taddr + 8u, v + 8);
+  }
+}
+
 __device__ __forceinline__ void bar_chain0() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 __device__ __forceinline__ void prefetch_tmap(const void* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
 }
-__device__ __forceinline__ void release_gpu_fence() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 
 // One activation task: 8 consecutive x of token m in group g (lane li of the group's 8 lanes) ->
 // their three byte limbs in the B image of the slot (rows 3m..3m+2, permuted k: the even k of the
@@ -162,20 +202,25 @@ __device__ __forceinline__ void prep_task(uint4 v, int m, int g, int li, uint8_t
   const int E = ef ? ef - 127 : -133 + (31 - __clz(int(amax & 127u) | 1));
   const int k = zero ? 0 : 19 - E;  // in [-108, 152]
   const float s1 = pow2f(k >> 1), s2 = pow2f(k - (k >> 1));
-  uint32_t lo[3] = {0, 0, 0}, hi[3] = {0, 0, 0};
+  int xq[8];
   int xs = 0;
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    const int xq = zero ? 0 : grid_value(hv[e], s1, s2);
-    xs += xq;
-    const uint32_t b0 = uint32_t(xq) & 127u, b1 = uint32_t(xq >> 7) & 127u, b2 = uint32_t(xq >> 14) & 255u;
-    const int sh = 8 * (e >> 1);
-    if (e & 1) {
-      hi[0] |= b0 << sh; hi[1] |= b1 << sh; hi[2] |= b2 << sh;
-    } else {
-      lo[0] |= b0 << sh; lo[1] |= b1 << sh; lo[2] |= b2 << sh;
-    }
+    xq[e] = zero ? 0 : grid_value(hv[e], s1, s2);
+    xs += xq[e];
   }
+  // limb l of element e is byte 0 of (x_q >> 7l) (l0, l1 masked to 7 bits); the even elements fill the
+  // low word of a limb's 8 bytes, the odd ones the high word
+  auto pack4 = [](uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+  };
+  uint32_t lo[3], hi[3];
+  lo[0] = pack4(xq[0], xq[2], xq[4], xq[6]) & 0x7F7F7F7Fu;
+  hi[0] = pack4(xq[1], xq[3], xq[5], xq[7]) & 0x7F7F7F7Fu;
+  lo[1] = pack4(xq[0] >> 7, xq[2] >> 7, xq[4] >> 7, xq[6] >> 7) & 0x7F7F7F7Fu;
+  hi[1] = pack4(xq[1] >> 7, xq[3] >> 7, xq[5] >> 7, xq[7] >> 7) & 0x7F7F7F7Fu;
+  lo[2] = pack4(xq[0] >> 14, xq[2] >> 14, xq[4] >> 14, xq[6] >> 14);
+  hi[2] = pack4(xq[1] >> 14, xq[3] >> 14, xq[5] >> 14, xq[7] >> 14);
 #pragma unroll
   for (int d = 1; d < 8; d <<= 1) xs += __shfl_xor_sync(0xFFFFFFFFu, xs, d);
   const int pb = 8 * li;
@@ -244,9 +289,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int h = 0; h < 2; ++h)
       for (int s = 0; s < 2; ++s) {
-        mbar_init(&bars->afull[h][s], 4);
-        mbar_init(&bars->dfull[h][s], 1);
-        mbar_init(&bars->dempty[h][s], 4);
+        mbar_init(&bars->afull[h][s], 4);   // the chain's workers have stored the unit's A
+        mbar_init(&bars->dfull[h][s], 1);   // the chain's 8 MMAs of the unit are complete
+        mbar_init(&bars->dempty[h][s], 4);  // the chain's workers have read the unit's accumulators
       }
     for (int s = 0; s < kNB; ++s) {
       mbar_init(&bars->bfull[s], 2 * MT);  // one arrival per warp batch of 32 tasks
@@ -361,6 +406,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1 || warp == 3) {
     // ------------------------------------------------------------------- MMA issuers (one per chain)
+    // An MMA of this shape costs its issuing thread ~100 cycles; two issuing threads overlap on the
+    // tensor core (one issuer for both chains measured 1.05-1.25x slower).
     if (lane == 0) {
       const int h = warp == 1 ? 0 : 1;
       constexpr uint32_t idesc = idesc_i8(128, 16);
@@ -451,26 +498,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       float H[MT];
 #pragma unroll
       for (int m = 0; m < MT; ++m) H[m] = 0.0f;
+      constexpr int NC = 3 * MT;
+      constexpr int NCP = NC <= 4 ? 4 : NC <= 8 ? 8 : 12;
+      uint32_t v[4][NCP];
 #pragma unroll
-      for (int gp = 0; gp < 2; ++gp) {
-        uint32_t v0[16], v1[16];
-        tmem_ld16(tl + uint32_t(kDBase + a * 128 + (4 * h + 2 * gp) * 16), v0);
-        tmem_ld16(tl + uint32_t(kDBase + a * 128 + (4 * h + 2 * gp + 1) * 16), v1);
-        tmem_ld_wait();
+      for (int gl = 0; gl < 4; ++gl) tmem_ld_cols<NC>(tl + uint32_t(kDBase + a * 128 + (4 * h + gl) * 16), v[gl]);
+      tmem_ld_wait();
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int gl = 2 * gp + hh;  // group of this chain, 0..3
-          const int g = 4 * h + gl;
-          const uint32_t* v = hh ? v1 : v0;
-          const float s = (gl & 1) ? bfhi(sw[gl >> 1]) : bflo(sw[gl >> 1]);
-          const float b = (gl & 1) ? bfhi(bw[gl >> 1]) : bflo(bw[gl >> 1]);
+      for (int gl = 0; gl < 4; ++gl) {
+        const int g = 4 * h + gl;
+        const float s = (gl & 1) ? bfhi(sw[gl >> 1]) : bflo(sw[gl >> 1]);
+        const float b = (gl & 1) ? bfhi(bw[gl >> 1]) : bflo(bw[gl >> 1]);
 #pragma unroll
-          for (int m = 0; m < MT; ++m) {
-            const int S = int(v[3 * m + 2]) * 16384 + int(v[3 * m + 1]) * 128 + int(v[3 * m]);
-            const float2 cx = xsc[g * kMaxTok + m];
-            H[m] = __fmaf_rn(__int2float_rn(S), __fmul_rn(s, cx.x), H[m]);
-            H[m] = __fmaf_rn(b, cx.y, H[m]);
-          }
+        for (int m = 0; m < MT; ++m) {
+          const int S = int(v[gl][3 * m + 2]) * 16384 + int(v[gl][3 * m + 1]) * 128 + int(v[gl][3 * m]);
+          const float2 cx = xsc[g * kMaxTok + m];
+          H[m] = __fmaf_rn(__int2float_rn(S), __fmul_rn(s, cx.x), H[m]);
+          H[m] = __fmaf_rn(b, cx.y, H[m]);
         }
       }
       tc_fence_before();
@@ -546,10 +590,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int contributed = sl - part_start + 1;
       bar_chain0();
       if (tid == 128) {
-        release_gpu_fence();
-        const unsigned old = atomicAdd(&p.cnt[tile], unsigned(contributed));
+        // acquire-release: publishes the rows' partials (ordered before it by the barrier) and, for the
+        // last arrival, makes the other CTAs' partials visible to this CTA
+        const unsigned old = atom_add_acq_rel(&p.cnt[tile], unsigned(contributed));
         bars->last = (old + unsigned(contributed) == unsigned(NSL)) ? 1 : 0;
-        release_gpu_fence();
       }
       bar_chain0();
       if (bars->last) {
@@ -641,28 +685,37 @@ struct Plan {
 // Unit indices are 32-bit in the kernel: U * grid must stay below 2^31.
 constexpr long long kMaxUnitProduct = (1LL << 31) - 1;
 
-// Rows per tile and grid: the slowest CTA's work (units x max(bytes / per-SM bandwidth, MMA issue
-// floor)) is minimised; ties go to the larger tile.
+// Rows per tile and grid, from a cost model of the slowest CTA, fitted to B200 timings of this kernel:
+// about 2 us of setup and first weight latency, 0.45 us per activation slice built, about 1.2 us per
+// unit (16 MMAs of ~98 tensor cycles each, plus the pipeline; the weight bytes of a 128-row unit stream
+// in 0.84 us at the per-SM share of HBM bandwidth), and about 5 us to finish a tile split between CTAs.
+// Ties go to the larger tile.
 static Plan make_plan(int N, int K, bool split, int sms) {
   const int NSL = K / 512;
   Plan best{};
   double best_cost = 1e30;
-  for (int R = kMaxRows; R >= kMinRows; R -= 8) {
-    const int T = (N + R - 1) / R;
-    long long G, per;
-    if (split) {
-      const long long U = (long long)T * NSL;
-      G = std::min<long long>(sms, U);
-      per = (U + G - 1) / G;
-    } else {
-      G = std::min(sms, T);
-      per = (long long)((T + G - 1) / G) * NSL;
-    }
-    const double unit_us = std::max(R * 288.0 / 44.0e3, 0.45);
-    const double cost = double(per) * unit_us;
-    if (cost < best_cost * 0.999) {
-      best_cost = cost;
-      best = Plan{R, int(G), T, NSL, split ? 0 : 1, (long long)T * NSL};
+  for (int w = 0; w < (split ? 2 : 1); ++w) {
+    const bool whole = !split || w == 1;
+    for (int R = kMaxRows; R >= kMinRows; R -= 8) {
+      const int T = (N + R - 1) / R;
+      long long G, per;
+      int slices;
+      if (!whole) {
+        const long long U = (long long)T * NSL;
+        G = std::min<long long>(sms, U);
+        per = (U + G - 1) / G;
+        slices = int(std::min<long long>(per, NSL));
+      } else {
+        G = std::min(sms, T);
+        per = (long long)((T + G - 1) / G) * NSL;
+        slices = NSL;
+      }
+      const double unit_us = std::max(R * 288.0 / 44.0e3, 1.2);
+      const double cost = 2.0 + 0.45 * std::min(slices, kNB) + double(per) * unit_us + (whole ? 0.0 : 5.0);
+      if (cost < best_cost * 0.999) {
+        best_cost = cost;
+        best = Plan{R, int(G), T, NSL, whole ? 1 : 0, (long long)T * NSL};
+      }
     }
   }
   return best;

@@ -46,7 +46,7 @@ def test_engine_prefix_cache_and_eos(small):
     first = list(eng.generate(p, 24, 12, Sampling(), {}))
     ref, _ = orc.generate_mtp(p, 12)
     assert first == ref
-    p2 = p[:24] + prompt(9, seed=5)
+    p2 = list(p[:24]) + list(prompt(9, seed=5))
     st = {}
     second = list(eng.generate(p2, 24, 12, Sampling(), st))
     ref2, _ = orc.generate_mtp(p2, 12)
@@ -90,7 +90,7 @@ def test_reference_style_loop_functions(small):
     from qmtp.mtp import backbone, decode_mtp, draft_chain, restore
 
     orc, lm = small
-    p = prompt(12, seed=9)
+    p = [int(v) for v in prompt(12, seed=9)]
     want, _ = decode_mtp(lm.make_cache(k=2, max_tokens=64), p, 14, use_graph=False)
     cache = lm.make_cache(k=2, max_tokens=64)
     cache.reset()
@@ -104,7 +104,7 @@ def test_reference_style_loop_functions(small):
     h_all = torch.cat(hs)
     t = int(torch.argmax(logits[0, -1]).item())
     out = [t]
-    nxt = torch.tensor(p[1:] + [t], dtype=torch.int32)
+    nxt = torch.tensor(list(p[1:]) + [t], dtype=torch.int32)
     drafts = None
     for i in range(0, len(p), S):
         n = min(S, len(p) - i)
