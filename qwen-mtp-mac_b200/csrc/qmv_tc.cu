@@ -61,10 +61,11 @@ constexpr int kXSlot = kGpu * kMaxTok * 8;         // per slot: [group][token] f
 constexpr int kOffB = kNS * kStage;                // 147456
 constexpr int kOffX = kOffB + kNB * kBSlot;        // 212992
 constexpr int kOffH = kOffX + kNB * kXSlot;        // 215040: chain-1 partials [2][kMaxTok][128] fp32
-constexpr int kOffBar = kOffH + 2 * kMaxTok * 128 * 4;  // 219136
+constexpr int kOffSB = kOffH + 2 * kMaxTok * 128 * 4;  // 219136: scales | biases per unit [2][2][128] x 16 B
+constexpr int kOffBar = kOffSB + 2 * 2 * 128 * 16;      // 227328
 constexpr int kSmemUsed = kOffBar + 512;
 constexpr int kSmem = kSmemUsed + 1024;            // slack for 1024-byte alignment of the base
-constexpr int kThreads = 384;                      // 12 warps
+constexpr int kThreads = 640;                      // 20 warps
 constexpr int kTmemCols = 512;
 constexpr int kABase = 0, kDBase = 256;
 constexpr int kMinRows = 64;                       // smallest tile the planner picks (workspace bound)
@@ -73,6 +74,8 @@ constexpr int kMinRows = 64;                       // smallest tile the planner 
 constexpr size_t kCntBytes = 65536;                // 16384 counters: tiles of up to 1M rows
 constexpr long long kMaxSplitTiles = kCntBytes / 4;
 static_assert(kOffB % 1024 == 0 && kStage % 1024 == 0, "stage alignment");
+static_assert(kSmem <= 232448, "shared memory per CTA");
+constexpr int kLeader = 12 * 32;                   // first thread of the chain-0 epilogue warps
 
 // Barriers.  Per unit j: weight stage j % kNS (full / empty); A and accumulator slot a = j & 1 per
 // chain h (afull / dfull / dempty [h][a]); activation operand slot (bfull / bempty); the chain-1 partial
@@ -458,33 +461,84 @@ __global__ void __launch_bounds__(kThreads, 1)
         build(j, 1, 64, 32);
       }
     }
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------------- row workers
+  } else if (warp < 12) {
+    // ------------------------------------------------------------------- unpacking warps
     const int h = warp < 8 ? 0 : 1;  // chain: groups 4h .. 4h+3 of every unit
     const int q = warp & 3;
     const int r = 32 * q + lane;
     const uint32_t tl = tmem + (uint32_t(32 * q) << 16);
     const int rsw = r & 7;
+    bool ok = true;
+    for (int j = 0; j < nun; ++j) {
+      const int st = j % kNS;
+      const int a = j & 1;
+      // unit j reuses the A slot and the scale/bias slot of unit j-2: its epilogue (which waited for its
+      // MMAs) must be done
+      if (ok && !*abort_flag) {
+        if (!mbar_wait_backoff(&bars->full[st], uint32_t((j / kNS) & 1), err, 32) ||
+            !mbar_wait_backoff(&bars->dempty[h][a], uint32_t(((j >> 1) & 1) ^ 1), err, 32)) {
+          ok = false;
+          *abort_flag = 1;
+        }
+      } else {
+        ok = false;
+      }
+      tc_fence_after();
+      const uint8_t* sg = sm + st * kStage;
+      const uint2 sv = *reinterpret_cast<const uint2*>(sg + kWStage + r * 16 + 8 * h);
+      const uint2 bv = *reinterpret_cast<const uint2*>(sg + kWStage + kSStage + r * 16 + 8 * h);
+      *reinterpret_cast<uint4*>(sm + kOffSB + ((a * 2 + h) * 128 + r) * 16) = make_uint4(sv.x, sv.y, bv.x, bv.y);
+      const uint8_t* rowp = sg + h * (kMaxRows * kBox) + r * kBox;  // box h holds groups 4h .. 4h+3
+#pragma unroll
+      for (int gl = 0; gl < 4; ++gl) {
+        const int c0 = 2 * gl;
+        const uint4 w0 = *reinterpret_cast<const uint4*>(rowp + 16 * (c0 ^ rsw));
+        const uint4 w1 = *reinterpret_cast<const uint4*>(rowp + 16 * ((c0 + 1) ^ rsw));
+        const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        uint32_t o[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          o[2 * i] = wd[i] & 0x0F0F0F0Fu;
+          o[2 * i + 1] = (wd[i] >> 4) & 0x0F0F0F0Fu;
+        }
+        tmem_st16(tl + uint32_t(kABase + a * 128 + (4 * h + gl) * 16), o);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && ok) {
+        mbar_arrive(&bars->empty[st]);
+        mbar_arrive(&bars->afull[h][a]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------- epilogue warps
+    const int h = warp < 16 ? 0 : 1;  // chain: groups 4h .. 4h+3 of every unit
+    const int q = warp & 3;
+    const int r = 32 * q + lane;
+    const uint32_t tl = tmem + (uint32_t(32 * q) << 16);
     float* hx = reinterpret_cast<float*>(sm + kOffH);  // [2][kMaxTok][128] chain-1 partials
     float Y[MT];
     bool own = false;  // chain 0: this CTA holds slice 0 of the current tile (Y is the tile's running prefix)
     int part_start = 0;
 #pragma unroll
     for (int m = 0; m < MT; ++m) Y[m] = 0.0f;
-    uint2 sv_prev = make_uint2(0, 0), bv_prev = make_uint2(0, 0);
     bool ok = true;
     UnitCursor ec = first;  // unit of the next epilogue
 
-    // Every worker warp runs the same sequence of epilogues and named barriers whatever happens: a wait
-    // that gives up only sets `ok` false (and the CTA's abort flag), so no warp is left at a barrier.
-    auto epilogue = [&](int jj, const uint2& sv, const uint2& bv) {
+    // Every epilogue warp runs the same sequence of epilogues and named barriers whatever happens: a
+    // wait that gives up only sets `ok` false (and the CTA's abort flag), so no warp is left at a barrier.
+    auto epilogue = [&](int jj) {
       const int a = jj & 1;
       const int tile = ec.tile, sl = ec.sl;
       ec.next(NSL);
       const int slot = slot_of(jj, sl);
       const uint32_t bpar = cache ? 0u : uint32_t((jj / kNB) & 1);
+      // dfull: the unit's MMAs are done; afull (already complete): orders the unpacking warp's scale /
+      // bias stores before the reads below
       if (ok && !*abort_flag) {
         if (!mbar_wait_backoff(&bars->dfull[h][a], uint32_t((jj >> 1) & 1), err, 32) ||
+            !mbar_wait_backoff(&bars->afull[h][a], uint32_t((jj >> 1) & 1), err, 32) ||
             !mbar_wait_backoff(&bars->bfull[slot], bpar, err, 32)) {
           ok = false;
           *abort_flag = 1;
@@ -494,7 +548,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const float2* xsc = reinterpret_cast<const float2*>(sm + kOffX + slot * kXSlot);
-      const uint32_t sw[2] = {sv.x, sv.y}, bw[2] = {bv.x, bv.y};
+      // this row's scales and biases of the chain's groups, left by the unpacking warp of the row
+      const uint4 sbv = *reinterpret_cast<const uint4*>(sm + kOffSB + ((a * 2 + h) * 128 + r) * 16);
+      const uint32_t sw[2] = {sbv.x, sbv.y}, bw[2] = {sbv.z, sbv.w};
       float H[MT];
 #pragma unroll
       for (int m = 0; m < MT; ++m) H[m] = 0.0f;
@@ -589,7 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int contributed = sl - part_start + 1;
       bar_chain0();
-      if (tid == 128) {
+      if (tid == kLeader) {
         // acquire-release: publishes the rows' partials (ordered before it by the barrier) and, for the
         // last arrival, makes the other CTAs' partials visible to this CTA
         const unsigned old = atom_add_acq_rel(&p.cnt[tile], unsigned(contributed));
@@ -615,60 +671,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             p.y[oi] = o;
           }
         }
-        if (tid == 128) p.cnt[tile] = 0u;  // ready for the next launch
+        if (tid == kLeader) p.cnt[tile] = 0u;  // ready for the next launch
       }
       bar_chain0();
       own = false;
     };
 
-    // Iteration j: the epilogue of unit j-2, then the unpacking of unit j.  Two units of A and of
-    // accumulators are in TMEM, so unit j reuses the slots of unit j-2 and its MMAs (issued after the
-    // unpacking of j) run while this warp does the epilogue of j-1 and the unpacking of j+1.
-    uint2 sv_prev2 = make_uint2(0, 0), bv_prev2 = make_uint2(0, 0);
-    for (int j = 0; j < nun; ++j) {
-      if (j >= 2) epilogue(j - 2, sv_prev2, bv_prev2);
-      sv_prev2 = sv_prev;
-      bv_prev2 = bv_prev;
-      const int st = j % kNS;
-      if (ok && !*abort_flag) {
-        if (!mbar_wait_backoff(&bars->full[st], uint32_t((j / kNS) & 1), err, 32)) {
-          ok = false;
-          *abort_flag = 1;
-        }
-      } else {
-        ok = false;
-      }
-      const uint8_t* sg = sm + st * kStage;
-      const uint2 sv = *reinterpret_cast<const uint2*>(sg + kWStage + r * 16 + 8 * h);
-      const uint2 bv = *reinterpret_cast<const uint2*>(sg + kWStage + kSStage + r * 16 + 8 * h);
-      const int a = j & 1;
-      const uint8_t* rowp = sg + h * (kMaxRows * kBox) + r * kBox;  // box h holds groups 4h .. 4h+3
-#pragma unroll
-      for (int gl = 0; gl < 4; ++gl) {
-        const int c0 = 2 * gl;
-        const uint4 w0 = *reinterpret_cast<const uint4*>(rowp + 16 * (c0 ^ rsw));
-        const uint4 w1 = *reinterpret_cast<const uint4*>(rowp + 16 * ((c0 + 1) ^ rsw));
-        const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        uint32_t o[16];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          o[2 * i] = wd[i] & 0x0F0F0F0Fu;
-          o[2 * i + 1] = (wd[i] >> 4) & 0x0F0F0F0Fu;
-        }
-        tmem_st16(tl + uint32_t(kABase + a * 128 + (4 * h + gl) * 16), o);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0 && ok) {
-        mbar_arrive(&bars->empty[st]);
-        mbar_arrive(&bars->afull[h][a]);
-      }
-      sv_prev = sv;
-      bv_prev = bv;
-    }
-    if (nun >= 2) epilogue(nun - 2, sv_prev2, bv_prev2);
-    if (nun >= 1) epilogue(nun - 1, sv_prev, bv_prev);
+    for (int j = 0; j < nun; ++j) epilogue(j);
   }
 
   tc_fence_before();
