@@ -76,8 +76,17 @@ int qmtp_qmv_affine_g64_split(const void* x, long long ldx, const void* w, const
                               void* workspace, size_t ws_bytes, void* stream);
 
 /* Tiling the affine kernel picks for an N x K matrix (split != 0: the _split entry point): weight
- * rows per tile, CTAs, work units (tile x 512-k slice).  Host-only query. */
-int qmtp_qmv_plan(int N, int K, int split, int* rows_per_tile, int* grid, int* units);
+ * rows per tile, CTAs, work units (tile x 512-k slice) and CTAs per thread-block cluster (> 1: each
+ * tile is shared by the CTAs of one cluster, whose first CTA adds the others' slice partials in order
+ * through distributed shared memory; every entry point may pick this mode, it needs no workspace).
+ * Host-only query (it may query the device's cluster occupancy once). */
+int qmtp_qmv_plan(int N, int K, int split, int* rows_per_tile, int* grid, int* units, int* cluster);
+
+/* Overrides the affine kernel's planner for every later call in the process (no counterpart in the
+ * reference; for tests and measurements): 0 = cost model (default), 1 = whole tiles per CTA only,
+ * 2 = cluster mode wherever the shape allows it, 3 = workspace split wherever a workspace is given.
+ * Every mode gives the same bits. */
+int qmtp_qmv_set_mode(int mode);
 
 /* Multi-row 4-bit GEMV, NVFP4 (e2m1 nibbles, e4m3 scale per 16): qmv_kernel.py:86-101 qmv_nvfp4.
  *   x bf16 [M, K]; w uint32 [N, K/8]; scales uint8 [N, K/16]; y bf16 [M, ldy]. K % 1024 == 0. */

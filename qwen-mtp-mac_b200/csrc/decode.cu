@@ -210,22 +210,6 @@ __global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld,
 constexpr int kAttnSplits = 8;
 constexpr int kAttnBatch = 8;   // keys a warp fetches at once in the score pass
 
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ float ld_dsmem(const float* local, uint32_t rank) {
-  uint32_t la = static_cast<uint32_t>(__cvta_generic_to_shared(local)), ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-  return v;
-}
-
 __global__ void __launch_bounds__(256)
 attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ gate, const uint16_t* __restrict__ kc,
                  const uint16_t* __restrict__ vc, int max_pos, int nq, int nkv, const int* __restrict__ pos_ptr,

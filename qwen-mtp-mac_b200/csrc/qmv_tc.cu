@@ -39,6 +39,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -76,6 +77,10 @@ constexpr long long kMaxSplitTiles = kCntBytes / 4;
 static_assert(kOffB % 1024 == 0 && kStage % 1024 == 0, "stage alignment");
 static_assert(kSmem <= 232448, "shared memory per CTA");
 constexpr int kLeader = 12 * 32;                   // first thread of the chain-0 epilogue warps
+// Cluster mode: a CTA holds at most this many slices of its tile, so that its per-slice partials
+// ([unit][kMaxTok][128] fp32, 2 KB a unit) fit in the B slots it leaves free.
+constexpr int kMaxClusterUnits = 6;
+static_assert(kMaxClusterUnits * kMaxTok * 128 * 4 <= (kNB - kMaxClusterUnits) * kBSlot, "cluster partials");
 
 // Barriers.  Per unit j: weight stage j % kNS (full / empty); A and accumulator slot a = j & 1 per
 // chain h (afull / dfull / dempty [h][a]); activation operand slot (bfull / bempty); the chain-1 partial
@@ -102,6 +107,7 @@ struct Params {
   unsigned* err;
   int U;              // units = ntiles * NSL (U * gridDim.x < 2^31, checked by the host)
   int ldy, N, K, NSL, R, ntiles, whole;
+  int cs;             // cluster mode (> 1): CTAs per tile, one tile per cluster
 };
 
 // (tile, slice) of consecutive units, advanced without divisions.
@@ -266,7 +272,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned* err = p.err;
 
   int u0, u1;
-  if (p.whole) {
+  const int cs = p.cs;
+  const uint32_t crank = cs > 1 ? cluster_rank() : 0u;
+  if (cs > 1) {
+    // cluster c = blockIdx.x / cs holds tile c; rank k takes slices [k, k + 1) * NSL / cs
+    const int per = NSL / cs;
+    u0 = int(blockIdx.x) / cs * NSL + int(crank) * per;
+    u1 = u0 + per;
+  } else if (p.whole) {
     u0 = int(blockIdx.x) * p.ntiles / int(gridDim.x) * NSL;
     u1 = int(blockIdx.x + 1) * p.ntiles / int(gridDim.x) * NSL;
   } else {
@@ -278,9 +291,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   // cache mode: every slice the CTA needs has its own B slot, built once up front; stream mode (more
   // than kNB distinct slices): slot j % kNB is rebuilt for each unit
   const bool cache = NSL <= kNB || nun <= kNB;
+  // slots by slice when a CTA may revisit slices (several tiles), else by unit (cluster mode: one
+  // tile, slots [0, nun); its slice partials go to the free slots after them)
+  const bool by_slice = NSL <= kNB && cs == 1;
   // B slot of unit j whose slice is sl
-  auto slot_of = [&](int j, int sl) { return cache ? (NSL <= kNB ? sl : j) : (j & (kNB - 1)); };
-  const int nbuild = cache ? min(nun, NSL <= kNB ? NSL : nun) : min(nun, kNB);
+  auto slot_of = [&](int j, int sl) { return cache ? (by_slice ? sl : j) : (j & (kNB - 1)); };
+  const int nbuild = cache ? min(nun, by_slice ? NSL : nun) : min(nun, kNB);
+  // cluster mode: this CTA's slice partials, [unit][row][kMaxTok] fp32
+  float* cpart = reinterpret_cast<float*>(sm + kOffB + nun * kBSlot);
+  float Y[MT];  // chain-0 epilogue threads: running sum of the current tile's slices
+#pragma unroll
+  for (int m = 0; m < MT; ++m) Y[m] = 0.0f;
 
   if (tid == 0) {
     prefetch_tmap(&tw);
@@ -518,11 +539,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = 32 * q + lane;
     const uint32_t tl = tmem + (uint32_t(32 * q) << 16);
     float* hx = reinterpret_cast<float*>(sm + kOffH);  // [2][kMaxTok][128] chain-1 partials
-    float Y[MT];
     bool own = false;  // chain 0: this CTA holds slice 0 of the current tile (Y is the tile's running prefix)
     int part_start = 0;
-#pragma unroll
-    for (int m = 0; m < MT; ++m) Y[m] = 0.0f;
     bool ok = true;
     UnitCursor ec = first;  // unit of the next epilogue
 
@@ -605,6 +623,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int m = 0; m < MT; ++m) P[m] = __fadd_rn(H[m], hb[m * 128 + r]);
       __syncwarp();
       if (lane == 0 && ok) mbar_arrive(&bars->hempty[jj & 1]);
+      if (cs > 1) {
+        // cluster mode: rank 0 keeps the running sum of slices [0, NSL / cs); the other ranks leave
+        // each slice's partial in shared memory for rank 0, which adds them in slice order at the end
+        if (crank == 0) {
+#pragma unroll
+          for (int m = 0; m < MT; ++m) Y[m] = jj == 0 ? P[m] : __fadd_rn(Y[m], P[m]);
+        } else {
+          float pv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+          for (int m = 0; m < MT; ++m) pv[m] = P[m];
+          *reinterpret_cast<float4*>(cpart + ((size_t)jj * 128 + r) * kMaxTok) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+        }
+        return;
+      }
       const size_t tbase = (size_t)tile * (size_t)NSL * (kMaxTok * 128);
       if (sl == 0) {
         own = true;
@@ -684,27 +716,95 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (cs > 1) {
+    // Every thread of every CTA of the cluster passes both barriers (no path leaves the kernel early,
+    // and every wait above is bounded).  The first makes the ranks' slice partials visible to rank 0,
+    // the second keeps every rank's shared memory alive until rank 0 has read it.
+    cluster_sync_all();
+    if (crank == 0 && warp >= 12 && warp < 16) {
+      const int r = 32 * (warp & 3) + lane;
+      const int row = int(blockIdx.x) / cs * R + r;
+      if (r < R && row < p.N) {
+        const int per = NSL / cs;
+        // rank k's slices, three loads in flight at a time, added in slice order
+        for (int k = 1; k < cs; ++k) {
+          for (int j0 = 0; j0 < per; j0 += 3) {
+            float4 v[3];
+#pragma unroll
+            for (int j = 0; j < 3; ++j)
+              if (j0 + j < per) v[j] = ld_dsmem_v4(cpart + ((size_t)(j0 + j) * 128 + r) * kMaxTok, uint32_t(k));
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+              if (j0 + j < per) {
+                const float pv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                for (int m = 0; m < MT; ++m) Y[m] = __fadd_rn(Y[m], pv[m]);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          uint16_t o = f2bf(Y[m]);
+          const size_t oi = (size_t)m * p.ldy + row;
+          if (p.res) o = f2bf(__fadd_rn(bf2f(p.res[oi]), bf2f(o)));
+          p.y[oi] = o;
+        }
+      }
+    }
+    cluster_sync_all();
+  }
 }
 
 // ----------------------------------------------------------------------------- host side
 struct Plan {
-  int R, G, ntiles, NSL, whole;
+  int R, G, ntiles, NSL, whole, cs;
   long long U;
 };
 // Unit indices are 32-bit in the kernel: U * grid must stay below 2^31.
 constexpr long long kMaxUnitProduct = (1LL << 31) - 1;
 
-// Rows per tile and grid, from a cost model of the slowest CTA, fitted to B200 timings of this kernel:
-// about 2 us of setup and first weight latency, 0.45 us per activation slice built, about 1.2 us per
-// unit (16 MMAs of ~98 tensor cycles each, plus the pipeline; the weight bytes of a 128-row unit stream
-// in 0.84 us at the per-SM share of HBM bandwidth), and about 5 us to finish a tile split between CTAs.
-// Ties go to the larger tile.
+// Clusters of `cs` CTAs (228 KB of shared memory each) that can be resident at once on this device.
+static int max_clusters(int cs);
+
+// Planner override for tests and measurements (qmtp_qmv_set_mode): 0 = cost model, 1 = whole tiles
+// only, 2 = cluster mode where the shape allows it, 3 = workspace split where a workspace is given.
+static std::atomic<int> g_mode{0};
+
+// Rows per tile, grid and mode, from a cost model of the slowest CTA, fitted to B200 timings of this
+// kernel: about 2 us of setup and first weight latency, 0.45 us per activation slice built, about
+// 1.1 us per unit (16 MMAs of ~98 tensor cycles each, plus the pipeline; the weight bytes of a 128-row
+// unit stream in 0.84 us at the per-SM share of HBM bandwidth), about 5 us to finish a tile split
+// between CTAs through the workspace and about 1 us to finish it inside a cluster.  Ties go to the
+// larger tile and to the earlier mode (whole tiles, cluster, workspace split).
 static Plan make_plan(int N, int K, bool split, int sms) {
   const int NSL = K / 512;
   Plan best{};
   double best_cost = 1e30;
+  const int mode = g_mode.load(std::memory_order_relaxed);
+  const bool try_cluster = mode == 0 || mode == 2;
+  if (mode == 1) split = false;
+  // cluster mode: one tile per cluster of cs CTAs, at most kMaxClusterUnits slices per CTA, all
+  // clusters resident at once
+  for (int cs = 2; cs <= 4 && try_cluster; cs *= 2) {
+    if (NSL % cs || NSL / cs > kMaxClusterUnits) continue;
+    const int mc = max_clusters(cs);
+    for (int R = kMaxRows; R >= kMinRows; R -= 8) {
+      const int T = (N + R - 1) / R;
+      if (T > mc) continue;
+      const int per = NSL / cs;
+      const double unit_us = std::max(R * 288.0 / 44.0e3, 1.1);
+      const double cost = 2.0 + 0.45 * per + per * unit_us + 1.0;
+      if (cost < best_cost * 0.999) {
+        best_cost = cost;
+        best = Plan{R, T * cs, T, NSL, 0, cs, (long long)T * NSL};
+      }
+    }
+  }
+  if (mode == 2 && best_cost < 1e30) return best;
   for (int w = 0; w < (split ? 2 : 1); ++w) {
     const bool whole = !split || w == 1;
+    if (mode == 3 && whole && split) continue;
     for (int R = kMaxRows; R >= kMinRows; R -= 8) {
       const int T = (N + R - 1) / R;
       long long G, per;
@@ -719,11 +819,11 @@ static Plan make_plan(int N, int K, bool split, int sms) {
         per = (long long)((T + G - 1) / G) * NSL;
         slices = NSL;
       }
-      const double unit_us = std::max(R * 288.0 / 44.0e3, 1.2);
+      const double unit_us = std::max(R * 288.0 / 44.0e3, 1.1);
       const double cost = 2.0 + 0.45 * std::min(slices, kNB) + double(per) * unit_us + (whole ? 0.0 : 5.0);
       if (cost < best_cost * 0.999) {
         best_cost = cost;
-        best = Plan{R, int(G), T, NSL, whole ? 1 : 0, (long long)T * NSL};
+        best = Plan{R, int(G), T, NSL, whole ? 1 : 0, 1, (long long)T * NSL};
       }
     }
   }
@@ -743,17 +843,52 @@ static bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const v
 }
 
 template <int MT>
-static int launch_mt(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb, const Params& p, int G,
-                     cudaStream_t st) {
-  auto kern = qmv_tc_kernel<MT>;
+static bool prepare() {
   static std::once_flag once;
   static bool ok = false;
   std::call_once(once, [&] {
-    ok = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) == cudaSuccess;
+    ok = cudaFuncSetAttribute(qmv_tc_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) == cudaSuccess;
   });
-  if (!ok) return QMTP_ERR_CUDA;
-  launch_kernel(kern, dim3(G), dim3(kThreads), kSmem, st, tw, ts, tb, p);
+  return ok;
+}
+
+template <int MT>
+static int launch_mt(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb, const Params& p, int G,
+                     cudaStream_t st) {
+  if (!prepare<MT>()) return QMTP_ERR_CUDA;
+  launch_kernel_cluster(qmv_tc_kernel<MT>, dim3(G), dim3(kThreads), kSmem, st, p.cs, tw, ts, tb, p);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+static int max_clusters(int cs) {
+  static std::mutex mu;
+  static int cache[2][64] = {};  // [cs == 4][device]: clusters + 1, 0 = not queried
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lk(mu);
+  int& c = cache[cs == 4 ? 1 : 0][dev];
+  if (c == 0) {
+    int n = 0;
+    if (prepare<1>()) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(unsigned(cs));
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = kSmem;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = unsigned(cs);
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, qmv_tc_kernel<1>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+    }
+    c = n + 1;
+  }
+  return c - 1;
 }
 
 static size_t ws_part_bytes(int N, int K) {
@@ -797,6 +932,7 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
   p.R = pl.R;
   p.ntiles = pl.ntiles;
   p.whole = pl.whole;
+  p.cs = pl.cs;
   p.U = int(pl.U);
   p.err = device_error_ptr();
   if (split) {
@@ -821,11 +957,12 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
   return QMTP_OK;
 }
 
-int qmv_tc_plan(int N, int K, int split, int* rows, int* grid, int* units) {
+int qmv_tc_plan(int N, int K, int split, int* rows, int* grid, int* units, int* cluster) {
   const tq::Plan pl = tq::make_plan(N, K, split != 0, sm_count());
   if (rows) *rows = pl.R;
   if (grid) *grid = pl.G;
   if (units) *units = int(pl.U);
+  if (cluster) *cluster = pl.cs;
   return QMTP_OK;
 }
 
@@ -853,7 +990,13 @@ extern "C" int qmtp_qmv_affine_g64_split(const void* x, long long ldx, const voi
   return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, workspace, ws_bytes, stream);
 }
 
-extern "C" int qmtp_qmv_plan(int N, int K, int split, int* rows_per_tile, int* grid, int* units) {
+extern "C" int qmtp_qmv_set_mode(int mode) {
+  if (mode < 0 || mode > 3) return QMTP_ERR_ARG;
+  tq::g_mode.store(mode, std::memory_order_relaxed);
+  return QMTP_OK;
+}
+
+extern "C" int qmtp_qmv_plan(int N, int K, int split, int* rows_per_tile, int* grid, int* units, int* cluster) {
   if (N < 1 || K < 512 || K % 512) return QMTP_ERR_SHAPE;
-  return qmv_tc_plan(N, K, split, rows_per_tile, grid, units);
+  return qmv_tc_plan(N, K, split, rows_per_tile, grid, units, cluster);
 }

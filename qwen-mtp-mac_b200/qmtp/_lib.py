@@ -38,7 +38,8 @@ SIGNATURES: dict[str, list] = {
     "qmtp_quantize_affine_g64": [_P, _P, _P, _P, _I, _I, _P],
     "qmtp_qmv_affine_g64_split": [_P, ctypes.c_longlong, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, ctypes.c_size_t,
                                   _P],
-    "qmtp_qmv_plan": [_I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)],
+    "qmtp_qmv_plan": [_I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)],
+    "qmtp_qmv_set_mode": [_I],
 }
 
 
@@ -176,8 +177,15 @@ def device_error(clear: bool = True) -> int:
     return v.value
 
 
+def qmv_set_mode(mode: int) -> None:
+    """Planner override of the affine qmv kernel (0 cost model, 1 whole tiles, 2 clusters, 3 workspace
+    split); process-wide."""
+    check(lib().qmtp_qmv_set_mode(int(mode)), "qmv_set_mode")
+
+
 def qmv_plan(N: int, K: int, split: bool = True) -> dict:
-    """Tiling the affine qmv kernel picks for an N x K matrix: rows per tile, CTAs, work units."""
-    vals = [ctypes.c_int(0) for _ in range(3)]
+    """Tiling the affine qmv kernel picks for an N x K matrix: rows per tile, CTAs, work units and
+    CTAs per cluster (1: no cluster)."""
+    vals = [ctypes.c_int(0) for _ in range(4)]
     check(lib().qmtp_qmv_plan(N, K, int(split), *[ctypes.byref(v) for v in vals]), "qmv_plan")
-    return dict(zip(("rows_per_tile", "grid", "units"), (v.value for v in vals)))
+    return dict(zip(("rows_per_tile", "grid", "units", "cluster"), (v.value for v in vals)))

@@ -10,6 +10,18 @@ from tests._util import affine_layer, randn_bf16, to_np, to_torch
 
 pytestmark = pytest.mark.gpu
 G = Path(__file__).resolve().parent / "golden"
+# (planner mode, workspace given): the cost model with and without a workspace, whole tiles only,
+# clusters wherever the shape allows them, the workspace split wherever a workspace is given
+MODES = [(0, True), (0, False), (1, True), (2, False), (3, True)]
+
+
+@pytest.fixture
+def planner():
+    """Sets the affine qmv planner mode for a test; restores the cost model afterwards."""
+    from qmtp import _lib
+
+    yield _lib.qmv_set_mode
+    _lib.qmv_set_mode(0)
 
 
 def _run_affine(x, wq, s, b, dev, ldy=None, split=True, res=None):
@@ -28,13 +40,14 @@ def _run_affine(x, wq, s, b, dev, ldy=None, split=True, res=None):
 
 @pytest.mark.parametrize("K", [512, 1024, 2048, 4096, 8192, 12288])
 @pytest.mark.parametrize("M", [1, 2, 3, 4])
-def test_qmv_affine_bit_exact(K, M, dev):
+def test_qmv_affine_bit_exact(K, M, dev, planner):
     for N in (1, 37, 1000, 4096):
         _, wq, s, b = affine_layer(N, K, seed=K + N)
         x = randn_bf16((M, K), M)
         ref = ops.qmv_affine(x, wq, s, b)
-        for split in (True, False):
-            assert np.array_equal(_run_affine(x, wq, s, b, dev, split=split), ref), (K, M, N, split)
+        for mode, split in MODES:
+            planner(mode)
+            assert np.array_equal(_run_affine(x, wq, s, b, dev, split=split), ref), (K, M, N, mode, split)
 
 
 def test_qmv_affine_shared_workspace_across_shapes(dev):
@@ -65,9 +78,10 @@ def test_qmv_affine_config1_bit_exact(M, dev):
 
 @pytest.mark.parametrize("N,K", [(12352, 4096), (4096, 4096), (4096, 12288), (24576, 4096), (10240, 4096),
                                  (4096, 8192), (777, 12288)])
-def test_qmv_affine_decoder_shapes_split(N, K, dev):
-    """The decoder's projection shapes: split tiles (slice partials finished by the last CTA) give the
-    oracle's bits, the workspace counters return to zero, and repeated calls agree."""
+def test_qmv_affine_decoder_shapes(N, K, dev, planner):
+    """The decoder's projection shapes in every planner mode: split tiles (slice partials finished by
+    the last CTA through the workspace, or by the first CTA of a cluster through distributed shared
+    memory) give the oracle's bits, the workspace counters return to zero, repeated calls agree."""
     from qmtp import qmv_kernel, _lib
 
     _, wq, s, b = affine_layer(N, K, seed=N + K)
@@ -75,37 +89,47 @@ def test_qmv_affine_decoder_shapes_split(N, K, dev):
     ref = ops.qmv_affine(x, wq, s, b)
     ws = torch.zeros(_lib.lib().qmtp_qmv_workspace(N, K), dtype=torch.uint8, device=dev)
     xt, wt, st, bt = (to_torch(a, dev) for a in (x, wq, s, b))
-    for _ in range(3):
-        got = to_np(qmv_kernel.qmv_affine(xt, wt, st, bt, ws=ws))
-        assert np.array_equal(got, ref), (N, K)
-    plan = _lib.qmv_plan(N, K, True)
-    T = (N + plan["rows_per_tile"] - 1) // plan["rows_per_tile"]
+    for mode in (0, 1, 2, 3):
+        planner(mode)
+        for _ in range(2):
+            got = to_np(qmv_kernel.qmv_affine(xt, wt, st, bt, ws=ws))
+            assert np.array_equal(got, ref), (N, K, mode)
+        plan = _lib.qmv_plan(N, K, True)
+        T = (N + plan["rows_per_tile"] - 1) // plan["rows_per_tile"]
+        assert plan["units"] == T * (K // 512)
+        if plan["cluster"] > 1:
+            assert plan["grid"] == T * plan["cluster"] and (K // 512) % plan["cluster"] == 0
+        if mode == 2 and N == 4096:
+            assert plan["cluster"] > 1, plan
+        if mode == 1:
+            assert plan["cluster"] == 1 and plan["grid"] <= T
     head = ws.view(torch.int32)[:16384]
     assert int(head.abs().sum()) == 0, "arrival counters left non-zero"
-    assert plan["units"] == T * (K // 512)
 
 
-def test_qmv_affine_residual_in_place(dev):
+def test_qmv_affine_residual_in_place(dev, planner):
     _, wq, s, b = affine_layer(4096, 12288, seed=3)
     x = randn_bf16((3, 12288), 4)
     res = randn_bf16((3, 4096), 6)
     y = ops.qmv_affine(x, wq, s, b)
     ref = ops.f32_to_bf16(ops.bf16_to_f32(res) + ops.bf16_to_f32(y))
-    for split in (True, False):
-        assert np.array_equal(_run_affine(x, wq, s, b, dev, split=split, res=res), ref)
+    for mode, split in MODES:
+        planner(mode)
+        assert np.array_equal(_run_affine(x, wq, s, b, dev, split=split, res=res), ref), mode
 
 
-def test_qmv_affine_many_rows_and_ldy(dev):
+def test_qmv_affine_many_rows_and_ldy(dev, planner):
     _, wq, s, b = affine_layer(333, 4096, seed=11)
     x = randn_bf16((9, 4096), 12)
     ref = ops.qmv_affine(x, wq, s, b)
-    for split in (True, False):
+    for mode, split in MODES:
+        planner(mode)
         got = _run_affine(x, wq, s, b, dev, ldy=400, split=split)
         assert np.array_equal(got[:, :333], ref)
         assert np.all(got[:, 333:] == ops.f32_to_bf16(np.float32([7.0]))[0])
 
 
-def test_qmv_affine_extreme_x_bit_exact(dev):
+def test_qmv_affine_extreme_x_bit_exact(dev, planner):
     """Activations over bf16's whole finite range, all-zero groups, subnormal-only groups, and a group
     holding an infinity (its token row becomes NaN, the others are unaffected)."""
     r = np.random.default_rng(31)
@@ -122,8 +146,9 @@ def test_qmv_affine_extreme_x_bit_exact(dev):
     _, wq, s, b = affine_layer(N, K, seed=8)
     ref = ops.qmv_affine(x, wq, s, b)
     assert np.isnan(ops.bf16_to_f32(ref[2])).all()
-    for split in (True, False):
-        assert np.array_equal(_run_affine(x, wq, s, b, dev, split=split), ref)
+    for mode, split in MODES:
+        planner(mode)
+        assert np.array_equal(_run_affine(x, wq, s, b, dev, split=split), ref), mode
 
 
 def test_qmv_affine_split_ldx(dev):
