@@ -319,6 +319,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait: gives up after `limit` polls, records DEVERR_TIMEOUT and returns false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err,
                                                   uint32_t limit = (1u << 24)) {
+#pragma unroll 1  // a wait loop: unrolling only grows the code
   for (uint32_t it = 0; it < limit; ++it)
     if (mbar_try_wait(bar, parity)) return true;
   if (err) atomicOr(err, DEVERR_TIMEOUT);
@@ -341,6 +342,7 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // Bounded sleeping wait: at most `limit` polls of up to 1 us each; on timeout records DEVERR_TIMEOUT.
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, unsigned* err,
                                                 uint32_t limit = (1u << 20)) {
+#pragma unroll 1  // a wait loop: unrolling only grows the code
   for (uint32_t it = 0; it < limit; ++it)
     if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
   if (err) atomicOr(err, DEVERR_TIMEOUT);
@@ -351,6 +353,7 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
 // warps that run ahead of the critical one take no issue slots while they wait.
 __device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, unsigned* err, uint32_t ns,
                                                   uint32_t limit = (1u << 22)) {
+#pragma unroll 1  // a wait loop: unrolling only grows the code
   for (uint32_t it = 0; it < limit; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     __nanosleep(ns);
@@ -361,6 +364,7 @@ __device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity
 // Bounded tight wait for the thread on the critical path (no sleep between polls).
 __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, unsigned* err,
                                                uint32_t limit = (1u << 26)) {
+#pragma unroll 1  // a wait loop: unrolling only grows the code
   for (uint32_t it = 0; it < limit; ++it)
     if (mbar_try_wait(bar, parity)) return true;
   if (err) atomicOr(err, DEVERR_TIMEOUT);

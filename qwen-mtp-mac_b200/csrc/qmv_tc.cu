@@ -143,8 +143,11 @@ __device__ __forceinline__ float pow2f(int k) {
 // of two that are normal fp32 numbers; bf16 x has 8 significant bits and |x| < 2^(E+1), so both
 // products are exact whenever the result is at least 1/2 in magnitude (a product that underflows
 // belongs to an element that rounds to 0 either way), and the conversion does the one rounding.
-__device__ __forceinline__ int grid_value(uint32_t h, float s1, float s2) {
-  return __float2int_rn(__fmul_rn(__fmul_rn(bf2f(uint16_t(h)), s1), s2));
+// The rounding is done by adding 1.5 * 2^23: every |x * 2^(19-E)| is below 2^20, so the sum lies in
+// [2^23, 2^24), where the fp32 spacing is 1 and the addition rounds to the nearest integer, ties to
+// even; the integer is the sum's low mantissa bits.
+__device__ __forceinline__ int grid_value(float x, float s1, float s2) {
+  return __float_as_int(__fadd_rn(__fmul_rn(__fmul_rn(x, s1), s2), 12582912.0f)) - 0x4B400000;
 }
 // The first NC (<= 12) accumulator columns of a lane quarter (32x32b shape): only the 3 * MT limb
 // columns of a group are read.  Completion is awaited by the caller (tmem_ld_wait).
@@ -192,30 +195,25 @@ __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
 // 8 then the odd k, as the nibble unpacking orders the weights) and, from lane 0 of the group, the
 // group factors (c, xf).  All 8 lanes of a group are in one warp.
 __device__ __forceinline__ void prep_task(uint4 v, int m, int g, int li, uint8_t* bimg, float2* xsc) {
-  const uint32_t hv[8] = {v.x & 0xFFFFu, v.x >> 16, v.y & 0xFFFFu, v.y >> 16,
-                          v.z & 0xFFFFu, v.z >> 16, v.w & 0xFFFFu, v.w >> 16};
-  uint32_t amax = 0, nf = 0;
+  // largest magnitude of the group as a bf16 bit pattern (patterns order like magnitudes; an infinity
+  // or NaN has a pattern >= 0x7F80, above every finite one)
+  const uint32_t a2 = __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu), __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
+  uint32_t amax = max(a2 & 0xFFFFu, a2 >> 16);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const uint32_t a = hv[e] & 0x7FFFu;
-    nf |= a >= 0x7F80u ? 1u : 0u;
-    amax = max(amax, a);
-  }
-#pragma unroll
-  for (int d = 1; d < 8; d <<= 1) {
-    amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, d));
-    nf |= __shfl_xor_sync(0xFFFFFFFFu, nf, d);
-  }
-  const bool zero = nf || amax == 0;
+  for (int d = 1; d < 8; d <<= 1) amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, d));
+  const bool nf = amax >= 0x7F80u;
   const int ef = int(amax >> 7);
   const int E = ef ? ef - 127 : -133 + (31 - __clz(int(amax & 127u) | 1));
-  const int k = zero ? 0 : 19 - E;  // in [-108, 152]
+  // k in [-109, 152]: both factors are normal fp32 powers of two.  An all-zero group gives x_q = 0; a
+  // group with a non-finite element gets NaN factors below, whatever its x_q.
+  const int k = 19 - E;
   const float s1 = pow2f(k >> 1), s2 = pow2f(k - (k >> 1));
+  const float xv[8] = {bflo(v.x), bfhi(v.x), bflo(v.y), bfhi(v.y), bflo(v.z), bfhi(v.z), bflo(v.w), bfhi(v.w)};
   int xq[8];
   int xs = 0;
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    xq[e] = zero ? 0 : grid_value(hv[e], s1, s2);
+    xq[e] = grid_value(xv[e], s1, s2);
     xs += xq[e];
   }
   // limb l of element e is byte 0 of (x_q >> 7l) (l0, l1 masked to 7 bits); the even elements fill the
@@ -356,33 +354,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_trigger();
   pdl_wait();
 
-  // Builds the activation operand of units [j0, j0 + nb) (their slots) with `nthr` threads starting
-  // at thread `t0`: all loads first, then the tasks in slot order, one bfull arrival per warp batch.
-  auto build = [&](int j0, int nb, int t0, int nthr) {
+  // Builds the activation operand of units [j0, j0 + nb) (their slots) with `nthr` threads, this one
+  // being number `me` of them: the tasks in slot order, each task's x loaded two tasks ahead, one
+  // bfull arrival per warp batch.  The loop is not unrolled: the kernel's roles run different code at
+  // the same time, and a small loop body keeps them in the instruction cache.
+  constexpr int kBuilders = 320;  // up-front build: warps 0, 2 and 12-19
+  auto build = [&](int j0, int nb, int me, int nthr) {
     const int per_slot = 64 * MT;
     const int total = nb * per_slot;
-    const int me = tid - t0;
     const int sbase = (first.sl + j0) % NSL;  // slice of unit j0
-    // trips per thread: up to kNB slots over all threads, or one slot over one warp
-    constexpr int kMaxIt = (kNB * 64 * MT + kThreads - 1) / kThreads > 2 * MT ? (kNB * 64 * MT + kThreads - 1) / kThreads
-                                                                                : 2 * MT;
-    uint4 v[kMaxIt];
-#pragma unroll
-    for (int i = 0; i < kMaxIt; ++i) {
-      const int t = me + i * nthr;
-      if (t < total) {
-        const int jb = t / per_slot, r = t - jb * per_slot;
-        const int sl = sbase + jb < NSL ? sbase + jb : sbase + jb - NSL;
-        const int m = r >> 6, g = (r >> 3) & 7, li = r & 7;
-        v[i] = *reinterpret_cast<const uint4*>(p.x + (size_t)m * (size_t)p.ldx + (size_t)sl * 512 + g * 64 + li * 8);
-      }
-    }
+    auto load = [&](int t) {
+      const int jb = t / per_slot, r = t - jb * per_slot;
+      const int sl = sbase + jb < NSL ? sbase + jb : sbase + jb - NSL;
+      const int m = r >> 6, g = (r >> 3) & 7, li = r & 7;
+      return *reinterpret_cast<const uint4*>(p.x + (size_t)m * (size_t)p.ldx + (size_t)sl * 512 + g * 64 + li * 8);
+    };
+    uint4 va = make_uint4(0u, 0u, 0u, 0u), vb = va;
+    if (me < total) va = load(me);
+    if (me + nthr < total) vb = load(me + nthr);
     int cur_slot = -1;  // slot of this warp's open batch run (its bfull arrivals are owed)
     int batches = 0;
-#pragma unroll
-    for (int i = 0; i < kMaxIt; ++i) {
-      const int t = me + i * nthr;
-      if (t < total) {  // warp-uniform: total and nthr are multiples of 32
+#pragma unroll 1
+    for (int t = me; t < total; t += nthr) {  // warp-uniform: total and nthr are multiples of 32
+      const uint4 v = va;
+      va = vb;
+      if (t + 2 * nthr < total) vb = load(t + 2 * nthr);
+      {
         const int jb = t / per_slot, r = t - jb * per_slot;
         const int slot = slot_of(j0 + jb, sbase + jb < NSL ? sbase + jb : sbase + jb - NSL);
         if (slot != cur_slot && cur_slot >= 0) {
@@ -395,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         cur_slot = slot;
         ++batches;
         const int m = r >> 6, g = (r >> 3) & 7, li = r & 7;
-        prep_task(v[i], m, g, li, sm + kOffB + slot * kBSlot, reinterpret_cast<float2*>(sm + kOffX + slot * kXSlot));
+        prep_task(v, m, g, li, sm + kOffB + slot * kBSlot, reinterpret_cast<float2*>(sm + kOffX + slot * kXSlot));
       }
     }
     if (cur_slot >= 0) {
@@ -406,8 +403,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   };
 
-  // every warp builds the activation operand first (the weights are still in flight)
-  build(0, nbuild, 0, kThreads);
+  // The activation operand is built up front by the producer warp (after its first requests), warp 2
+  // and the epilogue warps (idle until the first accumulators are ready), while the unpacking warps
+  // already turn the first weight stages into A operands and the MMA issuers wait for the first slot.
+  if (warp == 0 || warp == 2 || warp >= 12) build(0, nbuild, warp == 0 ? lane : warp == 2 ? 32 + lane : tid - 320, kBuilders);
 
   if (warp == 0) {
     // ------------------------------------------------------------------- TMA producer
@@ -479,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           *abort_flag = 1;
           break;
         }
-        build(j, 1, 64, 32);
+        build(j, 1, lane, 32);
       }
     }
   } else if (warp < 12) {
@@ -578,6 +577,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int gl = 0; gl < 4; ++gl) tmem_ld_cols<NC>(tl + uint32_t(kDBase + a * 128 + (4 * h + gl) * 16), v[gl]);
       tmem_ld_wait();
+      // the accumulators and this unit's scales / biases are in registers: release the A, D and side
+      // buffer slots of the chain to unit jj + 2
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && ok) mbar_arrive(&bars->dempty[h][a]);
 #pragma unroll
       for (int gl = 0; gl < 4; ++gl) {
         const int g = 4 * h + gl;
@@ -591,11 +595,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           H[m] = __fmaf_rn(b, cx.y, H[m]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0 && ok) {
-        mbar_arrive(&bars->dempty[h][a]);
-        if (!cache) mbar_arrive(&bars->bempty[slot]);
+      if (!cache) {
+        __syncwarp();
+        if (lane == 0 && ok) mbar_arrive(&bars->bempty[slot]);
       }
       float* hb = hx + (jj & 1) * (kMaxTok * 128);
       if (h == 1) {
@@ -726,20 +728,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = int(blockIdx.x) / cs * R + r;
       if (r < R && row < p.N) {
         const int per = NSL / cs;
-        // rank k's slices, three loads in flight at a time, added in slice order
+        // the other ranks' slices in slice order: a rank's loads all in flight at once, then the adds
+#pragma unroll 1
         for (int k = 1; k < cs; ++k) {
-          for (int j0 = 0; j0 < per; j0 += 3) {
-            float4 v[3];
+          float4 v[kMaxClusterUnits];
 #pragma unroll
-            for (int j = 0; j < 3; ++j)
-              if (j0 + j < per) v[j] = ld_dsmem_v4(cpart + ((size_t)(j0 + j) * 128 + r) * kMaxTok, uint32_t(k));
+          for (int j = 0; j < kMaxClusterUnits; ++j)
+            if (j < per) v[j] = ld_dsmem_v4(cpart + ((size_t)j * 128 + r) * kMaxTok, uint32_t(k));
 #pragma unroll
-            for (int j = 0; j < 3; ++j) {
-              if (j0 + j < per) {
-                const float pv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+          for (int j = 0; j < kMaxClusterUnits; ++j) {
+            if (j < per) {
+              const float pv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
 #pragma unroll
-                for (int m = 0; m < MT; ++m) Y[m] = __fadd_rn(Y[m], pv[m]);
-              }
+              for (int m = 0; m < MT; ++m) Y[m] = __fadd_rn(Y[m], pv[m]);
             }
           }
         }
