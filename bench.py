@@ -281,6 +281,8 @@ def run_ours(args):
         torch.cuda.empty_cache()
         res["moe_ep"] = moe_ep_measure(args, dev, rank, world)
         dist.barrier()
+        res["lmhead_shard"] = head_shard_measure(args, dev, rank, world)
+        dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res), flush=True)
@@ -527,6 +529,61 @@ def moe_ep_measure(args, dev, rank, world):
                         "one CUDA graph per layer",
             "timing": "CUDA events around graph replays, max over ranks",
             "device_error": int(derr.item())}
+
+
+def head_shard_measure(args, dev, rank, world):
+    """Config 3's two-stage head (V = 248320, D = 4096, M = 3, k = 64) sharded by vocabulary over the
+    initialised process group (ShardedTwoStageHead: local coarse GEMV + top-k + rescoring on V/G rows,
+    NCCL all-gather of the candidate lists, merge), against the whole head on one GPU.  Device time per
+    call, max over ranks; `identical` = every rank's result equals the single-GPU head's bit for bit."""
+    import torch
+    import torch.distributed as dist
+
+    from qmtp.lm_head2 import ShardedTwoStageHead, TwoStageHead
+    from qmtp.qmv_kernel import QuantizedLinear, quantize
+
+    V, D, M, k = 248320, 4096, 3, 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    W = (torch.randn(V, D, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    h = torch.randn(M, D, generator=g, device=dev).to(torch.bfloat16)
+    coarse = QuantizedLinear(*quantize(W))
+    whole = TwoStageHead(W, k, coarse)
+    sharded = ShardedTwoStageHead.from_full(W, k, coarse=coarse)
+
+    def timed(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / reps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    reps = max(args.steps, 10)
+    ref = [t.clone() for t in whole.select(h)]
+    got = sharded.select(h)
+    same = all(torch.equal(a.view(torch.int16) if a.dtype == torch.bfloat16 else a,
+                           b.view(torch.int16) if b.dtype == torch.bfloat16 else b) for a, b in zip(ref, got))
+    ok = torch.tensor([1 if same else 0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    us_whole = timed(lambda: whole.select(h), reps)
+    us_shard = timed(lambda: sharded.select(h), reps)
+    local_bytes = sharded.weight.shape[0] * (D // 2 + (D // 64) * 4)
+    del whole, sharded, W, coarse
+    torch.cuda.empty_cache()
+    return {"kernel": "lmhead2_shard", "workload": f"two-stage head V={V} D={D} M={M} k={k} sharded by "
+                                                   f"vocabulary over {world} GPUs",
+            "n_gpus": world, "us_per_call": round(us_shard, 2), "us_per_call_1gpu": round(us_whole, 2),
+            "speedup": round(us_whole / us_shard, 3), "local_coarse_bytes": int(local_bytes),
+            "identical": bool(ok.item()), "reps": reps,
+            "timing": "CUDA events around eager calls (local head, 2 NCCL all-gathers, merge), max over ranks"}
 
 
 # ------------------------------------------------------------------------------ reference arm

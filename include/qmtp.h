@@ -199,6 +199,23 @@ int qmtp_lmhead2(const void* h, const void* wq, const void* scales, const void* 
                  const void* w_fine, int M, int V, int K, int k, int* out_idx, void* out_fine,
                  int* out_argmax, void* coarse_out, void* workspace, size_t ws_bytes, void* stream);
 
+/* Two-stage head sharded by vocabulary over G GPUs (lm_head2.py:111-117 split by output rows; the
+ * NCCL exchange between the two calls is the host's, e.g. torch.distributed all_gather):
+ *   qmtp_lmhead2_shard: on the rank holding vocabulary rows [v0, v0 + Vs): coarse logits of the shard,
+ *     its top k (value descending, index ascending) and their exact bf16 logits.  out_words uint64
+ *     [M, k]: (order key of the coarse logit << 32) | (0xFFFFFFFF - global index), so a larger word is
+ *     a better candidate; out_fine bf16 [M, k].  workspace: qmtp_lmhead2_shard_workspace(M, Vs, k).
+ *   qmtp_lmhead2_merge: every rank's lists gathered rank-major (words [G, M, k], fine [G, M, k]) ->
+ *     the same out_idx / out_fine / out_argmax as qmtp_lmhead2 on the whole vocabulary, bit for bit
+ *     (each shard's list holds its own best k, so the best k of the union are the global best k).
+ *     G * k <= 4096. */
+size_t qmtp_lmhead2_shard_workspace(int M, int Vs, int k);
+int qmtp_lmhead2_shard(const void* h, const void* wq, const void* scales, const void* biases,
+                       const void* w_fine, int M, int Vs, int K, int k, long long v0, void* out_words,
+                       void* out_fine, void* workspace, size_t ws_bytes, void* stream);
+int qmtp_lmhead2_merge(const void* words, const void* fine, int G, int M, int k, int* out_idx,
+                       void* out_fine, int* out_argmax, void* stream);
+
 /* The two-stage head of qmtp_lmhead2 for callers that cannot allocate device memory (a plugin
  * living inside another framework's memory pool, code that may run during stream capture, a
  * serving loop that must not synchronise the device through cudaMalloc).  This entry point has no

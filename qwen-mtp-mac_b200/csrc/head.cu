@@ -121,11 +121,13 @@ topk_partial_kernel(const uint16_t* __restrict__ vals, long long ld, int V, int 
 constexpr int kMergeThreads = 1024;
 
 // Sorts G*k candidate words of row m (descending), keeps k, rescoring + argmax.  W may be null
-// (selection only).
+// (selection only).  out_words (may be null): the k kept words with their vocabulary index moved
+// up by idx_base (a vocabulary shard's first row), the form qmtp_lmhead2_merge takes.
 __global__ void __launch_bounds__(kMergeThreads)
 topk_merge_kernel(const uint64_t* __restrict__ cand, int G, int k, int NP, const uint16_t* __restrict__ W,
                   const uint16_t* __restrict__ h, int K, int32_t* __restrict__ out_idx,
-                  uint16_t* __restrict__ out_fine, int32_t* __restrict__ out_amax) {
+                  uint16_t* __restrict__ out_fine, int32_t* __restrict__ out_amax, uint32_t idx_base,
+                  uint64_t* __restrict__ out_words) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ __align__(16) unsigned char sm_raw[];
@@ -146,7 +148,10 @@ topk_merge_kernel(const uint64_t* __restrict__ cand, int G, int k, int NP, const
       __syncthreads();
     }
   }
-  for (int j = tid; j < k; j += blockDim.x) out_idx[(long long)m * k + j] = int32_t(cand_idx(s[j]));
+  for (int j = tid; j < k; j += blockDim.x) {
+    out_idx[(long long)m * k + j] = int32_t(cand_idx(s[j]));
+    if (out_words) out_words[(long long)m * k + j] = cand_word(uint32_t(s[j] >> 32), cand_idx(s[j]) + idx_base);
+  }
   if (!W) return;
   const uint16_t* hr = h + (long long)m * K;
   for (int j = warp; j < k; j += blockDim.x / 32) {
@@ -226,6 +231,69 @@ __global__ void argmax_final_kernel(const uint64_t* __restrict__ part, int G, in
   if (lane == 0) out[m] = int32_t(cand_idx(best));
 }
 
+// Merges the candidate lists of G vocabulary shards (words [G][M][k] with global indices, fine bf16
+// logits alongside): per row the k best words over all shards, in order, their fine logits, and the
+// argmax of those.  The best k of the union equal the best k of the whole vocabulary, because every
+// shard's list holds its own best k under the same order.
+constexpr int kShardMergeThreads = 512;
+__global__ void __launch_bounds__(kShardMergeThreads)
+lmhead2_merge_kernel(const uint64_t* __restrict__ words, const uint16_t* __restrict__ fine, int G, int M, int k,
+                     int NP, int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_fine,
+                     int32_t* __restrict__ out_amax) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ __align__(16) unsigned char sm_raw[];
+  uint64_t* s = reinterpret_cast<uint64_t*>(sm_raw);  // [NP] words
+  int* pos = reinterpret_cast<int*>(s + NP);           // [NP] source position g * k + j
+  uint64_t* fk = reinterpret_cast<uint64_t*>(pos + NP + (NP & 1));  // [k] fine candidate words
+  const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = G * k;
+  for (int i = tid; i < NP; i += blockDim.x) {
+    if (i < n) {
+      const int g = i / k, j = i - g * k;
+      s[i] = words[((long long)g * M + m) * k + j];
+      pos[i] = i;
+    } else {
+      s[i] = 0ull;
+      pos[i] = -1;
+    }
+  }
+  __syncthreads();
+  for (int size = 2; size <= NP; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < NP / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const uint64_t a = s[lo], b = s[hi];
+        if ((a < b) == desc) {
+          s[lo] = b;
+          s[hi] = a;
+          const int t = pos[lo];
+          pos[lo] = pos[hi];
+          pos[hi] = t;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int j = tid; j < k; j += blockDim.x) {
+    const int p = pos[j], g = p / k, jj = p - g * k;
+    const uint32_t v = cand_idx(s[j]);
+    const uint16_t f = fine[((long long)g * M + m) * k + jj];
+    out_idx[(long long)m * k + j] = int32_t(v);
+    out_fine[(long long)m * k + j] = f;
+    fk[j] = cand_word(key16(f), v);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    uint64_t best = 0;
+    for (int j = lane; j < k; j += 32) best = max(best, fk[j]);
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, d));
+    if (lane == 0 && out_amax) out_amax[m] = int32_t(cand_idx(best));
+  }
+}
+
 static int topk_blocks(int V, int k) {
   // enough blocks to spread the selection, each slice >= k entries and <= 12288 keys (smem)
   int G = 32;
@@ -248,9 +316,20 @@ extern "C" size_t qmtp_topk_workspace(int M, int V, int k) {
   return size_t(M) * topk_blocks(V, k) * k * sizeof(uint64_t);
 }
 
+static int topk_rescore(const void* vals, int ld, int M, int V, int k, const void* w_fine, const void* h, int K,
+                        int* out_idx, void* out_fine, int* out_argmax, void* workspace, size_t ws_bytes,
+                        uint32_t idx_base, void* out_words, void* stream);
+
 extern "C" int qmtp_topk_rescore(const void* vals, int ld, int M, int V, int k, const void* w_fine, const void* h,
                                  int K, int* out_idx, void* out_fine, int* out_argmax, void* workspace,
                                  size_t ws_bytes, void* stream) {
+  return topk_rescore(vals, ld, M, V, k, w_fine, h, K, out_idx, out_fine, out_argmax, workspace, ws_bytes, 0u,
+                      nullptr, stream);
+}
+
+static int topk_rescore(const void* vals, int ld, int M, int V, int k, const void* w_fine, const void* h, int K,
+                        int* out_idx, void* out_fine, int* out_argmax, void* workspace, size_t ws_bytes,
+                        uint32_t idx_base, void* out_words, void* stream) {
   if (!vals || !out_idx || !workspace) return QMTP_ERR_ARG;
   if (M < 1 || V < 1 || k < 1 || k > 256 || k > V || ld < V) return QMTP_ERR_SHAPE;
   if (w_fine && (!h || !out_fine || K < 256 || K % 256 != 0)) return QMTP_ERR_SHAPE;
@@ -270,7 +349,8 @@ extern "C" int qmtp_topk_rescore(const void* vals, int ld, int M, int V, int k, 
   if (attr != cudaSuccess) return QMTP_ERR_CUDA;
   launch_kernel(topk_merge_kernel, dim3(M), dim3(kMergeThreads), smemB, st, cand, G, k, NP, static_cast<const uint16_t*>(w_fine),
                                                       static_cast<const uint16_t*>(h), K, out_idx,
-                                                      static_cast<uint16_t*>(out_fine), out_argmax);
+                                                      static_cast<uint16_t*>(out_fine), out_argmax, idx_base,
+                                                      static_cast<uint64_t*>(out_words));
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 
@@ -309,6 +389,47 @@ extern "C" int qmtp_lmhead2(const void* h, const void* wq, const void* scales, c
   if (rc != QMTP_OK) return rc;
   return qmtp_topk_rescore(coarse, V, M, V, k, w_fine, h, K, out_idx, out_fine, out_argmax, ws + coarse_bytes,
                            ws_bytes - coarse_bytes, stream);
+}
+
+// ----------------------------------------------------------------------------- vocabulary shards
+extern "C" size_t qmtp_lmhead2_shard_workspace(int M, int Vs, int k) {
+  const size_t head = qmtp_lmhead2_workspace(M, Vs, k);
+  if (head == 0) return 0;
+  return head + (size_t(M) * k * sizeof(int32_t) + 255) / 256 * 256;
+}
+
+extern "C" int qmtp_lmhead2_shard(const void* h, const void* wq, const void* scales, const void* biases,
+                                  const void* w_fine, int M, int Vs, int K, int k, long long v0, void* out_words,
+                                  void* out_fine, void* workspace, size_t ws_bytes, void* stream) {
+  if (!h || !wq || !scales || !biases || !w_fine || !out_words || !out_fine || !workspace) return QMTP_ERR_ARG;
+  if (M < 1 || Vs < 1 || k < 1 || k > Vs || v0 < 0 || v0 + Vs > 0x7FFFFFFFLL) return QMTP_ERR_SHAPE;
+  const size_t need = qmtp_lmhead2_shard_workspace(M, Vs, k);
+  if (need == 0 || ws_bytes < need) return QMTP_ERR_ARG;
+  if (!aligned16(out_words) || !aligned16(workspace)) return QMTP_ERR_ALIGN;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  const size_t coarse_bytes = (size_t(M) * Vs * sizeof(uint16_t) + 255) / 256 * 256;
+  const size_t topk_bytes = qmtp_topk_workspace(M, Vs, k);
+  int* idx_local = reinterpret_cast<int*>(ws + coarse_bytes + (topk_bytes + 255) / 256 * 256);
+  if (coarse_bytes + (topk_bytes + 255) / 256 * 256 + size_t(M) * k * sizeof(int32_t) > ws_bytes) return QMTP_ERR_ARG;
+  int rc = qmtp_qmv_affine_g64(h, wq, scales, biases, ws, M, Vs, K, Vs, stream);
+  if (rc != QMTP_OK) return rc;
+  return topk_rescore(ws, Vs, M, Vs, k, w_fine, h, K, idx_local, out_fine, nullptr, ws + coarse_bytes, topk_bytes,
+                      uint32_t(v0), out_words, stream);
+}
+
+extern "C" int qmtp_lmhead2_merge(const void* words, const void* fine, int G, int M, int k, int* out_idx,
+                                  void* out_fine, int* out_argmax, void* stream) {
+  if (!words || !fine || !out_idx || !out_fine) return QMTP_ERR_ARG;
+  if (G < 1 || M < 1 || k < 1 || size_t(G) * k > 4096) return QMTP_ERR_SHAPE;
+  const int NP = pow2_at_least(G * k);
+  const size_t smem = size_t(NP) * (sizeof(uint64_t) + sizeof(int)) + (NP & 1) * sizeof(int) + size_t(k) * sizeof(uint64_t);
+  static const cudaError_t attr =
+      cudaFuncSetAttribute(lmhead2_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  if (attr != cudaSuccess) return QMTP_ERR_CUDA;
+  launch_kernel(lmhead2_merge_kernel, dim3(M), dim3(kShardMergeThreads), smem, static_cast<cudaStream_t>(stream),
+                static_cast<const uint64_t*>(words), static_cast<const uint16_t*>(fine), G, M, k, NP, out_idx,
+                static_cast<uint16_t*>(out_fine), out_argmax);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 
 // ----------------------------------------------------------------------------- no-allocation head

@@ -66,6 +66,8 @@ SIGNATURES.update({
     "qmtp_argmax_bf16": [_P, _I, _I, _I, _P, _P, ctypes.c_size_t, _P],
     "qmtp_qmv_affine_g64_res": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_lmhead2_noalloc": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P],
+    "qmtp_lmhead2_shard": [_P, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_longlong, _P, _P, _P, ctypes.c_size_t, _P],
+    "qmtp_lmhead2_merge": [_P, _P, _I, _I, _I, _P, _P, _P, _P],
     "qmtp_embed": [_P, _I, _P, _P, _P, _I, _I, _P, _I, _P],
     "qmtp_embed_nvfp4": [_P, _I, _P, _P, _I, _I, _P, _I, _P],
     "qmtp_qmv_nvfp4_g16_res": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
@@ -105,6 +107,7 @@ CTRL_SIZE = 32
 SIZE_QUERIES: dict[str, list] = {
     "qmtp_qmv_workspace": [_I, _I],
     "qmtp_lmhead2_workspace": [_I, _I, _I],
+    "qmtp_lmhead2_shard_workspace": [_I, _I, _I],
     "qmtp_topk_workspace": [_I, _I, _I],
     "qmtp_argmax_workspace": [_I, _I],
     "qmtp_moe_workspace": [_I, _I, _I, _I, _I],

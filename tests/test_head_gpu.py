@@ -66,3 +66,42 @@ def test_topk_many_ties(dev):
     _lib.check(_lib.lib().qmtp_topk_rescore(v.data_ptr(), 30000, 2, 30000, k, None, None, 0, idx.data_ptr(), None,
                                             None, ws.data_ptr(), ws.numel(), _lib.stream()), "topk")
     assert np.array_equal(to_np(idx).view(np.int32), ops.topk_bf16(vals, k))
+
+
+@pytest.mark.parametrize("G,V,M,k", [(2, 248320, 3, 64), (3, 248320, 1, 64), (8, 248320, 3, 64), (5, 50000, 2, 256),
+                                     (4, 1000, 3, 64)])
+def test_vocab_shards_merge_to_the_whole_head(G, V, M, k, dev):
+    """qmtp_lmhead2_shard on G vocabulary shards (run here one after another on one GPU) and
+    qmtp_lmhead2_merge of their lists give qmtp_lmhead2's result on the whole vocabulary bit for bit,
+    including ties across shard boundaries."""
+    from qmtp import _lib
+    from qmtp.lm_head2 import ShardedTwoStageHead
+
+    D = 4096 if V > 10000 else 1024
+    W = randn_bf16((V, D), V + G, 0.02)
+    h = randn_bf16((M, D), 3)
+    hf = ops.bf16_to_f32(h)
+    bounds = [ShardedTwoStageHead.split(V, G, r) for r in range(G)]
+    for m in range(M):  # a tied pair straddling a boundary, ranked first for token m
+        a, c = bounds[0][1] - 1 - m, bounds[-1][0] + m
+        W[a] = W[c] = ops.f32_to_bf16(0.05 * hf[m])
+    wq, s, b = ops.quantize_affine(W)
+    Wt, wqt, st, bt, ht = (to_torch(x, dev) for x in (W, wq, s, b, h))
+    L = _lib.lib()
+    words = torch.empty((G, M, k), dtype=torch.int64, device=dev)
+    fine = torch.empty((G, M, k), dtype=torch.bfloat16, device=dev)
+    for r, (v0, vs) in enumerate(bounds):
+        ws = torch.empty(L.qmtp_lmhead2_shard_workspace(M, vs, k), dtype=torch.uint8, device=dev)
+        _lib.check(L.qmtp_lmhead2_shard(ht.data_ptr(), wqt[v0:].data_ptr(), st[v0:].data_ptr(), bt[v0:].data_ptr(),
+                                        Wt[v0:].data_ptr(), M, vs, D, k, v0, words[r].data_ptr(), fine[r].data_ptr(),
+                                        ws.data_ptr(), ws.numel(), _lib.stream()), "shard")
+    idx = torch.empty((M, k), dtype=torch.int32, device=dev)
+    fv = torch.empty((M, k), dtype=torch.bfloat16, device=dev)
+    amax = torch.empty((M,), dtype=torch.int32, device=dev)
+    _lib.check(L.qmtp_lmhead2_merge(words.data_ptr(), fine.data_ptr(), G, M, k, idx.data_ptr(), fv.data_ptr(),
+                                    amax.data_ptr(), _lib.stream()), "merge")
+    _, ridx, rfine, ramax = ops.two_stage_head(h, wq, s, b, W, k)
+    assert all(ridx[m, 0] == bounds[0][1] - 1 - m and ridx[m, 1] == bounds[-1][0] + m for m in range(M))
+    assert np.array_equal(to_np(idx).view(np.int32), ridx)
+    assert np.array_equal(to_np(fv), rfine)
+    assert np.array_equal(to_np(amax).view(np.int32), ramax)
