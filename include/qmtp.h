@@ -75,6 +75,15 @@ int qmtp_qmv_affine_g64_split(const void* x, long long ldx, const void* w, const
                               const void* biases, void* y, const void* res, int M, int N, int K, int ldy,
                               void* workspace, size_t ws_bytes, void* stream);
 
+/* qmtp_qmv_affine_g64_split on RMS-normalised rows: y = RMSNorm(x; norm_w, eps) . W^T (+ res), the
+ * decoder's input_ln / post_ln (mlx_lm RMSNorm, the rmsnorm of qmtp_rmsnorm) computed by every CTA in
+ * the kernel's prologue instead of a separate launch.  Same bits as qmtp_rmsnorm followed by
+ * qmtp_qmv_affine_g64.  x: the un-normalised rows (bf16 [M, ldx]); norm_w bf16 [K]; K % 1024 == 0,
+ * K <= 32768.  workspace: as for qmtp_qmv_affine_g64_split, or NULL (no workspace split). */
+int qmtp_qmv_affine_g64_norm(const void* x, long long ldx, const void* norm_w, float eps, const void* w,
+                             const void* scales, const void* biases, void* y, const void* res, int M, int N,
+                             int K, int ldy, void* workspace, size_t ws_bytes, void* stream);
+
 /* Tiling the affine kernel picks for an N x K matrix (split != 0: the _split entry point): weight
  * rows per tile, CTAs, work units (tile x 512-k slice) and CTAs per thread-block cluster (> 1: each
  * tile is shared by the CTAs of one cluster, whose first CTA adds the others' slice partials in order

@@ -94,6 +94,7 @@ struct Bars {
   uint32_t tmem;
   int abort;
   int last;
+  float rn[kMaxTok];  // RMSNorm prologue: 1 / rms per token
 };
 static_assert(sizeof(Bars) <= 512, "barrier block");
 
@@ -108,6 +109,8 @@ struct Params {
   int U;              // units = ntiles * NSL (U * gridDim.x < 2^31, checked by the host)
   int ldy, N, K, NSL, R, ntiles, whole;
   int cs;             // cluster mode (> 1): CTAs per tile, one tile per cluster
+  const uint16_t* nw; // non-null: the activation is RMSNorm(x rows) with this weight [K] (prologue)
+  float eps;
 };
 
 // (tile, slice) of consecutive units, advanced without divisions.
@@ -190,6 +193,27 @@ __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
   return old;
 }
 
+// Two fp32 values rounded to nearest-even bf16 and packed (lo in bits 0-15), one conversion
+// instruction.  Finite and infinite values round exactly as f2bf; a NaN may come out with another
+// payload, which the activation grid treats like any NaN (the token row becomes NaN).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+// 8 normalised activations: bf16(w * bf16(x * r)) element by element (the RMSNorm of
+// oracle qo_rmsnorm / rmsnorm_wide_kernel, r = 1 / rms of the token's row).
+__device__ __forceinline__ uint4 rms_apply(uint4 xv, uint4 wv, float r) {
+  const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ws[4] = {wv.x, wv.y, wv.z, wv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const uint32_t t = pack_bf16x2(__fmul_rn(bflo(xs[h]), r), __fmul_rn(bfhi(xs[h]), r));
+    o[h] = pack_bf16x2(__fmul_rn(bflo(ws[h]), bflo(t)), __fmul_rn(bfhi(ws[h]), bfhi(t)));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // One activation task: 8 consecutive x of token m in group g (lane li of the group's 8 lanes) ->
 // their three byte limbs in the B image of the slot (rows 3m..3m+2, permuted k: the even k of the
 // 8 then the odd k, as the nibble unpacking orders the weights) and, from lane 0 of the group, the
@@ -258,7 +282,9 @@ __device__ __forceinline__ void prep_task(uint4 v, int m, int g, int li, uint8_t
 //          are in flight meanwhile);
 //   2      in stream mode (more than 8 slices and units), builds the later slices one unit at a time;
 //   4-7    chain-0 workers, 8-11 chain-1 workers: warp w serves TMEM lane quarter w % 4, thread = row.
-template <int MT>
+// NORM: the activation is RMSNorm(x rows) (p.nw), computed in the prologue (a separate instantiation
+// keeps the plain kernel's code small).
+template <int MT, bool NORM>
 __global__ void __launch_bounds__(kThreads, 1)
     qmv_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
                   const __grid_constant__ CUtensorMap tb, const __grid_constant__ Params p) {
@@ -359,28 +385,76 @@ __global__ void __launch_bounds__(kThreads, 1)
   // bfull arrival per warp batch.  The loop is not unrolled: the kernel's roles run different code at
   // the same time, and a small loop body keeps them in the instruction cache.
   constexpr int kBuilders = 320;  // up-front build: warps 0, 2 and 12-19
+  const bool builder = warp == 0 || warp == 2 || warp >= 12;
+  const int bme = warp == 0 ? lane : warp == 2 ? 32 + lane : tid - 320;  // builder index
+  // RMSNorm prologue: 1 / rms per token in rn[m], over the whole row of every token, in the reduction
+  // order of rmsnorm_wide_kernel: chains of 32 elements (fma), the xor butterfly over 32 chains, the
+  // 1024-element group sums in order.  The group sums use the chain-1 partial buffer, which no
+  // epilogue touches before the build has started (so not before both prologue barriers); rn itself
+  // is read during the whole build and sits in the barrier block.
+  float* rn = bars->rn;
+  if (NORM && builder) {
+    float* grp = reinterpret_cast<float*>(sm + kOffH);  // [kMaxTok][32] group sums
+    const int C = p.K / 32;
+#pragma unroll 1
+    for (int v = bme; v < MT * C; v += kBuilders) {  // warp-uniform: C is a multiple of 32
+      const int m = v / C, c = v - m * C;
+      const uint16_t* src = p.x + (size_t)m * (size_t)p.ldx + 32 * c;
+      float ss = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src + 8 * q);
+        const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          ss = __fmaf_rn(bflo(uu[h]), bflo(uu[h]), ss);
+          ss = __fmaf_rn(bfhi(uu[h]), bfhi(uu[h]), ss);
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) grp[m * 32 + (c >> 5)] = ss;
+    }
+    asm volatile("bar.sync 2, 320;" ::: "memory");
+    if (bme < MT) {
+      float t = grp[bme * 32];
+      for (int i = 1; i < p.K / 1024; ++i) t = __fadd_rn(t, grp[bme * 32 + i]);
+      rn[bme] = rsqrt_rn(__fadd_rn(__fdiv_rn(t, float(p.K)), p.eps));
+    }
+    asm volatile("bar.sync 2, 320;" ::: "memory");
+  }
   auto build = [&](int j0, int nb, int me, int nthr) {
     const int per_slot = 64 * MT;
     const int total = nb * per_slot;
     const int sbase = (first.sl + j0) % NSL;  // slice of unit j0
-    auto load = [&](int t) {
+    auto kof = [&](int t) {  // k offset of task t
       const int jb = t / per_slot, r = t - jb * per_slot;
       const int sl = sbase + jb < NSL ? sbase + jb : sbase + jb - NSL;
-      const int m = r >> 6, g = (r >> 3) & 7, li = r & 7;
-      return *reinterpret_cast<const uint4*>(p.x + (size_t)m * (size_t)p.ldx + (size_t)sl * 512 + g * 64 + li * 8);
+      return sl * 512 + ((r >> 3) & 7) * 64 + (r & 7) * 8;
     };
-    uint4 va = make_uint4(0u, 0u, 0u, 0u), vb = va;
-    if (me < total) va = load(me);
-    if (me + nthr < total) vb = load(me + nthr);
+    auto load = [&](int t) {
+      const int m = (t % per_slot) >> 6;
+      return *reinterpret_cast<const uint4*>(p.x + (size_t)m * (size_t)p.ldx + kof(t));
+    };
+    // the RMSNorm weights of a task's 8 elements (prologue mode), fetched with its x
+    auto loadw = [&](int t) { return NORM ? *reinterpret_cast<const uint4*>(p.nw + kof(t)) : make_uint4(0u, 0u, 0u, 0u); };
+    uint4 va = make_uint4(0u, 0u, 0u, 0u), vb = va, wa = va, wb = va;
+    if (me < total) { va = load(me); wa = loadw(me); }
+    if (me + nthr < total) { vb = load(me + nthr); wb = loadw(me + nthr); }
     int cur_slot = -1;  // slot of this warp's open batch run (its bfull arrivals are owed)
     int batches = 0;
 #pragma unroll 1
     for (int t = me; t < total; t += nthr) {  // warp-uniform: total and nthr are multiples of 32
-      const uint4 v = va;
+      uint4 v = va;
+      const uint4 wv = wa;
       va = vb;
-      if (t + 2 * nthr < total) vb = load(t + 2 * nthr);
+      wa = wb;
+      if (t + 2 * nthr < total) {
+        vb = load(t + 2 * nthr);
+        wb = loadw(t + 2 * nthr);
+      }
       {
         const int jb = t / per_slot, r = t - jb * per_slot;
+        if (NORM) v = rms_apply(v, wv, rn[r >> 6]);
         const int slot = slot_of(j0 + jb, sbase + jb < NSL ? sbase + jb : sbase + jb - NSL);
         if (slot != cur_slot && cur_slot >= 0) {
           fence_proxy_async();
@@ -406,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // The activation operand is built up front by the producer warp (after its first requests), warp 2
   // and the epilogue warps (idle until the first accumulators are ready), while the unpacking warps
   // already turn the first weight stages into A operands and the MMA issuers wait for the first slot.
-  if (warp == 0 || warp == 2 || warp >= 12) build(0, nbuild, warp == 0 ? lane : warp == 2 ? 32 + lane : tid - 320, kBuilders);
+  if (builder) build(0, nbuild, bme, kBuilders);
 
   if (warp == 0) {
     // ------------------------------------------------------------------- TMA producer
@@ -843,12 +917,13 @@ static bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const v
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int MT>
+template <int MT, bool NORM>
 static bool prepare() {
   static std::once_flag once;
   static bool ok = false;
   std::call_once(once, [&] {
-    ok = cudaFuncSetAttribute(qmv_tc_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) == cudaSuccess;
+    ok = cudaFuncSetAttribute(qmv_tc_kernel<MT, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
+         cudaSuccess;
   });
   return ok;
 }
@@ -856,8 +931,13 @@ static bool prepare() {
 template <int MT>
 static int launch_mt(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb, const Params& p, int G,
                      cudaStream_t st) {
-  if (!prepare<MT>()) return QMTP_ERR_CUDA;
-  launch_kernel_cluster(qmv_tc_kernel<MT>, dim3(G), dim3(kThreads), kSmem, st, p.cs, tw, ts, tb, p);
+  if (p.nw) {
+    if (!prepare<MT, true>()) return QMTP_ERR_CUDA;
+    launch_kernel_cluster(qmv_tc_kernel<MT, true>, dim3(G), dim3(kThreads), kSmem, st, p.cs, tw, ts, tb, p);
+  } else {
+    if (!prepare<MT, false>()) return QMTP_ERR_CUDA;
+    launch_kernel_cluster(qmv_tc_kernel<MT, false>, dim3(G), dim3(kThreads), kSmem, st, p.cs, tw, ts, tb, p);
+  }
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 
@@ -870,7 +950,7 @@ static int max_clusters(int cs) {
   int& c = cache[cs == 4 ? 1 : 0][dev];
   if (c == 0) {
     int n = 0;
-    if (prepare<1>()) {
+    if (prepare<1, false>()) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(unsigned(cs));
       cfg.blockDim = dim3(kThreads);
@@ -882,7 +962,7 @@ static int max_clusters(int cs) {
       at[0].val.clusterDim.z = 1;
       cfg.attrs = at;
       cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&n, qmv_tc_kernel<1>, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, qmv_tc_kernel<1, false>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         n = 0;
       }
@@ -907,13 +987,16 @@ size_t qmv_tc_workspace(int N, int K) {
 
 // All affine qmv entry points land here.  workspace == nullptr: whole tiles per CTA.
 int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const void* b, void* y, const void* res,
-           int M, int N, int K, int ldy, void* workspace, size_t ws_bytes, void* stream) {
+           int M, int N, int K, int ldy, void* workspace, size_t ws_bytes, void* stream, const void* norm_w,
+           float eps) {
   using namespace tq;
   if (!x || !w || !s || !b || !y) return QMTP_ERR_ARG;
   if (M < 1 || N < 1 || K < 512 || K % 512 != 0 || ldy < N) return QMTP_ERR_SHAPE;
   if (ldx == 0) ldx = K;
   if (ldx < K || ldx % 8) return QMTP_ERR_SHAPE;
   if (!aligned16(x) || !aligned16(w) || !aligned16(s) || !aligned16(b)) return QMTP_ERR_ALIGN;
+  if (norm_w && (K % 1024 != 0 || K > 32768)) return QMTP_ERR_SHAPE;
+  if (norm_w && !aligned16(norm_w)) return QMTP_ERR_ALIGN;
   const bool split = workspace != nullptr;
   if (split && (qmv_tc_workspace(N, K) == 0 || ws_bytes < qmv_tc_workspace(N, K))) return QMTP_ERR_SHAPE;
   if (split && (reinterpret_cast<uintptr_t>(workspace) & 255u)) return QMTP_ERR_ALIGN;
@@ -934,6 +1017,8 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
   p.ntiles = pl.ntiles;
   p.whole = pl.whole;
   p.cs = pl.cs;
+  p.nw = static_cast<const uint16_t*>(norm_w);
+  p.eps = eps;
   p.U = int(pl.U);
   p.err = device_error_ptr();
   if (split) {
@@ -973,13 +1058,13 @@ using namespace qmtp;
 
 extern "C" int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const void* biases, void* y,
                                    int M, int N, int K, int ldy, void* stream) {
-  return qmv_tc(x, 0, w, scales, biases, y, nullptr, M, N, K, ldy, nullptr, 0, stream);
+  return qmv_tc(x, 0, w, scales, biases, y, nullptr, M, N, K, ldy, nullptr, 0, stream, nullptr, 0.0f);
 }
 
 extern "C" int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void* scales, const void* biases, void* y,
                                        const void* res, int M, int N, int K, int ldy, void* stream) {
   if (!res) return QMTP_ERR_ARG;
-  return qmv_tc(x, 0, w, scales, biases, y, res, M, N, K, ldy, nullptr, 0, stream);
+  return qmv_tc(x, 0, w, scales, biases, y, res, M, N, K, ldy, nullptr, 0, stream, nullptr, 0.0f);
 }
 
 extern "C" size_t qmtp_qmv_workspace(int N, int K) { return qmv_tc_workspace(N, K); }
@@ -988,7 +1073,14 @@ extern "C" int qmtp_qmv_affine_g64_split(const void* x, long long ldx, const voi
                                          const void* biases, void* y, const void* res, int M, int N, int K, int ldy,
                                          void* workspace, size_t ws_bytes, void* stream) {
   if (!workspace) return QMTP_ERR_ARG;
-  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, workspace, ws_bytes, stream);
+  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, workspace, ws_bytes, stream, nullptr, 0.0f);
+}
+
+extern "C" int qmtp_qmv_affine_g64_norm(const void* x, long long ldx, const void* norm_w, float eps, const void* w,
+                                        const void* scales, const void* biases, void* y, const void* res, int M,
+                                        int N, int K, int ldy, void* workspace, size_t ws_bytes, void* stream) {
+  if (!norm_w) return QMTP_ERR_ARG;
+  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, workspace, ws_bytes, stream, norm_w, eps);
 }
 
 extern "C" int qmtp_qmv_set_mode(int mode) {

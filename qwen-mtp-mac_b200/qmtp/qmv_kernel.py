@@ -60,12 +60,13 @@ def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "
 
 def qmv_affine(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                group_size: int = 64, out: torch.Tensor | None = None, res: torch.Tensor | None = None,
-               ws: torch.Tensor | None = None, split: bool = True) -> torch.Tensor:
+               ws: torch.Tensor | None = None, split: bool = True, norm=None) -> torch.Tensor:
     """y = x @ dequant(w).T for the affine 4-bit group-64 format (bf16 in, bf16 out).
     x: [..., K] bf16; w: uint32/int32 [N, K/8]; scales, biases: bf16 [N, K/64] -> [..., N].
     res (bf16, same shape as out): y = bf16(res + bf16(x . W^T)), may alias out.
     split=True (default) lets CTAs share a tile (needs a workspace: `ws`, or the cached one of the
-    current stream); split=False gives each CTA whole tiles and needs none.  Both give the same bits."""
+    current stream); split=False gives each CTA whole tiles and needs none.  Both give the same bits.
+    norm=(weight bf16 [K], eps): x is first RMS-normalised (mlx_lm RMSNorm) inside the kernel."""
     if group_size != 64:
         raise NotImplementedError("affine qmv is implemented for group_size=64")
     xf, K = _flat(x)
@@ -81,7 +82,16 @@ def qmv_affine(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: t
     if res is not None and (res.shape != out.shape or res.dtype != torch.bfloat16):
         raise ValueError("res must match out")
     L = _lib.lib()
-    if split:
+    if norm is not None:
+        nw, eps = norm
+        _lib.require_cuda(nw)
+        if split and ws is None:
+            ws = workspace(N, K, x.device)
+        rc = L.qmtp_qmv_affine_g64_norm(xf.data_ptr(), K, nw.data_ptr(), float(eps), w.data_ptr(), scales.data_ptr(),
+                                        biases.data_ptr(), out.data_ptr(), _lib.ptr(res), M, N, K, out.shape[-1],
+                                        _lib.ptr(ws if split else None),
+                                        (ws.numel() * ws.element_size()) if split else 0, _lib.stream())
+    elif split:
         if ws is None:
             ws = workspace(N, K, x.device)
         rc = L.qmtp_qmv_affine_g64_split(xf.data_ptr(), K, w.data_ptr(), scales.data_ptr(), biases.data_ptr(),

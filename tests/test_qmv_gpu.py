@@ -238,3 +238,36 @@ def test_no_device_error_recorded(dev):
 
     torch.cuda.synchronize()
     assert _lib.device_error(clear=True) == 0
+
+
+@pytest.mark.parametrize("K", [1024, 4096, 8192])
+@pytest.mark.parametrize("M", [1, 3, 4])
+def test_qmv_affine_norm_prologue(K, M, dev, planner):
+    """The RMSNorm prologue (qmtp_qmv_affine_g64_norm) gives the bits of the oracle's rmsnorm followed
+    by its qmv, in every planner mode, with a residual, and for rows over bf16's range (an infinity
+    makes its token row NaN)."""
+    from oracle import model as om
+    from qmtp import qmv_kernel
+
+    r = np.random.default_rng(K + M)
+    for N in (37, 4096, 12352):
+        _, wq, s, b = affine_layer(N, K, seed=N + K)
+        x = randn_bf16((M, K), M + 40, 3.0)
+        nw = ops.f32_to_bf16((1.0 + 0.1 * r.standard_normal(K)).astype(np.float32))
+        if M == 4:
+            x[1] = ops.f32_to_bf16(ops.bf16_to_f32(x[1]) * np.float32(2.0 ** -100))  # tiny row
+            x[3, 77] = 0x7F80  # +inf
+        res = randn_bf16((M, N), 9)
+        xn = om.rmsnorm(x, nw, 1e-6)
+        ref = ops.qmv_affine(xn, wq, s, b)
+        ref_res = ops.f32_to_bf16(ops.bf16_to_f32(res) + ops.bf16_to_f32(ref))
+        xt, wt, st, bt, nt = (to_torch(a, dev) for a in (x, wq, s, b, nw))
+        for mode, split in MODES:
+            planner(mode)
+            got = to_np(qmv_kernel.qmv_affine(xt, wt, st, bt, split=split, norm=(nt, 1e-6)))
+            assert np.array_equal(got, ref), (N, mode, split)
+            out = to_torch(res, dev)
+            qmv_kernel.qmv_affine(xt, wt, st, bt, out=out, res=out, split=split, norm=(nt, 1e-6))
+            assert np.array_equal(to_np(out), ref_res), (N, mode, split, "res")
+        if M == 4:
+            assert np.isnan(ops.bf16_to_f32(ref[3])).all()
