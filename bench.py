@@ -351,10 +351,10 @@ def run_kernel(args):
             Ls = [qmv_kernel.quantize((torch.randn(N, Kd, generator=g, device=dev) * 0.02).to(torch.bfloat16))
                   for _ in range(copies)]
             nbytes = N * Kd // 2 + N * (Kd // 64) * 4 + M * Kd * 2 + M * N * 2
-            ws = qmv_kernel.workspace(N, Kd, dev)
-            split = fmt != "affine-whole"
-            run = lambda i: qmv_kernel.qmv_affine(x, *Ls[i % copies], out=y, ws=ws, split=split)
-            label = f"qmv affine g64 N={N} K={Kd} M={M}" + ("" if split else " (whole tiles)")
+            if fmt == "affine-whole":
+                _lib.qmv_set_mode(1)
+            run = lambda i: qmv_kernel.qmv_affine(x, *Ls[i % copies], out=y)
+            label = f"qmv affine g64 N={N} K={Kd} M={M}" + (" (whole tiles)" if fmt == "affine-whole" else "")
         unit_bytes = nbytes
     elif args.kernel == "gdn":
         S, Hk, Hv, D, KC = 3, 16, 32, 128, 4

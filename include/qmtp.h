@@ -60,17 +60,15 @@ int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const 
 int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void* scales, const void* biases,
                             void* y, const void* res, int M, int N, int K, int ldy, void* stream);
 
-/* Bytes of the workspace qmtp_qmv_affine_g64_split needs for an N x K matrix (any M): 64 KiB of tile
- * arrival counters (always at the start, so matrices of any shape can share one workspace) plus the
- * slice partials.  0 if N x K is not supported (K % 512 != 0, or N above 2^20 rows). */
+/* Workspace bytes for qmtp_qmv_affine_g64_split / _norm: 256 for every supported N x K (0 if K % 512
+ * != 0).  The kernel no longer uses it -- a tile shared between CTAs is finished inside their
+ * thread-block cluster -- and the argument is kept so existing callers keep working. */
 size_t qmtp_qmv_workspace(int N, int K);
 
-/* qmtp_qmv_affine_g64 (+ optional residual, res may be NULL) with tiles shared between CTAs: a
- * tile's 512-k slices may be computed by different CTAs, and the CTA that finishes a tile's last
- * share adds the slice partials in order, so every SM streams weights even for N = 4096.  Same bits
- * as qmtp_qmv_affine_g64.  x rows at x + m * ldx (elements; 0 = K).  workspace: 256-byte aligned,
- * >= qmtp_qmv_workspace(N, K) bytes, ZERO-FILLED before its first use; every launch leaves its
- * arrival counters at zero again.  Launches that may run concurrently need separate workspaces. */
+/* qmtp_qmv_affine_g64 (+ optional residual, res may be NULL) with strided rows: x rows at
+ * x + m * ldx (elements; 0 = K).  Same bits as qmtp_qmv_affine_g64 (every entry point may share a
+ * tile's 512-k slices between the CTAs of a cluster; the slice partials are added in order).
+ * workspace / ws_bytes: ignored, may be NULL / 0. */
 int qmtp_qmv_affine_g64_split(const void* x, long long ldx, const void* w, const void* scales,
                               const void* biases, void* y, const void* res, int M, int N, int K, int ldy,
                               void* workspace, size_t ws_bytes, void* stream);
@@ -79,12 +77,12 @@ int qmtp_qmv_affine_g64_split(const void* x, long long ldx, const void* w, const
  * decoder's input_ln / post_ln (mlx_lm RMSNorm, the rmsnorm of qmtp_rmsnorm) computed by every CTA in
  * the kernel's prologue instead of a separate launch.  Same bits as qmtp_rmsnorm followed by
  * qmtp_qmv_affine_g64.  x: the un-normalised rows (bf16 [M, ldx]); norm_w bf16 [K]; K % 1024 == 0,
- * K <= 32768.  workspace: as for qmtp_qmv_affine_g64_split, or NULL (no workspace split). */
+ * K <= 32768.  workspace / ws_bytes: ignored, may be NULL / 0. */
 int qmtp_qmv_affine_g64_norm(const void* x, long long ldx, const void* norm_w, float eps, const void* w,
                              const void* scales, const void* biases, void* y, const void* res, int M, int N,
                              int K, int ldy, void* workspace, size_t ws_bytes, void* stream);
 
-/* Tiling the affine kernel picks for an N x K matrix (split != 0: the _split entry point): weight
+/* Tiling the affine kernel picks for an N x K matrix (split: ignored): weight
  * rows per tile, CTAs, work units (tile x 512-k slice) and CTAs per thread-block cluster (> 1: each
  * tile is shared by the CTAs of one cluster, whose first CTA adds the others' slice partials in order
  * through distributed shared memory; every entry point may pick this mode, it needs no workspace).
@@ -93,8 +91,7 @@ int qmtp_qmv_plan(int N, int K, int split, int* rows_per_tile, int* grid, int* u
 
 /* Overrides the affine kernel's planner for every later call in the process (no counterpart in the
  * reference; for tests and measurements): 0 = cost model (default), 1 = whole tiles per CTA only,
- * 2 = cluster mode wherever the shape allows it, 3 = workspace split wherever a workspace is given.
- * Every mode gives the same bits. */
+ * 2 = cluster mode wherever the shape allows it.  Every mode gives the same bits. */
 int qmtp_qmv_set_mode(int mode);
 
 /* Multi-row 4-bit GEMV, NVFP4 (e2m1 nibbles, e4m3 scale per 16): qmv_kernel.py:86-101 qmv_nvfp4.

@@ -15,22 +15,25 @@
 // launch may give a CTA whole tiles or slices of a tile, and every token row is independent of the
 // others (batch-invariant).
 //
-// Design:
-//   * a tile is R <= 128 weight rows (the MMA's M); a unit of work is (tile, slice of 512 k).  CTAs
-//     take contiguous unit ranges (one CTA per SM, 220 KB of shared memory); a tile split between CTAs
-//     is finished by the CTA that arrives last (one arrival counter per tile at the start of a caller
-//     workspace, fp32 slice partials after them; no CTA ever waits for another);
-//   * all 12 warps first build the B operand of every slice the CTA needs (the three byte limbs of every
-//     token, 16 x 64 bytes per group, canonical K-major layout) and the per-group factors from x, while
-//     the first weight stages are in flight;
+// Design (one CTA of 20 warps per SM, 228 KB of shared memory, all 512 TMEM columns):
+//   * a tile is R <= 128 weight rows (the MMA's M); a unit of work is (tile, slice of 512 k).  A CTA
+//     takes whole tiles, or (cluster mode) the CTAs of a thread-block cluster share one tile: rank k
+//     computes slices [k, k + 1) * NSL / cs, keeps each slice's partial in its shared memory, and rank
+//     0 adds the other ranks' partials to its own running sum in slice order through distributed
+//     shared memory (two cluster barriers; no global workspace, no atomics);
+//   * warps 0, 2 and 12-19 first build the B operand of every slice the CTA needs (the three byte
+//     limbs of every token, 16 x 64 bytes per group, canonical K-major layout) and the per-group
+//     factors from x -- optionally RMS-normalising the token rows first (the NORM instantiation) --
+//     while the first weight stages are in flight and already being unpacked;
 //   * warp 0 is the TMA producer: per unit, two 128-byte-wide boxes of packed nibbles (128-byte swizzle)
 //     and the unit's scales and biases land in a 4-stage ring;
-//   * the two chains of a slice (groups 0-3 and 4-7) have their own workers: warps 4-7
-//     for chain 0, warps 8-11 for chain 1.  A worker thread owns one weight row (TMEM
-//     lane quarter = warp % 4): it unpacks its row's nibbles of the chain's groups into bytes (two LOP3s
-//     per word) and stores them into TMEM as the A operand; two units later it reads the integer
-//     accumulators back and runs the chain.  The chain-1 workers hand their partial to the chain-0
-//     workers of the same rows, which add the slices in order;
+//   * the two chains of a slice (groups 0-3 and 4-7) each have 4 unpacking warps (4-7, 8-11) and 4
+//     epilogue warps (12-15, 16-19); warp w serves TMEM lane quarter w % 4 and a thread owns one
+//     weight row.  An unpacking thread turns its row's nibbles into bytes (two LOP3s per word) and
+//     stores them into TMEM as the A operand, and hands the unit's scales and biases to the epilogue
+//     through a shared-memory side buffer; an epilogue thread reads the integer accumulators back and
+//     runs the chain.  The chain-1 epilogue hands its partial to the chain-0 epilogue of the same row,
+//     which adds the slices in order;
 //   * warp 1 (chain 0) and warp 3 (chain 1) each issue the chain's 8 MMAs of a unit (M=128, N=16, K=32,
 //     A from TMEM, B from shared memory) and one commit.  TMEM: A slots [0,256), accumulator slots
 //     [256,512), two units in flight.
@@ -69,14 +72,9 @@ constexpr int kSmem = kSmemUsed + 1024;            // slack for 1024-byte alignm
 constexpr int kThreads = 640;                      // 20 warps
 constexpr int kTmemCols = 512;
 constexpr int kABase = 0, kDBase = 256;
-constexpr int kMinRows = 64;                       // smallest tile the planner picks (workspace bound)
-// Split-mode workspace: arrival counters first, at a fixed place whatever the matrix, so the slice
-// partials of one shape never land on the counters of another shape sharing the workspace.
-constexpr size_t kCntBytes = 65536;                // 16384 counters: tiles of up to 1M rows
-constexpr long long kMaxSplitTiles = kCntBytes / 4;
+constexpr int kMinRows = 64;                       // smallest tile the planner picks
 static_assert(kOffB % 1024 == 0 && kStage % 1024 == 0, "stage alignment");
 static_assert(kSmem <= 232448, "shared memory per CTA");
-constexpr int kLeader = 12 * 32;                   // first thread of the chain-0 epilogue warps
 // Cluster mode: a CTA holds at most this many slices of its tile, so that its per-slice partials
 // ([unit][kMaxTok][128] fp32, 2 KB a unit) fit in the B slots it leaves free.
 constexpr int kMaxClusterUnits = 6;
@@ -103,11 +101,8 @@ struct Params {
   long long ldx;
   uint16_t* y;
   const uint16_t* res;
-  float* part;        // split mode: slice partials [ntiles][NSL][kMaxTok][128]
-  unsigned* cnt;      // split mode: arrival count per tile (0 between launches)
   unsigned* err;
-  int U;              // units = ntiles * NSL (U * gridDim.x < 2^31, checked by the host)
-  int ldy, N, K, NSL, R, ntiles, whole;
+  int ldy, N, K, NSL, R, ntiles;  // ntiles * (gridDim.x + 1) and ntiles * NSL < 2^31 (host-checked)
   int cs;             // cluster mode (> 1): CTAs per tile, one tile per cluster
   const uint16_t* nw; // non-null: the activation is RMSNorm(x rows) with this weight [K] (prologue)
   float eps;
@@ -183,14 +178,8 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* v) {
   }
 }
 
-__device__ __forceinline__ void bar_chain0() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 __device__ __forceinline__ void prefetch_tmap(const void* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
-}
-__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
-  unsigned old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
 }
 
 // Two fp32 values rounded to nearest-even bf16 and packed (lo in bits 0-15), one conversion
@@ -303,12 +292,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int per = NSL / cs;
     u0 = int(blockIdx.x) / cs * NSL + int(crank) * per;
     u1 = u0 + per;
-  } else if (p.whole) {
+  } else {
+    // whole tiles: CTA b takes tiles [b, b + 1) * ntiles / grid
     u0 = int(blockIdx.x) * p.ntiles / int(gridDim.x) * NSL;
     u1 = int(blockIdx.x + 1) * p.ntiles / int(gridDim.x) * NSL;
-  } else {
-    u0 = int(blockIdx.x) * p.U / int(gridDim.x);
-    u1 = int(blockIdx.x + 1) * p.U / int(gridDim.x);
   }
   const int nun = u1 - u0;
   const UnitCursor first{u0 / NSL, u0 % NSL};
@@ -393,36 +380,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   // epilogue touches before the build has started (so not before both prologue barriers); rn itself
   // is read during the whole build and sits in the barrier block.
   float* rn = bars->rn;
-  if (NORM && builder) {
+  auto reduce_rows = [&](int me) {
     float* grp = reinterpret_cast<float*>(sm + kOffH);  // [kMaxTok][32] group sums
     const int C = p.K / 32;
+    // chains are taken two per trip with all eight loads issued first (for K = 4096 and up to four
+    // tokens, one trip)
 #pragma unroll 1
-    for (int v = bme; v < MT * C; v += kBuilders) {  // warp-uniform: C is a multiple of 32
-      const int m = v / C, c = v - m * C;
-      const uint16_t* src = p.x + (size_t)m * (size_t)p.ldx + 32 * c;
-      float ss = 0.0f;
+    for (int v0 = me; v0 < MT * C; v0 += 2 * kBuilders) {  // warp-uniform: C is a multiple of 32
+      uint4 u[2][4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 u = *reinterpret_cast<const uint4*>(src + 8 * q);
-        const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+      for (int i = 0; i < 2; ++i) {
+        const int v = v0 + i * kBuilders;
+        if (v < MT * C) {
+          const int m = v / C, c = v - m * C;
+          const uint16_t* src = p.x + (size_t)m * (size_t)p.ldx + 32 * c;
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          ss = __fmaf_rn(bflo(uu[h]), bflo(uu[h]), ss);
-          ss = __fmaf_rn(bfhi(uu[h]), bfhi(uu[h]), ss);
+          for (int q = 0; q < 4; ++q) u[i][q] = *reinterpret_cast<const uint4*>(src + 8 * q);
         }
       }
-      ss = warp_sum(ss);
-      if (lane == 0) grp[m * 32 + (c >> 5)] = ss;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int v = v0 + i * kBuilders;
+        if (v < MT * C) {  // warp-uniform
+          const int m = v / C, c = v - m * C;
+          float ss = 0.0f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t uu[4] = {u[i][q].x, u[i][q].y, u[i][q].z, u[i][q].w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              ss = __fmaf_rn(bflo(uu[h]), bflo(uu[h]), ss);
+              ss = __fmaf_rn(bfhi(uu[h]), bfhi(uu[h]), ss);
+            }
+          }
+          ss = warp_sum(ss);
+          if (lane == 0) grp[m * 32 + (c >> 5)] = ss;
+        }
+      }
     }
     asm volatile("bar.sync 2, 320;" ::: "memory");
-    if (bme < MT) {
-      float t = grp[bme * 32];
-      for (int i = 1; i < p.K / 1024; ++i) t = __fadd_rn(t, grp[bme * 32 + i]);
-      rn[bme] = rsqrt_rn(__fadd_rn(__fdiv_rn(t, float(p.K)), p.eps));
+    if (me < MT) {
+      float t = grp[me * 32];
+      for (int i = 1; i < p.K / 1024; ++i) t = __fadd_rn(t, grp[me * 32 + i]);
+      rn[me] = rsqrt_rn(__fadd_rn(__fdiv_rn(t, float(p.K)), p.eps));
     }
     asm volatile("bar.sync 2, 320;" ::: "memory");
-  }
-  auto build = [&](int j0, int nb, int me, int nthr) {
+  };
+  // reduce: the up-front build by all builders computes the RMSNorm factors first, with its own
+  // first loads already in flight
+  auto build = [&](int j0, int nb, int me, int nthr, bool reduce) {
     const int per_slot = 64 * MT;
     const int total = nb * per_slot;
     const int sbase = (first.sl + j0) % NSL;  // slice of unit j0
@@ -440,6 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint4 va = make_uint4(0u, 0u, 0u, 0u), vb = va, wa = va, wb = va;
     if (me < total) { va = load(me); wa = loadw(me); }
     if (me + nthr < total) { vb = load(me + nthr); wb = loadw(me + nthr); }
+    if (NORM && reduce) reduce_rows(me);
     int cur_slot = -1;  // slot of this warp's open batch run (its bfull arrivals are owed)
     int batches = 0;
 #pragma unroll 1
@@ -480,7 +487,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   // The activation operand is built up front by the producer warp (after its first requests), warp 2
   // and the epilogue warps (idle until the first accumulators are ready), while the unpacking warps
   // already turn the first weight stages into A operands and the MMA issuers wait for the first slot.
-  if (builder) build(0, nbuild, bme, kBuilders);
+  // In stream mode warp 2 goes on building the later slots one unit at a time (one call site keeps a
+  // single copy of the build code).
+  if (builder) {
+    int j = 0, nb = nbuild, me = bme, nthr = kBuilders;
+    for (;;) {
+      build(j, nb, me, nthr, j == 0);
+      if (warp != 2 || cache) break;
+      j = j == 0 ? kNB : j + 1;
+      if (j >= nun) break;
+      const int slot = j % kNB;
+      if (*abort_flag || !mbar_wait_backoff(&bars->bempty[slot], uint32_t(((j / kNB) & 1) ^ 1), err, 64)) {
+        *abort_flag = 1;
+        break;
+      }
+      nb = 1;
+      me = lane;
+      nthr = 32;
+    }
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------------------- TMA producer
@@ -544,17 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 2) {
-    // ------------------------------------------------------------------- stream-mode operand builds
-    if (!cache) {
-      for (int j = kNB; j < nun; ++j) {
-        const int slot = j % kNB;
-        if (*abort_flag || !mbar_wait_backoff(&bars->bempty[slot], uint32_t(((j / kNB) & 1) ^ 1), err, 64)) {
-          *abort_flag = 1;
-          break;
-        }
-        build(j, 1, lane, 32);
-      }
-    }
+    // (stream-mode operand builds: above)
   } else if (warp < 12) {
     // ------------------------------------------------------------------- unpacking warps
     const int h = warp < 8 ? 0 : 1;  // chain: groups 4h .. 4h+3 of every unit
@@ -612,8 +627,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = 32 * q + lane;
     const uint32_t tl = tmem + (uint32_t(32 * q) << 16);
     float* hx = reinterpret_cast<float*>(sm + kOffH);  // [2][kMaxTok][128] chain-1 partials
-    bool own = false;  // chain 0: this CTA holds slice 0 of the current tile (Y is the tile's running prefix)
-    int part_start = 0;
     bool ok = true;
     UnitCursor ec = first;  // unit of the next epilogue
 
@@ -713,76 +726,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return;
       }
-      const size_t tbase = (size_t)tile * (size_t)NSL * (kMaxTok * 128);
-      if (sl == 0) {
-        own = true;
-        part_start = 0;
+      // whole tiles: Y is the running sum of the tile's slices, in order
 #pragma unroll
-        for (int m = 0; m < MT; ++m) Y[m] = P[m];
-      } else if (own) {
-#pragma unroll
-        for (int m = 0; m < MT; ++m) Y[m] = __fadd_rn(Y[m], P[m]);
-      } else {
-        if (jj == 0) part_start = sl;
-#pragma unroll
-        for (int m = 0; m < MT; ++m) p.part[tbase + (size_t)sl * (kMaxTok * 128) + m * 128 + r] = P[m];
-      }
-      const bool end = sl == NSL - 1 || jj == nun - 1;
-      if (!end) return;
+      for (int m = 0; m < MT; ++m) Y[m] = sl == 0 ? P[m] : __fadd_rn(Y[m], P[m]);
+      if (sl != NSL - 1) return;
       const int row = tile * R + r;
-      const bool valid = r < R && row < p.N;
-      if (own && sl == NSL - 1) {
-        // the whole tile was computed here
-        if (valid) {
+      if (r < R && row < p.N) {
 #pragma unroll
-          for (int m = 0; m < MT; ++m) {
-            uint16_t o = f2bf(Y[m]);
-            const size_t oi = (size_t)m * p.ldy + row;
-            if (p.res) o = f2bf(__fadd_rn(bf2f(p.res[oi]), bf2f(o)));
-            p.y[oi] = o;
-          }
+        for (int m = 0; m < MT; ++m) {
+          uint16_t o = f2bf(Y[m]);
+          const size_t oi = (size_t)m * p.ldy + row;
+          if (p.res) o = f2bf(__fadd_rn(bf2f(p.res[oi]), bf2f(o)));
+          p.y[oi] = o;
         }
-        own = false;
-        return;
       }
-      // a split tile: publish this CTA's share; the last CTA to arrive finishes the tile.  The barrier
-      // orders every row's stores before thread 128's gpu-scope release fence and the arrival count.
-      if (own) {
-#pragma unroll
-        for (int m = 0; m < MT; ++m) p.part[tbase + m * 128 + r] = Y[m];
-      }
-      const int contributed = sl - part_start + 1;
-      bar_chain0();
-      if (tid == kLeader) {
-        // acquire-release: publishes the rows' partials (ordered before it by the barrier) and, for the
-        // last arrival, makes the other CTAs' partials visible to this CTA
-        const unsigned old = atom_add_acq_rel(&p.cnt[tile], unsigned(contributed));
-        bars->last = (old + unsigned(contributed) == unsigned(NSL)) ? 1 : 0;
-      }
-      bar_chain0();
-      if (bars->last) {
-        // slices covered by the prefix: those of the CTA that owns unit tile * NSL
-        const int v = tile * NSL;
-        const int G = int(gridDim.x);
-        const int owner = ((v + 1) * G + p.U - 1) / p.U - 1;
-        const int ou1 = (owner + 1) * p.U / G;
-        const int alen = min(ou1, v + NSL) - v;
-        if (valid) {
-#pragma unroll
-          for (int m = 0; m < MT; ++m) {
-            const float* pp = p.part + tbase + m * 128 + r;
-            float acc = __ldcg(pp);
-            for (int s2 = alen; s2 < NSL; ++s2) acc = __fadd_rn(acc, __ldcg(pp + (size_t)s2 * (kMaxTok * 128)));
-            uint16_t o = f2bf(acc);
-            const size_t oi = (size_t)m * p.ldy + row;
-            if (p.res) o = f2bf(__fadd_rn(bf2f(p.res[oi]), bf2f(o)));
-            p.y[oi] = o;
-          }
-        }
-        if (tid == kLeader) p.cnt[tile] = 0u;  // ready for the next launch
-      }
-      bar_chain0();
-      own = false;
     };
 
     for (int j = 0; j < nun; ++j) epilogue(j);
@@ -833,73 +790,55 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ----------------------------------------------------------------------------- host side
 struct Plan {
-  int R, G, ntiles, NSL, whole, cs;
-  long long U;
+  int R, G, ntiles, NSL, cs;
 };
-// Unit indices are 32-bit in the kernel: U * grid must stay below 2^31.
+// Tile and unit indices are 32-bit in the kernel.
 constexpr long long kMaxUnitProduct = (1LL << 31) - 1;
 
 // Clusters of `cs` CTAs (228 KB of shared memory each) that can be resident at once on this device.
 static int max_clusters(int cs);
 
 // Planner override for tests and measurements (qmtp_qmv_set_mode): 0 = cost model, 1 = whole tiles
-// only, 2 = cluster mode where the shape allows it, 3 = workspace split where a workspace is given.
+// only, 2 = cluster mode where the shape allows it.
 static std::atomic<int> g_mode{0};
 
 // Rows per tile, grid and mode, from a cost model of the slowest CTA, fitted to B200 timings of this
 // kernel: about 2 us of setup and first weight latency, 0.45 us per activation slice built, about
-// 1.1 us per unit (16 MMAs of ~98 tensor cycles each, plus the pipeline; the weight bytes of a 128-row
-// unit stream in 0.84 us at the per-SM share of HBM bandwidth), about 5 us to finish a tile split
-// between CTAs through the workspace and about 1 us to finish it inside a cluster.  Ties go to the
-// larger tile and to the earlier mode (whole tiles, cluster, workspace split).
-static Plan make_plan(int N, int K, bool split, int sms) {
+// 1.05 us per unit (16 MMAs of ~98 issue cycles each over two issuers, plus the pipeline; the weight
+// bytes of a 128-row unit stream in 0.84 us at the per-SM share of HBM bandwidth) and about 1.5 us to
+// finish a tile shared inside a cluster.  Ties go to the larger tile and to cluster mode.
+static Plan make_plan(int N, int K, int sms) {
   const int NSL = K / 512;
   Plan best{};
   double best_cost = 1e30;
   const int mode = g_mode.load(std::memory_order_relaxed);
-  const bool try_cluster = mode == 0 || mode == 2;
-  if (mode == 1) split = false;
   // cluster mode: one tile per cluster of cs CTAs, at most kMaxClusterUnits slices per CTA, all
   // clusters resident at once
-  for (int cs = 2; cs <= 4 && try_cluster; cs *= 2) {
+  for (int cs = 2; cs <= 4 && mode != 1; cs *= 2) {
     if (NSL % cs || NSL / cs > kMaxClusterUnits) continue;
     const int mc = max_clusters(cs);
     for (int R = kMaxRows; R >= kMinRows; R -= 8) {
       const int T = (N + R - 1) / R;
       if (T > mc) continue;
       const int per = NSL / cs;
-      const double unit_us = std::max(R * 288.0 / 44.0e3, 1.1);
-      const double cost = 2.0 + 0.45 * per + per * unit_us + 1.0;
+      const double unit_us = std::max(R * 288.0 / 44.0e3, 1.05);
+      const double cost = 2.0 + 0.45 * per + per * unit_us + 1.5;
       if (cost < best_cost * 0.999) {
         best_cost = cost;
-        best = Plan{R, T * cs, T, NSL, 0, cs, (long long)T * NSL};
+        best = Plan{R, T * cs, T, NSL, cs};
       }
     }
   }
   if (mode == 2 && best_cost < 1e30) return best;
-  for (int w = 0; w < (split ? 2 : 1); ++w) {
-    const bool whole = !split || w == 1;
-    if (mode == 3 && whole && split) continue;
-    for (int R = kMaxRows; R >= kMinRows; R -= 8) {
-      const int T = (N + R - 1) / R;
-      long long G, per;
-      int slices;
-      if (!whole) {
-        const long long U = (long long)T * NSL;
-        G = std::min<long long>(sms, U);
-        per = (U + G - 1) / G;
-        slices = int(std::min<long long>(per, NSL));
-      } else {
-        G = std::min(sms, T);
-        per = (long long)((T + G - 1) / G) * NSL;
-        slices = NSL;
-      }
-      const double unit_us = std::max(R * 288.0 / 44.0e3, 1.1);
-      const double cost = 2.0 + 0.45 * std::min(slices, kNB) + double(per) * unit_us + (whole ? 0.0 : 5.0);
-      if (cost < best_cost * 0.999) {
-        best_cost = cost;
-        best = Plan{R, int(G), T, NSL, whole ? 1 : 0, 1, (long long)T * NSL};
-      }
+  for (int R = kMaxRows; R >= kMinRows; R -= 8) {
+    const int T = (N + R - 1) / R;
+    const int G = std::min(sms, T);
+    const long long per = (long long)((T + G - 1) / G) * NSL;
+    const double unit_us = std::max(R * 288.0 / 44.0e3, 1.05);
+    const double cost = 2.0 + 0.45 * std::min(NSL, kNB) + double(per) * unit_us;
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = Plan{R, G, T, NSL, 1};
     }
   }
   return best;
@@ -972,23 +911,11 @@ static int max_clusters(int cs) {
   return c - 1;
 }
 
-static size_t ws_part_bytes(int N, int K) {
-  const long long T = (N + kMinRows - 1) / kMinRows;
-  return (size_t)T * (size_t)(K / 512) * kMaxTok * 128 * sizeof(float);
-}
-
 }  // namespace tq
 
-size_t qmv_tc_workspace(int N, int K) {
-  if (N < 1 || K < 512 || K % 512) return 0;
-  if ((N + tq::kMinRows - 1) / tq::kMinRows > tq::kMaxSplitTiles) return 0;
-  return tq::kCntBytes + tq::ws_part_bytes(N, K);
-}
-
-// All affine qmv entry points land here.  workspace == nullptr: whole tiles per CTA.
+// All affine qmv entry points land here.
 int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const void* b, void* y, const void* res,
-           int M, int N, int K, int ldy, void* workspace, size_t ws_bytes, void* stream, const void* norm_w,
-           float eps) {
+           int M, int N, int K, int ldy, void* stream, const void* norm_w, float eps) {
   using namespace tq;
   if (!x || !w || !s || !b || !y) return QMTP_ERR_ARG;
   if (M < 1 || N < 1 || K < 512 || K % 512 != 0 || ldy < N) return QMTP_ERR_SHAPE;
@@ -997,11 +924,9 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
   if (!aligned16(x) || !aligned16(w) || !aligned16(s) || !aligned16(b)) return QMTP_ERR_ALIGN;
   if (norm_w && (K % 1024 != 0 || K > 32768)) return QMTP_ERR_SHAPE;
   if (norm_w && !aligned16(norm_w)) return QMTP_ERR_ALIGN;
-  const bool split = workspace != nullptr;
-  if (split && (qmv_tc_workspace(N, K) == 0 || ws_bytes < qmv_tc_workspace(N, K))) return QMTP_ERR_SHAPE;
-  if (split && (reinterpret_cast<uintptr_t>(workspace) & 255u)) return QMTP_ERR_ALIGN;
-  const Plan pl = make_plan(N, K, split, sm_count());
-  if (pl.U * (long long)(pl.G + 1) > kMaxUnitProduct) return QMTP_ERR_SHAPE;
+  const Plan pl = make_plan(N, K, sm_count());
+  if ((long long)pl.ntiles * (pl.G + 1) > kMaxUnitProduct || (long long)pl.ntiles * pl.NSL > kMaxUnitProduct)
+    return QMTP_ERR_SHAPE;
   CUtensorMap tw, ts, tb;
   if (!encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, K / 2, N, kBox, pl.R, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, s, K / 64, N, 8, pl.R, CU_TENSOR_MAP_SWIZZLE_NONE) ||
@@ -1015,16 +940,10 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
   p.NSL = pl.NSL;
   p.R = pl.R;
   p.ntiles = pl.ntiles;
-  p.whole = pl.whole;
   p.cs = pl.cs;
   p.nw = static_cast<const uint16_t*>(norm_w);
   p.eps = eps;
-  p.U = int(pl.U);
   p.err = device_error_ptr();
-  if (split) {
-    p.cnt = static_cast<unsigned*>(workspace);
-    p.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCntBytes);
-  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int m0 = 0; m0 < M; m0 += kMaxTok) {
     const int mm = std::min(kMaxTok, M - m0);
@@ -1043,11 +962,11 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
   return QMTP_OK;
 }
 
-int qmv_tc_plan(int N, int K, int split, int* rows, int* grid, int* units, int* cluster) {
-  const tq::Plan pl = tq::make_plan(N, K, split != 0, sm_count());
+int qmv_tc_plan(int N, int K, int* rows, int* grid, int* units, int* cluster) {
+  const tq::Plan pl = tq::make_plan(N, K, sm_count());
   if (rows) *rows = pl.R;
   if (grid) *grid = pl.G;
-  if (units) *units = int(pl.U);
+  if (units) *units = int((long long)pl.ntiles * pl.NSL);
   if (cluster) *cluster = pl.cs;
   return QMTP_OK;
 }
@@ -1058,38 +977,48 @@ using namespace qmtp;
 
 extern "C" int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const void* biases, void* y,
                                    int M, int N, int K, int ldy, void* stream) {
-  return qmv_tc(x, 0, w, scales, biases, y, nullptr, M, N, K, ldy, nullptr, 0, stream, nullptr, 0.0f);
+  return qmv_tc(x, 0, w, scales, biases, y, nullptr, M, N, K, ldy, stream, nullptr, 0.0f);
 }
 
 extern "C" int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void* scales, const void* biases, void* y,
                                        const void* res, int M, int N, int K, int ldy, void* stream) {
   if (!res) return QMTP_ERR_ARG;
-  return qmv_tc(x, 0, w, scales, biases, y, res, M, N, K, ldy, nullptr, 0, stream, nullptr, 0.0f);
+  return qmv_tc(x, 0, w, scales, biases, y, res, M, N, K, ldy, stream, nullptr, 0.0f);
 }
 
-extern "C" size_t qmtp_qmv_workspace(int N, int K) { return qmv_tc_workspace(N, K); }
+// The workspace of the _split / _norm entry points is no longer used: a tile shared between CTAs is
+// finished inside their thread-block cluster.  The query keeps answering 256 bytes for every valid
+// shape so that callers which allocate it keep working.
+extern "C" size_t qmtp_qmv_workspace(int N, int K) {
+  if (N < 1 || K < 512 || K % 512) return 0;
+  return 256;
+}
 
 extern "C" int qmtp_qmv_affine_g64_split(const void* x, long long ldx, const void* w, const void* scales,
                                          const void* biases, void* y, const void* res, int M, int N, int K, int ldy,
                                          void* workspace, size_t ws_bytes, void* stream) {
-  if (!workspace) return QMTP_ERR_ARG;
-  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, workspace, ws_bytes, stream, nullptr, 0.0f);
+  (void)workspace;
+  (void)ws_bytes;
+  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, stream, nullptr, 0.0f);
 }
 
 extern "C" int qmtp_qmv_affine_g64_norm(const void* x, long long ldx, const void* norm_w, float eps, const void* w,
                                         const void* scales, const void* biases, void* y, const void* res, int M,
                                         int N, int K, int ldy, void* workspace, size_t ws_bytes, void* stream) {
+  (void)workspace;
+  (void)ws_bytes;
   if (!norm_w) return QMTP_ERR_ARG;
-  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, workspace, ws_bytes, stream, norm_w, eps);
+  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, stream, norm_w, eps);
 }
 
 extern "C" int qmtp_qmv_set_mode(int mode) {
-  if (mode < 0 || mode > 3) return QMTP_ERR_ARG;
+  if (mode < 0 || mode > 2) return QMTP_ERR_ARG;
   tq::g_mode.store(mode, std::memory_order_relaxed);
   return QMTP_OK;
 }
 
 extern "C" int qmtp_qmv_plan(int N, int K, int split, int* rows_per_tile, int* grid, int* units, int* cluster) {
+  (void)split;
   if (N < 1 || K < 512 || K % 512) return QMTP_ERR_SHAPE;
-  return qmv_tc_plan(N, K, split, rows_per_tile, grid, units, cluster);
+  return qmv_tc_plan(N, K, rows_per_tile, grid, units, cluster);
 }

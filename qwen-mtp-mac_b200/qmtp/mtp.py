@@ -100,11 +100,6 @@ class MTPDecoder:
         self._gdn_args = {}
         for i in self.lin_ids:
             self._gdn_args[i] = self._make_gdn_args(i)
-        # split-K workspace of the affine projections (tile partials + arrival counters), sized for the
-        # largest matrix the decoder multiplies; zero-filled once, the kernel leaves the counters at zero
-        shapes = [(lin.out_features, lin.in_features) for lin in _linears(W) if lin.mode == "affine"]
-        ws = max([int(self.L.qmtp_qmv_workspace(n, k_)) for n, k_ in shapes] + [256])
-        self.qws = torch.zeros(ws, dtype=torch.uint8, device=dev)
         self.graph = None
         self.launches = 0      # kernels launched by the library calls of this decoder
         self.prof = None       # list of (bytes, start event, end event, shape) while profiling qmv
@@ -155,7 +150,7 @@ class MTPDecoder:
 
     def _qmv(self, x, lin, y, M, res=None, ldy=None, norm=None):
         """4-bit GEMV y = x . W^T (+ res): affine layers on the tensor-core kernel with split tiles
-        (qmtp_qmv_affine_g64_split, one launch per 4 rows), NVFP4 layers (an NVFP4 checkpoint) on
+        (qmtp_qmv_affine_g64_split, one launch per 4 rows; shared tiles finished inside a cluster), NVFP4 layers (an NVFP4 checkpoint) on
         qmtp_qmv_nvfp4_g16_res.  norm (an RMSNorm weight): x is RMS-normalised first -- inside the
         affine kernel (qmtp_qmv_affine_g64_norm), or by qmtp_rmsnorm into self.xn for NVFP4."""
         N, K = lin.out_features, lin.in_features
@@ -178,12 +173,12 @@ class MTPDecoder:
             self._chk(self.L.qmtp_qmv_affine_g64_norm(x.data_ptr(), K, norm.data_ptr(), self.a.eps, lin.weight.data_ptr(),
                                                       lin.scales.data_ptr(), lin.biases.data_ptr(), y.data_ptr(),
                                                       res.data_ptr() if res is not None else None, M, N, K, ldy,
-                                                      self.qws.data_ptr(), self.qws.numel(), self._st()), "qmv")
+                                                      None, 0, self._st()), "qmv")
         else:
             self._chk(self.L.qmtp_qmv_affine_g64_split(x.data_ptr(), K, lin.weight.data_ptr(), lin.scales.data_ptr(),
                                                        lin.biases.data_ptr(), y.data_ptr(),
                                                        res.data_ptr() if res is not None else None, M, N, K, ldy,
-                                                       self.qws.data_ptr(), self.qws.numel(), self._st()), "qmv")
+                                                       None, 0, self._st()), "qmv")
         if self.prof is not None:
             e1 = torch.cuda.Event(enable_timing=True)
             e1.record()

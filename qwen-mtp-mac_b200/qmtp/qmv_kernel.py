@@ -19,23 +19,6 @@ from . import _lib
 MIN_ROWS, MAX_ROWS = 3, 4  # reference defaults (qmv_kernel.py:105); informational here
 GROUP_SIZE = 64
 
-# Split-K workspaces, one per (device, stream): the kernel's tile arrival counters must not be shared by
-# launches that can run at the same time.  Zero-filled once; every launch leaves the counters at zero.
-_WS: dict = {}
-
-
-def workspace(N: int, K: int, device=None) -> torch.Tensor:
-    """The cached split-K workspace of the current stream, grown to cover an N x K matrix."""
-    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
-    need = int(_lib.lib().qmtp_qmv_workspace(N, K))
-    ws = _WS.get(key)
-    if ws is None or ws.numel() < need:
-        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=dev)
-        _WS[key] = ws
-    return ws
-
-
 def _flat(x: torch.Tensor):
     K = x.shape[-1]
     return x.reshape(-1, K), K
@@ -64,8 +47,9 @@ def qmv_affine(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: t
     """y = x @ dequant(w).T for the affine 4-bit group-64 format (bf16 in, bf16 out).
     x: [..., K] bf16; w: uint32/int32 [N, K/8]; scales, biases: bf16 [N, K/64] -> [..., N].
     res (bf16, same shape as out): y = bf16(res + bf16(x . W^T)), may alias out.
-    split=True (default) lets CTAs share a tile (needs a workspace: `ws`, or the cached one of the
-    current stream); split=False gives each CTA whole tiles and needs none.  Both give the same bits.
+    split=True (default) calls the strided entry point (qmtp_qmv_affine_g64_split), split=False the
+    plain ones; both give the same bits, and either may share a tile between the CTAs of a cluster.
+    ws: accepted for compatibility, not needed.
     norm=(weight bf16 [K], eps): x is first RMS-normalised (mlx_lm RMSNorm) inside the kernel."""
     if group_size != 64:
         raise NotImplementedError("affine qmv is implemented for group_size=64")
@@ -85,18 +69,13 @@ def qmv_affine(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: t
     if norm is not None:
         nw, eps = norm
         _lib.require_cuda(nw)
-        if split and ws is None:
-            ws = workspace(N, K, x.device)
         rc = L.qmtp_qmv_affine_g64_norm(xf.data_ptr(), K, nw.data_ptr(), float(eps), w.data_ptr(), scales.data_ptr(),
                                         biases.data_ptr(), out.data_ptr(), _lib.ptr(res), M, N, K, out.shape[-1],
-                                        _lib.ptr(ws if split else None),
-                                        (ws.numel() * ws.element_size()) if split else 0, _lib.stream())
+                                        None, 0, _lib.stream())
     elif split:
-        if ws is None:
-            ws = workspace(N, K, x.device)
         rc = L.qmtp_qmv_affine_g64_split(xf.data_ptr(), K, w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
-                                         out.data_ptr(), _lib.ptr(res), M, N, K, out.shape[-1], ws.data_ptr(),
-                                         ws.numel() * ws.element_size(), _lib.stream())
+                                         out.data_ptr(), _lib.ptr(res), M, N, K, out.shape[-1], None, 0,
+                                         _lib.stream())
     elif res is not None:
         rc = L.qmtp_qmv_affine_g64_res(xf.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
                                        out.data_ptr(), res.data_ptr(), M, N, K, out.shape[-1], _lib.stream())

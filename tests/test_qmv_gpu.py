@@ -10,9 +10,9 @@ from tests._util import affine_layer, randn_bf16, to_np, to_torch
 
 pytestmark = pytest.mark.gpu
 G = Path(__file__).resolve().parent / "golden"
-# (planner mode, workspace given): the cost model with and without a workspace, whole tiles only,
-# clusters wherever the shape allows them, the workspace split wherever a workspace is given
-MODES = [(0, True), (0, False), (1, True), (2, False), (3, True)]
+# (planner mode, through the strided _split entry point): the cost model through both entry points,
+# whole tiles only, clusters wherever the shape allows them
+MODES = [(0, True), (0, False), (1, True), (2, False)]
 
 
 @pytest.fixture
@@ -50,12 +50,11 @@ def test_qmv_affine_bit_exact(K, M, dev, planner):
             assert np.array_equal(_run_affine(x, wq, s, b, dev, split=split), ref), (K, M, N, mode, split)
 
 
-def test_qmv_affine_shared_workspace_across_shapes(dev):
-    """One workspace serves matrices of every shape in turn (the decoder's use): the slice partials
-    of a large matrix never disturb the tile counters of a smaller one."""
-    from qmtp import qmv_kernel, _lib
+def test_qmv_affine_many_shapes_in_turn(dev):
+    """Matrices of every shape in turn through one stream (the decoder's use), twice: cluster and
+    whole-tile launches of different shapes leave nothing behind that disturbs the next one."""
+    from qmtp import qmv_kernel
 
-    ws = torch.zeros(_lib.lib().qmtp_qmv_workspace(24576, 4096), dtype=torch.uint8, device=dev)
     cases = []
     for N, K in ((24576, 4096), (1, 2048), (4096, 12288), (37, 4096), (12352, 4096), (5, 8192)):
         _, wq, s, b = affine_layer(N, K, seed=N ^ K)
@@ -64,7 +63,7 @@ def test_qmv_affine_shared_workspace_across_shapes(dev):
     for _ in range(2):
         for x, wq, s, b, ref in cases:
             xt, wt, st, bt = (to_torch(a, dev) for a in (x, wq, s, b))
-            assert np.array_equal(to_np(qmv_kernel.qmv_affine(xt, wt, st, bt, ws=ws)), ref), wq.shape
+            assert np.array_equal(to_np(qmv_kernel.qmv_affine(xt, wt, st, bt)), ref), wq.shape
 
 
 @pytest.mark.parametrize("M", [1, 2, 3, 4])
@@ -79,20 +78,19 @@ def test_qmv_affine_config1_bit_exact(M, dev):
 @pytest.mark.parametrize("N,K", [(12352, 4096), (4096, 4096), (4096, 12288), (24576, 4096), (10240, 4096),
                                  (4096, 8192), (777, 12288)])
 def test_qmv_affine_decoder_shapes(N, K, dev, planner):
-    """The decoder's projection shapes in every planner mode: split tiles (slice partials finished by
-    the last CTA through the workspace, or by the first CTA of a cluster through distributed shared
-    memory) give the oracle's bits, the workspace counters return to zero, repeated calls agree."""
+    """The decoder's projection shapes in every planner mode: shared tiles (slice partials finished by
+    the first CTA of a cluster through distributed shared memory) give the oracle's bits, repeated
+    calls agree."""
     from qmtp import qmv_kernel, _lib
 
     _, wq, s, b = affine_layer(N, K, seed=N + K)
     x = randn_bf16((3, K), 5)
     ref = ops.qmv_affine(x, wq, s, b)
-    ws = torch.zeros(_lib.lib().qmtp_qmv_workspace(N, K), dtype=torch.uint8, device=dev)
     xt, wt, st, bt = (to_torch(a, dev) for a in (x, wq, s, b))
-    for mode in (0, 1, 2, 3):
+    for mode in (0, 1, 2):
         planner(mode)
         for _ in range(2):
-            got = to_np(qmv_kernel.qmv_affine(xt, wt, st, bt, ws=ws))
+            got = to_np(qmv_kernel.qmv_affine(xt, wt, st, bt))
             assert np.array_equal(got, ref), (N, K, mode)
         plan = _lib.qmv_plan(N, K, True)
         T = (N + plan["rows_per_tile"] - 1) // plan["rows_per_tile"]
@@ -103,8 +101,6 @@ def test_qmv_affine_decoder_shapes(N, K, dev, planner):
             assert plan["cluster"] > 1, plan
         if mode == 1:
             assert plan["cluster"] == 1 and plan["grid"] <= T
-    head = ws.view(torch.int32)[:16384]
-    assert int(head.abs().sum()) == 0, "arrival counters left non-zero"
 
 
 def test_qmv_affine_residual_in_place(dev, planner):
@@ -160,10 +156,8 @@ def test_qmv_affine_split_ldx(dev):
     ref = ops.qmv_affine(np.ascontiguousarray(xw[:, :K]), wq, s, b)
     xt, wt, st, bt = (to_torch(a, dev) for a in (xw, wq, s, b))
     y = torch.empty((3, N), dtype=torch.bfloat16, device=dev)
-    ws = torch.zeros(_lib.lib().qmtp_qmv_workspace(N, K), dtype=torch.uint8, device=dev)
     _lib.check(_lib.lib().qmtp_qmv_affine_g64_split(xt.data_ptr(), ldx, wt.data_ptr(), st.data_ptr(), bt.data_ptr(),
-                                                   y.data_ptr(), None, 3, N, K, N, ws.data_ptr(), ws.numel(),
-                                                   _lib.stream()), "split")
+                                                   y.data_ptr(), None, 3, N, K, N, None, 0, _lib.stream()), "split")
     assert np.array_equal(to_np(y), ref)
 
 
