@@ -57,16 +57,19 @@ constexpr int kWStage = 2 * kMaxRows * kBox;       // 32768: two boxes
 constexpr int kSStage = kMaxRows * 16;             // 2048: 8 bf16 per row
 constexpr int kStage = kWStage + 2 * kSStage;      // 36864
 constexpr int kNS = 4;                             // weight ring stages
-constexpr int kBGroup = 1024;                      // B image of one group: 16 rows x 64 bytes
+// B image of one group: 16 rows x 64 bytes as 4 x 2 core matrices (8 rows x 16 bytes each).  The
+// four 16-byte k chunks sit kLbo = 272 bytes apart and the groups 1088 bytes apart (not multiples of
+// 128), so the 32 lanes of a build store spread over all 32 banks (two wavefronts for 256 bytes);
+// the 16-byte holes after chunks 0 and 1 hold the group's factors (c, xf) of tokens 0-1 and 2-3.
+constexpr int kLbo = 272;
+constexpr int kBGroup = 1088;
 constexpr int kNB = 8;                             // B slots
-constexpr int kBSlot = kGpu * kBGroup;             // 8192
+constexpr int kBSlot = kGpu * kBGroup;             // 8704
 constexpr int kMaxTok = 4;                         // tokens per launch (3 limbs each: 12 of 16 B rows)
-constexpr int kXSlot = kGpu * kMaxTok * 8;         // per slot: [group][token] float2 (c, xf)
 constexpr int kOffB = kNS * kStage;                // 147456
-constexpr int kOffX = kOffB + kNB * kBSlot;        // 212992
-constexpr int kOffH = kOffX + kNB * kXSlot;        // 215040: chain-1 partials [2][kMaxTok][128] fp32
-constexpr int kOffSB = kOffH + 2 * kMaxTok * 128 * 4;  // 219136: scales | biases per unit [2][2][128] x 16 B
-constexpr int kOffBar = kOffSB + 2 * 2 * 128 * 16;      // 227328
+constexpr int kOffH = kOffB + kNB * kBSlot;        // 217088: chain-1 partials [2][kMaxTok][128] fp32
+constexpr int kOffSB = kOffH + 2 * kMaxTok * 128 * 4;  // 221184: scales | biases per unit [2][2][128] x 16 B
+constexpr int kOffBar = kOffSB + 2 * 2 * 128 * 16;      // 229376
 constexpr int kSmemUsed = kOffBar + 512;
 constexpr int kSmem = kSmemUsed + 1024;            // slack for 1024-byte alignment of the base
 constexpr int kThreads = 640;                      // 20 warps
@@ -74,6 +77,9 @@ constexpr int kTmemCols = 512;
 constexpr int kABase = 0, kDBase = 256;
 constexpr int kMinRows = 64;                       // smallest tile the planner picks
 static_assert(kOffB % 1024 == 0 && kStage % 1024 == 0, "stage alignment");
+static_assert(3 * kLbo + 2 * 128 <= kBGroup && kLbo - 256 >= 16 && kBGroup % 16 == 0, "B group layout");
+// Byte offset of a group's (c, xf) float2 for token m inside its B image (the holes after chunks 0, 1).
+__host__ __device__ constexpr int xs_offset(int g, int m) { return g * kBGroup + 256 + (m >> 1) * kLbo + (m & 1) * 8; }
 static_assert(kSmem <= 232448, "shared memory per CTA");
 // Cluster mode: a CTA holds at most this many slices of its tile, so that its per-slice partials
 // ([unit][kMaxTok][128] fp32, 2 KB a unit) fit in the B slots it leaves free.
@@ -207,7 +213,7 @@ __device__ __forceinline__ uint4 rms_apply(uint4 xv, uint4 wv, float r) {
 // their three byte limbs in the B image of the slot (rows 3m..3m+2, permuted k: the even k of the
 // 8 then the odd k, as the nibble unpacking orders the weights) and, from lane 0 of the group, the
 // group factors (c, xf).  All 8 lanes of a group are in one warp.
-__device__ __forceinline__ void prep_task(uint4 v, int m, int g, int li, uint8_t* bimg, float2* xsc) {
+__device__ __forceinline__ void prep_task(uint4 v, int m, int g, int li, uint8_t* bimg) {
   // largest magnitude of the group as a bf16 bit pattern (patterns order like magnitudes; an infinity
   // or NaN has a pattern >= 0x7F80, above every finite one)
   const uint32_t a2 = __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu), __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
@@ -247,7 +253,7 @@ __device__ __forceinline__ void prep_task(uint4 v, int m, int g, int li, uint8_t
 #pragma unroll
   for (int l = 0; l < 3; ++l) {
     const int j = 3 * m + l;
-    const int off = g * kBGroup + ((pb >> 4) * 2 + (j >> 3)) * 128 + (j & 7) * 16 + (pb & 15);
+    const int off = g * kBGroup + (pb >> 4) * kLbo + (j >> 3) * 128 + (j & 7) * 16 + (pb & 15);
     *reinterpret_cast<uint2*>(bimg + off) = make_uint2(lo[l], hi[l]);
   }
   if (li == 0) {
@@ -260,7 +266,7 @@ __device__ __forceinline__ void prep_task(uint4 v, int m, int g, int li, uint8_t
       c = pow2f(E - 19);
       xf = __fmul_rn(__int2float_rn(xs), c);
     }
-    xsc[g * kMaxTok + m] = make_float2(c, xf);
+    *reinterpret_cast<float2*>(bimg + xs_offset(g, m)) = make_float2(c, xf);
   }
 }
 
@@ -473,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         cur_slot = slot;
         ++batches;
         const int m = r >> 6, g = (r >> 3) & 7, li = r & 7;
-        prep_task(v, m, g, li, sm + kOffB + slot * kBSlot, reinterpret_cast<float2*>(sm + kOffX + slot * kXSlot));
+        prep_task(v, m, g, li, sm + kOffB + slot * kBSlot);
       }
     }
     if (cur_slot >= 0) {
@@ -549,15 +555,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d0 = tmem + uint32_t(kDBase + a * 128 + 64 * h);
         const uint32_t a0 = tmem + uint32_t(kABase + a * 128 + 64 * h);
-        // descriptor of the chain's first group; group gi / k-half k2 start (gi*1024 + k2*512) bytes
-        // later (the start-address field holds address / 16 and stays below 2^14)
-        const uint64_t bd = umma_desc(bsm + uint32_t(slot * kBSlot + 4 * h * kBGroup), 256u, 128u);
+        // descriptor of the chain's first group; group gi / k-half k2 start gi * kBGroup + k2 * 2 * kLbo
+        // bytes later (the start-address field holds address / 16 and stays below 2^14)
+        const uint64_t bd = umma_desc(bsm + uint32_t(slot * kBSlot + 4 * h * kBGroup), uint32_t(kLbo), 128u);
 #pragma unroll
         for (int gi = 0; gi < 4; ++gi) {
 #pragma unroll
           for (int k2 = 0; k2 < 2; ++k2)
             umma_i8(d0 + uint32_t(gi * 16), a0 + uint32_t(gi * 16 + 8 * k2),
-                    bd + uint64_t((gi * kBGroup + k2 * 512) >> 4), idesc, uint32_t(k2));
+                    bd + uint64_t((gi * kBGroup + k2 * 2 * kLbo) >> 4), idesc, uint32_t(k2));
         }
         umma_commit(&bars->dfull[h][a]);
         issued = true;
@@ -651,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
       }
       tc_fence_after();
-      const float2* xsc = reinterpret_cast<const float2*>(sm + kOffX + slot * kXSlot);
+      const uint8_t* bslot = sm + kOffB + slot * kBSlot;
       // this row's scales and biases of the chain's groups, left by the unpacking warp of the row
       const uint4 sbv = *reinterpret_cast<const uint4*>(sm + kOffSB + ((a * 2 + h) * 128 + r) * 16);
       const uint32_t sw[2] = {sbv.x, sbv.y}, bw[2] = {sbv.z, sbv.w};
@@ -677,7 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
           const int S = int(v[gl][3 * m + 2]) * 16384 + int(v[gl][3 * m + 1]) * 128 + int(v[gl][3 * m]);
-          const float2 cx = xsc[g * kMaxTok + m];
+          const float2 cx = *reinterpret_cast<const float2*>(bslot + xs_offset(g, m));
           H[m] = __fmaf_rn(__int2float_rn(S), __fmul_rn(s, cx.x), H[m]);
           H[m] = __fmaf_rn(b, cx.y, H[m]);
         }
