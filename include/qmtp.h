@@ -205,6 +205,14 @@ int qmtp_lmhead2(const void* h, const void* wq, const void* scales, const void* 
                  const void* w_fine, int M, int V, int K, int k, int* out_idx, void* out_fine,
                  int* out_argmax, void* coarse_out, void* workspace, size_t ws_bytes, void* stream);
 
+/* qmtp_lmhead2 with the reference's own coarse format (lm_head2.py:19: NVFP4, group 16): coarse
+ * logits by qmtp_qmv_nvfp4_g16 (wq uint32 [V, K/8] e2m1 nibbles, scales uint8 [V, K/16] e4m3),
+ * then the same top-k selection, exact bf16 rescoring and argmax.  K % 1024 == 0; workspace:
+ * qmtp_lmhead2_workspace(M, V, k). */
+int qmtp_lmhead2_nvfp4(const void* h, const void* wq, const void* scales, const void* w_fine, int M, int V,
+                       int K, int k, int* out_idx, void* out_fine, int* out_argmax, void* coarse_out,
+                       void* workspace, size_t ws_bytes, void* stream);
+
 /* Two-stage head sharded by vocabulary over G GPUs (lm_head2.py:111-117 split by output rows; the
  * NCCL exchange between the two calls is the host's, e.g. torch.distributed all_gather):
  *   qmtp_lmhead2_shard: on the rank holding vocabulary rows [v0, v0 + Vs): coarse logits of the shard,

@@ -244,6 +244,15 @@ def two_stage_head(h, wq, s, b, W, k=64):
     return coarse, idx, fine, amax
 
 
+def two_stage_head_nvfp4(h, wq, s_u8, W, k=64):
+    """lm_head2.py:14-29 with the reference's NVFP4 g16 coarse copy (lm_head2.py:19) restated:
+    (coarse bf16 [M,V], idx [M,k], fine bf16 [M,k], argmax [M])."""
+    coarse = qmv_nvfp4(h, wq, s_u8)
+    idx = topk_bf16(coarse, k)
+    fine, amax = rescore_bf16(W, h, idx)
+    return coarse, idx, fine, amax
+
+
 def dot_bf16(w_row, h_row) -> np.float32:
     """C qo_dot_bf16: the fine-logit dot product in its fixed order (fp32, before bf16 rounding)."""
     w = np.ascontiguousarray(w_row, np.uint16)

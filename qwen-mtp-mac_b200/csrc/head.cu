@@ -391,6 +391,22 @@ extern "C" int qmtp_lmhead2(const void* h, const void* wq, const void* scales, c
                            ws_bytes - coarse_bytes, stream);
 }
 
+// The reference's own head format (lm_head2.py:19: nn.QuantizedLinear.from_linear(lin, group_size=16,
+// bits=4, mode="nvfp4")): the coarse logits from the NVFP4 g16 GEMV, the same selection and rescoring.
+extern "C" int qmtp_lmhead2_nvfp4(const void* h, const void* wq, const void* scales, const void* w_fine, int M, int V,
+                                  int K, int k, int* out_idx, void* out_fine, int* out_argmax, void* coarse_out,
+                                  void* workspace, size_t ws_bytes, void* stream) {
+  if (!h || !wq || !scales || !w_fine || !out_idx || !out_fine || !workspace) return QMTP_ERR_ARG;
+  if (ws_bytes < qmtp_lmhead2_workspace(M, V, k)) return QMTP_ERR_ARG;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  const size_t coarse_bytes = (size_t(M) * V * sizeof(uint16_t) + 255) / 256 * 256;
+  void* coarse = coarse_out ? coarse_out : ws;
+  int rc = qmtp_qmv_nvfp4_g16(h, wq, scales, coarse, M, V, K, V, stream);
+  if (rc != QMTP_OK) return rc;
+  return qmtp_topk_rescore(coarse, V, M, V, k, w_fine, h, K, out_idx, out_fine, out_argmax, ws + coarse_bytes,
+                           ws_bytes - coarse_bytes, stream);
+}
+
 // ----------------------------------------------------------------------------- vocabulary shards
 extern "C" size_t qmtp_lmhead2_shard_workspace(int M, int Vs, int k) {
   const size_t head = qmtp_lmhead2_workspace(M, Vs, k);

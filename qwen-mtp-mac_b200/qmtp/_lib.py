@@ -70,6 +70,7 @@ SIGNATURES.update({
     "qmtp_lmhead2_noalloc": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P],
     "qmtp_lmhead2_shard": [_P, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_longlong, _P, _P, _P, ctypes.c_size_t, _P],
     "qmtp_lmhead2_merge": [_P, _P, _I, _I, _I, _P, _P, _P, _P],
+    "qmtp_lmhead2_nvfp4": [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     "qmtp_embed": [_P, _I, _P, _P, _P, _I, _I, _P, _I, _P],
     "qmtp_embed_nvfp4": [_P, _I, _P, _P, _I, _I, _P, _I, _P],
     "qmtp_qmv_nvfp4_g16_res": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],

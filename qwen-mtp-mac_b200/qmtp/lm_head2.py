@@ -4,8 +4,8 @@ Reference: lm_head2.py:14-29 ``TwoStageHead(weight, k=64)`` (coarse quantized fu
 argpartition top-k, exact rescoring of the k rows with the original bf16 weights, full-size logits
 with -inf elsewhere) and lm_head2.py:32-36 ``k_for(sampling)``.
 
-The coarse stage here is the affine 4-bit group-64 format (the reference builds NVFP4 group-16;
-the B200 build is judged on affine g64).  ``__call__`` keeps the reference's output contract;
+The coarse stage is the affine 4-bit group-64 format by default or, with
+``mode="nvfp4"``, the reference's own NVFP4 group-16 format (lm_head2.py:19).  ``__call__`` keeps the reference's output contract;
 ``select`` is the engine's path: candidates, exact logits and the greedy token without
 materialising [.., V] logits.  Ties are resolved as (value descending, vocab index ascending).
 """
@@ -18,12 +18,24 @@ from .qmv_kernel import QuantizedLinear
 
 
 class TwoStageHead:
-    def __init__(self, weight: torch.Tensor, k: int = 64, coarse: QuantizedLinear | None = None):
-        """weight: bf16 [V, D] (kept resident, only k rows per position are read)."""
+    def __init__(self, weight: torch.Tensor, k: int = 64, coarse: QuantizedLinear | None = None,
+                 mode: str = "affine"):
+        """weight: bf16 [V, D] (kept resident, only k rows per position are read).  coarse: a 4-bit copy
+        (affine g64 or NVFP4 g16); built from weight in `mode` ("affine" or "nvfp4") when not given."""
         if weight.dtype != torch.bfloat16 or weight.dim() != 2:
             raise ValueError("TwoStageHead expects a bf16 [V, D] weight")
         self.weight = weight
-        self.coarse = coarse if coarse is not None else QuantizedLinear.from_linear(weight, group_size=64, bits=4)
+        if coarse is None:
+            if mode == "nvfp4":
+                from .moe import quantize as quantize_fp4
+
+                wq, sc = quantize_fp4(weight[None], "nvfp4")
+                coarse = QuantizedLinear(wq[0], sc[0], None, group_size=16, mode="nvfp4")
+            elif mode == "affine":
+                coarse = QuantizedLinear.from_linear(weight, group_size=64, bits=4)
+            else:
+                raise ValueError(f"unknown coarse mode {mode!r}")
+        self.coarse = coarse
         self.k = k
         self._ws: dict = {}
 
@@ -56,11 +68,17 @@ class TwoStageHead:
             idx, fine, amax = out
         ws = self._workspace(M, k)
         c = self.coarse
-        _lib.check(_lib.lib().qmtp_lmhead2(
-            h2.data_ptr(), c.weight.data_ptr(), c.scales.data_ptr(), c.biases.data_ptr(), self.weight.data_ptr(),
-            M, self.vocab, D, k, idx.data_ptr(), fine.data_ptr(), amax.data_ptr(),
-            None if coarse_out is None else coarse_out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream()),
-            "TwoStageHead")
+        if c.mode == "nvfp4":
+            rc = _lib.lib().qmtp_lmhead2_nvfp4(
+                h2.data_ptr(), c.weight.data_ptr(), c.scales.data_ptr(), self.weight.data_ptr(), M, self.vocab, D, k,
+                idx.data_ptr(), fine.data_ptr(), amax.data_ptr(), None if coarse_out is None else coarse_out.data_ptr(),
+                ws.data_ptr(), ws.numel(), _lib.stream())
+        else:
+            rc = _lib.lib().qmtp_lmhead2(
+                h2.data_ptr(), c.weight.data_ptr(), c.scales.data_ptr(), c.biases.data_ptr(), self.weight.data_ptr(),
+                M, self.vocab, D, k, idx.data_ptr(), fine.data_ptr(), amax.data_ptr(),
+                None if coarse_out is None else coarse_out.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream())
+        _lib.check(rc, "TwoStageHead")
         return idx, fine, amax
 
     def __call__(self, h: torch.Tensor) -> torch.Tensor:
@@ -100,6 +118,8 @@ class ShardedTwoStageHead:
         if local is None:
             if weight_shard is None or weight_shard.dtype != torch.bfloat16 or weight_shard.dim() != 2:
                 raise ValueError("ShardedTwoStageHead expects a bf16 [Vs, D] weight shard")
+            if coarse is not None and coarse.mode != "affine":
+                raise NotImplementedError("the sharded head's coarse stage is affine g64")
             self.coarse = coarse if coarse is not None else QuantizedLinear.from_linear(weight_shard)
         self._local = local or self._local_lib
         self._merge = merge or self._merge_lib

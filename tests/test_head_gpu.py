@@ -105,3 +105,29 @@ def test_vocab_shards_merge_to_the_whole_head(G, V, M, k, dev):
     assert np.array_equal(to_np(idx).view(np.int32), ridx)
     assert np.array_equal(to_np(fv), rfine)
     assert np.array_equal(to_np(amax).view(np.int32), ramax)
+
+
+@pytest.mark.parametrize("V,D,M,k", [(248320, 4096, 3, 64), (50000, 4096, 1, 256), (4096, 1024, 2, 64)])
+def test_two_stage_head_nvfp4_coarse_bit_exact(V, D, M, k, dev):
+    """The reference's own head format (lm_head2.py:19, NVFP4 g16 coarse copy): index sets, order,
+    exact logits and argmax bit-exact against the oracle; the coarse copy built on the GPU from the
+    bf16 weight equals the oracle's quantizer."""
+    from qmtp.lm_head2 import TwoStageHead
+    from qmtp.qmv_kernel import QuantizedLinear
+
+    W = randn_bf16((V, D), V + 3, 0.02)
+    h = randn_bf16((M, D), 11)
+    nq, ns = ops.quantize_fp4(W, "nvfp4")
+    head = TwoStageHead(to_torch(W, dev), k, QuantizedLinear(to_torch(nq, dev), to_torch(ns, dev), None,
+                                                             group_size=16, mode="nvfp4"))
+    idx, fine, amax = head.select(to_torch(h, dev))
+    _, ridx, rfine, ramax = ops.two_stage_head_nvfp4(h, nq, ns, W, k)
+    assert np.array_equal(to_np(idx).view(np.int32), ridx)
+    assert np.array_equal(to_np(fine), rfine)
+    assert np.array_equal(to_np(amax).view(np.int32), ramax)
+    if V == 4096:
+        built = TwoStageHead(to_torch(W, dev), k, mode="nvfp4")
+        assert np.array_equal(to_np(built.coarse.weight).view(np.uint32), nq.view(np.uint32))
+        assert np.array_equal(to_np(built.coarse.scales), ns)
+        got = [to_np(t) for t in built.select(to_torch(h, dev))]
+        assert np.array_equal(got[0].view(np.int32), ridx)
