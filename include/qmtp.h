@@ -82,6 +82,22 @@ int qmtp_qmv_affine_g64_norm(const void* x, long long ldx, const void* norm_w, f
                              const void* scales, const void* biases, void* y, const void* res, int M, int N,
                              int K, int ldy, void* workspace, size_t ws_bytes, void* stream);
 
+/* qmtp_qmv_affine_g64_split with the SwiGLU of an MLP in front: y = (silu(gate) * up) . W^T (+ res), the
+ * gate at gu[m, k] and the up projection at gu[m, K + k] (ldgu >= 2K elements; 0 = 2K); silu and the
+ * bf16 roundings of the decoder's qmtp_swiglu, computed by every CTA while it builds its operand.  Same
+ * bits as qmtp_swiglu followed by qmtp_qmv_affine_g64.  (mlx-lm's MLP: down(silu(gate(x)) * up(x)).) */
+int qmtp_qmv_affine_g64_swiglu(const void* gu, long long ldgu, const void* w, const void* scales,
+                               const void* biases, void* y, const void* res, int M, int N, int K, int ldy,
+                               void* stream);
+
+/* qmtp_qmv_affine_g64_split with the GatedDeltaNet output gate in front (gdn_fused.py:10,144, the
+ * norm of qmtp_gdn_norm_gate): x = bf16(RMSNorm_head(yg; norm_w, eps) * silu(z)) over heads of 128,
+ * yg fp32 [M, ldyg] (floats), z bf16 [M, ldz], norm_w bf16 [128].  Same bits as qmtp_gdn_norm_gate
+ * followed by qmtp_qmv_affine_g64. */
+int qmtp_qmv_affine_g64_gated(const float* yg, long long ldyg, const void* z, long long ldz, const void* norm_w,
+                              float eps, const void* w, const void* scales, const void* biases, void* y,
+                              const void* res, int M, int N, int K, int ldy, void* stream);
+
 /* Tiling the affine kernel picks for an N x K matrix (split: ignored): weight
  * rows per tile, CTAs, work units (tile x 512-k slice) and CTAs per thread-block cluster (> 1: each
  * tile is shared by the CTAs of one cluster, whose first CTA adds the others' slice partials in order

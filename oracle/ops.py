@@ -181,6 +181,16 @@ def gdn_fused(win, conv_w, a, b, A_log, dt_bias, state, Hk, Hv, Dk, Dv, KC, snap
     return y, so, sm
 
 
+def swiglu(gu, I):
+    """C qo_swiglu (mlx-lm SwiGLU with the bf16 formulas of gdn_fused.py:22-41): gu bf16 [S, >=2I] =
+    [gate | up] -> bf16(silu(gate) * up) [S, I]."""
+    gu = np.ascontiguousarray(gu, np.uint16)
+    S = gu.shape[0]
+    out = np.empty((S, I), np.uint16)
+    lib().qo_swiglu(_p(gu), _I(gu.shape[1]), _I(S), _I(I), _p(out))
+    return out
+
+
 def gdn_norm_gate(y, z, w, eps):
     """C qo_gdn_norm_gate (gdn_fused.py:114-129): y fp32 [S, H, Dv], z bf16 [S, H*Dv] -> bf16 [S, H*Dv]."""
     y = np.ascontiguousarray(y, np.float32)

@@ -110,9 +110,15 @@ struct Params {
   unsigned* err;
   int ldy, N, K, NSL, R, ntiles;  // ntiles * (gridDim.x + 1) and ntiles * NSL < 2^31 (host-checked)
   int cs;             // cluster mode (> 1): CTAs per tile, one tile per cluster
-  const uint16_t* nw; // non-null: the activation is RMSNorm(x rows) with this weight [K] (prologue)
+  // activation prologue (template parameter PRO): kProRms: x = RMSNorm(x rows; nw, eps); kProSwiglu:
+  // x = silu(g) * u with g = x[:, k] and u = x[:, K + k]; kProGated: x = bf16(RMSNorm_head(y; nw, eps)
+  // * silu(z)), y fp32 rows at x (ldx in floats), z bf16 rows [ldz], heads of 128.
+  const uint16_t* nw;
   float eps;
+  const uint16_t* z;
+  long long ldz;
 };
+enum : int { kProNone = 0, kProRms = 1, kProSwiglu = 2, kProGated = 3 };
 
 // (tile, slice) of consecutive units, advanced without divisions.
 struct UnitCursor {
@@ -209,6 +215,52 @@ __device__ __forceinline__ uint4 rms_apply(uint4 xv, uint4 wv, float r) {
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// 8 SwiGLU activations: bf16(silu(g) * u) element by element (the decoder's swiglu_kernel).
+__device__ __forceinline__ uint4 swiglu_apply(uint4 gv, uint4 uv) {
+  const uint32_t gs[4] = {gv.x, gv.y, gv.z, gv.w}, us[4] = {uv.x, uv.y, uv.z, uv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const uint32_t lo = f2bf(__fmul_rn(silu_bf(bflo(gs[h])), bflo(us[h])));
+    const uint32_t hi = f2bf(__fmul_rn(silu_bf(bfhi(gs[h])), bfhi(us[h])));
+    o[h] = lo | (hi << 16);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+// 8 gated-norm activations of one head of 128 (gdn_norm_gate_kernel): this task holds elements
+// [8i, 8i + 8) of the head, i = lane % 16, so the head's 16 tasks are 16 lanes of one warp.  The sum of
+// squares is that kernel's: per 4 elements a sequential fma chain (norm lane 2i and 2i + 1), then the
+// xor butterfly over the 32 chains -- done here on the pairs (lane xor 8, 4, 2, 1, then the pair).
+// Every lane of the warp must call it.
+__device__ __forceinline__ uint4 gated_apply(float4 y0, float4 y1, uint4 zv, uint4 wv, float eps) {
+  float a = 0.0f, b = 0.0f;
+  a = __fmaf_rn(y0.x, y0.x, a);
+  a = __fmaf_rn(y0.y, y0.y, a);
+  a = __fmaf_rn(y0.z, y0.z, a);
+  a = __fmaf_rn(y0.w, y0.w, a);
+  b = __fmaf_rn(y1.x, y1.x, b);
+  b = __fmaf_rn(y1.y, y1.y, b);
+  b = __fmaf_rn(y1.z, y1.z, b);
+  b = __fmaf_rn(y1.w, y1.w, b);
+#pragma unroll
+  for (int d = 8; d >= 1; d >>= 1) {
+    a = __fadd_rn(a, __shfl_xor_sync(0xFFFFFFFFu, a, d));
+    b = __fadd_rn(b, __shfl_xor_sync(0xFFFFFFFFu, b, d));
+  }
+  const float r = rsqrt_rn(__fadd_rn(__fmul_rn(__fadd_rn(a, b), 1.0f / 128.0f), eps));
+  const float yv[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+  const uint32_t zs[4] = {zv.x, zv.y, zv.z, zv.w}, ws[4] = {wv.x, wv.y, wv.z, wv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const float xl = R(__fmul_rn(bflo(ws[h]), R(__fmul_rn(yv[2 * h], r))));
+    const float xh = R(__fmul_rn(bfhi(ws[h]), R(__fmul_rn(yv[2 * h + 1], r))));
+    o[h] = uint32_t(f2bf(__fmul_rn(xl, silu_f32(bflo(zs[h]))))) |
+           (uint32_t(f2bf(__fmul_rn(xh, silu_f32(bfhi(zs[h]))))) << 16);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // One activation task: 8 consecutive x of token m in group g (lane li of the group's 8 lanes) ->
 // their three byte limbs in the B image of the slot (rows 3m..3m+2, permuted k: the even k of the
 // 8 then the odd k, as the nibble unpacking orders the weights) and, from lane 0 of the group, the
@@ -277,9 +329,9 @@ __device__ __forceinline__ void prep_task(uint4 v, int m, int g, int li, uint8_t
 //          are in flight meanwhile);
 //   2      in stream mode (more than 8 slices and units), builds the later slices one unit at a time;
 //   4-7    chain-0 workers, 8-11 chain-1 workers: warp w serves TMEM lane quarter w % 4, thread = row.
-// NORM: the activation is RMSNorm(x rows) (p.nw), computed in the prologue (a separate instantiation
-// keeps the plain kernel's code small).
-template <int MT, bool NORM>
+// PRO: the activation prologue (kProNone, kProRms, kProSwiglu, kProGated; a separate instantiation
+// per prologue keeps each kernel's code small).
+template <int MT, int PRO>
 __global__ void __launch_bounds__(kThreads, 1)
     qmv_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
                   const __grid_constant__ CUtensorMap tb, const __grid_constant__ Params p) {
@@ -443,31 +495,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int sl = sbase + jb < NSL ? sbase + jb : sbase + jb - NSL;
       return sl * 512 + ((r >> 3) & 7) * 64 + (r & 7) * 8;
     };
+    // a task's inputs: x (or y's first 4 / g), and per prologue the RMSNorm weights, u, or y's last 4,
+    // z and the gated-norm weights
+    struct In {
+      uint4 a, b, c, d;
+    };
     auto load = [&](int t) {
       const int m = (t % per_slot) >> 6;
-      return *reinterpret_cast<const uint4*>(p.x + (size_t)m * (size_t)p.ldx + kof(t));
+      const int k = kof(t);
+      In in;
+      if (PRO == kProGated) {
+        const float* yr = reinterpret_cast<const float*>(p.x) + (size_t)m * (size_t)p.ldx + k;
+        in.a = *reinterpret_cast<const uint4*>(yr);
+        in.b = *reinterpret_cast<const uint4*>(yr + 4);
+        in.c = *reinterpret_cast<const uint4*>(p.z + (size_t)m * (size_t)p.ldz + k);
+        in.d = *reinterpret_cast<const uint4*>(p.nw + (k & 127));
+      } else {
+        in.a = *reinterpret_cast<const uint4*>(p.x + (size_t)m * (size_t)p.ldx + k);
+        if (PRO == kProRms) in.b = *reinterpret_cast<const uint4*>(p.nw + k);
+        if (PRO == kProSwiglu) in.b = *reinterpret_cast<const uint4*>(p.x + (size_t)m * (size_t)p.ldx + p.K + k);
+      }
+      return in;
     };
-    // the RMSNorm weights of a task's 8 elements (prologue mode), fetched with its x
-    auto loadw = [&](int t) { return NORM ? *reinterpret_cast<const uint4*>(p.nw + kof(t)) : make_uint4(0u, 0u, 0u, 0u); };
-    uint4 va = make_uint4(0u, 0u, 0u, 0u), vb = va, wa = va, wb = va;
-    if (me < total) { va = load(me); wa = loadw(me); }
-    if (me + nthr < total) { vb = load(me + nthr); wb = loadw(me + nthr); }
-    if (NORM && reduce) reduce_rows(me);
+    In va{}, vb{};
+    if (me < total) va = load(me);
+    if (me + nthr < total) vb = load(me + nthr);
+    if (PRO == kProRms && reduce) reduce_rows(me);
     int cur_slot = -1;  // slot of this warp's open batch run (its bfull arrivals are owed)
     int batches = 0;
 #pragma unroll 1
     for (int t = me; t < total; t += nthr) {  // warp-uniform: total and nthr are multiples of 32
-      uint4 v = va;
-      const uint4 wv = wa;
+      const In in = va;
       va = vb;
-      wa = wb;
-      if (t + 2 * nthr < total) {
-        vb = load(t + 2 * nthr);
-        wb = loadw(t + 2 * nthr);
-      }
+      if (t + 2 * nthr < total) vb = load(t + 2 * nthr);
       {
         const int jb = t / per_slot, r = t - jb * per_slot;
-        if (NORM) v = rms_apply(v, wv, rn[r >> 6]);
+        uint4 v = in.a;
+        if (PRO == kProRms) v = rms_apply(in.a, in.b, rn[r >> 6]);
+        if (PRO == kProSwiglu) v = swiglu_apply(in.a, in.b);
+        if (PRO == kProGated)
+          v = gated_apply(make_float4(__uint_as_float(in.a.x), __uint_as_float(in.a.y), __uint_as_float(in.a.z),
+                                      __uint_as_float(in.a.w)),
+                          make_float4(__uint_as_float(in.b.x), __uint_as_float(in.b.y), __uint_as_float(in.b.z),
+                                      __uint_as_float(in.b.w)),
+                          in.c, in.d, p.eps);
         const int slot = slot_of(j0 + jb, sbase + jb < NSL ? sbase + jb : sbase + jb - NSL);
         if (slot != cur_slot && cur_slot >= 0) {
           fence_proxy_async();
@@ -862,28 +933,34 @@ static bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const v
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int MT, bool NORM>
+template <int MT, int PRO>
 static bool prepare() {
   static std::once_flag once;
   static bool ok = false;
   std::call_once(once, [&] {
-    ok = cudaFuncSetAttribute(qmv_tc_kernel<MT, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
+    ok = cudaFuncSetAttribute(qmv_tc_kernel<MT, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
          cudaSuccess;
   });
   return ok;
 }
 
-template <int MT>
-static int launch_mt(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb, const Params& p, int G,
-                     cudaStream_t st) {
-  if (p.nw) {
-    if (!prepare<MT, true>()) return QMTP_ERR_CUDA;
-    launch_kernel_cluster(qmv_tc_kernel<MT, true>, dim3(G), dim3(kThreads), kSmem, st, p.cs, tw, ts, tb, p);
-  } else {
-    if (!prepare<MT, false>()) return QMTP_ERR_CUDA;
-    launch_kernel_cluster(qmv_tc_kernel<MT, false>, dim3(G), dim3(kThreads), kSmem, st, p.cs, tw, ts, tb, p);
-  }
+template <int MT, int PRO>
+static int launch_pro(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb, const Params& p, int G,
+                      cudaStream_t st) {
+  if (!prepare<MT, PRO>()) return QMTP_ERR_CUDA;
+  launch_kernel_cluster(qmv_tc_kernel<MT, PRO>, dim3(G), dim3(kThreads), kSmem, st, p.cs, tw, ts, tb, p);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+template <int MT>
+static int launch_mt(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb, const Params& p, int pro,
+                     int G, cudaStream_t st) {
+  switch (pro) {
+    case kProRms: return launch_pro<MT, kProRms>(tw, ts, tb, p, G, st);
+    case kProSwiglu: return launch_pro<MT, kProSwiglu>(tw, ts, tb, p, G, st);
+    case kProGated: return launch_pro<MT, kProGated>(tw, ts, tb, p, G, st);
+    default: return launch_pro<MT, kProNone>(tw, ts, tb, p, G, st);
+  }
 }
 
 static int max_clusters(int cs) {
@@ -895,7 +972,7 @@ static int max_clusters(int cs) {
   int& c = cache[cs == 4 ? 1 : 0][dev];
   if (c == 0) {
     int n = 0;
-    if (prepare<1, false>()) {
+    if (prepare<1, kProNone>()) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(unsigned(cs));
       cfg.blockDim = dim3(kThreads);
@@ -907,7 +984,7 @@ static int max_clusters(int cs) {
       at[0].val.clusterDim.z = 1;
       cfg.attrs = at;
       cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&n, qmv_tc_kernel<1, false>, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, qmv_tc_kernel<1, kProNone>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         n = 0;
       }
@@ -920,16 +997,42 @@ static int max_clusters(int cs) {
 }  // namespace tq
 
 // All affine qmv entry points land here.
+// Activation prologue of a call: pro (tq::kPro*), the norm weight and eps, the gate rows (kProGated).
+struct QmvPro {
+  int pro;
+  const void* nw;
+  float eps;
+  const void* z;
+  long long ldz;
+};
+
 int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const void* b, void* y, const void* res,
-           int M, int N, int K, int ldy, void* stream, const void* norm_w, float eps) {
+           int M, int N, int K, int ldy, void* stream, const QmvPro& pr) {
   using namespace tq;
   if (!x || !w || !s || !b || !y) return QMTP_ERR_ARG;
   if (M < 1 || N < 1 || K < 512 || K % 512 != 0 || ldy < N) return QMTP_ERR_SHAPE;
-  if (ldx == 0) ldx = K;
-  if (ldx < K || ldx % 8) return QMTP_ERR_SHAPE;
+  if (ldx == 0) ldx = pr.pro == kProSwiglu ? 2LL * K : K;
   if (!aligned16(x) || !aligned16(w) || !aligned16(s) || !aligned16(b)) return QMTP_ERR_ALIGN;
-  if (norm_w && (K % 1024 != 0 || K > 32768)) return QMTP_ERR_SHAPE;
-  if (norm_w && !aligned16(norm_w)) return QMTP_ERR_ALIGN;
+  switch (pr.pro) {
+    case kProNone:
+      if (ldx < K || ldx % 8) return QMTP_ERR_SHAPE;
+      break;
+    case kProRms:
+      if (ldx < K || ldx % 8 || K % 1024 != 0 || K > 32768) return QMTP_ERR_SHAPE;
+      if (!pr.nw) return QMTP_ERR_ARG;
+      if (!aligned16(pr.nw)) return QMTP_ERR_ALIGN;
+      break;
+    case kProSwiglu:
+      if (ldx < 2LL * K || ldx % 8) return QMTP_ERR_SHAPE;
+      break;
+    case kProGated:  // x: fp32 rows, ldx in floats; heads of 128
+      if (ldx < K || ldx % 4 || pr.ldz < K || pr.ldz % 8) return QMTP_ERR_SHAPE;
+      if (!pr.nw || !pr.z) return QMTP_ERR_ARG;
+      if (!aligned16(pr.nw) || !aligned16(pr.z)) return QMTP_ERR_ALIGN;
+      break;
+    default:
+      return QMTP_ERR_ARG;
+  }
   const Plan pl = make_plan(N, K, sm_count());
   if ((long long)pl.ntiles * (pl.G + 1) > kMaxUnitProduct || (long long)pl.ntiles * pl.NSL > kMaxUnitProduct)
     return QMTP_ERR_SHAPE;
@@ -947,21 +1050,25 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
   p.R = pl.R;
   p.ntiles = pl.ntiles;
   p.cs = pl.cs;
-  p.nw = static_cast<const uint16_t*>(norm_w);
-  p.eps = eps;
+  p.nw = static_cast<const uint16_t*>(pr.nw);
+  p.eps = pr.eps;
+  p.ldz = pr.ldz;
   p.err = device_error_ptr();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int m0 = 0; m0 < M; m0 += kMaxTok) {
     const int mm = std::min(kMaxTok, M - m0);
-    p.x = static_cast<const uint16_t*>(x) + (size_t)m0 * (size_t)ldx;
+    p.x = pr.pro == kProGated
+              ? reinterpret_cast<const uint16_t*>(static_cast<const float*>(x) + (size_t)m0 * (size_t)ldx)
+              : static_cast<const uint16_t*>(x) + (size_t)m0 * (size_t)ldx;
+    p.z = pr.z ? static_cast<const uint16_t*>(pr.z) + (size_t)m0 * (size_t)pr.ldz : nullptr;
     p.y = static_cast<uint16_t*>(y) + (size_t)m0 * (size_t)ldy;
     p.res = res ? static_cast<const uint16_t*>(res) + (size_t)m0 * (size_t)ldy : nullptr;
     int rc;
     switch (mm) {
-      case 1: rc = launch_mt<1>(tw, ts, tb, p, pl.G, st); break;
-      case 2: rc = launch_mt<2>(tw, ts, tb, p, pl.G, st); break;
-      case 3: rc = launch_mt<3>(tw, ts, tb, p, pl.G, st); break;
-      default: rc = launch_mt<4>(tw, ts, tb, p, pl.G, st); break;
+      case 1: rc = launch_mt<1>(tw, ts, tb, p, pr.pro, pl.G, st); break;
+      case 2: rc = launch_mt<2>(tw, ts, tb, p, pr.pro, pl.G, st); break;
+      case 3: rc = launch_mt<3>(tw, ts, tb, p, pr.pro, pl.G, st); break;
+      default: rc = launch_mt<4>(tw, ts, tb, p, pr.pro, pl.G, st); break;
     }
     if (rc != QMTP_OK) return rc;
   }
@@ -983,13 +1090,13 @@ using namespace qmtp;
 
 extern "C" int qmtp_qmv_affine_g64(const void* x, const void* w, const void* scales, const void* biases, void* y,
                                    int M, int N, int K, int ldy, void* stream) {
-  return qmv_tc(x, 0, w, scales, biases, y, nullptr, M, N, K, ldy, stream, nullptr, 0.0f);
+  return qmv_tc(x, 0, w, scales, biases, y, nullptr, M, N, K, ldy, stream, QmvPro{tq::kProNone, nullptr, 0.0f, nullptr, 0});
 }
 
 extern "C" int qmtp_qmv_affine_g64_res(const void* x, const void* w, const void* scales, const void* biases, void* y,
                                        const void* res, int M, int N, int K, int ldy, void* stream) {
   if (!res) return QMTP_ERR_ARG;
-  return qmv_tc(x, 0, w, scales, biases, y, res, M, N, K, ldy, stream, nullptr, 0.0f);
+  return qmv_tc(x, 0, w, scales, biases, y, res, M, N, K, ldy, stream, QmvPro{tq::kProNone, nullptr, 0.0f, nullptr, 0});
 }
 
 // The workspace of the _split / _norm entry points is no longer used: a tile shared between CTAs is
@@ -1005,7 +1112,7 @@ extern "C" int qmtp_qmv_affine_g64_split(const void* x, long long ldx, const voi
                                          void* workspace, size_t ws_bytes, void* stream) {
   (void)workspace;
   (void)ws_bytes;
-  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, stream, nullptr, 0.0f);
+  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, stream, QmvPro{tq::kProNone, nullptr, 0.0f, nullptr, 0});
 }
 
 extern "C" int qmtp_qmv_affine_g64_norm(const void* x, long long ldx, const void* norm_w, float eps, const void* w,
@@ -1014,7 +1121,22 @@ extern "C" int qmtp_qmv_affine_g64_norm(const void* x, long long ldx, const void
   (void)workspace;
   (void)ws_bytes;
   if (!norm_w) return QMTP_ERR_ARG;
-  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, stream, norm_w, eps);
+  return qmv_tc(x, ldx, w, scales, biases, y, res, M, N, K, ldy, stream, QmvPro{tq::kProRms, norm_w, eps, nullptr, 0});
+}
+
+extern "C" int qmtp_qmv_affine_g64_swiglu(const void* gu, long long ldgu, const void* w, const void* scales,
+                                          const void* biases, void* y, const void* res, int M, int N, int K, int ldy,
+                                          void* stream) {
+  return qmv_tc(gu, ldgu, w, scales, biases, y, res, M, N, K, ldy, stream,
+                QmvPro{tq::kProSwiglu, nullptr, 0.0f, nullptr, 0});
+}
+
+extern "C" int qmtp_qmv_affine_g64_gated(const float* yg, long long ldyg, const void* z, long long ldz,
+                                         const void* norm_w, float eps, const void* w, const void* scales,
+                                         const void* biases, void* y, const void* res, int M, int N, int K, int ldy,
+                                         void* stream) {
+  return qmv_tc(yg, ldyg, w, scales, biases, y, res, M, N, K, ldy, stream,
+                QmvPro{tq::kProGated, norm_w, eps, z, ldz});
 }
 
 extern "C" int qmtp_qmv_set_mode(int mode) {

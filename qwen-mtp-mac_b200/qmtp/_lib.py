@@ -40,6 +40,9 @@ SIGNATURES: dict[str, list] = {
                                   _P],
     "qmtp_qmv_plan": [_I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)],
     "qmtp_qmv_set_mode": [_I],
+    "qmtp_qmv_affine_g64_swiglu": [_P, ctypes.c_longlong, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "qmtp_qmv_affine_g64_gated": [_P, ctypes.c_longlong, _P, ctypes.c_longlong, _P, ctypes.c_float, _P, _P, _P, _P, _P,
+                                  _I, _I, _I, _I, _P],
     "qmtp_qmv_affine_g64_norm": [_P, ctypes.c_longlong, _P, ctypes.c_float, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P,
                                  ctypes.c_size_t, _P],
 }

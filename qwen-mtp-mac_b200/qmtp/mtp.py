@@ -148,19 +148,32 @@ class MTPDecoder:
                                    a.hidden, out.data_ptr(), a.hidden, self._st())
         self._chk(rc, "embed")
 
-    def _qmv(self, x, lin, y, M, res=None, ldy=None, norm=None):
+    def _qmv(self, x, lin, y, M, res=None, ldy=None, norm=None, swiglu=False, gated=None):
         """4-bit GEMV y = x . W^T (+ res): affine layers on the tensor-core kernel with split tiles
         (qmtp_qmv_affine_g64_split, one launch per 4 rows; shared tiles finished inside a cluster), NVFP4 layers (an NVFP4 checkpoint) on
         qmtp_qmv_nvfp4_g16_res.  norm (an RMSNorm weight): x is RMS-normalised first -- inside the
-        affine kernel (qmtp_qmv_affine_g64_norm), or by qmtp_rmsnorm into self.xn for NVFP4."""
+        affine kernel (qmtp_qmv_affine_g64_norm), or by qmtp_rmsnorm into self.xn for NVFP4.
+        swiglu: x is [gate | up] and the projection's input is silu(gate) * up (qmtp_qmv_affine_g64_swiglu;
+        NVFP4: qmtp_swiglu into self.act first).  gated = (z pointer, z row stride, norm weight): x is the
+        GatedDeltaNet core output (fp32) and the input is its gated norm (qmtp_qmv_affine_g64_gated;
+        NVFP4: qmtp_gdn_norm_gate into self.gdn_out first)."""
         N, K = lin.out_features, lin.in_features
         ldy = ldy or N
         nv = lin.mode == "nvfp4"
         if norm is not None and nv:
             self._norm(x, norm, self.xn, M)
             x, norm = self.xn, None
+        if swiglu and nv:
+            self._chk(self.L.qmtp_swiglu(x.data_ptr(), 2 * K, M, K, self.act.data_ptr(), self._st()), "swiglu")
+            x, swiglu = self.act, False
+        if gated is not None and nv:
+            a = self.a
+            self._chk(self.L.qmtp_gdn_norm_gate(x.data_ptr(), gated[0], gated[1], gated[2].data_ptr(),
+                                                self.gdn_out.data_ptr(), K, M, a.lin_hv, a.lin_dv, a.eps,
+                                                self._st()), "norm_gate")
+            x, gated = self.gdn_out, None
         if self.qmv_log is not None:
-            self.qmv_log.append((x, lin, y, M, res, ldy, norm))
+            self.qmv_log.append((x, lin, y, M, res, ldy, norm, swiglu, gated))
         self.launches += (M + 3) // 4
         if self.prof is not None:
             e0 = torch.cuda.Event(enable_timing=True)
@@ -169,6 +182,17 @@ class MTPDecoder:
             self._chk(self.L.qmtp_qmv_nvfp4_g16_res(x.data_ptr(), lin.weight.data_ptr(), lin.scales.data_ptr(),
                                                     y.data_ptr(), res.data_ptr() if res is not None else None,
                                                     M, N, K, ldy, self._st()), "qmv")
+        elif swiglu:
+            self._chk(self.L.qmtp_qmv_affine_g64_swiglu(x.data_ptr(), 2 * K, lin.weight.data_ptr(), lin.scales.data_ptr(),
+                                                        lin.biases.data_ptr(), y.data_ptr(),
+                                                        res.data_ptr() if res is not None else None, M, N, K, ldy,
+                                                        self._st()), "qmv")
+        elif gated is not None:
+            self._chk(self.L.qmtp_qmv_affine_g64_gated(x.data_ptr(), K, gated[0], gated[1], gated[2].data_ptr(),
+                                                       self.a.eps, lin.weight.data_ptr(), lin.scales.data_ptr(),
+                                                       lin.biases.data_ptr(), y.data_ptr(),
+                                                       res.data_ptr() if res is not None else None, M, N, K, ldy,
+                                                       self._st()), "qmv")
         elif norm is not None:
             self._chk(self.L.qmtp_qmv_affine_g64_norm(x.data_ptr(), K, norm.data_ptr(), self.a.eps, lin.weight.data_ptr(),
                                                       lin.scales.data_ptr(), lin.biases.data_ptr(), y.data_ptr(),
@@ -207,9 +231,9 @@ class MTPDecoder:
     # ------------------------------------------------------------------ layers
     def _attn_layer(self, L, x, rows, kc, vc, pos_slot):
         """Gated attention block: x (pre-norm residual stream, [rows, H]) += o_proj(attn(...)); the
-        projection input is input_ln(x), normalised inside the projection."""
+        projection input is the normalised rows in self.xn."""
         a = self.a
-        self._qmv(x, L["qkv_proj"], self.proj, rows, ldy=self.proj.shape[1], norm=L["input_ln"])
+        self._qmv(self.xn, L["qkv_proj"], self.proj, rows, ldy=self.proj.shape[1])
         self._chk(self.L.qmtp_attn_prep(self.proj.data_ptr(), self.proj.shape[1], rows, a.n_heads, a.n_kv,
                                         a.head_dim, a.rotary_dim, L["q_norm"].data_ptr(), L["k_norm"].data_ptr(),
                                         a.eps, self.cos.data_ptr(), self.sin.data_ptr(), self._cp(pos_slot), 0,
@@ -222,6 +246,8 @@ class MTPDecoder:
 
     def _mlp(self, L, x, rows):
         a = self.a
+        # post_ln inside gate_up's prologue; the SwiGLU as its own launch (in the graph it overlaps the down
+        # projection's prologue; computing it in every CTA of the projection measured 7 us slower)
         self._qmv(x, L["gate_up"], self.gu, rows, norm=L["post_ln"])
         self._chk(self.L.qmtp_swiglu(self.gu.data_ptr(), 2 * a.intermediate, rows, a.intermediate,
                                      self.act.data_ptr(), self._st()), "swiglu")
@@ -233,8 +259,11 @@ class MTPDecoder:
         self._embed(self.tokens_in.data_ptr(), S, self.h)
         for i in range(a.layers):
             L = W[f"layers.{i}"]
+            # input_ln as its own launch: for the 12352- and 10240-row projections it overlaps the
+            # projection's prologue better than the RMSNorm prologue (0.5-0.8 us per layer)
+            self._norm(self.h, L["input_ln"], self.xn, S)
             if a.is_linear(i):
-                self._qmv(self.h, L["in_proj"], self.proj, S, ldy=self.proj.shape[1], norm=L["input_ln"])
+                self._qmv(self.xn, L["in_proj"], self.proj, S, ldy=self.proj.shape[1])
                 self._chk(self.L.qmtp_gdn_fused_ex(ctypes.byref(self._gdn_args[i]), self._st()), "gdn")
                 Z = a.lin_hv * a.lin_dv
                 self._chk(self.L.qmtp_gdn_norm_gate(self.ygdn.data_ptr(), self.proj.data_ptr() + 2 * a.conv_dim,
@@ -270,6 +299,7 @@ class MTPDecoder:
                                       self.mcat.data_ptr() + 2 * H, 2 * H, rows, H, self._st()), "rmsnorm")
         self._qmv(self.mcat, M["fc"], self.mx, rows)
         Ly = M["layer"]
+        self._norm(self.mx, Ly["input_ln"], self.xn, rows)
         self._attn_layer(Ly, self.mx, rows, self.mkv[0], self.mkv[1], C["MPOS"])
         self._mlp(Ly, self.mx, rows)
         if not with_draft:

@@ -41,6 +41,40 @@ def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "
     return wq, sc, bi
 
 
+def qmv_affine_swiglu(gu: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                      out: torch.Tensor | None = None, res: torch.Tensor | None = None) -> torch.Tensor:
+    """y = (silu(gate) * up) @ dequant(w).T with gu = [gate | up] bf16 [M, 2K] (the MLP's down
+    projection with its SwiGLU computed in the kernel's prologue)."""
+    M, K2 = gu.shape
+    K, N = K2 // 2, w.shape[0]
+    _lib.require_cuda(gu, w, scales, biases, res)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=gu.device)
+    _lib.check(_lib.lib().qmtp_qmv_affine_g64_swiglu(gu.data_ptr(), gu.stride(0), w.data_ptr(), scales.data_ptr(),
+                                                      biases.data_ptr(), out.data_ptr(), _lib.ptr(res), M, N, K,
+                                                      out.shape[-1], _lib.stream()), "qmv_affine_swiglu")
+    return out
+
+
+def qmv_affine_gated(yg: torch.Tensor, z: torch.Tensor, norm_w: torch.Tensor, eps: float, w: torch.Tensor,
+                     scales: torch.Tensor, biases: torch.Tensor, out: torch.Tensor | None = None,
+                     res: torch.Tensor | None = None) -> torch.Tensor:
+    """y = bf16(RMSNorm_head(yg) * silu(z)) @ dequant(w).T over heads of 128 (the GatedDeltaNet output
+    gate computed in the out-projection's prologue); yg fp32 [M, K], z bf16 [M, >=K] (row stride any)."""
+    M, K = yg.shape
+    N = w.shape[0]
+    _lib.require_cuda(yg, norm_w, w, scales, biases, res)
+    if not z.is_cuda or z.stride(-1) != 1 or z.dtype != torch.bfloat16:
+        raise ValueError("z must be a bf16 CUDA tensor with unit stride along its rows")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=yg.device)
+    _lib.check(_lib.lib().qmtp_qmv_affine_g64_gated(yg.data_ptr(), yg.stride(0), z.data_ptr(), z.stride(0),
+                                                     norm_w.data_ptr(), float(eps), w.data_ptr(), scales.data_ptr(),
+                                                     biases.data_ptr(), out.data_ptr(), _lib.ptr(res), M, N, K,
+                                                     out.shape[-1], _lib.stream()), "qmv_affine_gated")
+    return out
+
+
 def qmv_affine(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                group_size: int = 64, out: torch.Tensor | None = None, res: torch.Tensor | None = None,
                ws: torch.Tensor | None = None, split: bool = True, norm=None) -> torch.Tensor:

@@ -265,3 +265,58 @@ def test_qmv_affine_norm_prologue(K, M, dev, planner):
             assert np.array_equal(to_np(out), ref_res), (N, mode, split, "res")
         if M == 4:
             assert np.isnan(ops.bf16_to_f32(ref[3])).all()
+
+
+@pytest.mark.parametrize("K", [4096, 12288])
+@pytest.mark.parametrize("M", [1, 3, 4])
+def test_qmv_affine_swiglu_prologue(K, M, dev, planner):
+    """The SwiGLU prologue (qmtp_qmv_affine_g64_swiglu) gives the bits of the oracle's swiglu followed by
+    its qmv, in every planner mode, with a residual; gate values over a wide range."""
+    from qmtp import qmv_kernel
+
+    r = np.random.default_rng(K + 7 * M)
+    for N in (37, 4096):
+        _, wq, s, b = affine_layer(N, K, seed=N + K + 1)
+        gu = ops.f32_to_bf16((r.standard_normal((M, 2 * K)) * np.exp(r.uniform(-4, 3, (M, 2 * K)))).astype(np.float32))
+        res = randn_bf16((M, N), 19)
+        x = ops.swiglu(gu, K)
+        ref = ops.qmv_affine(x, wq, s, b)
+        ref_res = ops.f32_to_bf16(ops.bf16_to_f32(res) + ops.bf16_to_f32(ref))
+        gt, wt, st, bt = (to_torch(a, dev) for a in (gu, wq, s, b))
+        for mode in (0, 1, 2):
+            planner(mode)
+            assert np.array_equal(to_np(qmv_kernel.qmv_affine_swiglu(gt, wt, st, bt)), ref), (N, mode)
+            out = to_torch(res, dev)
+            qmv_kernel.qmv_affine_swiglu(gt, wt, st, bt, out=out, res=out)
+            assert np.array_equal(to_np(out), ref_res), (N, mode, "res")
+
+
+@pytest.mark.parametrize("M", [1, 3, 4])
+def test_qmv_affine_gated_prologue(M, dev, planner):
+    """The GatedDeltaNet output gate in the out-projection's prologue (qmtp_qmv_affine_g64_gated) gives
+    the bits of the oracle's gdn_norm_gate followed by its qmv (32 heads of 128, K = 4096), with the
+    gate rows strided like the decoder's in_proj output, in every planner mode, with a residual."""
+    from qmtp import qmv_kernel
+
+    r = np.random.default_rng(100 + M)
+    H, Dv, N = 32, 128, 4096
+    K = H * Dv
+    _, wq, s, b = affine_layer(N, K, seed=77)
+    y = ops.bf16_to_f32(ops.f32_to_bf16((r.standard_normal((M, H, Dv)) * 0.3).astype(np.float32)))
+    y[0, 5] *= np.float32(2.0 ** -30)  # a nearly silent head
+    zfull = randn_bf16((M, 2 * K + 64), 23)  # the gate sits inside a wider row, as in the decoder
+    z = np.ascontiguousarray(zfull[:, 64:64 + K])
+    nw = ops.f32_to_bf16((1.0 + 0.2 * r.standard_normal(Dv)).astype(np.float32))
+    res = randn_bf16((M, N), 29)
+    x = ops.gdn_norm_gate(y, z, nw, 1e-6)
+    ref = ops.qmv_affine(x, wq, s, b)
+    ref_res = ops.f32_to_bf16(ops.bf16_to_f32(res) + ops.bf16_to_f32(ref))
+    yt = torch.from_numpy(y.reshape(M, K).copy()).to(dev)
+    zt = to_torch(zfull, dev)[:, 64:64 + K]
+    wt, st, bt, nt = (to_torch(a, dev) for a in (wq, s, b, nw))
+    for mode in (0, 1, 2):
+        planner(mode)
+        assert np.array_equal(to_np(qmv_kernel.qmv_affine_gated(yt, zt, nt, 1e-6, wt, st, bt)), ref), mode
+        out = to_torch(res, dev)
+        qmv_kernel.qmv_affine_gated(yt, zt, nt, 1e-6, wt, st, bt, out=out, res=out)
+        assert np.array_equal(to_np(out), ref_res), (mode, "res")
