@@ -215,7 +215,7 @@ int qmtp_gdn_norm_gate(const float* y, const void* z, int ld_z, const void* w, v
  *   h bf16 [M, K]; wq/scales/biases: affine g64 coarse head [V, K]; w_fine bf16 [V, K];
  *   -> out_idx int32 [M, k] (candidates in that order), out_fine bf16 [M, k] (exact logits),
  *      out_argmax int32 [M] (may be NULL), coarse_out bf16 [M, V] (may be NULL).
- *   workspace: qmtp_lmhead2_workspace(M, V, k) bytes, 16-B aligned.  k <= 256, K % 512 == 0. */
+ *   workspace: qmtp_lmhead2_workspace(M, V, k) bytes, 16-B aligned.  k <= 2048 (above 256 the selection is a radix select and the rescoring runs across the SMs), K % 512 == 0. */
 size_t qmtp_lmhead2_workspace(int M, int V, int k);
 int qmtp_lmhead2(const void* h, const void* wq, const void* scales, const void* biases,
                  const void* w_fine, int M, int V, int K, int k, int* out_idx, void* out_fine,
@@ -420,7 +420,7 @@ typedef struct {
 } qmtp_sampling;
 
 /* Exact speculative sampling over the two-stage head's candidates (engine.py:91-152: Engine._dist,
- * _sample_first, _verify).  idx int32 / fine bf16 [rows, ld]: K <= 256 candidates per row (vocabulary
+ * _sample_first, _verify).  idx int32 / fine bf16 [rows, ld]: K <= 2048 candidates per row (vocabulary
  * ids and exact logits, as qmtp_topk_rescore writes them).
  *   first_row < 0 (verify): drafts[0..k); draft i is accepted with probability p_i(d_i), else a token
  *     is drawn from p_i without d_i and the cycle stops; all accepted -> a bonus draw from row k.

@@ -231,6 +231,132 @@ __global__ void argmax_final_kernel(const uint64_t* __restrict__ part, int G, in
   if (lane == 0) out[m] = int32_t(cand_idx(best));
 }
 
+// ---- large candidate sets (k > 256, up to 2048: lm_head2.py:32-36 k_for with top_k up to 512)
+// topk_select: per row, the k largest of the G*k candidate words (all distinct: the index is part of
+// the word) by a most-significant-digit radix select over the six bytes that vary (the 16-bit key,
+// then the index), then the k words compacted and bitonic-sorted in shared memory.  The same total
+// order as topk_merge, so the same k candidates in the same order.
+constexpr int kSelectThreads = 1024;
+constexpr int kSelectMaxK = 2048;
+__global__ void __launch_bounds__(kSelectThreads)
+topk_select_kernel(const uint64_t* __restrict__ cand, int n, int k, int32_t* __restrict__ out_idx,
+                   uint64_t* __restrict__ sel_words, uint32_t idx_base, uint64_t* __restrict__ out_words) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ int hist[256];
+  __shared__ int s_res[4];
+  __shared__ int s_cnt;
+  __shared__ uint64_t s[kSelectMaxK];
+  const int m = blockIdx.x, tid = threadIdx.x;
+  const uint64_t* row = cand + (long long)m * n;
+  uint64_t prefix = 0, pmask = 0;
+  int need = k;
+  const int shifts[6] = {40, 32, 24, 16, 8, 0};
+  for (int pass = 0; pass < 6; ++pass) {
+    const int sh = shifts[pass];
+    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += blockDim.x) {
+      const uint64_t w = row[i];
+      if ((w & pmask) == prefix) atomicAdd(&hist[int((w >> sh) & 255u)], 1);
+    }
+    __syncthreads();
+    if (tid < 32) find_bin(hist, need, 0, s_res);
+    __syncthreads();
+    const int b = s_res[0];
+    need -= s_res[1];
+    prefix |= uint64_t(b) << sh;
+    pmask |= uint64_t(255) << sh;
+    __syncthreads();
+  }
+  // prefix is now the k-th largest word (the top two bytes of every word are zero)
+  if (tid == 0) s_cnt = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += blockDim.x) {
+    const uint64_t w = row[i];
+    if (w >= prefix) {
+      const int pos = atomicAdd(&s_cnt, 1);
+      if (pos < kSelectMaxK) s[pos] = w;  // exactly k words reach here (the words are distinct)
+    }
+  }
+  int P = 1;
+  while (P < k) P <<= 1;
+  __syncthreads();
+  for (int i = k + tid; i < P; i += blockDim.x) s[i] = 0ull;
+  __syncthreads();
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < P / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const uint64_t a = s[lo], bb = s[hi];
+        if ((a < bb) == desc) {
+          s[lo] = bb;
+          s[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int j = tid; j < k; j += blockDim.x) {
+    const uint64_t w = s[j];
+    out_idx[(long long)m * k + j] = int32_t(cand_idx(w));
+    sel_words[(long long)m * k + j] = w;
+    if (out_words) out_words[(long long)m * k + j] = cand_word(uint32_t(w >> 32), cand_idx(w) + idx_base);
+  }
+}
+
+// Exact bf16 logits of selected candidates: one warp per (row, candidate), the reduction order of
+// topk_merge_kernel's rescoring (qo_dot_bf16).
+constexpr int kRescoreWarps = 8;
+__global__ void __launch_bounds__(kRescoreWarps * 32)
+rescore_kernel(const int32_t* __restrict__ idx, int k, const uint16_t* __restrict__ W, const uint16_t* __restrict__ h,
+               int K, uint16_t* __restrict__ out_fine) {
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int m = blockIdx.y, j = blockIdx.x * kRescoreWarps + warp;
+  if (j >= k) return;
+  const uint32_t v = uint32_t(idx[(long long)m * k + j]);
+  const uint16_t* hr = h + (long long)m * K;
+  const uint16_t* wr = W + (long long)v * K;
+  float acc = 0.0f;
+  constexpr int kB = 8;
+  for (int c0 = lane; c0 < K / 8; c0 += 32 * kB) {
+    uint4 w4[kB];
+#pragma unroll
+    for (int u = 0; u < kB; ++u)
+      if (c0 + 32 * u < K / 8) w4[u] = ldg_nc_v4(wr + 8 * (c0 + 32 * u));
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      if (c0 + 32 * u >= K / 8) break;
+      const uint4 h4 = *reinterpret_cast<const uint4*>(hr + 8 * (c0 + 32 * u));
+      const uint32_t ww[4] = {w4[u].x, w4[u].y, w4[u].z, w4[u].w}, hh[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc = __fmaf_rn(bflo(ww[e]), bflo(hh[e]), acc);
+        acc = __fmaf_rn(bfhi(ww[e]), bfhi(hh[e]), acc);
+      }
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) out_fine[(long long)m * k + j] = f2bf(acc);
+}
+
+// Argmax of the k exact logits of each row (ties to the lower vocabulary index): one warp per row.
+__global__ void fine_argmax_kernel(const int32_t* __restrict__ idx, const uint16_t* __restrict__ fine, int k,
+                                   int32_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int m = blockIdx.x, lane = threadIdx.x;
+  uint64_t best = 0;
+  for (int j = lane; j < k; j += 32)
+    best = max(best, cand_word(key16(fine[(long long)m * k + j]), uint32_t(idx[(long long)m * k + j])));
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, d));
+  if (lane == 0) out[m] = int32_t(cand_idx(best));
+}
+
 // Merges the candidate lists of G vocabulary shards (words [G][M][k] with global indices, fine bf16
 // logits alongside): per row the k best words over all shards, in order, their fine logits, and the
 // argmax of those.  The best k of the union equal the best k of the whole vocabulary, because every
@@ -313,7 +439,8 @@ using namespace qmtp;
 
 extern "C" size_t qmtp_topk_workspace(int M, int V, int k) {
   if (M < 1 || V < 1 || k < 1) return 0;
-  return size_t(M) * topk_blocks(V, k) * k * sizeof(uint64_t);
+  const size_t cand = size_t(M) * topk_blocks(V, k) * k * sizeof(uint64_t);
+  return k > 256 ? cand + size_t(M) * k * sizeof(uint64_t) : cand;  // k > 256: + the selected words
 }
 
 static int topk_rescore(const void* vals, int ld, int M, int V, int k, const void* w_fine, const void* h, int K,
@@ -331,18 +458,33 @@ static int topk_rescore(const void* vals, int ld, int M, int V, int k, const voi
                         int* out_idx, void* out_fine, int* out_argmax, void* workspace, size_t ws_bytes,
                         uint32_t idx_base, void* out_words, void* stream) {
   if (!vals || !out_idx || !workspace) return QMTP_ERR_ARG;
-  if (M < 1 || V < 1 || k < 1 || k > 256 || k > V || ld < V) return QMTP_ERR_SHAPE;
+  if (M < 1 || V < 1 || k < 1 || k > kSelectMaxK || k > V || ld < V) return QMTP_ERR_SHAPE;
   if (w_fine && (!h || !out_fine || K < 256 || K % 256 != 0)) return QMTP_ERR_SHAPE;
   if (w_fine && (!aligned16(w_fine) || !aligned16(h))) return QMTP_ERR_ALIGN;
   const int G = topk_blocks(V, k);
   if (ws_bytes < qmtp_topk_workspace(M, V, k) || !aligned16(workspace)) return QMTP_ERR_ARG;
   const int NP = pow2_at_least(G * k);
-  if (NP > 8192) return QMTP_ERR_UNSUPPORTED;
+  if (k <= 256 && NP > 8192) return QMTP_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int slice = (V + G - 1) / G;
   const size_t smemA = (256 + 4 + 32) * sizeof(int) + size_t(slice) * sizeof(uint16_t);
   uint64_t* cand = static_cast<uint64_t*>(workspace);
   launch_kernel(topk_partial_kernel, dim3(dim3(G, M)), dim3(kTopkThreads), smemA, st, static_cast<const uint16_t*>(vals), ld, V, k, cand);
+  if (k > 256) {
+    // large k: radix select, then the rescoring spread over the SMs, then the argmax
+    uint64_t* sel = cand + size_t(M) * G * k;
+    launch_kernel(topk_select_kernel, dim3(M), dim3(kSelectThreads), 0, st, static_cast<const uint64_t*>(cand), G * k, k,
+                  out_idx, sel, idx_base, static_cast<uint64_t*>(out_words));
+    if (w_fine) {
+      launch_kernel(rescore_kernel, dim3((k + kRescoreWarps - 1) / kRescoreWarps, M), dim3(kRescoreWarps * 32), 0, st,
+                    static_cast<const int32_t*>(out_idx), k, static_cast<const uint16_t*>(w_fine),
+                    static_cast<const uint16_t*>(h), K, static_cast<uint16_t*>(out_fine));
+      if (out_argmax)
+        launch_kernel(fine_argmax_kernel, dim3(M), dim3(32), 0, st, static_cast<const int32_t*>(out_idx),
+                      static_cast<const uint16_t*>(out_fine), k, out_argmax);
+    }
+    return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+  }
   const size_t smemB = size_t(NP + k) * sizeof(uint64_t);
   static const cudaError_t attr =
       cudaFuncSetAttribute(topk_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);

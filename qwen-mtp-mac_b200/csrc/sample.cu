@@ -22,7 +22,7 @@
 namespace qmtp {
 namespace {
 
-constexpr int kSampMaxK = 256;
+constexpr int kSampMaxK = 2048;  // lm_head2.py:32-36: k_for returns at most 2048
 constexpr int kSampThreads = 256;
 
 __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {

@@ -198,8 +198,7 @@ class ShardedTwoStageHead:
 
 
 def k_for(sampling) -> int:
-    """lm_head2.py:32-36: 64 for greedy or top_k <= 32; else 4*top_k (top_k = 0 -> 256), max 2048.
-    This build's selection kernel supports k <= 256."""
+    """lm_head2.py:32-36: 64 for greedy or top_k <= 32; else 4*top_k (top_k = 0 -> 256), max 2048."""
     if sampling is None or sampling.temperature <= 0 or 0 < sampling.top_k <= 32:
         return 64
     return 256 if sampling.top_k <= 0 else min(4 * sampling.top_k, 2048)

@@ -81,7 +81,7 @@ class MTPDecoder:
         self.memb, self.mcat, self.mx, self.mxn = z(S, H), z(S, 2 * H), z(S, H), z(1, H)
         self._hstage, self._sel, self._last_S = z(S, H), z(1, dtype=i32), None  # reference-style calls
         self.dlogits = z(1, a.vocab)
-        self.KMAX = 256
+        self.KMAX = 2048  # k_for's largest candidate count (lm_head2.py:32-36)
         self.fine, self.idx = z(S, self.KMAX), z(S, self.KMAX, dtype=i32)
         self.coarse = z(S, a.vocab)
         self.topk_ws = torch.empty(self.L.qmtp_topk_workspace(S, a.vocab, self.KMAX), dtype=torch.uint8,
@@ -111,9 +111,6 @@ class MTPDecoder:
         next decode), since the sampler's parameters are part of its launches."""
         sp = sampling if sampling is not None and sampling.temperature > 0 else None
         K = k_for(sp)
-        if K > 256:
-            raise NotImplementedError(f"top_k = {sampling.top_k} needs {K} head candidates; this build "
-                                      "selects at most 256 (top_k <= 64, or top_k = 0)")
         key = None if sp is None else (float(sp.temperature), int(sp.top_k), float(sp.top_p), float(sp.min_p))
         old = None if self.sp is None else (float(self.sp.temperature), int(self.sp.top_k), float(self.sp.top_p),
                                             float(self.sp.min_p))

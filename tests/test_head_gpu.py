@@ -131,3 +131,24 @@ def test_two_stage_head_nvfp4_coarse_bit_exact(V, D, M, k, dev):
         assert np.array_equal(to_np(built.coarse.scales), ns)
         got = [to_np(t) for t in built.select(to_torch(h, dev))]
         assert np.array_equal(got[0].view(np.int32), ridx)
+
+
+@pytest.mark.parametrize("k,M", [(512, 3), (2048, 3), (1000, 1)])
+def test_two_stage_head_large_k_bit_exact(k, M, dev):
+    """Candidate sets above 256 (k_for up to 2048, lm_head2.py:32-36): the radix-select path gives the
+    oracle's index set, order, exact logits and argmax at V = 248320, ties included."""
+    W2 = randn_bf16((248320, 4096), 5, 0.02)
+    h = randn_bf16((M, 4096), 13)
+    hf = ops.bf16_to_f32(h)
+    W2[7] = W2[200000] = ops.f32_to_bf16(0.05 * hf[0])  # a tied pair ranked first for token 0
+    wq2, s2, b2 = ops.quantize_affine(W2)
+    from qmtp.lm_head2 import TwoStageHead
+    from qmtp.qmv_kernel import QuantizedLinear
+
+    head = TwoStageHead(to_torch(W2, dev), 64, QuantizedLinear(to_torch(wq2, dev), to_torch(s2, dev), to_torch(b2, dev)))
+    idx, fine, amax = head.select(to_torch(h, dev), k=k)
+    _, ridx, rfine, ramax = ops.two_stage_head(h, wq2, s2, b2, W2, k)
+    assert ridx[0, 0] == 7 and ridx[0, 1] == 200000
+    assert np.array_equal(to_np(idx).view(np.int32), ridx)
+    assert np.array_equal(to_np(fine), rfine)
+    assert np.array_equal(to_np(amax).view(np.int32), ramax)

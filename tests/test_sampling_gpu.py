@@ -35,8 +35,9 @@ def _call(idx, fine, drafts, sp, V, seed, ctr, dev, first_row=-1):
     return to_np(out).view(np.int32)
 
 
-@pytest.mark.parametrize("K", [64, 160, 256])
-@pytest.mark.parametrize("sp", [(0.8, 0, 1.0, 0.0), (1.0, 0, 0.9, 0.0), (0.6, 20, 1.0, 0.05), (1.2, 40, 0.95, 0.01)])
+@pytest.mark.parametrize("K", [64, 160, 256, 1024, 2048])
+@pytest.mark.parametrize("sp", [(0.8, 0, 1.0, 0.0), (1.0, 0, 0.9, 0.0), (0.6, 20, 1.0, 0.05), (1.2, 40, 0.95, 0.01),
+                                (0.9, 400, 0.97, 0.0)])
 def test_sample_matches_oracle(K, sp, dev):
     rng = np.random.default_rng(K + int(10 * sp[0]))
     V = 248320
@@ -66,7 +67,7 @@ def test_sample_rejects_bad_arguments(dev):
     L = _lib.lib()
     z = torch.zeros(300, dtype=torch.int32, device=dev)
     for sp, K in [((0.0, 0, 1.0, 0.0), 64), ((1.0, 0, 0.0, 0.0), 64), ((1.0, -1, 1.0, 0.0), 64),
-                  ((1.0, 0, 1.0, 0.0), 257)]:
+                  ((1.0, 0, 1.0, 0.0), 2049)]:
         a = _lib.SamplingArgs(*sp)
         rc = L.qmtp_sample(z.data_ptr(), z.data_ptr(), K, K, z.data_ptr(), 2, -1, ctypes.byref(a), 1000,
                            z.data_ptr(), z.data_ptr(), _lib.stream())
@@ -86,6 +87,8 @@ def small_pair():
     (dict(temperature=1.0, top_k=20, seed=5), False, False),                          # 64 candidates
     (dict(temperature=0.7, top_k=40, top_p=0.9, seed=3), True, False),                # 160 candidates
     (dict(temperature=0.005, top_k=0, top_p=1.0, seed=9), True, True),                # drafts often accepted
+    (dict(temperature=0.9, top_k=512, top_p=0.97, seed=13), True, False),             # 2048 candidates
+    (dict(temperature=1.1, top_k=100, seed=17), False, False),                        # 400 candidates
 ])
 def test_sampled_stream_matches_oracle(small_pair, sp, use_graph, override):
     from qmtp import model as qm
