@@ -390,6 +390,8 @@ int qmtp_moe_dispatch(const void* idx, int T, int S, const void* x, int H, int n
 #define QMTP_CTRL_NOUT 8      /* tokens emitted so far */
 #define QMTP_CTRL_CYCLES 9    /* verify cycles */
 #define QMTP_CTRL_ACC0 10     /* accepted-draft counters per draft position */
+#define QMTP_CTRL_NUSE 18     /* adaptive k: drafts the next verify may accept (0: all k) */
+#define QMTP_CTRL_VERIFIED 19 /* drafts verified so far (sum over cycles of the accept limit) */
 #define QMTP_CTRL_EMIT0 20    /* tokens emitted by the last cycle (KEEP of them) */
 #define QMTP_CTRL_MAX_K 8
 #define QMTP_CTRL_RNG 29      /* sampling: calls of qmtp_sample so far (the Philox call counter) */
@@ -403,6 +405,15 @@ int qmtp_moe_dispatch(const void* idx, int T, int S, const void* x, int H, int n
  * advances POS, the state-ring slot and the conv window by keep. */
 int qmtp_mtp_accept(const int* a, const int* in, int k, int* ctrl, int* out_tokens, int out_cap,
                     int ring_slots, int win_rows, int forced_keep, void* stream);
+
+/* Adaptive draft count (mtp.py:217-238: draft_chain(..., with_probs) and n_drafts(probs, tau)):
+ *   qmtp_draft_prob: prob = softmax(logits)[token] = 1 / sum_j exp(l_j - l_token) of the draft head's
+ *     bf16 logits [V] at its argmax token (device int); fixed reduction order (oracle qo_draft_prob).
+ *   qmtp_mtp_nuse: ctrl[QMTP_CTRL_NUSE] = n_drafts(probs[0..k), tau) (running product in double, at
+ *     least 1); qmtp_mtp_accept then accepts at most that many drafts and adds it to
+ *     ctrl[QMTP_CTRL_VERIFIED].  ctrl[QMTP_CTRL_NUSE] = 0 (the reset value) keeps all k. */
+int qmtp_draft_prob(const void* logits, int V, const int* token, float* prob, void* stream);
+int qmtp_mtp_nuse(const float* probs, int k, double tau, int* ctrl, void* stream);
 
 /* MPOS += KEEP (the MTP cache keeps the real pairs of this cycle; mtp.py:291-294). */
 int qmtp_mtp_advance(int* ctrl, void* stream);

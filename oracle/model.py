@@ -246,12 +246,15 @@ class OracleModel:
             return ops.sample(idx, fine, None, first_row=idx.shape[0] - 1, **kw)
         return ops.sample(idx, fine, drafts, **kw)
 
-    def draft_token(self, xn):
-        """Draft head: full-vocabulary 4-bit head (bench_ab.py:24 DRAFT_HEAD, engine.py:46-48) + argmax."""
-        return ops.argmax_bf16(qmv(xn, self.W["lm_head_q"]))
+    def draft_token(self, xn, with_prob=False):
+        """Draft head: full-vocabulary 4-bit head (bench_ab.py:24 DRAFT_HEAD, engine.py:46-48) + argmax;
+        with_prob: also the probability of the argmax (mtp.py:222-223)."""
+        logits = qmv(xn, self.W["lm_head_q"])
+        d = ops.argmax_bf16(logits)
+        return (d, ops.draft_prob(logits[0], int(d[0]))) if with_prob else d
 
     # -- mtp.py:199-209
-    def mtp_step(self, hidden, tokens, mcache):
+    def mtp_step(self, hidden, tokens, mcache, with_prob=False):
         a, M = self.a, self.W["mtp"]
         e = rmsnorm(embed(tokens, *self.W["embed"], a.hidden), M["pre_fc_norm_embedding"], a.eps)
         hh = rmsnorm(hidden, M["pre_fc_norm_hidden"], a.eps)
@@ -260,16 +263,23 @@ class OracleModel:
         x = self.decoder_layer(L, x, lambda y: self.attn(L, y, mcache))
         x_last = x[-1:]
         xn = rmsnorm(x_last, M["norm"], a.eps)
+        if with_prob:
+            d, p = self.draft_token(xn, True)
+            return d, x_last, p
         return self.draft_token(xn), x_last
 
     # -- mtp.py:212-226 (chain="pre")
-    def draft_chain(self, hidden, tokens, mcache, k):
-        d, x = self.mtp_step(hidden, tokens, mcache)
-        drafts = [int(d[0])]
+    def draft_chain(self, hidden, tokens, mcache, k, with_probs=False):
+        r = self.mtp_step(hidden, tokens, mcache, with_probs)
+        drafts, probs = [int(r[0][0])], [r[2]] if with_probs else []
+        x = r[1]
         for _ in range(1, k):
-            d, x = self.mtp_step(x, np.int32([drafts[-1]]), mcache)
-            drafts.append(int(d[0]))
-        return drafts
+            r = self.mtp_step(x, np.int32([drafts[-1]]), mcache, with_probs)
+            x = r[1]
+            drafts.append(int(r[0][0]))
+            if with_probs:
+                probs.append(r[2])
+        return (drafts, probs) if with_probs else drafts
 
     # -- mtp.py:241-303 / engine.py:121-128 (greedy)
     def generate_greedy(self, prompt_ids, max_tokens, eos=()):
@@ -282,7 +292,7 @@ class OracleModel:
             out.append(int(self.head(hn)[0]))
         return out
 
-    def prefill(self, prompt_ids, k=2, sampling=None):
+    def prefill(self, prompt_ids, k=2, sampling=None, tau=None):
         """mtp.py:258-263: prompt pass, first token t, first drafts; returns (cache, mcache, h, t, drafts).
         With sampling (temperature > 0) the first token is drawn (engine.py:110-115, call counter 0)."""
         cache = self.make_cache()
@@ -290,11 +300,11 @@ class OracleModel:
         p = np.int32(prompt_ids)
         h, hn = self.backbone(p, cache)
         t = int(self._sample(hn[-1:], sampling, 0)) if _sampled(sampling) else int(self.head(hn[-1:])[0])
-        drafts = self.draft_chain(h, np.concatenate([p[1:], np.int32([t])]), mcache, k)
+        drafts = self.draft_chain(h, np.concatenate([p[1:], np.int32([t])]), mcache, k, tau is not None)
         return cache, mcache, t, drafts
 
     def decode(self, cache, mcache, t, drafts, max_tokens, eos=(), k=2, max_cycles=None, draft_override=None,
-               sampling=None, rng_ctr=1):
+               sampling=None, rng_ctr=1, tau=None):
         """The verify loop of mtp.py:268-294 from a given state; returns (out tokens incl. t, stats).
         With sampling (temperature > 0) each cycle decides by exact speculative sampling (engine.py:
         121-152) with call counter rng_ctr, rng_ctr + 1, ..."""
@@ -302,6 +312,12 @@ class OracleModel:
         out = [t]
         cycles = verified = 0
         acc_pos = [0] * k
+        # adaptive k (mtp.py:229-238): drafts arrive with their probabilities; only the first
+        # n_drafts(probs, tau) may be accepted (verifying all k rows gives the same rows: batch-invariant)
+        n_use = k
+        if tau is not None:
+            drafts, probs = drafts
+            n_use = ops.n_drafts(probs, tau)
         while len(out) < max_tokens and out[-1] not in eos:
             if max_cycles is not None and cycles >= max_cycles:
                 break
@@ -319,11 +335,11 @@ class OracleModel:
             else:
                 av = [int(v) for v in self.head(hn)]
                 n_acc = 0
-                while n_acc < k and av[n_acc] == drafts[n_acc]:
+                while n_acc < n_use and av[n_acc] == drafts[n_acc]:
                     acc_pos[n_acc] += 1
                     n_acc += 1
             cycles += 1
-            verified += k
+            verified += n_use
             keep = n_acc + 1
             out += av[:keep]
             if keep < S:
@@ -334,7 +350,10 @@ class OracleModel:
                         c.trim(S - keep)
             mcache.trim(k - 1)
             t = av[keep - 1]
-            drafts = self.draft_chain(h[:keep], np.int32(av[:keep]), mcache, k)
+            drafts = self.draft_chain(h[:keep], np.int32(av[:keep]), mcache, k, tau is not None)
+            if tau is not None:
+                drafts, probs = drafts
+                n_use = ops.n_drafts(probs, tau)
         dt = time.perf_counter() - t0
         for i, tok in enumerate(out):
             if tok in eos:
@@ -358,12 +377,13 @@ class OracleModel:
         return cache, KVCache(mtp[0].copy(), mtp[1].copy(), int(mtp[2]))
 
     def generate_mtp(self, prompt_ids, max_tokens, eos=(), k=2, max_cycles=None, draft_override=None,
-                     sampling=None):
+                     sampling=None, tau=None):
         """mtp.py:241-303 (fixed k; greedy, or sampled when sampling.temperature > 0).
         draft_override(cycle) -> list of k tokens or None replaces the drafts a cycle verifies (test
         hook for acceptance and rollback; the MTP caches still follow the computed drafts)."""
-        cache, mcache, t, drafts = self.prefill(prompt_ids, k, sampling)
-        return self.decode(cache, mcache, t, drafts, max_tokens, eos, k, max_cycles, draft_override, sampling)
+        cache, mcache, t, drafts = self.prefill(prompt_ids, k, sampling, tau)
+        return self.decode(cache, mcache, t, drafts, max_tokens, eos, k, max_cycles, draft_override, sampling,
+                           tau=tau)
 
     # -- mtp.py:136-140
     def restore(self, c: GDNCache, keep: int) -> None:

@@ -246,6 +246,24 @@ def argmax_bf16(vals):
     return out
 
 
+def draft_prob(logits, token):
+    """C qo_draft_prob: softmax(logits)[token] (the draft head's argmax probability, mtp.py:222-223)."""
+    v = np.ascontiguousarray(logits, np.uint16).reshape(-1)
+    lib().qo_draft_prob.restype = ctypes.c_float
+    return float(lib().qo_draft_prob(_p(v), _I(v.size), _I(int(token))))
+
+
+def n_drafts(probs, tau):
+    """mtp.py:229-238: drafts to verify -- while the running product stays >= tau (at least 1)."""
+    n, acc = 0, 1.0
+    for p in probs:
+        acc *= p
+        if n and acc < tau:
+            break
+        n += 1
+    return n
+
+
 def two_stage_head(h, wq, s, b, W, k=64):
     """lm_head2.py:23-29 restated: (coarse bf16 [M,V], idx [M,k], fine bf16 [M,k], argmax [M])."""
     coarse = qmv_affine(h, wq, s, b)

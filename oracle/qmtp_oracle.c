@@ -859,6 +859,32 @@ QO_API void qo_attention(const uint16_t* q, const uint16_t* gate, const uint16_t
   free(qf); free(kf); free(num); free(acc);
 }
 
+/* Probability the draft head gives its argmax token (mtp.py:222-223, softmax(logits).max()) in the
+ * reduction order of draft_prob_kernel: 1024 strided sequential partial sums of exp(l_j - l_token),
+ * the xor butterfly over each 32 partials, the 32 group sums in order; 1 / total. */
+QO_API float qo_draft_prob(const uint16_t* logits, int V, int token) {
+  float part[1024], grp[32];
+  float lmax = qo_bf2f(logits[token]);
+  for (int t = 0; t < 1024; ++t) {
+    float s = 0.0f;
+    for (int j = t; j < V; j += 1024) s = s + qo_expf(qo_bf2f(logits[j]) - lmax);
+    part[t] = s;
+  }
+  for (int w = 0; w < 32; ++w) {
+    float v[32];
+    for (int l = 0; l < 32; ++l) v[l] = part[32 * w + l];
+    for (int d = 16; d >= 1; d >>= 1) {
+      float nv[32];
+      for (int l = 0; l < 32; ++l) nv[l] = v[l] + v[l ^ d];
+      for (int l = 0; l < 32; ++l) v[l] = nv[l];
+    }
+    grp[w] = v[0];
+  }
+  float tot = grp[0];
+  for (int w = 1; w < 32; ++w) tot = tot + grp[w];
+  return 1.0f / tot;
+}
+
 /* SwiGLU (mlx-lm MLP: down(silu(gate(x)) * up(x))): act = R(silu_bf(g) * u); gu bf16 [S, 2I]
  * (gate columns then up columns, row stride ld) -> out bf16 [S, I]. */
 QO_API void qo_swiglu(const uint16_t* gu, int ld, int S, int I, uint16_t* out) {

@@ -363,13 +363,17 @@ __global__ void accept_kernel(const int32_t* __restrict__ a, const int32_t* __re
   pdl_wait();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   int n_acc = 0;
+  // adaptive k (mtp.py:229-238): only the first NUSE drafts are verified (0: all k)
+  const int nuse = ctrl[QMTP_CTRL_NUSE];
+  const int lim = nuse > 0 && nuse < k ? nuse : k;
   if (forced_keep > 0) {
     n_acc = forced_keep - 1;
   } else {
-    while (n_acc < k && a[n_acc] == in[1 + n_acc]) {
+    while (n_acc < lim && a[n_acc] == in[1 + n_acc]) {
       ctrl[QMTP_CTRL_ACC0 + n_acc] += 1;
       ++n_acc;
     }
+    ctrl[QMTP_CTRL_VERIFIED] += lim;
   }
   const int keep = n_acc + 1;
   int nout = ctrl[QMTP_CTRL_NOUT];
@@ -389,6 +393,56 @@ __global__ void accept_kernel(const int32_t* __restrict__ a, const int32_t* __re
   ctrl[QMTP_CTRL_WPAR] = par;
   ctrl[QMTP_CTRL_CONV_ROW] = par * win_rows + keep;
   ctrl[QMTP_CTRL_WOUT_ROW] = (par ^ 1) * win_rows;
+}
+
+// Probability the draft head gives its argmax token (mtp.py:222-223: softmax(logits).max()): 1 / sum_j
+// exp(l_j - l_max) over the vocabulary.  One CTA of 1024 threads; the sum is fixed in order: thread t
+// adds the elements j = t, t + 1024, ... in order, the xor butterfly within each warp, then the 32
+// warp sums in order (oracle qo_draft_prob).
+constexpr int kProbThreads = 1024;
+__global__ void __launch_bounds__(kProbThreads)
+draft_prob_kernel(const uint16_t* __restrict__ logits, int V, const int32_t* __restrict__ token, float* __restrict__ prob,
+                  unsigned* err) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float ws[kProbThreads / 32];
+  const int tid = threadIdx.x;
+  const int t = *token;
+  if (t < 0 || t >= V) {  // uniform: every thread reads the same token
+    if (tid == 0) {
+      atomicOr(err, DEVERR_BADARG);
+      *prob = 0.0f;
+    }
+    return;
+  }
+  const float lmax = bf2f(logits[t]);
+  float s = 0.0f;
+  for (int j = tid; j < V; j += kProbThreads) s = __fadd_rn(s, q_expf(__fsub_rn(bf2f(logits[j]), lmax)));
+  s = warp_sum(s);
+  if ((tid & 31) == 0) ws[tid >> 5] = s;
+  __syncthreads();
+  if (tid == 0) {
+    float tot = ws[0];
+    for (int w = 1; w < kProbThreads / 32; ++w) tot = __fadd_rn(tot, ws[w]);
+    *prob = __fdiv_rn(1.0f, tot);
+  }
+}
+
+// n_drafts (mtp.py:229-238): the drafts to verify next, from the chain's k probabilities -- keep
+// multiplying while the running product stays >= tau (at least one draft); double precision like the
+// reference's Python float product.
+__global__ void mtp_nuse_kernel(const float* __restrict__ probs, int k, double tau, int* __restrict__ ctrl) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int n = 0;
+  double acc = 1.0;
+  for (int i = 0; i < k; ++i) {
+    acc *= double(probs[i]);
+    if (n && acc < tau) break;
+    ++n;
+  }
+  ctrl[QMTP_CTRL_NUSE] = n;
 }
 
 // MTP cache bookkeeping between the two draft steps: MPOS += keep (mtp.py:291-294: the k-1 chained
@@ -510,6 +564,21 @@ extern "C" int qmtp_mtp_accept(const int* a, const int* in, int k, int* ctrl, in
     return QMTP_ERR_SHAPE;
   launch_kernel(accept_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), a, in, k, ctrl, out_tokens, out_cap, ring_slots,
                                                                   win_rows, forced_keep);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_draft_prob(const void* logits, int V, const int* token, float* prob, void* stream) {
+  if (!logits || !token || !prob) return QMTP_ERR_ARG;
+  if (V < 1) return QMTP_ERR_SHAPE;
+  launch_kernel(draft_prob_kernel, dim3(1), dim3(kProbThreads), 0, static_cast<cudaStream_t>(stream),
+                static_cast<const uint16_t*>(logits), V, token, prob, device_error_ptr());
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_mtp_nuse(const float* probs, int k, double tau, int* ctrl, void* stream) {
+  if (!probs || !ctrl) return QMTP_ERR_ARG;
+  if (k < 1 || k > QMTP_CTRL_MAX_K) return QMTP_ERR_SHAPE;
+  launch_kernel(mtp_nuse_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), probs, k, tau, ctrl);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 

@@ -82,6 +82,8 @@ SIGNATURES.update({
     "qmtp_attention": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P, _P],
     "qmtp_swiglu": [_P, _I, _I, _I, _P, _P],
     "qmtp_mtp_accept": [_P, _P, _I, _P, _P, _I, _I, _I, _I, _P],
+    "qmtp_draft_prob": [_P, _I, _P, _P, _P],
+    "qmtp_mtp_nuse": [_P, _I, ctypes.c_double, _P, _P],
     "qmtp_mtp_advance": [_P, _P],
     "qmtp_next_tokens": [_P, _P, _I, _P, _P, _P],
     "qmtp_quantize_fp4": [_I, _P, ctypes.c_longlong, _I, _P, _P, _P],
@@ -95,7 +97,7 @@ SIGNATURES.update({
 })
 
 # control block layout (include/qmtp.h QMTP_CTRL_*)
-CTRL = dict(SLOT=0, CONV_ROW=1, WOUT_ROW=2, WPAR=3, POS=4, MPOS=5, KEEP=6, SEL=7, NOUT=8, CYCLES=9, ACC0=10,
+CTRL = dict(SLOT=0, CONV_ROW=1, WOUT_ROW=2, WPAR=3, POS=4, MPOS=5, KEEP=6, SEL=7, NOUT=8, CYCLES=9, ACC0=10, NUSE=18, VERIFIED=19,
             EMIT0=20, RNG=29, SEED_LO=30, SEED_HI=31)
 
 

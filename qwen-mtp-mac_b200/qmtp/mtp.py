@@ -45,8 +45,9 @@ class MTPDecoder:
     """Device state + launch sequence of one MTP decoding session (batch 1; greedy or sampled)."""
 
     def __init__(self, args: ModelArgs, W: Weights, k: int = 2, max_tokens: int = 1024, device="cuda",
-                 sampling: Sampling | None = None):
+                 sampling: Sampling | None = None, tau: float | None = None):
         self.a, self.W, self.k = args, W, k
+        self.tau = None
         # sampling with temperature > 0: exact speculative sampling (engine.py:91-152) over the
         # k_for(sampling) candidates of the two-stage head (lm_head2.py:32-36); otherwise greedy
         self.sp, self.K, self._sargs = None, 64, None
@@ -81,6 +82,7 @@ class MTPDecoder:
         self.memb, self.mcat, self.mx, self.mxn = z(S, H), z(S, 2 * H), z(S, H), z(1, H)
         self._hstage, self._sel, self._last_S = z(S, H), z(1, dtype=i32), None  # reference-style calls
         self.dlogits = z(1, a.vocab)
+        self.probs = z(k, dtype=f32)  # adaptive k: the draft head's argmax probability per draft
         self.KMAX = 2048  # k_for's largest candidate count (lm_head2.py:32-36)
         self.fine, self.idx = z(S, self.KMAX), z(S, self.KMAX, dtype=i32)
         self.coarse = z(S, a.vocab)
@@ -104,12 +106,29 @@ class MTPDecoder:
         self.launches = 0      # kernels launched by the library calls of this decoder
         self.prof = None       # list of (bytes, start event, end event, shape) while profiling qmv
         self.qmv_log = None    # list of the _qmv argument tuples of a cycle while recording
+        if tau is not None:
+            self.set_tau(tau)
+
+    def set_tau(self, tau: float | None):
+        """Adaptive draft count (mtp.py:229-238, generate_mtp's tau): None verifies every draft; a number
+        accepts only the first n_drafts(probs, tau) drafts of each cycle, probs being the draft head's
+        argmax probabilities.  Greedy decoding only.  A change drops the captured cycle graph."""
+        tau = None if tau is None else float(tau)
+        if tau is not None and self.sp is not None:
+            raise NotImplementedError("the adaptive draft count is built for greedy decoding")
+        if tau != self.tau:
+            self.graph = None
+            if tau is None:
+                self.ctrl[C["NUSE"]] = 0
+        self.tau = tau
 
     def set_sampling(self, sampling: Sampling | None, _init: bool = False):
         """Greedy (None or temperature 0) or exact speculative sampling with these parameters; the
         candidate count is k_for(sampling).  A change drops the captured cycle graph (recaptured by the
         next decode), since the sampler's parameters are part of its launches."""
         sp = sampling if sampling is not None and sampling.temperature > 0 else None
+        if sp is not None and getattr(self, "tau", None) is not None:
+            raise NotImplementedError("the adaptive draft count is built for greedy decoding")
         K = k_for(sp)
         key = None if sp is None else (float(sp.temperature), int(sp.top_k), float(sp.top_p), float(sp.min_p))
         old = None if self.sp is None else (float(self.sp.temperature), int(self.sp.top_k), float(self.sp.top_p),
@@ -127,7 +146,7 @@ class MTPDecoder:
         return _lib.stream()
 
     _KERNELS = {"rmsnorm": 1, "attn_prep": 1, "attention": 1, "swiglu": 1, "embed": 1, "gdn": 1, "norm_gate": 1,
-                "accept": 1, "advance": 1, "next_tokens": 1, "argmax": 2}
+                "accept": 1, "advance": 1, "next_tokens": 1, "argmax": 2, "draft_prob": 1, "nuse": 1}
 
     def _chk(self, rc, what):
         self.launches += self._KERNELS.get(what, 0)
@@ -325,14 +344,25 @@ class MTPDecoder:
         """mtp.py:212-226, k drafts, chain on the MTP's own pre-norm output (chain="pre")."""
         sel = self._cp(C["SEL"])
         self.mtp_step(hidden, None, tok, self.S, sel, self.drafts.data_ptr())
+        self._draft_prob(0)
         self._chk(self.L.qmtp_mtp_advance(self.ctrl.data_ptr(), self._st()), "advance")
         for j in range(1, self.k):
             # the chained step reads the previous step's output row: row SEL after the first step, 0 after
             hsel = sel if j == 1 else None
             self.mtp_step(self.mx, hsel, self.drafts.data_ptr() + 4 * (j - 1), 1, None,
                           self.drafts.data_ptr() + 4 * j)
+            self._draft_prob(j)
+        if self.tau is not None:
+            self._chk(self.L.qmtp_mtp_nuse(self.probs.data_ptr(), self.k, self.tau, self.ctrl.data_ptr(), self._st()),
+                      "nuse")
         self._chk(self.L.qmtp_next_tokens(self.a_tok.data_ptr(), self.drafts.data_ptr(), self.k, self.ctrl.data_ptr(),
                                           self.tokens_in.data_ptr(), self._st()), "next_tokens")
+
+    def _draft_prob(self, j):
+        """Adaptive k: probability of draft j under the draft head (mtp.py:222-223)."""
+        if self.tau is not None:
+            self._chk(self.L.qmtp_draft_prob(self.dlogits.data_ptr(), self.a.vocab, self.drafts.data_ptr() + 4 * j,
+                                             self.probs.data_ptr() + 4 * j, self._st()), "draft_prob")
 
     def cycle(self):
         """One verify + accept + draft cycle (mtp.py:268-294), device-side only."""
@@ -498,6 +528,7 @@ def decode_mtp(dec: MTPDecoder, prompt_ids, max_tokens, eos=(), use_graph=True, 
     if use_graph:
         dec.ensure_graph()
     torch.cuda.synchronize()
+    verified0 = int(dec.ctrl[C["VERIFIED"]])
     t0 = time.perf_counter()
     out = [t]
     k = dec.k
@@ -518,7 +549,9 @@ def decode_mtp(dec: MTPDecoder, prompt_ids, max_tokens, eos=(), use_graph=True, 
     ctrl = dec.ctrl.tolist()
     acc = [ctrl[C["ACC0"] + i] for i in range(k)]
     stats = {"tps": (len(out) - 1) / dt if dt > 0 else 0.0, "tok_ciclo": (len(out) - 1) / max(cycles, 1),
-             "acept": [n / max(cycles, 1) for n in acc], "borradores_ciclo": float(k), "cycles": cycles,
+             "acept": [n / max(cycles, 1) for n in acc],
+             "borradores_ciclo": (ctrl[C["VERIFIED"]] - verified0) / max(cycles, 1) if dec.tau is not None else float(k),
+             "cycles": cycles,
              "seconds": dt, "cached_tokens": dec.cached_tokens}
     return out, stats
 
@@ -641,7 +674,11 @@ def draft_chain(lm, mtp, hidden, tokens, mcache: MTPDecoder, k, head=None, chain
             dec.ctrl[C["MPOS"]] += 1  # the chained entry is visible to the next chained step
         drafts.append(torch.argmax(logits[0, -1]).to(torch.int32).reshape(1))
         if with_probs:
-            probs.append(torch.softmax(logits[0, -1].float(), dim=-1).max().reshape(1))
+            pr = torch.empty(1, dtype=torch.float32, device=dec.dev)
+            row = logits[0, -1].contiguous()
+            _lib.check(dec.L.qmtp_draft_prob(row.data_ptr(), row.numel(), drafts[-1].data_ptr(), pr.data_ptr(),
+                                             _lib.stream()), "draft_prob")
+            probs.append(pr)
     dec.ctrl[C["MPOS"]] = mpos
     d = torch.cat(drafts)[None]
     return (d, torch.cat(probs)[None]) if with_probs else d
@@ -662,15 +699,15 @@ def n_drafts(probs, tau):
 def generate_mtp(lm, mtp, prompt_ids, max_tokens, eos, head=None, k=1, bb_hidden="pre", chain="pre", tau=None):
     """mtp.py:241-303 with the reference's signature: greedy MTP decoding of prompt_ids, returns
     (tokens, stats).  Runs decode_mtp (the graph-captured loop) on the model's session for this k.
-    bb_hidden and chain must be "pre" and tau None (fixed k): the variants the build implements."""
+    bb_hidden and chain must be "pre" (the variant the build implements); tau: None = always k drafts, a
+    number = adaptive k (n_drafts over the draft head's probabilities, mtp.py:229-238)."""
     _check_mtp(lm, mtp)
     _check_head(lm, head)
     if bb_hidden != "pre" or chain != "pre":
         raise NotImplementedError('only bb_hidden="pre", chain="pre" are built')
-    if tau is not None:
-        raise NotImplementedError("adaptive k (tau) is not built; the verify step has a fixed k")
     dec = lm.session(k=k, max_tokens=max_tokens)
     dec.set_sampling(None)
+    dec.set_tau(tau)
     return decode_mtp(dec, prompt_ids, max_tokens, tuple(eos))
 
 

@@ -60,3 +60,46 @@ def test_config4_loop_shape_on_small_model(small_pair):
     ref, _ = orc.generate_mtp(p, 256)
     out, st = decode_mtp(_decoder(W), p, 256, use_graph=True)
     assert len(out) == 256 and out == ref
+
+
+@pytest.mark.parametrize("tau,override", [(0.0, True), (3e-7, True), (3e-7, False), (0.5, True), (0.999, False)])
+def test_adaptive_draft_count_matches_oracle(small_pair, tau, override):
+    """Adaptive k (mtp.py:229-238): drafts accepted only up to n_drafts(probs, tau), probs being the
+    draft head's argmax probabilities.  The token stream equals plain greedy decoding, and the
+    acceptance statistics and drafts verified per cycle equal the oracle's adaptive loop."""
+    from qmtp.mtp import decode_mtp
+
+    orc, W = small_pair
+    p = prompt(33, seed=8)
+    ov = greedy_overrides(orc.generate_greedy(p, 40), om.SMALL.vocab) if override else None
+    ref, rst = orc.generate_mtp(p, 40, draft_override=ov, tau=tau)
+    assert ref == orc.generate_greedy(p, 40)
+    dec = _decoder(W)
+    dec.set_tau(tau)
+    ov2 = greedy_overrides(orc.generate_greedy(p, 40), om.SMALL.vocab) if override else None
+    out, st = decode_mtp(dec, p, 40, use_graph=True, draft_override=ov2)
+    assert out == ref
+    assert st["acept"] == rst["acept"] and st["cycles"] == rst["cycles"]
+    assert st["borradores_ciclo"] == rst["borradores_ciclo"]
+    if tau == 0.999:
+        assert st["borradores_ciclo"] == 1.0  # random weights: no draft is that likely
+    if tau == 0.0:
+        assert st["borradores_ciclo"] == 2.0  # every draft is verified
+
+
+def test_draft_prob_matches_oracle(dev):
+    """The draft head's argmax probability (qmtp_draft_prob) equals the oracle's bit for bit."""
+    import torch
+
+    from oracle import ops
+    from qmtp import _lib
+    from tests._util import randn_bf16, to_torch
+
+    for V, scale in ((248320, 3.0), (16384, 0.5), (1000, 20.0)):
+        lg = randn_bf16((V,), V, scale)
+        t = int(ops.argmax_bf16(lg[None])[0])
+        pr = torch.empty(1, dtype=torch.float32, device=dev)
+        tok = torch.tensor([t], dtype=torch.int32, device=dev)
+        _lib.check(_lib.lib().qmtp_draft_prob(to_torch(lg, dev).data_ptr(), V, tok.data_ptr(), pr.data_ptr(),
+                                              _lib.stream()), "draft_prob")
+        assert float(pr.item()) == ops.draft_prob(lg, t), V
