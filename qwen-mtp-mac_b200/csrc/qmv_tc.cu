@@ -110,6 +110,7 @@ struct Params {
   unsigned* err;
   int ldy, N, K, NSL, R, ntiles;  // ntiles * (gridDim.x + 1) and ntiles * NSL < 2^31 (host-checked)
   int cs;             // cluster mode (> 1): CTAs per tile, one tile per cluster
+  int pair;           // pair mode (cs == 2): a cluster owns a run of tiles and splits its units in two
   // activation prologue (template parameter PRO): kProRms: x = RMSNorm(x rows; nw, eps); kProSwiglu:
   // x = silu(g) * u with g = x[:, k] and u = x[:, K + k]; kProGated: x = bf16(RMSNorm_head(y; nw, eps)
   // * silu(z)), y fp32 rows at x (ldx in floats), z bf16 rows [ldz], heads of 128.
@@ -120,10 +121,19 @@ struct Params {
 };
 enum : int { kProNone = 0, kProRms = 1, kProSwiglu = 2, kProGated = 3 };
 
-// (tile, slice) of consecutive units, advanced without divisions.
+// (tile, slice) of a CTA's units in processing order, advanced without divisions: `left` units of the
+// current run, then (pair mode) one jump to a second run of `jl` units starting at (jt, js).
 struct UnitCursor {
-  int tile, sl;
+  int tile, sl, left, jt, js, jl;
+  template <bool JUMP>
   __device__ __forceinline__ void next(int NSL) {
+    if (JUMP && --left == 0 && jl > 0) {
+      tile = jt;
+      sl = js;
+      left = jl;
+      jl = 0;
+      return;
+    }
     if (++sl == NSL) {
       sl = 0;
       ++tile;
@@ -329,9 +339,9 @@ __device__ __forceinline__ void prep_task(uint4 v, int m, int g, int li, uint8_t
 //          are in flight meanwhile);
 //   2      in stream mode (more than 8 slices and units), builds the later slices one unit at a time;
 //   4-7    chain-0 workers, 8-11 chain-1 workers: warp w serves TMEM lane quarter w % 4, thread = row.
-// PRO: the activation prologue (kProNone, kProRms, kProSwiglu, kProGated; a separate instantiation
-// per prologue keeps each kernel's code small).
-template <int MT, int PRO>
+// PRO: the activation prologue (kProNone, kProRms, kProSwiglu, kProGated); PAIR: pair mode (2-CTA
+// clusters owning tile runs).  A separate instantiation per variant keeps each kernel's code small.
+template <int MT, int PRO, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     qmv_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
                   const __grid_constant__ CUtensorMap tb, const __grid_constant__ Params p) {
@@ -345,7 +355,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   int u0, u1;
   const int cs = p.cs;
   const uint32_t crank = cs > 1 ? cluster_rank() : 0u;
-  if (cs > 1) {
+  // pair mode: rank 1's range may start with the last `tail` units of the tile rank 0 starts (rank 0's
+  // "head"); rank 1 processes them last, so their weight stages are free for their slice partials
+  int tail = 0, head = 0, n1 = 0;
+  if (PAIR) {
+    const int ncl = int(gridDim.x) / 2, c = int(blockIdx.x) / 2;
+    const int t0 = c * p.ntiles / ncl, t1 = (c + 1) * p.ntiles / ncl;
+    const int half = (t1 - t0) * NSL / 2;
+    head = half % NSL;  // rank 0's last tile ends after `head` slices (0: tile-aligned split)
+    tail = head ? NSL - head : 0;
+    n1 = (t1 - t0) * NSL - half;  // units of rank 1
+    u0 = t0 * NSL + (crank ? half : 0);
+    u1 = crank ? t1 * NSL : t0 * NSL + half;
+  } else if (cs > 1) {
     // cluster c = blockIdx.x / cs holds tile c; rank k takes slices [k, k + 1) * NSL / cs
     const int per = NSL / cs;
     u0 = int(blockIdx.x) / cs * NSL + int(crank) * per;
@@ -356,13 +378,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     u1 = int(blockIdx.x + 1) * p.ntiles / int(gridDim.x) * NSL;
   }
   const int nun = u1 - u0;
-  const UnitCursor first{u0 / NSL, u0 % NSL};
+  const int tl = crank ? tail : 0;  // this CTA's tail units (processed last)
+  const int nA = nun - tl;          // units before them
+  const UnitCursor first = nA > 0 && tl > 0 ? UnitCursor{(u0 + tl) / NSL, (u0 + tl) % NSL, nA, u0 / NSL, u0 % NSL, tl}
+                                            : UnitCursor{u0 / NSL, u0 % NSL, nun, 0, 0, 0};
   // cache mode: every slice the CTA needs has its own B slot, built once up front; stream mode (more
   // than kNB distinct slices): slot j % kNB is rebuilt for each unit
   const bool cache = NSL <= kNB || nun <= kNB;
   // slots by slice when a CTA may revisit slices (several tiles), else by unit (cluster mode: one
   // tile, slots [0, nun); its slice partials go to the free slots after them)
-  const bool by_slice = NSL <= kNB && cs == 1;
+  const bool by_slice = NSL <= kNB && (cs == 1 || PAIR);
   // B slot of unit j whose slice is sl
   auto slot_of = [&](int j, int sl) { return cache ? (by_slice ? sl : j) : (j & (kNB - 1)); };
   const int nbuild = cache ? min(nun, by_slice ? NSL : nun) : min(nun, kNB);
@@ -421,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pre = min(kNS, nun);
   UnitCursor pc = first;  // producer's cursor: the next unit to request
   if (warp == 0 && lane == 0)
-    for (int j = 0; j < pre; ++j, pc.next(NSL)) issue(j, pc);
+    for (int j = 0; j < pre; ++j, pc.template next<PAIR>(NSL)) issue(j, pc);
   pdl_trigger();
   pdl_wait();
 
@@ -588,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------- TMA producer
     if (lane == 0) {
       int j = pre;
-      for (; j < nun; ++j, pc.next(NSL)) {
+      for (; j < nun; ++j, pc.template next<PAIR>(NSL)) {
         const int st = j % kNS;
         if (*abort_flag || !mbar_wait_backoff(&bars->empty[st], ((j / kNS) & 1) ^ 1, err, 64)) break;
         fence_proxy_async();
@@ -613,7 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t bsm = smem_u32(sm + kOffB);
       bool issued = false;
       UnitCursor c = first;
-      for (int j = 0; j < nun; ++j, c.next(NSL)) {
+      for (int j = 0; j < nun; ++j, c.template next<PAIR>(NSL)) {
         const int a = j & 1;
         const int slot = slot_of(j, c.sl);
         const uint32_t bpar = cache ? 0u : uint32_t((j / kNB) & 1);
@@ -712,7 +737,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto epilogue = [&](int jj) {
       const int a = jj & 1;
       const int tile = ec.tile, sl = ec.sl;
-      ec.next(NSL);
+      ec.template next<PAIR>(NSL);
       const int slot = slot_of(jj, sl);
       const uint32_t bpar = cache ? 0u : uint32_t((jj / kNB) & 1);
       // dfull: the unit's MMAs are done; afull (already complete): orders the unpacking warp's scale /
@@ -789,7 +814,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int m = 0; m < MT; ++m) P[m] = __fadd_rn(H[m], hb[m * 128 + r]);
       __syncwarp();
       if (lane == 0 && ok) mbar_arrive(&bars->hempty[jj & 1]);
-      if (cs > 1) {
+      if (PAIR && jj >= nA) {
+        // a tail unit: its partial waits for rank 0 in this unit's weight stage (the last kNS units
+        // of a CTA leave their stages unused once unpacked)
+        float pv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int m = 0; m < MT; ++m) pv[m] = P[m];
+        *reinterpret_cast<float4*>(sm + (jj % kNS) * kStage + size_t(r) * 16) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+        return;
+      }
+      if (!PAIR && cs > 1) {
         // cluster mode: rank 0 keeps the running sum of slices [0, NSL / cs); the other ranks leave
         // each slice's partial in shared memory for rank 0, which adds them in slice order at the end
         if (crank == 0) {
@@ -826,7 +860,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
-  if (cs > 1) {
+  if (PAIR) {
+    // Pair mode: rank 0 finishes its head tile with rank 1's tail partials, in slice order, between
+    // two cluster barriers (the same rules as below).
+    cluster_sync_all();
+    if (crank == 0 && head > 0 && warp >= 12 && warp < 16) {
+      const int r = 32 * (warp & 3) + lane;
+      const int row = (u1 - 1) / NSL * R + r;
+      if (r < R && row < p.N) {
+        float4 v[kNS];
+#pragma unroll
+        for (int i = 0; i < kNS; ++i)
+          if (i < tail)
+            v[i] = ld_dsmem_v4(reinterpret_cast<const float*>(sm + ((n1 - tail + i) % kNS) * kStage + size_t(r) * 16),
+                               1u);
+#pragma unroll
+        for (int i = 0; i < kNS; ++i) {
+          if (i < tail) {
+            const float pv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+            for (int m = 0; m < MT; ++m) Y[m] = __fadd_rn(Y[m], pv[m]);
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          uint16_t o = f2bf(Y[m]);
+          const size_t oi = (size_t)m * p.ldy + row;
+          if (p.res) o = f2bf(__fadd_rn(bf2f(p.res[oi]), bf2f(o)));
+          p.y[oi] = o;
+        }
+      }
+    }
+    cluster_sync_all();
+  } else if (cs > 1) {
     // Every thread of every CTA of the cluster passes both barriers (no path leaves the kernel early,
     // and every wait above is bounded).  The first makes the ranks' slice partials visible to rank 0,
     // the second keeps every rank's shared memory alive until rank 0 has read it.
@@ -867,7 +933,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ----------------------------------------------------------------------------- host side
 struct Plan {
-  int R, G, ntiles, NSL, cs;
+  int R, G, ntiles, NSL, cs, pair;
 };
 // Tile and unit indices are 32-bit in the kernel.
 constexpr long long kMaxUnitProduct = (1LL << 31) - 1;
@@ -884,7 +950,7 @@ static std::atomic<int> g_mode{0};
 // 1.05 us per unit (16 MMAs of ~98 issue cycles each over two issuers, plus the pipeline; the weight
 // bytes of a 128-row unit stream in 0.84 us at the per-SM share of HBM bandwidth) and about 1.5 us to
 // finish a tile shared inside a cluster.  Ties go to the larger tile and to cluster mode.
-static Plan make_plan(int N, int K, int sms) {
+static Plan make_plan(int N, int K, int sms, bool allow_pair) {
   const int NSL = K / 512;
   Plan best{};
   double best_cost = 1e30;
@@ -902,7 +968,27 @@ static Plan make_plan(int N, int K, int sms) {
       const double cost = 2.0 + 0.45 * per + per * unit_us + 1.5;
       if (cost < best_cost * 0.999) {
         best_cost = cost;
-        best = Plan{R, T * cs, T, NSL, cs};
+        best = Plan{R, T * cs, T, NSL, cs, 0};
+      }
+    }
+  }
+  // pair mode: every resident 2-CTA cluster owns a run of whole tiles and splits its units between its
+  // two CTAs (a tile cut in the middle is finished by rank 0 from rank 1's partials)
+  if (mode != 1 && NSL <= kNB && allow_pair) {
+    const int ncl = max_clusters(2);
+    for (int R = kMaxRows; R >= kMinRows && ncl > 0; R -= 8) {
+      const int T = (N + R - 1) / R;
+      // up to 4 tiles a cluster: beyond that whole tiles balance well and measured faster (head: 112
+      // against 115 us at M = 3)
+      if (T < ncl || T > 4 * ncl) continue;
+      const int tpc = (T + ncl - 1) / ncl;  // most tiles a cluster owns
+      const int per = (tpc * NSL + 1) / 2;
+      const bool cut = (tpc * NSL / 2) % NSL != 0 || T % ncl != 0;
+      const double unit_us = std::max(R * 288.0 / 44.0e3, 1.05);
+      const double cost = 2.0 + 0.45 * std::min(NSL, kNB) + per * unit_us + (cut ? 1.5 : 0.5);
+      if (cost < best_cost * 0.999) {
+        best_cost = cost;
+        best = Plan{R, 2 * ncl, T, NSL, 2, 1};
       }
     }
   }
@@ -915,7 +1001,7 @@ static Plan make_plan(int N, int K, int sms) {
     const double cost = 2.0 + 0.45 * std::min(NSL, kNB) + double(per) * unit_us;
     if (cost < best_cost * 0.999) {
       best_cost = cost;
-      best = Plan{R, G, T, NSL, 1};
+      best = Plan{R, G, T, NSL, 1, 0};
     }
   }
   return best;
@@ -933,23 +1019,35 @@ static bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const v
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int MT, int PRO>
+template <int MT, int PRO, bool PAIR>
 static bool prepare() {
   static std::once_flag once;
   static bool ok = false;
   std::call_once(once, [&] {
-    ok = cudaFuncSetAttribute(qmv_tc_kernel<MT, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
+    ok = cudaFuncSetAttribute(qmv_tc_kernel<MT, PRO, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
          cudaSuccess;
   });
   return ok;
 }
 
+template <int MT, int PRO, bool PAIR>
+static int launch_variant(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb, const Params& p, int G,
+                          cudaStream_t st) {
+  if (!prepare<MT, PRO, PAIR>()) return QMTP_ERR_CUDA;
+  launch_kernel_cluster(qmv_tc_kernel<MT, PRO, PAIR>, dim3(G), dim3(kThreads), kSmem, st, p.cs, tw, ts, tb, p);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+// Pair mode is instantiated for the plain and RMSNorm prologues only (the planner offers it to those).
 template <int MT, int PRO>
 static int launch_pro(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb, const Params& p, int G,
                       cudaStream_t st) {
-  if (!prepare<MT, PRO>()) return QMTP_ERR_CUDA;
-  launch_kernel_cluster(qmv_tc_kernel<MT, PRO>, dim3(G), dim3(kThreads), kSmem, st, p.cs, tw, ts, tb, p);
-  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+  if constexpr (PRO == kProNone || PRO == kProRms) {
+    if (p.pair) return launch_variant<MT, PRO, true>(tw, ts, tb, p, G, st);
+  } else {
+    if (p.pair) return QMTP_ERR_UNSUPPORTED;
+  }
+  return launch_variant<MT, PRO, false>(tw, ts, tb, p, G, st);
 }
 
 template <int MT>
@@ -972,7 +1070,7 @@ static int max_clusters(int cs) {
   int& c = cache[cs == 4 ? 1 : 0][dev];
   if (c == 0) {
     int n = 0;
-    if (prepare<1, kProNone>()) {
+    if (prepare<1, kProNone, false>()) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(unsigned(cs));
       cfg.blockDim = dim3(kThreads);
@@ -984,7 +1082,7 @@ static int max_clusters(int cs) {
       at[0].val.clusterDim.z = 1;
       cfg.attrs = at;
       cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&n, qmv_tc_kernel<1, kProNone>, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, qmv_tc_kernel<1, kProNone, false>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         n = 0;
       }
@@ -1033,7 +1131,7 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
     default:
       return QMTP_ERR_ARG;
   }
-  const Plan pl = make_plan(N, K, sm_count());
+  const Plan pl = make_plan(N, K, sm_count(), pr.pro == kProNone || pr.pro == kProRms);
   if ((long long)pl.ntiles * (pl.G + 1) > kMaxUnitProduct || (long long)pl.ntiles * pl.NSL > kMaxUnitProduct)
     return QMTP_ERR_SHAPE;
   CUtensorMap tw, ts, tb;
@@ -1050,6 +1148,7 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
   p.R = pl.R;
   p.ntiles = pl.ntiles;
   p.cs = pl.cs;
+  p.pair = pl.pair;
   p.nw = static_cast<const uint16_t*>(pr.nw);
   p.eps = pr.eps;
   p.ldz = pr.ldz;
@@ -1076,7 +1175,7 @@ int qmv_tc(const void* x, long long ldx, const void* w, const void* s, const voi
 }
 
 int qmv_tc_plan(int N, int K, int* rows, int* grid, int* units, int* cluster) {
-  const tq::Plan pl = tq::make_plan(N, K, sm_count());
+  const tq::Plan pl = tq::make_plan(N, K, sm_count(), true);
   if (rows) *rows = pl.R;
   if (grid) *grid = pl.G;
   if (units) *units = int((long long)pl.ntiles * pl.NSL);

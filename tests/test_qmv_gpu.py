@@ -95,12 +95,15 @@ def test_qmv_affine_decoder_shapes(N, K, dev, planner):
         plan = _lib.qmv_plan(N, K, True)
         T = (N + plan["rows_per_tile"] - 1) // plan["rows_per_tile"]
         assert plan["units"] == T * (K // 512)
-        if plan["cluster"] > 1:
-            assert plan["grid"] == T * plan["cluster"] and (K // 512) % plan["cluster"] == 0
+        if plan["cluster"] > 1:  # one tile per cluster, or pair mode (2-CTA clusters owning tile runs)
+            one_tile = plan["grid"] == T * plan["cluster"] and (K // 512) % plan["cluster"] == 0
+            assert one_tile or (plan["cluster"] == 2 and plan["grid"] < 2 * T), plan
         if mode == 2 and N == 4096:
             assert plan["cluster"] > 1, plan
         if mode == 1:
             assert plan["cluster"] == 1 and plan["grid"] <= T
+        if mode == 2 and N >= 10240 and K <= 4096:
+            assert plan["cluster"] == 2 and plan["grid"] == 148, plan  # pair mode (148 SMs: 74 pairs)
 
 
 def test_qmv_affine_residual_in_place(dev, planner):
@@ -320,3 +323,23 @@ def test_qmv_affine_gated_prologue(M, dev, planner):
         out = to_torch(res, dev)
         qmv_kernel.qmv_affine_gated(yt, zt, nt, 1e-6, wt, st, bt, out=out, res=out)
         assert np.array_equal(to_np(out), ref_res), (mode, "res")
+
+
+@pytest.mark.parametrize("K", [512, 1024, 2048, 4096])
+@pytest.mark.parametrize("M", [1, 3, 4])
+def test_qmv_affine_pair_mode_tails(K, M, dev, planner):
+    """Pair mode (2-CTA clusters owning runs of tiles; a tile cut in the middle is finished by rank 0
+    from rank 1's partials) for every slice count up to 8: tile counts just above the cluster count
+    give clusters with one tile (cut in half), two and three tiles, with a residual."""
+    from qmtp import qmv_kernel
+
+    for N in (9500, 21000):
+        _, wq, s, b = affine_layer(N, K, seed=N + K + M)
+        x = randn_bf16((M, K), 3 + M)
+        res = randn_bf16((M, N), 4)
+        ref = ops.qmv_affine(x, wq, s, b)
+        ref_res = ops.f32_to_bf16(ops.bf16_to_f32(res) + ops.bf16_to_f32(ref))
+        for mode in (2, 0):
+            planner(mode)
+            assert np.array_equal(_run_affine(x, wq, s, b, dev), ref), (N, mode)
+            assert np.array_equal(_run_affine(x, wq, s, b, dev, res=res), ref_res), (N, mode, "res")
