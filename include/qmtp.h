@@ -197,9 +197,26 @@ typedef struct qmtp_gdn_args {
   int ring_slots;            /* > S */
   float* y;                  /* fp32 [S, Hv, Dv] */
   int S, Hk, Hv, Dk, Dv, KC, snap;
+  /* Optional gated RMS norm of the same step (gdn_fused.py:114-129, qmtp_gdn_norm_gate below):
+   * gate_out bf16 [S, >= Hv*Dv] (row stride ld_gate_out) = bf16(R(gate_w * R(y * r)) * silu(gate_z)),
+   * gate_z bf16 [S, >= Hv*Dv] (row stride ld_gate_z), gate_w bf16 [Dv].  NULL gate_out: no norm.
+   * With the decode shape (S <= 4, KC == 4, Dk == Dv == 128, 16-byte aligned conv_w, 8-byte aligned
+   * window rows) the norm runs inside the step's launch (an 8-CTA cluster per value head sums
+   * y^2 over distributed shared memory); otherwise as a second launch. */
+  const void* gate_z;
+  long long ld_gate_z;
+  const void* gate_w;
+  void* gate_out;
+  long long ld_gate_out;
+  float gate_eps;
 } qmtp_gdn_args;
 
 int qmtp_gdn_fused_ex(const qmtp_gdn_args* args, void* stream);
+
+/* Kernel choice of qmtp_gdn_fused / qmtp_gdn_fused_ex, for tests: 0 = automatic (the decode-shape
+ * kernel where it applies), 1 = always the general kernel (and a separate gated-norm launch).  Both
+ * give the same bits.  Returns the previous mode. */
+int qmtp_gdn_set_mode(int mode);
 
 /* Gated RMS norm of gdn_fused.py:114-129 (gdn_norm_gate): per (token, head) row of Dv,
  * out = bf16(R(w * R(y * r)) * silu_f32(z)), r = 1/sqrt(mean(y^2) + eps).

@@ -342,6 +342,274 @@ gdn_norm_gate_kernel(const float* __restrict__ y, const uint16_t* __restrict__ z
   }
 }
 
+// ----------------------------------------------------------------------------- decode shape
+// The verify step of the decode loop: S <= 4 tokens, KC == 4 taps, Dk == Dv == 128.  Same
+// arithmetic as gdn_fused_kernel (+ gdn_norm_gate_kernel with GATE), laid out for latency:
+//  * constants (conv taps, A_log, dt_bias, the norm weight) are loaded before the dependency wait;
+//  * warps 0..2S-1 each own one (token, q|k) vector: lane l convolves channels 4l..4l+3 from 8-byte
+//    window loads, then the warp applies the RMS norm itself (the fma chain over the lane's 4
+//    channels and the xor butterfly of gdn_fused_kernel's phase 2), so no barrier separates conv
+//    and norm;
+//  * warp 8 convolves the CTA's 16 v channels (and, with GATE, computes silu(z) of its outputs),
+//    warp 9 the gates: neither sits on a q/k warp's path;
+//  * the next conv window is written from the registers the convolution loaded (q/k channels by one
+//    CTA of the key head, v channels by their owner);
+//  * GATE: the 8 CTAs of a value head form a cluster; after the delta rule each holds its 16 rows of
+//    y in shared memory, and a warp per token reads the head's 128 values over distributed shared
+//    memory in gdn_norm_gate_kernel's lane order (lane l: rows 4l..4l+3).
+// Grid (Dv / 16, Hv), 320 threads.
+constexpr int kDecS = 4, kDecKC = 4, kDecRows = 16, kDecVWarp = 8, kDecGWarp = 9, kDecWarps = 10;
+
+template <bool GATE>
+__global__ void __launch_bounds__(kDecWarps * 32)
+gdn_decode_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
+  pdl_trigger();
+  constexpr int Dk = 128, Dv = 128, NP = 4, KC = kDecKC;
+  __shared__ __align__(16) float qk[2 * kDecS][Dk];  // [t][q|k][Dk], normalised
+  __shared__ float vs[kDecS][kDecRows];
+  __shared__ float gs[kDecS], bs[kDecS];
+  __shared__ __align__(16) float ys[kDecS][kDecRows];
+  __shared__ float gz[kDecS][kDecRows];
+  __shared__ float rs[kDecS];
+  const int S = A.S, Hk = A.Hk, Hv = A.Hv;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hv = blockIdx.y, dv0 = blockIdx.x * kDecRows;
+  const int rep = Hv / Hk, hk = hv / rep;
+  const long long C = 2LL * Hk * Dk + (long long)Hv * Dv;
+  const uint16_t* conv_src = static_cast<const uint16_t*>(A.conv_src);
+  const uint16_t* qkv = static_cast<const uint16_t*>(A.qkv);
+  const uint16_t* conv_w = static_cast<const uint16_t*>(A.conv_w);
+  const bool vec = warp < 2 * S;
+  const int tv = warp >> 1, isk = warp & 1;
+  const long long chq = (long long)isk * Hk * Dk + (long long)hk * Dk + NP * lane;  // first of 4 channels
+  const long long chv = 2LL * Hk * Dk + (long long)hv * Dv + dv0 + (lane & 15);
+
+  // ---- constants (model weights; no kernel of the decode writes them)
+  uint32_t cw[8] = {};  // vec: taps of channels chq..chq+3 (bf16 pairs); v warp: cw[0..1] = taps of chv
+  float Aneg = 0.0f, dtb = 0.0f, nw = 0.0f;
+  if (vec) {
+    const uint4 c0 = *reinterpret_cast<const uint4*>(conv_w + chq * KC);
+    const uint4 c1 = *reinterpret_cast<const uint4*>(conv_w + chq * KC + 8);
+    cw[0] = c0.x; cw[1] = c0.y; cw[2] = c0.z; cw[3] = c0.w; cw[4] = c1.x; cw[5] = c1.y; cw[6] = c1.z; cw[7] = c1.w;
+  } else if (warp == kDecVWarp && lane < kDecRows) {
+    const uint2 c = *reinterpret_cast<const uint2*>(conv_w + chv * KC);
+    cw[0] = c.x; cw[1] = c.y;
+  } else if (warp == kDecGWarp && lane < S) {
+    Aneg = -q_expf(A.A_log[hv]);
+    dtb = bf2f(static_cast<const uint16_t*>(A.dt_bias)[hv]);
+  }
+  if (GATE && tid < S * kDecRows) nw = bf2f(static_cast<const uint16_t*>(A.gate_w)[dv0 + (tid & 15)]);
+  pdl_wait();
+
+  const int off = A.conv_row_off ? *A.conv_row_off : 0;
+  const size_t per = size_t(Hv) * Dv * Dk;
+  const float* sin = A.state_in;
+  int cur = 0;
+  if (A.ring) {
+    cur = *A.ring_cur;
+    if (cur < 0 || cur >= A.ring_slots) {  // uniform over the grid: every CTA leaves here
+      if (tid == 0) atomicOr(err, DEVERR_BADARG);
+      return;
+    }
+    sin = A.ring + size_t(cur) * per;
+  }
+  // phase-3 state rows (warps 0..7, rows dv0 + 2w, 2w + 1): independent of the convolution
+  float st[2][NP];
+  if (warp < 8) {
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const float4 s4 = *reinterpret_cast<const float4*>(sin + (size_t(hv) * Dv + dv0 + 2 * warp + rr) * Dk + NP * lane);
+      st[rr][0] = s4.x; st[rr][1] = s4.y; st[rr][2] = s4.z; st[rr][3] = s4.w;
+    }
+  }
+  uint16_t* wo = A.win_out ? static_cast<uint16_t*>(A.win_out) +
+                                 (long long)(A.win_out_row_off ? *A.win_out_row_off : 0) * C
+                           : nullptr;
+
+  if (vec) {
+    // ---- phase 1+2 for vector (tv, isk): window rows tv..tv+3 of channels chq..chq+3
+    uint2 wr[KC];
+#pragma unroll
+    for (int j = 0; j < KC; ++j) {
+      const int r = tv + j;
+      const uint16_t* p = r < KC - 1 ? conv_src + (long long)(off + r) * A.ld_conv + chq
+                                     : qkv + (long long)(r - (KC - 1)) * A.ld_qkv + chq;
+      wr[j] = *reinterpret_cast<const uint2*>(p);
+    }
+    float x[NP];
+#pragma unroll
+    for (int c = 0; c < NP; ++c) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int j = 0; j < KC; ++j) {
+        const uint32_t tw = cw[2 * c + (j >> 1)];
+        const float tap = (j & 1) ? bfhi(tw) : bflo(tw);
+        const uint32_t ww = (c < 2) ? wr[j].x : wr[j].y;
+        const float wv = (c & 1) ? bfhi(ww) : bflo(ww);
+        acc = __fmaf_rn(tap, wv, acc);
+      }
+      x[c] = silu_bf(R(acc));
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NP; ++c) ss = __fmaf_rn(x[c], x[c], ss);
+    ss = warp_sum(ss);
+    const float r = rsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / float(Dk)), 1e-6f));
+    const float kscale = R(rsqrt_rn(float(Dk)));
+    float o[NP];
+#pragma unroll
+    for (int c = 0; c < NP; ++c)
+      o[c] = isk ? R(__fmul_rn(R(__fmul_rn(x[c], r)), kscale)) : __fmul_rn(R(__fmul_rn(x[c], r)), 1.0f / float(Dk));
+    *reinterpret_cast<float4*>(&qk[warp][NP * lane]) = make_float4(o[0], o[1], o[2], o[3]);
+    // next window, q/k channels: written by the first CTA of the key head (token 0's warp the rows
+    // 0..KC-1, token t's warp row t+KC-1)
+    if (wo && hv == hk * rep && blockIdx.x == 0) {
+      if (tv == 0) {
+#pragma unroll
+        for (int j = 0; j < KC; ++j) *reinterpret_cast<uint2*>(wo + j * C + chq) = wr[j];
+      } else {
+        *reinterpret_cast<uint2*>(wo + (tv + KC - 1) * C + chq) = wr[KC - 1];
+      }
+    }
+  } else if (warp == kDecVWarp) {
+    if (lane < kDecRows) {
+      // ---- v channel chv over the S tokens (rows 0..KC-2+S of the window)
+      uint16_t wv[KC - 1 + kDecS];
+#pragma unroll
+      for (int r = 0; r < KC - 1 + kDecS; ++r)
+        if (r < KC - 1 + S)
+          wv[r] = r < KC - 1 ? conv_src[(long long)(off + r) * A.ld_conv + chv]
+                             : qkv[(long long)(r - (KC - 1)) * A.ld_qkv + chv];
+#pragma unroll
+      for (int t = 0; t < kDecS; ++t)
+        if (t < S) {
+          float acc = 0.0f;
+#pragma unroll
+          for (int j = 0; j < KC; ++j) {
+            const float tap = (j & 1) ? bfhi(cw[j >> 1]) : bflo(cw[j >> 1]);
+            acc = __fmaf_rn(tap, bf2f(wv[t + j]), acc);
+          }
+          vs[t][lane] = silu_bf(R(acc));
+        }
+      if (wo) {
+#pragma unroll
+        for (int r = 0; r < KC - 1 + kDecS; ++r)
+          if (r < KC - 1 + S) wo[r * C + chv] = wv[r];
+      }
+    } else if (GATE) {
+      // ---- silu(z) of the gated norm's outputs (token t, row dv0 + d)
+      const int d = lane - kDecRows;
+      const uint16_t* z = static_cast<const uint16_t*>(A.gate_z);
+#pragma unroll
+      for (int t = 0; t < kDecS; ++t)
+        if (t < S) gz[t][d] = silu_f32(bf2f(z[(long long)t * A.ld_gate_z + (long long)hv * Dv + dv0 + d]));
+    }
+  } else if (warp == kDecGWarp && lane < S) {
+    // ---- gates of token t = lane
+    const uint16_t* av = static_cast<const uint16_t*>(A.a);
+    const uint16_t* bv = static_cast<const uint16_t*>(A.b);
+    const float sp = softplus_bf(R(__fadd_rn(bf2f(av[(long long)lane * A.ld_ab + hv]), dtb)));
+    gs[lane] = q_expf(__fmul_rn(Aneg, sp));
+    bs[lane] = sigmoid_bf(bf2f(bv[(long long)lane * A.ld_ab + hv]));
+  }
+  __syncthreads();
+
+  // ---- phase 3: delta rule for rows dv0 + 2w + rr (same sequence as gdn_fused_kernel's decode path)
+  if (warp < 8) {
+    float op[kDecS][2];
+#pragma unroll
+    for (int t = 0; t < kDecS; ++t) {
+      if (t >= S) break;
+      const float4 q4 = *reinterpret_cast<const float4*>(&qk[2 * t][NP * lane]);
+      const float4 k4 = *reinterpret_cast<const float4*>(&qk[2 * t + 1][NP * lane]);
+      const float qf[4] = {q4.x, q4.y, q4.z, q4.w}, kf[4] = {k4.x, k4.y, k4.z, k4.w};
+      const float gt = gs[t], bt = bs[t];
+      float* dst = nullptr;
+      if (A.ring) {
+        if (A.snap || t == S - 1) dst = A.ring + size_t((cur + t + 1) % A.ring_slots) * per;
+      } else if (t == S - 1) {
+        dst = A.state_out;
+      } else if (A.snap && A.state_mid) {
+        dst = A.state_mid + size_t(t) * per;
+      }
+      float kv[2];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        kv[rr] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          st[rr][i] = __fmul_rn(st[rr][i], gt);
+          kv[rr] = __fmaf_rn(st[rr][i], kf[i], kv[rr]);
+        }
+      }
+#pragma unroll
+      for (int d = 16; d >= 1; d >>= 1)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) kv[rr] = __fadd_rn(kv[rr], __shfl_xor_sync(0xFFFFFFFFu, kv[rr], d));
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int d = 2 * warp + rr;
+        const float delta = __fmul_rn(__fsub_rn(vs[t][d], kv[rr]), bt);
+        op[t][rr] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          st[rr][i] = __fmaf_rn(kf[i], delta, st[rr][i]);
+          op[t][rr] = __fmaf_rn(st[rr][i], qf[i], op[t][rr]);
+        }
+        if (dst)
+          *reinterpret_cast<float4*>(dst + (size_t(hv) * Dv + dv0 + d) * Dk + NP * lane) =
+              make_float4(st[rr][0], st[rr][1], st[rr][2], st[rr][3]);
+      }
+    }
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1)
+#pragma unroll
+      for (int t = 0; t < kDecS; ++t)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+          if (t < S) op[t][rr] = __fadd_rn(op[t][rr], __shfl_xor_sync(0xFFFFFFFFu, op[t][rr], d));
+    if (lane == 0) {
+#pragma unroll
+      for (int t = 0; t < kDecS; ++t)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+          if (t < S) {
+            const float yv = R(op[t][rr]);
+            A.y[(size_t(t) * Hv + hv) * Dv + dv0 + 2 * warp + rr] = yv;
+            if (GATE) ys[t][2 * warp + rr] = yv;
+          }
+    }
+  }
+  if (GATE) {
+    // ---- gated norm: r_t from the value head's 128 values of y, gathered over the cluster
+    __syncwarp();
+    cluster_sync_all();
+    if (warp < S) {
+      const float4 v = ld_dsmem_v4(&ys[warp][4 * (lane & 3)], uint32_t(lane >> 2));
+      float ss = 0.0f;
+      ss = __fmaf_rn(v.x, v.x, ss);
+      ss = __fmaf_rn(v.y, v.y, ss);
+      ss = __fmaf_rn(v.z, v.z, ss);
+      ss = __fmaf_rn(v.w, v.w, ss);
+      ss = warp_sum(ss);
+      if (lane == 0) rs[warp] = rsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / float(Dv)), A.gate_eps));
+    }
+    __syncwarp();
+    cluster_arrive_release();  // this CTA's remote reads are done
+    __syncthreads();
+    if (tid < S * kDecRows) {
+      const int t = tid >> 4, d = tid & 15;
+      const float xn = R(__fmul_rn(nw, R(__fmul_rn(ys[t][d], rs[t]))));
+      static_cast<uint16_t*>(A.gate_out)[(long long)t * A.ld_gate_out + (long long)hv * Dv + dv0 + d] =
+          f2bf(__fmul_rn(xn, gz[t][d]));
+    }
+    __syncwarp();
+    cluster_wait_acquire();  // no CTA leaves while a peer may still read its ys
+  }
+}
+
+static int g_gdn_mode = 0;
+
 }  // namespace qmtp
 
 using namespace qmtp;
@@ -376,10 +644,40 @@ extern "C" int qmtp_gdn_fused_ex(const qmtp_gdn_args* args, void* stream) {
   const void* sp[] = {A.state_in, A.state_out, A.state_mid, A.ring};
   for (const void* p : sp)
     if (p && !aligned16(p)) return QMTP_ERR_ALIGN;
+  const bool gate = A.gate_out != nullptr;
+  if (gate && (!A.gate_z || !A.gate_w)) return QMTP_ERR_ARG;
+  if (gate && (A.Dv != 128 || A.ld_gate_z < (long long)A.Hv * A.Dv || A.ld_gate_out < (long long)A.Hv * A.Dv))
+    return QMTP_ERR_SHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto a8 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; };
+  const long long C = 2LL * A.Hk * A.Dk + (long long)A.Hv * A.Dv;
+  const bool decode = g_gdn_mode == 0 && A.S <= kDecS && A.KC == kDecKC && A.Dv == 128 && aligned16(A.conv_w) &&
+                      a8(A.conv_src) && a8(A.qkv) && A.ld_conv % 4 == 0 && A.ld_qkv % 4 == 0 && C % 4 == 0 &&
+                      (!A.win_out || a8(A.win_out));
+  if (decode) {
+    const dim3 grid(128 / kDecRows, A.Hv), block(kDecWarps * 32);
+    if (gate)
+      launch_kernel_cluster(gdn_decode_kernel<true>, grid, block, 0, st, 128 / kDecRows, A, device_error_ptr());
+    else
+      launch_kernel(gdn_decode_kernel<false>, grid, block, 0, st, A, device_error_ptr());
+    return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+  }
   const size_t smem = size_t(A.S) * (2 * 128 + kFusedDVB + 2) * sizeof(float);
   dim3 grid(A.Hv, (A.Dv + kFusedDVB - 1) / kFusedDVB);
-  launch_kernel(gdn_fused_kernel<4>, dim3(grid), dim3(kFusedWarps * 32), smem, static_cast<cudaStream_t>(stream), A, device_error_ptr());
+  launch_kernel(gdn_fused_kernel<4>, dim3(grid), dim3(kFusedWarps * 32), smem, st, A, device_error_ptr());
+  if (cudaGetLastError() != cudaSuccess) return QMTP_ERR_CUDA;
+  if (!gate) return QMTP_OK;
+  const int rows = A.S * A.Hv, wpb = 8;
+  launch_kernel(gdn_norm_gate_kernel<4>, dim3((rows + wpb - 1) / wpb), dim3(wpb * 32), 0, st, static_cast<const float*>(A.y),
+                static_cast<const uint16_t*>(A.gate_z), A.ld_gate_z, static_cast<const uint16_t*>(A.gate_w),
+                static_cast<uint16_t*>(A.gate_out), A.ld_gate_out, A.S, A.Hv, A.gate_eps);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_gdn_set_mode(int mode) {
+  const int prev = g_gdn_mode;
+  if (mode == 0 || mode == 1) g_gdn_mode = mode;
+  return prev;
 }
 
 extern "C" int qmtp_gdn_fused(const void* win, const void* conv_w, const void* a, const void* b, int ld_ab,

@@ -58,13 +58,16 @@ class GdnArgs(ctypes.Structure):
                 ("state_in", _P), ("state_out", _P), ("state_mid", _P),
                 ("ring", _P), ("ring_cur", _P), ("ring_slots", _I),
                 ("y", _P),
-                ("S", _I), ("Hk", _I), ("Hv", _I), ("Dk", _I), ("Dv", _I), ("KC", _I), ("snap", _I)]
+                ("S", _I), ("Hk", _I), ("Hv", _I), ("Dk", _I), ("Dv", _I), ("KC", _I), ("snap", _I),
+                ("gate_z", _P), ("ld_gate_z", ctypes.c_longlong), ("gate_w", _P), ("gate_out", _P),
+                ("ld_gate_out", ctypes.c_longlong), ("gate_eps", _F)]
 
 
 SIGNATURES.update({
     "qmtp_gdn_step": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
     "qmtp_gdn_fused": [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
     "qmtp_gdn_fused_ex": [ctypes.POINTER(GdnArgs), _P],
+    "qmtp_gdn_set_mode": [_I],
     "qmtp_gdn_norm_gate": [_P, _P, _I, _P, _P, _I, _I, _I, _I, _F, _P],
     "qmtp_lmhead2": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     "qmtp_topk_rescore": [_P, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t, _P],

@@ -11,6 +11,8 @@ A_log (fp32 [Hv]), dt_bias (bf16 [Hv]), norm_weight (bf16 [Dv]) and norm_eps.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -58,8 +60,36 @@ def gdn_norm_gate(y, z, weight, eps, out=None):
 
 def gdn_middle(layer, qkv, z, a, b, conv_state, state, snap):
     """gdn_fused.py:149: qkv [1,S,C], z [1,S,Hv,Dv], a/b [1,S,Hv], conv_state [1,KC-1,C],
-    state [1,Hv,Dv,Dk] -> (out [1,S,Hv*Dv] bf16, conv window [1,S+KC-1,C], state, snapshots)."""
-    win = torch.cat([conv_state, qkv], dim=1)
-    y, st, mids = gdn_core(layer, win, a, b, state, snap)
-    out = gdn_norm_gate(y, z, layer.norm_weight, layer.norm_eps)
+    state [1,Hv,Dv,Dk] -> (out [1,S,Hv*Dv] bf16, conv window [1,S+KC-1,C], state, snapshots).
+
+    One qmtp_gdn_fused_ex call with the gated norm attached: at the decode shape (S <= 4) a single
+    launch, otherwise the core and gdn_norm_gate as two."""
+    Hk, Hv, Dk, Dv, KC = (layer.num_k_heads, layer.num_v_heads, layer.head_k_dim, layer.head_v_dim,
+                          layer.conv_kernel_size)
+    win = torch.cat([conv_state, qkv], dim=1).contiguous()
+    S, C = win.shape[-2] - (KC - 1), win.shape[-1]
+    a2, b2 = a.reshape(S, -1), b.reshape(S, -1)
+    if a2.stride(0) != b2.stride(0) or a2.stride(1) != 1 or b2.stride(1) != 1:
+        a2, b2 = a2.contiguous(), b2.contiguous()
+    z2 = z.reshape(S, Hv * Dv)
+    if z2.stride(1) != 1:
+        z2 = z2.contiguous()
+    state = state.to(torch.float32).contiguous()
+    _lib.require_cuda(win, state, layer.norm_weight)
+    if not z2.is_cuda:
+        raise RuntimeError("qmtp ops run on CUDA tensors only (no CPU fallback)")
+    dev = win.device
+    y = torch.empty((S, Hv, Dv), dtype=torch.float32, device=dev)
+    st = torch.empty_like(state)
+    mids = torch.empty((max(S - 1, 1), *state.shape), dtype=torch.float32, device=dev)
+    out = torch.empty((1, S, Hv * Dv), dtype=torch.bfloat16, device=dev)
+    A = _lib.GdnArgs(conv_src=win.data_ptr(), ld_conv=C, conv_row_off=None, qkv=win.data_ptr() + 2 * (KC - 1) * C,
+                     ld_qkv=C, win_out=None, win_out_row_off=None, conv_w=layer.conv1d_weight.data_ptr(),
+                     a=a2.data_ptr(), b=b2.data_ptr(), ld_ab=a2.stride(0), A_log=layer.A_log.data_ptr(),
+                     dt_bias=layer.dt_bias.data_ptr(), state_in=state.data_ptr(), state_out=st.data_ptr(),
+                     state_mid=mids.data_ptr(), ring=None, ring_cur=None, ring_slots=0, y=y.data_ptr(), S=S, Hk=Hk,
+                     Hv=Hv, Dk=Dk, Dv=Dv, KC=KC, snap=int(bool(snap)), gate_z=z2.data_ptr(), ld_gate_z=z2.stride(0),
+                     gate_w=layer.norm_weight.data_ptr(), gate_out=out.data_ptr(), ld_gate_out=Hv * Dv,
+                     gate_eps=float(layer.norm_eps))
+    _lib.check(_lib.lib().qmtp_gdn_fused_ex(ctypes.byref(A), _lib.stream()), "gdn_middle")
     return out, win, st, mids

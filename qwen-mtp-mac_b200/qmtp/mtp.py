@@ -242,7 +242,18 @@ class MTPDecoder:
             A_log=L["A_log"].data_ptr(), dt_bias=L["dt_bias"].data_ptr(), state_in=None, state_out=None,
             state_mid=None, ring=self.ring[i].data_ptr(), ring_cur=self._cp(C["SLOT"]), ring_slots=self.slots,
             y=self.ygdn.data_ptr(), S=self.S, Hk=a.lin_hk, Hv=a.lin_hv, Dk=a.lin_dk, Dv=a.lin_dv, KC=a.conv_k,
-            snap=1)
+            snap=1,
+            # the gated norm (gdn_fused.py:114-129) in the same call: z = the in_proj rows after qkv
+            gate_z=p + 2 * Cd, ld_gate_z=ldp, gate_w=L["norm"].data_ptr(), gate_out=self.gdn_out.data_ptr(),
+            ld_gate_out=Z, gate_eps=a.eps)
+
+    def _gdn_launches(self, i):
+        """Kernels one qmtp_gdn_fused_ex call of layer i launches: 1 where the decode-shape kernel
+        applies (it folds the gated norm), else the general core plus the gated norm."""
+        a, g = self.a, self._gdn_args[i]
+        decode = (self.S <= 4 and a.conv_k == 4 and a.lin_dk == 128 and a.lin_dv == 128 and g.conv_w % 16 == 0
+                  and g.conv_src % 8 == 0 and g.qkv % 8 == 0 and g.ld_conv % 4 == 0 and g.ld_qkv % 4 == 0)
+        return 1 if decode else 2
 
     # ------------------------------------------------------------------ layers
     def _attn_layer(self, L, x, rows, kc, vc, pos_slot):
@@ -280,12 +291,9 @@ class MTPDecoder:
             self._norm(self.h, L["input_ln"], self.xn, S)
             if a.is_linear(i):
                 self._qmv(self.xn, L["in_proj"], self.proj, S, ldy=self.proj.shape[1])
-                self._chk(self.L.qmtp_gdn_fused_ex(ctypes.byref(self._gdn_args[i]), self._st()), "gdn")
-                Z = a.lin_hv * a.lin_dv
-                self._chk(self.L.qmtp_gdn_norm_gate(self.ygdn.data_ptr(), self.proj.data_ptr() + 2 * a.conv_dim,
-                                                    self.proj.shape[1], L["norm"].data_ptr(),
-                                                    self.gdn_out.data_ptr(), Z, S, a.lin_hv, a.lin_dv, a.eps,
-                                                    self._st()), "norm_gate")
+                # conv, norms, gates, delta rule, snapshots and the gated norm into self.gdn_out
+                self.launches += self._gdn_launches(i)
+                self._chk(self.L.qmtp_gdn_fused_ex(ctypes.byref(self._gdn_args[i]), self._st()), "gdn_ex")
                 self._qmv(self.gdn_out, L["out_proj"], self.h, S, res=self.h)
             else:
                 kc, vc = self.kv[i]
