@@ -321,7 +321,6 @@ def run_kernel(args):
     import torch
 
     from qmtp import _lib, qmv_kernel
-    from qmtp.gdn_fused import gdn_core
     from qmtp.lm_head2 import TwoStageHead
 
     dev = torch.device("cuda", 0)
@@ -359,20 +358,38 @@ def run_kernel(args):
     elif args.kernel == "gdn":
         S, Hk, Hv, D, KC = 3, 16, 32, 128, 4
         Cd = 2 * Hk * D + Hv * D
-        copies = 16
-        states = [torch.randn(1, Hv, D, D, generator=g, device=dev) * 0.1 for _ in range(copies)]
-        win = torch.randn(1, S + KC - 1, Cd, generator=g, device=dev).to(torch.bfloat16)
-        ab = torch.randn(1, S, 2 * Hv, generator=g, device=dev).to(torch.bfloat16)
+        copies = 16  # 16 rings of 4 x 2 MiB states in rotation (> L2)
 
-        class Layer:
-            num_k_heads, num_v_heads, head_k_dim, head_v_dim, conv_kernel_size = Hk, Hv, D, D, KC
-            conv1d_weight = (torch.randn(Cd, KC, generator=g, device=dev) * 0.5).to(torch.bfloat16)
-            A_log = torch.log(torch.rand(Hv, generator=g, device=dev) * 15 + 1)
-            dt_bias = torch.randn(Hv, generator=g, device=dev).to(torch.bfloat16)
+        # the decoder's form (MTPDecoder._make_gdn_args): state ring with a snapshot per token, conv rows
+        # at a device row offset, the next window written back, the gated norm attached
+        conv_w = (torch.randn(Cd, KC, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        A_log = torch.log(torch.rand(Hv, generator=g, device=dev) * 15 + 1)
+        dt_bias = torch.randn(Hv, generator=g, device=dev).to(torch.bfloat16)
+        norm_w = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+        Z = Hv * D
+        ldp = Cd + Z + 2 * Hv
+        proj = torch.randn(S, ldp, generator=g, device=dev).to(torch.bfloat16)
+        slots = S + 1
+        rings = [torch.randn(slots, Hv, D, D, generator=g, device=dev) * 0.1 for _ in range(copies)]
+        wins = [torch.randn(2 * (S + KC - 1), Cd, generator=g, device=dev).to(torch.bfloat16) for _ in range(copies)]
+        ctrl = torch.tensor([0, S + KC - 1, 0], dtype=torch.int32, device=dev)  # slot, conv row, window-out row
+        y_ = torch.empty(S, Hv, D, dtype=torch.float32, device=dev)
+        gout = torch.empty(S, Z, dtype=torch.bfloat16, device=dev)
+        gargs = [_lib.GdnArgs(conv_src=wins[i].data_ptr(), ld_conv=Cd, conv_row_off=ctrl.data_ptr() + 4,
+                              qkv=proj.data_ptr(), ld_qkv=ldp, win_out=wins[i].data_ptr(),
+                              win_out_row_off=ctrl.data_ptr() + 8, conv_w=conv_w.data_ptr(),
+                              a=proj.data_ptr() + 2 * (Cd + Z + Hv), b=proj.data_ptr() + 2 * (Cd + Z), ld_ab=ldp,
+                              A_log=A_log.data_ptr(), dt_bias=dt_bias.data_ptr(), ring=rings[i].data_ptr(),
+                              ring_cur=ctrl.data_ptr(), ring_slots=slots, y=y_.data_ptr(), S=S, Hk=Hk, Hv=Hv, Dk=D,
+                              Dv=D, KC=KC, snap=1, gate_z=proj.data_ptr() + 2 * Cd, ld_gate_z=ldp,
+                              gate_w=norm_w.data_ptr(), gate_out=gout.data_ptr(), ld_gate_out=Z, gate_eps=1e-6)
+                 for i in range(copies)]
+        import ctypes
 
-        run = lambda i: gdn_core(Layer, win, ab[..., :Hv], ab[..., Hv:], states[i % copies], snap=True)
-        unit_bytes = Hv * D * D * 4 * (1 + S) + (S + KC - 1) * Cd * 2 + S * Hv * D * 4
-        label = "GatedDeltaNet fused verify step T=3 (snapshots)"
+        run = lambda i: _lib.check(_lib.lib().qmtp_gdn_fused_ex(ctypes.byref(gargs[i % copies]), _lib.stream()),
+                                   "gdn_fused_ex")
+        unit_bytes = Hv * D * D * 4 * (1 + S) + (S + KC - 1) * Cd * 2 * 2 + S * Z * 2 * 2 + S * Hv * D * 4
+        label = "GatedDeltaNet verify step T=3 (ring snapshots, window write-back, gated norm)"
     elif args.kernel == "moe":
         from qmtp import moe
 

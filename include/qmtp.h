@@ -209,6 +209,12 @@ typedef struct qmtp_gdn_args {
   void* gate_out;
   long long ld_gate_out;
   float gate_eps;
+  /* Nonzero: the control words, the state (state_in or the ring slot) and the conv rows at conv_src
+   * are read before the kernel's dependency wait, overlapping the previous launch.  Only valid when
+   * none of them was written by the launch directly before this one on the stream, and that launch
+   * is a libqmtp GEMV (qmtp_qmv_*: it signals its successor only after its own dependency wait), or
+   * there is no programmatic dependency at all.  The decoder's in_proj -> step sequence qualifies. */
+  int preload;
 } qmtp_gdn_args;
 
 int qmtp_gdn_fused_ex(const qmtp_gdn_args* args, void* stream);

@@ -25,6 +25,9 @@ namespace qmtp {
 // the only exception: the qmv kernel prefetches them before the wait), and pdl_trigger() early so
 // its own successor can start its prologue.  Calling pdl_wait() in every kernel keeps the chain
 // transitive (a kernel finishing implies all earlier kernels finished).  QMTP_PDL=0 disables it.
+// The 4-bit GEMV kernels trigger only after their own wait: a kernel launched behind one of them
+// may start before it finishes, but never before the launch two back has finished, so data written
+// two or more launches back may be read before the wait (qmtp_gdn_args.preload).
 bool pdl_enabled();
 
 template <typename... KArgs, typename... Args>

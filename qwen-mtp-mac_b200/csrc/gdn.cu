@@ -342,27 +342,40 @@ gdn_norm_gate_kernel(const float* __restrict__ y, const uint16_t* __restrict__ z
   }
 }
 
+// Four independent silu evaluations in one out-of-line call (the compiler interleaves them).  Each
+// inlined silu carries a correctly rounded division; the decode-shape kernel runs once per layer with
+// a cold instruction cache, so its roles share these single copies instead.
+static __device__ __noinline__ float4 silu_bf4(float4 x) {
+  return make_float4(silu_bf(x.x), silu_bf(x.y), silu_bf(x.z), silu_bf(x.w));
+}
+static __device__ __noinline__ float4 silu_f32x4(float4 x) {
+  return make_float4(silu_f32(x.x), silu_f32(x.y), silu_f32(x.z), silu_f32(x.w));
+}
+
 // ----------------------------------------------------------------------------- decode shape
 // The verify step of the decode loop: S <= 4 tokens, KC == 4 taps, Dk == Dv == 128.  Same
 // arithmetic as gdn_fused_kernel (+ gdn_norm_gate_kernel with GATE), laid out for latency:
-//  * constants (conv taps, A_log, dt_bias, the norm weight) are loaded before the dependency wait;
+//  * constants (conv taps, A_log, dt_bias, the norm weight) are loaded before the dependency wait,
+//    and with `preload` the previous step's state too (control words, state rows, old window rows);
 //  * warps 0..2S-1 each own one (token, q|k) vector: lane l convolves channels 4l..4l+3 from 8-byte
 //    window loads, then the warp applies the RMS norm itself (the fma chain over the lane's 4
 //    channels and the xor butterfly of gdn_fused_kernel's phase 2), so no barrier separates conv
 //    and norm;
-//  * warp 8 convolves the CTA's 16 v channels (and, with GATE, computes silu(z) of its outputs),
-//    warp 9 the gates: neither sits on a q/k warp's path;
+//  * warp 8 convolves the CTA's 16 v channels, warp 9 computes the gates and warp 10 (GATE) silu(z)
+//    of the gated norm's outputs: none of them sits on a q/k warp's path;
 //  * the next conv window is written from the registers the convolution loaded (q/k channels by one
 //    CTA of the key head, v channels by their owner);
 //  * GATE: the 8 CTAs of a value head form a cluster; after the delta rule each holds its 16 rows of
 //    y in shared memory, and a warp per token reads the head's 128 values over distributed shared
 //    memory in gdn_norm_gate_kernel's lane order (lane l: rows 4l..4l+3).
-// Grid (Dv / 16, Hv), 320 threads.
-constexpr int kDecS = 4, kDecKC = 4, kDecRows = 16, kDecVWarp = 8, kDecGWarp = 9, kDecWarps = 10;
+// Grid (Dv / 16, Hv), 352 threads.
+constexpr int kDecS = 4, kDecKC = 4, kDecRows = 16, kDecVWarp = 8, kDecGWarp = 9, kDecZWarp = 10;
+constexpr int kDecWarps = 11;
 
-template <bool GATE>
+template <bool GATE, int S>
 __global__ void __launch_bounds__(kDecWarps * 32)
 gdn_decode_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
+  static_assert(S >= 1 && S <= kDecS, "decode shape: 1..4 tokens");
   pdl_trigger();
   constexpr int Dk = 128, Dv = 128, NP = 4, KC = kDecKC;
   __shared__ __align__(16) float qk[2 * kDecS][Dk];  // [t][q|k][Dk], normalised
@@ -371,7 +384,7 @@ gdn_decode_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
   __shared__ __align__(16) float ys[kDecS][kDecRows];
   __shared__ float gz[kDecS][kDecRows];
   __shared__ float rs[kDecS];
-  const int S = A.S, Hk = A.Hk, Hv = A.Hv;
+  const int Hk = A.Hk, Hv = A.Hv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hv = blockIdx.y, dv0 = blockIdx.x * kDecRows;
   const int rep = Hv / Hk, hk = hv / rep;
@@ -380,6 +393,7 @@ gdn_decode_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
   const uint16_t* qkv = static_cast<const uint16_t*>(A.qkv);
   const uint16_t* conv_w = static_cast<const uint16_t*>(A.conv_w);
   const bool vec = warp < 2 * S;
+  const bool vwarp = warp == kDecVWarp && lane < kDecRows;
   const int tv = warp >> 1, isk = warp & 1;
   const long long chq = (long long)isk * Hk * Dk + (long long)hk * Dk + NP * lane;  // first of 4 channels
   const long long chv = 2LL * Hk * Dk + (long long)hv * Dv + dv0 + (lane & 15);
@@ -391,7 +405,7 @@ gdn_decode_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
     const uint4 c0 = *reinterpret_cast<const uint4*>(conv_w + chq * KC);
     const uint4 c1 = *reinterpret_cast<const uint4*>(conv_w + chq * KC + 8);
     cw[0] = c0.x; cw[1] = c0.y; cw[2] = c0.z; cw[3] = c0.w; cw[4] = c1.x; cw[5] = c1.y; cw[6] = c1.z; cw[7] = c1.w;
-  } else if (warp == kDecVWarp && lane < kDecRows) {
+  } else if (vwarp) {
     const uint2 c = *reinterpret_cast<const uint2*>(conv_w + chv * KC);
     cw[0] = c.x; cw[1] = c.y;
   } else if (warp == kDecGWarp && lane < S) {
@@ -399,63 +413,79 @@ gdn_decode_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
     dtb = bf2f(static_cast<const uint16_t*>(A.dt_bias)[hv]);
   }
   if (GATE && tid < S * kDecRows) nw = bf2f(static_cast<const uint16_t*>(A.gate_w)[dv0 + (tid & 15)]);
-  pdl_wait();
 
-  const int off = A.conv_row_off ? *A.conv_row_off : 0;
-  const size_t per = size_t(Hv) * Dv * Dk;
-  const float* sin = A.state_in;
-  int cur = 0;
-  if (A.ring) {
-    cur = *A.ring_cur;
-    if (cur < 0 || cur >= A.ring_slots) {  // uniform over the grid: every CTA leaves here
-      if (tid == 0) atomicOr(err, DEVERR_BADARG);
-      return;
-    }
-    sin = A.ring + size_t(cur) * per;
-  }
-  // phase-3 state rows (warps 0..7, rows dv0 + 2w, 2w + 1): independent of the convolution
+  // ---- state of the previous step: control words, the state rows of phase 3 (warps 0..7, rows
+  // dv0 + 2w, 2w + 1) and the window's conv rows (0..KC-2).  Before the dependency wait when the
+  // caller says the launch just before wrote none of them (preload), else after it.
+  int off = 0, wrow = 0, cur = 0;
   float st[2][NP];
-  if (warp < 8) {
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      const float4 s4 = *reinterpret_cast<const float4*>(sin + (size_t(hv) * Dv + dv0 + 2 * warp + rr) * Dk + NP * lane);
-      st[rr][0] = s4.x; st[rr][1] = s4.y; st[rr][2] = s4.z; st[rr][3] = s4.w;
+  uint2 wr[KC];                    // vec: window rows tv..tv+KC-1 of channels chq..chq+3
+  uint16_t wv[KC - 1 + kDecS];     // v warp: window rows 0..KC-2+S of channel chv
+  auto load_prev = [&]() -> bool {
+    off = A.conv_row_off ? *A.conv_row_off : 0;
+    wrow = A.win_out_row_off ? *A.win_out_row_off : 0;
+    const float* sin = A.state_in;
+    if (A.ring) {
+      cur = *A.ring_cur;
+      if (cur < 0 || cur >= A.ring_slots) return false;  // uniform over the grid
+      sin = A.ring + size_t(cur) * (size_t(Hv) * Dv * Dk);
     }
+    if (warp < 8) {
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const float4 s4 =
+            *reinterpret_cast<const float4*>(sin + (size_t(hv) * Dv + dv0 + 2 * warp + rr) * Dk + NP * lane);
+        st[rr][0] = s4.x; st[rr][1] = s4.y; st[rr][2] = s4.z; st[rr][3] = s4.w;
+      }
+    }
+    if (vec) {
+#pragma unroll
+      for (int j = 0; j < KC; ++j)
+        if (tv + j < KC - 1) wr[j] = *reinterpret_cast<const uint2*>(conv_src + (long long)(off + tv + j) * A.ld_conv + chq);
+    } else if (vwarp) {
+#pragma unroll
+      for (int r = 0; r < KC - 1; ++r) wv[r] = conv_src[(long long)(off + r) * A.ld_conv + chv];
+    }
+    return true;
+  };
+  bool ok = true;
+  if (A.preload) ok = load_prev();
+  pdl_wait();
+  if (!A.preload) ok = load_prev();
+  if (!ok) {
+    if (tid == 0) atomicOr(err, DEVERR_BADARG);
+    return;
   }
-  uint16_t* wo = A.win_out ? static_cast<uint16_t*>(A.win_out) +
-                                 (long long)(A.win_out_row_off ? *A.win_out_row_off : 0) * C
-                           : nullptr;
+  const size_t per = size_t(Hv) * Dv * Dk;
+  uint16_t* wo = A.win_out ? static_cast<uint16_t*>(A.win_out) + (long long)wrow * C : nullptr;
 
   if (vec) {
-    // ---- phase 1+2 for vector (tv, isk): window rows tv..tv+3 of channels chq..chq+3
-    uint2 wr[KC];
+    // ---- phase 1+2 for vector (tv, isk): the new rows of the window, then conv + silu + RMS norm
 #pragma unroll
-    for (int j = 0; j < KC; ++j) {
-      const int r = tv + j;
-      const uint16_t* p = r < KC - 1 ? conv_src + (long long)(off + r) * A.ld_conv + chq
-                                     : qkv + (long long)(r - (KC - 1)) * A.ld_qkv + chq;
-      wr[j] = *reinterpret_cast<const uint2*>(p);
-    }
-    float x[NP];
+    for (int j = 0; j < KC; ++j)
+      if (tv + j >= KC - 1) wr[j] = *reinterpret_cast<const uint2*>(qkv + (long long)(tv + j - (KC - 1)) * A.ld_qkv + chq);
+    float acc[NP];
 #pragma unroll
     for (int c = 0; c < NP; ++c) {
-      float acc = 0.0f;
+      acc[c] = 0.0f;
 #pragma unroll
       for (int j = 0; j < KC; ++j) {
         const uint32_t tw = cw[2 * c + (j >> 1)];
         const float tap = (j & 1) ? bfhi(tw) : bflo(tw);
         const uint32_t ww = (c < 2) ? wr[j].x : wr[j].y;
-        const float wv = (c & 1) ? bfhi(ww) : bflo(ww);
-        acc = __fmaf_rn(tap, wv, acc);
+        const float wvf = (c & 1) ? bfhi(ww) : bflo(ww);
+        acc[c] = __fmaf_rn(tap, wvf, acc[c]);
       }
-      x[c] = silu_bf(R(acc));
     }
+    const float4 x4 = silu_bf4(make_float4(R(acc[0]), R(acc[1]), R(acc[2]), R(acc[3])));
+    const float x[NP] = {x4.x, x4.y, x4.z, x4.w};
     float ss = 0.0f;
 #pragma unroll
     for (int c = 0; c < NP; ++c) ss = __fmaf_rn(x[c], x[c], ss);
     ss = warp_sum(ss);
     const float r = rsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / float(Dk)), 1e-6f));
-    const float kscale = R(rsqrt_rn(float(Dk)));
+    static_assert(Dk == 128, "kscale below is R(1 / sqrt(128))");
+    const float kscale = __uint_as_float(0x3DB50000u);  // R(rsqrt_rn(128.0f)): 0x3DB504F3 rounded to bf16
     float o[NP];
 #pragma unroll
     for (int c = 0; c < NP; ++c)
@@ -471,38 +501,26 @@ gdn_decode_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
         *reinterpret_cast<uint2*>(wo + (tv + KC - 1) * C + chq) = wr[KC - 1];
       }
     }
-  } else if (warp == kDecVWarp) {
-    if (lane < kDecRows) {
-      // ---- v channel chv over the S tokens (rows 0..KC-2+S of the window)
-      uint16_t wv[KC - 1 + kDecS];
+  } else if (vwarp) {
+    // ---- v channel chv over the S tokens (rows 0..KC-2+S of the window)
 #pragma unroll
-      for (int r = 0; r < KC - 1 + kDecS; ++r)
-        if (r < KC - 1 + S)
-          wv[r] = r < KC - 1 ? conv_src[(long long)(off + r) * A.ld_conv + chv]
-                             : qkv[(long long)(r - (KC - 1)) * A.ld_qkv + chv];
+    for (int r = KC - 1; r < KC - 1 + S; ++r) wv[r] = qkv[(long long)(r - (KC - 1)) * A.ld_qkv + chv];
+    float acc[kDecS] = {};
 #pragma unroll
-      for (int t = 0; t < kDecS; ++t)
-        if (t < S) {
-          float acc = 0.0f;
+    for (int t = 0; t < S; ++t) {
 #pragma unroll
-          for (int j = 0; j < KC; ++j) {
-            const float tap = (j & 1) ? bfhi(cw[j >> 1]) : bflo(cw[j >> 1]);
-            acc = __fmaf_rn(tap, bf2f(wv[t + j]), acc);
-          }
-          vs[t][lane] = silu_bf(R(acc));
-        }
-      if (wo) {
-#pragma unroll
-        for (int r = 0; r < KC - 1 + kDecS; ++r)
-          if (r < KC - 1 + S) wo[r * C + chv] = wv[r];
+      for (int j = 0; j < KC; ++j) {
+        const float tap = (j & 1) ? bfhi(cw[j >> 1]) : bflo(cw[j >> 1]);
+        acc[t] = __fmaf_rn(tap, bf2f(wv[t + j]), acc[t]);
       }
-    } else if (GATE) {
-      // ---- silu(z) of the gated norm's outputs (token t, row dv0 + d)
-      const int d = lane - kDecRows;
-      const uint16_t* z = static_cast<const uint16_t*>(A.gate_z);
+    }
+    const float4 v4 = silu_bf4(make_float4(R(acc[0]), R(acc[1]), R(acc[2]), R(acc[3])));
+    const float vv[kDecS] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
-      for (int t = 0; t < kDecS; ++t)
-        if (t < S) gz[t][d] = silu_f32(bf2f(z[(long long)t * A.ld_gate_z + (long long)hv * Dv + dv0 + d]));
+    for (int t = 0; t < S; ++t) vs[t][lane] = vv[t];
+    if (wo) {
+#pragma unroll
+      for (int r = 0; r < KC - 1 + S; ++r) wo[r * C + chv] = wv[r];
     }
   } else if (warp == kDecGWarp && lane < S) {
     // ---- gates of token t = lane
@@ -511,22 +529,33 @@ gdn_decode_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
     const float sp = softplus_bf(R(__fadd_rn(bf2f(av[(long long)lane * A.ld_ab + hv]), dtb)));
     gs[lane] = q_expf(__fmul_rn(Aneg, sp));
     bs[lane] = sigmoid_bf(bf2f(bv[(long long)lane * A.ld_ab + hv]));
+  } else if (GATE && warp == kDecZWarp && lane < kDecRows) {
+    // ---- silu(z) of the gated norm's outputs (token t, row dv0 + lane)
+    const uint16_t* z = static_cast<const uint16_t*>(A.gate_z);
+    float zv[kDecS] = {};
+#pragma unroll
+    for (int t = 0; t < S; ++t) zv[t] = bf2f(z[(long long)t * A.ld_gate_z + (long long)hv * Dv + dv0 + lane]);
+    const float4 g4 = silu_f32x4(make_float4(zv[0], zv[1], zv[2], zv[3]));
+    const float gv[kDecS] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+    for (int t = 0; t < S; ++t) gz[t][lane] = gv[t];
   }
   __syncthreads();
 
   // ---- phase 3: delta rule for rows dv0 + 2w + rr (same sequence as gdn_fused_kernel's decode path)
   if (warp < 8) {
-    float op[kDecS][2];
+    float op[S][2];
 #pragma unroll
-    for (int t = 0; t < kDecS; ++t) {
-      if (t >= S) break;
+    for (int t = 0; t < S; ++t) {
       const float4 q4 = *reinterpret_cast<const float4*>(&qk[2 * t][NP * lane]);
       const float4 k4 = *reinterpret_cast<const float4*>(&qk[2 * t + 1][NP * lane]);
       const float qf[4] = {q4.x, q4.y, q4.z, q4.w}, kf[4] = {k4.x, k4.y, k4.z, k4.w};
       const float gt = gs[t], bt = bs[t];
       float* dst = nullptr;
       if (A.ring) {
-        if (A.snap || t == S - 1) dst = A.ring + size_t((cur + t + 1) % A.ring_slots) * per;
+        int slot = cur + t + 1;  // cur < ring_slots and t + 1 <= S < ring_slots
+        if (slot >= A.ring_slots) slot -= A.ring_slots;
+        if (A.snap || t == S - 1) dst = A.ring + size_t(slot) * per;
       } else if (t == S - 1) {
         dst = A.state_out;
       } else if (A.snap && A.state_mid) {
@@ -564,20 +593,18 @@ gdn_decode_kernel(qmtp_gdn_args A, unsigned* __restrict__ err) {
 #pragma unroll
     for (int d = 16; d >= 1; d >>= 1)
 #pragma unroll
-      for (int t = 0; t < kDecS; ++t)
+      for (int t = 0; t < S; ++t)
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr)
-          if (t < S) op[t][rr] = __fadd_rn(op[t][rr], __shfl_xor_sync(0xFFFFFFFFu, op[t][rr], d));
+        for (int rr = 0; rr < 2; ++rr) op[t][rr] = __fadd_rn(op[t][rr], __shfl_xor_sync(0xFFFFFFFFu, op[t][rr], d));
     if (lane == 0) {
 #pragma unroll
-      for (int t = 0; t < kDecS; ++t)
+      for (int t = 0; t < S; ++t)
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr)
-          if (t < S) {
-            const float yv = R(op[t][rr]);
-            A.y[(size_t(t) * Hv + hv) * Dv + dv0 + 2 * warp + rr] = yv;
-            if (GATE) ys[t][2 * warp + rr] = yv;
-          }
+        for (int rr = 0; rr < 2; ++rr) {
+          const float yv = R(op[t][rr]);
+          A.y[(size_t(t) * Hv + hv) * Dv + dv0 + 2 * warp + rr] = yv;
+          if (GATE) ys[t][2 * warp + rr] = yv;
+        }
     }
   }
   if (GATE) {
@@ -656,10 +683,18 @@ extern "C" int qmtp_gdn_fused_ex(const qmtp_gdn_args* args, void* stream) {
                       (!A.win_out || a8(A.win_out));
   if (decode) {
     const dim3 grid(128 / kDecRows, A.Hv), block(kDecWarps * 32);
-    if (gate)
-      launch_kernel_cluster(gdn_decode_kernel<true>, grid, block, 0, st, 128 / kDecRows, A, device_error_ptr());
-    else
-      launch_kernel(gdn_decode_kernel<false>, grid, block, 0, st, A, device_error_ptr());
+    auto go = [&](auto kern_gate, auto kern_plain) {
+      if (gate)
+        launch_kernel_cluster(kern_gate, grid, block, 0, st, 128 / kDecRows, A, device_error_ptr());
+      else
+        launch_kernel(kern_plain, grid, block, 0, st, A, device_error_ptr());
+    };
+    switch (A.S) {
+      case 1: go(gdn_decode_kernel<true, 1>, gdn_decode_kernel<false, 1>); break;
+      case 2: go(gdn_decode_kernel<true, 2>, gdn_decode_kernel<false, 2>); break;
+      case 3: go(gdn_decode_kernel<true, 3>, gdn_decode_kernel<false, 3>); break;
+      default: go(gdn_decode_kernel<true, 4>, gdn_decode_kernel<false, 4>); break;
+    }
     return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
   }
   const size_t smem = size_t(A.S) * (2 * 128 + kFusedDVB + 2) * sizeof(float);

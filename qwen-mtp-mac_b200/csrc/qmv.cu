@@ -126,9 +126,10 @@ __global__ void __launch_bounds__(W * 32, 1) qmv_kernel(const __grid_constant__ 
     for (int t = 0; t < pre; ++t) issue(t);
   }
   // The weights are constant: their first tiles are fetched while the previous kernel may still
-  // run; everything below reads or writes activations and waits for it.
-  pdl_trigger();
+  // run; everything below reads or writes activations and waits for it.  The trigger follows the
+  // wait (a successor that starts implies the previous launch has finished).
   pdl_wait();
+  pdl_trigger();
 
   // x prologue: this thread's 32 elements of every row as (even, odd) fp32 pairs times 2^-14.
   // The reference scales the weights (half-bit e2m1 decode = value * 2^-14, qmv_kernel.py:16-25);

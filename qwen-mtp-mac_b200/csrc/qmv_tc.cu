@@ -447,8 +447,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   UnitCursor pc = first;  // producer's cursor: the next unit to request
   if (warp == 0 && lane == 0)
     for (int j = 0; j < pre; ++j, pc.template next<PAIR>(NSL)) issue(j, pc);
-  pdl_trigger();
+  // trigger after the wait: a successor that starts implies the previous launch has finished (the
+  // successor's CTAs still launch long before this kernel ends: its main loop follows)
   pdl_wait();
+  pdl_trigger();
 
   // Builds the activation operand of units [j0, j0 + nb) (their slots) with `nthr` threads, this one
   // being number `me` of them: the tasks in slot order, each task's x loaded two tasks ahead, one

@@ -60,7 +60,7 @@ class GdnArgs(ctypes.Structure):
                 ("y", _P),
                 ("S", _I), ("Hk", _I), ("Hv", _I), ("Dk", _I), ("Dv", _I), ("KC", _I), ("snap", _I),
                 ("gate_z", _P), ("ld_gate_z", ctypes.c_longlong), ("gate_w", _P), ("gate_out", _P),
-                ("ld_gate_out", ctypes.c_longlong), ("gate_eps", _F)]
+                ("ld_gate_out", ctypes.c_longlong), ("gate_eps", _F), ("preload", _I)]
 
 
 SIGNATURES.update({

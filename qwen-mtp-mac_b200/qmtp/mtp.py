@@ -245,7 +245,10 @@ class MTPDecoder:
             snap=1,
             # the gated norm (gdn_fused.py:114-129) in the same call: z = the in_proj rows after qkv
             gate_z=p + 2 * Cd, ld_gate_z=ldp, gate_w=L["norm"].data_ptr(), gate_out=self.gdn_out.data_ptr(),
-            ld_gate_out=Z, gate_eps=a.eps)
+            ld_gate_out=Z, gate_eps=a.eps,
+            # in_proj (a qmtp GEMV) is the launch before every step; state, windows and control words
+            # were written cycles earlier, so they are read before the dependency wait
+            preload=1)
 
     def _gdn_launches(self, i):
         """Kernels one qmtp_gdn_fused_ex call of layer i launches: 1 where the decode-shape kernel

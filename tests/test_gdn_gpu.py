@@ -82,11 +82,13 @@ def test_gdn_middle_and_norm_gate(S, gdn_mode, dev):
         assert np.array_equal(to_np(mids)[:, 0], rsm)
 
 
-@pytest.mark.parametrize("S,gate", [(3, False), (3, True), (1, True), (2, True), (4, True), (6, True)])
-def test_gdn_ring_mode_matches_explicit(S, gate, gdn_mode, dev):
+@pytest.mark.parametrize("S,gate,preload", [(3, False, 0), (3, True, 0), (3, True, 1), (1, True, 1), (2, True, 0),
+                                             (4, True, 1), (6, True, 1)])
+def test_gdn_ring_mode_matches_explicit(S, gate, preload, gdn_mode, dev):
     """Device-indexed state ring + conv rows at a device offset + next-window output written at a
     device row offset inside the same buffer (the decoder's layout), with and without the gated norm
-    (strided z and output rows, as the decoder passes them)."""
+    (strided z and output rows, as the decoder passes them), with the previous step's state read
+    before or after the dependency wait (preload; the launch before is a torch copy here)."""
     from qmtp import _lib
 
     d = fused_inputs(S=S, seed=50 + S)
@@ -119,7 +121,7 @@ def test_gdn_ring_mode_matches_explicit(S, gate, gdn_mode, dev):
                      conv_w=cw.data_ptr(), a=a_t.data_ptr(), b=b_t.data_ptr(),
                      ld_ab=Hv, A_log=al.data_ptr(), dt_bias=dtb.data_ptr(), state_in=None, state_out=None,
                      state_mid=None, ring=ring.data_ptr(), ring_cur=ctrl.data_ptr(), ring_slots=slots,
-                     y=y.data_ptr(), S=S, Hk=Hk, Hv=Hv, Dk=D, Dv=D, KC=KC, snap=1)
+                     y=y.data_ptr(), S=S, Hk=Hk, Hv=Hv, Dk=D, Dv=D, KC=KC, snap=1, preload=preload)
     if gate:
         A.gate_z, A.ld_gate_z = proj.data_ptr() + 2 * C, ldp
         A.gate_w, A.gate_out, A.ld_gate_out, A.gate_eps = w_t.data_ptr(), out.data_ptr(), out.shape[1], 1e-6
