@@ -76,6 +76,13 @@ inline cudaError_t launch_kernel_cluster(void (*kern)(KArgs...), dim3 grid, dim3
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// L2 prefetch of `bytes` (a multiple of 16) at the 16-byte aligned address p.  A hint: no data
+// comes back and no ordering is implied, and L2 is where every kernel's stores land, so it is safe
+// before the dependency wait even for lines an earlier kernel is still writing.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // The two halves of cluster_sync_all, for a barrier whose wait is deferred (e.g. "my peers may
 // still read my shared memory": arrive after the last remote read, wait before exiting).
 __device__ __forceinline__ void cluster_arrive_release() {

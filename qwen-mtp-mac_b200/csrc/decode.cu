@@ -215,6 +215,20 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
                  const uint16_t* __restrict__ vc, int max_pos, int nq, int nkv, const int* __restrict__ pos_ptr,
                  int pos_add, uint16_t* __restrict__ out, unsigned* err) {
   pdl_trigger();
+  {
+    // this split's key and value rows into L2 while the previous launches finish; the position is
+    // read before the wait as an address hint only (a stale value prefetches other rows, no more)
+    const int w = int(cluster_rank()), hq = blockIdx.x / kAttnSplits, s = blockIdx.y;
+    int Lh = (pos_ptr ? *pos_ptr : 0) + pos_add + s + 1;
+    Lh = Lh < 0 ? 0 : (Lh > max_pos ? max_pos : Lh);
+    const int kh = hq / (nq / nkv);
+    const int nk = w < Lh ? (Lh - w + kAttnSplits - 1) / kAttnSplits : 0;
+    for (int n = threadIdx.x; n < nk; n += blockDim.x) {
+      const long long r = ((long long)kh * max_pos + w + kAttnSplits * n) * 256;
+      prefetch_l2(kc + r, 512);
+      prefetch_l2(vc + r, 512);
+    }
+  }
   pdl_wait();
   constexpr int Dh = 256, NP = 8;
   extern __shared__ __align__(16) float sm[];
@@ -524,6 +538,7 @@ extern "C" int qmtp_attention(const void* q, const void* gate, const void* k_cac
                               void* stream) {
   if (!q || !gate || !k_cache || !v_cache || !out) return QMTP_ERR_ARG;
   if (Dh != 256 || S < 1 || nq < 1 || nkv < 1 || nq % nkv || max_pos < 8) return QMTP_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache)) return QMTP_ERR_ALIGN;  // 16-byte rows
   const size_t smem = (size_t(Dh) + 2 + 8 + size_t(max_pos / kAttnSplits + 1)) * sizeof(float);
   if (smem > 200 * 1024) return QMTP_ERR_SHAPE;
   static const cudaError_t attr =

@@ -6,8 +6,8 @@
 // key `key16`; a candidate is the 64-bit word (key16 << 32) | (0xFFFFFFFF - index), so "larger
 // word" means "better candidate" and any max/sort over these words is order-independent.
 //
-//   topk_partial  grid (G, M): block g of row m radix-selects the top k of its slice of the row
-//                 (two 8-bit histogram passes in shared memory) and writes k candidate words;
+//   topk_partial  grid (G, M): block g of row m selects the top k of its slice of the row (the k-th
+//                 largest key found bit by bit with block-wide counts) and writes k candidate words;
 //   topk_merge    grid (M): bitonic-sorts the G*k candidate words, keeps the first k, rescoring
 //                 each against the bf16 weight row (one warp per candidate, fixed reduction order
 //                 of oracle qo_dot_bf16), and takes the argmax of the fine logits;
@@ -51,32 +51,59 @@ __device__ void find_bin(const int* hist, int k, int base, int* s_res) {
   }
 }
 
-// Exact top-k of n (>= k) 16-bit keys in shared memory: T and g with g < k <= g + #(key == T).
-__device__ void block_select16(const uint16_t* keys, int n, int k, int* hist, int* s_res, int& T, int& g) {
-  const int tid = threadIdx.x;
-  for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
-  __syncthreads();
-  for (int i = tid; i < n; i += blockDim.x) atomicAdd(&hist[keys[i] >> 8], 1);
-  __syncthreads();
-  if (tid < 32) find_bin(hist, k, 0, s_res);
-  __syncthreads();
-  const int b1 = s_res[0], g1 = s_res[1];
-  __syncthreads();
-  for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
-  __syncthreads();
-  for (int i = tid; i < n; i += blockDim.x) {
-    const uint32_t kk = keys[i];
-    if (int(kk >> 8) == b1) atomicAdd(&hist[kk & 255u], 1);
+// Exact top-k of n (>= k) 16-bit keys in shared memory: T = the k-th largest key and g = #(key > T)
+// (so g < k <= g + #(key == T)).  T is built from the top bit down, two bits a round: the largest
+// candidate c with #(key >= T | c) >= k (the count only falls as the threshold rises).  Each thread
+// holds its contiguous share of the keys in registers and a round is three block-wide counts; a
+// histogram instead piles its shared-memory atomics onto the few bins logit keys occupy.
+// blockDim.x == kTopkThreads, n <= kTopkThreads * 2 * kSelRegs; s_cnt: 3 * 32 ints.
+constexpr int kTopkThreads = 256;
+constexpr int kSelRegs = 24;  // 48 keys a thread: slices up to 12288 keys
+__device__ void block_select16(const uint16_t* keys, int n, int k, int* s_cnt, int& T, int& g) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = int(blockDim.x) >> 5;
+  const int per = (n + int(blockDim.x) - 1) / int(blockDim.x);
+  const int a0 = min(n, tid * per), a1 = min(n, a0 + per);
+  uint32_t kr[kSelRegs];  // key pairs; missing keys are 0, below every threshold asked (>= 1)
+#pragma unroll
+  for (int i = 0; i < kSelRegs; ++i) {
+    const int e0 = a0 + 2 * i, e1 = e0 + 1;
+    kr[i] = (e0 < a1 ? uint32_t(keys[e0]) : 0u) | ((e1 < a1 ? uint32_t(keys[e1]) : 0u) << 16);
   }
-  __syncthreads();
-  if (tid < 32) find_bin(hist, k, g1, s_res);
-  __syncthreads();
-  T = (b1 << 8) | s_res[0];
-  g = s_res[1];
-  __syncthreads();
+  auto count3 = [&](uint32_t t1, uint32_t t2, uint32_t t3, int (&c)[3]) {
+    int c1 = 0, c2 = 0, c3 = 0;
+#pragma unroll
+    for (int i = 0; i < kSelRegs; ++i) {
+      const uint32_t lo = kr[i] & 0xFFFFu, hi = kr[i] >> 16;
+      c1 += int(lo >= t1) + int(hi >= t1);
+      c2 += int(lo >= t2) + int(hi >= t2);
+      c3 += int(lo >= t3) + int(hi >= t3);
+    }
+    c1 = __reduce_add_sync(0xFFFFFFFFu, c1);
+    c2 = __reduce_add_sync(0xFFFFFFFFu, c2);
+    c3 = __reduce_add_sync(0xFFFFFFFFu, c3);
+    if (lane == 0) { s_cnt[warp] = c1; s_cnt[32 + warp] = c2; s_cnt[64 + warp] = c3; }
+    __syncthreads();
+    c[0] = c[1] = c[2] = 0;
+    for (int w = 0; w < nw; ++w) { c[0] += s_cnt[w]; c[1] += s_cnt[32 + w]; c[2] += s_cnt[64 + w]; }
+    __syncthreads();
+  };
+  uint32_t t = 0;
+  for (int b = 14; b >= 0; b -= 2) {  // bits b+1, b
+    int c[3];
+    count3(t | (1u << b), t | (2u << b), t | (3u << b), c);
+    t |= (c[2] >= k ? 3u : c[1] >= k ? 2u : c[0] >= k ? 1u : 0u) << b;
+  }
+  T = int(t);
+  if (t == 0xFFFFu) {
+    g = 0;
+  } else {
+    int c[3];
+    count3(t + 1, t + 1, t + 1, c);
+    g = c[0];
+  }
 }
 
-constexpr int kTopkThreads = 256;
+
 
 __global__ void __launch_bounds__(kTopkThreads)
 topk_partial_kernel(const uint16_t* __restrict__ vals, long long ld, int V, int k, uint64_t* __restrict__ cand) {
@@ -90,10 +117,39 @@ topk_partial_kernel(const uint16_t* __restrict__ vals, long long ld, int V, int 
   const int G = gridDim.x, blk = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
   const int i0 = int((long long)blk * V / G), i1 = int((long long)(blk + 1) * V / G), n = i1 - i0;
   const uint16_t* row = vals + (long long)m * ld + i0;
-  for (int i = tid; i < n; i += blockDim.x) keys[i] = uint16_t(key16(row[i]));
+  {
+    // 16-byte loads over the aligned middle of the slice, issued four at a time before any is used
+    // (the slice is ~8K keys: a plain element loop would wait out one L2 round trip per element)
+    const int mis = int((reinterpret_cast<uintptr_t>(row) >> 1) & 7u);
+    const int head = min(n, mis ? 8 - mis : 0);
+    const int nv = (n - head) / 8, tail0 = head + 8 * nv;
+    for (int i = tid; i < head; i += blockDim.x) keys[i] = uint16_t(key16(row[i]));
+    for (int i = tail0 + tid; i < n; i += blockDim.x) keys[i] = uint16_t(key16(row[i]));
+    const uint4* v = reinterpret_cast<const uint4*>(row + head);
+    constexpr int U = 4;
+    for (int c0 = tid; c0 < nv; c0 += U * int(blockDim.x)) {
+      uint4 u[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (c0 + j * int(blockDim.x) < nv) u[j] = v[c0 + j * blockDim.x];
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const int c = c0 + j * int(blockDim.x);
+        if (c < nv) {
+          const uint32_t w[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+          uint16_t* kd = keys + head + 8 * c;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            kd[2 * e] = uint16_t(key16(uint16_t(w[e] & 0xFFFFu)));
+            kd[2 * e + 1] = uint16_t(key16(uint16_t(w[e] >> 16)));
+          }
+        }
+      }
+    }
+  }
   __syncthreads();
   int T, g;
-  block_select16(keys, n, k, hist, s_res, T, g);
+  block_select16(keys, n, k, hist, T, g);
   // emit: every key > T, then the (k - g) lowest-index keys == T, each thread over a contiguous range
   const int per = (n + blockDim.x - 1) / blockDim.x;
   const int a0 = min(n, tid * per), a1 = min(n, a0 + per);

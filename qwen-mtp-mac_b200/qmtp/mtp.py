@@ -308,7 +308,8 @@ class MTPDecoder:
         """Two-stage head (lm_head2.py:23-29) + greedy argmax: coarse qmv, then selection/rescoring."""
         a = self.a
         self._qmv(self.hn, self.W["lm_head_q"], self.coarse, self.S)
-        self.launches += 2
+        # selection, then merge + rescoring + argmax (above 256 candidates: radix select, rescoring, argmax)
+        self.launches += 2 if self.K <= 256 else 4
         self._chk(self.L.qmtp_topk_rescore(self.coarse.data_ptr(), a.vocab, self.S, a.vocab, self.K,
                                            self.W["lm_head"].data_ptr(), self.hn.data_ptr(), a.hidden,
                                            self.idx.data_ptr(), self.fine.data_ptr(), self.a_tok.data_ptr(),
