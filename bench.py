@@ -150,6 +150,12 @@ def run_ours(args):
     gen_tokens = 256  # config 4 generates 256 tokens; the e2e leg decodes all of them
     dec = MTPDecoder(cfg, W, k=K_DRAFTS, max_tokens=max(Wu + 3 * K + 64, gen_tokens + 64), device=dev,
                      sampling=sp)
+    if args.draft_vocab:
+        # draft head over the first draft_vocab ids (mtp.py:170-196 load_draft_head; the reference's
+        # bench_ab.py compares such heads with the full one).  Config 4 itself drafts over the full head.
+        from qmtp.mtp import load_draft_head
+
+        dec.set_draft_head(load_draft_head(args.draft_vocab, {"bits": 4, "group_size": 64}, lm=qm.Model(cfg, W)))
 
     # ---- prefill, one eager cycle (library setup), capture
     t = dec.prefill(prompt)
@@ -236,10 +242,13 @@ def run_ours(args):
     peak, peak_kind = _peaks()
     qbytes = sum(b for b, _ in prof)
     achieved = qbytes / (qmv_ms_cycle / 1e3) / 1e9
-    ratio = _traffic_ratio("qmv_affine_g64_inproj_M3.md" if args.weights == "affine" else "qmv_nvfp4_g16_head_M1.md")
+    tsum = "qmv_affine_g64_inproj_M3.md" if args.weights == "affine" else "qmv_nvfp4_g16_head_M1.md"
+    ratio = _traffic_ratio(tsum)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "traffic": None if ratio is None else round(ratio * qbytes / len(prof)),
+                "traffic_source": f"DRAM bytes / algorithmic bytes of one launch in profiles/{tsum} (ncu), times "
+                                  "this cycle's mean algorithmic bytes per launch",
                 "kernel": ("qmv_affine_g64" if args.weights == "affine" else "qmv_nvfp4_g16 (trunk) + qmv_affine_g64 (coarse head)")
                           + " (all 4-bit projections + coarse head of a cycle)",
                 "bytes_per_cycle": qbytes, "qmv_ms_per_cycle": round(qmv_ms_cycle, 4),
@@ -256,6 +265,8 @@ def run_ours(args):
                                   + f" MTP decode k=2, batch 1, {args.prompt}-token uniform random prompt",
                       "step": "one verify cycle (verify 3 tokens + accept/rollback + 2 draft steps)",
                       "prompt_tokens": args.prompt, "drafts": K_DRAFTS, "parallelism": f"replicas x{world}",
+                      "draft_head": (f"first {args.draft_vocab} ids (load_draft_head)" if args.draft_vocab
+                                     else "full vocabulary"),
                       "l2": "weights ~7.5 GB per cycle >> 126 MB L2 (no flush needed)",
                       "weights_build_s": round(t_build, 1),
                       **({} if sp is None else {"sampling": {"temperature": sp.temperature, "top_k": sp.top_k,
@@ -272,7 +283,8 @@ def run_ours(args):
 
     # ---- CPU oracle on a bounded sample of the same decode, from the same post-prefill state
     if post_prefill is not None:
-        res["cpu_baseline"] = cpu_baseline_from_state(cfg, W, post_prefill, gpu_stream, args.cpu_cycles, sp)
+        res["cpu_baseline"] = cpu_baseline_from_state(cfg, W, post_prefill, gpu_stream, args.cpu_cycles, sp,
+                                                      args.draft_vocab)
     if world > 1:
         # the sharded workload of the build: config 5's MoE layer expert-parallel over the same ranks
         dist.barrier()
@@ -288,7 +300,7 @@ def run_ours(args):
         print(json.dumps(res), flush=True)
 
 
-def cpu_baseline_from_state(cfg, W, state, gpu_tokens, cycles, sampling=None):
+def cpu_baseline_from_state(cfg, W, state, gpu_tokens, cycles, sampling=None, draft_vocab=0):
     import numpy as np
 
     from oracle import model as om
@@ -299,6 +311,8 @@ def cpu_baseline_from_state(cfg, W, state, gpu_tokens, cycles, sampling=None):
     Wn = qm.to_numpy(W)
     ocfg = om.ModelArgs(**{k: getattr(cfg, k) for k in om.ModelArgs.__dataclass_fields__})
     orc = om.OracleModel(ocfg, Wn)
+    if draft_vocab:
+        orc.set_draft_head(draft_vocab)
     layers, mtp, pending = state
     cache, mcache = orc.load_state(layers, mtp)
     copy_s = time.time() - t0
@@ -657,6 +671,8 @@ def main():
     ap.add_argument("--top-p", type=float, default=1.0)
     ap.add_argument("--min-p", type=float, default=0.0)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--draft-vocab", type=int, default=0,
+                    help="draft head over the first N ids (load_draft_head; 0 = the full vocabulary of config 4)")
     ap.add_argument("--kernel", default=None, choices=["qmv", "gdn", "head", "moe"],
                     help="time one kernel at a config shape instead of the decode loop")
     ap.add_argument("--shape", default="12288,4096,3", help="qmv: N,K,M[,affine|affine-whole|nvfp4]")

@@ -298,6 +298,13 @@ size_t qmtp_argmax_workspace(int M, int V);
 int qmtp_argmax_bf16(const void* vals, int ld, int M, int V, int* out, void* workspace,
                      size_t ws_bytes, void* stream);
 
+/* qmtp_argmax_bf16 for a head over a vocabulary subset (mtp.py:156-167 DraftHead with ids,
+ * load_draft_head(vocab, quant, freq, extra_ids)): row i of vals scores vocabulary id ids[i] (int32
+ * [V], may be NULL for ids[i] = i); out[m] = ids[argmax], out_local[m] (may be NULL) = the argmax row
+ * itself.  Same tie rule (lower row) and workspace as qmtp_argmax_bf16. */
+int qmtp_argmax_bf16_ids(const void* vals, int ld, int M, int V, const int* ids, int* out, int* out_local,
+                         void* workspace, size_t ws_bytes, void* stream);
+
 /* --------------------------------------------------------------------------------------------
  * Decoder ops of the synthetic Qwen3.5 model (mtp.py:143-153 backbone, mtp.py:35-45 MTP layer;
  * layer structure of mlx-lm qwen3_5, cross-checked with transformers' Qwen3.5).  Positions may come

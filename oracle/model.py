@@ -146,6 +146,27 @@ class OracleModel:
         self.a = args
         self.W = W
         self.cos, self.sin = rope_tables(args)
+        self.draft_ids = None          # draft head over a vocabulary subset (set_draft_head)
+        self.draft_W = W.get("lm_head_q")
+
+    def set_draft_head(self, vocab=None, counts=None, extra_ids=()):
+        """mtp.py:170-196 load_draft_head: the draft head scores `vocab` rows of the lm_head -- the first
+        `vocab` ids, or with `counts` the `vocab` most frequent ids plus extra_ids, ascending -- with the
+        head's 4-bit g64 quantization (per row and group, so the subset's rows equal the full copy's).
+        vocab None: the full-vocabulary head."""
+        V = self.a.vocab
+        lin = self.W["lm_head_q"]
+        if vocab is None or (counts is None and vocab >= V):
+            self.draft_ids, self.draft_W = None, self.W["lm_head_q"]
+            return
+        if counts is None:
+            rows = np.arange(min(vocab, V))
+            self.draft_ids = None
+        else:
+            top = set(np.argsort(-np.asarray(counts)[:V])[:vocab].tolist()) | {int(e) for e in extra_ids}
+            rows = np.array(sorted(top), dtype=np.int64)
+            self.draft_ids = rows.astype(np.int32)
+        self.draft_W = tuple(np.ascontiguousarray(t[rows]) for t in lin)
 
     def make_cache(self):
         a = self.a
@@ -249,9 +270,10 @@ class OracleModel:
     def draft_token(self, xn, with_prob=False):
         """Draft head: full-vocabulary 4-bit head (bench_ab.py:24 DRAFT_HEAD, engine.py:46-48) + argmax;
         with_prob: also the probability of the argmax (mtp.py:222-223)."""
-        logits = qmv(xn, self.W["lm_head_q"])
-        d = ops.argmax_bf16(logits)
-        return (d, ops.draft_prob(logits[0], int(d[0]))) if with_prob else d
+        logits = qmv(xn, self.draft_W)
+        i = ops.argmax_bf16(logits)
+        d = i if self.draft_ids is None else self.draft_ids[i]
+        return (d, ops.draft_prob(logits[0], int(i[0]))) if with_prob else d
 
     # -- mtp.py:199-209
     def mtp_step(self, hidden, tokens, mcache, with_prob=False):
@@ -293,7 +315,7 @@ class OracleModel:
         return out
 
     def prefill(self, prompt_ids, k=2, sampling=None, tau=None):
-        """mtp.py:258-263: prompt pass, first token t, first drafts; returns (cache, mcache, h, t, drafts).
+        """mtp.py:258-263: prompt pass, first token t, first drafts; returns (cache, mcache, t, drafts).
         With sampling (temperature > 0) the first token is drawn (engine.py:110-115, call counter 0)."""
         cache = self.make_cache()
         mcache = self._kv()

@@ -83,6 +83,16 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// 16-byte asynchronous global -> shared copy (both addresses 16-byte aligned), bypassing L1, and its
+// group commit / wait: the thread's copies are in shared memory after cp_async_wait_all (other threads
+// see them after a barrier).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // The two halves of cluster_sync_all, for a barrier whose wait is deferred (e.g. "my peers may
 // still read my shared memory": arrive after the last remote read, wait before exiting).
 __device__ __forceinline__ void cluster_arrive_release() {

@@ -209,6 +209,7 @@ __global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld,
 // shared memory.  Rank 0 then merges the 8 splits in order through distributed shared memory.
 constexpr int kAttnSplits = 8;
 constexpr int kAttnBatch = 8;   // keys a warp fetches at once in the score pass
+constexpr int kAttnVStage = 32; // value rows of a split copied to shared memory while the scores run
 
 __global__ void __launch_bounds__(256)
 attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ gate, const uint16_t* __restrict__ kc,
@@ -236,6 +237,8 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
   float* s_md = s_num + Dh;          // [2] split max, denominator
   float* s_red = s_md + 2;           // [8] per-warp maxima
   float* s_sc = s_red + 8;           // [max_pos / 8 + 1] scores, then exponentials
+  // the first kAttnVStage value rows of the split: [kAttnVStage][Dh / 2] bf16 pairs, 16-byte aligned
+  uint32_t* s_v = reinterpret_cast<uint32_t*>(sm + ((Dh + 10 + max_pos / kAttnSplits + 1 + 3) & ~3));
   const int w = int(cluster_rank());  // key split
   const int h = blockIdx.x / kAttnSplits, s = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -246,6 +249,22 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
   }
   const int kh = h / (nq / nkv);
   const int nk = w < L ? (L - w + kAttnSplits - 1) / kAttnSplits : 0;  // keys of this split
+  // loads that do not wait for q: the first kAttnVStage value rows of the split into shared memory
+  // (asynchronous copies, 16 bytes a thread and step) and this warp's first round of key rows
+  {
+    const int nv = min(nk, kAttnVStage);
+    for (int c = tid; c < nv * (Dh / 8); c += 256) {
+      const int n = c / (Dh / 8), part = c - n * (Dh / 8);
+      cp_async16(s_v + n * (Dh / 2) + part * 4, vc + ((long long)kh * max_pos + w + kAttnSplits * n) * Dh + part * 8);
+    }
+    cp_async_commit();
+  }
+  uint4 kr[kAttnBatch];
+#pragma unroll
+  for (int u = 0; u < kAttnBatch; ++u) {
+    const int n = warp + 8 * u;
+    if (n < nk) kr[u] = *reinterpret_cast<const uint4*>(kc + ((long long)kh * max_pos + w + kAttnSplits * n) * Dh + NP * lane);
+  }
   float qf[NP];
   {
     const uint4 u = *reinterpret_cast<const uint4*>(q + ((long long)s * nq + h) * Dh + NP * lane);
@@ -259,12 +278,13 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
   // same values); the max is exact, hence order-free
   float mx = __int_as_float(0xFF800000);
   for (int n0 = warp; n0 < nk; n0 += 8 * kAttnBatch) {
-    uint4 kr[kAttnBatch];
+    if (n0 != warp) {  // the first round was fetched above
 #pragma unroll
-    for (int u = 0; u < kAttnBatch; ++u) {
-      const int n = n0 + 8 * u;
-      if (n < nk)
-        kr[u] = *reinterpret_cast<const uint4*>(kc + ((long long)kh * max_pos + w + kAttnSplits * n) * Dh + NP * lane);
+      for (int u = 0; u < kAttnBatch; ++u) {
+        const int n = n0 + 8 * u;
+        if (n < nk)
+          kr[u] = *reinterpret_cast<const uint4*>(kc + ((long long)kh * max_pos + w + kAttnSplits * n) * Dh + NP * lane);
+      }
     }
     float acc[kAttnBatch];
 #pragma unroll
@@ -298,22 +318,25 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
   for (int i = 1; i < 8; ++i) mw = s_red[i] > mw ? s_red[i] : mw;
   // exponentials (parallel), then the two sequential chains of the split
   for (int n = tid; n < nk; n += 256) s_sc[n] = q_expf(__fsub_rn(s_sc[n], mw));
+  cp_async_wait_all();  // this thread's value-row copies; the barrier publishes everyone's
   __syncthreads();
-  if (tid == 0) {
+  if (tid == Dh / 2) {  // warp 4: idle in the numerator pass below
     float den = 0.0f;
     for (int n = 0; n < nk; ++n) den = __fadd_rn(den, s_sc[n]);
     s_md[0] = mw;
     s_md[1] = den;
   }
   if (tid < Dh / 2) {
-    // thread t owns dims 2t, 2t+1: one 32-bit load per key, 32 keys in flight per batch
+    // thread t owns dims 2t, 2t+1: one 32-bit word per key, keys ascending; the first kAttnVStage
+    // keys from shared memory, the rest 32 keys in flight per batch
     float num0 = 0.0f, num1 = 0.0f;
     const uint32_t* vb = reinterpret_cast<const uint32_t*>(vc + ((long long)kh * max_pos + w) * Dh) + tid;
     for (int n0 = 0; n0 < nk; n0 += 32) {
       uint32_t v2[32];
+      static_assert(kAttnVStage == 32, "the first batch is the staged one");
 #pragma unroll
       for (int u = 0; u < 32; ++u)
-        if (n0 + u < nk) v2[u] = vb[(long long)kAttnSplits * (n0 + u) * (Dh / 2)];
+        if (n0 + u < nk) v2[u] = n0 == 0 ? s_v[u * (Dh / 2) + tid] : vb[(long long)kAttnSplits * (n0 + u) * (Dh / 2)];
 #pragma unroll
       for (int u = 0; u < 32; ++u)
         if (n0 + u < nk) {
@@ -539,7 +562,9 @@ extern "C" int qmtp_attention(const void* q, const void* gate, const void* k_cac
   if (!q || !gate || !k_cache || !v_cache || !out) return QMTP_ERR_ARG;
   if (Dh != 256 || S < 1 || nq < 1 || nkv < 1 || nq % nkv || max_pos < 8) return QMTP_ERR_UNSUPPORTED;
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache)) return QMTP_ERR_ALIGN;  // 16-byte rows
-  const size_t smem = (size_t(Dh) + 2 + 8 + size_t(max_pos / kAttnSplits + 1)) * sizeof(float);
+  // scores etc. (rounded up to 16 bytes), then the staged value rows
+  const size_t smem = ((size_t(Dh) + 2 + 8 + size_t(max_pos / kAttnSplits + 1) + 3) & ~size_t(3)) * sizeof(float) +
+                      size_t(kAttnVStage) * Dh * sizeof(uint16_t);
   if (smem > 200 * 1024) return QMTP_ERR_SHAPE;
   static const cudaError_t attr =
       cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);

@@ -276,7 +276,10 @@ argmax_partial_kernel(const uint16_t* __restrict__ vals, long long ld, int V, ui
   }
 }
 
-__global__ void argmax_final_kernel(const uint64_t* __restrict__ part, int G, int32_t* __restrict__ out) {
+// ids (may be null): the vocabulary id of every scored row (a draft head over a vocabulary subset,
+// mtp.py:165-167 DraftHead.token); out gets ids[i] and out_local (may be null) the row i itself.
+__global__ void argmax_final_kernel(const uint64_t* __restrict__ part, int G, const int32_t* __restrict__ ids,
+                                    int32_t* __restrict__ out, int32_t* __restrict__ out_local) {
   pdl_trigger();
   pdl_wait();
   const int m = blockIdx.x, lane = threadIdx.x;
@@ -284,7 +287,11 @@ __global__ void argmax_final_kernel(const uint64_t* __restrict__ part, int G, in
   for (int i = lane; i < G; i += 32) best = max(best, part[(long long)m * G + i]);
 #pragma unroll
   for (int d = 16; d >= 1; d >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, d));
-  if (lane == 0) out[m] = int32_t(cand_idx(best));
+  if (lane == 0) {
+    const int32_t i = int32_t(cand_idx(best));
+    out[m] = ids ? ids[i] : i;
+    if (out_local) out_local[m] = i;
+  }
 }
 
 // ---- large candidate sets (k > 256, up to 2048: lm_head2.py:32-36 k_for with top_k up to 512)
@@ -557,8 +564,8 @@ extern "C" size_t qmtp_argmax_workspace(int M, int V) {
   return size_t(M) * std::min(256, std::max(1, V / 1024)) * sizeof(uint64_t);
 }
 
-extern "C" int qmtp_argmax_bf16(const void* vals, int ld, int M, int V, int* out, void* workspace, size_t ws_bytes,
-                                void* stream) {
+extern "C" int qmtp_argmax_bf16_ids(const void* vals, int ld, int M, int V, const int* ids, int* out, int* out_local,
+                                    void* workspace, size_t ws_bytes, void* stream) {
   if (!vals || !out || !workspace) return QMTP_ERR_ARG;
   if (M < 1 || V < 1 || ld < V) return QMTP_ERR_SHAPE;
   if (ws_bytes < qmtp_argmax_workspace(M, V)) return QMTP_ERR_ARG;
@@ -566,8 +573,14 @@ extern "C" int qmtp_argmax_bf16(const void* vals, int ld, int M, int V, int* out
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint64_t* part = static_cast<uint64_t*>(workspace);
   launch_kernel(argmax_partial_kernel, dim3(dim3(G, M)), dim3(256), 0, st, static_cast<const uint16_t*>(vals), ld, V, part);
-  launch_kernel(argmax_final_kernel, dim3(M), dim3(32), 0, st, part, G, out);
+  launch_kernel(argmax_final_kernel, dim3(M), dim3(32), 0, st, static_cast<const uint64_t*>(part), G,
+                static_cast<const int32_t*>(ids), out, out_local);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_argmax_bf16(const void* vals, int ld, int M, int V, int* out, void* workspace, size_t ws_bytes,
+                                void* stream) {
+  return qmtp_argmax_bf16_ids(vals, ld, M, V, nullptr, out, nullptr, workspace, ws_bytes, stream);
 }
 
 extern "C" size_t qmtp_lmhead2_workspace(int M, int V, int k) {

@@ -72,6 +72,7 @@ SIGNATURES.update({
     "qmtp_lmhead2": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     "qmtp_topk_rescore": [_P, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t, _P],
     "qmtp_argmax_bf16": [_P, _I, _I, _I, _P, _P, ctypes.c_size_t, _P],
+    "qmtp_argmax_bf16_ids": [_P, _I, _I, _I, _P, _P, _P, _P, ctypes.c_size_t, _P],
     "qmtp_qmv_affine_g64_res": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "qmtp_lmhead2_noalloc": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P],
     "qmtp_lmhead2_shard": [_P, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_longlong, _P, _P, _P, ctypes.c_size_t, _P],

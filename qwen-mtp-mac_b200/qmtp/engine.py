@@ -29,13 +29,24 @@ class Engine:
     token ids (the tokenizer's, engine.py:46); ``max_context``: prompt + generated tokens a request
     may hold (bounded by the model's KV-cache length)."""
 
-    def __init__(self, model: Model, k: int = 2, eos=(), max_context: int | None = None):
+    def __init__(self, model: Model, k: int = 2, eos=(), max_context: int | None = None, draft_vocab: int = 65536,
+                 draft_counts=None):
+        """draft_vocab / draft_counts: engine.py:38,46-48 -- with corpus counts (build_draft_vocab.py's
+        file or array) the draft head scores the draft_vocab most frequent ids plus the EOS ids
+        (load_draft_head(..., freq=True)); without, the full-vocabulary head."""
+        from .mtp import load_draft_head
+
         self.lm = model
         self.k = k
         self.eos = set(int(t) for t in eos)
         self.max_context = min(max_context or model.args.max_pos, model.args.max_pos)
+        head = None
+        if draft_counts is not None:
+            head = load_draft_head(draft_vocab, {"bits": 4, "group_size": 64}, True, sorted(self.eos), lm=model,
+                                   counts=draft_counts)
+        self.head = head
         self.dec = MTPDecoder(model.args, model.weights, k=k, max_tokens=self.max_context,
-                              device=model.weights["norm"].device)
+                              device=model.weights["norm"].device, draft_head=head)
 
     @classmethod
     def from_checkpoint(cls, path, k: int = 2, eos=(), mtp_files=(), max_pos: int = 4096, device="cuda"):

@@ -45,7 +45,7 @@ class MTPDecoder:
     """Device state + launch sequence of one MTP decoding session (batch 1; greedy or sampled)."""
 
     def __init__(self, args: ModelArgs, W: Weights, k: int = 2, max_tokens: int = 1024, device="cuda",
-                 sampling: Sampling | None = None, tau: float | None = None):
+                 sampling: Sampling | None = None, tau: float | None = None, draft_head=None):
         self.a, self.W, self.k = args, W, k
         self.tau = None
         # sampling with temperature > 0: exact speculative sampling (engine.py:91-152) over the
@@ -82,6 +82,9 @@ class MTPDecoder:
         self.memb, self.mcat, self.mx, self.mxn = z(S, H), z(S, 2 * H), z(S, H), z(1, H)
         self._hstage, self._sel, self._last_S = z(S, H), z(1, dtype=i32), None  # reference-style calls
         self.dlogits = z(1, a.vocab)
+        # draft head (mtp.py:156-196): the 4-bit full-vocabulary head, or a vocabulary subset
+        # (set_draft_head); dloc holds each draft's row in the draft head's logits
+        self.dproj, self.dids, self.dloc = W["lm_head_q"], None, z(max(k, 1), dtype=i32)
         self.probs = z(k, dtype=f32)  # adaptive k: the draft head's argmax probability per draft
         self.KMAX = 2048  # k_for's largest candidate count (lm_head2.py:32-36)
         self.fine, self.idx = z(S, self.KMAX), z(S, self.KMAX, dtype=i32)
@@ -108,6 +111,8 @@ class MTPDecoder:
         self.qmv_log = None    # list of the _qmv argument tuples of a cycle while recording
         if tau is not None:
             self.set_tau(tau)
+        if draft_head is not None:
+            self.set_draft_head(draft_head)
 
     def set_tau(self, tau: float | None):
         """Adaptive draft count (mtp.py:229-238, generate_mtp's tau): None verifies every draft; a number
@@ -121,6 +126,24 @@ class MTPDecoder:
             if tau is None:
                 self.ctrl[C["NUSE"]] = 0
         self.tau = tau
+
+    def set_draft_head(self, head):
+        """The head that proposes drafts (mtp.py:156-167 DraftHead): None for the model's full-vocabulary
+        4-bit head, or a DraftHead over a vocabulary subset (load_draft_head).  It changes the drafts,
+        never the output stream (the full two-stage head verifies).  A change drops the captured graph."""
+        proj = self.W["lm_head_q"] if head is None else head.proj
+        ids = None if head is None else head.ids
+        if proj.in_features != self.a.hidden:
+            raise ValueError("the draft head takes the hidden size")
+        if ids is not None:
+            ids = torch.as_tensor(ids, dtype=torch.int32, device=self.dev).contiguous()
+            if ids.numel() != proj.out_features:
+                raise ValueError("a draft head needs one vocabulary id per row")
+        if proj is self.dproj and (ids is None) == (self.dids is None) and (ids is None or torch.equal(ids, self.dids)):
+            return
+        self.dproj, self.dids = proj, ids
+        self.dlogits = torch.zeros(1, proj.out_features, dtype=torch.bfloat16, device=self.dev)
+        self.graph = None
 
     def set_sampling(self, sampling: Sampling | None, _init: bool = False):
         """Greedy (None or temperature 0) or exact speculative sampling with these parameters; the
@@ -318,7 +341,8 @@ class MTPDecoder:
     def mtp_step(self, hidden, hidden_sel, tok, rows, out_sel, draft_out, with_draft=True):
         """mtp.py:199-209 for `rows` (hidden, token) pairs at MTP positions MPOS + r: the MTP layer
         output lands in self.mx; the draft token of row out_sel (device int, or row 0) goes to
-        draft_out (DraftHead.token = argmax of the full-vocab 4-bit head, mtp.py:165-167)."""
+        draft_out, a slot of self.drafts (DraftHead.token = the id of the draft head's argmax row,
+        mtp.py:165-167)."""
         a, M = self.a, self.W["mtp"]
         H = a.hidden
         self._embed(tok, rows, self.memb)
@@ -334,9 +358,13 @@ class MTPDecoder:
             return
         self._chk(self.L.qmtp_rmsnorm(self.mx.data_ptr(), H, out_sel, M["norm"].data_ptr(), a.eps,
                                       self.mxn.data_ptr(), H, 1, H, self._st()), "rmsnorm")
-        self._qmv(self.mxn, self.W["lm_head_q"], self.dlogits, 1)
-        self._chk(self.L.qmtp_argmax_bf16(self.dlogits.data_ptr(), a.vocab, 1, a.vocab, draft_out,
-                                          self.argmax_ws.data_ptr(), self.argmax_ws.numel(), self._st()), "argmax")
+        Vd = self.dproj.out_features
+        self._qmv(self.mxn, self.dproj, self.dlogits, 1)
+        loc = self.dloc.data_ptr() + (draft_out - self.drafts.data_ptr())  # draft_out points into drafts
+        self._chk(self.L.qmtp_argmax_bf16_ids(self.dlogits.data_ptr(), Vd, 1, Vd,
+                                              None if self.dids is None else self.dids.data_ptr(), draft_out, loc,
+                                              self.argmax_ws.data_ptr(), self.argmax_ws.numel(), self._st()),
+                  "argmax")
 
     def _sample(self, first_row=-1):
         """Sampling mode: the emitted tokens (verify) or the first token (first_row) over a_tok."""
@@ -373,8 +401,9 @@ class MTPDecoder:
     def _draft_prob(self, j):
         """Adaptive k: probability of draft j under the draft head (mtp.py:222-223)."""
         if self.tau is not None:
-            self._chk(self.L.qmtp_draft_prob(self.dlogits.data_ptr(), self.a.vocab, self.drafts.data_ptr() + 4 * j,
-                                             self.probs.data_ptr() + 4 * j, self._st()), "draft_prob")
+            self._chk(self.L.qmtp_draft_prob(self.dlogits.data_ptr(), self.dproj.out_features,
+                                             self.dloc.data_ptr() + 4 * j, self.probs.data_ptr() + 4 * j, self._st()),
+                      "draft_prob")
 
     def cycle(self):
         """One verify + accept + draft cycle (mtp.py:268-294), device-side only."""
@@ -576,24 +605,61 @@ def decode_mtp(dec: MTPDecoder, prompt_ids, max_tokens, eos=(), use_graph=True, 
 
 
 class DraftHead:
-    """mtp.py:156-167: the cheap head that proposes drafts.  Only the full-vocabulary form exists here
-    (ids=None): the 4-bit affine copy of the lm_head, as the synthetic configuration uses."""
+    """mtp.py:156-167: the cheap head that proposes drafts.  proj is a 4-bit QuantizedLinear over some
+    rows of the lm_head; ids (None, or int32 [rows]) the vocabulary id of each row -- with ids it scores
+    only that subset of the vocabulary."""
 
     def __init__(self, proj, ids=None):
         if ids is not None:
-            raise NotImplementedError("a draft head over a vocabulary subset is not built (full vocabulary only)")
+            ids = torch.as_tensor(ids, dtype=torch.int32, device=proj.weight.device).contiguous()
+            if ids.numel() != proj.out_features:
+                raise ValueError("one vocabulary id per row of proj")
         self.proj, self.ids = proj, ids
 
     def __call__(self, x):
         return self.proj(x)
 
     def token(self, logits):
-        return torch.argmax(logits, dim=-1)
+        i = torch.argmax(logits, dim=-1)
+        return i if self.ids is None else self.ids[i]
+
+
+def load_draft_head(vocab, quant=None, freq=False, extra_ids=(), *, lm, counts=None):
+    """mtp.py:170-196 with the reference's arguments: a draft head over `vocab` rows of the lm_head, the
+    first `vocab` ids or, with freq=True, the `vocab` most frequent ids of a corpus (`counts`: the
+    per-id counts build_draft_vocab.py writes, an array or the path of its .npy file) plus extra_ids,
+    ascending.  It never changes the output (the full head verifies), only the acceptance.  quant: the
+    4-bit g64 affine format of the model's head (the reference's {"bits": 4, "group_size": 64}); its
+    rows are quantized row by row, so the subset is a gather of the model's 4-bit head (lm_head_q).
+    `lm` (keyword) is the model; the reference reads the head from its checkpoint instead."""
+    from .qmv_kernel import QuantizedLinear
+
+    if quant is not None and (quant.get("bits", 4), quant.get("group_size", 64)) != (4, 64):
+        raise NotImplementedError("draft heads are 4-bit, group 64 (the model's coarse head format)")
+    full = lm.weights["lm_head_q"]
+    if full.mode != "affine":
+        raise NotImplementedError("a vocabulary-subset draft head over an NVFP4 head is not built")
+    V = full.out_features
+    if freq:
+        if counts is None:
+            raise ValueError("freq=True needs the corpus counts (counts=...)")
+        c = np.load(counts) if isinstance(counts, (str, bytes)) or hasattr(counts, "__fspath__") else np.asarray(counts)
+        c = c[:V]
+        top = set(np.argsort(-c)[:vocab].tolist()) | {int(e) for e in extra_ids}
+        rows = torch.tensor(sorted(top), dtype=torch.int64, device=full.weight.device)
+        proj = QuantizedLinear(full.weight.index_select(0, rows).contiguous(),
+                               full.scales.index_select(0, rows).contiguous(),
+                               full.biases.index_select(0, rows).contiguous())
+        return DraftHead(proj, rows.to(torch.int32))
+    n = min(int(vocab), V)
+    if n == V:
+        return DraftHead(full)
+    return DraftHead(QuantizedLinear(full.weight[:n], full.scales[:n], full.biases[:n]))
 
 
 def _check_head(lm, head):
-    if head is not None and getattr(head, "proj", None) is not lm.weights["lm_head_q"]:
-        raise NotImplementedError("the draft head must be the model's 4-bit full-vocabulary head (lm_head_q)")
+    if head is not None and not isinstance(head, DraftHead):
+        raise TypeError("head must be a DraftHead (load_draft_head) or None")
 
 
 def _check_mtp(lm, mtp):
@@ -648,6 +714,7 @@ def mtp_step(lm, mtp, hidden, tokens, mcache: MTPDecoder, head=None):
     n = tok.numel()
     if hid.shape[0] != n or not 1 <= n <= dec.S:
         raise ValueError(f"mtp_step takes 1..{dec.S} (hidden, token) pairs with this cache")
+    dec.set_draft_head(head)
     return _mtp_pairs(dec, hid, tok, commit=True)
 
 
@@ -677,6 +744,7 @@ def draft_chain(lm, mtp, hidden, tokens, mcache: MTPDecoder, k, head=None, chain
     tok = torch.as_tensor(tokens, dtype=torch.int32).reshape(-1).to(dec.dev)
     if hid.shape[0] != tok.numel() or not 1 <= tok.numel() <= dec.S:
         raise ValueError(f"draft_chain takes 1..{dec.S} (hidden, token) pairs with this cache")
+    dec.set_draft_head(head)
     drafts, probs = [], []
     logits, x, _ = _mtp_pairs(dec, hid, tok, commit=True)
     mpos = int(dec.ctrl[C["MPOS"]].item())
@@ -684,11 +752,12 @@ def draft_chain(lm, mtp, hidden, tokens, mcache: MTPDecoder, k, head=None, chain
         if i:
             logits, x, _ = _mtp_pairs(dec, x[0], drafts[-1].reshape(1), commit=False)
             dec.ctrl[C["MPOS"]] += 1  # the chained entry is visible to the next chained step
-        drafts.append(torch.argmax(logits[0, -1]).to(torch.int32).reshape(1))
+        local = torch.argmax(logits[0, -1]).to(torch.int32).reshape(1)  # first maximum: the lower row
+        drafts.append(local if dec.dids is None else dec.dids[local.long()])
         if with_probs:
             pr = torch.empty(1, dtype=torch.float32, device=dec.dev)
             row = logits[0, -1].contiguous()
-            _lib.check(dec.L.qmtp_draft_prob(row.data_ptr(), row.numel(), drafts[-1].data_ptr(), pr.data_ptr(),
+            _lib.check(dec.L.qmtp_draft_prob(row.data_ptr(), row.numel(), local.data_ptr(), pr.data_ptr(),
                                              _lib.stream()), "draft_prob")
             probs.append(pr)
     dec.ctrl[C["MPOS"]] = mpos
@@ -720,6 +789,7 @@ def generate_mtp(lm, mtp, prompt_ids, max_tokens, eos, head=None, k=1, bb_hidden
     dec = lm.session(k=k, max_tokens=max_tokens)
     dec.set_sampling(None)
     dec.set_tau(tau)
+    dec.set_draft_head(head)
     return decode_mtp(dec, prompt_ids, max_tokens, tuple(eos))
 
 

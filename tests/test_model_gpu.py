@@ -103,3 +103,48 @@ def test_draft_prob_matches_oracle(dev):
         _lib.check(_lib.lib().qmtp_draft_prob(to_torch(lg, dev).data_ptr(), V, tok.data_ptr(), pr.data_ptr(),
                                               _lib.stream()), "draft_prob")
         assert float(pr.item()) == ops.draft_prob(lg, t), V
+
+
+@pytest.mark.parametrize("mode,tau", [("first", 3e-6), ("freq", 6e-6)])  # taus giving 1.3 and 1.6 drafts a cycle
+def test_draft_head_subset_matches_oracle(small_pair, mode, tau):
+    """A draft head over a vocabulary subset (mtp.py:156-196 DraftHead with ids, load_draft_head): the
+    first drafts after the prompt, the adaptive draft count's statistics (which read the subset head's
+    argmax probabilities every cycle) and the stream equal the oracle's with the same subset, and the
+    stream still equals plain greedy decoding."""
+    from qmtp import model as qm
+    from qmtp.mtp import decode_mtp, load_draft_head
+
+    orc, W = small_pair
+    lm = qm.Model(qm.SMALL, W)
+    V = om.SMALL.vocab
+    if mode == "first":
+        head = load_draft_head(5000, {"bits": 4, "group_size": 64}, lm=lm)
+        assert head.ids is None and head.proj.out_features == 5000
+        orc.set_draft_head(5000)
+    else:
+        counts = np.random.default_rng(3).integers(0, 1000, V)  # many equal counts
+        head = load_draft_head(3000, None, True, (7, V - 1), lm=lm, counts=counts)
+        orc.set_draft_head(3000, counts, (7, V - 1))
+        assert head.ids.tolist() == orc.draft_ids.tolist()
+        assert 7 in orc.draft_ids and V - 1 in orc.draft_ids
+    try:
+        p = prompt(33, seed=8)
+        _, _, t, drafts = orc.prefill(p, 2)
+        dec = _decoder(W)
+        dec.set_draft_head(head)
+        dec.prefill(p)
+        assert dec.tokens_in.tolist() == [int(t)] + [int(d) for d in drafts]
+        if mode == "freq":
+            assert set(int(d) for d in drafts) <= set(orc.draft_ids.tolist())
+        ref, rst = orc.generate_mtp(p, 40, tau=tau)
+        assert ref == orc.generate_greedy(p, 40)
+        assert 1.0 < rst["borradores_ciclo"] < 2.0
+        dec = _decoder(W)
+        dec.set_draft_head(head)
+        dec.set_tau(tau)
+        out, st = decode_mtp(dec, p, 40, use_graph=True)
+        assert out == ref
+        assert st["acept"] == rst["acept"] and st["cycles"] == rst["cycles"]
+        assert st["borradores_ciclo"] == rst["borradores_ciclo"]
+    finally:
+        orc.set_draft_head(None)
