@@ -209,7 +209,8 @@ __global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld,
 // shared memory.  Rank 0 then merges the 8 splits in order through distributed shared memory.
 constexpr int kAttnSplits = 8;
 constexpr int kAttnBatch = 8;   // keys a warp fetches at once in the score pass
-constexpr int kAttnVStage = 32; // value rows of a split copied to shared memory while the scores run
+constexpr int kAttnVStage = 128; // value rows of a split copied to shared memory while the scores run
+                                 // (64 KB: three CTAs an SM still fit; contexts up to 1024 keys)
 
 __global__ void __launch_bounds__(256)
 attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ gate, const uint16_t* __restrict__ kc,
@@ -327,16 +328,18 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
     s_md[1] = den;
   }
   if (tid < Dh / 2) {
-    // thread t owns dims 2t, 2t+1: one 32-bit word per key, keys ascending; the first kAttnVStage
-    // keys from shared memory, the rest 32 keys in flight per batch
+    // thread t owns dims 2t, 2t+1: one 32-bit word per key, keys ascending, 32 keys a batch; the
+    // first kAttnVStage keys from shared memory, the rest from global memory
     float num0 = 0.0f, num1 = 0.0f;
     const uint32_t* vb = reinterpret_cast<const uint32_t*>(vc + ((long long)kh * max_pos + w) * Dh) + tid;
     for (int n0 = 0; n0 < nk; n0 += 32) {
       uint32_t v2[32];
-      static_assert(kAttnVStage == 32, "the first batch is the staged one");
+      static_assert(kAttnVStage % 32 == 0, "a batch is staged whole or not at all");
+      const bool staged = n0 < kAttnVStage;
 #pragma unroll
       for (int u = 0; u < 32; ++u)
-        if (n0 + u < nk) v2[u] = n0 == 0 ? s_v[u * (Dh / 2) + tid] : vb[(long long)kAttnSplits * (n0 + u) * (Dh / 2)];
+        if (n0 + u < nk)
+          v2[u] = staged ? s_v[(n0 + u) * (Dh / 2) + tid] : vb[(long long)kAttnSplits * (n0 + u) * (Dh / 2)];
 #pragma unroll
       for (int u = 0; u < 32; ++u)
         if (n0 + u < nk) {
