@@ -338,6 +338,14 @@ int qmtp_attention(const void* q, const void* gate, const void* k_cache, const v
                    int S, int nq, int nkv, int Dh, const int* pos_ptr, int pos_add, void* out,
                    void* stream);
 
+/* qmtp_attn_prep followed by qmtp_attention in one launch, with the same results and cache writes:
+ * the attention kernel prepares its own q row and the new key it needs from the projection output
+ * qkv (the arguments of qmtp_attn_prep), reads the gate there, and writes the S new key / value rows
+ * to the caches.  S <= 8; Dh 256, rotary 64; qkv, qn_w, kn_w, the caches 16-byte aligned. */
+int qmtp_attention_fused(const void* qkv, int ld, int S, int nq, int nkv, int Dh, int rotary, const void* qn_w,
+                         const void* kn_w, float eps, const float* cos_t, const float* sin_t, const int* pos_ptr,
+                         int pos_add, void* k_cache, void* v_cache, int max_pos, void* out, void* stream);
+
 /* SwiGLU of mlx-lm's MLP: out [S, I] = bf16(silu(gate) * up), gu [S, ld] = (gate | up) columns. */
 int qmtp_swiglu(const void* gu, int ld, int S, int I, void* out, void* stream);
 

@@ -128,31 +128,13 @@ __global__ void rmsnorm_wide_kernel(const uint16_t* __restrict__ x, long long ld
 }
 
 // ----------------------------------------------------------------------------- attention prep
-// One warp per (token s, head hh) with hh < nq query heads, then nkv key heads; Dh == 256,
-// lane l owns dims [8l, 8l+8); RoPE pairs (i, i + R/2) for i < R/2 (R == 64: lanes 0..7).
-__global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld, int S, int nq, int nkv,
-                                 const uint16_t* __restrict__ qn_w, const uint16_t* __restrict__ kn_w, float eps,
-                                 const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                 const int* __restrict__ pos_ptr, int pos_add, uint16_t* __restrict__ qo,
-                                 uint16_t* __restrict__ gate, uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
-                                 int max_pos, unsigned* err) {
-  pdl_trigger();
+// One (token, head) row of q or k, Dh == 256, by one warp: RMS norm with the weight row (lane l owns
+// dims [8l, 8l+8), wn4 its 8 weights), then rotate-half RoPE over dims [0, 64) at position pos (pairs
+// (i, i + 32), lanes 0..7, lane l paired with lane l ^ 4).  Returns the lane's 8 bf16 results packed.
+__device__ __forceinline__ uint4 prep_head_row(const uint16_t* __restrict__ src, uint4 wn4, float eps,
+                                               const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                               int pos, int lane) {
   constexpr int Dh = 256, NP = 8, RH = 32;  // rotary half
-  const int lane = threadIdx.x & 31;
-  const int wid = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  if (wid >= S * (nq + nkv)) return;
-  const int s = wid / (nq + nkv), hh = wid - s * (nq + nkv);
-  // the q / k norm weights are constant: fetched while the previous kernel may still run
-  const uint4 wn4 = *reinterpret_cast<const uint4*>((hh < nq ? qn_w : kn_w) + NP * lane);
-  pdl_wait();
-  const int pos = (pos_ptr ? *pos_ptr : 0) + pos_add + s;
-  if (pos < 0 || pos >= max_pos) {
-    if (lane == 0) atomicOr(err, DEVERR_BADARG);
-    return;
-  }
-  const bool isq = hh < nq;
-  const uint16_t* row = qkv + (long long)s * ld;
-  const uint16_t* src = isq ? row + (long long)hh * 2 * Dh : row + (long long)nq * 2 * Dh + (long long)(hh - nq) * Dh;
   float x[NP];
   {
     const uint4 u = *reinterpret_cast<const uint4*>(src + NP * lane);
@@ -171,7 +153,6 @@ __global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld,
     for (int e = 0; e < NP; ++e)
       x[e] = R(__fmul_rn((e & 1) ? bfhi(wv[e >> 1]) : bflo(wv[e >> 1]), R(__fmul_rn(x[e], r))));
   }
-  // rotate-half over dims [0, 64): lane l (< 8) pairs with lane l ^ 4
   float o[NP];
 #pragma unroll
   for (int e = 0; e < NP; ++e) {
@@ -188,7 +169,35 @@ __global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld,
   uint32_t pk[4];
 #pragma unroll
   for (int h = 0; h < 4; ++h) pk[h] = f2bf(o[2 * h]) | (uint32_t(f2bf(o[2 * h + 1])) << 16);
-  const uint4 packed = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  return make_uint4(pk[0], pk[1], pk[2], pk[3]);
+}
+
+// One warp per (token s, head hh) with hh < nq query heads, then nkv key heads (prep_head_row); the
+// gate and v rows are copied through.
+__global__ void attn_prep_kernel(const uint16_t* __restrict__ qkv, long long ld, int S, int nq, int nkv,
+                                 const uint16_t* __restrict__ qn_w, const uint16_t* __restrict__ kn_w, float eps,
+                                 const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                 const int* __restrict__ pos_ptr, int pos_add, uint16_t* __restrict__ qo,
+                                 uint16_t* __restrict__ gate, uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
+                                 int max_pos, unsigned* err) {
+  pdl_trigger();
+  constexpr int Dh = 256, NP = 8;
+  const int lane = threadIdx.x & 31;
+  const int wid = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (wid >= S * (nq + nkv)) return;
+  const int s = wid / (nq + nkv), hh = wid - s * (nq + nkv);
+  // the q / k norm weights are constant: fetched while the previous kernel may still run
+  const uint4 wn4 = *reinterpret_cast<const uint4*>((hh < nq ? qn_w : kn_w) + NP * lane);
+  pdl_wait();
+  const int pos = (pos_ptr ? *pos_ptr : 0) + pos_add + s;
+  if (pos < 0 || pos >= max_pos) {
+    if (lane == 0) atomicOr(err, DEVERR_BADARG);
+    return;
+  }
+  const bool isq = hh < nq;
+  const uint16_t* row = qkv + (long long)s * ld;
+  const uint16_t* src = isq ? row + (long long)hh * 2 * Dh : row + (long long)nq * 2 * Dh + (long long)(hh - nq) * Dh;
+  const uint4 packed = prep_head_row(src, wn4, eps, cos_t, sin_t, pos, lane);
   if (isq) {
     *reinterpret_cast<uint4*>(qo + ((long long)s * nq + hh) * Dh + NP * lane) = packed;
     *reinterpret_cast<uint4*>(gate + ((long long)s * nq + hh) * Dh + NP * lane) =
@@ -212,11 +221,34 @@ constexpr int kAttnBatch = 8;   // keys a warp fetches at once in the score pass
 constexpr int kAttnVStage = 128; // value rows of a split copied to shared memory while the scores run
                                  // (64 KB: three CTAs an SM still fit; contexts up to 1024 keys)
 
-__global__ void __launch_bounds__(256)
-attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ gate, const uint16_t* __restrict__ kc,
-                 const uint16_t* __restrict__ vc, int max_pos, int nq, int nkv, const int* __restrict__ pos_ptr,
-                 int pos_add, uint16_t* __restrict__ out, unsigned* err) {
+// FUSED: the kernel also does attn_prep_kernel's work for what it reads (qmtp_attention_fused).  Warp 0
+// prepares this CTA's q row from the projection output, warp 1 the split's new key (of the S new
+// positions at most one falls in a split, S <= 8) and copies its value row; the new key and value
+// stand in for the cache rows wherever they are used, and one CTA per (kv head, new position) writes
+// them to the caches.  The gate is read from the projection output.
+struct AttnFuse {
+  const uint16_t* qkv;   // bf16 [S, ld]: per query head (q, gate), then k heads, then v heads
+  long long ld;
+  const uint16_t* qn_w;  // bf16 [Dh] q / k RMS norm weights
+  const uint16_t* kn_w;
+  float eps;
+  const float* cos_t;    // [max_pos, 32] RoPE tables
+  const float* sin_t;
+  int S;
+};
+
+template <bool FUSED>
+__global__ void __launch_bounds__(256, 3)  // 3 CTAs an SM: the 8-CTA clusters of a launch fit in one wave
+attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ gate, uint16_t* __restrict__ kc,
+                 uint16_t* __restrict__ vc, int max_pos, int nq, int nkv, const int* __restrict__ pos_ptr,
+                 int pos_add, uint16_t* __restrict__ out, unsigned* err, AttnFuse F) {
   pdl_trigger();
+  __shared__ __align__(16) uint4 s_q[32], s_knew[32], s_vnew[32];  // FUSED: prepared q, new key and value rows
+  uint4 wq4 = make_uint4(0, 0, 0, 0);  // FUSED: the lane's 8 norm weights (constants, fetched before the wait)
+  if (FUSED) {
+    const int wp = threadIdx.x >> 5;
+    if (wp < 2) wq4 = *reinterpret_cast<const uint4*>((wp == 0 ? F.qn_w : F.kn_w) + 8 * (threadIdx.x & 31));
+  }
   {
     // this split's key and value rows into L2 while the previous launches finish; the position is
     // read before the wait as an address hint only (a stale value prefetches other rows, no more)
@@ -250,13 +282,21 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
   }
   const int kh = h / (nq / nkv);
   const int nk = w < L ? (L - w + kAttnSplits - 1) / kAttnSplits : 0;  // keys of this split
+  // FUSED: this split's new key, if any: position pos0 + t_new (t_new <= s) is key n_new of the split
+  const int pos0 = L - s - 1;
+  int t_new = -1, n_new = -1;
+  if (FUSED) {
+    const int t = ((w - pos0) % kAttnSplits + kAttnSplits) % kAttnSplits;
+    if (t <= s) { t_new = t; n_new = (pos0 + t - w) / kAttnSplits; }
+  }
   // loads that do not wait for q: the first kAttnVStage value rows of the split into shared memory
   // (asynchronous copies, 16 bytes a thread and step) and this warp's first round of key rows
   {
     const int nv = min(nk, kAttnVStage);
     for (int c = tid; c < nv * (Dh / 8); c += 256) {
       const int n = c / (Dh / 8), part = c - n * (Dh / 8);
-      cp_async16(s_v + n * (Dh / 2) + part * 4, vc + ((long long)kh * max_pos + w + kAttnSplits * n) * Dh + part * 8);
+      if (n != n_new)  // FUSED: the new row is written below from the projection output
+        cp_async16(s_v + n * (Dh / 2) + part * 4, vc + ((long long)kh * max_pos + w + kAttnSplits * n) * Dh + part * 8);
     }
     cp_async_commit();
   }
@@ -266,9 +306,29 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
     const int n = warp + 8 * u;
     if (n < nk) kr[u] = *reinterpret_cast<const uint4*>(kc + ((long long)kh * max_pos + w + kAttnSplits * n) * Dh + NP * lane);
   }
+  if (FUSED) {
+    if (warp == 0) {
+      s_q[lane] = prep_head_row(F.qkv + (long long)s * F.ld + (long long)h * 2 * Dh, wq4, F.eps, F.cos_t, F.sin_t,
+                                pos0 + s, lane);
+    } else if (warp == 1 && t_new >= 0) {
+      const uint16_t* row = F.qkv + (long long)t_new * F.ld + (long long)nq * 2 * Dh;
+      const uint4 kk = prep_head_row(row + (long long)kh * Dh, wq4, F.eps, F.cos_t, F.sin_t, pos0 + t_new, lane);
+      const uint4 vv = *reinterpret_cast<const uint4*>(row + (long long)nkv * Dh + (long long)kh * Dh + NP * lane);
+      s_knew[lane] = kk;
+      s_vnew[lane] = vv;
+      if (n_new < kAttnVStage) *reinterpret_cast<uint4*>(s_v + n_new * (Dh / 2) + 4 * lane) = vv;
+      // the caches: one CTA per (kv head, new position) -- the first query head of the group, last token
+      if (h % (nq / nkv) == 0 && s == F.S - 1) {
+        const long long r = ((long long)kh * max_pos + pos0 + t_new) * Dh + NP * lane;
+        *reinterpret_cast<uint4*>(kc + r) = kk;
+        *reinterpret_cast<uint4*>(vc + r) = vv;
+      }
+    }
+    __syncthreads();
+  }
   float qf[NP];
   {
-    const uint4 u = *reinterpret_cast<const uint4*>(q + ((long long)s * nq + h) * Dh + NP * lane);
+    const uint4 u = FUSED ? s_q[lane] : *reinterpret_cast<const uint4*>(q + ((long long)s * nq + h) * Dh + NP * lane);
     const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) { qf[2 * e] = bflo(uu[e]); qf[2 * e + 1] = bfhi(uu[e]); }
@@ -290,7 +350,8 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
     float acc[kAttnBatch];
 #pragma unroll
     for (int u = 0; u < kAttnBatch; ++u) {
-      const uint32_t uu[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
+      const uint4 k4 = (FUSED && n0 + 8 * u == n_new) ? s_knew[lane] : kr[u];
+      const uint32_t uu[4] = {k4.x, k4.y, k4.z, k4.w};
       acc[u] = 0.0f;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -339,7 +400,9 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
 #pragma unroll
       for (int u = 0; u < 32; ++u)
         if (n0 + u < nk)
-          v2[u] = staged ? s_v[(n0 + u) * (Dh / 2) + tid] : vb[(long long)kAttnSplits * (n0 + u) * (Dh / 2)];
+          v2[u] = staged ? s_v[(n0 + u) * (Dh / 2) + tid]
+                  : (FUSED && n0 + u == n_new) ? reinterpret_cast<const uint32_t*>(s_vnew)[tid]
+                                               : vb[(long long)kAttnSplits * (n0 + u) * (Dh / 2)];
 #pragma unroll
       for (int u = 0; u < 32; ++u)
         if (n0 + u < nk) {
@@ -376,7 +439,8 @@ attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ ga
         acc = __fmaf_rn(cw, nn[ww], acc);
       }
     const float o = R(__fdiv_rn(acc, dsum));
-    const float gt = bf2f(gate[((long long)s * nq + h) * Dh + d]);
+    const float gt = bf2f(FUSED ? F.qkv[(long long)s * F.ld + (long long)h * 2 * Dh + Dh + d]
+                                : gate[((long long)s * nq + h) * Dh + d]);
     out[(long long)s * nq * Dh + (long long)h * Dh + d] = f2bf(__fmul_rn(o, sigmoid_bf(gt)));
   }
   cluster_sync_all();  // rank 0 has read the other CTAs' shared memory before they exit
@@ -559,19 +623,19 @@ extern "C" int qmtp_attn_prep(const void* qkv, int ld, int S, int nq, int nkv, i
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 
-extern "C" int qmtp_attention(const void* q, const void* gate, const void* k_cache, const void* v_cache, int max_pos,
-                              int S, int nq, int nkv, int Dh, const int* pos_ptr, int pos_add, void* out,
-                              void* stream) {
-  if (!q || !gate || !k_cache || !v_cache || !out) return QMTP_ERR_ARG;
+static int attention_launch(bool fused, const void* q, const void* gate, void* k_cache, void* v_cache, int max_pos,
+                            int S, int nq, int nkv, int Dh, const int* pos_ptr, int pos_add, void* out, const AttnFuse& F,
+                            void* stream) {
   if (Dh != 256 || S < 1 || nq < 1 || nkv < 1 || nq % nkv || max_pos < 8) return QMTP_ERR_UNSUPPORTED;
-  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache)) return QMTP_ERR_ALIGN;  // 16-byte rows
+  if (!aligned16(k_cache) || !aligned16(v_cache)) return QMTP_ERR_ALIGN;  // 16-byte rows
   // scores etc. (rounded up to 16 bytes), then the staged value rows
   const size_t smem = ((size_t(Dh) + 2 + 8 + size_t(max_pos / kAttnSplits + 1) + 3) & ~size_t(3)) * sizeof(float) +
                       size_t(kAttnVStage) * Dh * sizeof(uint16_t);
   if (smem > 200 * 1024) return QMTP_ERR_SHAPE;
-  static const cudaError_t attr =
-      cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  if (attr != cudaSuccess) return QMTP_ERR_CUDA;
+  static const cudaError_t attr[2] = {
+      cudaFuncSetAttribute(attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+      cudaFuncSetAttribute(attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)};
+  if (attr[0] != cudaSuccess || attr[1] != cudaSuccess) return QMTP_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(nq * kAttnSplits), unsigned(S));
   cfg.blockDim = dim3(256);
@@ -586,10 +650,33 @@ extern "C" int qmtp_attention(const void* q, const void* gate, const void* k_cac
   at[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = at;
   cfg.numAttrs = 2;
-  cudaLaunchKernelEx(&cfg, attention_kernel, static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(gate),
-                     static_cast<const uint16_t*>(k_cache), static_cast<const uint16_t*>(v_cache), max_pos, nq, nkv,
-                     pos_ptr, pos_add, static_cast<uint16_t*>(out), device_error_ptr());
+  cudaLaunchKernelEx(&cfg, fused ? attention_kernel<true> : attention_kernel<false>, static_cast<const uint16_t*>(q),
+                     static_cast<const uint16_t*>(gate), static_cast<uint16_t*>(k_cache),
+                     static_cast<uint16_t*>(v_cache), max_pos, nq, nkv, pos_ptr, pos_add, static_cast<uint16_t*>(out),
+                     device_error_ptr(), F);
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_attention(const void* q, const void* gate, const void* k_cache, const void* v_cache, int max_pos,
+                              int S, int nq, int nkv, int Dh, const int* pos_ptr, int pos_add, void* out,
+                              void* stream) {
+  if (!q || !gate || !k_cache || !v_cache || !out) return QMTP_ERR_ARG;
+  if (!aligned16(q)) return QMTP_ERR_ALIGN;
+  return attention_launch(false, q, gate, const_cast<void*>(k_cache), const_cast<void*>(v_cache), max_pos, S, nq, nkv,
+                          Dh, pos_ptr, pos_add, out, AttnFuse{}, stream);
+}
+
+extern "C" int qmtp_attention_fused(const void* qkv, int ld, int S, int nq, int nkv, int Dh, int rotary,
+                                    const void* qn_w, const void* kn_w, float eps, const float* cos_t,
+                                    const float* sin_t, const int* pos_ptr, int pos_add, void* k_cache, void* v_cache,
+                                    int max_pos, void* out, void* stream) {
+  if (!qkv || !qn_w || !kn_w || !cos_t || !sin_t || !k_cache || !v_cache || !out) return QMTP_ERR_ARG;
+  if (Dh != 256 || rotary != 64 || S < 1 || S > kAttnSplits || ld % 8) return QMTP_ERR_UNSUPPORTED;
+  if (!aligned16(qkv) || !aligned16(qn_w) || !aligned16(kn_w)) return QMTP_ERR_ALIGN;
+  AttnFuse F{static_cast<const uint16_t*>(qkv), ld, static_cast<const uint16_t*>(qn_w),
+             static_cast<const uint16_t*>(kn_w), eps, cos_t, sin_t, S};
+  return attention_launch(true, nullptr, nullptr, k_cache, v_cache, max_pos, S, nq, nkv, Dh, pos_ptr, pos_add, out, F,
+                          stream);
 }
 
 extern "C" int qmtp_swiglu(const void* gu, int ld, int S, int I, void* out, void* stream) {

@@ -77,7 +77,6 @@ class MTPDecoder:
         self.ygdn = z(S, a.lin_hv, a.lin_dv, dtype=f32)
         self.gdn_out = z(S, a.lin_hv * a.lin_dv)
         self.att_out = z(S, a.n_heads * a.head_dim)
-        self.qb, self.gb = z(S, a.n_heads, a.head_dim), z(S, a.n_heads, a.head_dim)
         self.gu, self.act = z(S, 2 * a.intermediate), z(S, a.intermediate)
         self.memb, self.mcat, self.mx, self.mxn = z(S, H), z(S, 2 * H), z(S, H), z(1, H)
         self._hstage, self._sel, self._last_S = z(S, H), z(1, dtype=i32), None  # reference-style calls
@@ -287,14 +286,13 @@ class MTPDecoder:
         projection input is the normalised rows in self.xn."""
         a = self.a
         self._qmv(self.xn, L["qkv_proj"], self.proj, rows, ldy=self.proj.shape[1])
-        self._chk(self.L.qmtp_attn_prep(self.proj.data_ptr(), self.proj.shape[1], rows, a.n_heads, a.n_kv,
-                                        a.head_dim, a.rotary_dim, L["q_norm"].data_ptr(), L["k_norm"].data_ptr(),
-                                        a.eps, self.cos.data_ptr(), self.sin.data_ptr(), self._cp(pos_slot), 0,
-                                        self.qb.data_ptr(), self.gb.data_ptr(), kc.data_ptr(), vc.data_ptr(),
-                                        a.max_pos, self._st()), "attn_prep")
-        self._chk(self.L.qmtp_attention(self.qb.data_ptr(), self.gb.data_ptr(), kc.data_ptr(), vc.data_ptr(),
-                                        a.max_pos, rows, a.n_heads, a.n_kv, a.head_dim, self._cp(pos_slot), 0,
-                                        self.att_out.data_ptr(), self._st()), "attention")
+        # q/k norms, RoPE, the cache writes and the attention in one launch (qmtp_attn_prep's work done by
+        # the attention kernel for the rows it reads)
+        self._chk(self.L.qmtp_attention_fused(self.proj.data_ptr(), self.proj.shape[1], rows, a.n_heads, a.n_kv,
+                                              a.head_dim, a.rotary_dim, L["q_norm"].data_ptr(), L["k_norm"].data_ptr(),
+                                              a.eps, self.cos.data_ptr(), self.sin.data_ptr(), self._cp(pos_slot), 0,
+                                              kc.data_ptr(), vc.data_ptr(), a.max_pos, self.att_out.data_ptr(),
+                                              self._st()), "attention")
         self._qmv(self.att_out, L["o_proj"], x, rows, res=x)
 
     def _mlp(self, L, x, rows):
