@@ -324,6 +324,15 @@ int qmtp_embed_nvfp4(const int* tokens, int T, const void* wq, const void* scale
 int qmtp_rmsnorm(const void* x, int ld_x, const int* row_sel, const void* w, float eps, void* out,
                  int ld_out, int M, int D, void* stream);
 
+/* Embedding rows (affine g64 table, as qmtp_embed) and RMS norms (as qmtp_rmsnorm) in one launch:
+ * row m of job 0 is the embedding of tok[m], written to raw (bf16 [M, >= D], row stride ld_raw; may be
+ * NULL) and, RMS-normalised with w0, to out0; job 1 (x1 not NULL) is qmtp_rmsnorm of rows *row_sel1 + m
+ * (row_sel1 may be NULL: 0) of x1 with w1 into out1.  The decoder uses it for the embedding + layer 0's
+ * input norm of a verify step and for an MTP step's embedding + its two pre-fc norms (mtp.py:202-203). */
+int qmtp_embed_rmsnorm(const int* tok, int M, const void* wq, const void* scales, const void* biases, int V, int D,
+                       void* raw, int ld_raw, const void* w0, void* out0, int ld_out0, const void* x1, int ld_x1,
+                       const int* row_sel1, const void* w1, void* out1, int ld_out1, float eps, void* stream);
+
 /* Gated-attention input prep (Dh 256, rotary 64): per-head q/k RMS norm, rotate-half RoPE from the
  * cos/sin tables [max_pos][32], q and gate out [S, nq, Dh], k and v appended to the caches
  * [nkv, max_pos, Dh] at position *pos_ptr + pos_add + s.  qkv, qn_w, kn_w 16-byte aligned. */

@@ -78,27 +78,14 @@ __global__ void embed_nvfp4_kernel(const int32_t* __restrict__ tok, const uint32
 
 // ----------------------------------------------------------------------------- RMSNorm
 // Wide tree: blockDim = D/32 threads, thread c owns elements [32c, 32c+32).
-__global__ void rmsnorm_wide_kernel(const uint16_t* __restrict__ x, long long ld_x, const int* __restrict__ row_sel,
-                                    const uint16_t* __restrict__ w, float eps, uint16_t* __restrict__ out,
-                                    long long ld_o, int D) {
-  pdl_trigger();
+// RMS norm of one row of D = 32 * blockDim.x elements (thread c holds v = elements [32c, 32c + 32)):
+// a 32-fma chain per thread, the warp butterfly, the warps' sums in order, then bf16(w * R(x * r)) into
+// orow.  wq4: the thread's 32 weights.  Every thread of the block calls it.
+__device__ __forceinline__ void rmsnorm_row(const float (&v)[32], const uint4 (&wq4)[4], float eps, int D,
+                                            uint16_t* __restrict__ orow) {
   __shared__ float s_blk[32];
   __shared__ float s_r;
-  const int m = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
-  uint4 wq4[4];  // the norm weight is constant: fetched while the previous kernel may still run
-#pragma unroll
-  for (int q = 0; q < 4; ++q) wq4[q] = *reinterpret_cast<const uint4*>(w + 32 * c + 8 * q);
-  pdl_wait();
-  const long long row = row_sel ? (long long)(*row_sel) + m : m;
-  const uint16_t* xr = x + row * ld_x + 32 * c;
-  float v[32];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint4 u = *reinterpret_cast<const uint4*>(xr + 8 * q);
-    const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int h = 0; h < 4; ++h) { v[8 * q + 2 * h] = bflo(uu[h]); v[8 * q + 2 * h + 1] = bfhi(uu[h]); }
-  }
+  const int c = threadIdx.x, lane = c & 31, warp = c >> 5;
   float ss = 0.0f;
 #pragma unroll
   for (int e = 0; e < 32; ++e) ss = __fmaf_rn(v[e], v[e], ss);
@@ -112,7 +99,6 @@ __global__ void rmsnorm_wide_kernel(const uint16_t* __restrict__ x, long long ld
   }
   __syncthreads();
   const float r = s_r;
-  uint16_t* orow = out + (long long)m * ld_o + 32 * c;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const uint32_t ww[4] = {wq4[q].x, wq4[q].y, wq4[q].z, wq4[q].w};
@@ -123,7 +109,86 @@ __global__ void rmsnorm_wide_kernel(const uint16_t* __restrict__ x, long long ld
       const uint16_t hi = f2bf(__fmul_rn(bfhi(ww[h]), R(__fmul_rn(v[8 * q + 2 * h + 1], r))));
       o[h] = lo | (uint32_t(hi) << 16);
     }
-    *reinterpret_cast<uint4*>(orow + 8 * q) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(orow + 32 * c + 8 * q) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__device__ __forceinline__ void load_row32(const uint16_t* __restrict__ xr, float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 u = *reinterpret_cast<const uint4*>(xr + 8 * q);
+    const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) { v[8 * q + 2 * h] = bflo(uu[h]); v[8 * q + 2 * h + 1] = bfhi(uu[h]); }
+  }
+}
+
+__global__ void rmsnorm_wide_kernel(const uint16_t* __restrict__ x, long long ld_x, const int* __restrict__ row_sel,
+                                    const uint16_t* __restrict__ w, float eps, uint16_t* __restrict__ out,
+                                    long long ld_o, int D) {
+  pdl_trigger();
+  const int m = blockIdx.x, c = threadIdx.x;
+  uint4 wq4[4];  // the norm weight is constant: fetched while the previous kernel may still run
+#pragma unroll
+  for (int q = 0; q < 4; ++q) wq4[q] = *reinterpret_cast<const uint4*>(w + 32 * c + 8 * q);
+  pdl_wait();
+  const long long row = row_sel ? (long long)(*row_sel) + m : m;
+  float v[32];
+  load_row32(x + row * ld_x + 32 * c, v);
+  rmsnorm_row(v, wq4, eps, D, out + (long long)m * ld_o);
+}
+
+// Embedding rows and RMS norms in one launch, grid (M, jobs): job 0 dequantizes the embedding row of
+// tok[m] (affine g64 table, embed_kernel's arithmetic), writes it to raw (if not null) and its RMS norm
+// with w0 to out0; job 1 (x1 not null) is rmsnorm_wide_kernel on row row_sel1 + m of x1 with w1 into
+// out1.  The verify step uses job 0 (the embedding and layer 0's input norm), an MTP step both (its
+// two pre-fc norms).
+__global__ void embed_rmsnorm_kernel(const int32_t* __restrict__ tok, const uint32_t* __restrict__ wq,
+                                     const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, int V,
+                                     uint16_t* __restrict__ raw, long long ld_raw, const uint16_t* __restrict__ w0,
+                                     uint16_t* __restrict__ out0, long long ld_o0, const uint16_t* __restrict__ x1,
+                                     long long ld_x1, const int* __restrict__ row_sel1, const uint16_t* __restrict__ w1,
+                                     uint16_t* __restrict__ out1, long long ld_o1, float eps, int D, unsigned* err) {
+  pdl_trigger();
+  const int m = blockIdx.x, job = blockIdx.y, c = threadIdx.x;
+  const uint16_t* w = job == 0 ? w0 : w1;
+  uint4 wq4[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) wq4[q] = *reinterpret_cast<const uint4*>(w + 32 * c + 8 * q);
+  pdl_wait();
+  float v[32];
+  if (job == 0) {
+    const int r = tok[m];
+    if (r < 0 || r >= V) {  // uniform over the block: it leaves before any barrier
+      if (c == 0) atomicOr(err, DEVERR_BADARG);
+      return;
+    }
+    const int G = D / 64;
+    const float s = bf2f(sc[size_t(r) * G + c / 2]), b = bf2f(bi[size_t(r) * G + c / 2]);  // elements 32c.. in group c/2
+    uint32_t pk[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t word = wq[size_t(r) * (D / 8) + 4 * c + q];
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const uint16_t lo = f2bf(__fmaf_rn(s, float((word >> (4 * j)) & 15u), b));
+        const uint16_t hi = f2bf(__fmaf_rn(s, float((word >> (4 * (j + 1))) & 15u), b));
+        v[8 * q + j] = bf2f(lo);
+        v[8 * q + j + 1] = bf2f(hi);
+        pk[4 * q + j / 2] = lo | (uint32_t(hi) << 16);
+      }
+    }
+    if (raw) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(raw + (long long)m * ld_raw + 32 * c + 8 * q) =
+            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    }
+    rmsnorm_row(v, wq4, eps, D, out0 + (long long)m * ld_o0);
+  } else {
+    const long long row = row_sel1 ? (long long)(*row_sel1) + m : m;
+    load_row32(x1 + row * ld_x1 + 32 * c, v);
+    rmsnorm_row(v, wq4, eps, D, out1 + (long long)m * ld_o1);
   }
 }
 
@@ -604,6 +669,27 @@ extern "C" int qmtp_rmsnorm(const void* x, int ld_x, const int* row_sel, const v
   launch_kernel(rmsnorm_wide_kernel, dim3(M), dim3(D / 32), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const uint16_t*>(x), ld_x, row_sel, static_cast<const uint16_t*>(w), eps,
       static_cast<uint16_t*>(out), ld_out, D);
+  return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
+}
+
+extern "C" int qmtp_embed_rmsnorm(const int* tok, int M, const void* wq, const void* scales, const void* biases,
+                                  int V, int D, void* raw, int ld_raw, const void* w0, void* out0, int ld_out0,
+                                  const void* x1, int ld_x1, const int* row_sel1, const void* w1, void* out1,
+                                  int ld_out1, float eps, void* stream) {
+  if (!tok || !wq || !scales || !biases || !w0 || !out0) return QMTP_ERR_ARG;
+  if (x1 && (!w1 || !out1)) return QMTP_ERR_ARG;
+  if (M < 1 || V < 1 || D % 1024 != 0 || D > 32768 || ld_out0 < D || ld_out0 % 8) return QMTP_ERR_SHAPE;
+  if (raw && (ld_raw < D || ld_raw % 8)) return QMTP_ERR_SHAPE;
+  if (x1 && (ld_x1 < D || ld_out1 < D || ld_x1 % 8 || ld_out1 % 8)) return QMTP_ERR_SHAPE;
+  const void* al[] = {w0, out0, raw, x1, w1, out1};
+  for (const void* p : al)
+    if (p && !aligned16(p)) return QMTP_ERR_ALIGN;
+  launch_kernel(embed_rmsnorm_kernel, dim3(M, x1 ? 2 : 1), dim3(D / 32), 0, static_cast<cudaStream_t>(stream), tok,
+                static_cast<const uint32_t*>(wq), static_cast<const uint16_t*>(scales),
+                static_cast<const uint16_t*>(biases), V, static_cast<uint16_t*>(raw), (long long)ld_raw,
+                static_cast<const uint16_t*>(w0), static_cast<uint16_t*>(out0), (long long)ld_out0,
+                static_cast<const uint16_t*>(x1), (long long)ld_x1, row_sel1, static_cast<const uint16_t*>(w1),
+                static_cast<uint16_t*>(out1), (long long)ld_out1, eps, D, device_error_ptr());
   return cudaGetLastError() == cudaSuccess ? QMTP_OK : QMTP_ERR_CUDA;
 }
 

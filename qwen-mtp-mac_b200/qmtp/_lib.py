@@ -84,6 +84,7 @@ SIGNATURES.update({
     "qmtp_rmsnorm": [_P, _I, _P, _P, _F, _P, _I, _I, _I, _P],
     "qmtp_attn_prep": [_P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _P, _P, _I, _P, _P, _P, _P, _I, _P],
     "qmtp_attention": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P, _P],
+    "qmtp_embed_rmsnorm": [_P, _I, _P, _P, _P, _I, _I, _P, _I, _P, _P, _I, _P, _I, _P, _P, _P, _I, _F, _P],
     "qmtp_attention_fused": [_P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _P, _P, _I, _P, _P, _I, _P, _P],
     "qmtp_swiglu": [_P, _I, _I, _I, _P, _P],
     "qmtp_mtp_accept": [_P, _P, _I, _P, _P, _I, _I, _I, _I, _P],

@@ -167,7 +167,8 @@ class MTPDecoder:
     def _st(self):
         return _lib.stream()
 
-    _KERNELS = {"rmsnorm": 1, "attn_prep": 1, "attention": 1, "swiglu": 1, "embed": 1, "gdn": 1, "norm_gate": 1,
+    _KERNELS = {"rmsnorm": 1, "attn_prep": 1, "attention": 1, "swiglu": 1, "embed": 1, "embed_norm": 1, "gdn": 1,
+                "norm_gate": 1,
                 "accept": 1, "advance": 1, "next_tokens": 1, "argmax": 2, "draft_prob": 1, "nuse": 1}
 
     def _chk(self, rc, what):
@@ -248,6 +249,26 @@ class MTPDecoder:
             nbytes = N * K // 2 + scale_bytes + M * K * 2 + M * N * 2 * (2 if res is not None else 1)
             self.prof.append((nbytes, e0, e1, (M, N, K)))
 
+    def _embed_norm(self, tok, rows, raw, w0, out0, ld_o0, hid=None, hid_sel=None, w1=None, out1=None, ld_o1=None):
+        """Embedding rows of tok, optionally kept raw, RMS-normalised with w0 into out0; with hid also the
+        RMS norm of hid's rows (from device row hid_sel) with w1 into out1.  One launch for an affine
+        table (qmtp_embed_rmsnorm), else the embedding and the norms as separate launches."""
+        a, E, H = self.a, self.W["embed"], self.a.hidden
+        if E.mode == "nvfp4":
+            emb = raw if raw is not None else self.memb
+            self._embed(tok, rows, emb)
+            self._norm(emb, w0, out0, rows, ld_o=ld_o0)
+            if hid is not None:
+                self._chk(self.L.qmtp_rmsnorm(hid.data_ptr(), H, hid_sel, w1.data_ptr(), a.eps, out1.data_ptr(),
+                                              ld_o1, rows, H, self._st()), "rmsnorm")
+            return
+        self._chk(self.L.qmtp_embed_rmsnorm(tok, rows, E.weight.data_ptr(), E.scales.data_ptr(), E.biases.data_ptr(),
+                                            a.vocab, H, None if raw is None else raw.data_ptr(), H, w0.data_ptr(),
+                                            out0.data_ptr(), ld_o0, None if hid is None else hid.data_ptr(), H, hid_sel,
+                                            None if w1 is None else w1.data_ptr(),
+                                            None if out1 is None else out1.data_ptr(), ld_o1 or H, a.eps, self._st()),
+                  "embed_norm")
+
     def _norm(self, x, w, out, M, ld_x=None, ld_o=None, row_sel=None):
         H = w.shape[0]
         self._chk(self.L.qmtp_rmsnorm(x.data_ptr(), ld_x or H, row_sel, w.data_ptr(), self.a.eps, out.data_ptr(),
@@ -307,12 +328,14 @@ class MTPDecoder:
     def backbone(self):
         """mtp.py:143-153 on the k+1 verify tokens in self.tokens_in: h (pre-norm) and hn (post-norm)."""
         a, W, S = self.a, self.W, self.S
-        self._embed(self.tokens_in.data_ptr(), S, self.h)
+        # the embedding rows (the residual stream h) and layer 0's input norm in one launch
+        self._embed_norm(self.tokens_in.data_ptr(), S, self.h, W["layers.0"]["input_ln"], self.xn, a.hidden)
         for i in range(a.layers):
             L = W[f"layers.{i}"]
             # input_ln as its own launch: for the 12352- and 10240-row projections it overlaps the
             # projection's prologue better than the RMSNorm prologue (0.5-0.8 us per layer)
-            self._norm(self.h, L["input_ln"], self.xn, S)
+            if i:
+                self._norm(self.h, L["input_ln"], self.xn, S)
             if a.is_linear(i):
                 self._qmv(self.xn, L["in_proj"], self.proj, S, ldy=self.proj.shape[1])
                 # conv, norms, gates, delta rule, snapshots and the gated norm into self.gdn_out
@@ -343,10 +366,10 @@ class MTPDecoder:
         mtp.py:165-167)."""
         a, M = self.a, self.W["mtp"]
         H = a.hidden
-        self._embed(tok, rows, self.memb)
-        self._norm(self.memb, M["pre_fc_norm_embedding"], self.mcat, rows, ld_o=2 * H)
-        self._chk(self.L.qmtp_rmsnorm(hidden.data_ptr(), H, hidden_sel, M["pre_fc_norm_hidden"].data_ptr(), a.eps,
-                                      self.mcat.data_ptr() + 2 * H, 2 * H, rows, H, self._st()), "rmsnorm")
+        # the embedding and both pre-fc norms (mtp.py:202-203) into [e | h] = mcat, one launch
+        mcat_h = self.mcat[:, H:]
+        self._embed_norm(tok, rows, None, M["pre_fc_norm_embedding"], self.mcat, 2 * H, hidden, hidden_sel,
+                         M["pre_fc_norm_hidden"], mcat_h, 2 * H)
         self._qmv(self.mcat, M["fc"], self.mx, rows)
         Ly = M["layer"]
         self._norm(self.mx, Ly["input_ln"], self.xn, rows)
