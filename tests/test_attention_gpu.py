@@ -39,9 +39,10 @@ def test_attention_bit_exact(pos0, dev):
 
 @pytest.mark.parametrize("pos0,S", [(0, 3), (5, 3), (6, 1), (100, 4), (131, 3), (509, 3), (1020, 4)])
 def test_attention_fused_bit_exact(pos0, S, dev):
-    """qmtp_attention_fused (q/k RMS norms + RoPE + cache writes + attention in one launch) against the
-    oracle's qo_attn_prep + qo_attention: the same output and the same cache contents.  The caches hold
-    random data at the new positions, which the kernel must not read."""
+    """qmtp_attention_fused (q/k RMS norms + RoPE + cache writes + attention in one launch), and the
+    two-launch form qmtp_attn_prep + qmtp_attention, against the oracle's qo_attn_prep + qo_attention:
+    the same q, gate, output and cache contents.  The caches hold random data at the new positions,
+    which the fused kernel must not read."""
     from qmtp import _lib
 
     nq, nkv, Dh, R, max_pos, eps = 16, 4, 256, 64, 1024, 1e-6
@@ -75,3 +76,17 @@ def test_attention_fused_bit_exact(pos0, S, dev):
     assert _lib.device_error() == 0
     assert np.array_equal(to_np(out), want)
     assert np.array_equal(to_np(kc_t), kc) and np.array_equal(to_np(vc_t), vc)
+    # the two-launch form (qmtp_attn_prep, then qmtp_attention) from the same stale caches
+    kc2, vc2 = to_torch(randn_bf16((nkv, max_pos, Dh), 15 + pos0, 1.0), dev), to_torch(randn_bf16((nkv, max_pos, Dh), 16 + pos0, 1.0), dev)
+    qb = torch.empty((S, nq, Dh), dtype=torch.bfloat16, device=dev)
+    gb = torch.empty_like(qb)
+    _lib.check(_lib.lib().qmtp_attn_prep(t[0].data_ptr(), ld, S, nq, nkv, Dh, R, t[1].data_ptr(), t[2].data_ptr(), eps,
+                                         ct.data_ptr(), st.data_ptr(), pos.data_ptr(), 1, qb.data_ptr(), gb.data_ptr(),
+                                         kc2.data_ptr(), vc2.data_ptr(), max_pos, _lib.stream()), "attn_prep")
+    out2 = torch.empty_like(out)
+    _lib.check(_lib.lib().qmtp_attention(qb.data_ptr(), gb.data_ptr(), kc2.data_ptr(), vc2.data_ptr(), max_pos, S, nq,
+                                         nkv, Dh, pos.data_ptr(), 1, out2.data_ptr(), _lib.stream()), "attention")
+    torch.cuda.synchronize()
+    assert np.array_equal(to_np(qb), q) and np.array_equal(to_np(gb), g)
+    assert np.array_equal(to_np(out2), want)
+    assert np.array_equal(to_np(kc2), kc) and np.array_equal(to_np(vc2), vc)
