@@ -147,7 +147,7 @@ class OracleModel:
         self.W = W
         self.cos, self.sin = rope_tables(args)
         self.draft_ids = None          # draft head over a vocabulary subset (set_draft_head)
-        self.draft_W = W.get("lm_head_q")
+        self.draft_W = None            # its rows; None: the full 4-bit head W["lm_head_q"]
 
     def set_draft_head(self, vocab=None, counts=None, extra_ids=()):
         """mtp.py:170-196 load_draft_head: the draft head scores `vocab` rows of the lm_head -- the first
@@ -157,7 +157,7 @@ class OracleModel:
         V = self.a.vocab
         lin = self.W["lm_head_q"]
         if vocab is None or (counts is None and vocab >= V):
-            self.draft_ids, self.draft_W = None, self.W["lm_head_q"]
+            self.draft_ids, self.draft_W = None, None
             return
         if counts is None:
             rows = np.arange(min(vocab, V))
@@ -270,7 +270,7 @@ class OracleModel:
     def draft_token(self, xn, with_prob=False):
         """Draft head: full-vocabulary 4-bit head (bench_ab.py:24 DRAFT_HEAD, engine.py:46-48) + argmax;
         with_prob: also the probability of the argmax (mtp.py:222-223)."""
-        logits = qmv(xn, self.draft_W)
+        logits = qmv(xn, self.W["lm_head_q"] if self.draft_W is None else self.draft_W)
         i = ops.argmax_bf16(logits)
         d = i if self.draft_ids is None else self.draft_ids[i]
         return (d, ops.draft_prob(logits[0], int(i[0]))) if with_prob else d
