@@ -58,3 +58,27 @@ def test_load_draft_head_selects_the_oracles_rows():
     first = load_draft_head(500, {"bits": 4, "group_size": 64}, lm=lm)
     assert first.ids is None and first.proj.out_features == 500
     assert load_draft_head(V, None, lm=lm).proj is lm.weights["lm_head_q"]
+
+
+def test_draft_head_argument_checks():
+    """Host-side refusals of load_draft_head / DraftHead (no kernel runs)."""
+    import pytest
+    import torch
+    from types import SimpleNamespace
+
+    from qmtp.mtp import DraftHead, load_draft_head
+    from qmtp.qmv_kernel import QuantizedLinear
+
+    W = om.synthetic_weights(om.SMALL, seed=0)
+    wq, s, b = (torch.from_numpy(np.asarray(t).view(np.int32 if t.dtype == np.uint32 else np.int16)) for t in
+                W["lm_head_q"])
+    full = QuantizedLinear(wq, s, b)
+    lm = SimpleNamespace(weights={"lm_head_q": full})
+    with pytest.raises(ValueError):
+        load_draft_head(100, None, True, lm=lm)                     # freq needs the corpus counts
+    with pytest.raises(NotImplementedError):
+        load_draft_head(100, {"bits": 8, "group_size": 64}, lm=lm)  # draft heads are 4-bit g64
+    with pytest.raises(ValueError):
+        DraftHead(QuantizedLinear(wq[:10], s[:10], b[:10]), torch.arange(9))  # one id per row
+    h = DraftHead(QuantizedLinear(wq[:3], s[:3], b[:3]), torch.tensor([5, 9, 2]))
+    assert h.token(torch.tensor([[0.1, 0.7, 0.7]])).tolist() == [9]  # first maximum, mapped through ids
